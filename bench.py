@@ -1,0 +1,419 @@
+#!/usr/bin/env python
+"""Mesh GPT training throughput (fwd + bwd + AdamW) on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg4|cfg3] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU: every rank trains the full model
+on its own 32 sequences (cfg4) and all-reduces the FP32 gradient over NCCL
+before AdamW (weak scaling).  Rank 0 prints one JSON line.
+
+* value  - tokens/s of the whole job with batches already in HBM, timed with
+  CUDA events on the model's stream between barriers, max over ranks.
+* e2e    - the same metric through the public API (MeshGpt.train_batch_with_
+  optimizer) with host batches in pinned memory: each step copies its inputs
+  host->device and reads the loss back.
+* roofline - the dominant kernel (largest share of the last timed step, from
+  CUDA events captured between the graph's launches) against the measured
+  peaks in MEASURED_PEAKS.json.
+* cpu_baseline - the f64 oracle port of the reference's CPU verify path
+  (oracle/gpt_ref.py) timed on this host on a bounded sample (N=1, rank 0).
+* --impl reference - the reference's CPU path (the oracle port: the Rust
+  reference cannot be built here) on the host cores, same metric/config.
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # W512 L8 H8 (hd 64) T1024, 32 sequences per GPU,
+    # A=4, F=6 (reference defaults), Zipf(1.1) tokens over vocab 64.
+    "cfg4": dict(vocab_size=64, context=1024, width=512, heads=8, layers=8, attention_mesh_depth=4,
+                 ffn_mesh_depth=6, sequences=32),
+    # W256 L4 H4 (hd 64) T256, batch 64.
+    "cfg3": dict(vocab_size=64, context=256, width=256, heads=4, layers=4, attention_mesh_depth=4,
+                 ffn_mesh_depth=6, sequences=64),
+}
+OPTIMIZER = dict(learning_rate=3e-4, weight_decay=0.1, beta1=0.9, beta2=0.999, epsilon=1e-8)
+SEED = 7
+METRIC = "Mesh-GPT train tokens/s (fwd+bwd+AdamW)"
+
+
+def model_kwargs(cfg):
+    return {k: v for k, v in cfg.items() if k != "sequences"}
+
+
+# ------------------------------------------------------------- CPU baseline
+def _oracle_sequence(args):
+    """One full training step of the f64 oracle on one sequence (a worker)."""
+    import numpy as np
+
+    from oracle.data import zipf_batch
+    from oracle.gpt_config import GptConfig
+    from oracle.gpt_ref import ReferenceGpt, adamw_step
+    cfg_kw, rank, step = args
+    cfg = GptConfig(**cfg_kw)
+    model = ReferenceGpt(cfg, seed=SEED)
+    x, y = zipf_batch(SEED, rank, step, 1, cfg.context, cfg.vocab_size)
+    t0 = time.perf_counter()
+    _, grad = model.loss_and_gradient(x, y, cfg.context)
+    p = model.parameters.copy()
+    m, v = np.zeros_like(p), np.zeros_like(p)
+    adamw_step(p, m, v, grad, 1, OPTIMIZER["learning_rate"], OPTIMIZER["weight_decay"], OPTIMIZER["beta1"],
+               OPTIMIZER["beta2"], OPTIMIZER["epsilon"], (np.float32(0.9), np.float32(0.999)))
+    return time.perf_counter() - t0
+
+
+def _pool_workers():
+    # Each worker holds ~1.3 GB of f64 activations at cfg4; cap the pool.
+    return max(1, min(os.cpu_count() or 1, 16))
+
+
+def run_oracle_tasks(cfg, tasks, workers):
+    """Runs `tasks` oracle sequences over a spawn pool of single-threaded
+    workers; returns (wall seconds, tokens)."""
+    import multiprocessing as mp
+    env = {"OMP_NUM_THREADS": "1", "OPENBLAS_NUM_THREADS": "1", "MKL_NUM_THREADS": "1"}
+    old = {k: os.environ.get(k) for k in env}
+    os.environ.update(env)
+    try:
+        ctx = mp.get_context("spawn")
+        with ctx.Pool(workers) as pool:
+            t0 = time.perf_counter()
+            pool.map(_oracle_sequence, [(model_kwargs(cfg), 0, i) for i in range(tasks)], chunksize=1)
+            wall = time.perf_counter() - t0
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    return wall, tasks * cfg["context"]
+
+
+def cpu_baseline(cfg):
+    workers = _pool_workers()
+    wall, tokens = run_oracle_tasks(cfg, workers, workers)
+    return {"value": tokens / wall, "unit": "tokens/s", "cores": workers, "kind": "port",
+            "sample": f"{workers} sequences x {cfg['context']} tokens, one f64 oracle fwd+bwd+AdamW each, "
+                      f"one single-threaded spawn worker per sequence ({wall:.1f} s wall)"}
+
+
+def reference_arm(args, cfg):
+    """--impl reference: the reference's CPU path (oracle port) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    workers = _pool_workers()
+    warm = min(args.warmup, workers)
+    if warm:
+        run_oracle_tasks(cfg, warm, workers)
+    wall, tokens = run_oracle_tasks(cfg, args.steps, workers)
+    value = tokens / wall
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * wall / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": config_block(args, cfg),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port",
+                         "sample": f"each step = one {cfg['context']}-token sequence fwd+bwd+AdamW of the f64 "
+                                   f"oracle (the Rust reference cannot be built here), {workers} spawn workers"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(args, cfg):
+    return {"workload": f"{args.config}: Mesh GPT W{cfg['width']} L{cfg['layers']} H{cfg['heads']} "
+                        f"T{cfg['context']} V{cfg['vocab_size']} A{cfg['attention_mesh_depth']} "
+                        f"F{cfg['ffn_mesh_depth']}, {cfg['sequences']} sequences/GPU",
+            "global_batch": cfg["sequences"] * args.gpus, "seq_len": cfg["context"],
+            "tokens_per_step": cfg["sequences"] * cfg["context"] * args.gpus,
+            "parallelism": f"dp{args.gpus}", "optimizer": dict(OPTIMIZER),
+            "l2": "working set > L2: ~4 GB of activations per step per GPU, no flush needed"}
+
+
+# ------------------------------------------------------------------ roofline
+def kernel_work(name, cfg, rows):
+    """Algorithmic work of one launch: (kind, amount).  Attention kernels count
+    the causal-masked multiply-adds (2 FLOPs each); row kernels count the bytes
+    their inputs and outputs must cross HBM once."""
+    W, H, T = cfg["width"], cfg["heads"], cfg["context"]
+    hd = W // H
+    seqs = rows // T
+    pairs = T * (T + 1) // 2 * seqs * H
+    f = 4
+    work = {
+        "attention_forward": ("tensor", 2 * 2 * hd * pairs),
+        "attention_backward_dkdv": ("tensor", 4 * 2 * hd * pairs),
+        "attention_backward_dq": ("tensor", 3 * 2 * hd * pairs),
+        "qkv_forward": ("hbm", f * rows * W * 4),      # x -> Q, K, V
+        "post_forward": ("hbm", f * rows * W * 5),     # O, V, x -> x_mid, x_next
+        "post_backward": ("hbm", f * rows * (W * 7 + H)),  # dx, x_mid, O, V -> dO, dV, dx_mid, delta
+        "qkv_backward": ("hbm", f * rows * W * 6),     # dQ, dK, dV, x, dx_mid -> dx
+        "head_forward_backward": ("hbm", f * rows * (3 * W + cfg["vocab_size"])),
+    }
+    return work.get(name)
+
+
+def roofline(times, cfg, rows, peaks):
+    """Dominant kernel of the step (largest summed time) and its roofline."""
+    totals, counts = {}, {}
+    for name, ms in times:
+        totals[name] = totals.get(name, 0.0) + ms
+        counts[name] = counts.get(name, 0) + 1
+    name = max(totals, key=totals.get)
+    step_ms = sum(totals.values())
+    avg_ms = totals[name] / counts[name]
+    kw = kernel_work(name, cfg, rows)
+    out = {"kernel": name, "share": totals[name] / step_ms, "launches_per_step": counts[name],
+           "avg_launch_ms": avg_ms}
+    if kw is None:
+        out.update(bound=None, achieved=None, peak=None, unit=None, frac=None, traffic=None)
+        return out
+    kind, amount = kw
+    if kind == "hbm":
+        achieved = amount / (avg_ms * 1e-3) / 1e9
+        peak = peaks.get("hbm_gbs")
+        unit = "GB/s"
+        out["algorithmic_bytes_per_launch"] = amount
+    else:
+        # FP32 SIMT attention: measured against the FP32 FMA pipe would need a
+        # measured FP32 peak; MEASURED_PEAKS.json holds the bf16 tensor peak.
+        achieved = amount / (avg_ms * 1e-3) / 1e12
+        peak = peaks.get("bf16_tflops")
+        unit = "TFLOP/s"
+        out["algorithmic_flops_per_launch"] = amount
+        out["note"] = ("FP32 SIMT kernel (CUDA cores); peak is the measured dense bf16 tensor peak, "
+                       "nominal FP32 SIMT peak is 148 SMs x 128 FMA x 2 x 1.965 GHz = 74.4 TFLOP/s")
+        out["frac_of_fp32_simt_nominal"] = achieved / 74.4
+    out.update(bound=kind, achieved=achieved, peak=peak, unit=unit,
+               frac=(achieved / peak if peak else None), traffic=traffic_from_profiles(name))
+    out["peak_source"] = "measured (MEASURED_PEAKS.json)" if peaks.get("_measured") else "fallback"
+    return out
+
+
+def traffic_from_profiles(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any
+    (a line 'traffic_bytes_per_launch <kernel> <bytes>')."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for fn in sorted(os.listdir(d)):
+        if not fn.endswith((".md", ".txt")):
+            continue
+        for line in open(os.path.join(d, fn)):
+            parts = line.strip().strip("`").split()
+            if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == kernel:
+                try:
+                    return float(parts[2])
+                except ValueError:
+                    pass
+    return None
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        p["_measured"] = True
+        return p
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "_measured": False}
+
+
+# -------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.device)], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="cfg4", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        reference_arm(args, cfg)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+
+    # The CPU baseline's spawn pool runs before any CUDA call.
+    base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        base = cpu_baseline(cfg)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from grokking_abmod_b200 import AdamWOptions, GptConfig, MeshGpt, nccl_unique_id
+    from grokking_abmod_b200.data import zipf_batch
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    model = MeshGpt(local, GptConfig(**model_kwargs(cfg)), SEED)
+    if world > 1:
+        box = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        model.attach_nccl(box[0], rank, world)
+    opt = AdamWOptions(**OPTIMIZER)
+    T, seqs = cfg["context"], cfg["sequences"]
+    rows = seqs * T
+    total = args.warmup + args.steps
+    batches = [zipf_batch(SEED, rank, s, seqs, T, cfg["vocab_size"]) for s in range(total)]
+    dev = [(torch.from_numpy(x.view(np.int32)).cuda(), torch.from_numpy(y.view(np.int32)).cuda())
+           for x, y in batches]
+    loss_dev = torch.zeros(1, dtype=torch.float64, device="cuda")
+    stream = torch.cuda.ExternalStream(model.stream())
+    model.set_timing(True)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident batches
+    for s in range(args.warmup):
+        model.train_batch_device(dev[s][0].data_ptr(), dev[s][1].data_ptr(), rows, T, opt, loss_dev.data_ptr())
+    model.check()
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for s in range(args.warmup, total):
+        model.train_batch_device(dev[s][0].data_ptr(), dev[s][1].data_ptr(), rows, T, opt, loss_dev.data_ptr())
+    end.record(stream)
+    barrier()
+    clock_info = clocks.stop()
+    ms = max_over_ranks(start.elapsed_time(end))
+    model.check()
+    final_loss = float(loss_dev.item())
+    times = model.kernel_times()
+    value = rows * world * args.steps / (ms / 1000.0)
+
+    # ---- end to end through the public API, pinned host batches
+    pinned = []
+    for x, y in batches:
+        px = torch.from_numpy(x.view(np.int32)).pin_memory()
+        py = torch.from_numpy(y.view(np.int32)).pin_memory()
+        pinned.append((px, py, px.numpy().view(np.uint32), py.numpy().view(np.uint32)))
+    for s in range(args.warmup):
+        model.train_batch_with_optimizer(pinned[s][2], pinned[s][3], T, opt)
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for s in range(args.warmup, total):
+        model.train_batch_with_optimizer(pinned[s][2], pinned[s][3], T, opt)
+    e_end.record(stream)
+    barrier()
+    e_ms = max_over_ranks(e_start.elapsed_time(e_end))
+    e2e = rows * world * args.steps / (e_ms / 1000.0)
+
+    if rank == 0:
+        peaks = load_peaks()
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic: seeded Zipf(1.1) tokens over vocab 64, "
+                                                          "random-init (seeded reference init) weights",
+            "config": config_block(args, cfg),
+            "e2e": {"value": e2e, "unit": "tokens/s", "ms_per_step": e_ms / args.steps,
+                    "h2d_bytes_per_step": 2 * rows * 4, "d2h_bytes_per_step": 8,
+                    "api": "MeshGpt.train_batch_with_optimizer (mb_gpt_train_step), pinned host batches"},
+            "roofline": roofline(times, cfg, rows, peaks),
+            "cpu_baseline": base,
+            "gpu_launches": model.step_launches(rows, T) * args.steps,
+            "clocks": clock_info,
+            "final_loss": final_loss,
+            "kernel_ms_last_step": _summarize(times),
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _summarize(times):
+    out = {}
+    for name, ms in times:
+        out[name] = round(out.get(name, 0.0) + ms, 4)
+    return out
+
+
+if __name__ == "__main__":
+    main()

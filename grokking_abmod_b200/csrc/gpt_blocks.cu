@@ -1,0 +1,342 @@
+// Fused Mesh GPT block kernels (forward and backward) for sm_100a.
+//
+// Per block the reference launches ~4A+F mesh layers, five RMSNorms, two
+// RoPEs, XSA and five gradient additions as separate kernels, each making a
+// full HBM round trip (src/gpt/gpu.rs:2177-2278, :2351-2502).  Here one
+// row-tile kernel runs each row-local span of the block, keeping every
+// intermediate in registers and shared memory:
+//
+//   qkv_forward    x -> RMSNorm -> {Q,K,V} meshes -> QK-Norm -> RoPE
+//   post_forward   (O, V, x) -> XSA -> O mesh -> +x -> RMSNorm -> FFN mesh -> +x_mid
+//   post_backward  recomputes the FFN and O meshes, backpropagates through
+//                  them, RMSNorm and XSA, and emits dO, dV(XSA), dx_mid and
+//                  the attention row statistic delta = dO . O
+//   qkv_backward   recomputes Q/K/V meshes and QK-Norm, inverse RoPE,
+//                  backpropagates to dx
+//
+// Mesh layers follow src/gpt/gpu.rs:103-146 (forward/backward) and
+// :1087-1149 (edge gradients); RMSNorm :65-94/:1035-1077; RoPE :175-208;
+// XSA :781-897.
+
+#include "gpt_rows.cuh"
+
+namespace mb {
+
+template <class T>
+__device__ __forceinline__ float2 ld2(const float* p, int row, int rows, int W, int cp) {
+  if (row < rows) return __ldg(reinterpret_cast<const float2*>(p + (size_t)row * W) + cp);
+  return make_float2(0.f, 0.f);
+}
+
+__device__ __forceinline__ void st2(float* p, int row, int rows, int W, int cp, float2 v) {
+  if (row < rows) reinterpret_cast<float2*>(p + (size_t)row * W)[cp] = v;
+}
+
+// Per-head RMS (QK-Norm): returns 1/rms of the owned pair's head, and the
+// normalized pair in v.
+__device__ __forceinline__ float head_rmsnorm(float2& v, int hp) {
+  float s = head_sum(v.x * v.x + v.y * v.y, hp);
+  float inv = 1.0f / sqrtf(s / (float)(2 * hp) + kRmsEpsilon);
+  v = v * inv;
+  return inv;
+}
+
+template <int W, int RPT>
+__global__ void __launch_bounds__(RowTile<W, RPT>::NT)
+    qkv_forward(Dims d, const float* __restrict__ x, const uint32_t* __restrict__ tokens,
+                const float* __restrict__ emb, float* __restrict__ x_out, const float* __restrict__ wq,
+                const float* __restrict__ wk, const float* __restrict__ wv, const float2* __restrict__ rope_cs,
+                float* __restrict__ q_out, float* __restrict__ k_out, float* __restrict__ v_out) {
+  using T = RowTile<W, RPT>;
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  float* bufs = smem;               // 2 exchange buffers
+  float* red = smem + 2 * T::BUF;   // 2 * TR * WPR
+  Ctx<T> c;
+  int phase = 0;
+  const int hp = d.head_width / 2;
+  const int ntiles = (d.rows + T::TR - 1) / T::TR;
+  const float4* wgs[3] = {reinterpret_cast<const float4*>(wq), reinterpret_cast<const float4*>(wk),
+                          reinterpret_cast<const float4*>(wv)};
+  float* outs[3] = {q_out, k_out, v_out};
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    float2 n[RPT];
+    float inv[RPT];
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) {
+      const int r = tile * T::TR + c.row(k);
+      if (tokens != nullptr) {
+        // Block 0: the embedding lookup (src/gpt/gpu.rs:41-56) is fused here.
+        n[k] = make_float2(0.f, 0.f);
+        if (r < d.rows) {
+          uint32_t t = __ldg(tokens + r);
+          t = t < (uint32_t)d.vocab ? t : 0u;
+          n[k] = __ldg(reinterpret_cast<const float2*>(emb + (size_t)t * W) + c.cp);
+          if (x_out != nullptr) st2(x_out, r, d.rows, W, c.cp, n[k]);
+        }
+      } else {
+        n[k] = ld2<T>(x, r, d.rows, W, c.cp);
+      }
+    }
+    rmsnorm_rows<T>(c, n, inv, red, phase, W);
+    for (int m = 0; m < 3; ++m) {
+      float2 a[RPT];
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) a[k] = n[k];
+      mesh_forward<W, T>(c, d, a, wgs[m], d.attn_depth, bufs, false);
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) {
+        const int r = tile * T::TR + c.row(k);
+        float2 v = a[k];
+        if (m < 2) {
+          head_rmsnorm(v, hp);
+          v = rope_pair(v, c.cp, hp, r % d.sequence, rope_cs, false);
+        }
+        st2(outs[m], r, d.rows, W, c.cp, v);
+      }
+      __syncthreads();
+    }
+  }
+}
+
+template <int W, int RPT>
+__global__ void __launch_bounds__(RowTile<W, RPT>::NT)
+    post_forward(Dims d, const float* __restrict__ o, const float* __restrict__ v, const float* __restrict__ x,
+                 const float* __restrict__ wo, const float* __restrict__ wf, float* __restrict__ xmid_out,
+                 float* __restrict__ xnext_out) {
+  using T = RowTile<W, RPT>;
+  extern __shared__ float4 smem4[];
+  float* smem = reinterpret_cast<float*>(smem4);
+  float* bufs = smem;
+  float* red = smem + 2 * T::BUF;
+  Ctx<T> c;
+  int phase = 0;
+  const int hp = d.head_width / 2;
+  const int ntiles = (d.rows + T::TR - 1) / T::TR;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    float2 a[RPT], res[RPT];
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) {
+      const int r = tile * T::TR + c.row(k);
+      float2 y = ld2<T>(o, r, d.rows, W, c.cp);
+      float2 vv = ld2<T>(v, r, d.rows, W, c.cp);
+      res[k] = ld2<T>(x, r, d.rows, W, c.cp);
+      // XSA: z = y - (y.u)u, u = v / max(|v|, eps)   (src/gpt/gpu.rs:829-853)
+      float sq = head_sum(vv.x * vv.x + vv.y * vv.y, hp);
+      float iv = 1.0f / fmaxf(sqrtf(sq), kXsaEpsilon);
+      float2 u = vv * iv;
+      float proj = head_sum(y.x * u.x + y.y * u.y, hp);
+      a[k] = make_float2(y.x - proj * u.x, y.y - proj * u.y);
+    }
+    mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(wo), d.attn_depth, bufs, false);
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) {
+      res[k] = res[k] + a[k];
+      st2(xmid_out, tile * T::TR + c.row(k), d.rows, W, c.cp, res[k]);
+      a[k] = res[k];
+    }
+    float inv[RPT];
+    __syncthreads();
+    rmsnorm_rows<T>(c, a, inv, red, phase, W);
+    mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(wf), d.ffn_depth, bufs, false);
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) st2(xnext_out, tile * T::TR + c.row(k), d.rows, W, c.cp, res[k] + a[k]);
+    __syncthreads();
+  }
+}
+
+// Writes the per-thread edge-gradient slots of one mesh stack as the partial
+// of (CTA, row lane): layout [slot][depth][W][2].
+template <class T>
+__device__ __forceinline__ void flush_partials(const Ctx<T>& c, const float4* acc, int depth, float* partial) {
+  if (partial == nullptr) return;
+  const int slot = blockIdx.x * T::RL + c.rl;
+  float4* out = reinterpret_cast<float4*>(partial) + (size_t)slot * depth * T::PAIRS;
+  for (int l = 0; l < depth; ++l) out[l * T::PAIRS + c.cp] = acc[l * T::NT + c.tid];
+}
+
+template <class T>
+__device__ __forceinline__ void zero_slots(const Ctx<T>& c, float4* acc, int layers) {
+  for (int l = 0; l < layers; ++l) acc[l * T::NT + c.tid] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+template <int W, int RPT>
+__global__ void __launch_bounds__(RowTile<W, RPT>::NT)
+    post_backward(Dims d, const float* __restrict__ dxn, const float* __restrict__ xmid, const float* __restrict__ o,
+                  const float* __restrict__ v, const float* __restrict__ wo, const float* __restrict__ wf,
+                  float* __restrict__ do_out, float* __restrict__ dvx_out, float* __restrict__ dxm_out,
+                  float* __restrict__ delta_out, float* __restrict__ part_o, float* __restrict__ part_f) {
+  using T = RowTile<W, RPT>;
+  extern __shared__ float4 smem4[];
+  const int dmax = d.ffn_depth > d.attn_depth ? d.ffn_depth : d.attn_depth;
+  float4* acc_f = smem4;                           // ffn_depth * NT slots
+  float4* acc_o = smem4 + d.ffn_depth * T::NT;     // attn_depth * NT slots
+  float* smem = reinterpret_cast<float*>(smem4 + (d.ffn_depth + d.attn_depth) * T::NT);
+  float* bufs = smem;                              // dmax activation buffers
+  float* xch = smem + dmax * T::BUF;               // 2 exchange buffers
+  float* red = xch + 2 * T::BUF;
+  Ctx<T> c;
+  zero_slots<T>(c, acc_f, d.ffn_depth);
+  zero_slots<T>(c, acc_o, d.attn_depth);
+  int phase = 0;
+  const int hp = d.head_width / 2;
+  const int ntiles = (d.rows + T::TR - 1) / T::TR;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    float2 g[RPT], n2[RPT], dy[RPT];
+    float inv2[RPT];
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) {
+      const int r = tile * T::TR + c.row(k);
+      g[k] = ld2<T>(dxn, r, d.rows, W, c.cp);
+      n2[k] = ld2<T>(xmid, r, d.rows, W, c.cp);
+    }
+    // FFN: x_next = x_mid + FFN(RMSNorm(x_mid)).
+    rmsnorm_rows<T>(c, n2, inv2, red, phase, W);
+    {
+      float2 a[RPT];
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) a[k] = n2[k];
+      mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(wf), d.ffn_depth, bufs, true);
+    }
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) dy[k] = g[k];
+    mesh_backward<W, T>(c, d, dy, reinterpret_cast<const float4*>(wf), d.ffn_depth, bufs, xch, acc_f);
+    rmsnorm_rows_backward<T>(c, n2, inv2, dy, red, phase, W);
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) g[k] = g[k] + dy[k];  // dx_mid
+    // Attention output path: x_mid = x + Omesh(XSA(O, V)).
+    float2 y[RPT], u[RPT];
+    float proj[RPT], iv[RPT], sq[RPT];
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) {
+      const int r = tile * T::TR + c.row(k);
+      y[k] = ld2<T>(o, r, d.rows, W, c.cp);
+      float2 vv = ld2<T>(v, r, d.rows, W, c.cp);
+      sq[k] = head_sum(vv.x * vv.x + vv.y * vv.y, hp);
+      iv[k] = 1.0f / fmaxf(sqrtf(sq[k]), kXsaEpsilon);
+      u[k] = vv * iv[k];
+      proj[k] = head_sum(y[k].x * u[k].x + y[k].y * u[k].y, hp);
+    }
+    __syncthreads();  // the FFN backward may still read bufs
+    {
+      float2 a[RPT];
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) a[k] = make_float2(y[k].x - proj[k] * u[k].x, y[k].y - proj[k] * u[k].y);
+      mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(wo), d.attn_depth, bufs, true);
+    }
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) dy[k] = g[k];
+    mesh_backward<W, T>(c, d, dy, reinterpret_cast<const float4*>(wo), d.attn_depth, bufs, xch, acc_o);
+    // XSA backward (src/gpt/gpu.rs:861-897); dy is dL/dz.
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) {
+      const int r = tile * T::TR + c.row(k);
+      float gp = head_sum(dy[k].x * u[k].x + dy[k].y * u[k].y, hp);
+      float2 dO = make_float2(dy[k].x - gp * u[k].x, dy[k].y - gp * u[k].y);
+      float2 dv;
+      const bool above = sq[k] >= kXsaEpsilon * kXsaEpsilon;
+      dv.x = -gp * y[k].x - proj[k] * dy[k].x;
+      dv.y = -gp * y[k].y - proj[k] * dy[k].y;
+      if (above) {
+        dv.x += 2.0f * proj[k] * gp * u[k].x;
+        dv.y += 2.0f * proj[k] * gp * u[k].y;
+      }
+      dv = dv * iv[k];
+      float delta = head_sum(dO.x * y[k].x + dO.y * y[k].y, hp);
+      st2(do_out, r, d.rows, W, c.cp, dO);
+      st2(dvx_out, r, d.rows, W, c.cp, dv);
+      st2(dxm_out, r, d.rows, W, c.cp, g[k]);
+      if ((c.cp % hp) == 0 && r < d.rows) delta_out[(size_t)(c.cp / hp) * d.rows + r] = delta;
+    }
+    __syncthreads();
+  }
+  flush_partials<T>(c, acc_f, d.ffn_depth, part_f);
+  flush_partials<T>(c, acc_o, d.attn_depth, part_o);
+}
+
+template <int W, int RPT>
+__global__ void __launch_bounds__(RowTile<W, RPT>::NT)
+    qkv_backward(Dims d, const float* __restrict__ dq, const float* __restrict__ dk, const float* __restrict__ dv,
+                 const float* __restrict__ x, const float* __restrict__ dxm, const float* __restrict__ wq,
+                 const float* __restrict__ wk, const float* __restrict__ wv, const float2* __restrict__ rope_cs,
+                 float* __restrict__ dx_out, float* __restrict__ part_q, float* __restrict__ part_k,
+                 float* __restrict__ part_v) {
+  using T = RowTile<W, RPT>;
+  extern __shared__ float4 smem4[];
+  const int A = d.attn_depth;
+  float4* accs = smem4;  // 3 * A * NT slots
+  float* smem = reinterpret_cast<float*>(smem4 + 3 * A * T::NT);
+  float* bufs = smem;
+  float* xch = smem + A * T::BUF;
+  float* red = xch + 2 * T::BUF;
+  Ctx<T> c;
+  zero_slots<T>(c, accs, 3 * A);
+  int phase = 0;
+  const int hp = d.head_width / 2;
+  const int ntiles = (d.rows + T::TR - 1) / T::TR;
+  const float4* wgs[3] = {reinterpret_cast<const float4*>(wq), reinterpret_cast<const float4*>(wk),
+                          reinterpret_cast<const float4*>(wv)};
+  const float* grads[3] = {dq, dk, dv};
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    float2 n1[RPT], dn[RPT];
+    float inv1[RPT];
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) {
+      n1[k] = ld2<T>(x, tile * T::TR + c.row(k), d.rows, W, c.cp);
+      dn[k] = make_float2(0.f, 0.f);
+    }
+    rmsnorm_rows<T>(c, n1, inv1, red, phase, W);
+    for (int m = 0; m < 3; ++m) {
+      float2 a[RPT];
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) a[k] = n1[k];
+      __syncthreads();  // the previous mesh backward may still read bufs
+      mesh_forward<W, T>(c, d, a, wgs[m], A, bufs, true);
+      float2 gm[RPT];
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) {
+        const int r = tile * T::TR + c.row(k);
+        float2 gg = ld2<T>(grads[m], r, d.rows, W, c.cp);
+        if (m < 2) {
+          // QK-Norm then RoPE in forward; backward: inverse RoPE, then the
+          // per-head RMSNorm adjoint.
+          float2 qn = a[k];
+          float ih = head_rmsnorm(qn, hp);
+          gg = rope_pair(gg, c.cp, hp, r % d.sequence, rope_cs, true);
+          float dot = head_sum(gg.x * qn.x + gg.y * qn.y, hp) / (float)(2 * hp);
+          gg = make_float2(ih * (gg.x - qn.x * dot), ih * (gg.y - qn.y * dot));
+        }
+        gm[k] = gg;
+      }
+      mesh_backward<W, T>(c, d, gm, wgs[m], A, bufs, xch, accs + m * A * T::NT);
+#pragma unroll
+      for (int k = 0; k < RPT; ++k) dn[k] = dn[k] + gm[k];
+    }
+    rmsnorm_rows_backward<T>(c, n1, inv1, dn, red, phase, W);
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) {
+      const int r = tile * T::TR + c.row(k);
+      st2(dx_out, r, d.rows, W, c.cp, ld2<T>(dxm, r, d.rows, W, c.cp) + dn[k]);
+    }
+  }
+  __syncthreads();
+  flush_partials<T>(c, accs, A, part_q);
+  flush_partials<T>(c, accs + A * T::NT, A, part_k);
+  flush_partials<T>(c, accs + 2 * A * T::NT, A, part_v);
+}
+
+// ---------------------------------------------------------------- host glue
+template <int W, int RPT>
+struct BlockKernels {
+  using T = RowTile<W, RPT>;
+  static size_t smem_forward() { return (size_t)(2 * T::BUF + 2 * T::TR * T::WPR) * sizeof(float); }
+  static size_t smem_post_backward(int A, int F) {
+    int dmax = A > F ? A : F;
+    return (size_t)(A + F) * T::NT * sizeof(float4) + (size_t)((dmax + 2) * T::BUF + 2 * T::TR * T::WPR) * sizeof(float);
+  }
+  static size_t smem_qkv_backward(int A) {
+    return (size_t)3 * A * T::NT * sizeof(float4) + (size_t)((A + 2) * T::BUF + 2 * T::TR * T::WPR) * sizeof(float);
+  }
+};
+
+}  // namespace mb

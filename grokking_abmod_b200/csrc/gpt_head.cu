@@ -1,0 +1,334 @@
+// Tied embedding mesh, vocabulary head, cross-entropy, embedding gradient,
+// gradient reduction and AdamW for Mesh GPT on sm_100a.
+//
+// Reference kernels restated: gpt_embed / gpt_embedding_transpose / gpt_head /
+// gpt_cross_entropy / gpt_head_backward (src/gpt/gpu.rs:41-56, :904-1021),
+// gpt_embedding_gradient_partials / _reduce (:1159-1218), the embedding mesh
+// forward/backward over the vocabulary (:2094-2156, :2564-2605),
+// gpt_mesh_gradient_reduce (:1126-1149) and gpt_adam (:1369-1391).
+
+#include "common.cuh"
+
+namespace mb {
+
+// ---- embedding mesh over the vocabulary: one CTA per token row, one thread
+// per channel.  acts: [A+1][V][W] (acts[0] = fixed codes).  Also writes the
+// transposed final layer Et [W][V] for coalesced head reads.
+__global__ void embedding_forward(int W, int V, int depth, int connectivity, int log2w,
+                                  const float* __restrict__ weights, float* __restrict__ acts,
+                                  float* __restrict__ et) {
+  extern __shared__ float row[];
+  const int t = blockIdx.x, ch = threadIdx.x;
+  float x = acts[(size_t)t * W + ch];
+  for (int l = 0; l < depth; ++l) {
+    row[ch] = x;
+    __syncthreads();
+    const int s = connectivity == 0 ? 1 : (1 << (l % log2w));
+    const float* w = weights + (size_t)l * 2 * W + 2 * ch;
+    float z = x * w[0] + row[(ch + s) % W] * w[1];
+    x = l + 1 != depth ? elu(z) : z;
+    acts[((size_t)(l + 1) * V + t) * W + ch] = x;
+    __syncthreads();
+  }
+  et[(size_t)ch * V + t] = x;
+}
+
+// Backward through the embedding mesh for one token row per CTA; writes the
+// per-row edge-gradient partial [V][depth][W][2] (reduced by reduce_partials).
+__global__ void embedding_backward(int W, int V, int depth, int connectivity, int log2w,
+                                   const float* __restrict__ weights, const float* __restrict__ acts,
+                                   const float* __restrict__ dE, float* __restrict__ partial) {
+  extern __shared__ float row[];
+  const int t = blockIdx.x, ch = threadIdx.x;
+  float g = dE[(size_t)t * W + ch];
+  for (int l = depth - 1; l >= 0; --l) {
+    const int s = connectivity == 0 ? 1 : (1 << (l % log2w));
+    const float* w = weights + (size_t)l * 2 * W;
+    const float* xin = acts + ((size_t)l * V + t) * W;
+    if (l + 1 != depth) g *= elu_slope(acts[((size_t)(l + 1) * V + t) * W + ch]);
+    const int nb = (ch + s) % W;
+    float* out = partial + ((size_t)t * depth + l) * 2 * W + 2 * ch;
+    out[0] = g * xin[ch];
+    out[1] = g * xin[nb];
+    row[ch] = g * w[2 * ch + 1];
+    __syncthreads();
+    const int prev = (ch - s + W) % W;
+    g = g * w[2 * ch] + row[prev];
+    __syncthreads();
+  }
+}
+
+// ---- fused head: final RMSNorm, logits = n E^T, cross-entropy, dlogits,
+// dn = dlogits E and the RMSNorm adjoint -> dx.  One CTA handles HR rows with
+// one warp per row for the row reductions.
+constexpr int kHeadRows = 16;
+constexpr int kHeadThreads = 256;
+
+__global__ void __launch_bounds__(kHeadThreads)
+    head_forward_backward(int rows, int W, int V, const float* __restrict__ x, const float* __restrict__ E,
+                          const float* __restrict__ Et, const uint32_t* __restrict__ targets,
+                          const float* __restrict__ supervised, float* __restrict__ logits_out,
+                          float* __restrict__ nf_out, float* __restrict__ dlogits_out,
+                          float* __restrict__ loss_rows, float* __restrict__ dx_out) {
+  extern __shared__ float sm[];
+  float* n = sm;                        // [HR][W]
+  float* dn = n + kHeadRows * W;        // [HR][W]
+  float* lg = dn + kHeadRows * W;       // [HR][V]
+  float* inv = lg + kHeadRows * V;      // [HR]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * kHeadRows;
+  // targets == nullptr: inference, logits only.
+  const float sup = targets != nullptr ? *supervised : 1.0f;
+  // 1. RMSNorm (heads = 1)
+  for (int rr = warp; rr < kHeadRows; rr += kHeadThreads / 32) {
+    const int r = r0 + rr;
+    float s = 0.f;
+    for (int ch = lane; ch < W; ch += 32) {
+      float v = r < rows ? x[(size_t)r * W + ch] : 0.f;
+      n[rr * W + ch] = v;
+      s += v * v;
+    }
+    s = group_sum<32>(s);
+    float iv = 1.0f / sqrtf(s / (float)W + kRmsEpsilon);
+    if (lane == 0) inv[rr] = iv;
+    for (int ch = lane; ch < W; ch += 32) {
+      float v = n[rr * W + ch] * iv;
+      n[rr * W + ch] = v;
+      if (r < rows && nf_out != nullptr) nf_out[(size_t)r * W + ch] = v;
+    }
+  }
+  __syncthreads();
+  // 2. logits
+  for (int i = threadIdx.x; i < kHeadRows * V; i += kHeadThreads) {
+    const int rr = i / V, t = i % V;
+    const float* nr = n + rr * W;
+    float acc = 0.f;
+    for (int ch = 0; ch < W; ++ch) acc += nr[ch] * __ldg(Et + (size_t)ch * V + t);
+    lg[i] = acc;
+    if (logits_out != nullptr && r0 + rr < rows) logits_out[(size_t)(r0 + rr) * V + t] = acc;
+  }
+  if (targets == nullptr) return;
+  __syncthreads();
+  // 3. cross-entropy per row (src/gpt/gpu.rs:955-994)
+  for (int rr = warp; rr < kHeadRows; rr += kHeadThreads / 32) {
+    const int r = r0 + rr;
+    float* l = lg + rr * V;
+    const uint32_t tg = r < rows ? targets[r] : kIgnoreTarget;
+    if (tg == kIgnoreTarget) {
+      for (int t = lane; t < V; t += 32) l[t] = 0.f;
+      if (lane == 0 && r < rows) loss_rows[r] = 0.f;
+    } else {
+      float m = -INFINITY;
+      for (int t = lane; t < V; t += 32) m = fmaxf(m, l[t]);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      float s = 0.f;
+      for (int t = lane; t < V; t += 32) s += expf(l[t] - m);
+      s = group_sum<32>(s);
+      const float lt = l[tg < (uint32_t)V ? tg : 0];
+      __syncwarp();
+      if (lane == 0) loss_rows[r] = logf(s) + m - lt;
+      for (int t = lane; t < V; t += 32) {
+        float p = expf(l[t] - m) / s;
+        l[t] = (p - (t == (int)tg ? 1.0f : 0.0f)) / sup;
+      }
+    }
+    __syncwarp();
+    if (r < rows)
+      for (int t = lane; t < V; t += 32) dlogits_out[(size_t)r * V + t] = l[t];
+  }
+  __syncthreads();
+  // 4. dn = dlogits E
+  for (int i = threadIdx.x; i < kHeadRows * W; i += kHeadThreads) {
+    const int rr = i / W, ch = i % W;
+    const float* l = lg + rr * V;
+    float acc = 0.f;
+    for (int t = 0; t < V; ++t) acc += l[t] * __ldg(E + (size_t)t * W + ch);
+    dn[i] = acc;
+  }
+  __syncthreads();
+  // 5. RMSNorm adjoint
+  for (int rr = warp; rr < kHeadRows; rr += kHeadThreads / 32) {
+    const int r = r0 + rr;
+    if (r >= rows) continue;
+    float s = 0.f;
+    for (int ch = lane; ch < W; ch += 32) s += dn[rr * W + ch] * n[rr * W + ch];
+    s = group_sum<32>(s) / (float)W;
+    const float iv = inv[rr];
+    for (int ch = lane; ch < W; ch += 32)
+      dx_out[(size_t)r * W + ch] = iv * (dn[rr * W + ch] - n[rr * W + ch] * s);
+  }
+}
+
+// ---- embedding gradient partials: dE[t][c] = sum_r dlogits[r][t] nf[r][c]
+// + [tok_r == t] dx0[r][c] over a chunk of rows.  Grid (W / 64, chunks);
+// 256 threads own a 4 x 4 (token, channel) patch of a 64-channel slab, for
+// V up to 64 per pass (larger vocabularies loop over token slabs).
+constexpr int kEmbChunk = 256;
+
+__global__ void __launch_bounds__(256)
+    embedding_gradient_partials(int rows, int W, int V, const uint32_t* __restrict__ tokens,
+                                const float* __restrict__ dlogits, const float* __restrict__ nf,
+                                const float* __restrict__ dx0, float* __restrict__ partial) {
+  __shared__ float sl[32][64 + 1];   // dlogits rows x tokens
+  __shared__ float sn[32][64 + 1];   // nf rows x channels
+  __shared__ float sx[32][64 + 1];   // dx0 rows x channels
+  __shared__ int stok[32];
+  const int c0 = blockIdx.x * 64;
+  const int r0 = blockIdx.y * kEmbChunk;
+  const int r1 = min(rows, r0 + kEmbChunk);
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;  // channels tx*4.., tokens ty*4..
+  for (int t0 = 0; t0 < V; t0 += 64) {
+    float acc[4][4] = {};
+    for (int rb = r0; rb < r1; rb += 32) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < 32 * 64; i += 256) {
+        const int rr = i / 64, j = i % 64;
+        const int r = rb + rr;
+        const bool ok = r < r1;
+        sl[rr][j] = ok && t0 + j < V ? dlogits[(size_t)r * V + t0 + j] : 0.f;
+        sn[rr][j] = ok && c0 + j < W ? nf[(size_t)r * W + c0 + j] : 0.f;
+        sx[rr][j] = ok && c0 + j < W ? dx0[(size_t)r * W + c0 + j] : 0.f;
+      }
+      if (threadIdx.x < 32) stok[threadIdx.x] = rb + (int)threadIdx.x < r1 ? (int)tokens[rb + threadIdx.x] : -1;
+      __syncthreads();
+      for (int rr = 0; rr < 32; ++rr) {
+        const int tok = stok[rr] - t0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float a = sl[rr][ty * 4 + i];
+          const bool hit = tok == ty * 4 + i;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            acc[i][j] += a * sn[rr][tx * 4 + j];
+            if (hit) acc[i][j] += sx[rr][tx * 4 + j];
+          }
+        }
+      }
+    }
+    for (int i = 0; i < 4; ++i) {
+      const int t = t0 + ty * 4 + i;
+      if (t >= V) continue;
+      for (int j = 0; j < 4; ++j) {
+        const int ch = c0 + tx * 4 + j;
+        if (ch < W) partial[((size_t)blockIdx.y * V + t) * W + ch] = acc[i][j];
+      }
+    }
+  }
+}
+
+// ---- deterministic reduction of per-slot partials: out[p] = sum_s part[s][p]
+// in slot order.  One job per parameter group (or the embedding adjoint).
+struct ReduceJob {
+  const float* partial;  // [slots][size]
+  float* out;            // [size]
+  int slots;
+  int size;
+};
+
+__global__ void reduce_partials(const ReduceJob* __restrict__ jobs, int njobs) {
+  const ReduceJob job = jobs[blockIdx.y];
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < job.size; p += gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < job.slots; ++k) s += job.partial[(size_t)k * job.size + p];
+    job.out[p] = s;
+  }
+}
+
+// ---- AdamW (src/gpt/gpu.rs:1369-1391) over the flat parameter buffer.  The
+// bias-correction powers accumulate in f32 on the device exactly as the
+// reference host accumulates them (src/gpt/gpu.rs:1980-1981).
+struct OptimizerState {
+  float learning_rate, weight_decay, beta1, beta2, epsilon;
+  float beta1_power, beta2_power;
+  int step;
+};
+
+// Sets this step's hyperparameters and advances the bias-correction powers
+// (beta_power *= beta in f32, once per update).
+__global__ void optimizer_set(OptimizerState* st, OptimizerState h) {
+  st->learning_rate = h.learning_rate;
+  st->weight_decay = h.weight_decay;
+  st->beta1 = h.beta1;
+  st->beta2 = h.beta2;
+  st->epsilon = h.epsilon;
+  st->beta1_power = __fmul_rn(st->beta1_power, h.beta1);
+  st->beta2_power = __fmul_rn(st->beta2_power, h.beta2);
+  st->step += 1;
+}
+
+__global__ void adamw(int n, const OptimizerState* __restrict__ st, const float* __restrict__ grad,
+                      float* __restrict__ w, float* __restrict__ m, float* __restrict__ v) {
+  const float lr = st->learning_rate, wd = st->weight_decay, b1 = st->beta1, b2 = st->beta2, eps = st->epsilon;
+  const float c1 = __fsub_rn(1.0f, st->beta1_power), c2 = __fsub_rn(1.0f, st->beta2_power);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float g = grad[i];
+    // Unfused f32 arithmetic, term by term as src/bin/mesh-gpt.rs:459-466.
+    const float mi = __fadd_rn(__fmul_rn(b1, m[i]), __fmul_rn(__fsub_rn(1.0f, b1), g));
+    const float vi = __fadd_rn(__fmul_rn(b2, v[i]), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, b2), g), g));
+    m[i] = mi;
+    v[i] = vi;
+    const float mh = __fdiv_rn(mi, c1);
+    const float vh = __fdiv_rn(vi, c2);
+    const float step = __fadd_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), __fmul_rn(wd, w[i]));
+    w[i] = __fsub_rn(w[i], __fmul_rn(lr, step));
+  }
+}
+
+// ---- batch validation and supervised count (src/gpt/config.rs:230-253), on
+// the device so device-resident batches need no host round trip.  flags bit 0:
+// token outside the vocabulary; bit 1: target outside the vocabulary; bit 2: no
+// supervised target.
+__global__ void count_supervised(int rows, int V, const uint32_t* __restrict__ tokens,
+                                 const uint32_t* __restrict__ targets, float* __restrict__ supervised,
+                                 int* __restrict__ flags) {
+  __shared__ int s_count[32];
+  __shared__ int s_flags[32];
+  int cnt = 0, fl = 0;
+  for (int i = threadIdx.x; i < rows; i += blockDim.x) {
+    const uint32_t t = tokens[i], y = targets[i];
+    if (t >= (uint32_t)V) fl |= 1;
+    if (y != kIgnoreTarget) {
+      if (y >= (uint32_t)V) fl |= 2;
+      ++cnt;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    fl |= __shfl_xor_sync(0xffffffffu, fl, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_count[threadIdx.x >> 5] = cnt;
+    s_flags[threadIdx.x >> 5] = fl;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int c = 0, f = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      c += s_count[w];
+      f |= s_flags[w];
+    }
+    if (c == 0) f |= 4;
+    *supervised = (float)(c > 0 ? c : 1);
+    *flags |= f;
+  }
+}
+
+// ---- mean cross-entropy: f64 sum of the f32 per-row losses in a fixed
+// order (the reference sums on the host in f64, src/gpt/gpu.rs:2310-2312).
+__global__ void loss_reduce(int rows, const float* __restrict__ loss_rows, const float* __restrict__ supervised,
+                            double* __restrict__ loss) {
+  __shared__ double s[1024];
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < rows; i += blockDim.x) acc += (double)loss_rows[i];
+  s[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o >= 1; o >>= 1) {
+    if ((int)threadIdx.x < o) s[threadIdx.x] += s[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *loss = s[0] / (double)(*supervised);
+}
+
+}  // namespace mb

@@ -1,0 +1,1117 @@
+// Mesh GPT executor (host C++) and its C ABI.
+//
+// Replaces SpecializedMeshGpt (src/gpt/gpu.rs:1701-2092) and its op-by-op
+// plan (src/gpt/gpu.rs:1395-1547, :2158-2607): instead of ~500 small launches
+// and a host sync per step, one training step is a fixed sequence of
+// 7*layers+10 fused kernels on one stream, captured once per batch shape as a
+// CUDA graph; the loss stays on the device until the caller reads it.
+//
+// Device layout (HBM, all FP32 unless noted):
+//   weights / adam_m / adam_v / gradient : flat [P] in the reference's layout
+//       order (embedding mesh, then per block Q, K, V, O, FFN meshes; each
+//       group layer-major with (self, neighbour) pairs) - SoA instead of the
+//       reference's AoS [w, m, v] so AdamW streams 4 coalesced arrays.
+//   embedding acts [A+1][V][W] and its transpose Et [W][V]
+//   per workspace (one per (rows, sequence) shape, up to 3 retained):
+//       x[L+1], per block Q, K, V, O, x_mid [N][W], lse2 [H][N];
+//       backward scratch dx, dO, dV(XSA), dx_mid, dQ, dK, dV [N][W],
+//       delta [H][N], head scratch nf [N][W], dlogits [N][V]; per-CTA
+//       gradient partials [slots][group size] per parameter group.
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cmath>
+#include <cstring>
+#include <deque>
+#include <memory>
+#include <mutex>
+#include <string>
+
+#include "host.h"
+
+#include "gpt_attention.cu"
+#include "gpt_blocks.cu"
+#include "gpt_head.cu"
+
+namespace mb {
+
+#define MB_CUDA(call)                                                                               \
+  do {                                                                                              \
+    cudaError_t e_ = (call);                                                                        \
+    if (e_ != cudaSuccess)                                                                          \
+      throw Error(MB_ERR_CUDA, std::string(#call) + " failed: " + cudaGetErrorString(e_));          \
+  } while (0)
+
+// ------------------------------------------------------------------ memory
+class DeviceArena {
+ public:
+  ~DeviceArena() {
+    for (void* p : ptrs_) cudaFree(p);
+  }
+  template <class T>
+  T* alloc(size_t n) {
+    void* p = nullptr;
+    const size_t bytes = n == 0 ? 16 : n * sizeof(T);
+    MB_CUDA(cudaMalloc(&p, bytes));
+    ptrs_.push_back(p);
+    bytes_ += bytes;
+    return static_cast<T*>(p);
+  }
+  size_t bytes() const { return bytes_; }
+
+ private:
+  std::vector<void*> ptrs_;
+  size_t bytes_ = 0;
+};
+
+// ------------------------------------------------- width-specialised blocks
+struct BlockOps {
+  virtual ~BlockOps() = default;
+  int row_lanes = 1, tile_rows = 1, tile_rows_bwd = 1;
+  int occ_qf = 1, occ_pf = 1, occ_pb = 1, occ_qb = 1;
+  size_t smem_f = 0, smem_pb = 0, smem_qb = 0;
+  virtual void qkv_forward(cudaStream_t s, int grid, const Dims& d, const float* x, const uint32_t* tokens,
+                           const float* emb, float* x_out, const float* wq, const float* wk, const float* wv,
+                           const float2* rope, float* q, float* k, float* v) = 0;
+  virtual void post_forward(cudaStream_t s, int grid, const Dims& d, const float* o, const float* v,
+                            const float* x, const float* wo, const float* wf, float* xm, float* xn) = 0;
+  virtual void post_backward(cudaStream_t s, int grid, const Dims& d, const float* dxn, const float* xm,
+                             const float* o, const float* v, const float* wo, const float* wf, float* dO,
+                             float* dvx, float* dxm, float* delta, float* part_o, float* part_f) = 0;
+  virtual void qkv_backward(cudaStream_t s, int grid, const Dims& d, const float* dq, const float* dk,
+                            const float* dv, const float* x, const float* dxm, const float* wq, const float* wk,
+                            const float* wv, const float2* rope, float* dx, float* pq, float* pk, float* pv) = 0;
+};
+
+constexpr int kRptForward = 8;
+constexpr int kRptBackward = 4;
+
+template <int W>
+struct BlockOpsW final : BlockOps {
+  using TF = RowTile<W, kRptForward>;
+  using TB = RowTile<W, kRptBackward>;
+  explicit BlockOpsW(int A, int F) {
+    row_lanes = TB::RL;
+    tile_rows = TF::TR;
+    tile_rows_bwd = TB::TR;
+    smem_f = BlockKernels<W, kRptForward>::smem_forward();
+    smem_pb = BlockKernels<W, kRptBackward>::smem_post_backward(A, F);
+    smem_qb = BlockKernels<W, kRptBackward>::smem_qkv_backward(A);
+    MB_CUDA(cudaFuncSetAttribute(qkv_forward_k(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_f));
+    MB_CUDA(cudaFuncSetAttribute(post_forward_k(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_f));
+    MB_CUDA(cudaFuncSetAttribute(post_backward_k(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_pb));
+    MB_CUDA(cudaFuncSetAttribute(qkv_backward_k(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_qb));
+    MB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_qf, qkv_forward_k(), TF::NT, smem_f));
+    MB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_pf, post_forward_k(), TF::NT, smem_f));
+    MB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_pb, post_backward_k(), TB::NT, smem_pb));
+    MB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_qb, qkv_backward_k(), TB::NT, smem_qb));
+    require(occ_qf > 0 && occ_pf > 0 && occ_pb > 0 && occ_qb > 0,
+            "fused block kernels do not fit on this device for these mesh depths", MB_ERR_UNSUPPORTED);
+  }
+  static auto qkv_forward_k() { return &mb::qkv_forward<W, kRptForward>; }
+  static auto post_forward_k() { return &mb::post_forward<W, kRptForward>; }
+  static auto post_backward_k() { return &mb::post_backward<W, kRptBackward>; }
+  static auto qkv_backward_k() { return &mb::qkv_backward<W, kRptBackward>; }
+  void qkv_forward(cudaStream_t s, int grid, const Dims& d, const float* x, const uint32_t* tokens,
+                   const float* emb, float* x_out, const float* wq, const float* wk, const float* wv,
+                   const float2* rope, float* q, float* k, float* v) override {
+    mb::qkv_forward<W, kRptForward><<<grid, TF::NT, smem_f, s>>>(d, x, tokens, emb, x_out, wq, wk, wv, rope, q, k, v);
+  }
+  void post_forward(cudaStream_t s, int grid, const Dims& d, const float* o, const float* v, const float* x,
+                    const float* wo, const float* wf, float* xm, float* xn) override {
+    mb::post_forward<W, kRptForward><<<grid, TF::NT, smem_f, s>>>(d, o, v, x, wo, wf, xm, xn);
+  }
+  void post_backward(cudaStream_t s, int grid, const Dims& d, const float* dxn, const float* xm, const float* o,
+                     const float* v, const float* wo, const float* wf, float* dO, float* dvx, float* dxm,
+                     float* delta, float* part_o, float* part_f) override {
+    mb::post_backward<W, kRptBackward><<<grid, TB::NT, smem_pb, s>>>(d, dxn, xm, o, v, wo, wf, dO, dvx, dxm, delta,
+                                                                     part_o, part_f);
+  }
+  void qkv_backward(cudaStream_t s, int grid, const Dims& d, const float* dq, const float* dk, const float* dv,
+                    const float* x, const float* dxm, const float* wq, const float* wk, const float* wv,
+                    const float2* rope, float* dx, float* pq, float* pk, float* pv) override {
+    mb::qkv_backward<W, kRptBackward><<<grid, TB::NT, smem_qb, s>>>(d, dq, dk, dv, x, dxm, wq, wk, wv, rope, dx, pq,
+                                                                    pk, pv);
+  }
+};
+
+std::unique_ptr<BlockOps> make_block_ops(int W, int A, int F) {
+  switch (W) {
+    case 64: return std::make_unique<BlockOpsW<64>>(A, F);
+    case 128: return std::make_unique<BlockOpsW<128>>(A, F);
+    case 256: return std::make_unique<BlockOpsW<256>>(A, F);
+    case 384: return std::make_unique<BlockOpsW<384>>(A, F);
+    case 512: return std::make_unique<BlockOpsW<512>>(A, F);
+  }
+  throw Error(MB_ERR_UNSUPPORTED, "unsupported width");
+}
+
+// ------------------------------------------------- head-width attention ops
+struct AttentionOps {
+  virtual ~AttentionOps() = default;
+  virtual void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
+                       const float* v, float* o, float* lse) = 0;
+  virtual void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q,
+                             const float* k, const float* v, const float* dout, const float* lse,
+                             const float* delta, const float* dv_add, float* dk, float* dv) = 0;
+  virtual void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
+                           const float* v, const float* dout, const float* lse, const float* delta,
+                           float* dq) = 0;
+};
+
+template <int HD>
+struct AttentionOpsD final : AttentionOps {
+  using K = AttentionKernels<HD>;
+  AttentionOpsD() {
+    MB_CUDA(cudaFuncSetAttribute(&attention_forward<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)K::smem_forward()));
+    MB_CUDA(cudaFuncSetAttribute(&attention_backward_dq<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)K::smem_dq()));
+    MB_CUDA(cudaFuncSetAttribute(&attention_backward_dkdv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)K::smem_dkdv()));
+  }
+  void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
+               const float* v, float* o, float* lse) override {
+    dim3 grid((rows + 63) / 64, H);
+    attention_forward<HD><<<grid, 256, K::smem_forward(), s>>>(rows, W, T, hd, 1.0f / sqrtf((float)hd), q, k, v, o,
+                                                                lse);
+  }
+  void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
+                     const float* v, const float* dout, const float* lse, const float* delta, const float* dv_add,
+                     float* dk, float* dv) override {
+    dim3 grid((rows + 63) / 64, H);
+    attention_backward_dkdv<HD><<<grid, 256, K::smem_dkdv(), s>>>(rows, W, T, hd, 1.0f / sqrtf((float)hd), q, k, v,
+                                                                   dout, lse, delta, dv_add, dk, dv);
+  }
+  void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
+                   const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
+    dim3 grid((rows + 63) / 64, H);
+    attention_backward_dq<HD><<<grid, 256, K::smem_dq(), s>>>(rows, W, T, hd, 1.0f / sqrtf((float)hd), q, k, v, dout,
+                                                               lse, delta, dq);
+  }
+};
+
+std::unique_ptr<AttentionOps> make_attention_ops(int hd) {
+  if (hd <= 16) return std::make_unique<AttentionOpsD<16>>();
+  if (hd <= 32) return std::make_unique<AttentionOpsD<32>>();
+  if (hd <= 64) return std::make_unique<AttentionOpsD<64>>();
+  throw Error(MB_ERR_UNSUPPORTED, "unsupported head width");
+}
+
+// ------------------------------------------------------------------- NCCL
+struct NcclApi {
+  void* handle = nullptr;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    // Reuses the NCCL already loaded by the process (e.g. torch's) when present.
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h == nullptr) return;
+    api.handle = h;
+    api.get_unique_id = (decltype(api.get_unique_id))dlsym(h, "ncclGetUniqueId");
+    api.comm_init_rank = (decltype(api.comm_init_rank))dlsym(h, "ncclCommInitRank");
+    api.all_reduce = (decltype(api.all_reduce))dlsym(h, "ncclAllReduce");
+    api.comm_destroy = (decltype(api.comm_destroy))dlsym(h, "ncclCommDestroy");
+    api.comm_abort = (decltype(api.comm_abort))dlsym(h, "ncclCommAbort");
+    api.error_string = (decltype(api.error_string))dlsym(h, "ncclGetErrorString");
+  });
+  require(api.handle != nullptr && api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy,
+          "libnccl.so.2 could not be loaded", MB_ERR_NCCL);
+  return api;
+}
+
+void nccl_check(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess)
+    throw Error(MB_ERR_NCCL, std::string(what) + " failed: " + (nccl().error_string ? nccl().error_string(r) : "?"));
+}
+
+// ---------------------------------------------------------------- workspace
+struct Workspace {
+  int rows = 0, seq = 0;
+  DeviceArena mem;
+  std::vector<float*> x;  // L + 1
+  std::vector<float*> q, k, v, o, xm, lse;
+  float *nf, *dlog, *logits, *loss_rows, *g, *dO, *dvx, *dxm, *delta, *dq, *dk, *dv, *emb_partial, *dE;
+  float* emb_mesh_partial;
+  float2* rope;
+  uint32_t *tokens, *targets;
+  float* supervised;
+  int* flags;
+  double* loss;
+  std::vector<float*> part;  // per parameter group
+  ReduceJob* d_jobs_emb;     // dE reduction
+  ReduceJob* d_jobs;         // group reductions
+  int njobs = 0, max_job = 0, emb_chunks = 0;
+  int grid_qf = 1, grid_pf = 1, grid_pb = 1, grid_qb = 1;
+  cudaGraphExec_t graph = nullptr;
+  // Kernel boundary events captured into the graph when timing is enabled:
+  // marks[i] precedes launch i, marks.back() follows the last one.
+  std::vector<cudaEvent_t> marks;
+  std::vector<std::string> mark_names;
+  ~Workspace() {
+    if (graph) cudaGraphExecDestroy(graph);
+    for (cudaEvent_t e : marks) cudaEventDestroy(e);
+  }
+};
+
+// --------------------------------------------------------------------- model
+class GptModel {
+ public:
+  GptModel(int device, const mb_gpt_config& cfg, uint64_t seed) : cfg_(cfg), device_(device) {
+    validate_kernel_shapes(cfg);
+    layout_ = make_layout(cfg);
+    int count = 0;
+    MB_CUDA(cudaGetDeviceCount(&count));
+    require(device >= 0 && device < count, "CUDA device index out of range");
+    MB_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    MB_CUDA(cudaGetDeviceProperties(&prop, device));
+    require(prop.major >= 10, "this library is built for sm_100a (B200)", MB_ERR_UNSUPPORTED);
+    sms_ = prop.multiProcessorCount;
+    MB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    blocks_ = make_block_ops(cfg.width, cfg.attention_mesh_depth, cfg.ffn_mesh_depth);
+    attention_ = make_attention_ops(cfg.width / cfg.heads);
+    const size_t P = layout_.count();
+    w_ = mem_.alloc<float>(P);
+    m_ = mem_.alloc<float>(P);
+    v_ = mem_.alloc<float>(P);
+    grad_ = mem_.alloc<float>(P);
+    const size_t VW = (size_t)cfg.vocab_size * cfg.width;
+    emb_acts_ = mem_.alloc<float>(VW * (cfg.attention_mesh_depth + 1));
+    et_ = mem_.alloc<float>(VW);
+    opt_ = mem_.alloc<OptimizerState>(1);
+    std::vector<float> codes = token_codes(cfg);
+    MB_CUDA(cudaMemcpy(emb_acts_, codes.data(), VW * sizeof(float), cudaMemcpyHostToDevice));
+    set_parameters(initial_parameters(cfg, seed));
+  }
+
+  ~GptModel() {
+    workspaces_.clear();
+    for (cudaEvent_t e : opt_marks_) cudaEventDestroy(e);
+    detach_nccl();
+    if (stream_) cudaStreamDestroy(stream_);
+  }
+
+  const mb_gpt_config& config() const { return cfg_; }
+  size_t count() const { return layout_.count(); }
+  cudaStream_t stream() const { return stream_; }
+
+  void set_parameters(const std::vector<float>& values) { set_parameters(values.data(), values.size()); }
+  void set_parameters(const float* values, size_t n) {
+    require(n == count(), "parameter count does not match GPT configuration");
+    for (size_t i = 0; i < n; ++i) require(std::isfinite(values[i]), "parameters must contain only finite values",
+                                           MB_ERR_NONFINITE);
+    MB_CUDA(cudaSetDevice(device_));
+    MB_CUDA(cudaMemcpyAsync(w_, values, n * sizeof(float), cudaMemcpyHostToDevice, stream_));
+    MB_CUDA(cudaMemsetAsync(m_, 0, n * sizeof(float), stream_));
+    MB_CUDA(cudaMemsetAsync(v_, 0, n * sizeof(float), stream_));
+    OptimizerState st{0.f, 0.f, 0.9f, 0.999f, 1e-8f, 1.0f, 1.0f, 0};
+    MB_CUDA(cudaMemcpyAsync(opt_, &st, sizeof(st), cudaMemcpyHostToDevice, stream_));
+    MB_CUDA(cudaStreamSynchronize(stream_));
+  }
+
+  void get_parameters(float* out, size_t n) {
+    require(n == count(), "parameter count does not match GPT configuration");
+    MB_CUDA(cudaSetDevice(device_));
+    MB_CUDA(cudaMemcpyAsync(out, w_, n * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    MB_CUDA(cudaStreamSynchronize(stream_));
+    for (size_t i = 0; i < n; ++i) require(std::isfinite(out[i]), "parameters must contain only finite values",
+                                           MB_ERR_NONFINITE);
+  }
+
+  // ---- host-batch entry points (validate on the host like the reference)
+  double train_step(const uint32_t* in, const uint32_t* tgt, size_t rows, size_t seq, const mb_adamw* opt) {
+    validate_optimizer(*opt);
+    validate_batch(cfg_, in, tgt, rows, seq);
+    MB_CUDA(cudaSetDevice(device_));
+    Workspace& ws = workspace(rows, seq);
+    MB_CUDA(cudaMemcpyAsync(ws.tokens, in, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    MB_CUDA(cudaMemcpyAsync(ws.targets, tgt, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    run_gradient_graph(ws);
+    allreduce_and_update(opt);
+    return read_loss(ws);
+  }
+
+  double loss_and_gradient(const uint32_t* in, const uint32_t* tgt, size_t rows, size_t seq, float* grad,
+                           size_t n) {
+    require(n == count(), "gradient length does not match GPT configuration");
+    validate_batch(cfg_, in, tgt, rows, seq);
+    MB_CUDA(cudaSetDevice(device_));
+    Workspace& ws = workspace(rows, seq);
+    MB_CUDA(cudaMemcpyAsync(ws.tokens, in, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    MB_CUDA(cudaMemcpyAsync(ws.targets, tgt, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    run_gradient_graph(ws);
+    const double loss = read_loss(ws);
+    MB_CUDA(cudaMemcpyAsync(grad, grad_, n * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    MB_CUDA(cudaStreamSynchronize(stream_));
+    for (size_t i = 0; i < n; ++i) require(std::isfinite(grad[i]), "gradients must contain only finite values",
+                                           MB_ERR_NONFINITE);
+    return loss;
+  }
+
+  double cross_entropy(const uint32_t* in, const uint32_t* tgt, size_t rows, size_t seq) {
+    validate_batch(cfg_, in, tgt, rows, seq);
+    MB_CUDA(cudaSetDevice(device_));
+    Workspace& ws = workspace(rows, seq);
+    MB_CUDA(cudaMemcpyAsync(ws.tokens, in, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    MB_CUDA(cudaMemcpyAsync(ws.targets, tgt, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    enqueue_forward(ws, true);
+    launch_loss(ws);
+    return read_loss(ws);
+  }
+
+  void logits(const uint32_t* in, size_t rows, size_t seq, float* out, bool hidden) {
+    validate_batch(cfg_, in, nullptr, rows, seq);
+    MB_CUDA(cudaSetDevice(device_));
+    Workspace& ws = workspace(rows, seq);
+    MB_CUDA(cudaMemcpyAsync(ws.tokens, in, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    enqueue_forward(ws, false);
+    const size_t n = rows * (hidden ? cfg_.width : cfg_.vocab_size);
+    MB_CUDA(cudaMemcpyAsync(out, hidden ? ws.x[cfg_.layers] : ws.logits, n * sizeof(float), cudaMemcpyDeviceToHost,
+                            stream_));
+    MB_CUDA(cudaStreamSynchronize(stream_));
+    for (size_t i = 0; i < n; ++i) require(std::isfinite(out[i]), "logits must contain only finite values",
+                                           MB_ERR_NONFINITE);
+  }
+
+  void token_embeddings(float* out, size_t n) {
+    const size_t VW = (size_t)cfg_.vocab_size * cfg_.width;
+    require(n == VW, "token embedding buffer must hold vocab * width floats");
+    MB_CUDA(cudaSetDevice(device_));
+    launch_embedding_forward();
+    MB_CUDA(cudaMemcpyAsync(out, emb_acts_ + VW * cfg_.attention_mesh_depth, VW * sizeof(float),
+                            cudaMemcpyDeviceToHost, stream_));
+    MB_CUDA(cudaStreamSynchronize(stream_));
+  }
+
+  // ---- device-batch entry point (no host synchronisation)
+  void train_step_device(const uint32_t* d_in, const uint32_t* d_tgt, size_t rows, size_t seq, const mb_adamw* opt,
+                         double* d_loss) {
+    validate_optimizer(*opt);
+    require(seq >= 1 && seq <= cfg_.context && rows >= 1 && rows % seq == 0 && rows <= 131072,
+            "tokens must form a nonempty batch of equal sequences within context and 131072 rows");
+    MB_CUDA(cudaSetDevice(device_));
+    Workspace& ws = workspace(rows, seq);
+    MB_CUDA(cudaMemcpyAsync(ws.tokens, d_in, rows * sizeof(uint32_t), cudaMemcpyDeviceToDevice, stream_));
+    MB_CUDA(cudaMemcpyAsync(ws.targets, d_tgt, rows * sizeof(uint32_t), cudaMemcpyDeviceToDevice, stream_));
+    run_gradient_graph(ws);
+    allreduce_and_update(opt);
+    if (d_loss != nullptr)
+      MB_CUDA(cudaMemcpyAsync(d_loss, ws.loss, sizeof(double), cudaMemcpyDeviceToDevice, stream_));
+    last_ = &ws;
+  }
+
+  void check() {
+    MB_CUDA(cudaSetDevice(device_));
+    MB_CUDA(cudaStreamSynchronize(stream_));
+    for (auto& w : workspaces_) {
+      int flags = 0;
+      MB_CUDA(cudaMemcpy(&flags, w->flags, sizeof(int), cudaMemcpyDeviceToHost));
+      if (flags) {
+        MB_CUDA(cudaMemset(w->flags, 0, sizeof(int)));
+        if (flags & 1) throw Error(MB_ERR_INVALID, "token ID is outside the vocabulary");
+        if (flags & 2) throw Error(MB_ERR_INVALID, "target ID is outside the vocabulary");
+        if (flags & 4) throw Error(MB_ERR_INVALID, "batch must contain at least one supervised target");
+      }
+    }
+  }
+
+  void set_timing(bool on) {
+    if (on == timing_) return;
+    timing_ = on;
+    for (auto& w : workspaces_) {  // recapture with or without boundary events
+      if (w->graph) cudaGraphExecDestroy(w->graph);
+      w->graph = nullptr;
+    }
+  }
+
+  // Per-launch durations (ms) of the most recent training step: the graph's
+  // kernels followed by the optimizer kernels.
+  std::vector<std::pair<std::string, float>> kernel_times() {
+    MB_CUDA(cudaStreamSynchronize(stream_));
+    std::vector<std::pair<std::string, float>> out;
+    require(timing_ && last_ != nullptr && last_->marks.size() > 1, "no timed step has run");
+    for (size_t i = 0; i + 1 < last_->marks.size(); ++i) {
+      float ms = 0.f;
+      MB_CUDA(cudaEventElapsedTime(&ms, last_->marks[i], last_->marks[i + 1]));
+      out.emplace_back(last_->mark_names[i], ms);
+    }
+    for (size_t i = 0; i + 1 < opt_marks_.size(); ++i) {
+      float ms = 0.f;
+      MB_CUDA(cudaEventElapsedTime(&ms, opt_marks_[i], opt_marks_[i + 1]));
+      out.emplace_back(opt_names_[i], ms);
+    }
+    return out;
+  }
+
+  size_t allocated_bytes() const {
+    size_t b = mem_.bytes();
+    for (auto& w : workspaces_) b += w->mem.bytes();
+    return b;
+  }
+
+  size_t step_launches() const {
+    // count + embedding fwd + 3 per block fwd + head + loss + 4 per block bwd
+    // (attention backward is two kernels) + embedding partials + 2 reduces +
+    // embedding bwd + optimizer advance + AdamW
+    return 1 + 1 + 3 * (size_t)cfg_.layers + 1 + 1 + 4 * (size_t)cfg_.layers + 1 + 2 + 1 + 2;
+  }
+
+  // ---- data parallelism
+  void attach_nccl(const uint8_t* id, int rank, int world) {
+    require(world >= 1 && rank >= 0 && rank < world, "invalid rank / world size");
+    detach_nccl();
+    MB_CUDA(cudaSetDevice(device_));
+    ncclUniqueId uid;
+    static_assert(sizeof(uid) == MB_NCCL_ID_BYTES, "NCCL unique id size");
+    std::memcpy(&uid, id, sizeof(uid));
+    nccl_check(nccl().comm_init_rank(&comm_, world, uid, rank), "ncclCommInitRank");
+    world_ = world;
+  }
+  void detach_nccl() {
+    if (comm_ != nullptr) {
+      cudaStreamSynchronize(stream_);
+      nccl().comm_destroy(comm_);
+      comm_ = nullptr;
+    }
+    world_ = 1;
+  }
+
+ private:
+  Workspace& workspace(size_t rows, size_t seq) {
+    for (size_t i = 0; i < workspaces_.size(); ++i) {
+      if (workspaces_[i]->rows == (int)rows && workspaces_[i]->seq == (int)seq) {
+        auto w = std::move(workspaces_[i]);
+        workspaces_.erase(workspaces_.begin() + i);
+        workspaces_.push_back(std::move(w));
+        return *workspaces_.back();
+      }
+    }
+    if (workspaces_.size() == 3) {
+      MB_CUDA(cudaStreamSynchronize(stream_));
+      if (last_ == workspaces_.front().get()) last_ = nullptr;
+      workspaces_.pop_front();
+    }
+    workspaces_.push_back(build_workspace((int)rows, (int)seq));
+    return *workspaces_.back();
+  }
+
+  Dims dims(const Workspace& ws) const {
+    Dims d;
+    d.rows = ws.rows;
+    d.sequence = ws.seq;
+    d.heads = cfg_.heads;
+    d.head_width = cfg_.width / cfg_.heads;
+    d.vocab = cfg_.vocab_size;
+    d.attn_depth = cfg_.attention_mesh_depth;
+    d.ffn_depth = cfg_.ffn_mesh_depth;
+    d.connectivity = cfg_.connectivity;
+    d.log2w = 31 - __builtin_clz(cfg_.width);
+    return d;
+  }
+
+  std::unique_ptr<Workspace> build_workspace(int rows, int seq) {
+    auto ws = std::make_unique<Workspace>();
+    ws->rows = rows;
+    ws->seq = seq;
+    const int L = cfg_.layers, H = cfg_.heads, W = cfg_.width, V = cfg_.vocab_size;
+    const size_t NW = (size_t)rows * W;
+    DeviceArena& a = ws->mem;
+    for (int b = 0; b <= L; ++b) ws->x.push_back(a.alloc<float>(NW));
+    for (int b = 0; b < L; ++b) {
+      ws->q.push_back(a.alloc<float>(NW));
+      ws->k.push_back(a.alloc<float>(NW));
+      ws->v.push_back(a.alloc<float>(NW));
+      ws->o.push_back(a.alloc<float>(NW));
+      ws->xm.push_back(a.alloc<float>(NW));
+      ws->lse.push_back(a.alloc<float>((size_t)H * rows));
+    }
+    ws->nf = a.alloc<float>(NW);
+    ws->dlog = a.alloc<float>((size_t)rows * V);
+    ws->logits = a.alloc<float>((size_t)rows * V);
+    ws->loss_rows = a.alloc<float>(rows);
+    ws->g = a.alloc<float>(NW);
+    ws->dO = a.alloc<float>(NW);
+    ws->dvx = a.alloc<float>(NW);
+    ws->dxm = a.alloc<float>(NW);
+    ws->delta = a.alloc<float>((size_t)H * rows);
+    ws->dq = a.alloc<float>(NW);
+    ws->dk = a.alloc<float>(NW);
+    ws->dv = a.alloc<float>(NW);
+    ws->emb_chunks = (rows + kEmbChunk - 1) / kEmbChunk;
+    ws->emb_partial = a.alloc<float>((size_t)ws->emb_chunks * V * W);
+    ws->dE = a.alloc<float>((size_t)V * W);
+    ws->emb_mesh_partial = a.alloc<float>((size_t)V * layout_.groups[layout_.embedding].size);
+    ws->tokens = a.alloc<uint32_t>(rows);
+    ws->targets = a.alloc<uint32_t>(rows);
+    ws->supervised = a.alloc<float>(1);
+    ws->flags = a.alloc<int>(1);
+    ws->loss = a.alloc<double>(1);
+    MB_CUDA(cudaMemset(ws->flags, 0, sizeof(int)));
+    // RoPE table [seq][hd/2] of (cos, sin), angle = pos / 10000^(i / (hd/2)),
+    // evaluated in f64 (src/gpt/gpu.rs:175-208 evaluates it in f32).
+    const int half = W / H / 2;
+    std::vector<float2> cs((size_t)seq * half);
+    for (int p = 0; p < seq; ++p)
+      for (int i = 0; i < half; ++i) {
+        const double ang = (double)p / std::pow(10000.0, (double)i / half);
+        cs[(size_t)p * half + i] = make_float2((float)std::cos(ang), (float)std::sin(ang));
+      }
+    ws->rope = a.alloc<float2>(cs.size());
+    MB_CUDA(cudaMemcpy(ws->rope, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    // Persistent grids: every SM busy, at most one tile per CTA.
+    auto grid = [&](int tile_rows, int occ) {
+      const int tiles = (rows + tile_rows - 1) / tile_rows;
+      return std::max(1, std::min(tiles, sms_ * occ));
+    };
+    ws->grid_qf = grid(blocks_->tile_rows, blocks_->occ_qf);
+    ws->grid_pf = grid(blocks_->tile_rows, blocks_->occ_pf);
+    ws->grid_pb = grid(blocks_->tile_rows_bwd, blocks_->occ_pb);
+    ws->grid_qb = grid(blocks_->tile_rows_bwd, blocks_->occ_qb);
+    const int slots_pb = ws->grid_pb * blocks_->row_lanes;
+    const int slots_qb = ws->grid_qb * blocks_->row_lanes;
+    std::vector<ReduceJob> jobs;
+    ws->part.assign(layout_.groups.size(), nullptr);
+    for (size_t gi = 0; gi < layout_.groups.size(); ++gi) {
+      const Group& g = layout_.groups[gi];
+      int slots;
+      if ((int)gi == layout_.embedding) {
+        ws->part[gi] = ws->emb_mesh_partial;
+        slots = V;
+      } else {
+        const int within = (int)((gi - 1) % 5);  // q, k, v, o, ffn
+        slots = within < 3 ? slots_qb : slots_pb;
+        ws->part[gi] = a.alloc<float>((size_t)slots * g.size);
+      }
+      jobs.push_back(ReduceJob{ws->part[gi], grad_ + g.offset, slots, (int)g.size});
+      ws->max_job = std::max(ws->max_job, (int)g.size);
+    }
+    ws->njobs = (int)jobs.size();
+    ws->d_jobs = a.alloc<ReduceJob>(jobs.size());
+    MB_CUDA(cudaMemcpy(ws->d_jobs, jobs.data(), jobs.size() * sizeof(ReduceJob), cudaMemcpyHostToDevice));
+    ReduceJob ej{ws->emb_partial, ws->dE, ws->emb_chunks, V * W};
+    ws->d_jobs_emb = a.alloc<ReduceJob>(1);
+    MB_CUDA(cudaMemcpy(ws->d_jobs_emb, &ej, sizeof(ej), cudaMemcpyHostToDevice));
+    return ws;
+  }
+
+  const float* group(int gi) const { return w_ + layout_.groups[gi].offset; }
+
+  void launch_embedding_forward() {
+    const int W = cfg_.width, V = cfg_.vocab_size;
+    embedding_forward<<<V, W, W * sizeof(float), stream_>>>(W, V, cfg_.attention_mesh_depth, cfg_.connectivity,
+                                                            31 - __builtin_clz(W), group(layout_.embedding),
+                                                            emb_acts_, et_);
+  }
+
+  const float* final_embedding() const {
+    return emb_acts_ + (size_t)cfg_.vocab_size * cfg_.width * cfg_.attention_mesh_depth;
+  }
+
+  void enqueue_forward(Workspace& ws, bool with_targets) {
+    const Dims d = dims(ws);
+    const int L = cfg_.layers, W = cfg_.width, V = cfg_.vocab_size, H = cfg_.heads;
+    mark("count_supervised");
+    if (with_targets)
+      count_supervised<<<1, 1024, 0, stream_>>>(ws.rows, V, ws.tokens, ws.targets, ws.supervised, ws.flags);
+    mark("embedding_forward");
+    launch_embedding_forward();
+    for (int b = 0; b < L; ++b) {
+      const BlockGroups& bg = layout_.blocks[b];
+      mark("qkv_forward");
+      blocks_->qkv_forward(stream_, ws.grid_qf, d, ws.x[b], b == 0 ? ws.tokens : nullptr, final_embedding(),
+                           b == 0 ? ws.x[0] : nullptr, group(bg.query), group(bg.key), group(bg.value), ws.rope,
+                           ws.q[b], ws.k[b], ws.v[b]);
+      mark("attention_forward");
+      attention_->forward(stream_, ws.rows, W, ws.seq, H, W / H, ws.q[b], ws.k[b], ws.v[b], ws.o[b], ws.lse[b]);
+      mark("post_forward");
+      blocks_->post_forward(stream_, ws.grid_pf, d, ws.o[b], ws.v[b], ws.x[b], group(bg.projection), group(bg.ffn),
+                            ws.xm[b], ws.x[b + 1]);
+    }
+    const size_t head_smem = (size_t)(2 * kHeadRows * W + kHeadRows * V + kHeadRows) * sizeof(float);
+    mark("head_forward_backward");
+    head_forward_backward<<<(ws.rows + kHeadRows - 1) / kHeadRows, kHeadThreads, head_smem, stream_>>>(
+        ws.rows, W, V, ws.x[L], final_embedding(), et_, with_targets ? ws.targets : nullptr, ws.supervised,
+        with_targets ? nullptr : ws.logits, ws.nf, ws.dlog, ws.loss_rows, ws.g);
+    MB_CUDA(cudaGetLastError());
+  }
+
+  void launch_loss(Workspace& ws) {
+    mark("loss_reduce");
+    loss_reduce<<<1, 1024, 0, stream_>>>(ws.rows, ws.loss_rows, ws.supervised, ws.loss);
+  }
+
+  void enqueue_backward(Workspace& ws) {
+    const Dims d = dims(ws);
+    const int L = cfg_.layers, W = cfg_.width, V = cfg_.vocab_size, H = cfg_.heads;
+    for (int b = L - 1; b >= 0; --b) {
+      const BlockGroups& bg = layout_.blocks[b];
+      mark("post_backward");
+      blocks_->post_backward(stream_, ws.grid_pb, d, ws.g, ws.xm[b], ws.o[b], ws.v[b], group(bg.projection),
+                             group(bg.ffn), ws.dO, ws.dvx, ws.dxm, ws.delta, ws.part[bg.projection],
+                             ws.part[bg.ffn]);
+      mark("attention_backward_dkdv");
+      attention_->backward_dkdv(stream_, ws.rows, W, ws.seq, H, W / H, ws.q[b], ws.k[b], ws.v[b], ws.dO, ws.lse[b],
+                                ws.delta, ws.dvx, ws.dk, ws.dv);
+      mark("attention_backward_dq");
+      attention_->backward_dq(stream_, ws.rows, W, ws.seq, H, W / H, ws.q[b], ws.k[b], ws.v[b], ws.dO, ws.lse[b],
+                              ws.delta, ws.dq);
+      mark("qkv_backward");
+      blocks_->qkv_backward(stream_, ws.grid_qb, d, ws.dq, ws.dk, ws.dv, ws.x[b], ws.dxm, group(bg.query),
+                            group(bg.key), group(bg.value), ws.rope, ws.g, ws.part[bg.query], ws.part[bg.key],
+                            ws.part[bg.value]);
+    }
+    // Tied embedding: input-lookup and head contributions, then the mesh.
+    dim3 eg((W + 63) / 64, ws.emb_chunks);
+    mark("embedding_gradient_partials");
+    embedding_gradient_partials<<<eg, 256, 0, stream_>>>(ws.rows, W, V, ws.tokens, ws.dlog, ws.nf, ws.g,
+                                                         ws.emb_partial);
+    mark("reduce_partials");
+    reduce_partials<<<dim3((V * W + 255) / 256, 1), 256, 0, stream_>>>(ws.d_jobs_emb, 1);
+    mark("embedding_backward");
+    embedding_backward<<<V, W, W * sizeof(float), stream_>>>(W, V, cfg_.attention_mesh_depth, cfg_.connectivity,
+                                                             31 - __builtin_clz(W), group(layout_.embedding),
+                                                             emb_acts_, ws.dE, ws.emb_mesh_partial);
+    mark("reduce_partials");
+    reduce_partials<<<dim3((ws.max_job + 255) / 256, ws.njobs), 256, 0, stream_>>>(ws.d_jobs, ws.njobs);
+    mark("end");
+    MB_CUDA(cudaGetLastError());
+  }
+
+  void run_gradient_graph(Workspace& ws) {
+    if (ws.graph == nullptr) {
+      cudaGraph_t g = nullptr;
+      for (cudaEvent_t e : ws.marks) cudaEventDestroy(e);
+      ws.marks.clear();
+      ws.mark_names.clear();
+      MB_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+      capturing_ = &ws;
+      try {
+        enqueue_forward(ws, true);
+        launch_loss(ws);
+        enqueue_backward(ws);
+      } catch (...) {
+        capturing_ = nullptr;
+        cudaStreamEndCapture(stream_, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      capturing_ = nullptr;
+      MB_CUDA(cudaStreamEndCapture(stream_, &g));
+      cudaError_t e = cudaGraphInstantiate(&ws.graph, g, 0);
+      cudaGraphDestroy(g);
+      MB_CUDA(e);
+    }
+    MB_CUDA(cudaGraphLaunch(ws.graph, stream_));
+    last_ = &ws;
+  }
+
+  void allreduce_and_update(const mb_adamw* opt) {
+    const size_t P = count();
+    auto omark = [&](size_t i, const char* name) {
+      if (!timing_) return;
+      if (opt_marks_.size() <= i) {
+        cudaEvent_t e;
+        MB_CUDA(cudaEventCreate(&e));
+        opt_marks_.push_back(e);
+        opt_names_.push_back(name);
+      }
+      MB_CUDA(cudaEventRecord(opt_marks_[i], stream_));
+    };
+    omark(0, "nccl_allreduce");
+    if (comm_ != nullptr && world_ > 1)
+      nccl_check(nccl().all_reduce(grad_, grad_, P, ncclFloat32, ncclAvg, comm_, stream_), "ncclAllReduce");
+    OptimizerState st{opt->learning_rate, opt->weight_decay, opt->beta1, opt->beta2, opt->epsilon, 0.f, 0.f, 0};
+    omark(1, "optimizer_set");
+    optimizer_set<<<1, 1, 0, stream_>>>(opt_, st);
+    const int threads = 256;
+    const int blocks = std::min((int)((P + threads - 1) / threads), sms_ * 8);
+    omark(2, "adamw");
+    adamw<<<blocks, threads, 0, stream_>>>((int)P, opt_, grad_, w_, m_, v_);
+    omark(3, "end");
+    MB_CUDA(cudaGetLastError());
+  }
+
+  double read_loss(Workspace& ws) {
+    double loss = 0.0;
+    MB_CUDA(cudaMemcpyAsync(&loss, ws.loss, sizeof(double), cudaMemcpyDeviceToHost, stream_));
+    MB_CUDA(cudaStreamSynchronize(stream_));
+    require(std::isfinite(loss), "cross-entropy must contain only finite values", MB_ERR_NONFINITE);
+    return loss;
+  }
+
+  mb_gpt_config cfg_;
+  int device_ = 0, sms_ = 1;
+  Layout layout_;
+  cudaStream_t stream_ = nullptr;
+  DeviceArena mem_;
+  std::unique_ptr<BlockOps> blocks_;
+  std::unique_ptr<AttentionOps> attention_;
+  float *w_ = nullptr, *m_ = nullptr, *v_ = nullptr, *grad_ = nullptr, *emb_acts_ = nullptr, *et_ = nullptr;
+  OptimizerState* opt_ = nullptr;
+  std::deque<std::unique_ptr<Workspace>> workspaces_;
+  Workspace* last_ = nullptr;
+  ncclComm_t comm_ = nullptr;
+  int world_ = 1;
+  bool timing_ = false;
+  Workspace* capturing_ = nullptr;
+  std::vector<cudaEvent_t> opt_marks_;
+  std::vector<std::string> opt_names_;
+
+  // Records a boundary event before the next launch (timing mode, inside
+  // graph capture only).
+  void mark(const char* name) {
+    if (!timing_ || capturing_ == nullptr) return;
+    Workspace& ws = *capturing_;
+    cudaEvent_t e;
+    MB_CUDA(cudaEventCreate(&e));
+    ws.marks.push_back(e);
+    ws.mark_names.push_back(name);
+    MB_CUDA(cudaEventRecordWithFlags(e, stream_, cudaEventRecordExternal));
+  }
+};
+
+}  // namespace mb
+
+// ================================================================== C ABI
+using mb::Error;
+
+struct mb_gpt {
+  std::unique_ptr<mb::GptModel> model;
+};
+
+namespace {
+thread_local std::string g_error;
+thread_local int g_code = MB_OK;
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    g_code = MB_OK;
+    return MB_OK;
+  } catch (const Error& e) {
+    g_error = e.what();
+    g_code = e.code;
+  } catch (const std::bad_alloc&) {
+    g_error = "host allocation failed";
+    g_code = MB_ERR_INVALID;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    g_code = MB_ERR_INVALID;
+  }
+  return g_code;
+}
+
+mb::GptModel& model_of(mb_gpt* m) {
+  mb::require(m != nullptr && m->model != nullptr, "model handle is null");
+  return *m->model;
+}
+
+void need(const void* p, const char* what) { mb::require(p != nullptr, std::string(what) + " must not be null"); }
+}  // namespace
+
+extern "C" {
+
+int mb_last_error(char* buf, size_t len) {
+  if (buf != nullptr && len > 0) {
+    std::strncpy(buf, g_error.c_str(), len - 1);
+    buf[len - 1] = '\0';
+  }
+  return g_code;
+}
+
+int mb_version(int* major, int* minor) {
+  return guarded([&] {
+    need(major, "major");
+    need(minor, "minor");
+    *major = 0;
+    *minor = 1;
+  });
+}
+
+int mb_device_count(int* count) {
+  return guarded([&] {
+    need(count, "count");
+    MB_CUDA(cudaGetDeviceCount(count));
+  });
+}
+
+int mb_gpt_validate(const mb_gpt_config* c) {
+  return guarded([&] {
+    need(c, "config");
+    mb::validate_kernel_shapes(*c);
+  });
+}
+
+int mb_gpt_parameter_count(const mb_gpt_config* c, size_t* count) {
+  return guarded([&] {
+    need(c, "config");
+    need(count, "count");
+    *count = mb::make_layout(*c).count();
+  });
+}
+
+int mb_gpt_initial_parameters(const mb_gpt_config* c, uint64_t seed, float* out, size_t count) {
+  return guarded([&] {
+    need(c, "config");
+    need(out, "out");
+    std::vector<float> p = mb::initial_parameters(*c, seed);
+    mb::require(count == p.size(), "parameter count does not match GPT configuration");
+    std::memcpy(out, p.data(), p.size() * sizeof(float));
+  });
+}
+
+int mb_gpt_token_codes(const mb_gpt_config* c, float* out, size_t count) {
+  return guarded([&] {
+    need(c, "config");
+    need(out, "out");
+    std::vector<float> codes = mb::token_codes(*c);
+    mb::require(count == codes.size(), "token code buffer must hold vocab * width floats");
+    std::memcpy(out, codes.data(), codes.size() * sizeof(float));
+  });
+}
+
+int mb_gpt_create(int device, const mb_gpt_config* c, uint64_t seed, mb_gpt** out) {
+  return guarded([&] {
+    need(c, "config");
+    need(out, "model");
+    *out = nullptr;
+    auto h = std::make_unique<mb_gpt>();
+    h->model = std::make_unique<mb::GptModel>(device, *c, seed);
+    *out = h.release();
+  });
+}
+
+int mb_gpt_destroy(mb_gpt* m) {
+  return guarded([&] { delete m; });
+}
+
+int mb_gpt_get_config(const mb_gpt* m, mb_gpt_config* c) {
+  return guarded([&] {
+    need(m, "model");
+    need(c, "config");
+    *c = m->model->config();
+  });
+}
+
+int mb_gpt_get_parameters(mb_gpt* m, float* out, size_t count) {
+  return guarded([&] {
+    need(out, "out");
+    model_of(m).get_parameters(out, count);
+  });
+}
+
+int mb_gpt_set_parameters(mb_gpt* m, const float* values, size_t count) {
+  return guarded([&] {
+    need(values, "values");
+    model_of(m).set_parameters(values, count);
+  });
+}
+
+int mb_gpt_logits(mb_gpt* m, const uint32_t* tokens, size_t rows, size_t sequence, float* out) {
+  return guarded([&] {
+    need(out, "out");
+    model_of(m).logits(tokens, rows, sequence, out, false);
+  });
+}
+
+int mb_gpt_hidden_states(mb_gpt* m, const uint32_t* tokens, size_t rows, size_t sequence, float* out) {
+  return guarded([&] {
+    need(out, "out");
+    model_of(m).logits(tokens, rows, sequence, out, true);
+  });
+}
+
+int mb_gpt_token_embeddings(mb_gpt* m, float* out, size_t count) {
+  return guarded([&] {
+    need(out, "out");
+    model_of(m).token_embeddings(out, count);
+  });
+}
+
+int mb_gpt_cross_entropy(mb_gpt* m, const uint32_t* in, const uint32_t* tgt, size_t rows, size_t sequence,
+                         double* loss) {
+  return guarded([&] {
+    need(loss, "loss");
+    need(tgt, "targets");
+    *loss = model_of(m).cross_entropy(in, tgt, rows, sequence);
+  });
+}
+
+int mb_gpt_loss_and_gradient(mb_gpt* m, const uint32_t* in, const uint32_t* tgt, size_t rows, size_t sequence,
+                             double* loss, float* gradient, size_t count) {
+  return guarded([&] {
+    need(loss, "loss");
+    need(gradient, "gradient");
+    need(tgt, "targets");
+    *loss = model_of(m).loss_and_gradient(in, tgt, rows, sequence, gradient, count);
+  });
+}
+
+int mb_gpt_train_step(mb_gpt* m, const uint32_t* in, const uint32_t* tgt, size_t rows, size_t sequence,
+                      const mb_adamw* opt, double* loss) {
+  return guarded([&] {
+    need(opt, "optimizer");
+    need(tgt, "targets");
+    const double l = model_of(m).train_step(in, tgt, rows, sequence, opt);
+    if (loss != nullptr) *loss = l;
+  });
+}
+
+int mb_gpt_train_step_device(mb_gpt* m, const uint32_t* d_in, const uint32_t* d_tgt, size_t rows, size_t sequence,
+                             const mb_adamw* opt, double* d_loss) {
+  return guarded([&] {
+    need(opt, "optimizer");
+    need(d_in, "inputs");
+    need(d_tgt, "targets");
+    model_of(m).train_step_device(d_in, d_tgt, rows, sequence, opt, d_loss);
+  });
+}
+
+int mb_gpt_check(mb_gpt* m) {
+  return guarded([&] { model_of(m).check(); });
+}
+
+int mb_gpt_stream(mb_gpt* m, void** stream) {
+  return guarded([&] {
+    need(stream, "stream");
+    *stream = (void*)model_of(m).stream();
+  });
+}
+
+int mb_gpt_allocated_device_bytes(mb_gpt* m, size_t* bytes) {
+  return guarded([&] {
+    need(bytes, "bytes");
+    *bytes = model_of(m).allocated_bytes();
+  });
+}
+
+int mb_gpt_step_launches(mb_gpt* m, size_t rows, size_t sequence, size_t* launches) {
+  return guarded([&] {
+    need(launches, "launches");
+    (void)rows;
+    (void)sequence;
+    *launches = model_of(m).step_launches();
+  });
+}
+
+int mb_gpt_set_timing(mb_gpt* m, int enable) {
+  return guarded([&] { model_of(m).set_timing(enable != 0); });
+}
+
+int mb_gpt_kernel_times(mb_gpt* m, char* names, size_t names_len, float* ms, size_t* count) {
+  return guarded([&] {
+    need(count, "count");
+    auto t = model_of(m).kernel_times();
+    std::string joined;
+    for (size_t i = 0; i < t.size(); ++i) {
+      if (i) joined += ',';
+      joined += t[i].first;
+      if (ms != nullptr && i < *count) ms[i] = t[i].second;
+    }
+    if (names != nullptr && names_len > 0) {
+      std::strncpy(names, joined.c_str(), names_len - 1);
+      names[names_len - 1] = '\0';
+    }
+    *count = t.size();
+  });
+}
+
+int mb_nccl_unique_id(uint8_t id[MB_NCCL_ID_BYTES]) {
+  return guarded([&] {
+    need(id, "id");
+    ncclUniqueId uid;
+    mb::nccl_check(mb::nccl().get_unique_id(&uid), "ncclGetUniqueId");
+    std::memcpy(id, &uid, sizeof(uid));
+  });
+}
+
+int mb_gpt_attach_nccl(mb_gpt* m, const uint8_t id[MB_NCCL_ID_BYTES], int rank, int world_size) {
+  return guarded([&] {
+    need(id, "id");
+    model_of(m).attach_nccl(id, rank, world_size);
+  });
+}
+
+int mb_gpt_detach_nccl(mb_gpt* m) {
+  return guarded([&] { model_of(m).detach_nccl(); });
+}
+
+int mb_random_units(uint64_t seed, float* out, size_t count) {
+  return guarded([&] {
+    need(out, "out");
+    mb::Random r(seed);
+    for (size_t i = 0; i < count; ++i) out[i] = r.unit();
+  });
+}
+
+int mb_equation_dataset(uint32_t modulus, uint32_t operation, double fraction, uint64_t seed,
+                        uint32_t* residue_tokens, uint32_t* train, size_t* n_train, uint32_t* valid,
+                        size_t* n_valid) {
+  return guarded([&] {
+    need(n_train, "n_train");
+    need(n_valid, "n_valid");
+    std::vector<uint32_t> res;
+    std::vector<mb::Equation> tr, va;
+    mb::equation_dataset(modulus, operation, fraction, seed, res, tr, va);
+    if (residue_tokens != nullptr) std::memcpy(residue_tokens, res.data(), res.size() * sizeof(uint32_t));
+    if (train != nullptr) {
+      mb::require(*n_train >= tr.size(), "train buffer too small");
+      std::memcpy(train, tr.data(), tr.size() * sizeof(mb::Equation));
+    }
+    if (valid != nullptr) {
+      mb::require(*n_valid >= va.size(), "validation buffer too small");
+      std::memcpy(valid, va.data(), va.size() * sizeof(mb::Equation));
+    }
+    *n_train = tr.size();
+    *n_valid = va.size();
+  });
+}
+
+int mb_equation_sampler(size_t examples, uint64_t seed, size_t batch, size_t steps, uint32_t* indices,
+                        uint32_t* sizes) {
+  return guarded([&] {
+    need(indices, "indices");
+    need(sizes, "sizes");
+    mb::require(examples >= 1 && examples <= 65536, "sampler needs 1..65536 training equations");
+    mb::require(batch >= 1 && batch <= examples && batch <= 131072 / 4, "invalid equation minibatch size");
+    std::vector<uint32_t> idx(examples);
+    for (size_t i = 0; i < examples; ++i) idx[i] = (uint32_t)i;
+    mb::Random r(seed ^ 0x6261746368657303ull);
+    mb::shuffle(idx, r);
+    size_t pos = 0, out = 0;
+    for (size_t s = 0; s < steps; ++s) {
+      if (pos == examples) {
+        mb::shuffle(idx, r);
+        pos = 0;
+      }
+      const size_t end = std::min(examples, pos + batch);
+      sizes[s] = (uint32_t)(end - pos);
+      for (size_t i = pos; i < end; ++i) indices[out++] = idx[i];
+      pos = end;
+    }
+  });
+}
+
+int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t sequences, size_t context,
+                  uint32_t vocab, double exponent, uint32_t* inputs, uint32_t* targets) {
+  return guarded([&] {
+    need(inputs, "inputs");
+    need(targets, "targets");
+    mb::zipf_batch(base_seed, rank, step, sequences, context, vocab, exponent, inputs, targets);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,240 @@
+// Row-tile engine for the Mesh GPT block kernels.
+//
+// A CTA owns a tile of TR token rows of width W.  Thread (rl, cp) owns the
+// channel pair (2cp, 2cp+1) of rows rl, rl+RL, ... (RPT rows), keeps those
+// values in registers, and exchanges neighbour channels through shared memory
+// once per mesh layer.  Per-edge weight gradients accumulate per thread (no
+// atomics) and are written as per-(CTA, row-lane) partials that a separate
+// kernel reduces in a fixed order, so every result is bitwise reproducible.
+#pragma once
+
+#include "common.cuh"
+
+namespace mb {
+
+template <int W, int RPT_>
+struct RowTile {
+  static_assert(W % 64 == 0 && W >= 64 && W <= 1024, "width must be a multiple of 64 in 64..1024");
+  static constexpr int PAIRS = W / 2;
+  static constexpr int RL = PAIRS >= 256 ? 1 : 256 / PAIRS;  // row lanes
+  static constexpr int NT = PAIRS * RL;                        // threads per CTA
+  static constexpr int RPT = RPT_;                             // rows per thread
+  static constexpr int TR = RL * RPT;                          // rows per tile
+  static constexpr int WPR = PAIRS / 32;                       // warps per row
+  static constexpr int BUF = TR * W;                           // floats per tile buffer
+};
+
+// Parameters every block kernel needs.
+struct Dims {
+  int rows;          // token rows N (a multiple of sequence)
+  int sequence;      // T
+  int heads;         // H
+  int head_width;    // W / H
+  int vocab;         // V
+  int attn_depth;    // A
+  int ffn_depth;     // F
+  int connectivity;  // 0 = neighbor (stride 1), 1 = butterfly
+  int log2w;         // floor(log2 W)
+};
+
+__device__ __forceinline__ int mesh_stride(const Dims& d, int layer) {
+  // src/gpt/config.rs:117-122
+  return d.connectivity == 0 ? 1 : (1 << (layer % d.log2w));
+}
+
+template <class T>
+struct Ctx {
+  int tid, rl, cp, lane, warp;
+  __device__ Ctx() {
+    tid = threadIdx.x;
+    rl = tid / T::PAIRS;
+    cp = tid % T::PAIRS;
+    lane = tid & 31;
+    warp = tid >> 5;
+  }
+  __device__ __forceinline__ int row(int k) const { return k * T::RL + rl; }
+};
+
+// Value pair at channels (2cp+shift, 2cp+1+shift) mod W of one shared row.
+template <int W>
+__device__ __forceinline__ float2 gather_pair(const float* srow, int cp, int shift) {
+  int c0 = 2 * cp + shift;
+  c0 = ((c0 % W) + W) % W;
+  if ((c0 & 1) == 0) return *reinterpret_cast<const float2*>(srow + c0);
+  int c1 = c0 + 1 == W ? 0 : c0 + 1;
+  return make_float2(srow[c0], srow[c1]);
+}
+
+// Full-row sums (heads = 1) of one value per owned row.  `red` holds
+// 2 * TR * WPR floats; `phase` alternates the halves so back-to-back
+// reductions need one barrier each.
+template <class T>
+__device__ __forceinline__ void row_sums(const Ctx<T>& c, float (&v)[T::RPT], float* red, int& phase) {
+#pragma unroll
+  for (int k = 0; k < T::RPT; ++k) v[k] = group_sum<32>(v[k]);
+  if constexpr (T::WPR > 1) {
+    float* r = red + phase * T::TR * T::WPR;
+    phase ^= 1;
+    const int wir = c.cp >> 5;  // warp index within the row
+    if (c.lane == 0) {
+#pragma unroll
+      for (int k = 0; k < T::RPT; ++k) r[c.row(k) * T::WPR + wir] = v[k];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < T::RPT; ++k) {
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < T::WPR; ++j) s += r[c.row(k) * T::WPR + j];
+      v[k] = s;
+    }
+  }
+}
+
+// Per-head sums over hp = head_width/2 consecutive lanes (hp a power of two <= 32).
+__device__ __forceinline__ float head_sum(float v, int hp) {
+  switch (hp) {
+    case 32: return group_sum<32>(v);
+    case 16: return group_sum<16>(v);
+    case 8: return group_sum<8>(v);
+    case 4: return group_sum<4>(v);
+    case 2: return group_sum<2>(v);
+    default: return v;
+  }
+}
+
+// One forward mesh layer over the owned rows: y = f(x[c] w0 + x[c+s] w1).
+// `buf` is a tile buffer the layer input is published into; the caller
+// guarantees no thread still reads it from an earlier phase.
+template <int W, class T>
+__device__ __forceinline__ void mesh_layer_forward(const Ctx<T>& c, float2 (&a)[T::RPT], float4 w, int stride,
+                                                   bool activated, float* buf) {
+#pragma unroll
+  for (int k = 0; k < T::RPT; ++k) *reinterpret_cast<float2*>(buf + c.row(k) * W + 2 * c.cp) = a[k];
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < T::RPT; ++k) {
+    const float* srow = buf + c.row(k) * W;
+    float2 nb;
+    if (stride == 1) {
+      int c2 = 2 * c.cp + 2 == W ? 0 : 2 * c.cp + 2;
+      nb = make_float2(a[k].y, srow[c2]);
+    } else {
+      nb = gather_pair<W>(srow, c.cp, stride);
+    }
+    float z0 = a[k].x * w.x + nb.x * w.y;
+    float z1 = a[k].y * w.z + nb.y * w.w;
+    a[k] = activated ? make_float2(elu(z0), elu(z1)) : make_float2(z0, z1);
+  }
+}
+
+// Forward through a whole mesh stack.  With `keep`, layer l's input stays in
+// bufs[l] for a later backward pass; otherwise two buffers alternate.
+template <int W, class T>
+__device__ __forceinline__ void mesh_forward(const Ctx<T>& c, const Dims& d, float2 (&a)[T::RPT],
+                                             const float4* wg, int depth, float* bufs, bool keep) {
+  for (int l = 0; l < depth; ++l) {
+    float4 w = __ldg(wg + l * T::PAIRS + c.cp);
+    float* buf = bufs + (keep ? l : (l & 1)) * T::BUF;
+    mesh_layer_forward<W, T>(c, a, w, mesh_stride(d, l), l + 1 != depth, buf);
+  }
+}
+
+// Backward through a mesh stack whose layer inputs sit in bufs[0..depth-1]
+// (written by mesh_forward with keep = true).  dy enters as the gradient of
+// the stack output and leaves as the gradient of its input.  Edge gradients
+// add into the thread's private accumulator slots acc[l * NT + tid].
+template <int W, class T>
+__device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, float2 (&dy)[T::RPT],
+                                              const float4* wg, int depth, const float* bufs, float* xch,
+                                              float4* acc) {
+  for (int l = depth - 1; l >= 0; --l) {
+    const int s = mesh_stride(d, l);
+    const float4 w = __ldg(wg + l * T::PAIRS + c.cp);
+    const float* xin = bufs + l * T::BUF;
+    const float* yout = bufs + (l + 1) * T::BUF;  // valid when l + 1 < depth
+    float* ex = xch + (l & 1) * T::BUF;
+    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < T::RPT; ++k) {
+      const int r = c.row(k);
+      float2 dz = dy[k];
+      if (l + 1 != depth) {
+        float2 y = *reinterpret_cast<const float2*>(yout + r * W + 2 * c.cp);
+        dz.x *= elu_slope(y.x);
+        dz.y *= elu_slope(y.y);
+      }
+      float2 x = *reinterpret_cast<const float2*>(xin + r * W + 2 * c.cp);
+      float2 nb = gather_pair<W>(xin + r * W, c.cp, s);
+      g.x += dz.x * x.x;
+      g.y += dz.x * nb.x;
+      g.z += dz.y * x.y;
+      g.w += dz.y * nb.y;
+      dy[k] = dz;
+      *reinterpret_cast<float2*>(ex + r * W + 2 * c.cp) = make_float2(dz.x * w.y, dz.y * w.w);
+    }
+    float4& slot = acc[l * T::NT + c.tid];
+    slot.x += g.x;
+    slot.y += g.y;
+    slot.z += g.z;
+    slot.w += g.w;
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < T::RPT; ++k) {
+      float2 t = gather_pair<W>(ex + c.row(k) * W, c.cp, -s);
+      dy[k] = make_float2(dy[k].x * w.x + t.x, dy[k].y * w.z + t.y);
+    }
+  }
+}
+
+// RMSNorm over the full row: returns normalized values and 1/rms per row.
+template <class T>
+__device__ __forceinline__ void rmsnorm_rows(const Ctx<T>& c, float2 (&x)[T::RPT], float (&inv)[T::RPT], float* red,
+                                             int& phase, int width) {
+  float s[T::RPT];
+#pragma unroll
+  for (int k = 0; k < T::RPT; ++k) s[k] = x[k].x * x[k].x + x[k].y * x[k].y;
+  row_sums<T>(c, s, red, phase);
+#pragma unroll
+  for (int k = 0; k < T::RPT; ++k) {
+    inv[k] = 1.0f / sqrtf(s[k] / (float)width + kRmsEpsilon);
+    x[k] = x[k] * inv[k];
+  }
+}
+
+// RMSNorm backward over the full row: g <- inv * (g - n * mean(g * n)).
+template <class T>
+__device__ __forceinline__ void rmsnorm_rows_backward(const Ctx<T>& c, const float2 (&n)[T::RPT],
+                                                      const float (&inv)[T::RPT], float2 (&g)[T::RPT], float* red,
+                                                      int& phase, int width) {
+  float s[T::RPT];
+#pragma unroll
+  for (int k = 0; k < T::RPT; ++k) s[k] = g[k].x * n[k].x + g[k].y * n[k].y;
+  row_sums<T>(c, s, red, phase);
+#pragma unroll
+  for (int k = 0; k < T::RPT; ++k) {
+    float m = s[k] / (float)width;
+    g[k] = make_float2(inv[k] * (g[k].x - n[k].x * m), inv[k] * (g[k].y - n[k].y * m));
+  }
+}
+
+// Slice RoPE on one owned pair of one row (split-half pairs within a head).
+// `inverse` rotates by -angle (backward).  cs: table [T][hd/2] of (cos, sin).
+__device__ __forceinline__ float2 rope_pair(float2 v, int cp, int hp, int pos, const float2* cs, bool inverse) {
+  const int j = cp % hp;  // lane within the head
+  if (hp == 1) {
+    float2 t = __ldg(cs + pos);
+    float sn = inverse ? -t.y : t.y;
+    return make_float2(v.x * t.x - v.y * sn, v.y * t.x + v.x * sn);
+  }
+  const int half = hp / 2;
+  float2 p = shfl_xor2(v, half);
+  const bool left = j < half;
+  const int i0 = left ? 2 * j : 2 * j - hp;
+  float2 t0 = __ldg(cs + pos * hp + i0);
+  float2 t1 = __ldg(cs + pos * hp + i0 + 1);
+  float sg = (left ? -1.0f : 1.0f) * (inverse ? -1.0f : 1.0f);
+  return make_float2(v.x * t0.x + sg * p.x * t0.y, v.y * t1.x + sg * p.y * t1.y);
+}
+
+}  // namespace mb

@@ -1,0 +1,168 @@
+/*
+ * meshb200.h - C ABI of the B200-native (sm_100a) Mesh GPT training hot path.
+ *
+ * This library replaces, behind plain C types, the model-level API that the
+ * reference's Rust host code calls (fxeqxmulfx/grokking_abmod):
+ *   SpecializedMeshGpt::{new, parameters, set_parameters, logits,
+ *   loss_and_gradient, train_batch_with_optimizer, token_embeddings,
+ *   hidden_states}                         src/gpt/gpu.rs:1718-2092
+ * plus the seeded data and initialisation helpers it depends on
+ * (src/mesh.rs:256-288, src/gpt/config.rs:144-591, src/gpt/grokking.rs:128-306).
+ *
+ * Conventions (mirroring the reference's error model, src/lib.rs:11):
+ *   - Every entry point returns an int status: 0 = success, < 0 = error.  The
+ *     message of the calling thread's last error is available through
+ *     mb_last_error().  Nothing aborts, traps or frees caller memory.
+ *   - Host pointers ("host") and device pointers ("device") are marked.
+ *   - Validation (shapes, token ranges, finite values, configuration limits)
+ *     happens on the host before any launch, as the reference's launch
+ *     contracts do (src/gpt/config.rs:210-253).
+ *   - A model is single-threaded: one CUDA device, one stream, like the
+ *     reference's CudaContext + default stream (src/gpt/gpu.rs:1735-1736).
+ */
+#ifndef MESHB200_H
+#define MESHB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define MB_OK 0
+#define MB_ERR_INVALID (-1)    /* invalid argument, configuration or batch */
+#define MB_ERR_CUDA (-2)       /* CUDA runtime failure */
+#define MB_ERR_NONFINITE (-3)  /* nonfinite loss, logits, gradients or parameters */
+#define MB_ERR_NCCL (-4)       /* collective failure or timeout */
+#define MB_ERR_UNSUPPORTED (-5) /* valid for the reference, outside this build's kernel shapes */
+
+#define MB_IGNORE_TARGET 0xFFFFFFFFu /* src/gpt/mod.rs:26 */
+
+/* GptConfig (src/gpt/config.rs:22-56); connectivity 0 = neighbor, 1 = butterfly.
+ * The default geometry (parity codes, token order, no normalisation) is the
+ * only embedding geometry on this path. */
+typedef struct mb_gpt_config {
+  uint32_t vocab_size;
+  uint32_t context;
+  uint32_t width;
+  uint32_t heads;
+  uint32_t layers;
+  uint32_t attention_mesh_depth;
+  uint32_t ffn_mesh_depth;
+  uint32_t connectivity;
+} mb_gpt_config;
+
+/* AdamWOptions (src/gpt/config.rs:258-295). */
+typedef struct mb_adamw {
+  float learning_rate;
+  float weight_decay;
+  float beta1;
+  float beta2;
+  float epsilon;
+} mb_adamw;
+
+typedef struct mb_gpt mb_gpt; /* opaque model handle */
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated
+ * to len) and returns its status code. */
+int mb_last_error(char* buf, size_t len);
+
+/* Library / device queries. */
+int mb_version(int* major, int* minor);
+int mb_device_count(int* count);
+
+/* ---- configuration and seeded initialisation (host only, no GPU) ---- */
+/* GptConfig::validate (src/gpt/config.rs:144-172) and the kernel-shape limits
+ * of this build (MB_ERR_UNSUPPORTED). */
+int mb_gpt_validate(const mb_gpt_config* config);
+/* Layout::count (src/gpt/config.rs:358-414). */
+int mb_gpt_parameter_count(const mb_gpt_config* config, size_t* count);
+/* Layout::initialize (src/gpt/config.rs:416-459); out: host, count floats. */
+int mb_gpt_initial_parameters(const mb_gpt_config* config, uint64_t seed, float* out, size_t count);
+/* token_codes (src/gpt/config.rs:552-591); out: host, vocab*width floats. */
+int mb_gpt_token_codes(const mb_gpt_config* config, float* out, size_t count);
+
+/* ---- model (SpecializedMeshGpt, src/gpt/gpu.rs:1701-2092) ---- */
+int mb_gpt_create(int device, const mb_gpt_config* config, uint64_t seed, mb_gpt** model);
+int mb_gpt_destroy(mb_gpt* model);
+int mb_gpt_get_config(const mb_gpt* model, mb_gpt_config* config);
+/* parameters() (:1846-1853); out: host. */
+int mb_gpt_get_parameters(mb_gpt* model, float* out, size_t count);
+/* set_parameters() (:1856-1872): sets weights and resets AdamW moments/steps. */
+int mb_gpt_set_parameters(mb_gpt* model, const float* values, size_t count);
+/* logits() (:1875-1887); tokens: host [rows]; out: host [rows][vocab]. */
+int mb_gpt_logits(mb_gpt* model, const uint32_t* tokens, size_t rows, size_t sequence, float* out);
+/* hidden_states() (:2070-2092): residual stream before the final RMSNorm;
+ * out: host [rows][width]. */
+int mb_gpt_hidden_states(mb_gpt* model, const uint32_t* tokens, size_t rows, size_t sequence, float* out);
+/* token_embeddings() (:2056-2067); out: host [vocab][width]. */
+int mb_gpt_token_embeddings(mb_gpt* model, float* out, size_t count);
+/* cross_entropy() (:1915-1929): mean supervised cross-entropy. */
+int mb_gpt_cross_entropy(mb_gpt* model, const uint32_t* inputs, const uint32_t* targets, size_t rows,
+                         size_t sequence, double* loss);
+/* loss_and_gradient() (:1932-1946); gradient: host [parameter_count]. */
+int mb_gpt_loss_and_gradient(mb_gpt* model, const uint32_t* inputs, const uint32_t* targets, size_t rows,
+                             size_t sequence, double* loss, float* gradient, size_t count);
+/* train_batch_with_optimizer() (:1971-2004): one AdamW step on host batches,
+ * returning the mean cross-entropy before the update. */
+int mb_gpt_train_step(mb_gpt* model, const uint32_t* inputs, const uint32_t* targets, size_t rows,
+                      size_t sequence, const mb_adamw* optimizer, double* loss);
+/* The same step on device-resident batches, enqueued on the model's stream
+ * without a host synchronisation (captured as a CUDA graph per batch shape).
+ * d_loss: device double written when the step completes; may be NULL.  Bad
+ * tokens/targets are reported by mb_gpt_check() after the step. */
+int mb_gpt_train_step_device(mb_gpt* model, const uint32_t* d_inputs, const uint32_t* d_targets, size_t rows,
+                             size_t sequence, const mb_adamw* optimizer, double* d_loss);
+/* Waits for the model's stream and reports device-side batch errors. */
+int mb_gpt_check(mb_gpt* model);
+/* The model's CUDA stream (cudaStream_t) for callers that order work on it. */
+int mb_gpt_stream(mb_gpt* model, void** stream);
+/* Device bytes owned by the model (allocated_device_bytes(), :1808-1844). */
+int mb_gpt_allocated_device_bytes(mb_gpt* model, size_t* bytes);
+/* Number of kernel launches one training step enqueues (diagnostics). */
+int mb_gpt_step_launches(mb_gpt* model, size_t rows, size_t sequence, size_t* launches);
+
+/* Kernel timing (diagnostics, no reference counterpart): with enable != 0
+ * the step graphs are recaptured with CUDA events between launches.
+ * mb_gpt_kernel_times writes the comma-separated launch names and per-launch
+ * milliseconds of the most recent training step (*count in: capacity of ms,
+ * out: number of launches). */
+int mb_gpt_set_timing(mb_gpt* model, int enable);
+int mb_gpt_kernel_times(mb_gpt* model, char* names, size_t names_len, float* ms, size_t* count);
+
+/* ---- data parallelism (no reference counterpart: the reference is single
+ * GPU).  Every rank holds the full model; train_step all-reduces (average)
+ * the flat FP32 gradient over NCCL before AdamW, so ranks stay identical. ---- */
+#define MB_NCCL_ID_BYTES 128
+int mb_nccl_unique_id(uint8_t id[MB_NCCL_ID_BYTES]);
+int mb_gpt_attach_nccl(mb_gpt* model, const uint8_t id[MB_NCCL_ID_BYTES], int rank, int world_size);
+int mb_gpt_detach_nccl(mb_gpt* model);
+
+/* ---- seeded data (src/mesh.rs:256-288, src/gpt/grokking.rs:128-306) ---- */
+/* SplitMix64 Random::unit() draws (f32). */
+int mb_random_units(uint64_t seed, float* out, size_t count);
+/* EquationDataset::new: operation 0=add 1=mul 2=sub 3=div 4=mixed
+ * 5=square-sum 6=quadratic 7=quadratic-linear 8=cubic-product 9=cubic-mixed.
+ * Writes the residue permutation (modulus u32) and the split as
+ * (a, b, answer) triples; sizes are returned through *n_train / *n_valid
+ * (call with NULL arrays to query them). */
+int mb_equation_dataset(uint32_t modulus, uint32_t operation, double train_fraction, uint64_t seed,
+                        uint32_t* residue_tokens, uint32_t* train, size_t* n_train, uint32_t* valid,
+                        size_t* n_valid);
+/* EquationSampler (src/gpt/grokking.rs:274-306): writes the index sequence
+ * of `steps` successive sample(batch) calls; sizes[i] = rows of call i. */
+int mb_equation_sampler(size_t examples, uint64_t seed, size_t batch, size_t steps, uint32_t* indices,
+                        uint32_t* sizes);
+/* Zipf(s) token streams of the benchmark: `sequences` streams of context+1
+ * tokens from Random(base_seed + 1000003*rank + step); inputs and targets are
+ * host [sequences*context]. */
+int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t sequences, size_t context,
+                  uint32_t vocab, double exponent, uint32_t* inputs, uint32_t* targets);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MESHB200_H */

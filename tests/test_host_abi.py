@@ -1,0 +1,119 @@
+"""The C ABI library on the host (no GPU): it loads, exports every entry point
+that include/meshb200.h declares, and its host-side generators (seeded
+initialisation, token codes, equation datasets, sampler, Zipf streams)
+reproduce the oracle bit for bit."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from grokking_abmod_b200 import GptConfig, MeshError, UnsupportedShape, initial_parameters, parameter_count, \
+    token_codes
+from grokking_abmod_b200 import _lib
+from grokking_abmod_b200.data import EquationDataset, EquationSampler, random_units, zipf_batch
+from oracle import data as odata
+from oracle import gpt_config as ocfg
+from oracle.rng import Random
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "meshb200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^int (mb_\w+)\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_entry_point():
+    lib = _lib.load()
+    names = declared_symbols()
+    assert len(names) >= 25
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures must cover the header exactly"
+
+
+def test_version_and_errors():
+    lib = _lib.load()
+    a, b = ctypes.c_int(), ctypes.c_int()
+    assert lib.mb_version(ctypes.byref(a), ctypes.byref(b)) == 0
+    assert lib.mb_version(None, None) == _lib.MB_ERR_INVALID
+    buf = ctypes.create_string_buffer(256)
+    assert lib.mb_last_error(buf, 256) == _lib.MB_ERR_INVALID
+    assert b"must not be null" in buf.value
+
+
+def _pairs():
+    yield ocfg.GptConfig(), GptConfig()
+    for kw in (dict(vocab_size=64, context=256, width=256, heads=4, layers=4),
+               dict(vocab_size=99, context=4, width=128),
+               dict(vocab_size=7, context=5, width=8, heads=2, layers=2, attention_mesh_depth=3, ffn_mesh_depth=4,
+                    connectivity="butterfly"),
+               dict(vocab_size=129, width=2, heads=1, layers=1, attention_mesh_depth=2, ffn_mesh_depth=2)):
+        yield ocfg.GptConfig(**kw), GptConfig(**kw)
+
+
+def test_initial_parameters_and_codes_match_oracle_bitwise():
+    for oc, pc in _pairs():
+        assert parameter_count(pc) == ocfg.Layout(oc).count()
+        for seed in (0, 7, 11, 2**63 + 5):
+            a = initial_parameters(pc, seed)
+            b = ocfg.Layout(oc).initialize(seed)
+            assert a.tobytes() == b.tobytes()
+        assert token_codes(pc).tobytes() == ocfg.token_codes(oc).tobytes()
+
+
+def test_config_validation_and_unsupported_shapes():
+    with pytest.raises(MeshError):
+        parameter_count(GptConfig(heads=3))
+    with pytest.raises(MeshError):
+        parameter_count(GptConfig(layers=65))
+    lib = _lib.load()
+    c = GptConfig(width=8, heads=2).to_c()
+    assert lib.mb_gpt_validate(ctypes.byref(c)) == _lib.MB_ERR_UNSUPPORTED
+    c = GptConfig(vocab_size=64, width=512, heads=8, context=1024, layers=8).to_c()
+    assert lib.mb_gpt_validate(ctypes.byref(c)) == 0
+
+
+def test_random_units_match_splitmix():
+    r = Random(12345)
+    expected = np.array([r.unit() for _ in range(1000)], dtype=np.float32)
+    assert random_units(12345, 1000).tobytes() == expected.tobytes()
+
+
+def test_equation_dataset_matches_oracle():
+    for p, op, frac, seed in ((97, "add", 0.5, 7), (97, "div", 0.5, 11), (7, "mixed", 0.3, 3),
+                              (13, "cubic-mixed", 0.7, 99)):
+        a = EquationDataset(p, op, frac, seed)
+        b = odata.EquationDataset(p, op, frac, seed)
+        assert list(a.residue_tokens) == b.residue_tokens
+        assert [tuple(r) for r in a.training] == b.training
+        assert [tuple(r) for r in a.validation] == b.validation
+        idx = list(range(min(50, len(b.training))))
+        xa, ya = a.batch(False, idx)
+        xb, yb = b.batch(False, idx)
+        assert np.array_equal(xa, xb) and np.array_equal(ya, yb)
+    with pytest.raises(MeshError):
+        EquationDataset(4, "add", 0.5, 7)
+    with pytest.raises(MeshError):
+        EquationDataset(7, "add", 1.0, 7)
+
+
+def test_sampler_matches_oracle():
+    a = EquationSampler(25, 7)
+    b = odata.EquationSampler(25, 7)
+    for _ in range(7):
+        assert list(a.sample(12)) == b.sample(12)
+    a = EquationSampler(4704, 7).take(512, 12)
+    b = odata.EquationSampler(4704, 7)
+    for got in a:
+        assert list(got) == b.sample(512)
+
+
+def test_zipf_matches_oracle():
+    for seed, rank, step in ((7, 0, 0), (7, 3, 5), (123, 1, 99)):
+        xa, ya = zipf_batch(seed, rank, step, 3, 17)
+        xb, yb = odata.zipf_batch(seed, rank, step, 3, 17)
+        assert np.array_equal(xa, xb) and np.array_equal(ya, yb)
