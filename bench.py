@@ -37,6 +37,10 @@ CONFIGS = {
     # A=4, F=6 (reference defaults), Zipf(1.1) tokens over vocab 64.
     "cfg4": dict(vocab_size=64, context=1024, width=512, heads=8, layers=8, attention_mesh_depth=4,
                  ffn_mesh_depth=6, sequences=32),
+    # cfg4 model and context with 8 sequences (8192 rows, ~1.3 GB on the
+    # device): the small case for ncu section captures of the cfg4 kernels.
+    "cfg4s": dict(vocab_size=64, context=1024, width=512, heads=8, layers=8, attention_mesh_depth=4,
+                  ffn_mesh_depth=6, sequences=8),
     # W256 L4 H4 (hd 64) T256, batch 64.
     "cfg3": dict(vocab_size=64, context=256, width=256, heads=4, layers=4, attention_mesh_depth=4,
                  ffn_mesh_depth=6, sequences=64),

@@ -282,6 +282,9 @@ class GptModel {
     MB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     blocks_ = make_block_ops(cfg.width, cfg.attention_mesh_depth, cfg.ffn_mesh_depth);
     attention_ = make_attention_ops(cfg.width / cfg.heads);
+    head_smem_ = (size_t)(2 * kHeadRows * cfg.width + kHeadRows * cfg.vocab_size + kHeadRows) * sizeof(float);
+    MB_CUDA(cudaFuncSetAttribute(&head_forward_backward, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)head_smem_));
     const size_t P = layout_.count();
     w_ = mem_.alloc<float>(P);
     m_ = mem_.alloc<float>(P);
@@ -639,9 +642,8 @@ class GptModel {
       blocks_->post_forward(stream_, ws.grid_pf, d, ws.o[b], ws.v[b], ws.x[b], group(bg.projection), group(bg.ffn),
                             ws.xm[b], ws.x[b + 1]);
     }
-    const size_t head_smem = (size_t)(2 * kHeadRows * W + kHeadRows * V + kHeadRows) * sizeof(float);
     mark("head_forward_backward");
-    head_forward_backward<<<(ws.rows + kHeadRows - 1) / kHeadRows, kHeadThreads, head_smem, stream_>>>(
+    head_forward_backward<<<(ws.rows + kHeadRows - 1) / kHeadRows, kHeadThreads, head_smem_, stream_>>>(
         ws.rows, W, V, ws.x[L], final_embedding(), et_, with_targets ? ws.targets : nullptr, ws.supervised,
         with_targets ? nullptr : ws.logits, ws.nf, ws.dlog, ws.loss_rows, ws.g);
     MB_CUDA(cudaGetLastError());
@@ -753,6 +755,7 @@ class GptModel {
 
   mb_gpt_config cfg_;
   int device_ = 0, sms_ = 1;
+  size_t head_smem_ = 0;
   Layout layout_;
   cudaStream_t stream_ = nullptr;
   DeviceArena mem_;
