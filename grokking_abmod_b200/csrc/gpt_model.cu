@@ -798,32 +798,21 @@ namespace {
 thread_local std::string g_error;
 thread_local int g_code = MB_OK;
 
-template <class F>
-int guarded(F&& f) {
-  try {
-    f();
-    g_code = MB_OK;
-    return MB_OK;
-  } catch (const Error& e) {
-    g_error = e.what();
-    g_code = e.code;
-  } catch (const std::bad_alloc&) {
-    g_error = "host allocation failed";
-    g_code = MB_ERR_INVALID;
-  } catch (const std::exception& e) {
-    g_error = e.what();
-    g_code = MB_ERR_INVALID;
-  }
-  return g_code;
-}
+using mb::guarded;
+using mb::need;
 
 mb::GptModel& model_of(mb_gpt* m) {
   mb::require(m != nullptr && m->model != nullptr, "model handle is null");
   return *m->model;
 }
-
-void need(const void* p, const char* what) { mb::require(p != nullptr, std::string(what) + " must not be null"); }
 }  // namespace
+
+namespace mb {
+void set_last_error(int code, const char* message) {
+  g_code = code;
+  g_error = message;
+}
+}  // namespace mb
 
 extern "C" {
 

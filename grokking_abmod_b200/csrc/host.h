@@ -22,6 +22,29 @@ inline void require(bool ok, const std::string& message, int code = MB_ERR_INVAL
   if (!ok) throw Error(code, message);
 }
 
+inline void need(const void* p, const char* what) { require(p != nullptr, std::string(what) + " must not be null"); }
+
+// The calling thread's last status and message (read by mb_last_error).
+void set_last_error(int code, const char* message);
+
+// Runs an entry point body, converting exceptions into a status code.
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    set_last_error(MB_OK, "");
+    return MB_OK;
+  } catch (const Error& e) {
+    set_last_error(e.code, e.what());
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    set_last_error(MB_ERR_INVALID, "host allocation failed");
+  } catch (const std::exception& e) {
+    set_last_error(MB_ERR_INVALID, e.what());
+  }
+  return MB_ERR_INVALID;
+}
+
 // ---- SplitMix64 (src/mesh.rs:256-288)
 struct Random {
   uint64_t state;

@@ -140,6 +140,25 @@ int mb_nccl_unique_id(uint8_t id[MB_NCCL_ID_BYTES]);
 int mb_gpt_attach_nccl(mb_gpt* model, const uint8_t id[MB_NCCL_ID_BYTES], int rank, int world_size);
 int mb_gpt_detach_nccl(mb_gpt* model);
 
+/* ---- per-op entry points: device pointers, the caller's cudaStream_t (NULL =
+ * legacy default stream), no host synchronisation.  One two-parent mesh stack
+ * of `depth` layers over rows x width (ELU, alpha 1, on every layer but the
+ * last; layer l reads channels c and (c + stride_l) mod width); weights
+ * [depth][width][2] = (self, neighbour) per channel. ---- */
+/* Forward of a stack: gpt_mesh<W,0> layer by layer (src/gpt/gpu.rs:103-146,
+ * host loop :2206-2232). */
+int mb_op_mesh_forward(const float* x, float* y, size_t rows, uint32_t width, uint32_t depth,
+                       uint32_t connectivity, const float* weights, void* stream);
+/* Backward of a stack from its input x and output gradient dy: dx and the
+ * edge gradients dweights [depth][width][2] (gpt_mesh<W,1>,
+ * gpt_mesh_gradient and gpt_mesh_gradient_reduce, src/gpt/gpu.rs:103-146,
+ * :1087-1149, host loop :2371-2444).  The stack is recomputed from x.  The
+ * per-CTA gradient partials live in scratch memory taken with
+ * cudaMallocAsync on `stream` and released on it. */
+int mb_op_mesh_backward(const float* x, const float* dy, float* dx, float* dweights, size_t rows,
+                        uint32_t width, uint32_t depth, uint32_t connectivity, const float* weights,
+                        void* stream);
+
 /* ---- seeded data (src/mesh.rs:256-288, src/gpt/grokking.rs:128-306) ---- */
 /* SplitMix64 Random::unit() draws (f32). */
 int mb_random_units(uint64_t seed, float* out, size_t count);
