@@ -91,6 +91,10 @@ SIGNATURES = {
     "mb_op_mesh_backward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
                                            ctypes.c_void_p, ctypes.c_void_p]),
+    "mb_op_mesh_backward_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                   ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
+                                                   ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
+                                                   ctypes.c_void_p]),
     "mb_random_units": (ctypes.c_int, [ctypes.c_uint64, c_float_p, ctypes.c_size_t]),
     "mb_equation_dataset": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_double, ctypes.c_uint64,
                                            c_u32_p, c_u32_p, c_size_p, c_u32_p, c_size_p]),

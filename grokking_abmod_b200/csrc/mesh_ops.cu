@@ -178,6 +178,35 @@ void launch_mesh_backward(const MeshOpShape& s, int grid, const float* x, const 
   OPS_CUDA(cudaGetLastError());
 }
 
+// ---- allocation-free mesh backward
+//
+// mb_op_mesh_backward_noalloc keeps its gradient partials in this file-scope
+// device array instead of memory from cudaMalloc/cudaMallocAsync.  Every GPU
+// that loads the library holds the array (4 MiB) until the process exits.
+// Host code must not pass `g_noalloc_partials` itself to a kernel: on the host
+// that name is only a stand-in symbol, not a device address.  The address is
+// looked up once per device with cudaGetSymbolAddress (noalloc_scratch).
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;  // 4 MiB of f32
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mutex;
+float* g_noalloc_address[256] = {};
+
+// Device address of g_noalloc_partials on the current device; the first call
+// on a device looks it up (with that device current) and caches it.
+float* noalloc_scratch() {
+  int dev = 0;
+  OPS_CUDA(cudaGetDevice(&dev));
+  require(dev >= 0 && dev < 256, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_address[dev] == nullptr) {
+    void* p = nullptr;
+    OPS_CUDA(cudaGetSymbolAddress(&p, g_noalloc_partials));
+    g_noalloc_address[dev] = static_cast<float*>(p);
+  }
+  return g_noalloc_address[dev];
+}
+
 }  // namespace
 }  // namespace mb
 
@@ -224,3 +253,25 @@ int mb_op_mesh_backward(const float* x, const float* dy, float* dx, float* dweig
 }
 
 }  // extern "C"
+
+extern "C" int mb_op_mesh_backward_noalloc(const float* x, const float* dy, float* dx, float* dweights, size_t rows,
+                                           uint32_t width, uint32_t depth, uint32_t connectivity,
+                                           const float* weights, void* stream) {
+  return guarded([&] {
+    need(x, "x");
+    need(dy, "dy");
+    need(dx, "dx");
+    need(dweights, "dweights");
+    need(weights, "weights");
+    MeshOpShape s = mesh_shape(rows, width, depth, connectivity);
+    // One CTA needs row_lanes partial slots of depth*2*width floats; the grid
+    // is capped so that all its slots fit the static scratch.
+    const size_t per_cta = (size_t)s.rl * s.depth * 2 * s.W;
+    require(per_cta <= kNoAllocScratchFloats,
+            "mesh stack too large for the allocation-free scratch (row_lanes * depth * 2 * width must be <= "
+            "1048576 floats)");
+    const int cap = (int)(kNoAllocScratchFloats / per_cta);
+    const int grid = std::min(grid_for(s, s.occ_bwd), cap);
+    launch_mesh_backward(s, grid, x, dy, weights, dx, dweights, noalloc_scratch(), (cudaStream_t)stream);
+  });
+}

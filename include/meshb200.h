@@ -159,6 +159,24 @@ int mb_op_mesh_backward(const float* x, const float* dy, float* dx, float* dweig
                         uint32_t width, uint32_t depth, uint32_t connectivity, const float* weights,
                         void* stream);
 
+/* The same mesh stack backward without any allocation (no reference
+ * counterpart: the reference always allocates its workspace).  For callers
+ * that must not allocate device memory per call - a service that fixes its
+ * device memory at start-up, or a host whose own caching allocator must see
+ * every allocation - this variant keeps its gradient partials in a 4 MiB
+ * static device array that every GPU loading the library holds until exit.
+ * Limit: row_lanes * depth * 2 * width <= 1048576 floats per CTA (always true
+ * for the supported widths and depths <= 16); larger requests return
+ * MB_ERR_INVALID, and the CTA count is capped so all partials fit.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture.
+ * All calls share the array: every partial a call reads is written by the
+ * same call first, so nothing needs clearing, but calls that overlap on the
+ * GPU (other streams, other threads) race on it and must be serialised. */
+int mb_op_mesh_backward_noalloc(const float* x, const float* dy, float* dx, float* dweights, size_t rows,
+                                uint32_t width, uint32_t depth, uint32_t connectivity, const float* weights,
+                                void* stream);
+
 /* ---- seeded data (src/mesh.rs:256-288, src/gpt/grokking.rs:128-306) ---- */
 /* SplitMix64 Random::unit() draws (f32). */
 int mb_random_units(uint64_t seed, float* out, size_t count);
