@@ -13,7 +13,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmeshb200.so")
 
-SOURCES = ["gpt_model.cu", "mesh_ops.cu", "config.cpp", "data.cpp"]
+SOURCES = ["gpt_model.cu", "mesh_ops.cu", "gemm_tc.cu", "config.cpp", "data.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

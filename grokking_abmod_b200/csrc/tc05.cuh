@@ -1,0 +1,163 @@
+// Blackwell (sm_100a) tensor-core building blocks: tcgen05.mma with TF32
+// operands, TMEM allocation / loads / stores, mbarrier waits with bounded
+// spins, and the shared-memory operand layout they consume.
+//
+// FP32 accuracy from TF32 tensor cores ("3xTF32"): each FP32 operand x is
+// split into hi = rna_tf32(x) and lo = x - hi (exact in FP32), and a product
+// a.b is accumulated as hi_a.hi_b + hi_a.lo_b + lo_a.hi_b in FP32 (TMEM).
+// The dropped lo_a.lo_b term and TF32 truncation of lo leave a relative error
+// near 2^-21 per product, the level of FP32 accumulation itself.
+//
+// Operand tiles live in shared memory without swizzling, blocked into 8 x 4
+// "core matrices" of 128 contiguous bytes: element (r, c) of an R x C tile is
+// at float offset ((r / 8) * (C / 4) + c / 4) * 32 + (r % 8) * 4 + c % 4.
+// The same bytes serve as a K-major operand (rows = M or N, columns = K) and
+// as an MN-major operand (rows = K, columns = N); only the descriptor's
+// leading / stride byte offsets differ (PTX ISA, tcgen05 shared memory
+// descriptor; CUTLASS cute/arch/mma_sm100_desc.hpp documents the fields).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mb {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Float offset of element (r, c) in a blocked tile with C columns.
+__device__ __forceinline__ int blk(int r, int c, int C) { return ((r >> 3) * (C >> 2) + (c >> 2)) * 32 + (r & 7) * 4 + (c & 3); }
+
+// Shared-memory matrix descriptor, no swizzle, sm_100 version field = 1.
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+
+// K-major operand: rows = M (or N), K along columns.  Step s covers K
+// columns [8s, 8s+8) (two core matrices, 128 B apart).
+__device__ __forceinline__ uint64_t desc_kmajor(const float* tile, int C, int s) {
+  return sdesc(smem_addr(tile) + (uint32_t)s * 256u, 128u, (uint32_t)(C / 4) * 128u);
+}
+
+// MN-major operand: rows = K, N along columns.  Step s covers K rows
+// [8s, 8s+8); core matrices adjacent in N are 128 B apart.
+__device__ __forceinline__ uint64_t desc_mnmajor(const float* tile, int C, int s) {
+  return sdesc(smem_addr(tile) + (uint32_t)s * (uint32_t)(C / 4) * 128u, (uint32_t)(C / 4) * 128u, 128u);
+}
+
+// Instruction descriptor: FP32 accumulator, TF32 A and B, M x N.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D (TMEM) (+)= A (smem) * B (smem)
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// D (TMEM) (+)= A (TMEM, K-major, lane = row) * B (smem)
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// Arrives on the mbarrier once every tcgen05 operation this thread issued so
+// far has completed.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Generic-proxy shared-memory writes become visible to the tensor cores.
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void bar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+// Waits for the mbarrier phase with the given parity.  Gives up after
+// `limit` polls (returns false) so a lost arrival can never hang the GPU.
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 24)) {
+  const uint32_t a = smem_addr(bar);
+  for (uint32_t i = 0; i < limit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// TMEM allocation by one full warp; the base address lands in *dst (smem).
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols) : "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's TMEM lane (warp w reads
+// lanes 32w..32w+31; the caller adds (32w) << 16 to the address).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// TF32 hi part (round to nearest, ties away) of an FP32 value.
+__device__ __forceinline__ float tf32_hi(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+}  // namespace tc
+}  // namespace mb

@@ -44,3 +44,19 @@ def mesh_backward(x, dy, weights, connectivity: int = 0):
     check(_lib.load().mb_op_mesh_backward(_dev(x, "x"), _dev(dy, "dy"), _dev(dx, "dx"), _dev(dw, "dweights"), rows,
                                           width, depth, connectivity, _dev(weights, "weights"), _stream()))
     return dx, dw
+
+
+def gemm_tf32x3(a, b):
+    """C = A . B^T in FP32 via tcgen05 3xTF32; a [m][k], b [n][k] float32 CUDA tensors."""
+    import torch
+    m, k = a.shape
+    n, k2 = b.shape
+    if k != k2:
+        raise ValueError("inner dimensions differ")
+    c = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    status = torch.zeros(1, dtype=torch.int32, device=a.device)
+    check(_lib.load().mb_op_gemm_tf32x3(_dev(a, "a"), _dev(b, "b"), _dev(c, "c"), m, n, k,
+                                        ctypes.c_void_p(status.data_ptr()), _stream()))
+    if int(status.item()) != 0:
+        raise RuntimeError("tensor-core completion wait timed out")
+    return c
