@@ -49,9 +49,27 @@ __device__ __forceinline__ void load_split_rows(float* hi, float* lo, const floa
   }
 }
 
+// B [K][N] row-major -> hi/lo blocked tiles [BK rows][BN cols] (MN-major view).
+__device__ __forceinline__ void load_split_cols(float* hi, float* lo, const float* __restrict__ g, int k0, int K,
+                                                int n0, int N) {
+  constexpr int C4 = kGemmBN / 4;
+  for (int i = threadIdx.x; i < kGemmBK * C4; i += blockDim.x) {
+    const int rl = i & 7, c4 = (i >> 3) % C4, rh = (i >> 3) / C4;
+    const int r = rh * 8 + rl, c = c4 * 4;
+    float vv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) vv[j] = (k0 + r < K && n0 + c + j < N) ? g[(size_t)(k0 + r) * N + n0 + c + j] : 0.f;
+    const float4 v = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    const float4 h = make_float4(tc::tf32_hi(v.x), tc::tf32_hi(v.y), tc::tf32_hi(v.z), tc::tf32_hi(v.w));
+    const int off = tc::blk(r, c, kGemmBN);
+    *reinterpret_cast<float4*>(hi + off) = h;
+    *reinterpret_cast<float4*>(lo + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+  }
+}
+
 __global__ void __launch_bounds__(128, 1)
     gemm_tf32x3_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M, int N,
-                       int K, int* __restrict__ err) {
+                       int K, int mode, int* __restrict__ err) {
   extern __shared__ __align__(128) float sm[];
   float* Ah = sm;
   float* Al = Ah + kGemmBM * kGemmBK;
@@ -62,7 +80,7 @@ __global__ void __launch_bounds__(128, 1)
   __shared__ int failed;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * kGemmBN;
-  if (warp == 0) tc::tmem_alloc(&tmem_base, 64);
+  if (warp == 0) tc::tmem_alloc(&tmem_base, 128);
   if (tid == 0) {
     tc::bar_init(&bar, 1);
     tc::bar_init_fence();
@@ -72,12 +90,34 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base;
-  constexpr uint32_t idesc = tc::idesc_tf32(kGemmBM, kGemmBN, false, false);
+  const uint32_t idesc = tc::idesc_tf32(kGemmBM, kGemmBN, false, mode == 1);
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
   uint32_t phase = 0;
   const int nk = (K + kGemmBK - 1) / kGemmBK;
   for (int kb = 0; kb < nk; ++kb) {
-    load_split_rows<kGemmBM>(Ah, Al, A, m0, M, kb * kGemmBK, K);
-    load_split_rows<kGemmBN>(Bh, Bl, B, n0, N, kb * kGemmBK, K);
+    if (mode == 2) {
+      // This thread's row of the A block, split and stored to TMEM columns
+      // [64, 96) (hi) and [96, 128) (lo) of its lane.
+      float hi[16], lo[16];
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int r = m0 + tid, c = kb * kGemmBK + half * 16 + j;
+          const float x = (r < M && c < K) ? A[(size_t)r * K + c] : 0.f;
+          hi[j] = tc::tf32_hi(x);
+          lo[j] = x - hi[j];
+        }
+        tc::tmem_st16(tmem + lane_off + 64 + half * 16, hi);
+        tc::tmem_st16(tmem + lane_off + 96 + half * 16, lo);
+      }
+      tc::tmem_st_wait();
+    } else {
+      load_split_rows<kGemmBM>(Ah, Al, A, m0, M, kb * kGemmBK, K);
+    }
+    if (mode == 1)
+      load_split_cols(Bh, Bl, B, kb * kGemmBK, K, n0, N);
+    else
+      load_split_rows<kGemmBN>(Bh, Bl, B, n0, N, kb * kGemmBK, K);
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
@@ -86,10 +126,18 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
       for (int s = 0; s < kGemmBK / 8; ++s) {
         const uint64_t ah = tc::desc_kmajor(Ah, kGemmBK, s), al = tc::desc_kmajor(Al, kGemmBK, s);
-        const uint64_t bh = tc::desc_kmajor(Bh, kGemmBK, s), bl = tc::desc_kmajor(Bl, kGemmBK, s);
-        tc::mma_ss(tmem, ah, bh, idesc, (kb > 0 || s > 0) ? 1u : 0u);
-        tc::mma_ss(tmem, ah, bl, idesc, 1u);
-        tc::mma_ss(tmem, al, bh, idesc, 1u);
+        const uint64_t bh = mode == 1 ? tc::desc_mnmajor(Bh, kGemmBN, s) : tc::desc_kmajor(Bh, kGemmBK, s);
+        const uint64_t bl = mode == 1 ? tc::desc_mnmajor(Bl, kGemmBN, s) : tc::desc_kmajor(Bl, kGemmBK, s);
+        const uint32_t acc = (kb > 0 || s > 0) ? 1u : 0u;
+        if (mode == 2) {
+          tc::mma_ts(tmem, tmem + 64 + 8 * s, bh, idesc, acc);
+          tc::mma_ts(tmem, tmem + 64 + 8 * s, bl, idesc, 1u);
+          tc::mma_ts(tmem, tmem + 96 + 8 * s, bh, idesc, 1u);
+        } else {
+          tc::mma_ss(tmem, ah, bh, idesc, acc);
+          tc::mma_ss(tmem, ah, bl, idesc, 1u);
+          tc::mma_ss(tmem, al, bh, idesc, 1u);
+        }
       }
       tc::commit(&bar);
     }
@@ -118,17 +166,18 @@ __global__ void __launch_bounds__(128, 1)
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 64);
+  if (warp == 0) tc::tmem_dealloc(tmem, 128);
 }
 
 }  // namespace
 
-void launch_gemm_tf32x3(const float* A, const float* B, float* C, int M, int N, int K, int* err, cudaStream_t st) {
+void launch_gemm_tf32x3(const float* A, const float* B, float* C, int M, int N, int K, int mode, int* err,
+                        cudaStream_t st) {
   const size_t smem = (size_t)(2 * kGemmBM * kGemmBK + 2 * kGemmBN * kGemmBK) * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(&gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) throw Error(MB_ERR_CUDA, std::string("gemm attribute: ") + cudaGetErrorString(e));
   dim3 grid((M + kGemmBM - 1) / kGemmBM, (N + kGemmBN - 1) / kGemmBN);
-  gemm_tf32x3_kernel<<<grid, 128, smem, st>>>(A, B, C, M, N, K, err);
+  gemm_tf32x3_kernel<<<grid, 128, smem, st>>>(A, B, C, M, N, K, mode, err);
   e = cudaGetLastError();
   if (e != cudaSuccess) throw Error(MB_ERR_CUDA, std::string("gemm launch: ") + cudaGetErrorString(e));
 }
@@ -136,13 +185,14 @@ void launch_gemm_tf32x3(const float* A, const float* B, float* C, int M, int N, 
 }  // namespace mb
 
 extern "C" int mb_op_gemm_tf32x3(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k,
-                                 int* d_status, void* stream) {
+                                 uint32_t layout, int* d_status, void* stream) {
   return mb::guarded([&] {
     mb::need(a, "a");
     mb::need(b, "b");
     mb::need(c, "c");
     mb::need(d_status, "status");
     mb::require(m >= 1 && n >= 1 && k >= 1, "GEMM dimensions must be positive");
-    mb::launch_gemm_tf32x3(a, b, c, (int)m, (int)n, (int)k, d_status, (cudaStream_t)stream);
+    mb::require(layout <= 2, "layout must be 0 (B [n][k]), 1 (B [k][n]) or 2 (B [n][k], A through TMEM)");
+    mb::launch_gemm_tf32x3(a, b, c, (int)m, (int)n, (int)k, (int)layout, d_status, (cudaStream_t)stream);
   });
 }

@@ -32,6 +32,7 @@
 
 #include "gpt_attention.cu"
 #include "gpt_blocks.cu"
+#include "gpt_attention_tc.cu"
 #include "gpt_head.cu"
 
 namespace mb {
@@ -192,7 +193,43 @@ struct AttentionOpsD final : AttentionOps {
   }
 };
 
-std::unique_ptr<AttentionOps> make_attention_ops(int hd) {
+// Tensor-core (tcgen05, 3xTF32) attention for head widths 32 and 64.
+template <int HD>
+struct AttentionOpsTc final : AttentionOps {
+  using K = TcAtt<HD>;
+  int* err;
+  explicit AttentionOpsTc(int* e) : err(e) {
+    MB_CUDA(cudaFuncSetAttribute(&attention_forward_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)K::smem_forward));
+    MB_CUDA(cudaFuncSetAttribute(&attention_backward_dq_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)K::smem_dq));
+    MB_CUDA(cudaFuncSetAttribute(&attention_backward_dkdv_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)K::smem_dkdv));
+  }
+  void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
+               const float* v, float* o, float* lse) override {
+    dim3 grid((rows + kTcRows - 1) / kTcRows, H);
+    attention_forward_tc<HD><<<grid, 128, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, k, v, o,
+                                                                 lse, err);
+  }
+  void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
+                     const float* v, const float* dout, const float* lse, const float* delta, const float* dv_add,
+                     float* dk, float* dv) override {
+    dim3 grid((rows + kTcRows - 1) / kTcRows, H);
+    attention_backward_dkdv_tc<HD><<<grid, 128, K::smem_dkdv, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, k, v,
+                                                                    dout, lse, delta, dv_add, dk, dv, err);
+  }
+  void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
+                   const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
+    dim3 grid((rows + kTcRows - 1) / kTcRows, H);
+    attention_backward_dq_tc<HD><<<grid, 128, K::smem_dq, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, k, v, dout,
+                                                                lse, delta, dq, err);
+  }
+};
+
+std::unique_ptr<AttentionOps> make_attention_ops(int hd, int* err) {
+  if (hd == 64) return std::make_unique<AttentionOpsTc<64>>(err);
+  if (hd == 32) return std::make_unique<AttentionOpsTc<32>>(err);
   if (hd <= 16) return std::make_unique<AttentionOpsD<16>>();
   if (hd <= 32) return std::make_unique<AttentionOpsD<32>>();
   if (hd <= 64) return std::make_unique<AttentionOpsD<64>>();
@@ -281,7 +318,9 @@ class GptModel {
     sms_ = prop.multiProcessorCount;
     MB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     blocks_ = make_block_ops(cfg.width, cfg.attention_mesh_depth, cfg.ffn_mesh_depth);
-    attention_ = make_attention_ops(cfg.width / cfg.heads);
+    tc_err_ = mem_.alloc<int>(1);
+    MB_CUDA(cudaMemset(tc_err_, 0, sizeof(int)));
+    attention_ = make_attention_ops(cfg.width / cfg.heads, tc_err_);
     head_smem_ = (size_t)(2 * kHeadRows * cfg.width + kHeadRows * cfg.vocab_size + kHeadRows) * sizeof(float);
     MB_CUDA(cudaFuncSetAttribute(&head_forward_backward, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)head_smem_));
@@ -418,6 +457,12 @@ class GptModel {
   void check() {
     MB_CUDA(cudaSetDevice(device_));
     MB_CUDA(cudaStreamSynchronize(stream_));
+    int tc_err = 0;
+    MB_CUDA(cudaMemcpy(&tc_err, tc_err_, sizeof(int), cudaMemcpyDeviceToHost));
+    if (tc_err) {
+      MB_CUDA(cudaMemset(tc_err_, 0, sizeof(int)));
+      throw Error(MB_ERR_CUDA, "a tensor-core completion wait timed out; the last step's results are invalid");
+    }
     for (auto& w : workspaces_) {
       int flags = 0;
       MB_CUDA(cudaMemcpy(&flags, w->flags, sizeof(int), cudaMemcpyDeviceToHost));
@@ -763,6 +808,7 @@ class GptModel {
   std::unique_ptr<AttentionOps> attention_;
   float *w_ = nullptr, *m_ = nullptr, *v_ = nullptr, *grad_ = nullptr, *emb_acts_ = nullptr, *et_ = nullptr;
   OptimizerState* opt_ = nullptr;
+  int* tc_err_ = nullptr;
   std::deque<std::unique_ptr<Workspace>> workspaces_;
   Workspace* last_ = nullptr;
   ncclComm_t comm_ = nullptr;

@@ -46,16 +46,17 @@ def mesh_backward(x, dy, weights, connectivity: int = 0):
     return dx, dw
 
 
-def gemm_tf32x3(a, b):
-    """C = A . B^T in FP32 via tcgen05 3xTF32; a [m][k], b [n][k] float32 CUDA tensors."""
+def gemm_tf32x3(a, b, layout: int = 0):
+    """FP32 GEMM via tcgen05 3xTF32.  layout 0: C = A . B^T with b [n][k];
+    1: C = A . B with b [k][n]; 2: as 0 with A staged through tensor memory."""
     import torch
     m, k = a.shape
-    n, k2 = b.shape
+    n, k2 = (b.shape[1], b.shape[0]) if layout == 1 else b.shape
     if k != k2:
         raise ValueError("inner dimensions differ")
     c = torch.empty((m, n), dtype=torch.float32, device=a.device)
     status = torch.zeros(1, dtype=torch.int32, device=a.device)
-    check(_lib.load().mb_op_gemm_tf32x3(_dev(a, "a"), _dev(b, "b"), _dev(c, "c"), m, n, k,
+    check(_lib.load().mb_op_gemm_tf32x3(_dev(a, "a"), _dev(b, "b"), _dev(c, "c"), m, n, k, layout,
                                         ctypes.c_void_p(status.data_ptr()), _stream()))
     if int(status.item()) != 0:
         raise RuntimeError("tensor-core completion wait timed out")
