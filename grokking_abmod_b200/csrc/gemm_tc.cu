@@ -49,21 +49,19 @@ __device__ __forceinline__ void load_split_rows(float* hi, float* lo, const floa
   }
 }
 
-// B [K][N] row-major -> hi/lo blocked tiles [BK rows][BN cols] (MN-major view).
+// B [K][N] row-major -> transposed hi/lo blocked tiles [BN rows][BK cols]
+// (K-major).  An MN-major TF32 descriptor would avoid the transpose, but on
+// sm_100a TF32 MMAs with an MN-major (transposed) operand read it as zeros,
+// so every operand here is staged K-major.
 __device__ __forceinline__ void load_split_cols(float* hi, float* lo, const float* __restrict__ g, int k0, int K,
                                                 int n0, int N) {
-  constexpr int C4 = kGemmBN / 4;
-  for (int i = threadIdx.x; i < kGemmBK * C4; i += blockDim.x) {
-    const int rl = i & 7, c4 = (i >> 3) % C4, rh = (i >> 3) / C4;
-    const int r = rh * 8 + rl, c = c4 * 4;
-    float vv[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) vv[j] = (k0 + r < K && n0 + c + j < N) ? g[(size_t)(k0 + r) * N + n0 + c + j] : 0.f;
-    const float4 v = make_float4(vv[0], vv[1], vv[2], vv[3]);
-    const float4 h = make_float4(tc::tf32_hi(v.x), tc::tf32_hi(v.y), tc::tf32_hi(v.z), tc::tf32_hi(v.w));
-    const int off = tc::blk(r, c, kGemmBN);
-    *reinterpret_cast<float4*>(hi + off) = h;
-    *reinterpret_cast<float4*>(lo + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+  for (int i = threadIdx.x; i < kGemmBK * kGemmBN; i += blockDim.x) {
+    const int n = i % kGemmBN, kk = i / kGemmBN;
+    const float x = (k0 + kk < K && n0 + n < N) ? g[(size_t)(k0 + kk) * N + n0 + n] : 0.f;
+    const float h = tc::tf32_hi(x);
+    const int off = tc::blk(n, kk, kGemmBK);
+    hi[off] = h;
+    lo[off] = x - h;
   }
 }
 
@@ -90,7 +88,7 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base;
-  const uint32_t idesc = tc::idesc_tf32(kGemmBM, kGemmBN, false, mode == 1);
+  const uint32_t idesc = tc::idesc_tf32(kGemmBM, kGemmBN, false, false);
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
   uint32_t phase = 0;
   const int nk = (K + kGemmBK - 1) / kGemmBK;
@@ -126,8 +124,7 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
       for (int s = 0; s < kGemmBK / 8; ++s) {
         const uint64_t ah = tc::desc_kmajor(Ah, kGemmBK, s), al = tc::desc_kmajor(Al, kGemmBK, s);
-        const uint64_t bh = mode == 1 ? tc::desc_mnmajor(Bh, kGemmBN, s) : tc::desc_kmajor(Bh, kGemmBK, s);
-        const uint64_t bl = mode == 1 ? tc::desc_mnmajor(Bl, kGemmBN, s) : tc::desc_kmajor(Bl, kGemmBK, s);
+        const uint64_t bh = tc::desc_kmajor(Bh, kGemmBK, s), bl = tc::desc_kmajor(Bl, kGemmBK, s);
         const uint32_t acc = (kb > 0 || s > 0) ? 1u : 0u;
         if (mode == 2) {
           tc::mma_ts(tmem, tmem + 64 + 8 * s, bh, idesc, acc);

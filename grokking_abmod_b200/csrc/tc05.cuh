@@ -11,10 +11,11 @@
 // Operand tiles live in shared memory without swizzling, blocked into 8 x 4
 // "core matrices" of 128 contiguous bytes: element (r, c) of an R x C tile is
 // at float offset ((r / 8) * (C / 4) + c / 4) * 32 + (r % 8) * 4 + c % 4.
-// The same bytes serve as a K-major operand (rows = M or N, columns = K) and
-// as an MN-major operand (rows = K, columns = N); only the descriptor's
-// leading / stride byte offsets differ (PTX ISA, tcgen05 shared memory
-// descriptor; CUTLASS cute/arch/mma_sm100_desc.hpp documents the fields).
+// Tiles are K-major operands (rows = M or N, columns = K); fields per the PTX
+// ISA tcgen05 shared memory descriptor (CUTLASS cute/arch/mma_sm100_desc.hpp
+// documents them).  Operands are never given MN-major: measured on this
+// sm_100a pool, a TF32 MMA with the transpose bit set for B reads zeros, so an
+// operand needed with its rows along N is stored transposed instead.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -46,11 +47,6 @@ __device__ __forceinline__ uint64_t desc_kmajor(const float* tile, int C, int s)
   return sdesc(smem_addr(tile) + (uint32_t)s * 256u, 128u, (uint32_t)(C / 4) * 128u);
 }
 
-// MN-major operand: rows = K, N along columns.  Step s covers K rows
-// [8s, 8s+8); core matrices adjacent in N are 128 B apart.
-__device__ __forceinline__ uint64_t desc_mnmajor(const float* tile, int C, int s) {
-  return sdesc(smem_addr(tile) + (uint32_t)s * (uint32_t)(C / 4) * 128u, (uint32_t)(C / 4) * 128u, 128u);
-}
 
 // Instruction descriptor: FP32 accumulator, TF32 A and B, M x N.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn) {
