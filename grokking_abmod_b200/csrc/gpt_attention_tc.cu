@@ -8,90 +8,135 @@
 //
 // Every product runs on tcgen05.mma kind::tf32 with each FP32 operand split
 // into hi/lo TF32 parts (hi.hi + hi.lo + lo.hi), accumulated in FP32 in
-// tensor memory.  One thread per tile row: thread i of the 128-thread CTA owns
-// TMEM lane i, so score rows are read with tcgen05.ld and softmax needs no
-// shuffles.  The probability (or dS) tile is written back to TMEM as hi/lo
-// parts and used directly as the A operand of the next MMA (A from TMEM).
-// Shared-memory operand tiles use the blocked layout of tc05.cuh and are all
-// K-major: an operand needed with its rows along N (V and K as the B of
-// P.V / dS.K, Q and dO as the B of the dK / dV products) is stored
-// transposed while it is split.  Thread 0
-// issues the MMAs and commits them to an mbarrier; all waits are bounded and
-// report through `err` instead of hanging.
+// tensor memory (TMEM).
+//
+// Data movement, B200-first:
+//  * A format pass writes, per head and per tile of rows, the hi/lo parts of
+//    every shared-memory operand as contiguous UMMA-canonical tiles
+//    (tc05.cuh's blocked layout): one key tile is 8 parts x 64 rows x hd;
+//    one query tile (dK/dV) is 8 parts x 32 rows x hd plus its LSE and delta.
+//    Operands needed with rows along N are stored transposed (K-major), since
+//    TF32 MMAs read a transposed (MN-major) operand as zeros here.
+//  * A single producer thread streams each step's tile into a multi-stage
+//    shared-memory ring with cp.async.bulk (plain, no multicast); the tile
+//    arrives as mbarrier transactions.
+//  * The 128-row operand owned by the CTA (Q in the forward, Q and dO in dQ,
+//    K and V in dK/dV) is split by the compute threads into TMEM, and every
+//    MMA uses the A-from-TMEM form; score / probability tiles also live in
+//    TMEM (thread i of the compute warps owns lane i = row i).
+//  * One thread issues all MMAs and commits them to mbarriers; all waits are
+//    bounded and report through `err` instead of hanging.
 
 #include "tc05.cuh"
 
 namespace mb {
 
-constexpr int kTcRows = 128;  // tile rows = TMEM lanes
-constexpr int kTcCols = 64;   // keys per step (forward, dQ)
-constexpr int kTcQ = 32;      // queries per step (dK/dV)
+constexpr int kTcRows = 128;     // CTA tile rows = TMEM lanes
+constexpr int kTcK = 64;         // key-tile rows (forward, dQ)
+constexpr int kTcQ = 32;         // query-tile rows (dK/dV)
+constexpr int kTcThreads = 320;  // 8 compute warps + producer warp + MMA warp
+constexpr int kTcCompute = 256;  // compute threads: row = tid % 128, column half = tid / 128
+constexpr int kTcProducer = 256, kTcIssuer = 288;
 
-// Rows [r0, r0+R) of head h (columns h*hd .. h*hd+HD) -> hi/lo blocked tiles
-// with HD columns; zero outside the matrix.
-// (128 threads; every load is issued before the first split so the L2
-// latencies overlap.)
-template <int R, int HD>
-__device__ __forceinline__ void tc_load_split(float* hi, float* lo, const float* __restrict__ g, int r0, int rows,
-                                              int W, int h) {
-  constexpr int C4 = HD / 4;
-  constexpr int N = R * C4 / 128;
-  float4 v[N];
-#pragma unroll
-  for (int n = 0; n < N; ++n) {
-    const int i = threadIdx.x + n * 128;
-    const int rl = i & 7, c4 = (i >> 3) % C4, rh = (i >> 3) / C4;
-    const int r = rh * 8 + rl;
-    v[n] = r0 + r < rows ? __ldg(reinterpret_cast<const float4*>(g + (size_t)(r0 + r) * W + h * HD) + c4)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-#pragma unroll
-  for (int n = 0; n < N; ++n) {
-    const int i = threadIdx.x + n * 128;
-    const int rl = i & 7, c4 = (i >> 3) % C4, rh = (i >> 3) / C4;
-    const int r = rh * 8 + rl;
-    const float4 hv = make_float4(tc::tf32_hi(v[n].x), tc::tf32_hi(v[n].y), tc::tf32_hi(v[n].z), tc::tf32_hi(v[n].w));
-    const int off = tc::blk(r, c4 * 4, HD);
-    *reinterpret_cast<float4*>(hi + off) = hv;
-    *reinterpret_cast<float4*>(lo + off) =
-        make_float4(v[n].x - hv.x, v[n].y - hv.y, v[n].z - hv.z, v[n].w - hv.w);
+template <int HD>
+struct TcFmt {
+  static constexpr int KPART = kTcK * HD;             // floats per key-tile part
+  static constexpr int KTILE = 8 * KPART;             // K, K', Vt, Vt', V, V', Kt, Kt'
+  static constexpr int QPART = kTcQ * HD;             // floats per query-tile part
+  static constexpr int QTILE = 8 * QPART + 2 * kTcQ;  // Q, Q', dO, dO', Qt, Qt', dOt, dOt', lse2, delta
+  static constexpr int K_HI = 0, K_LO = 1, VT_HI = 2, VT_LO = 3, V_HI = 4, V_LO = 5, KT_HI = 6, KT_LO = 7;
+  static constexpr int Q_HI = 0, Q_LO = 1, D_HI = 2, D_LO = 3, QT_HI = 4, QT_LO = 5, DT_HI = 6, DT_LO = 7;
+};
+
+__device__ __forceinline__ void split_store(float* base, int part_stride, int hi_part, int off, float x) {
+  const float h = tc::tf32_hi(x);
+  base[hi_part * part_stride + off] = h;
+  base[(hi_part + 1) * part_stride + off] = x - h;
+}
+
+// Key tiles of K and V: grid (ceil(rows/64), H), 256 threads.
+template <int HD>
+__global__ void __launch_bounds__(256) attention_format_keys(int rows, int W, const float* __restrict__ k,
+                                                               const float* __restrict__ v, float* __restrict__ fmt) {
+  using F = TcFmt<HD>;
+  const int t = blockIdx.x, h = blockIdx.y;
+  float* tile = fmt + ((size_t)h * gridDim.x + t) * F::KTILE;
+  for (int i = threadIdx.x; i < kTcK * HD; i += 256) {
+    const int r = i / HD, c = i % HD, row = t * kTcK + r;
+    const float kv = row < rows ? k[(size_t)row * W + h * HD + c] : 0.f;
+    const float vv = row < rows ? v[(size_t)row * W + h * HD + c] : 0.f;
+    const int rowmajor = tc::blk(r, c, HD), transposed = tc::blk(c, r, kTcK);
+    split_store(tile, F::KPART, F::K_HI, rowmajor, kv);
+    split_store(tile, F::KPART, F::V_HI, rowmajor, vv);
+    split_store(tile, F::KPART, F::KT_HI, transposed, kv);
+    split_store(tile, F::KPART, F::VT_HI, transposed, vv);
   }
 }
 
-// Rows [r0, r0+R) of head h -> hi/lo blocked tiles of the TRANSPOSE
-// ([HD rows][R columns]); zero outside the matrix.
-template <int R, int HD>
-__device__ __forceinline__ void tc_load_split_t(float* hi, float* lo, const float* __restrict__ g, int r0, int rows,
-                                                int W, int h) {
-  constexpr int C4 = HD / 4;
-  constexpr int N = R * C4 / 128;
-  float4 v[N];
-#pragma unroll
-  for (int n = 0; n < N; ++n) {
-    const int i = threadIdx.x + n * 128;
-    const int r = i % R, c4 = i / R;
-    v[n] = r0 + r < rows ? __ldg(reinterpret_cast<const float4*>(g + (size_t)(r0 + r) * W + h * HD) + c4)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
+// Query tiles of Q and dO with their LSE and delta: grid (ceil(rows/32), H).
+template <int HD>
+__global__ void __launch_bounds__(256) attention_format_queries(int rows, int W, const float* __restrict__ q,
+                                                                  const float* __restrict__ dout,
+                                                                  const float* __restrict__ lse2,
+                                                                  const float* __restrict__ delta,
+                                                                  float* __restrict__ fmt) {
+  using F = TcFmt<HD>;
+  const int t = blockIdx.x, h = blockIdx.y;
+  float* tile = fmt + ((size_t)h * gridDim.x + t) * F::QTILE;
+  for (int i = threadIdx.x; i < kTcQ * HD; i += 256) {
+    const int r = i / HD, c = i % HD, row = t * kTcQ + r;
+    const float qv = row < rows ? q[(size_t)row * W + h * HD + c] : 0.f;
+    const float dv = row < rows ? dout[(size_t)row * W + h * HD + c] : 0.f;
+    const int rowmajor = tc::blk(r, c, HD), transposed = tc::blk(c, r, kTcQ);
+    split_store(tile, F::QPART, F::Q_HI, rowmajor, qv);
+    split_store(tile, F::QPART, F::D_HI, rowmajor, dv);
+    split_store(tile, F::QPART, F::QT_HI, transposed, qv);
+    split_store(tile, F::QPART, F::DT_HI, transposed, dv);
   }
+  if (threadIdx.x < kTcQ) {
+    const int row = t * kTcQ + threadIdx.x;
+    tile[8 * F::QPART + threadIdx.x] = row < rows ? lse2[(size_t)h * rows + row] : 0.f;
+    tile[8 * F::QPART + kTcQ + threadIdx.x] = row < rows ? delta[(size_t)h * rows + row] : 0.f;
+  }
+}
+
+// This thread's row (HD floats, row-major) split into hi/lo TMEM columns.
+template <int HD>
+__device__ __forceinline__ void row_to_tmem(const float* __restrict__ g, int row, int rows, int W, int h,
+                                            uint32_t thi, uint32_t tlo) {
 #pragma unroll
-  for (int n = 0; n < N; ++n) {
-    const int i = threadIdx.x + n * 128;
-    const int r = i % R, c4 = i / R;
-    const float x[4] = {v[n].x, v[n].y, v[n].z, v[n].w};
+  for (int c = 0; c < HD; c += 16) {
+    float hi[16], lo[16];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float hv = tc::tf32_hi(x[j]);
-      const int off = tc::blk(c4 * 4 + j, r, R);
-      hi[off] = hv;
-      lo[off] = x[j] - hv;
+    for (int e = 0; e < 16; e += 4) {
+      const float4 x = row < rows ? __ldg(reinterpret_cast<const float4*>(g + (size_t)row * W + h * HD + c + e))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        hi[e + u] = tc::tf32_hi(xs[u]);
+        lo[e + u] = xs[u] - hi[e + u];
+      }
     }
+    tc::tmem_st16(thi + c, hi);
+    tc::tmem_st16(tlo + c, lo);
   }
 }
 
-// 64 TMEM columns of this thread's lane.
-__device__ __forceinline__ void tc_ld64(uint32_t taddr, float (&v)[64]) {
-  tc::tmem_ld32(taddr, v);
-  tc::tmem_ld32(taddr + 32, v + 32);
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Named barrier over the 256 compute threads.
+__device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// NC consecutive TMEM columns of this thread's lane.
+template <int NC>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v) {
+#pragma unroll
+  for (int c = 0; c < NC; c += 32) tc::tmem_ld32(taddr + c, v + c);
 }
 
 // Stores hi/lo TF32 parts of NC values into two TMEM column ranges.
@@ -110,25 +155,11 @@ __device__ __forceinline__ void tc_st_split(uint32_t thi, uint32_t tlo, const fl
   }
 }
 
-// S (+)= A . B^T for K-major hi/lo tiles with HD columns (3 MMAs per K step).
-template <int HD>
-__device__ __forceinline__ void tc_mma_nt(uint32_t d, const float* ah, const float* al, const float* bh,
-                                          const float* bl, uint32_t idesc) {
-#pragma unroll
-  for (int s = 0; s < HD / 8; ++s) {
-    const uint64_t a_h = tc::desc_kmajor(ah, HD, s), a_l = tc::desc_kmajor(al, HD, s);
-    const uint64_t b_h = tc::desc_kmajor(bh, HD, s), b_l = tc::desc_kmajor(bl, HD, s);
-    tc::mma_ss(d, a_h, b_h, idesc, s > 0 ? 1u : 0u);
-    tc::mma_ss(d, a_h, b_l, idesc, 1u);
-    tc::mma_ss(d, a_l, b_h, idesc, 1u);
-  }
-}
-
-// D (+)= A(TMEM hi/lo, KC K columns) . B^T, B given transposed as a K-major
-// smem hi/lo tile [N rows][KC columns].
+// D (+)= A . B^T with A = hi/lo TMEM columns (KC of them, K-major) and B a
+// K-major hi/lo shared tile [N rows][KC columns]: 3 MMAs per 8-wide K step.
 template <int KC>
-__device__ __forceinline__ void tc_mma_tn(uint32_t d, uint32_t ah, uint32_t al, const float* bh, const float* bl,
-                                          uint32_t idesc, bool accumulate) {
+__device__ __forceinline__ void mma_tmem_a(uint32_t d, uint32_t ah, uint32_t al, const float* bh, const float* bl,
+                                           uint32_t idesc, bool accumulate) {
 #pragma unroll
   for (int s = 0; s < KC / 8; ++s) {
     const uint64_t b_h = tc::desc_kmajor(bh, KC, s), b_l = tc::desc_kmajor(bl, KC, s);
@@ -138,406 +169,551 @@ __device__ __forceinline__ void tc_mma_tn(uint32_t d, uint32_t ah, uint32_t al, 
   }
 }
 
+// The same over K steps [s0, s0 + NSTEP) of a B tile with KC columns (A
+// columns 8s of the TMEM ranges).
+template <int KC, int NSTEP>
+__device__ __forceinline__ void mma_tmem_a_steps(uint32_t d, uint32_t ah, uint32_t al, const float* bh,
+                                                 const float* bl, uint32_t idesc, bool accumulate, int s0) {
+#pragma unroll
+  for (int i = 0; i < NSTEP; ++i) {
+    const int s = s0 + i;
+    const uint64_t b_h = tc::desc_kmajor(bh, KC, s), b_l = tc::desc_kmajor(bl, KC, s);
+    tc::mma_ts(d, ah + 8 * s, b_h, idesc, (accumulate || i > 0) ? 1u : 0u);
+    tc::mma_ts(d, ah + 8 * s, b_l, idesc, 1u);
+    tc::mma_ts(d, al + 8 * s, b_h, idesc, 1u);
+  }
+}
+
 template <int HD>
 struct TcAtt {
-  static constexpr int BIG = kTcRows * HD;    // floats of a 128-row operand tile
-  static constexpr int SMALL = kTcCols * HD;  // floats of a 64-row operand tile
-  static constexpr int QT = kTcQ * HD;        // floats of a 32-row operand tile
-  static constexpr size_t smem_forward = (size_t)(2 * BIG + 4 * SMALL) * sizeof(float);
-  static constexpr size_t smem_dq = (size_t)(4 * BIG + 6 * SMALL) * sizeof(float);
-  static constexpr size_t smem_dkdv = (size_t)(4 * BIG + 8 * QT + 2 * kTcQ) * sizeof(float);
+  using F = TcFmt<HD>;
+  static constexpr int FWD_STAGES = 3;
+  static constexpr int FWD_STAGE = 4 * F::KPART;  // K, K', Vt, Vt'
+  static constexpr int DQ_STAGES = 2;
+  static constexpr int DQ_STAGE = 6 * F::KPART;  // K, K', V, V', Kt, Kt'
+  static constexpr int KV_STAGES = 3;
+  static constexpr int KV_STAGE = F::QTILE;  // a whole query tile
+  static constexpr size_t smem_forward = (size_t)FWD_STAGES * FWD_STAGE * sizeof(float);
+  static constexpr size_t smem_dq = (size_t)DQ_STAGES * DQ_STAGE * sizeof(float);
+  static constexpr size_t smem_dkdv = (size_t)KV_STAGES * KV_STAGE * sizeof(float);
 };
 
+struct TcShared {
+  uint32_t tmem_base;
+  int failed;
+};
+
+// Inside a role loop: a wait that gives up marks the CTA failed and leaves.
+#define TC_WAIT_OR_FAIL(bar, parity)     \
+  if (!tc::bar_wait((bar), (parity))) {  \
+    sh.failed = 1;                       \
+    break;                               \
+  }
+
 // ------------------------------------------------------------------ forward
+// Threads 0-255 compute (row r = tid % 128 owns TMEM lane r; half = tid / 128
+// takes keys [32 half, 32 half + 32) of every 64-key step and keeps its own
+// online-softmax stream with its own O accumulator), thread 256 producer,
+// thread 288 MMA issuer.  The two streams merge once at the end, so no
+// per-step cross-warp reduction is needed.  O is rescaled lazily (only when a
+// row's running maximum grows by more than 2^8), as in FlashAttention-4.
+// TMEM: Q hi | Q lo | S0 | S1 | P hi | P lo | O0 | O1   (64 columns each).
+// mbarriers (parity = use index & 1): kv_full/kv_empty per stage, s_full /
+// s_empty per S buffer, p_full (256 arrivals), o_done (commit after P.V).
 template <int HD>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kTcThreads, 1)
     attention_forward_tc(int rows, int W, int T, float scale, const float* __restrict__ q,
-                         const float* __restrict__ k, const float* __restrict__ v, float* __restrict__ o,
-                         float* __restrict__ lse2, int* __restrict__ err) {
+                         const float* __restrict__ kfmt, float* __restrict__ o, float* __restrict__ lse2,
+                         int* __restrict__ err) {
   using A = TcAtt<HD>;
+  using F = TcFmt<HD>;
+  constexpr int NS = A::FWD_STAGES;
   extern __shared__ __align__(128) float sm[];
-  float* Qh = sm;
-  float* Ql = Qh + A::BIG;
-  float* Kh = Ql + A::BIG;
-  float* Kl = Kh + A::SMALL;
-  float* Vh = Kl + A::SMALL;
-  float* Vl = Vh + A::SMALL;
-  __shared__ uint64_t bar_s, bar_o;
-  __shared__ uint32_t tmem_base;
-  __shared__ int failed;
+  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full[2], s_empty[2], p_full, o_done;
+  __shared__ TcShared sh;
+  __shared__ float xm[2][kTcRows], xl[2][kTcRows];
   const int tid = threadIdx.x, warp = tid >> 5;
   const int nt = (rows + kTcRows - 1) / kTcRows;
   const int q0 = (nt - 1 - (int)blockIdx.x) * kTcRows;  // longest causal spans first
   const int h = blockIdx.y;
-  if (warp == 0) tc::tmem_alloc(&tmem_base, 256);
+  const int nkt = (rows + kTcK - 1) / kTcK;
+  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
   if (tid == 0) {
-    tc::bar_init(&bar_s, 1);
-    tc::bar_init(&bar_o, 1);
+    for (int b = 0; b < NS; ++b) {
+      tc::bar_init(&kv_full[b], 1);
+      tc::bar_init(&kv_empty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::bar_init(&s_full[b], 1);
+      tc::bar_init(&s_empty[b], kTcCompute);
+    }
+    tc::bar_init(&p_full, kTcCompute);
+    tc::bar_init(&o_done, 1);
     tc::bar_init_fence();
-    failed = 0;
+    sh.failed = 0;
   }
-  tc_load_split<kTcRows, HD>(Qh, Ql, q, q0, rows, W, h);
-  tc::fence_async_smem();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t lane = (uint32_t)(warp * 32) << 16;
-  const uint32_t tS = tmem_base, tPh = tS + 64, tPl = tS + 128, tO = tS + 192;
-  constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcCols, false, false);
-  constexpr uint32_t idO = tc::idesc_tf32(kTcRows, HD, false, false);
-  const float scale2 = scale * 1.4426950408889634f;
-  const int qr = q0 + tid, qs = qr - qr % T;
-  float m = -INFINITY, l = 0.f;
-  const int kbeg = q0 - q0 % T, kend = min(rows, q0 + kTcRows);
-  uint32_t ph_s = 0, ph_o = 0;
-  bool first = true;
-  for (int kt = kbeg; kt < kend; kt += kTcCols) {
-    if (!first) {
-      if (!tc::bar_wait(&bar_o, ph_o)) failed = 1;  // P.V of the previous step done
-      ph_o ^= 1;
-    }
-    tc_load_split<kTcCols, HD>(Kh, Kl, k, kt, rows, W, h);
-    tc_load_split_t<kTcCols, HD>(Vh, Vl, v, kt, rows, W, h);  // V^T [HD][64]
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (failed) break;
-    if (tid == 0) {
-      tc::fence_after_sync();
-      tc_mma_nt<HD>(tS, Qh, Ql, Kh, Kl, idS);
-      tc::commit(&bar_s);
-    }
-    if (!tc::bar_wait(&bar_s, ph_s)) failed = 1;
-    ph_s ^= 1;
-    tc::fence_after_sync();
-    float s[64];
-    tc_ld64(tS + lane, s);
-    float mx = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const int kr = kt + j;
-      const bool ok = kr <= qr && kr >= qs && kr < rows;
-      s[j] = ok ? s[j] * scale2 : -INFINITY;
-      mx = fmaxf(mx, s[j]);
-    }
-    const float mn = fmaxf(m, mx);
-    const float alpha = mn == -INFINITY ? 1.0f : exp2f(m - mn);
-    float rs = 0.f;
-#pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      s[j] = mn == -INFINITY ? 0.f : exp2f(s[j] - mn);
-      rs += s[j];
-    }
-    l = l * alpha + rs;
-    m = mn;
-    if (!first) {
-#pragma unroll
-      for (int c = 0; c < HD; c += 16) {
-        float ov[16];
-        tc::tmem_ld16(tO + lane + c, ov);
-        tc::tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) ov[j] *= alpha;
-        tc::tmem_st16(tO + lane + c, ov);
-      }
-    }
-    tc_st_split<64>(tPh + lane, tPl + lane, s);
+  const uint32_t t0 = sh.tmem_base;
+  const uint32_t tQh = t0, tQl = t0 + 64, tS = t0 + 128, tPh = t0 + 256, tPl = t0 + 320, tO = t0 + 384;
+  const int kbeg = ((q0 - q0 % T) / kTcK) * kTcK;  // 64-aligned start of the first sequence
+  const int kend = min(rows, q0 + kTcRows);
+  const int n = (kend - kbeg + kTcK - 1) / kTcK;
+  const int kt0 = kbeg / kTcK;
+  if (warp < 4) {
+    const uint32_t lane = (uint32_t)(warp * 32) << 16;
+    row_to_tmem<HD>(q, q0 + tid, rows, W, h, tQh + lane, tQl + lane);
     tc::tmem_st_wait();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (failed) break;
-    if (tid == 0) {
-      tc::fence_after_sync();
-      tc_mma_tn<kTcCols>(tO, tPh, tPl, Vh, Vl, idO, !first);
-      tc::commit(&bar_o);
-    }
-    first = false;
-  }
-  if (!first && !failed) {
-    if (!tc::bar_wait(&bar_o, ph_o)) failed = 1;
-  }
-  tc::fence_after_sync();
-  __syncthreads();
-  if (!failed) {
-    const float inv = l > 0.f ? 1.0f / l : 0.f;
-#pragma unroll
-    for (int c = 0; c < HD; c += 16) {
-      float ov[16];
-      tc::tmem_ld16(tO + lane + c, ov);
-      tc::tmem_ld_wait();
-      if (qr < rows && !first) {
-        float4* dst = reinterpret_cast<float4*>(o + (size_t)qr * W + h * HD + c);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          dst[j] = make_float4(ov[4 * j] * inv, ov[4 * j + 1] * inv, ov[4 * j + 2] * inv, ov[4 * j + 3] * inv);
-      }
-    }
-    if (qr < rows) lse2[(size_t)h * rows + qr] = m + log2f(l);
-  } else if (tid == 0) {
-    atomicExch(err, 1);
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem_base, 256);
+  tc::fence_after_sync();
+
+  if (tid < kTcCompute) {
+    // ---------------------------------------------------------- softmax
+    const int row = tid & (kTcRows - 1), half = tid >> 7;
+    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t myO = tO + 64 * half + lane;
+    const float scale2 = scale * 1.4426950408889634f;
+    const int qr = q0 + row, qs = qr - qr % T;
+    // Every query row of the CTA in one sequence: steps wholly below the
+    // diagonal need no mask.
+    const int seq0 = q0 - q0 % T;
+    const bool one_seq = (q0 + kTcRows - 1) / T == q0 / T && q0 + kTcRows <= rows;
+    float m = -INFINITY, l = 0.f;
+    bool done = false;
+    for (int j = 0; j < n; ++j) {
+      const int b = j & 1;
+      TC_WAIT_OR_FAIL(&s_full[b], (j >> 1) & 1);
+      tc::fence_after_sync();
+      float s[32];
+      tc::tmem_ld32(tS + 64 * b + 32 * half + lane, s);
+      tc::fence_before_sync();
+      tc::bar_arrive(&s_empty[b]);
+      const int kt = kbeg + j * kTcK;
+      const bool full = one_seq && kt >= seq0 && kt + kTcK - 1 <= q0;
+      const int kh = kt + 32 * half;
+      float mx = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, s[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int kr = kh + c;
+          s[c] = (kr <= qr && kr >= qs && kr < rows) ? s[c] : -INFINITY;
+          mx = fmaxf(mx, s[c]);
+        }
+      }
+      mx *= scale2;
+      const bool need = mx > m + 8.0f;  // false while every key so far is masked
+      float alpha = 1.0f;
+      if (need) {
+        alpha = ex2(m - mx);  // 0 when m = -inf
+        m = mx;
+      }
+      float rs = 0.f;
+      const float nm = m == -INFINITY ? 0.f : -m;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        s[c] = ex2(fmaf(s[c], scale2, nm));  // ex2(-inf) = 0 for masked keys
+        rs += s[c];
+      }
+      l = l * alpha + rs;
+      if (j > 0) {
+        // P.V of step j-1 complete: O is stable and the P buffer is free.
+        TC_WAIT_OR_FAIL(&o_done, (j - 1) & 1);
+        tc::fence_after_sync();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int c = 0; c < HD; c += 16) {
+            float ov[16];
+            tc::tmem_ld16(myO + c, ov);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ov[e] *= alpha;
+            tc::tmem_st16(myO + c, ov);
+          }
+        }
+      }
+      tc_st_split<32>(tPh + 32 * half + lane, tPl + 32 * half + lane, s);
+      tc::tmem_st_wait();
+      tc::fence_before_sync();
+      tc::bar_arrive(&p_full);
+      if (j + 1 == n) done = true;
+    }
+    if (done && !tc::bar_wait(&o_done, (n - 1) & 1)) sh.failed = 1;
+    tc::fence_after_sync();
+    xm[half][row] = m;
+    xl[half][row] = l;
+    compute_sync();
+    if (done && !sh.failed) {
+      // Merge the two streams: O = (O0 2^(m0-M) + O1 2^(m1-M)) / L.
+      const float m0 = xm[0][row], m1 = xm[1][row];
+      const float mt = fmaxf(m0, m1);
+      const float f0 = m0 == -INFINITY ? 0.f : ex2(m0 - mt), f1 = m1 == -INFINITY ? 0.f : ex2(m1 - mt);
+      const float L = xl[0][row] * f0 + xl[1][row] * f1;
+      const float inv = L > 0.f ? 1.0f / L : 0.f;
+      const uint32_t o0 = tO + lane, o1 = tO + 64 + lane;
+#pragma unroll
+      for (int c = 0; c < HD / 2; c += 16) {
+        const int col = (HD / 2) * half + c;
+        float a[16], bb[16];
+        tc::tmem_ld16(o0 + col, a);
+        tc::tmem_ld16(o1 + col, bb);
+        if (qr < rows) {
+          float4* dst = reinterpret_cast<float4*>(o + (size_t)qr * W + h * HD + col);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            dst[e] = make_float4((a[4 * e] * f0 + bb[4 * e] * f1) * inv, (a[4 * e + 1] * f0 + bb[4 * e + 1] * f1) * inv,
+                                 (a[4 * e + 2] * f0 + bb[4 * e + 2] * f1) * inv,
+                                 (a[4 * e + 3] * f0 + bb[4 * e + 3] * f1) * inv);
+        }
+      }
+      if (qr < rows && half == 0) lse2[(size_t)h * rows + qr] = mt + log2f(L);
+    }
+  } else if (tid == kTcProducer) {
+    // ---------------------------------------------------------- producer
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      if (j >= NS) {
+        TC_WAIT_OR_FAIL(&kv_empty[st], ((j - NS) / NS) & 1);
+      }
+      tc::bar_expect_tx(&kv_full[st], A::FWD_STAGE * 4);
+      tc::bulk_g2s(sm + st * A::FWD_STAGE, kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE, A::FWD_STAGE * 4,
+                   &kv_full[st]);
+    }
+  } else if (tid == kTcIssuer) {
+    // ---------------------------------------------------------- MMA issuer
+    constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcK, false, false);
+    constexpr uint32_t idO = tc::idesc_tf32(kTcRows, HD, false, false);
+    for (int j = 0; j <= n; ++j) {
+      if (j < n) {
+        const int st = j % NS, b = j & 1;
+        const float* stage = sm + st * A::FWD_STAGE;
+        TC_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
+        if (j >= 2) {
+          TC_WAIT_OR_FAIL(&s_empty[b], ((j - 2) >> 1) & 1);
+        }
+        tc::fence_after_sync();
+        // S_j = Q K_j^T
+        mma_tmem_a<HD>(tS + 64 * b, tQh, tQl, stage + F::K_HI * F::KPART, stage + F::K_LO * F::KPART, idS, false);
+        tc::commit(&s_full[b]);
+      }
+      if (j >= 1) {
+        const int pj = j - 1, pst = pj % NS;
+        const float* stage = sm + pst * A::FWD_STAGE;
+        TC_WAIT_OR_FAIL(&p_full, pj & 1);
+        tc::fence_after_sync();
+        // O_half += P[:, half] V[half keys]   (B = V^T tile, K-major over keys)
+        const float* vh = stage + F::VT_HI * F::KPART;
+        const float* vl = stage + F::VT_LO * F::KPART;
+        mma_tmem_a_steps<kTcK, 4>(tO, tPh, tPl, vh, vl, idO, pj > 0, 0);
+        mma_tmem_a_steps<kTcK, 4>(tO + 64, tPh, tPl, vh, vl, idO, pj > 0, 4);
+        tc::commit(&o_done);
+        tc::commit(&kv_empty[pst]);
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (sh.failed && tid == 0) atomicExch(err, 1);
+  if (warp == 0) tc::tmem_dealloc(t0, 512);
 }
 
 // ---------------------------------------------------------------------- dQ
+// TMEM: Q hi | Q lo | dO hi | dO lo | S then dS hi | dP | dS lo | dQ
+// Per key step: S = Q K^T, dP = dO V^T; dS = P (dP - delta) scale; dQ += dS K.
+// S and dS hi share columns, so S_{j+1} is issued once dQ_j has completed.
 template <int HD>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kTcThreads, 1)
     attention_backward_dq_tc(int rows, int W, int T, float scale, const float* __restrict__ q,
-                             const float* __restrict__ k, const float* __restrict__ v,
-                             const float* __restrict__ dout, const float* __restrict__ lse2,
-                             const float* __restrict__ delta, float* __restrict__ dq, int* __restrict__ err) {
+                             const float* __restrict__ dout, const float* __restrict__ kfmt,
+                             const float* __restrict__ lse2, const float* __restrict__ delta, float* __restrict__ dq,
+                             int* __restrict__ err) {
   using A = TcAtt<HD>;
+  using F = TcFmt<HD>;
+  constexpr int NS = A::DQ_STAGES;
   extern __shared__ __align__(128) float sm[];
-  float* Qh = sm;
-  float* Ql = Qh + A::BIG;
-  float* Dh = Ql + A::BIG;  // dO
-  float* Dl = Dh + A::BIG;
-  float* Kh = Dl + A::BIG;
-  float* Kl = Kh + A::SMALL;
-  float* Vh = Kl + A::SMALL;
-  float* Vl = Vh + A::SMALL;
-  float* Th = Vl + A::SMALL;  // K^T [HD][64]
-  float* Tl = Th + A::SMALL;
-  __shared__ uint64_t bar_s, bar_o;
-  __shared__ uint32_t tmem_base;
-  __shared__ int failed;
+  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full, d_full, q_done;
+  __shared__ TcShared sh;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int nt = (rows + kTcRows - 1) / kTcRows;
   const int q0 = (nt - 1 - (int)blockIdx.x) * kTcRows;
   const int h = blockIdx.y;
-  if (warp == 0) tc::tmem_alloc(&tmem_base, 512);
+  const int nkt = (rows + kTcK - 1) / kTcK;
+  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
   if (tid == 0) {
-    tc::bar_init(&bar_s, 1);
-    tc::bar_init(&bar_o, 1);
+    for (int b = 0; b < NS; ++b) {
+      tc::bar_init(&kv_full[b], 1);
+      tc::bar_init(&kv_empty[b], 1);
+    }
+    tc::bar_init(&s_full, 1);
+    tc::bar_init(&d_full, kTcCompute);
+    tc::bar_init(&q_done, 1);
     tc::bar_init_fence();
-    failed = 0;
+    sh.failed = 0;
   }
-  tc_load_split<kTcRows, HD>(Qh, Ql, q, q0, rows, W, h);
-  tc_load_split<kTcRows, HD>(Dh, Dl, dout, q0, rows, W, h);
-  tc::fence_async_smem();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
-  const uint32_t lane = (uint32_t)(warp * 32) << 16;
-  const uint32_t tS = tmem_base, tP = tS + 64, tSh = tS + 128, tSl = tS + 192, tQ = tS + 256;
-  constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcCols, false, false);
-  constexpr uint32_t idQ = tc::idesc_tf32(kTcRows, HD, false, false);
-  const float scale2 = scale * 1.4426950408889634f;
-  const int qr = q0 + tid, qs = qr - qr % T;
-  const bool in = qr < rows;
-  const float L = in ? lse2[(size_t)h * rows + qr] : 0.f;
-  const float dl = in ? delta[(size_t)h * rows + qr] : 0.f;
-  const int kbeg = q0 - q0 % T, kend = min(rows, q0 + kTcRows);
-  uint32_t ph_s = 0, ph_o = 0;
-  bool first = true;
-  for (int kt = kbeg; kt < kend; kt += kTcCols) {
-    if (!first) {
-      if (!tc::bar_wait(&bar_o, ph_o)) failed = 1;
-      ph_o ^= 1;
-    }
-    tc_load_split<kTcCols, HD>(Kh, Kl, k, kt, rows, W, h);
-    tc_load_split<kTcCols, HD>(Vh, Vl, v, kt, rows, W, h);
-    tc_load_split_t<kTcCols, HD>(Th, Tl, k, kt, rows, W, h);
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (failed) break;
-    if (tid == 0) {
-      tc::fence_after_sync();
-      tc_mma_nt<HD>(tS, Qh, Ql, Kh, Kl, idS);  // S  = Q K^T
-      tc_mma_nt<HD>(tP, Dh, Dl, Vh, Vl, idS);  // dP = dO V^T
-      tc::commit(&bar_s);
-    }
-    if (!tc::bar_wait(&bar_s, ph_s)) failed = 1;
-    ph_s ^= 1;
-    tc::fence_after_sync();
-    float s[64], dp[64];
-    tc_ld64(tS + lane, s);
-    tc_ld64(tP + lane, dp);
-#pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const int kr = kt + j;
-      const bool ok = kr <= qr && kr >= qs && kr < rows;
-      const float p = ok ? exp2f(s[j] * scale2 - L) : 0.f;
-      s[j] = p * (dp[j] - dl) * scale;
-    }
-    tc_st_split<64>(tSh + lane, tSl + lane, s);
+  const uint32_t t0 = sh.tmem_base;
+  const uint32_t tQh = t0, tQl = t0 + 64, tDh = t0 + 128, tDl = t0 + 192, tS = t0 + 256, tP = t0 + 320,
+                 tSl = t0 + 384, tG = t0 + 448;
+  const int kbeg = ((q0 - q0 % T) / kTcK) * kTcK;
+  const int kend = min(rows, q0 + kTcRows);
+  const int n = (kend - kbeg + kTcK - 1) / kTcK;
+  const int kt0 = kbeg / kTcK;
+  if (warp < 4) {
+    const uint32_t lane = (uint32_t)(warp * 32) << 16;
+    row_to_tmem<HD>(q, q0 + tid, rows, W, h, tQh + lane, tQl + lane);
+    row_to_tmem<HD>(dout, q0 + tid, rows, W, h, tDh + lane, tDl + lane);
     tc::tmem_st_wait();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (failed) break;
-    if (tid == 0) {
-      tc::fence_after_sync();
-      tc_mma_tn<kTcCols>(tQ, tSh, tSl, Th, Tl, idQ, !first);  // dQ += dS K
-      tc::commit(&bar_o);
-    }
-    first = false;
-  }
-  if (!first && !failed) {
-    if (!tc::bar_wait(&bar_o, ph_o)) failed = 1;
-  }
-  tc::fence_after_sync();
-  __syncthreads();
-  if (!failed) {
-#pragma unroll
-    for (int c = 0; c < HD; c += 16) {
-      float ov[16];
-      tc::tmem_ld16(tQ + lane + c, ov);
-      tc::tmem_ld_wait();
-      if (in && !first) {
-        float4* dst = reinterpret_cast<float4*>(dq + (size_t)qr * W + h * HD + c);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) dst[j] = make_float4(ov[4 * j], ov[4 * j + 1], ov[4 * j + 2], ov[4 * j + 3]);
-      }
-    }
-  } else if (tid == 0) {
-    atomicExch(err, 1);
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem_base, 512);
-}
+  tc::fence_after_sync();
 
-// ------------------------------------------------------------------- dK/dV
-// A CTA owns 128 keys of one head and walks the later queries 32 at a time:
-// S^T = K Q^T and dP^T = V dO^T (keys on TMEM lanes), P^T and dS^T go back to
-// TMEM as hi/lo parts, then dV += P^T dO and dK += dS^T Q with Q^T / dO^T
-// staged transposed.
-template <int HD>
-__global__ void __launch_bounds__(128, 1)
-    attention_backward_dkdv_tc(int rows, int W, int T, float scale, const float* __restrict__ q,
-                               const float* __restrict__ k, const float* __restrict__ v,
-                               const float* __restrict__ dout, const float* __restrict__ lse2,
-                               const float* __restrict__ delta, const float* __restrict__ dv_add,
-                               float* __restrict__ dk, float* __restrict__ dv, int* __restrict__ err) {
-  using A = TcAtt<HD>;
-  extern __shared__ __align__(128) float sm[];
-  float* Kh = sm;
-  float* Kl = Kh + A::BIG;
-  float* Vh = Kl + A::BIG;
-  float* Vl = Vh + A::BIG;
-  float* Qh = Vl + A::BIG;    // Q   [32][HD]
-  float* Ql = Qh + A::QT;
-  float* Dh = Ql + A::QT;     // dO  [32][HD]
-  float* Dl = Dh + A::QT;
-  float* Qth = Dl + A::QT;    // Q^T [HD][32]
-  float* Qtl = Qth + A::QT;
-  float* Dth = Qtl + A::QT;   // dO^T [HD][32]
-  float* Dtl = Dth + A::QT;
-  float* Ls = Dtl + A::QT;    // lse2 of the query step
-  float* Es = Ls + kTcQ;      // delta of the query step
-  __shared__ uint64_t bar_s, bar_o;
-  __shared__ uint32_t tmem_base;
-  __shared__ int failed;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int k0 = blockIdx.x * kTcRows;
-  const int h = blockIdx.y;
-  if (warp == 0) tc::tmem_alloc(&tmem_base, 512);
-  if (tid == 0) {
-    tc::bar_init(&bar_s, 1);
-    tc::bar_init(&bar_o, 1);
-    tc::bar_init_fence();
-    failed = 0;
-  }
-  tc_load_split<kTcRows, HD>(Kh, Kl, k, k0, rows, W, h);
-  tc_load_split<kTcRows, HD>(Vh, Vl, v, k0, rows, W, h);
-  tc::fence_async_smem();
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t lane = (uint32_t)(warp * 32) << 16;
-  // S^T then P^T hi | dP^T then dS^T hi | P^T lo | dS^T lo | dV | dK
-  const uint32_t tS = tmem_base, tP = tS + 32, tPl = tS + 64, tSl = tS + 96, tV = tS + 128, tK = tS + 128 + HD;
-  constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcQ, false, false);
-  constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
-  const float scale2 = scale * 1.4426950408889634f;
-  const int kr = k0 + tid;
-  const int ke = (kr / T + 1) * T;  // end of the key's sequence
-  const int last = min(rows, k0 + kTcRows) - 1;
-  const int qend = min(rows, (last / T + 1) * T);
-  uint32_t ph_s = 0, ph_o = 0;
-  bool first = true;
-  for (int qt = k0; qt < qend; qt += kTcQ) {
-    if (!first) {
-      if (!tc::bar_wait(&bar_o, ph_o)) failed = 1;
-      ph_o ^= 1;
-    }
-    tc_load_split<kTcQ, HD>(Qh, Ql, q, qt, rows, W, h);
-    tc_load_split<kTcQ, HD>(Dh, Dl, dout, qt, rows, W, h);
-    tc_load_split_t<kTcQ, HD>(Qth, Qtl, q, qt, rows, W, h);
-    tc_load_split_t<kTcQ, HD>(Dth, Dtl, dout, qt, rows, W, h);
-    if (tid < kTcQ) {
-      const int r = qt + tid;
-      Ls[tid] = r < rows ? lse2[(size_t)h * rows + r] : 0.f;
-      Es[tid] = r < rows ? delta[(size_t)h * rows + r] : 0.f;
-    }
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (failed) break;
-    if (tid == 0) {
+  if (tid < kTcCompute) {
+    // Thread (row, half) handles key columns [32 half, 32 half + 32).
+    const int row = tid & (kTcRows - 1), half = tid >> 7;
+    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    const float scale2 = scale * 1.4426950408889634f;
+    const int qr = q0 + row, qs = qr - qr % T;
+    const int seq0 = q0 - q0 % T;
+    const bool one_seq = (q0 + kTcRows - 1) / T == q0 / T && q0 + kTcRows <= rows;
+    const bool in = qr < rows;
+    const float L = in ? lse2[(size_t)h * rows + qr] : 0.f;
+    const float dl = in ? delta[(size_t)h * rows + qr] : 0.f;
+    bool done = false;
+    for (int j = 0; j < n; ++j) {
+      TC_WAIT_OR_FAIL(&s_full, j & 1);
       tc::fence_after_sync();
-      tc_mma_nt<HD>(tS, Kh, Kl, Qh, Ql, idS);  // S^T  = K Q^T
-      tc_mma_nt<HD>(tP, Vh, Vl, Dh, Dl, idS);  // dP^T = V dO^T
-      tc::commit(&bar_s);
+      float s[32], dp[32];
+      tc::tmem_ld32(tS + 32 * half + lane, s);
+      tc::tmem_ld32(tP + 32 * half + lane, dp);
+      const int kt = kbeg + j * kTcK;
+      const bool full = one_seq && kt >= seq0 && kt + kTcK - 1 <= q0;
+      const int kh = kt + 32 * half;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int kr = kh + c;
+        const bool ok = full || (kr <= qr && kr >= qs && kr < rows);
+        const float p = ok ? ex2(fmaf(s[c], scale2, -L)) : 0.f;
+        s[c] = p * (dp[c] - dl) * scale;
+      }
+      tc_st_split<32>(tS + 32 * half + lane, tSl + 32 * half + lane, s);  // dS hi over S
+      tc::tmem_st_wait();
+      tc::fence_before_sync();
+      tc::bar_arrive(&d_full);
+      if (j + 1 == n) done = true;
     }
-    if (!tc::bar_wait(&bar_s, ph_s)) failed = 1;
-    ph_s ^= 1;
+    if (done && !tc::bar_wait(&q_done, (n - 1) & 1)) sh.failed = 1;
     tc::fence_after_sync();
-    float s[kTcQ], dp[kTcQ];
-    tc::tmem_ld32(tS + lane, s);
-    tc::tmem_ld32(tP + lane, dp);
+    if (done && !sh.failed) {
 #pragma unroll
-    for (int j = 0; j < kTcQ; ++j) {
-      const int qj = qt + j;
-      const bool ok = qj >= kr && qj < ke && qj < rows && kr < rows;
-      const float p = ok ? exp2f(s[j] * scale2 - Ls[j]) : 0.f;
-      s[j] = p;
-      dp[j] = p * (dp[j] - Es[j]) * scale;
-    }
-    tc_st_split<kTcQ>(tS + lane, tPl + lane, s);   // P^T hi over S^T
-    tc_st_split<kTcQ>(tP + lane, tSl + lane, dp);  // dS^T hi over dP^T
-    tc::tmem_st_wait();
-    tc::fence_before_sync();
-    __syncthreads();
-    if (failed) break;
-    if (tid == 0) {
-      tc::fence_after_sync();
-      tc_mma_tn<kTcQ>(tV, tS, tPl, Dth, Dtl, idG, !first);  // dV += P^T dO
-      tc_mma_tn<kTcQ>(tK, tP, tSl, Qth, Qtl, idG, !first);  // dK += dS^T Q
-      tc::commit(&bar_o);
-    }
-    first = false;
-  }
-  if (!first && !failed) {
-    if (!tc::bar_wait(&bar_o, ph_o)) failed = 1;
-  }
-  tc::fence_after_sync();
-  __syncthreads();
-  if (!failed) {
-    const bool in = kr < rows && !first;
+      for (int c = 0; c < HD / 2; c += 16) {
+        const int col = (HD / 2) * half + c;
+        float gv[16];
+        tc::tmem_ld16(tG + lane + col, gv);
+        if (in) {
+          float4* dst = reinterpret_cast<float4*>(dq + (size_t)qr * W + h * HD + col);
 #pragma unroll
-    for (int c = 0; c < HD; c += 16) {
-      float gk[16], gv[16];
-      tc::tmem_ld16(tK + lane + c, gk);
-      tc::tmem_ld16(tV + lane + c, gv);
-      if (in) {
-        const size_t base = (size_t)kr * W + h * HD + c;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          dk[base + j] = gk[j];
-          dv[base + j] = gv[j] + (dv_add != nullptr ? dv_add[base + j] : 0.f);
+          for (int e = 0; e < 4; ++e) dst[e] = make_float4(gv[4 * e], gv[4 * e + 1], gv[4 * e + 2], gv[4 * e + 3]);
         }
       }
     }
-  } else if (tid == 0) {
-    atomicExch(err, 1);
+  } else if (tid == kTcProducer) {
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      if (j >= NS) {
+        TC_WAIT_OR_FAIL(&kv_empty[st], ((j - NS) / NS) & 1);
+      }
+      const float* tile = kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE;
+      float* stage = sm + st * A::DQ_STAGE;
+      tc::bar_expect_tx(&kv_full[st], A::DQ_STAGE * 4);
+      tc::bulk_g2s(stage, tile + F::K_HI * F::KPART, 2 * F::KPART * 4, &kv_full[st]);                 // K, K'
+      tc::bulk_g2s(stage + 2 * F::KPART, tile + F::V_HI * F::KPART, 4 * F::KPART * 4, &kv_full[st]);  // V, V', Kt, Kt'
+    }
+  } else if (tid == kTcIssuer) {
+    constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcK, false, false);
+    constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      const float* stage = sm + st * A::DQ_STAGE;  // K, K', V, V', Kt, Kt'
+      TC_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
+      if (j >= 1) {
+        TC_WAIT_OR_FAIL(&q_done, (j - 1) & 1);  // dQ_{j-1} has read dS (the S columns)
+      }
+      tc::fence_after_sync();
+      mma_tmem_a<HD>(tS, tQh, tQl, stage, stage + F::KPART, idS, false);                     // S  = Q K^T
+      mma_tmem_a<HD>(tP, tDh, tDl, stage + 2 * F::KPART, stage + 3 * F::KPART, idS, false);  // dP = dO V^T
+      tc::commit(&s_full);
+      TC_WAIT_OR_FAIL(&d_full, j & 1);
+      tc::fence_after_sync();
+      mma_tmem_a<kTcK>(tG, tS, tSl, stage + 4 * F::KPART, stage + 5 * F::KPART, idG, j > 0);  // dQ += dS K
+      tc::commit(&q_done);
+      tc::commit(&kv_empty[st]);
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem_base, 512);
+  if (sh.failed && tid == 0) atomicExch(err, 1);
+  if (warp == 0) tc::tmem_dealloc(t0, 512);
 }
+
+// ------------------------------------------------------------------- dK/dV
+// A CTA owns 128 keys of one head and walks the later queries 32 at a time.
+// TMEM: K hi | K lo | V hi | V lo (64 each) | S^T then P^T hi | dP^T then
+// dS^T hi | P^T lo | dS^T lo (32 each) | dV | dK (64 each).
+// Per query step: S^T = K Q^T, dP^T = V dO^T (keys on lanes); P^T, dS^T;
+// dV += P^T dO, dK += dS^T Q (B = dO^T / Q^T tiles).
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    attention_backward_dkdv_tc(int rows, int W, int T, float scale, const float* __restrict__ k,
+                               const float* __restrict__ v, const float* __restrict__ qfmt,
+                               const float* __restrict__ dv_add, float* __restrict__ dk, float* __restrict__ dv,
+                               int* __restrict__ err) {
+  using A = TcAtt<HD>;
+  using F = TcFmt<HD>;
+  constexpr int NS = A::KV_STAGES;
+  extern __shared__ __align__(128) float sm[];
+  __shared__ uint64_t q_full[NS], q_empty[NS], s_full, d_full, g_done;
+  __shared__ TcShared sh;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int k0 = blockIdx.x * kTcRows;
+  const int h = blockIdx.y;
+  const int nqt = (rows + kTcQ - 1) / kTcQ;
+  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
+  if (tid == 0) {
+    for (int b = 0; b < NS; ++b) {
+      tc::bar_init(&q_full[b], 1);
+      tc::bar_init(&q_empty[b], 1);
+    }
+    tc::bar_init(&s_full, 1);
+    tc::bar_init(&d_full, kTcCompute);
+    tc::bar_init(&g_done, 1);
+    tc::bar_init_fence();
+    sh.failed = 0;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t t0 = sh.tmem_base;
+  const uint32_t tKh = t0, tKl = t0 + 64, tVh = t0 + 128, tVl = t0 + 192, tS = t0 + 256, tP = t0 + 288,
+                 tPl = t0 + 320, tSl = t0 + 352, tdV = t0 + 384, tdK = t0 + 448;
+  const int last = min(rows, k0 + kTcRows) - 1;
+  const int qend = min(rows, (last / T + 1) * T);
+  const int n = (qend - k0 + kTcQ - 1) / kTcQ;
+  const int qt0 = k0 / kTcQ;
+  if (warp < 4) {
+    const uint32_t lane = (uint32_t)(warp * 32) << 16;
+    row_to_tmem<HD>(k, k0 + tid, rows, W, h, tKh + lane, tKl + lane);
+    row_to_tmem<HD>(v, k0 + tid, rows, W, h, tVh + lane, tVl + lane);
+    tc::tmem_st_wait();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+
+  if (tid < kTcCompute) {
+    // Thread (key row, half) handles query columns [16 half, 16 half + 16).
+    const int row = tid & (kTcRows - 1), half = tid >> 7;
+    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    const float scale2 = scale * 1.4426950408889634f;
+    const int kr = k0 + row;
+    const int ke = (kr / T + 1) * T;  // end of the key's sequence
+    // Every key row of the CTA in one sequence, so query steps wholly above
+    // the diagonal and inside the sequence need no mask.
+    const int kseq_end = (k0 / T + 1) * T;
+    const bool one_seq = (k0 + kTcRows - 1) / T == k0 / T && k0 + kTcRows <= rows;
+    bool done = false;
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      TC_WAIT_OR_FAIL(&s_full, j & 1);
+      tc::fence_after_sync();
+      const float* stage = sm + st * A::KV_STAGE;
+      const float* Ls = stage + 8 * F::QPART + 16 * half;  // lse2 of the query step
+      const float* Es = Ls + kTcQ;                         // delta of the query step
+      float s[16], dp[16];
+      tc::tmem_ld16(tS + 16 * half + lane, s);
+      tc::tmem_ld16(tP + 16 * half + lane, dp);
+      const int qt = k0 + j * kTcQ;
+      const bool full = one_seq && qt >= k0 + kTcRows - 1 && qt + kTcQ <= min(kseq_end, rows);
+      const int qh = qt + 16 * half;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const int qj = qh + c;
+        const bool ok = full || (qj >= kr && qj < ke && qj < rows && kr < rows);
+        const float p = ok ? ex2(fmaf(s[c], scale2, -Ls[c])) : 0.f;
+        s[c] = p;
+        dp[c] = p * (dp[c] - Es[c]) * scale;
+      }
+      tc_st_split<16>(tS + 16 * half + lane, tPl + 16 * half + lane, s);   // P^T hi over S^T
+      tc_st_split<16>(tP + 16 * half + lane, tSl + 16 * half + lane, dp);  // dS^T hi over dP^T
+      tc::tmem_st_wait();
+      tc::fence_before_sync();
+      tc::bar_arrive(&d_full);
+      if (j + 1 == n) done = true;
+    }
+    if (done && !tc::bar_wait(&g_done, (n - 1) & 1)) sh.failed = 1;
+    tc::fence_after_sync();
+    if (done && !sh.failed) {
+      const bool in = kr < rows;
+#pragma unroll
+      for (int c = 0; c < HD / 2; c += 16) {
+        const int col = (HD / 2) * half + c;
+        float gk[16], gv[16];
+        tc::tmem_ld16(tdK + lane + col, gk);
+        tc::tmem_ld16(tdV + lane + col, gv);
+        if (in) {
+          const size_t base = (size_t)kr * W + h * HD + col;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            dk[base + e] = gk[e];
+            dv[base + e] = gv[e] + (dv_add != nullptr ? dv_add[base + e] : 0.f);
+          }
+        }
+      }
+    }
+  } else if (tid == kTcProducer) {
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      if (j >= NS) {
+        TC_WAIT_OR_FAIL(&q_empty[st], ((j - NS) / NS) & 1);
+      }
+      tc::bar_expect_tx(&q_full[st], A::KV_STAGE * 4);
+      tc::bulk_g2s(sm + st * A::KV_STAGE, qfmt + ((size_t)h * nqt + qt0 + j) * F::QTILE, A::KV_STAGE * 4,
+                   &q_full[st]);
+    }
+  } else if (tid == kTcIssuer) {
+    constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcQ, false, false);
+    constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      const float* stage = sm + st * A::KV_STAGE;
+      TC_WAIT_OR_FAIL(&q_full[st], (j / NS) & 1);
+      if (j >= 1) {
+        TC_WAIT_OR_FAIL(&g_done, (j - 1) & 1);  // dV/dK of step j-1 have read P^T / dS^T
+      }
+      tc::fence_after_sync();
+      mma_tmem_a<HD>(tS, tKh, tKl, stage + F::Q_HI * F::QPART, stage + F::Q_LO * F::QPART, idS, false);  // S^T
+      mma_tmem_a<HD>(tP, tVh, tVl, stage + F::D_HI * F::QPART, stage + F::D_LO * F::QPART, idS, false);  // dP^T
+      tc::commit(&s_full);
+      TC_WAIT_OR_FAIL(&d_full, j & 1);
+      tc::fence_after_sync();
+      mma_tmem_a<kTcQ>(tdV, tS, tPl, stage + F::DT_HI * F::QPART, stage + F::DT_LO * F::QPART, idG, j > 0);
+      mma_tmem_a<kTcQ>(tdK, tP, tSl, stage + F::QT_HI * F::QPART, stage + F::QT_LO * F::QPART, idG, j > 0);
+      tc::commit(&g_done);
+      tc::commit(&q_empty[st]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (sh.failed && tid == 0) atomicExch(err, 1);
+  if (warp == 0) tc::tmem_dealloc(t0, 512);
+}
+
+#undef TC_WAIT_OR_FAIL
 
 }  // namespace mb

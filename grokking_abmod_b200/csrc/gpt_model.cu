@@ -151,6 +151,10 @@ std::unique_ptr<BlockOps> make_block_ops(int W, int A, int F) {
 // ------------------------------------------------- head-width attention ops
 struct AttentionOps {
   virtual ~AttentionOps() = default;
+  // Device scratch (floats) the kernels need for `rows` token rows; the model
+  // allocates it per workspace and sets `scratch` before enqueueing.
+  virtual size_t scratch_floats(int rows, int H) const { return 0; }
+  float* scratch = nullptr;
   virtual void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                        const float* v, float* o, float* lse) = 0;
   virtual void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q,
@@ -197,6 +201,7 @@ struct AttentionOpsD final : AttentionOps {
 template <int HD>
 struct AttentionOpsTc final : AttentionOps {
   using K = TcAtt<HD>;
+  using F = TcFmt<HD>;
   int* err;
   explicit AttentionOpsTc(int* e) : err(e) {
     MB_CUDA(cudaFuncSetAttribute(&attention_forward_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -206,24 +211,36 @@ struct AttentionOpsTc final : AttentionOps {
     MB_CUDA(cudaFuncSetAttribute(&attention_backward_dkdv_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)K::smem_dkdv));
   }
+  static size_t key_floats(int rows, int H) { return (size_t)H * ((rows + kTcK - 1) / kTcK) * F::KTILE; }
+  static size_t query_floats(int rows, int H) { return (size_t)H * ((rows + kTcQ - 1) / kTcQ) * F::QTILE; }
+  size_t scratch_floats(int rows, int H) const override { return key_floats(rows, H) + query_floats(rows, H); }
+  float* kfmt() const { return scratch; }
+  float* qfmt(int rows, int H) const { return scratch + key_floats(rows, H); }
+  void format_keys(cudaStream_t s, int rows, int W, int H, const float* k, const float* v) {
+    attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), 256, 0, s>>>(rows, W, k, v, kfmt());
+  }
   void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                const float* v, float* o, float* lse) override {
+    format_keys(s, rows, W, H, k, v);
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_forward_tc<HD><<<grid, 128, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, k, v, o,
-                                                                 lse, err);
+    attention_forward_tc<HD><<<grid, kTcThreads, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
+                                                                        kfmt(), o, lse, err);
   }
   void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                      const float* v, const float* dout, const float* lse, const float* delta, const float* dv_add,
                      float* dk, float* dv) override {
+    attention_format_queries<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), 256, 0, s>>>(rows, W, q, dout, lse, delta,
+                                                                                   qfmt(rows, H));
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dkdv_tc<HD><<<grid, 128, K::smem_dkdv, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, k, v,
-                                                                    dout, lse, delta, dv_add, dk, dv, err);
+    attention_backward_dkdv_tc<HD><<<grid, kTcThreads, K::smem_dkdv, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), k, v,
+                                                                           qfmt(rows, H), dv_add, dk, dv, err);
   }
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
+    format_keys(s, rows, W, H, k, v);
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dq_tc<HD><<<grid, 128, K::smem_dq, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, k, v, dout,
-                                                                lse, delta, dq, err);
+    attention_backward_dq_tc<HD><<<grid, kTcThreads, K::smem_dq, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, dout,
+                                                                       kfmt(), lse, delta, dq, err);
   }
 };
 
@@ -281,6 +298,7 @@ struct Workspace {
   std::vector<float*> q, k, v, o, xm, lse;
   float *nf, *dlog, *logits, *loss_rows, *g, *dO, *dvx, *dxm, *delta, *dq, *dk, *dv, *emb_partial, *dE;
   float* emb_mesh_partial;
+  float* att_scratch;
   float2* rope;
   uint32_t *tokens, *targets;
   float* supervised;
@@ -600,6 +618,7 @@ class GptModel {
     ws->emb_chunks = (rows + kEmbChunk - 1) / kEmbChunk;
     ws->emb_partial = a.alloc<float>((size_t)ws->emb_chunks * V * W);
     ws->dE = a.alloc<float>((size_t)V * W);
+    ws->att_scratch = a.alloc<float>(attention_->scratch_floats(rows, H));
     ws->emb_mesh_partial = a.alloc<float>((size_t)V * layout_.groups[layout_.embedding].size);
     ws->tokens = a.alloc<uint32_t>(rows);
     ws->targets = a.alloc<uint32_t>(rows);
@@ -669,6 +688,7 @@ class GptModel {
 
   void enqueue_forward(Workspace& ws, bool with_targets) {
     const Dims d = dims(ws);
+    attention_->scratch = ws.att_scratch;
     const int L = cfg_.layers, W = cfg_.width, V = cfg_.vocab_size, H = cfg_.heads;
     mark("count_supervised");
     if (with_targets)
@@ -701,6 +721,7 @@ class GptModel {
 
   void enqueue_backward(Workspace& ws) {
     const Dims d = dims(ws);
+    attention_->scratch = ws.att_scratch;
     const int L = cfg_.layers, W = cfg_.width, V = cfg_.vocab_size, H = cfg_.heads;
     for (int b = L - 1; b >= 0; --b) {
       const BlockGroups& bg = layout_.blocks[b];

@@ -90,6 +90,27 @@ __device__ __forceinline__ void bar_init(uint64_t* bar, uint32_t count) {
 }
 __device__ __forceinline__ void bar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
+// Arrival that also announces `bytes` of bulk-copy transactions to wait for.
+__device__ __forceinline__ void bar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+// Bulk (non-tensor, non-multicast) copy global -> this CTA's shared memory,
+// completing `bytes` transactions on the mbarrier.  Both addresses 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
+// One arrival (release semantics) on an mbarrier.
+__device__ __forceinline__ void bar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // Waits for the mbarrier phase with the given parity.  Gives up after
 // `limit` polls (returns false) so a lost arrival can never hang the GPU.
 __device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 24)) {
