@@ -31,6 +31,12 @@ class GptConfigC(ctypes.Structure):
         "attention_mesh_depth", "ffn_mesh_depth", "connectivity")]
 
 
+class SimpleConfigC(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in (
+        "architecture", "activation", "modulus", "width", "depth", "connectivity",
+        "embedding_mesh_depth", "full_mesh_initialization", "mesh_learning_rate_multiplier")]
+
+
 class AdamWC(ctypes.Structure):
     _fields_ = [(n, ctypes.c_float) for n in (
         "learning_rate", "weight_decay", "beta1", "beta2", "epsilon")]
@@ -105,6 +111,32 @@ SIGNATURES = {
                                            c_u32_p, c_u32_p]),
     "mb_zipf_batch": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_size_t,
                                      ctypes.c_size_t, ctypes.c_uint32, ctypes.c_double, c_u32_p, c_u32_p]),
+    "mb_simple_validate": (ctypes.c_int, [ctypes.POINTER(SimpleConfigC)]),
+    "mb_simple_parameter_count": (ctypes.c_int, [ctypes.POINTER(SimpleConfigC), c_size_p]),
+    "mb_simple_groups": (ctypes.c_int, [ctypes.POINTER(SimpleConfigC), c_u32_p, c_size_p]),
+    "mb_simple_initial_parameters": (ctypes.c_int, [ctypes.POINTER(SimpleConfigC), ctypes.c_uint64, c_float_p,
+                                                    ctypes.c_size_t]),
+    "mb_simple_encode": (ctypes.c_int, [ctypes.POINTER(SimpleConfigC), c_u32_p, ctypes.c_size_t, c_float_p,
+                                        c_u32_p]),
+    "mb_simple_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(SimpleConfigC), ctypes.c_uint64,
+                                        ctypes.POINTER(ctypes.c_void_p)]),
+    "mb_simple_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "mb_simple_get_parameters": (ctypes.c_int, [ctypes.c_void_p, c_float_p, ctypes.c_size_t]),
+    "mb_simple_set_parameters": (ctypes.c_int, [ctypes.c_void_p, c_float_p, ctypes.c_size_t]),
+    "mb_simple_upload_table": (ctypes.c_int, [ctypes.c_void_p, c_float_p, c_u32_p, ctypes.c_size_t,
+                                              ctypes.POINTER(ctypes.c_void_p)]),
+    "mb_simple_table_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "mb_simple_upload_batches": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_u32_p, ctypes.c_size_t,
+                                                ctypes.POINTER(ctypes.c_void_p)]),
+    "mb_simple_batches_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "mb_simple_train_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                            ctypes.c_size_t, ctypes.POINTER(AdamWC)]),
+    "mb_simple_evaluate": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_float_p, c_u32_p]),
+    "mb_simple_loss_and_gradient": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_u32_p, ctypes.c_size_t,
+                                                   c_double_p, c_float_p, ctypes.c_size_t]),
+    "mb_simple_stream": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "mb_simple_check": (ctypes.c_int, [ctypes.c_void_p]),
+    "mb_simple_step_launches": (ctypes.c_int, [ctypes.c_void_p, c_u32_p]),
 }
 
 _lib = None

@@ -13,7 +13,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmeshb200.so")
 
-SOURCES = ["gpt_model.cu", "mesh_ops.cu", "gemm_tc.cu", "config.cpp", "data.cpp"]
+SOURCES = ["gpt_model.cu", "mesh_ops.cu", "gemm_tc.cu", "simple_model.cu", "config.cpp", "data.cpp",
+           "simple_config.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -38,7 +39,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return LIB
     tmp = LIB + ".tmp"
-    cmd = [_nvcc(), "-std=c++17", "-O3", "-lineinfo", *ARCH, "-shared", "-Xcompiler", "-fPIC,-ffp-contract=off",
+    cmd = [_nvcc(), "-std=c++17", "-O3", "-lineinfo", "--threads", "0", *ARCH, "-shared", "-Xcompiler",
+           "-fPIC,-ffp-contract=off",
            "-I", os.path.join(ROOT, "include"), "-o", tmp]
     cmd += [os.path.join(CSRC, s) for s in SOURCES]
     cmd += ["-ldl"]

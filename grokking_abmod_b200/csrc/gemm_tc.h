@@ -1,0 +1,32 @@
+// Host interface of the tcgen05 3xTF32 GEMM (gemm_tc.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+
+namespace mb {
+
+// One GEMM operand of `rows` (M or N) x K: element (r, k) is p[r * ld + k]
+// (K-major) or, with k_outer, p[k * ld + r].
+struct GemmOperand {
+  const float* p;
+  int ld;
+  bool k_outer;
+};
+
+// Sets the kernel's shared-memory limit; call once per device before the
+// first launch (and before any stream capture).
+void gemm_prepare();
+// C[M][N] (row stride ldc) = A . B^T over K.  k_chunk > 0 and < K splits K
+// into chunks of that many (a multiple of 32) with partial tiles in
+// `partial` (gemm_partial_floats floats) summed in chunk order.  `err` is a
+// device flag set if an mbarrier wait gave up.
+void launch_gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, int M, int N, int K, int k_chunk,
+                 float* partial, int* err, cudaStream_t st, bool a_tmem = false);
+int gemm_chunks(int K, int k_chunk);
+size_t gemm_partial_floats(int M, int N, int K, int k_chunk);
+// Kernel launches of one launch_gemm call.
+int gemm_launches(int K, int k_chunk);
+
+}  // namespace mb

@@ -1,0 +1,39 @@
+// grok-simple models: host configuration, layout and initialisation shared
+// by the executor (simple_model.cu) and the C ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <vector>
+
+#include "host.h"
+
+namespace mb {
+namespace simple {
+
+enum Architecture : uint32_t { kMeshMlp = 0, kRotaryDense = 1, kSharedNeighbor = 2 };
+enum Activation : uint32_t { kRelu = 0, kSquare = 1 };
+enum Connectivity : uint32_t { kOwn = 0, kNeighbor = 1, kButterfly = 2 };
+
+constexpr uint32_t kMaxWidth = 16384, kMaxDepth = 64, kMaxClasses = 1024;  // src/simple/mod.rs:25-31
+constexpr size_t kMaxRows = 131072;
+constexpr size_t kMaxParameters = (size_t)1 << 28;
+// This build's fused row kernels keep a row per warp in shared memory.
+constexpr uint32_t kMaxKernelWidth = 512;
+
+void validate(const mb_simple_config& c);                // the reference's rules (MB_ERR_INVALID)
+void validate_kernel_shapes(const mb_simple_config& c);  // this build's kernels (MB_ERR_UNSUPPORTED)
+int parents(const mb_simple_config& c);
+int stride(const mb_simple_config& c, int layer);
+int mesh_layers(const mb_simple_config& c);
+// Dense (inputs, outputs) layers in parameter order.
+std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& c);
+std::vector<size_t> groups(const mb_simple_config& c);
+size_t parameter_count(const mb_simple_config& c);
+std::vector<float> initial_parameters(const mb_simple_config& c, uint64_t seed);
+// One-hot rows -> operand classes; throws MB_ERR_INVALID on other features.
+void decode_one_hot(const mb_simple_config& c, const float* features, const uint32_t* targets, size_t rows,
+                    std::vector<uint32_t>& a, std::vector<uint32_t>& b);
+
+}  // namespace simple
+}  // namespace mb

@@ -1,0 +1,187 @@
+// grok-simple configuration: validation, parameter groups, seeded
+// initialisation and one-hot decoding (host side of the C ABI).
+//
+// Restates src/simple/mod.rs: SimpleConfig::validate :561-694 (the rules that
+// concern mesh-mlp, tied-rotary-residual-dense-mlp and
+// shared-neighbor-mesh-mlp), layers :720-756, mesh_layers :758-765, groups
+// :871-889, initial_parameters :938-1036 (default near-identity shared
+// chain, uniform fan-in embedding) and encode :1039-1055.  Compiled with
+// -ffp-contract=off: the f32 uniform draws and the f64 Box-Muller draws
+// round exactly as the reference's.
+
+#include <cmath>
+#include <string>
+
+#include "simple.h"
+
+namespace mb {
+namespace simple {
+
+int parents(const mb_simple_config& c) { return c.connectivity == kOwn ? 1 : 2; }
+
+int stride(const mb_simple_config& c, int layer) {
+  // src/simple/mod.rs:178-186 with src/gpt/config.rs:117-122
+  if (c.connectivity == kOwn) return 0;
+  if (c.connectivity == kNeighbor) return 1;
+  const int log2w = 31 - __builtin_clz(c.width);
+  return 1 << (layer % log2w);
+}
+
+int mesh_layers(const mb_simple_config& c) {
+  if (c.architecture == kMeshMlp) return (int)c.depth - 1;
+  if (c.architecture == kSharedNeighbor) return (int)(c.embedding_mesh_depth + c.depth);
+  return 0;
+}
+
+std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& c) {
+  std::vector<std::pair<uint32_t, uint32_t>> l;
+  if (c.architecture == kMeshMlp) {
+    l.push_back({2 * c.modulus, c.width});
+    l.push_back({c.width, c.modulus});
+  } else if (c.architecture == kRotaryDense) {
+    l.push_back({c.modulus, c.width});
+    for (uint32_t i = 0; i < c.depth; ++i) l.push_back({c.width, c.width});
+  }
+  return l;
+}
+
+std::vector<size_t> groups(const mb_simple_config& c) {
+  std::vector<size_t> g;
+  if (c.architecture == kSharedNeighbor) {
+    for (uint32_t i = 0; i < c.embedding_mesh_depth; ++i) g.push_back(2 * (size_t)c.width);
+    for (uint32_t i = 0; i < c.depth; ++i) g.push_back(3 * (size_t)c.width);
+    return g;
+  }
+  for (auto& d : dense_layers(c)) g.push_back((size_t)d.first * d.second);
+  for (int i = 0; i < mesh_layers(c); ++i) g.push_back((size_t)parents(c) * c.width);
+  return g;
+}
+
+size_t parameter_count(const mb_simple_config& c) {
+  size_t n = 0;
+  for (size_t g : groups(c)) n += g;
+  return n;
+}
+
+void validate(const mb_simple_config& c) {
+  require(c.architecture <= kSharedNeighbor,
+          "architecture must be 0 (mesh-mlp), 1 (tied-rotary-residual-dense-mlp) or 2 (shared-neighbor-mesh-mlp)",
+          MB_ERR_UNSUPPORTED);
+  require(c.activation <= kSquare, "activation must be 0 (relu) or 1 (square)");
+  require(c.connectivity <= kButterfly, "connectivity must be 0 (own), 1 (neighbor) or 2 (butterfly)");
+  require(c.full_mesh_initialization <= 1, "full-mesh initialization must be 0 (kaiming) or 1 (identity-hidden)");
+  require(c.modulus >= 2 && c.modulus <= kMaxClasses, "modulus must be in 2..=1024");
+  require(c.width >= 1 && c.width <= kMaxWidth, "width must be in 1..=16384");
+  require(c.depth >= 1 && c.depth <= kMaxDepth, "depth must be in 1..=64");
+  if (c.architecture == kSharedNeighbor)
+    require(c.embedding_mesh_depth >= 1 && c.embedding_mesh_depth <= kMaxDepth,
+            "shared Neighbor embedding depth must be in 1..=64");
+  if (mesh_layers(c) > 0 && parents(c) == 2) require(c.width >= 2, "a second mesh parent needs a width of at least 2");
+  if (c.architecture != kMeshMlp)
+    require(c.width >= 2 && c.width % 2 == 0, "rotary roles need one-hot encoding and a positive even width");
+  if (c.full_mesh_initialization != 0)
+    require(c.architecture == kSharedNeighbor, "only a full mesh configures its mesh initialization");
+  if (c.architecture == kSharedNeighbor)
+    require(c.width >= c.modulus && c.width % 2 == 0 && c.connectivity != kOwn,
+            "shared Neighbor meshes need one-hot inputs, even width >= classes, two core parents and "
+            "embedding depth 1..=64");
+  require(c.mesh_learning_rate_multiplier >= 1, "the mesh learning rate multiplier must be positive");
+  if (c.mesh_learning_rate_multiplier != 1)
+    require(mesh_layers(c) > 0, "only mesh layers multiply their learning rate");
+  require(parameter_count(c) <= kMaxParameters, "models are limited to 268435456 parameters");
+}
+
+void validate_kernel_shapes(const mb_simple_config& c) {
+  validate(c);
+  require(c.width <= kMaxKernelWidth, "this build's fused row kernels support widths up to 512", MB_ERR_UNSUPPORTED);
+}
+
+namespace {
+struct Normal {
+  double radius, angle;
+};
+Normal box_muller(Random& r) {
+  const double radius = std::sqrt(-2.0 * std::log(1.0 - (double)r.unit()));
+  const double angle = 6.283185307179586 * (double)r.unit();  // TAU
+  return {radius, angle};
+}
+}  // namespace
+
+std::vector<float> initial_parameters(const mb_simple_config& c, uint64_t seed) {
+  validate(c);
+  Random r(seed ^ 0x73696d706c650004ull);
+  std::vector<float> p;
+  p.reserve(parameter_count(c));
+  const uint32_t w = c.width;
+  if (c.architecture == kSharedNeighbor) {
+    const double ratio = 0.1 / std::sqrt((double)c.embedding_mesh_depth);  // near-identity
+    const double deviation = ratio * 1.0;
+    for (size_t i = 0; i < (size_t)c.embedding_mesh_depth * w; ++i) {
+      const Normal n = box_muller(r);
+      p.push_back(1.0f);
+      p.push_back((float)(deviation * n.radius * std::cos(n.angle)));
+    }
+    for (uint32_t layer = 0; layer < c.depth; ++layer) {
+      const bool identity = c.full_mesh_initialization == 1 && layer > 0;
+      for (uint32_t u = 0; u < w; ++u) {
+        if (identity) {
+          p.push_back(1.0f);
+          p.push_back(0.0f);
+        } else {
+          const Normal n = box_muller(r);
+          p.push_back((float)(n.radius * std::cos(n.angle)));
+          p.push_back((float)(n.radius * std::sin(n.angle)));
+        }
+        p.push_back(0.0f);
+      }
+    }
+    return p;
+  }
+  const auto layers = dense_layers(c);
+  for (size_t index = 0; index < layers.size(); ++index) {
+    const size_t count = (size_t)layers[index].first * layers[index].second;
+    if (c.architecture == kRotaryDense && index > 0) {
+      const double deviation = std::sqrt(2.0 / (double)layers[index].first);  // Kaiming normal, ReLU gain
+      for (size_t off = 0; off < count; off += 2) {
+        const Normal n = box_muller(r);
+        p.push_back((float)(deviation * n.radius * std::cos(n.angle)));
+        if (off + 1 < count) p.push_back((float)(deviation * n.radius * std::sin(n.angle)));
+      }
+      continue;
+    }
+    const float bound = 1.0f / std::sqrt((float)layers[index].first);
+    for (size_t i = 0; i < count; ++i) p.push_back((2.0f * r.unit() - 1.0f) * bound);
+  }
+  for (size_t i = 0; i < (size_t)mesh_layers(c) * w; ++i) {
+    p.push_back(1.0f);
+    if (parents(c) == 2) p.push_back(0.0f);
+  }
+  return p;
+}
+
+void decode_one_hot(const mb_simple_config& c, const float* features, const uint32_t* targets, size_t rows,
+                    std::vector<uint32_t>& a, std::vector<uint32_t>& b) {
+  const uint32_t m = c.modulus;
+  a.resize(rows);
+  b.resize(rows);
+  for (size_t r = 0; r < rows; ++r) {
+    require(targets[r] < m, "answer classes must be below the modulus");
+    for (int half = 0; half < 2; ++half) {
+      const float* f = features + r * 2 * m + half * m;
+      uint32_t hot = m;
+      for (uint32_t k = 0; k < m; ++k) {
+        require(std::isfinite(f[k]), "features must contain only finite values", MB_ERR_NONFINITE);
+        if (f[k] == 1.0f && hot == m) {
+          hot = k;
+        } else {
+          require(f[k] == 0.0f, "this build's kernels read one-hot operand rows", MB_ERR_UNSUPPORTED);
+        }
+      }
+      require(hot < m, "this build's kernels read one-hot operand rows", MB_ERR_UNSUPPORTED);
+      (half == 0 ? a : b)[r] = hot;
+    }
+  }
+}
+
+}  // namespace simple
+}  // namespace mb

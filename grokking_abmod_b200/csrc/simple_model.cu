@@ -1,0 +1,1454 @@
+// grok-simple executor (host C++) and its kernels: mesh-mlp,
+// tied-rotary-residual-dense-mlp and shared-neighbor-mesh-mlp.
+//
+// Replaces GpuSimpleModel (src/simple/gpu.rs:1757-2073) and its op-by-op
+// plans (forward_with / backward_with, :2140-2700).  One training step is a
+// fixed launch sequence captured once per batch size into a CUDA graph; the
+// per-step values (minibatch offset, learning rates, AdamW corrections) sit
+// in a small device struct refreshed by one host->device copy before each
+// launch.
+//
+// Data flow, B200-first:
+//  * Operands are one-hot, so the first layer of every architecture is a
+//    gather of embedding rows by operand class (exact: the reference's dense
+//    product adds exact zeros, src/simple/dense_tiled.rs:88-159).
+//  * Row-local work runs one warp per row with the row in shared memory: the
+//    mesh stack of mesh-mlp (:240-339 of gpu.rs), the 64-layer pre-RMSNorm
+//    two-parent core of the shared-Neighbor model (:341-443, :505-630),
+//    RMSNorm and residual sums.  Backward kernels walk the layers in lockstep
+//    across the CTA's warps and reduce the per-row weight contributions in a
+//    fixed warp order into one partial per CTA; a second pass sums the CTA
+//    partials in order.  No atomics: results are bitwise reproducible.
+//  * Every dense contraction (readouts, their input and weight gradients, the
+//    residual dense projections) is a tcgen05 3xTF32 GEMM (gemm_tc.cu), with
+//    split-K over batch rows for weight gradients.
+//  * The shared-Neighbor readout (the transposed Neighbor chain,
+//    src/simple/reference.rs:257-268) equals h . E^T with E[k] the chain
+//    applied to class k's one-hot row (the reference's own identity,
+//    src/simple/mod.rs:1299-1335).  The chain therefore runs once per step on
+//    the `modulus` class rows instead of once per batch row, the readout and
+//    its gradients become GEMMs, and the chain's weight gradient is the chain
+//    backward of dE over those class rows.
+//  * Embedding gradients (operand gathers) are per-class ordered sums over
+//    the batch rows that use the class (one CTA per class).
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gemm_tc.h"
+#include "simple.h"
+
+namespace mb {
+namespace simple {
+
+#define SIMPLE_CUDA(call)                                                                           \
+  do {                                                                                              \
+    cudaError_t e_ = (call);                                                                        \
+    if (e_ != cudaSuccess)                                                                          \
+      throw Error(MB_ERR_CUDA, std::string(#call) + " failed: " + cudaGetErrorString(e_));          \
+  } while (0)
+
+constexpr float kEps = 1e-5f;         // RMSNORM_EPSILON, src/gpt/mod.rs:39
+constexpr int kFwdWarps = 8;          // forward row kernels: warps (= rows) per CTA
+constexpr int kBwdWarps = 16;         // backward row kernels: warps per CTA ...
+constexpr int kBwdRows = 2;           // ... each walking this many rows per layer
+constexpr int kMaxJ = kMaxKernelWidth / 32;  // row values per lane
+constexpr int kSplitK = 256;          // batch rows per weight-gradient GEMM chunk
+constexpr unsigned kFull = 0xffffffffu;
+
+// Values that change from step to step, read by the captured kernels.
+struct StepScalars {
+  uint32_t offset;
+  float lr_dense, lr_mesh, weight_decay, beta1, beta2, epsilon, correction1, correction2;
+};
+
+// Device status flags: [0] a tensor-core wait gave up, [1] nonfinite logits.
+enum { kFlagTc = 0, kFlagNonfinite = 1, kFlags = 2 };
+
+template <int ACT>
+__device__ __forceinline__ float act_f(float x) {
+  return ACT == kRelu ? fmaxf(x, 0.f) : x * x;
+}
+template <int ACT>
+__device__ __forceinline__ float act_g(float x) {
+  return ACT == kRelu ? (x > 0.f ? 1.f : 0.f) : 2.f * x;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+// Rotate90 roles: channel c of operand b's embedding is b[c^1], negated for
+// even c (src/simple/reference.rs:341-351).
+__device__ __forceinline__ float rotated(const float* e, int c) { return (c & 1) ? e[c - 1] : -e[c + 1]; }
+
+// ------------------------------------------------------------ batch gather
+__global__ void gather_batch(int n, const StepScalars* __restrict__ sc, const uint32_t* __restrict__ idx,
+                             const uint32_t* __restrict__ ta, const uint32_t* __restrict__ tb,
+                             const uint32_t* __restrict__ tt, uint32_t* __restrict__ a, uint32_t* __restrict__ b,
+                             uint32_t* __restrict__ y) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const uint32_t i = idx[(sc != nullptr ? sc->offset : 0u) + r];
+  a[r] = ta[i];
+  b[r] = tb[i];
+  y[r] = tt[i];
+}
+
+// ------------------------------------------------------------- mesh-mlp
+// h0 = W0[a] + W0[m + b]; per mesh layer h' = act(h)[c] w0 + act(h)[c+s] w1;
+// act = act(h_L) feeds the readout GEMM.  h[l] (l = 0..L) is kept for the
+// backward.
+template <int ACT>
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    mlp_forward(int n, int W, int m, int L, int p, const int* __restrict__ strides, const uint32_t* __restrict__ a,
+                const uint32_t* __restrict__ b, const float* __restrict__ w0, const float* __restrict__ mesh,
+                float* __restrict__ h, float* __restrict__ act) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  if (r >= n) return;
+  float* row = sm + warp * W;
+  const float* ea = w0 + (size_t)a[r] * W;
+  const float* eb = w0 + (size_t)(m + b[r]) * W;
+  const size_t nw = (size_t)n * W;
+  for (int c = lane; c < W; c += 32) {
+    const float v = ea[c] + eb[c];
+    h[(size_t)r * W + c] = v;
+    row[c] = act_f<ACT>(v);
+  }
+  for (int l = 0; l < L; ++l) {
+    __syncwarp();
+    const int s = strides[l];
+    const float* w = mesh + (size_t)l * W * p;
+    float v[kMaxJ];
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) {
+        float y = row[c] * w[c * p];
+        if (p == 2) y = fmaf(row[(c + s) % W], w[c * p + 1], y);
+        v[j] = y;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) {
+        h[(l + 1) * nw + (size_t)r * W + c] = v[j];
+        row[c] = act_f<ACT>(v[j]);
+      }
+    }
+  }
+  __syncwarp();
+  for (int c = lane; c < W; c += 32) act[(size_t)r * W + c] = row[c];
+}
+
+// dact = dlogits R^T in, dh0 out; per-CTA mesh weight partials
+// [gridDim.x][L][p*W].
+template <int ACT>
+__global__ void __launch_bounds__(kBwdWarps * 32)
+    mlp_backward(int n, int W, int L, int p, const int* __restrict__ strides, const float* __restrict__ mesh,
+                 const float* __restrict__ h, const float* __restrict__ dact, float* __restrict__ dh0,
+                 float* __restrict__ partials) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pw = p * W;
+  float* arow = sm + warp * 2 * W;  // act(h_l) of the current row
+  float* drow = arow + W;           // dh of the current row
+  float* contrib = sm + kBwdWarps * 2 * W;
+  const size_t nw = (size_t)n * W;
+  float dh[kBwdRows][kMaxJ];
+#pragma unroll
+  for (int i = 0; i < kBwdRows; ++i) {
+    const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      dh[i][j] = (r < n && c < W) ? dact[(size_t)r * W + c] * act_g<ACT>(h[L * nw + (size_t)r * W + c]) : 0.f;
+    }
+  }
+  for (int l = L - 1; l >= 0; --l) {
+    const int s = strides[l];
+    const float* w = mesh + (size_t)l * pw;
+    float* mine = contrib + warp * pw;
+    for (int t = lane; t < pw; t += 32) mine[t] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kBwdRows; ++i) {
+      const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+      const bool active = r < n;
+      float hl[kMaxJ];
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < kMaxJ; ++j) {
+        const int c = lane + 32 * j;
+        if (c < W) {
+          hl[j] = active ? h[l * nw + (size_t)r * W + c] : 0.f;
+          arow[c] = act_f<ACT>(hl[j]);
+          drow[c] = dh[i][j];
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < kMaxJ; ++j) {
+        const int c = lane + 32 * j;
+        if (c < W) {
+          const float d = drow[c];
+          mine[c * p] += d * arow[c];
+          float da = d * w[c * p];
+          if (p == 2) {
+            mine[c * p + 1] += d * arow[(c + s) % W];
+            const int q = (c - s + W) % W;
+            da = fmaf(drow[q], w[q * p + 1], da);
+          }
+          dh[i][j] = da * act_g<ACT>(hl[j]);
+        }
+      }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < pw; t += blockDim.x) {
+      float sum = 0.f;
+      for (int q = 0; q < kBwdWarps; ++q) sum += contrib[q * pw + t];
+      partials[((size_t)blockIdx.x * L + l) * pw + t] = sum;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < kBwdRows; ++i) {
+    const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+    if (r >= n) continue;
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) dh0[(size_t)r * W + c] = dh[i][j];
+    }
+  }
+}
+
+// out[t] = sum over CTAs (in order) of partials[cta][t].
+__global__ void reduce_cta_partials(const float* __restrict__ partials, int ctas, size_t count,
+                                    float* __restrict__ out) {
+  for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < count; t += (size_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int q = 0; q < ctas; ++q) s += partials[(size_t)q * count + t];
+    out[t] = s;
+  }
+}
+
+// ----------------------------------------------------- RMSNorm row helpers
+// y = x / sqrt(mean(x^2) + eps) over the warp's row; returns the inverse.
+__device__ __forceinline__ float row_inverse_rms(const float (&x)[kMaxJ], int W, int lane) {
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxJ; ++j)
+    if (lane + 32 * j < W) ss = fmaf(x[j], x[j], ss);
+  ss = warp_sum(ss);
+  return 1.0f / sqrtf(ss / (float)W + kEps);
+}
+
+// Rotary operand embedding h0 = E[a] + rot(E[b]) and n0 = RMSNorm(h0)
+// (tied-rotary-residual-dense-mlp; also the shared-Neighbor core input).
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    rotary_embed(int n, int W, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                 const float* __restrict__ E, float* __restrict__ h0, float* __restrict__ n0,
+                 float* __restrict__ inv0) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  if (r >= n) return;
+  const float* ea = E + (size_t)a[r] * W;
+  const float* eb = E + (size_t)b[r] * W;
+  float v[kMaxJ];
+#pragma unroll
+  for (int j = 0; j < kMaxJ; ++j) {
+    const int c = lane + 32 * j;
+    v[j] = c < W ? ea[c] + rotated(eb, c) : 0.f;
+  }
+  const float inv = row_inverse_rms(v, W, lane);
+#pragma unroll
+  for (int j = 0; j < kMaxJ; ++j) {
+    const int c = lane + 32 * j;
+    if (c < W) {
+      h0[(size_t)r * W + c] = v[j];
+      if (n0 != nullptr) n0[(size_t)r * W + c] = v[j] * inv;
+    }
+  }
+  if (inv0 != nullptr && lane == 0) inv0[r] = inv;
+}
+
+// h' = h + act(z); n' = RMSNorm(h') (a dense residual block's epilogue).
+template <int ACT>
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    residual_norm(int n, int W, const float* __restrict__ h, const float* __restrict__ z, float* __restrict__ hn,
+                  float* __restrict__ nn, float* __restrict__ inv_out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  if (r >= n) return;
+  float v[kMaxJ];
+#pragma unroll
+  for (int j = 0; j < kMaxJ; ++j) {
+    const int c = lane + 32 * j;
+    v[j] = c < W ? h[(size_t)r * W + c] + act_f<ACT>(z[(size_t)r * W + c]) : 0.f;
+  }
+  const float inv = row_inverse_rms(v, W, lane);
+#pragma unroll
+  for (int j = 0; j < kMaxJ; ++j) {
+    const int c = lane + 32 * j;
+    if (c < W) {
+      hn[(size_t)r * W + c] = v[j];
+      nn[(size_t)r * W + c] = v[j] * inv;
+    }
+  }
+  if (lane == 0) inv_out[r] = inv;
+}
+
+// dx = add + inv (dy - y <dy, y> / W) with y the normalised row.
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    rms_backward(int n, int W, const float* __restrict__ y, const float* __restrict__ inv,
+                 const float* __restrict__ dy, const float* add, float* dx) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  if (r >= n) return;
+  float yv[kMaxJ], dv[kMaxJ], dot = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxJ; ++j) {
+    const int c = lane + 32 * j;
+    yv[j] = c < W ? y[(size_t)r * W + c] : 0.f;
+    dv[j] = c < W ? dy[(size_t)r * W + c] : 0.f;
+    dot = fmaf(dv[j], yv[j], dot);
+  }
+  dot = warp_sum(dot) / (float)W;
+  const float iv = inv[r];
+#pragma unroll
+  for (int j = 0; j < kMaxJ; ++j) {
+    const int c = lane + 32 * j;
+    if (c < W) {
+      const float g = iv * (dv[j] - yv[j] * dot);
+      dx[(size_t)r * W + c] = add != nullptr ? add[(size_t)r * W + c] + g : g;
+    }
+  }
+}
+
+// dz = dh * act'(z)
+template <int ACT>
+__global__ void activation_gradient(size_t count, const float* __restrict__ dh, const float* __restrict__ z,
+                                    float* __restrict__ dz) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
+    dz[i] = dh[i] * act_g<ACT>(z[i]);
+}
+
+// ---------------------------------------------------- shared-Neighbor
+// Class rows of the shared linear Neighbor chain: states[0][k] = e_k,
+// states[l+1][k][c] = states[l][k][c] w0[c] + states[l][k][c+1] w1[c].
+// states[ed] is the embedding E used by the operands and the readout.
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    chain_forward(int m, int W, int ed, const float* __restrict__ chain, float* __restrict__ states) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int k = blockIdx.x * kFwdWarps + warp;
+  if (k >= m) return;
+  float* row = sm + warp * W;
+  const size_t mw = (size_t)m * W;
+  for (int c = lane; c < W; c += 32) {
+    row[c] = c == k ? 1.f : 0.f;
+    states[(size_t)k * W + c] = row[c];
+  }
+  for (int l = 0; l < ed; ++l) {
+    __syncwarp();
+    const float* w = chain + (size_t)l * 2 * W;
+    float v[kMaxJ];
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) v[j] = fmaf(row[(c + 1) % W], w[2 * c + 1], row[c] * w[2 * c]);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) {
+        row[c] = v[j];
+        states[(l + 1) * mw + (size_t)k * W + c] = v[j];
+      }
+    }
+  }
+}
+
+// The pre-RMSNorm residual two-parent core: h <- h + act(n[c] w0 + n[c+s] w1
+// + bias), n = RMSNorm(h); hs[l] keeps each layer's input, hf = RMSNorm(h).
+template <int ACT>
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    shared_forward(int n, int W, int depth, const int* __restrict__ strides, const uint32_t* __restrict__ a,
+                   const uint32_t* __restrict__ b, const float* __restrict__ E, const float* __restrict__ core,
+                   float* __restrict__ hs, float* __restrict__ hf, float* __restrict__ invf) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  if (r >= n) return;
+  float* row = sm + warp * W;
+  const float* ea = E + (size_t)a[r] * W;
+  const float* eb = E + (size_t)b[r] * W;
+  const size_t nw = (size_t)n * W;
+  float h[kMaxJ];
+#pragma unroll
+  for (int j = 0; j < kMaxJ; ++j) {
+    const int c = lane + 32 * j;
+    h[j] = c < W ? ea[c] + rotated(eb, c) : 0.f;
+  }
+  for (int l = 0; l < depth; ++l) {
+    const float inv = row_inverse_rms(h, W, lane);
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) {
+        hs[l * nw + (size_t)r * W + c] = h[j];
+        row[c] = h[j] * inv;
+      }
+    }
+    __syncwarp();
+    const int s = strides[l];
+    const float* w = core + (size_t)l * 3 * W;
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) {
+        const float z = fmaf(row[(c + s) % W], w[3 * c + 1], row[c] * w[3 * c]) + w[3 * c + 2];
+        h[j] += act_f<ACT>(z);
+      }
+    }
+  }
+  const float inv = row_inverse_rms(h, W, lane);
+#pragma unroll
+  for (int j = 0; j < kMaxJ; ++j) {
+    const int c = lane + 32 * j;
+    if (c < W) hf[(size_t)r * W + c] = h[j] * inv;
+  }
+  if (lane == 0) invf[r] = inv;
+}
+
+// Backward of the core: dhf (gradient of the final RMSNorm output) in, dh0
+// out; per-CTA weight partials [gridDim.x][depth][3W] (w0, w1, bias per unit).
+template <int ACT>
+__global__ void __launch_bounds__(kBwdWarps * 32)
+    shared_backward(int n, int W, int depth, const int* __restrict__ strides, const float* __restrict__ core,
+                    const float* __restrict__ hs, const float* __restrict__ hf, const float* __restrict__ invf,
+                    const float* __restrict__ dhf, float* __restrict__ dh0, float* __restrict__ partials) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pw = 3 * W;
+  float* nrow = sm + warp * 2 * W;
+  float* zrow = nrow + W;  // dz
+  float* contrib = sm + kBwdWarps * 2 * W;
+  const size_t nw = (size_t)n * W;
+  float dh[kBwdRows][kMaxJ];
+#pragma unroll
+  for (int i = 0; i < kBwdRows; ++i) {
+    const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+    const bool active = r < n;
+    float yv[kMaxJ], dv[kMaxJ], dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      yv[j] = (active && c < W) ? hf[(size_t)r * W + c] : 0.f;
+      dv[j] = (active && c < W) ? dhf[(size_t)r * W + c] : 0.f;
+      dot = fmaf(dv[j], yv[j], dot);
+    }
+    dot = warp_sum(dot) / (float)W;
+    const float iv = active ? invf[r] : 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) dh[i][j] = iv * (dv[j] - yv[j] * dot);
+  }
+  for (int l = depth - 1; l >= 0; --l) {
+    const int s = strides[l];
+    const float* w = core + (size_t)l * pw;
+    float* mine = contrib + warp * pw;
+    for (int t = lane; t < pw; t += 32) mine[t] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kBwdRows; ++i) {
+      const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+      const bool active = r < n;
+      float x[kMaxJ];
+#pragma unroll
+      for (int j = 0; j < kMaxJ; ++j) {
+        const int c = lane + 32 * j;
+        x[j] = (active && c < W) ? hs[l * nw + (size_t)r * W + c] : 0.f;
+      }
+      const float inv = row_inverse_rms(x, W, lane);
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < kMaxJ; ++j) {
+        const int c = lane + 32 * j;
+        if (c < W) nrow[c] = x[j] * inv;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < kMaxJ; ++j) {
+        const int c = lane + 32 * j;
+        if (c < W) {
+          const float z = fmaf(nrow[(c + s) % W], w[3 * c + 1], nrow[c] * w[3 * c]) + w[3 * c + 2];
+          zrow[c] = dh[i][j] * act_g<ACT>(z);
+        }
+      }
+      __syncwarp();
+      float dn[kMaxJ], dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < kMaxJ; ++j) {
+        const int c = lane + 32 * j;
+        dn[j] = 0.f;
+        if (c < W) {
+          const float dz = zrow[c];
+          mine[3 * c] += dz * nrow[c];
+          mine[3 * c + 1] += dz * nrow[(c + s) % W];
+          mine[3 * c + 2] += dz;
+          const int q = (c - s + W) % W;
+          dn[j] = fmaf(zrow[q], w[3 * q + 1], dz * w[3 * c]);
+          dot = fmaf(dn[j], nrow[c], dot);
+        }
+      }
+      dot = warp_sum(dot) / (float)W;
+#pragma unroll
+      for (int j = 0; j < kMaxJ; ++j) {
+        const int c = lane + 32 * j;
+        if (c < W) dh[i][j] += inv * (dn[j] - nrow[c] * dot);
+      }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < pw; t += blockDim.x) {
+      float sum = 0.f;
+      for (int q = 0; q < kBwdWarps; ++q) sum += contrib[q * pw + t];
+      partials[((size_t)blockIdx.x * depth + l) * pw + t] = sum;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < kBwdRows; ++i) {
+    const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+    if (r >= n) continue;
+#pragma unroll
+    for (int j = 0; j < kMaxJ; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) dh0[(size_t)r * W + c] = dh[i][j];
+    }
+  }
+}
+
+// Chain backward over the class rows: dv = dE[k]; for l = ed-1 .. 0 the
+// chain weights' gradient sums dv[c] v_l[c] and dv[c] v_l[c+1] over the
+// class rows (fixed order: warp-strided rows, then warps in order), and
+// dv <- dv[c] w0[c] + dv[c-1] w1[c-1].  One CTA; dv lives in `dvbuf`.
+constexpr int kChainWarps = 16;
+__global__ void __launch_bounds__(kChainWarps * 32)
+    chain_backward(int m, int W, int ed, const float* __restrict__ chain, const float* __restrict__ states,
+                   const float* __restrict__ dE, float* __restrict__ dvbuf, float* __restrict__ grad) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* vrow = sm + warp * 2 * W;
+  float* drow = vrow + W;
+  float* contrib = sm + kChainWarps * 2 * W;
+  float* mine = contrib + warp * 2 * W;
+  const size_t mw = (size_t)m * W;
+  for (int k = warp; k < m; k += kChainWarps)
+    for (int c = lane; c < W; c += 32) dvbuf[(size_t)k * W + c] = dE[(size_t)k * W + c];
+  for (int l = ed - 1; l >= 0; --l) {
+    const float* w = chain + (size_t)l * 2 * W;
+    for (int t = lane; t < 2 * W; t += 32) mine[t] = 0.f;
+    for (int k = warp; k < m; k += kChainWarps) {
+      __syncwarp();
+      for (int c = lane; c < W; c += 32) {
+        vrow[c] = states[l * mw + (size_t)k * W + c];
+        drow[c] = dvbuf[(size_t)k * W + c];
+      }
+      __syncwarp();
+      for (int c = lane; c < W; c += 32) {
+        const float d = drow[c];
+        mine[2 * c] += d * vrow[c];
+        mine[2 * c + 1] += d * vrow[(c + 1) % W];
+        const int q = (c + W - 1) % W;
+        dvbuf[(size_t)k * W + c] = fmaf(drow[q], w[2 * q + 1], d * w[2 * c]);
+      }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < 2 * W; t += blockDim.x) {
+      float sum = 0.f;
+      for (int q = 0; q < kChainWarps; ++q) sum += contrib[q * 2 * W + t];
+      grad[(size_t)l * 2 * W + t] = sum;
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------ embedding
+// Per class k (one CTA each): the ordered sum over batch rows of the
+// operand-embedding gradients that use row k of the embedding.
+//  mode 0 (mesh-mlp, 2m rows of W0): k < m takes rows with a == k,
+//         k >= m rows with b == k - m, both as dh0[r][c].
+//  mode 1 (rotary): rows with a == k add dh0[r][c]; rows with b == k add
+//         the transposed rotation of dh0[r] (dh0[r][c^1], negated for odd c).
+// `extra` ([rows][W], may be null) is added (the readout's share of dE).
+constexpr int kClassThreads = 256;
+__global__ void __launch_bounds__(kClassThreads)
+    class_gradient(int n, int W, int m, int mode, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                   const float* __restrict__ dh0, const float* __restrict__ extra, float* __restrict__ out) {
+  __shared__ int list[kClassThreads];
+  __shared__ int kinds[kClassThreads];
+  __shared__ int warp_count[kClassThreads / 32];
+  __shared__ int total;
+  const int k = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int kPer = kMaxKernelWidth / kClassThreads;
+  float acc[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+  for (int r0 = 0; r0 < n; r0 += kClassThreads) {
+    const int r = r0 + tid;
+    int kind = 0;
+    if (r < n) {
+      if (mode == 0) {
+        kind = (k < m) ? (a[r] == (uint32_t)k ? 1 : 0) : (b[r] == (uint32_t)(k - m) ? 1 : 0);
+      } else {
+        kind = (a[r] == (uint32_t)k ? 1 : 0) | (b[r] == (uint32_t)k ? 2 : 0);
+      }
+    }
+    const unsigned ballot = __ballot_sync(kFull, kind != 0);
+    if (lane == 0) warp_count[warp] = __popc(ballot);
+    __syncthreads();
+    if (tid == 0) {
+      int s = 0;
+      for (int q = 0; q < kClassThreads / 32; ++q) {
+        const int c = warp_count[q];
+        warp_count[q] = s;
+        s += c;
+      }
+      total = s;
+    }
+    __syncthreads();
+    if (kind != 0) {
+      const int pos = warp_count[warp] + __popc(ballot & ((1u << lane) - 1u));
+      list[pos] = r;
+      kinds[pos] = kind;
+    }
+    __syncthreads();
+    for (int e = 0; e < total; ++e) {
+      const int rr = list[e], kd = kinds[e];
+      const float* g = dh0 + (size_t)rr * W;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int c = tid + kClassThreads * j;
+        if (c < W) {
+          if (kd & 1) acc[j] += g[c];
+          if (kd & 2) acc[j] += (c & 1) ? -g[c ^ 1] : g[c ^ 1];
+        }
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int c = tid + kClassThreads * j;
+    if (c < W) out[(size_t)k * W + c] = acc[j] + (extra != nullptr ? extra[(size_t)k * W + c] : 0.f);
+  }
+}
+
+// ------------------------------------------------------- loss and update
+// dlogits = (softmax - onehot) / rows (src/simple/gpu.rs:664-739); flags
+// nonfinite logits.
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    cross_entropy_gradient(int n, int m, const float* __restrict__ logits, const uint32_t* __restrict__ y,
+                           float* __restrict__ dlog, int* __restrict__ flags) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  if (r >= n) return;
+  const float* x = logits + (size_t)r * m;
+  float mx = -INFINITY;
+  bool finite = true;
+  for (int k = lane; k < m; k += 32) {
+    finite &= isfinite(x[k]);
+    mx = fmaxf(mx, x[k]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+  float s = 0.f;
+  for (int k = lane; k < m; k += 32) s += expf(x[k] - mx);
+  s = warp_sum(s);
+  if (!__all_sync(kFull, finite) && lane == 0) atomicExch(flags + kFlagNonfinite, 1);
+  const float scale = 1.0f / (float)n;
+  const uint32_t t = y[r];
+  for (int k = lane; k < m; k += 32) {
+    const float p = expf(x[k] - mx) / s;
+    dlog[(size_t)r * m + k] = (p - (k == (int)t ? 1.f : 0.f)) * scale;
+  }
+}
+
+// First maximum per row; nonfinite rows get 0xFFFFFFFF
+// (src/simple/gpu.rs:748-772).
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    predictions(int n, int m, const float* __restrict__ logits, uint32_t* __restrict__ out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  if (r >= n) return;
+  const float* x = logits + (size_t)r * m;
+  float best = -INFINITY;
+  int arg = m;
+  bool finite = true;
+  for (int k = lane; k < m; k += 32) {
+    finite &= isfinite(x[k]);
+    if (x[k] > best || arg == m) {
+      if (arg == m || x[k] > best) {
+        best = x[k];
+        arg = k;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float ob = __shfl_xor_sync(kFull, best, o);
+    const int oa = __shfl_xor_sync(kFull, arg, o);
+    if (ob > best || (ob == best && oa < arg)) {
+      best = ob;
+      arg = oa;
+    }
+  }
+  finite = __all_sync(kFull, finite);
+  if (lane == 0) out[r] = finite ? (uint32_t)arg : 0xFFFFFFFFu;
+}
+
+// simple_adam (src/simple/gpu.rs:787-812) over the flat parameters; groups
+// from index `mesh_start` on train at lr_mesh.
+__global__ void adamw(size_t count, size_t mesh_start, const StepScalars* __restrict__ sc,
+                      const float* __restrict__ grad, float* __restrict__ w, float* __restrict__ m1,
+                      float* __restrict__ m2) {
+  const float b1 = sc->beta1, b2 = sc->beta2, eps = sc->epsilon, wd = sc->weight_decay;
+  const float c1 = sc->correction1, c2 = sc->correction2;
+  const float ob1 = __fsub_rn(1.0f, b1), ob2 = __fsub_rn(1.0f, b2);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+    const float lr = i < mesh_start ? sc->lr_dense : sc->lr_mesh;
+    const float g = grad[i];
+    const float mm = __fadd_rn(__fmul_rn(b1, m1[i]), __fmul_rn(ob1, g));
+    const float vv = __fadd_rn(__fmul_rn(b2, m2[i]), __fmul_rn(__fmul_rn(ob2, g), g));
+    m1[i] = mm;
+    m2[i] = vv;
+    const float mh = __fdiv_rn(mm, c1), vh = __fdiv_rn(vv, c2);
+    const float upd = __fadd_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), __fmul_rn(wd, w[i]));
+    w[i] = __fsub_rn(w[i], __fmul_rn(lr, upd));
+  }
+}
+
+// ================================================================ executor
+class DeviceBuffers {
+ public:
+  ~DeviceBuffers() {
+    for (void* p : ptrs_) cudaFree(p);
+  }
+  template <class T>
+  T* alloc(size_t n) {
+    void* p = nullptr;
+    SIMPLE_CUDA(cudaMalloc(&p, n == 0 ? 16 : n * sizeof(T)));
+    ptrs_.push_back(p);
+    return static_cast<T*>(p);
+  }
+
+ private:
+  std::vector<void*> ptrs_;
+};
+
+struct Workspace {
+  int n = 0;
+  DeviceBuffers mem;
+  uint32_t *a, *b, *y;
+  float *logits, *dlog;
+  float *h, *act, *dact, *dh0, *part;  // mesh-mlp
+  float *hs, *ns, *invs, *zs, *dh, *dz, *dn, *dhf, *dEread, *gemm_part;
+  float *hf, *invf, *states, *dEemb, *dv;  // shared-Neighbor
+  int bwd_ctas = 0;
+  cudaGraphExec_t step_graph = nullptr;
+  uint64_t graph_table = 0, graph_batches = 0;  // serials the graph was captured with
+  uint32_t step_launches = 0;
+  ~Workspace() {
+    if (step_graph) cudaGraphExecDestroy(step_graph);
+  }
+};
+
+}  // namespace simple
+}  // namespace mb
+
+struct mb_simple_table {
+  const void* owner;
+  uint64_t serial;
+  size_t rows;
+  mb::simple::DeviceBuffers mem;
+  uint32_t *a, *b, *t, *identity;
+};
+
+struct mb_simple_batches {
+  const void* owner;
+  uint64_t serial;
+  size_t count, table_rows;
+  mb::simple::DeviceBuffers mem;
+  uint32_t* idx;
+};
+
+namespace mb {
+namespace simple {
+
+class SimpleModel {
+ public:
+  SimpleModel(int device, const mb_simple_config& c, uint64_t seed) : c_(c), device_(device) {
+    validate_kernel_shapes(c);
+    int count = 0;
+    SIMPLE_CUDA(cudaGetDeviceCount(&count));
+    require(device >= 0 && device < count, "CUDA device index out of range");
+    SIMPLE_CUDA(cudaSetDevice(device));
+    SIMPLE_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    gemm_prepare();
+    groups_ = groups(c);
+    size_t off = 0;
+    for (size_t g : groups_) {
+      offsets_.push_back(off);
+      off += g;
+    }
+    P_ = off;
+    mesh_start_ = 0;
+    for (size_t i = 0; i < dense_layers(c).size(); ++i) mesh_start_ += groups_[i];
+    w_ = mem_.alloc<float>(P_);
+    m1_ = mem_.alloc<float>(P_);
+    m2_ = mem_.alloc<float>(P_);
+    grad_ = mem_.alloc<float>(P_);
+    flags_ = mem_.alloc<int>(kFlags);
+    scalars_ = mem_.alloc<StepScalars>(1);
+    SIMPLE_CUDA(cudaMemsetAsync(flags_, 0, kFlags * sizeof(int), stream_));
+    SIMPLE_CUDA(cudaMemsetAsync(grad_, 0, P_ * sizeof(float), stream_));
+    const int nstr = c.architecture == kMeshMlp ? std::max(1, mesh_layers(c)) : (int)c.depth;
+    std::vector<int> st(nstr);
+    for (int l = 0; l < nstr; ++l) st[l] = stride(c, l);
+    strides_ = mem_.alloc<int>(nstr);
+    SIMPLE_CUDA(cudaMemcpy(strides_, st.data(), nstr * sizeof(int), cudaMemcpyHostToDevice));
+    set_parameters(initial_parameters(c, seed).data(), P_);
+    set_attributes();
+  }
+  ~SimpleModel() {
+    workspaces_.clear();
+    if (stream_) cudaStreamDestroy(stream_);
+  }
+
+  const mb_simple_config& config() const { return c_; }
+  size_t count() const { return P_; }
+  cudaStream_t stream() const { return stream_; }
+
+  void set_parameters(const float* v, size_t n) {
+    require(n == P_, "parameter count does not match the model");
+    for (size_t i = 0; i < n; ++i) require(std::isfinite(v[i]), "parameters must be finite", MB_ERR_NONFINITE);
+    SIMPLE_CUDA(cudaSetDevice(device_));
+    SIMPLE_CUDA(cudaMemcpyAsync(w_, v, P_ * sizeof(float), cudaMemcpyHostToDevice, stream_));
+    SIMPLE_CUDA(cudaMemsetAsync(m1_, 0, P_ * sizeof(float), stream_));
+    SIMPLE_CUDA(cudaMemsetAsync(m2_, 0, P_ * sizeof(float), stream_));
+    SIMPLE_CUDA(cudaStreamSynchronize(stream_));
+    beta1_power_ = 1.0f;
+    beta2_power_ = 1.0f;
+  }
+
+  void get_parameters(float* out, size_t n) {
+    require(n == P_, "parameter count does not match the model");
+    SIMPLE_CUDA(cudaSetDevice(device_));
+    SIMPLE_CUDA(cudaMemcpyAsync(out, w_, P_ * sizeof(float), cudaMemcpyDeviceToHost, stream_));
+    SIMPLE_CUDA(cudaStreamSynchronize(stream_));
+    for (size_t i = 0; i < n; ++i) require(std::isfinite(out[i]), "nonfinite parameters", MB_ERR_NONFINITE);
+  }
+
+  mb_simple_table* upload_table(const float* features, const uint32_t* targets, size_t rows) {
+    require(rows >= 1 && rows <= kMaxRows, "tables need 1..=131072 rows");
+    std::vector<uint32_t> a, b;
+    decode_one_hot(c_, features, targets, rows, a, b);
+    std::vector<uint32_t> ident(rows);
+    for (size_t i = 0; i < rows; ++i) ident[i] = (uint32_t)i;
+    SIMPLE_CUDA(cudaSetDevice(device_));
+    auto t = std::make_unique<mb_simple_table>();
+    t->owner = this;
+    t->serial = ++serial_;
+    t->rows = rows;
+    t->a = t->mem.alloc<uint32_t>(rows);
+    t->b = t->mem.alloc<uint32_t>(rows);
+    t->t = t->mem.alloc<uint32_t>(rows);
+    t->identity = t->mem.alloc<uint32_t>(rows);
+    SIMPLE_CUDA(cudaMemcpy(t->a, a.data(), rows * 4, cudaMemcpyHostToDevice));
+    SIMPLE_CUDA(cudaMemcpy(t->b, b.data(), rows * 4, cudaMemcpyHostToDevice));
+    SIMPLE_CUDA(cudaMemcpy(t->t, targets, rows * 4, cudaMemcpyHostToDevice));
+    SIMPLE_CUDA(cudaMemcpy(t->identity, ident.data(), rows * 4, cudaMemcpyHostToDevice));
+    return t.release();
+  }
+
+  mb_simple_batches* upload_batches(const mb_simple_table* table, const uint32_t* idx, size_t count) {
+    check_table(table);
+    require(count >= 1 && count <= kMaxRows, "batches need 1..=131072 indices");
+    for (size_t i = 0; i < count; ++i) require(idx[i] < table->rows, "batch index is outside the table");
+    SIMPLE_CUDA(cudaSetDevice(device_));
+    auto bt = std::make_unique<mb_simple_batches>();
+    bt->owner = this;
+    bt->serial = ++serial_;
+    bt->count = count;
+    bt->table_rows = table->rows;
+    bt->idx = bt->mem.alloc<uint32_t>(count);
+    SIMPLE_CUDA(cudaMemcpy(bt->idx, idx, count * 4, cudaMemcpyHostToDevice));
+    return bt.release();
+  }
+
+  void train_step(const mb_simple_table* table, const mb_simple_batches* batches, size_t offset, size_t rows,
+                  const mb_adamw& o) {
+    check_table(table);
+    check_batches(table, batches, offset, rows);
+    mb::validate_optimizer(o);
+    SIMPLE_CUDA(cudaSetDevice(device_));
+    Workspace& ws = workspace((int)rows);
+    // AdamW corrections from f32 host powers (src/simple/gpu.rs:2044-2047).
+    beta1_power_ *= o.beta1;
+    beta2_power_ *= o.beta2;
+    StepScalars s{};
+    s.offset = (uint32_t)offset;
+    s.lr_dense = o.learning_rate;
+    s.lr_mesh = o.learning_rate * (float)c_.mesh_learning_rate_multiplier;
+    s.weight_decay = o.weight_decay;
+    s.beta1 = o.beta1;
+    s.beta2 = o.beta2;
+    s.epsilon = o.epsilon;
+    s.correction1 = 1.0f - beta1_power_;
+    s.correction2 = 1.0f - beta2_power_;
+    // Pageable source: the copy has consumed `s` when the call returns.
+    SIMPLE_CUDA(cudaMemcpyAsync(scalars_, &s, sizeof(s), cudaMemcpyHostToDevice, stream_));
+    if (ws.step_graph == nullptr || ws.graph_table != table->serial || ws.graph_batches != batches->serial) {
+      if (ws.step_graph) {
+        cudaGraphExecDestroy(ws.step_graph);
+        ws.step_graph = nullptr;
+      }
+      cudaGraph_t g = nullptr;
+      SIMPLE_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+      launches_ = 0;
+      try {
+        enqueue_gather(ws, table, batches->idx, true);
+        enqueue_forward(ws);
+        enqueue_loss(ws);
+        enqueue_backward(ws);
+        enqueue_update();
+      } catch (...) {
+        cudaStreamEndCapture(stream_, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      SIMPLE_CUDA(cudaStreamEndCapture(stream_, &g));
+      cudaError_t e = cudaGraphInstantiate(&ws.step_graph, g, 0);
+      cudaGraphDestroy(g);
+      SIMPLE_CUDA(e);
+      ws.graph_table = table->serial;
+      ws.graph_batches = batches->serial;
+      ws.step_launches = launches_;
+    }
+    last_launches_ = ws.step_launches;
+    SIMPLE_CUDA(cudaGraphLaunch(ws.step_graph, stream_));
+  }
+
+  void evaluate(const mb_simple_table* table, float* logits, uint32_t* preds) {
+    check_table(table);
+    SIMPLE_CUDA(cudaSetDevice(device_));
+    Workspace& ws = workspace((int)table->rows);
+    enqueue_gather(ws, table, table->identity, false);
+    enqueue_forward(ws);
+    const int n = ws.n, m = (int)c_.modulus;
+    predictions<<<(n + kFwdWarps - 1) / kFwdWarps, kFwdWarps * 32, 0, stream_>>>(n, m, ws.logits, ws.a); ++launches_;
+    SIMPLE_CUDA(cudaGetLastError());
+    std::vector<uint32_t> p(n);
+    SIMPLE_CUDA(cudaMemcpyAsync(p.data(), ws.a, n * 4, cudaMemcpyDeviceToHost, stream_));
+    if (logits != nullptr)
+      SIMPLE_CUDA(cudaMemcpyAsync(logits, ws.logits, (size_t)n * m * 4, cudaMemcpyDeviceToHost, stream_));
+    SIMPLE_CUDA(cudaStreamSynchronize(stream_));
+    check_tc();
+    for (uint32_t v : p) require(v != 0xFFFFFFFFu, "logits must contain only finite values", MB_ERR_NONFINITE);
+    if (preds != nullptr) std::memcpy(preds, p.data(), n * 4);
+  }
+
+  double loss_and_gradient(const mb_simple_table* table, const uint32_t* idx, size_t count, float* grad,
+                           size_t ngrad) {
+    require(ngrad == P_, "gradient length must equal the parameter count");
+    std::unique_ptr<mb_simple_batches> bt(upload_batches(table, idx, count));
+    Workspace& ws = workspace((int)count);
+    enqueue_gather(ws, table, bt->idx, false);
+    enqueue_forward(ws);
+    enqueue_loss(ws);
+    enqueue_backward(ws);
+    const int m = (int)c_.modulus;
+    std::vector<float> lg((size_t)count * m);
+    std::vector<uint32_t> tg(table->rows);
+    SIMPLE_CUDA(cudaMemcpyAsync(lg.data(), ws.logits, lg.size() * 4, cudaMemcpyDeviceToHost, stream_));
+    SIMPLE_CUDA(cudaMemcpyAsync(grad, grad_, P_ * 4, cudaMemcpyDeviceToHost, stream_));
+    SIMPLE_CUDA(cudaMemcpyAsync(tg.data(), table->t, table->rows * 4, cudaMemcpyDeviceToHost, stream_));
+    SIMPLE_CUDA(cudaStreamSynchronize(stream_));
+    check_tc();
+    // The mean answer cross-entropy from the f32 logits in f64, row order
+    // (src/simple/gpu.rs:2005-2019).
+    double loss = 0.0;
+    for (size_t r = 0; r < count; ++r) {
+      const float* x = lg.data() + r * m;
+      double mx = -INFINITY;
+      for (int k = 0; k < m; ++k) {
+        require(std::isfinite(x[k]), "logits must contain only finite values", MB_ERR_NONFINITE);
+        mx = std::max(mx, (double)x[k]);
+      }
+      double s = 0.0;
+      for (int k = 0; k < m; ++k) s += std::exp((double)x[k] - mx);
+      loss += std::log(s) + mx - (double)x[tg[idx[r]]];
+    }
+    for (size_t i = 0; i < P_; ++i) require(std::isfinite(grad[i]), "nonfinite gradients", MB_ERR_NONFINITE);
+    return loss / (double)count;
+  }
+
+  void check() {
+    SIMPLE_CUDA(cudaSetDevice(device_));
+    SIMPLE_CUDA(cudaStreamSynchronize(stream_));
+    check_tc();
+    int f[kFlags];
+    SIMPLE_CUDA(cudaMemcpy(f, flags_, sizeof(f), cudaMemcpyDeviceToHost));
+    if (f[kFlagNonfinite]) {
+      SIMPLE_CUDA(cudaMemset(flags_, 0, sizeof(f)));
+      throw Error(MB_ERR_NONFINITE, "nonfinite logits during training");
+    }
+  }
+
+  // Kernels launched by the latest training step (0 before the first).
+  uint32_t step_launches() const { return last_launches_; }
+
+ private:
+  void set_attributes() {
+    const int W = (int)c_.width;
+    const int bwd_smem = (kBwdWarps * 2 * W + kBwdWarps * 3 * W) * 4;
+    const int chain_smem = (kChainWarps * 2 * W + kChainWarps * 2 * W) * 4;
+    SIMPLE_CUDA(cudaFuncSetAttribute(&mlp_backward<kRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem));
+    SIMPLE_CUDA(cudaFuncSetAttribute(&mlp_backward<kSquare>, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem));
+    SIMPLE_CUDA(cudaFuncSetAttribute(&shared_backward<kRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem));
+    SIMPLE_CUDA(
+        cudaFuncSetAttribute(&shared_backward<kSquare>, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem));
+    SIMPLE_CUDA(cudaFuncSetAttribute(&chain_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, chain_smem));
+  }
+
+  void check_table(const mb_simple_table* t) const {
+    need(t, "table");
+    require(t->owner == this, "the table belongs to another model");
+  }
+  void check_batches(const mb_simple_table* t, const mb_simple_batches* b, size_t offset, size_t rows) const {
+    need(b, "batches");
+    require(b->owner == this, "the batches belong to another model");
+    require(b->table_rows == t->rows, "batch indices belong to a table with another row count");
+    require(rows >= 1 && rows <= kMaxRows && offset <= b->count && rows <= b->count - offset,
+            "minibatch is outside the uploaded indices");
+  }
+  void check_tc() {
+    int f = 0;
+    SIMPLE_CUDA(cudaMemcpy(&f, flags_ + kFlagTc, sizeof(int), cudaMemcpyDeviceToHost));
+    if (f) {
+      SIMPLE_CUDA(cudaMemset(flags_ + kFlagTc, 0, sizeof(int)));
+      throw Error(MB_ERR_CUDA, "a tensor-core wait gave up (bounded mbarrier wait)");
+    }
+  }
+
+  Workspace& workspace(int n) {
+    for (auto& w : workspaces_)
+      if (w->n == n) return *w;
+    if (workspaces_.size() == 3) workspaces_.erase(workspaces_.begin());
+    auto w = std::make_unique<Workspace>();
+    w->n = n;
+    const size_t W = c_.width, m = c_.modulus, N = (size_t)n;
+    const size_t nw = N * W;
+    auto& M = w->mem;
+    w->a = M.alloc<uint32_t>(N);
+    w->b = M.alloc<uint32_t>(N);
+    w->y = M.alloc<uint32_t>(N);
+    w->logits = M.alloc<float>(N * m);
+    w->dlog = M.alloc<float>(N * m);
+    w->dh0 = M.alloc<float>(nw);
+    w->dhf = M.alloc<float>(nw);
+    const int ctas = (int)((N + kBwdWarps * kBwdRows - 1) / (kBwdWarps * kBwdRows));
+    w->bwd_ctas = ctas;
+    size_t part = 0;
+    if (c_.architecture == kMeshMlp) {
+      const int L = mesh_layers(c_);
+      w->h = M.alloc<float>((L + 1) * nw);
+      w->act = M.alloc<float>(nw);
+      w->dact = w->dhf;
+      w->part = M.alloc<float>((size_t)ctas * std::max(L, 1) * parents(c_) * W);
+      part = gemm_partial_floats((int)W, (int)m, n, kSplitK);
+    } else if (c_.architecture == kRotaryDense) {
+      const size_t d = c_.depth;
+      w->hs = M.alloc<float>((d + 1) * nw);
+      w->ns = M.alloc<float>((d + 1) * nw);
+      w->invs = M.alloc<float>((d + 1) * N);
+      w->zs = M.alloc<float>(d * nw);
+      w->dh = M.alloc<float>(nw);
+      w->dz = M.alloc<float>(nw);
+      w->dn = M.alloc<float>(nw);
+      w->dEread = M.alloc<float>(m * W);
+      part = std::max(gemm_partial_floats((int)m, (int)W, n, kSplitK), gemm_partial_floats((int)W, (int)W, n, kSplitK));
+    } else {
+      const size_t d = c_.depth, ed = c_.embedding_mesh_depth;
+      w->hs = M.alloc<float>(d * nw);
+      w->hf = M.alloc<float>(nw);
+      w->invf = M.alloc<float>(N);
+      w->part = M.alloc<float>((size_t)ctas * d * 3 * W);
+      w->states = M.alloc<float>((ed + 1) * m * W);
+      w->dEemb = M.alloc<float>(m * W);
+      w->dEread = M.alloc<float>(m * W);
+      w->dv = M.alloc<float>(m * W);
+      part = gemm_partial_floats((int)m, (int)W, n, kSplitK);
+    }
+    w->gemm_part = M.alloc<float>(std::max<size_t>(part, 1));
+    workspaces_.push_back(std::move(w));
+    return *workspaces_.back();
+  }
+
+  void gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, int Mr, int Nc, int K, float* partial,
+            int k_chunk = 0) {
+    launch_gemm(A, B, C, ldc, Mr, Nc, K, k_chunk, partial, flags_ + kFlagTc, stream_);
+    launches_ += (uint32_t)gemm_launches(K, k_chunk);
+  }
+
+  void enqueue_gather(Workspace& ws, const mb_simple_table* t, const uint32_t* idx, bool step) {
+    const int n = ws.n;
+    gather_batch<<<(n + 255) / 256, 256, 0, stream_>>>(n, step ? scalars_ : nullptr, idx, t->a, t->b, t->t, ws.a,
+                                                        ws.b, ws.y); ++launches_;
+    SIMPLE_CUDA(cudaGetLastError());
+  }
+
+  template <int ACT>
+  void forward_impl(Workspace& ws) {
+    const int n = ws.n, W = (int)c_.width, m = (int)c_.modulus;
+    const size_t nw = (size_t)n * W;
+    const int fgrid = (n + kFwdWarps - 1) / kFwdWarps;
+    const float* w = w_;
+    if (c_.architecture == kMeshMlp) {
+      const int L = mesh_layers(c_), p = parents(c_);
+      const float* R = w + offsets_[1];
+      mlp_forward<ACT><<<fgrid, kFwdWarps * 32, kFwdWarps * W * 4, stream_>>>(
+          n, W, m, L, p, strides_, ws.a, ws.b, w + offsets_[0], w + (L > 0 ? offsets_[2] : 0), ws.h, ws.act); ++launches_;
+      // logits = act . R  (R [W][m]: B element (j, c) at R[c * m + j])
+      gemm({ws.act, W, false}, {R, m, true}, ws.logits, m, n, m, W, nullptr);
+    } else if (c_.architecture == kRotaryDense) {
+      const float* E = w + offsets_[0];
+      rotary_embed<<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.a, ws.b, E, ws.hs, ws.ns, ws.invs); ++launches_;
+      for (uint32_t l = 0; l < c_.depth; ++l) {
+        const float* D = w + offsets_[1 + l];
+        // z = n_l . D  (D [in][out]: B element (out, in) at D[in * W + out])
+        gemm({ws.ns + l * nw, W, false}, {D, W, true}, ws.zs + l * nw, W, n, W, W, nullptr);
+        residual_norm<ACT><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.hs + l * nw, ws.zs + l * nw,
+                                                                  ws.hs + (l + 1) * nw, ws.ns + (l + 1) * nw,
+                                                                  ws.invs + (l + 1) * n); ++launches_;
+      }
+      // logits = hf . E^T
+      gemm({ws.ns + c_.depth * nw, W, false}, {E, W, false}, ws.logits, m, n, m, W, nullptr);
+    } else {
+      const int ed = (int)c_.embedding_mesh_depth;
+      const float* chain = w;
+      const float* core = w + offsets_[ed];
+      chain_forward<<<(m + kFwdWarps - 1) / kFwdWarps, kFwdWarps * 32, kFwdWarps * W * 4, stream_>>>(m, W, ed, chain,
+                                                                                                    ws.states); ++launches_;
+      const float* E = ws.states + (size_t)ed * m * W;
+      shared_forward<ACT><<<fgrid, kFwdWarps * 32, kFwdWarps * W * 4, stream_>>>(
+          n, W, (int)c_.depth, strides_, ws.a, ws.b, E, core, ws.hs, ws.hf, ws.invf); ++launches_;
+      gemm({ws.hf, W, false}, {E, W, false}, ws.logits, m, n, m, W, nullptr);
+    }
+    SIMPLE_CUDA(cudaGetLastError());
+  }
+
+  void enqueue_forward(Workspace& ws) {
+    if (c_.activation == kRelu)
+      forward_impl<kRelu>(ws);
+    else
+      forward_impl<kSquare>(ws);
+  }
+
+  void enqueue_loss(Workspace& ws) {
+    const int n = ws.n, m = (int)c_.modulus;
+    cross_entropy_gradient<<<(n + kFwdWarps - 1) / kFwdWarps, kFwdWarps * 32, 0, stream_>>>(n, m, ws.logits, ws.y,
+                                                                                            ws.dlog, flags_); ++launches_;
+    SIMPLE_CUDA(cudaGetLastError());
+  }
+
+  template <int ACT>
+  void backward_impl(Workspace& ws) {
+    const int n = ws.n, W = (int)c_.width, m = (int)c_.modulus;
+    const size_t nw = (size_t)n * W;
+    const int fgrid = (n + kFwdWarps - 1) / kFwdWarps;
+    const int bwd_smem = (kBwdWarps * 2 * W + kBwdWarps * 3 * W) * 4;
+    float* g = grad_;
+    const float* w = w_;
+    if (c_.architecture == kMeshMlp) {
+      const int L = mesh_layers(c_), p = parents(c_);
+      const float* R = w + offsets_[1];
+      // dR = act^T . dlog  (split-K over rows)
+      gemm({ws.act, W, true}, {ws.dlog, m, true}, g + offsets_[1], m, W, m, n, ws.gemm_part, kSplitK);
+      // dact = dlog . R^T  (B element (c, j) at R[c * m + j])
+      gemm({ws.dlog, m, false}, {R, m, false}, ws.dact, W, n, W, m, nullptr);
+      if (L > 0) {
+        mlp_backward<ACT><<<ws.bwd_ctas, kBwdWarps * 32, bwd_smem, stream_>>>(n, W, L, p, strides_, w + offsets_[2],
+                                                                            ws.h, ws.dact, ws.dh0, ws.part); ++launches_;
+        const size_t cnt = (size_t)L * p * W;
+        reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
+            ws.part, ws.bwd_ctas, cnt, g + offsets_[2]); ++launches_;
+      } else {
+        activation_gradient<ACT><<<(int)std::min<size_t>((nw + 255) / 256, 1184), 256, 0, stream_>>>(
+            nw, ws.dact, ws.h, ws.dh0); ++launches_;
+      }
+      class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr, g + offsets_[0]); ++launches_;
+    } else if (c_.architecture == kRotaryDense) {
+      const float* E = w + offsets_[0];
+      const int d = (int)c_.depth;
+      const float* hf = ws.ns + d * nw;
+      // dE (readout share) = dlog^T . hf ; dhf = dlog . E
+      gemm({ws.dlog, m, true}, {hf, W, true}, ws.dEread, W, m, W, n, ws.gemm_part, kSplitK);
+      gemm({ws.dlog, m, false}, {E, W, true}, ws.dhf, W, n, W, m, nullptr);
+      rms_backward<<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, hf, ws.invs + d * n, ws.dhf, nullptr, ws.dh); ++launches_;
+      for (int l = d - 1; l >= 0; --l) {
+        const float* D = w + offsets_[1 + l];
+        activation_gradient<ACT><<<(int)std::min<size_t>((nw + 255) / 256, 1184), 256, 0, stream_>>>(
+            nw, ws.dh, ws.zs + l * nw, ws.dz); ++launches_;
+        // dD = n_l^T . dz ; dn = dz . D^T
+        gemm({ws.ns + l * nw, W, true}, {ws.dz, W, true}, g + offsets_[1 + l], W, W, W, n, ws.gemm_part, kSplitK);
+        gemm({ws.dz, W, false}, {D, W, false}, ws.dn, W, n, W, W, nullptr);
+        rms_backward<<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.ns + l * nw, ws.invs + l * n, ws.dn, ws.dh,
+                                                             ws.dh); ++launches_;
+      }
+      class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 1, ws.a, ws.b, ws.dh, ws.dEread, g + offsets_[0]); ++launches_;
+    } else {
+      const int ed = (int)c_.embedding_mesh_depth, d = (int)c_.depth;
+      const float* E = ws.states + (size_t)ed * m * W;
+      gemm({ws.dlog, m, true}, {ws.hf, W, true}, ws.dEread, W, m, W, n, ws.gemm_part, kSplitK);
+      gemm({ws.dlog, m, false}, {E, W, true}, ws.dhf, W, n, W, m, nullptr);
+      shared_backward<ACT><<<ws.bwd_ctas, kBwdWarps * 32, bwd_smem, stream_>>>(
+          n, W, d, strides_, w + offsets_[ed], ws.hs, ws.hf, ws.invf, ws.dhf, ws.dh0, ws.part); ++launches_;
+      const size_t cnt = (size_t)d * 3 * W;
+      reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
+          ws.part, ws.bwd_ctas, cnt, g + offsets_[ed]); ++launches_;
+      class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 1, ws.a, ws.b, ws.dh0, ws.dEread, ws.dEemb); ++launches_;
+      const int chain_smem = (kChainWarps * 2 * W + kChainWarps * 2 * W) * 4;
+      chain_backward<<<1, kChainWarps * 32, chain_smem, stream_>>>(m, W, ed, w, ws.states, ws.dEemb, ws.dv, g); ++launches_;
+    }
+    SIMPLE_CUDA(cudaGetLastError());
+  }
+
+  void enqueue_backward(Workspace& ws) {
+    if (c_.activation == kRelu)
+      backward_impl<kRelu>(ws);
+    else
+      backward_impl<kSquare>(ws);
+  }
+
+  void enqueue_update() {
+    adamw<<<(int)std::min<size_t>((P_ + 255) / 256, 1184), 256, 0, stream_>>>(P_, mesh_start_, scalars_, grad_, w_,
+                                                                               m1_, m2_); ++launches_;
+    SIMPLE_CUDA(cudaGetLastError());
+  }
+
+  mb_simple_config c_;
+  int device_;
+  cudaStream_t stream_ = nullptr;
+  DeviceBuffers mem_;
+  std::vector<size_t> groups_, offsets_;
+  size_t P_ = 0, mesh_start_ = 0;
+  float *w_, *m1_, *m2_, *grad_;
+  int* flags_;
+  int* strides_;
+  StepScalars* scalars_;
+  float beta1_power_ = 1.0f, beta2_power_ = 1.0f;
+  std::vector<std::unique_ptr<Workspace>> workspaces_;
+  uint64_t serial_ = 0;
+  uint32_t launches_ = 0, last_launches_ = 0;
+};
+
+}  // namespace simple
+}  // namespace mb
+
+struct mb_simple {
+  std::unique_ptr<mb::simple::SimpleModel> model;
+};
+
+// ------------------------------------------------------------------- C ABI
+using mb::guarded;
+using mb::need;
+using mb::require;
+
+extern "C" {
+
+int mb_simple_validate(const mb_simple_config* config) {
+  return guarded([&] {
+    need(config, "config");
+    mb::simple::validate(*config);
+  });
+}
+
+int mb_simple_parameter_count(const mb_simple_config* config, size_t* count) {
+  return guarded([&] {
+    need(config, "config");
+    need(count, "count");
+    mb::simple::validate(*config);
+    *count = mb::simple::parameter_count(*config);
+  });
+}
+
+int mb_simple_groups(const mb_simple_config* config, uint32_t* groups, size_t* n_groups) {
+  return guarded([&] {
+    need(config, "config");
+    need(n_groups, "n_groups");
+    mb::simple::validate(*config);
+    const auto g = mb::simple::groups(*config);
+    if (groups != nullptr) {
+      require(*n_groups >= g.size(), "groups buffer is too small");
+      for (size_t i = 0; i < g.size(); ++i) groups[i] = (uint32_t)g[i];
+    }
+    *n_groups = g.size();
+  });
+}
+
+int mb_simple_initial_parameters(const mb_simple_config* config, uint64_t seed, float* out, size_t count) {
+  return guarded([&] {
+    need(config, "config");
+    need(out, "out");
+    const auto p = mb::simple::initial_parameters(*config, seed);
+    require(count == p.size(), "parameter count does not match the model");
+    std::memcpy(out, p.data(), p.size() * sizeof(float));
+  });
+}
+
+int mb_simple_encode(const mb_simple_config* config, const uint32_t* equations, size_t n, float* features,
+                     uint32_t* targets) {
+  return guarded([&] {
+    need(config, "config");
+    need(equations, "equations");
+    need(features, "features");
+    need(targets, "targets");
+    mb::simple::validate(*config);
+    const uint32_t m = config->modulus;
+    for (size_t r = 0; r < n; ++r)
+      for (int j = 0; j < 3; ++j)
+        require(equations[3 * r + j] < m, "equation residue is outside the model's modulus");
+    std::memset(features, 0, n * 2 * m * sizeof(float));
+    for (size_t r = 0; r < n; ++r) {
+      features[r * 2 * m + equations[3 * r]] = 1.0f;
+      features[r * 2 * m + m + equations[3 * r + 1]] = 1.0f;
+      targets[r] = equations[3 * r + 2];
+    }
+  });
+}
+
+int mb_simple_create(int device, const mb_simple_config* config, uint64_t seed, mb_simple** out) {
+  return guarded([&] {
+    need(config, "config");
+    need(out, "out");
+    *out = nullptr;
+    auto h = std::make_unique<mb_simple>();
+    h->model = std::make_unique<mb::simple::SimpleModel>(device, *config, seed);
+    *out = h.release();
+  });
+}
+
+int mb_simple_destroy(mb_simple* model) {
+  return guarded([&] { delete model; });
+}
+
+int mb_simple_get_parameters(mb_simple* model, float* out, size_t count) {
+  return guarded([&] {
+    need(model, "model");
+    need(out, "out");
+    model->model->get_parameters(out, count);
+  });
+}
+
+int mb_simple_set_parameters(mb_simple* model, const float* values, size_t count) {
+  return guarded([&] {
+    need(model, "model");
+    need(values, "values");
+    model->model->set_parameters(values, count);
+  });
+}
+
+int mb_simple_upload_table(mb_simple* model, const float* features, const uint32_t* targets, size_t rows,
+                           mb_simple_table** out) {
+  return guarded([&] {
+    need(model, "model");
+    need(features, "features");
+    need(targets, "targets");
+    need(out, "out");
+    *out = model->model->upload_table(features, targets, rows);
+  });
+}
+
+int mb_simple_table_destroy(mb_simple_table* table) {
+  return guarded([&] { delete table; });
+}
+
+int mb_simple_upload_batches(mb_simple* model, const mb_simple_table* table, const uint32_t* indices, size_t count,
+                             mb_simple_batches** out) {
+  return guarded([&] {
+    need(model, "model");
+    need(indices, "indices");
+    need(out, "out");
+    *out = model->model->upload_batches(table, indices, count);
+  });
+}
+
+int mb_simple_batches_destroy(mb_simple_batches* batches) {
+  return guarded([&] { delete batches; });
+}
+
+int mb_simple_train_step(mb_simple* model, const mb_simple_table* table, const mb_simple_batches* batches,
+                         size_t offset, size_t rows, const mb_adamw* options) {
+  return guarded([&] {
+    need(model, "model");
+    need(options, "options");
+    model->model->train_step(table, batches, offset, rows, *options);
+  });
+}
+
+int mb_simple_evaluate(mb_simple* model, const mb_simple_table* table, float* logits, uint32_t* predictions) {
+  return guarded([&] {
+    need(model, "model");
+    model->model->evaluate(table, logits, predictions);
+  });
+}
+
+int mb_simple_loss_and_gradient(mb_simple* model, const mb_simple_table* table, const uint32_t* indices,
+                                size_t count, double* loss, float* gradient, size_t n_gradient) {
+  return guarded([&] {
+    need(model, "model");
+    need(indices, "indices");
+    need(loss, "loss");
+    need(gradient, "gradient");
+    *loss = model->model->loss_and_gradient(table, indices, count, gradient, n_gradient);
+  });
+}
+
+int mb_simple_stream(mb_simple* model, void** stream) {
+  return guarded([&] {
+    need(model, "model");
+    need(stream, "stream");
+    *stream = (void*)model->model->stream();
+  });
+}
+
+int mb_simple_check(mb_simple* model) {
+  return guarded([&] {
+    need(model, "model");
+    model->model->check();
+  });
+}
+
+int mb_simple_step_launches(mb_simple* model, uint32_t* launches) {
+  return guarded([&] {
+    need(model, "model");
+    need(launches, "launches");
+    *launches = model->model->step_launches();
+  });
+}
+
+}  // extern "C"

@@ -189,11 +189,14 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// TF32 hi part (round to nearest, ties away) of an FP32 value.
+// TF32 hi part (round to nearest, ties away from zero) of a finite FP32
+// value: adding half a TF32 ulp (bit 12) to the magnitude bits and clearing
+// the 13 dropped bits is exactly cvt.rna.tf32.f32 for every finite input
+// (carries into the exponent round up a binade; the sign bit is untouched).
+// Integer ALU work instead of a conversion on the XU pipe, which the softmax
+// loops already load with ex2.
 __device__ __forceinline__ float tf32_hi(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 }  // namespace tc

@@ -47,11 +47,12 @@ def mesh_backward(x, dy, weights, connectivity: int = 0):
 
 
 def gemm_tf32x3(a, b, layout: int = 0):
-    """FP32 GEMM via tcgen05 3xTF32.  layout 0: C = A . B^T with b [n][k];
-    1: C = A . B with b [k][n]; 2: as 0 with A staged through tensor memory."""
+    """FP32 GEMM via tcgen05 3xTF32, C [m][n] = A . B^T over k.  Layout bits:
+    1 = b given [k][n] (else [n][k]); 2 = A staged through tensor memory;
+    4 = a given [k][m] (else [m][k]; not with 2)."""
     import torch
-    m, k = a.shape
-    n, k2 = (b.shape[1], b.shape[0]) if layout == 1 else b.shape
+    m, k = (a.shape[1], a.shape[0]) if layout & 4 else a.shape
+    n, k2 = (b.shape[1], b.shape[0]) if layout & 1 else b.shape
     if k != k2:
         raise ValueError("inner dimensions differ")
     c = torch.empty((m, n), dtype=torch.float32, device=a.device)

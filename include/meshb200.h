@@ -208,6 +208,78 @@ int mb_equation_sampler(size_t examples, uint64_t seed, size_t batch, size_t ste
 int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t sequences, size_t context,
                   uint32_t vocab, double exponent, uint32_t* inputs, uint32_t* targets);
 
+/* ---- grok-simple models (src/simple/mod.rs, src/simple/gpu.rs) ----------
+ * Replaces GpuSimpleModel::{new, parameters, set_parameters, upload_table,
+ * upload_batches, logits, evaluate, loss_and_gradient, train_batch}
+ * (src/simple/gpu.rs:1757-2073) for three architectures of SimpleConfig
+ * (src/simple/mod.rs:500-558); the encoding is one-hot.
+ *   architecture 0 = mesh-mlp, 1 = tied-rotary-residual-dense-mlp,
+ *                2 = shared-neighbor-mesh-mlp
+ *   activation   0 = relu, 1 = square
+ *   connectivity 0 = own, 1 = neighbor, 2 = butterfly
+ *   full_mesh_initialization 0 = kaiming, 1 = identity-hidden
+ * Fields an architecture does not read are ignored, as in the reference. */
+typedef struct mb_simple_config {
+  uint32_t architecture;
+  uint32_t activation;
+  uint32_t modulus;
+  uint32_t width;
+  uint32_t depth;
+  uint32_t connectivity;
+  uint32_t embedding_mesh_depth;
+  uint32_t full_mesh_initialization;
+  uint32_t mesh_learning_rate_multiplier;
+} mb_simple_config;
+
+typedef struct mb_simple mb_simple;
+typedef struct mb_simple_table mb_simple_table;     /* DeviceTable (src/simple/gpu.rs:1868-1893) */
+typedef struct mb_simple_batches mb_simple_batches; /* DeviceBatches (:1896-1909) */
+
+/* SimpleConfig::validate (src/simple/mod.rs:561-694). */
+int mb_simple_validate(const mb_simple_config* config);
+/* SimpleConfig::parameter_count / groups (:871-893); pass groups = NULL to
+ * query *n_groups. */
+int mb_simple_parameter_count(const mb_simple_config* config, size_t* count);
+int mb_simple_groups(const mb_simple_config* config, uint32_t* groups, size_t* n_groups);
+/* SimpleConfig::initial_parameters (:938-1036), host out[count]. */
+int mb_simple_initial_parameters(const mb_simple_config* config, uint64_t seed, float* out, size_t count);
+/* SimpleConfig::encode (:1039-1055): host equations [n][3] (a, b, answer)
+ * -> host features [n][2*modulus], targets [n]. */
+int mb_simple_encode(const mb_simple_config* config, const uint32_t* equations, size_t n, float* features,
+                     uint32_t* targets);
+
+/* GpuSimpleModel::new (src/simple/gpu.rs:1758-1806). */
+int mb_simple_create(int device, const mb_simple_config* config, uint64_t seed, mb_simple** out);
+int mb_simple_destroy(mb_simple* model);
+/* parameters (:1819-1826) and set_parameters, which resets AdamW (:1856-1875). */
+int mb_simple_get_parameters(mb_simple* model, float* out, size_t count);
+int mb_simple_set_parameters(mb_simple* model, const float* values, size_t count);
+/* upload_table (:1878-1906): host features [rows][2*modulus] (one-hot
+ * operand blocks) and targets [rows] < modulus. */
+int mb_simple_upload_table(mb_simple* model, const float* features, const uint32_t* targets, size_t rows,
+                           mb_simple_table** out);
+int mb_simple_table_destroy(mb_simple_table* table);
+/* upload_batches (:1909-1920): host indices into the table. */
+int mb_simple_upload_batches(mb_simple* model, const mb_simple_table* table, const uint32_t* indices,
+                             size_t count, mb_simple_batches** out);
+int mb_simple_batches_destroy(mb_simple_batches* batches);
+/* train_batch (:2031-2073): one AdamW step on rows indices[offset ..
+ * offset + rows) of the batches, f32 host beta powers. */
+int mb_simple_train_step(mb_simple* model, const mb_simple_table* table, const mb_simple_batches* batches,
+                         size_t offset, size_t rows, const mb_adamw* options);
+/* evaluate (:1938-1995): logits [rows][modulus] and first-maximum
+ * predictions [rows] of every table row (either output may be NULL);
+ * nonfinite logits fail with MB_ERR_NONFINITE. */
+int mb_simple_evaluate(mb_simple* model, const mb_simple_table* table, float* logits, uint32_t* predictions);
+/* loss_and_gradient (:1998-2029): mean answer cross-entropy (f64, from the
+ * f32 logits) and every parameter gradient on the selected table rows. */
+int mb_simple_loss_and_gradient(mb_simple* model, const mb_simple_table* table, const uint32_t* indices,
+                                size_t count, double* loss, float* gradient, size_t n_gradient);
+/* Device stream, pending device errors, and kernels per train step. */
+int mb_simple_stream(mb_simple* model, void** stream);
+int mb_simple_check(mb_simple* model);
+int mb_simple_step_launches(mb_simple* model, uint32_t* launches);
+
 #ifdef __cplusplus
 }
 #endif

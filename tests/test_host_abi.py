@@ -117,3 +117,52 @@ def test_zipf_matches_oracle():
         xa, ya = zipf_batch(seed, rank, step, 3, 17)
         xb, yb = odata.zipf_batch(seed, rank, step, 3, 17)
         assert np.array_equal(xa, xb) and np.array_equal(ya, yb)
+
+
+# ------------------------------------------------------------ grok-simple
+def _simple_pairs():
+    from grokking_abmod_b200.simple import SimpleConfig
+    from oracle.simple_ref import SimpleConfig as OracleSimpleConfig
+    for kw in (dict(architecture="tied-rotary-residual-dense-mlp", width=128, depth=1),
+               dict(architecture="tied-rotary-residual-dense-mlp", modulus=7, width=10, depth=3,
+                    activation="square"),
+               dict(architecture="mesh-mlp", width=384, depth=5, connectivity="butterfly"),
+               dict(architecture="mesh-mlp", modulus=7, width=9, depth=3, connectivity="own"),
+               dict(architecture="mesh-mlp", modulus=5, width=16, depth=1),
+               dict(architecture="shared-neighbor-mesh-mlp", width=128, depth=64, embedding_mesh_depth=32,
+                    full_mesh_initialization="identity-hidden"),
+               dict(architecture="shared-neighbor-mesh-mlp", modulus=7, width=8, depth=3, embedding_mesh_depth=2,
+                    connectivity="butterfly", mesh_learning_rate_multiplier=3)):
+        yield OracleSimpleConfig(**kw), SimpleConfig(**kw)
+
+
+def test_simple_initial_parameters_groups_and_encoding_match_oracle():
+    from oracle.simple_ref import encode, initial_parameters as oracle_init
+    for oc, pc in _simple_pairs():
+        assert pc.parameter_count() == oc.parameter_count()
+        assert pc.groups() == oc.groups()
+        for seed in (0, 11, 2**63 + 5):
+            a, b = pc.initial_parameters(seed), oracle_init(oc, seed)
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (oc, seed)
+        eq = [(0, 1, 2), (oc.modulus - 1, 0, 1), (3 % oc.modulus, 2, 0)]
+        f1, t1 = pc.encode(eq)
+        f2, t2 = encode(oc, eq)
+        assert np.array_equal(f1, f2) and np.array_equal(t1, t2)
+
+
+def test_simple_validation_mirrors_the_reference():
+    from grokking_abmod_b200.simple import SimpleConfig
+    bad = [dict(architecture="shared-neighbor-mesh-mlp", width=64),
+           dict(architecture="shared-neighbor-mesh-mlp", width=128, connectivity="own"),
+           dict(architecture="tied-rotary-residual-dense-mlp", width=127),
+           dict(architecture="mesh-mlp", full_mesh_initialization="identity-hidden"),
+           dict(architecture="mesh-mlp", depth=1, mesh_learning_rate_multiplier=2),
+           dict(architecture="mesh-mlp", depth=0), dict(architecture="mesh-mlp", depth=65),
+           dict(architecture="mesh-mlp", modulus=1), dict(architecture="mesh-mlp", modulus=1025)]
+    for kw in bad:
+        with pytest.raises(MeshError):
+            SimpleConfig(**kw).validate()
+    with pytest.raises(ValueError):
+        SimpleConfig(architecture="bilinear").to_c()
+    with pytest.raises(MeshError):
+        SimpleConfig(modulus=7, width=8).encode([(7, 0, 0)])
