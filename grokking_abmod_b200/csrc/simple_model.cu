@@ -62,8 +62,11 @@ constexpr int kMaxJ = kMaxKernelWidth / 32;  // row values per lane
 constexpr int kSplitK = 256;          // batch rows per weight-gradient GEMM chunk
 constexpr unsigned kFull = 0xffffffffu;
 
-// Values that change from step to step, read by the captured kernels.
+// Values that change from step to step, read by the captured kernels: the
+// minibatch (table columns and index list), learning rates and corrections.
+// The step graph therefore serves every table and batch list of its size.
 struct StepScalars {
+  const uint32_t *idx, *ta, *tb, *tt;
   uint32_t offset;
   float lr_dense, lr_mesh, weight_decay, beta1, beta2, epsilon, correction1, correction2;
 };
@@ -97,7 +100,13 @@ __global__ void gather_batch(int n, const StepScalars* __restrict__ sc, const ui
                              uint32_t* __restrict__ y) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= n) return;
-  const uint32_t i = idx[(sc != nullptr ? sc->offset : 0u) + r];
+  if (sc != nullptr) {
+    idx = sc->idx + sc->offset;
+    ta = sc->ta;
+    tb = sc->tb;
+    tt = sc->tt;
+  }
+  const uint32_t i = idx[r];
   a[r] = ta[i];
   b[r] = tb[i];
   y[r] = tt[i];
@@ -769,7 +778,6 @@ struct Workspace {
   float *hf, *invf, *states, *dEemb, *dv;  // shared-Neighbor
   int bwd_ctas = 0;
   cudaGraphExec_t step_graph = nullptr;
-  uint64_t graph_table = 0, graph_batches = 0;  // serials the graph was captured with
   uint32_t step_launches = 0;
   ~Workspace() {
     if (step_graph) cudaGraphExecDestroy(step_graph);
@@ -781,7 +789,6 @@ struct Workspace {
 
 struct mb_simple_table {
   const void* owner;
-  uint64_t serial;
   size_t rows;
   mb::simple::DeviceBuffers mem;
   uint32_t *a, *b, *t, *identity;
@@ -789,7 +796,6 @@ struct mb_simple_table {
 
 struct mb_simple_batches {
   const void* owner;
-  uint64_t serial;
   size_t count, table_rows;
   mb::simple::DeviceBuffers mem;
   uint32_t* idx;
@@ -871,7 +877,6 @@ class SimpleModel {
     SIMPLE_CUDA(cudaSetDevice(device_));
     auto t = std::make_unique<mb_simple_table>();
     t->owner = this;
-    t->serial = ++serial_;
     t->rows = rows;
     t->a = t->mem.alloc<uint32_t>(rows);
     t->b = t->mem.alloc<uint32_t>(rows);
@@ -891,7 +896,6 @@ class SimpleModel {
     SIMPLE_CUDA(cudaSetDevice(device_));
     auto bt = std::make_unique<mb_simple_batches>();
     bt->owner = this;
-    bt->serial = ++serial_;
     bt->count = count;
     bt->table_rows = table->rows;
     bt->idx = bt->mem.alloc<uint32_t>(count);
@@ -910,6 +914,10 @@ class SimpleModel {
     beta1_power_ *= o.beta1;
     beta2_power_ *= o.beta2;
     StepScalars s{};
+    s.idx = batches->idx;
+    s.ta = table->a;
+    s.tb = table->b;
+    s.tt = table->t;
     s.offset = (uint32_t)offset;
     s.lr_dense = o.learning_rate;
     s.lr_mesh = o.learning_rate * (float)c_.mesh_learning_rate_multiplier;
@@ -921,11 +929,7 @@ class SimpleModel {
     s.correction2 = 1.0f - beta2_power_;
     // Pageable source: the copy has consumed `s` when the call returns.
     SIMPLE_CUDA(cudaMemcpyAsync(scalars_, &s, sizeof(s), cudaMemcpyHostToDevice, stream_));
-    if (ws.step_graph == nullptr || ws.graph_table != table->serial || ws.graph_batches != batches->serial) {
-      if (ws.step_graph) {
-        cudaGraphExecDestroy(ws.step_graph);
-        ws.step_graph = nullptr;
-      }
+    if (ws.step_graph == nullptr) {
       cudaGraph_t g = nullptr;
       SIMPLE_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
       launches_ = 0;
@@ -944,8 +948,6 @@ class SimpleModel {
       cudaError_t e = cudaGraphInstantiate(&ws.step_graph, g, 0);
       cudaGraphDestroy(g);
       SIMPLE_CUDA(e);
-      ws.graph_table = table->serial;
-      ws.graph_batches = batches->serial;
       ws.step_launches = launches_;
     }
     last_launches_ = ws.step_launches;
@@ -1262,7 +1264,6 @@ class SimpleModel {
   StepScalars* scalars_;
   float beta1_power_ = 1.0f, beta2_power_ = 1.0f;
   std::vector<std::unique_ptr<Workspace>> workspaces_;
-  uint64_t serial_ = 0;
   uint32_t launches_ = 0, last_launches_ = 0;
 };
 
