@@ -58,7 +58,7 @@ constexpr float kEps = 1e-5f;         // RMSNORM_EPSILON, src/gpt/mod.rs:39
 constexpr int kFwdWarps = 8;          // forward row kernels: warps (= rows) per CTA
 constexpr int kBwdWarps = 16;         // backward row kernels: warps per CTA ...
 constexpr int kBwdRows = 2;           // ... each walking this many rows per layer
-constexpr int kMaxJ = kMaxKernelWidth / 32;  // row values per lane
+constexpr int kMaxJ = kMaxKernelWidth / 32;  // row values per lane at the widest row
 constexpr int kSplitK = 256;          // batch rows per weight-gradient GEMM chunk
 constexpr unsigned kFull = 0xffffffffu;
 
@@ -116,7 +116,7 @@ __global__ void gather_batch(int n, const StepScalars* __restrict__ sc, const ui
 // h0 = W0[a] + W0[m + b]; per mesh layer h' = act(h)[c] w0 + act(h)[c+s] w1;
 // act = act(h_L) feeds the readout GEMM.  h[l] (l = 0..L) is kept for the
 // backward.
-template <int ACT>
+template <int ACT, int J>
 __global__ void __launch_bounds__(kFwdWarps * 32)
     mlp_forward(int n, int W, int m, int L, int p, const int* __restrict__ strides, const uint32_t* __restrict__ a,
                 const uint32_t* __restrict__ b, const float* __restrict__ w0, const float* __restrict__ mesh,
@@ -138,9 +138,9 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     __syncwarp();
     const int s = strides[l];
     const float* w = mesh + (size_t)l * W * p;
-    float v[kMaxJ];
+    float v[J];
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
       if (c < W) {
         float y = row[c] * w[c * p];
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     }
     __syncwarp();
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
       if (c < W) {
         h[(l + 1) * nw + (size_t)r * W + c] = v[j];
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
 
 // dact = dlogits R^T in, dh0 out; per-CTA mesh weight partials
 // [gridDim.x][L][p*W].
-template <int ACT>
+template <int ACT, int J>
 __global__ void __launch_bounds__(kBwdWarps * 32)
     mlp_backward(int n, int W, int L, int p, const int* __restrict__ strides, const float* __restrict__ mesh,
                  const float* __restrict__ h, const float* __restrict__ dact, float* __restrict__ dh0,
@@ -176,12 +176,12 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
   float* drow = arow + W;           // dh of the current row
   float* contrib = sm + kBwdWarps * 2 * W;
   const size_t nw = (size_t)n * W;
-  float dh[kBwdRows][kMaxJ];
+  float dh[kBwdRows][J];
 #pragma unroll
   for (int i = 0; i < kBwdRows; ++i) {
     const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
       dh[i][j] = (r < n && c < W) ? dact[(size_t)r * W + c] * act_g<ACT>(h[L * nw + (size_t)r * W + c]) : 0.f;
     }
@@ -195,10 +195,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
     for (int i = 0; i < kBwdRows; ++i) {
       const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
       const bool active = r < n;
-      float hl[kMaxJ];
+      float hl[J];
       __syncwarp();
 #pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
+      for (int j = 0; j < J; ++j) {
         const int c = lane + 32 * j;
         if (c < W) {
           hl[j] = active ? h[l * nw + (size_t)r * W + c] : 0.f;
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
       }
       __syncwarp();
 #pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
+      for (int j = 0; j < J; ++j) {
         const int c = lane + 32 * j;
         if (c < W) {
           const float d = drow[c];
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
     const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
     if (r >= n) continue;
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
       if (c < W) dh0[(size_t)r * W + c] = dh[i][j];
     }
@@ -255,10 +255,11 @@ __global__ void reduce_cta_partials(const float* __restrict__ partials, int ctas
 
 // ----------------------------------------------------- RMSNorm row helpers
 // y = x / sqrt(mean(x^2) + eps) over the warp's row; returns the inverse.
-__device__ __forceinline__ float row_inverse_rms(const float (&x)[kMaxJ], int W, int lane) {
+template <int J>
+__device__ __forceinline__ float row_inverse_rms(const float (&x)[J], int W, int lane) {
   float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j)
+  for (int j = 0; j < J; ++j)
     if (lane + 32 * j < W) ss = fmaf(x[j], x[j], ss);
   ss = warp_sum(ss);
   return 1.0f / sqrtf(ss / (float)W + kEps);
@@ -266,6 +267,7 @@ __device__ __forceinline__ float row_inverse_rms(const float (&x)[kMaxJ], int W,
 
 // Rotary operand embedding h0 = E[a] + rot(E[b]) and n0 = RMSNorm(h0)
 // (tied-rotary-residual-dense-mlp; also the shared-Neighbor core input).
+template <int J>
 __global__ void __launch_bounds__(kFwdWarps * 32)
     rotary_embed(int n, int W, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
                  const float* __restrict__ E, float* __restrict__ h0, float* __restrict__ n0,
@@ -275,15 +277,15 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
   if (r >= n) return;
   const float* ea = E + (size_t)a[r] * W;
   const float* eb = E + (size_t)b[r] * W;
-  float v[kMaxJ];
+  float v[J];
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int c = lane + 32 * j;
     v[j] = c < W ? ea[c] + rotated(eb, c) : 0.f;
   }
   const float inv = row_inverse_rms(v, W, lane);
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int c = lane + 32 * j;
     if (c < W) {
       h0[(size_t)r * W + c] = v[j];
@@ -294,22 +296,22 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
 }
 
 // h' = h + act(z); n' = RMSNorm(h') (a dense residual block's epilogue).
-template <int ACT>
+template <int ACT, int J>
 __global__ void __launch_bounds__(kFwdWarps * 32)
     residual_norm(int n, int W, const float* __restrict__ h, const float* __restrict__ z, float* __restrict__ hn,
                   float* __restrict__ nn, float* __restrict__ inv_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
   if (r >= n) return;
-  float v[kMaxJ];
+  float v[J];
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int c = lane + 32 * j;
     v[j] = c < W ? h[(size_t)r * W + c] + act_f<ACT>(z[(size_t)r * W + c]) : 0.f;
   }
   const float inv = row_inverse_rms(v, W, lane);
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int c = lane + 32 * j;
     if (c < W) {
       hn[(size_t)r * W + c] = v[j];
@@ -320,15 +322,16 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
 }
 
 // dx = add + inv (dy - y <dy, y> / W) with y the normalised row.
+template <int J>
 __global__ void __launch_bounds__(kFwdWarps * 32)
     rms_backward(int n, int W, const float* __restrict__ y, const float* __restrict__ inv,
                  const float* __restrict__ dy, const float* add, float* dx) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
   if (r >= n) return;
-  float yv[kMaxJ], dv[kMaxJ], dot = 0.f;
+  float yv[J], dv[J], dot = 0.f;
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int c = lane + 32 * j;
     yv[j] = c < W ? y[(size_t)r * W + c] : 0.f;
     dv[j] = c < W ? dy[(size_t)r * W + c] : 0.f;
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
   dot = warp_sum(dot) / (float)W;
   const float iv = inv[r];
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int c = lane + 32 * j;
     if (c < W) {
       const float g = iv * (dv[j] - yv[j] * dot);
@@ -355,45 +358,85 @@ __global__ void activation_gradient(size_t count, const float* __restrict__ dh, 
 }
 
 // ---------------------------------------------------- shared-Neighbor
-// Class rows of the shared linear Neighbor chain: states[0][k] = e_k,
-// states[l+1][k][c] = states[l][k][c] w0[c] + states[l][k][c+1] w1[c].
-// states[ed] is the embedding E used by the operands and the readout.
-__global__ void __launch_bounds__(kFwdWarps * 32)
+// The shared linear Neighbor chain over the class rows, one CTA: thread t
+// owns channel c = t % W of the rows k = t / W, t / W + RG, ... (RG = row
+// groups), and every layer ends with a block barrier.
+//   states[0][k] = e_k
+//   states[l+1][k][c] = states[l][k][c] w0[c] + states[l][k][c+1] w1[c]
+// states[ed] is the embedding E of the operands and of the readout.
+constexpr int kChainThreads = 1024;
+__global__ void __launch_bounds__(kChainThreads)
     chain_forward(int m, int W, int ed, const float* __restrict__ chain, float* __restrict__ states) {
-  extern __shared__ float sm[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int k = blockIdx.x * kFwdWarps + warp;
-  if (k >= m) return;
-  float* row = sm + warp * W;
+  const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
   const size_t mw = (size_t)m * W;
-  for (int c = lane; c < W; c += 32) {
-    row[c] = c == k ? 1.f : 0.f;
-    states[(size_t)k * W + c] = row[c];
-  }
+  if (rg < RG)
+    for (int k = rg; k < m; k += RG) states[(size_t)k * W + c] = c == k ? 1.f : 0.f;
+  __syncthreads();
   for (int l = 0; l < ed; ++l) {
-    __syncwarp();
-    const float* w = chain + (size_t)l * 2 * W;
-    float v[kMaxJ];
-#pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
-      const int c = lane + 32 * j;
-      if (c < W) v[j] = fmaf(row[(c + 1) % W], w[2 * c + 1], row[c] * w[2 * c]);
-    }
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
-      const int c = lane + 32 * j;
-      if (c < W) {
-        row[c] = v[j];
-        states[(l + 1) * mw + (size_t)k * W + c] = v[j];
-      }
-    }
+    const float w0 = chain[(size_t)l * 2 * W + 2 * c], w1 = chain[(size_t)l * 2 * W + 2 * c + 1];
+    const float* in = states + l * mw;
+    float* out = states + (l + 1) * mw;
+    if (rg < RG)
+      for (int k = rg; k < m; k += RG)
+        out[(size_t)k * W + c] = fmaf(in[(size_t)k * W + (c + 1) % W], w1, in[(size_t)k * W + c] * w0);
+    __syncthreads();
   }
+}
+
+// Chain backward over the class rows (one CTA, same thread layout): dv = dE;
+// for l = ed-1 .. 0 the chain weights' gradient sums dv[k][c] v_l[k][c] and
+// dv[k][c] v_l[k][c+1] over the rows (each thread over its rows in order,
+// then the row groups in order), and dv <- dv[c] w0[c] + dv[c-1] w1[c-1]
+// (double-buffered in dva / dvb).
+__global__ void __launch_bounds__(kChainThreads)
+    chain_backward(int m, int W, int ed, const float* __restrict__ chain, const float* __restrict__ states,
+                   const float* __restrict__ dE, float* dva, float* dvb, float* __restrict__ grad) {
+  __shared__ float part[2][kChainThreads];
+  const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
+  const int cp = (c + W - 1) % W;
+  const size_t mw = (size_t)m * W;
+  const float* dv = dE;
+  for (int l = ed - 1; l >= 0; --l) {
+    const float w0 = chain[(size_t)l * 2 * W + 2 * c], w1p = chain[(size_t)l * 2 * W + 2 * cp + 1];
+    const float* v = states + l * mw;
+    float* out = (l & 1) ? dva : dvb;
+    float g0 = 0.f, g1 = 0.f;
+    if (rg < RG)
+      for (int k = rg; k < m; k += RG) {
+        const float d = dv[(size_t)k * W + c];
+        g0 = fmaf(d, v[(size_t)k * W + c], g0);
+        g1 = fmaf(d, v[(size_t)k * W + (c + 1) % W], g1);
+        if (l > 0) out[(size_t)k * W + c] = fmaf(dv[(size_t)k * W + cp], w1p, d * w0);
+      }
+    part[0][threadIdx.x] = g0;
+    part[1][threadIdx.x] = g1;
+    __syncthreads();
+    if (threadIdx.x < W) {
+      float s0 = 0.f, s1 = 0.f;
+      for (int q = 0; q < RG; ++q) {
+        s0 += part[0][q * W + threadIdx.x];
+        s1 += part[1][q * W + threadIdx.x];
+      }
+      grad[(size_t)l * 2 * W + 2 * threadIdx.x] = s0;
+      grad[(size_t)l * 2 * W + 2 * threadIdx.x + 1] = s1;
+    }
+    __syncthreads();
+    dv = out;
+  }
+}
+
+// The core's weights, staged in shared memory when they fit (depth x 3W).
+constexpr int kCoreSmemFloats = 24576;  // 96 KiB
+__device__ __forceinline__ const float* stage_core(const float* __restrict__ core, int n_floats, float* sm) {
+  if (n_floats > kCoreSmemFloats) return core;
+  for (int i = threadIdx.x; i < n_floats; i += blockDim.x) sm[i] = core[i];
+  __syncthreads();
+  return sm;
 }
 
 // The pre-RMSNorm residual two-parent core: h <- h + act(n[c] w0 + n[c+s] w1
 // + bias), n = RMSNorm(h); hs[l] keeps each layer's input, hf = RMSNorm(h).
-template <int ACT>
+template <int ACT, int J>
 __global__ void __launch_bounds__(kFwdWarps * 32)
     shared_forward(int n, int W, int depth, const int* __restrict__ strides, const uint32_t* __restrict__ a,
                    const uint32_t* __restrict__ b, const float* __restrict__ E, const float* __restrict__ core,
@@ -401,22 +444,23 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
+  const float* wts = stage_core(core, depth * 3 * W, sm);
   if (r >= n) return;
-  float* row = sm + warp * W;
+  float* row = sm + (depth * 3 * W <= kCoreSmemFloats ? depth * 3 * W : 0) + warp * W;
   const float* ea = E + (size_t)a[r] * W;
   const float* eb = E + (size_t)b[r] * W;
   const size_t nw = (size_t)n * W;
-  float h[kMaxJ];
+  float h[J];
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int c = lane + 32 * j;
     h[j] = c < W ? ea[c] + rotated(eb, c) : 0.f;
   }
   for (int l = 0; l < depth; ++l) {
-    const float inv = row_inverse_rms(h, W, lane);
+    const float inv = row_inverse_rms<J>(h, W, lane);
     __syncwarp();
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
       if (c < W) {
         hs[l * nw + (size_t)r * W + c] = h[j];
@@ -425,9 +469,9 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     }
     __syncwarp();
     const int s = strides[l];
-    const float* w = core + (size_t)l * 3 * W;
+    const float* w = wts + (size_t)l * 3 * W;
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
       if (c < W) {
         const float z = fmaf(row[(c + s) % W], w[3 * c + 1], row[c] * w[3 * c]) + w[3 * c + 2];
@@ -435,9 +479,9 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
       }
     }
   }
-  const float inv = row_inverse_rms(h, W, lane);
+  const float inv = row_inverse_rms<J>(h, W, lane);
 #pragma unroll
-  for (int j = 0; j < kMaxJ; ++j) {
+  for (int j = 0; j < J; ++j) {
     const int c = lane + 32 * j;
     if (c < W) hf[(size_t)r * W + c] = h[j] * inv;
   }
@@ -446,7 +490,8 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
 
 // Backward of the core: dhf (gradient of the final RMSNorm output) in, dh0
 // out; per-CTA weight partials [gridDim.x][depth][3W] (w0, w1, bias per unit).
-template <int ACT>
+// The next layer's saved inputs are loaded while the current layer computes.
+template <int ACT, int J>
 __global__ void __launch_bounds__(kBwdWarps * 32)
     shared_backward(int n, int W, int depth, const int* __restrict__ strides, const float* __restrict__ core,
                     const float* __restrict__ hs, const float* __restrict__ hf, const float* __restrict__ invf,
@@ -454,18 +499,20 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pw = 3 * W;
-  float* nrow = sm + warp * 2 * W;
+  const float* wts = stage_core(core, depth * pw, sm);
+  float* base = sm + (depth * pw <= kCoreSmemFloats ? depth * pw : 0);
+  float* nrow = base + warp * 2 * W;
   float* zrow = nrow + W;  // dz
-  float* contrib = sm + kBwdWarps * 2 * W;
+  float* contrib = base + kBwdWarps * 2 * W;
   const size_t nw = (size_t)n * W;
-  float dh[kBwdRows][kMaxJ];
+  float dh[kBwdRows][J];
 #pragma unroll
   for (int i = 0; i < kBwdRows; ++i) {
     const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
     const bool active = r < n;
-    float yv[kMaxJ], dv[kMaxJ], dot = 0.f;
+    float yv[J], dv[J], dot = 0.f;
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
       yv[j] = (active && c < W) ? hf[(size_t)r * W + c] : 0.f;
       dv[j] = (active && c < W) ? dhf[(size_t)r * W + c] : 0.f;
@@ -474,33 +521,44 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
     dot = warp_sum(dot) / (float)W;
     const float iv = active ? invf[r] : 0.f;
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) dh[i][j] = iv * (dv[j] - yv[j] * dot);
+    for (int j = 0; j < J; ++j) dh[i][j] = iv * (dv[j] - yv[j] * dot);
   }
-  for (int l = depth - 1; l >= 0; --l) {
-    const int s = strides[l];
-    const float* w = core + (size_t)l * pw;
-    float* mine = contrib + warp * pw;
-    for (int t = lane; t < pw; t += 32) mine[t] = 0.f;
+  float xn[kBwdRows][J];  // saved input of the layer about to be processed
+  auto load_inputs = [&](int l) {
 #pragma unroll
     for (int i = 0; i < kBwdRows; ++i) {
       const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
-      const bool active = r < n;
-      float x[kMaxJ];
 #pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
+      for (int j = 0; j < J; ++j) {
         const int c = lane + 32 * j;
-        x[j] = (active && c < W) ? hs[l * nw + (size_t)r * W + c] : 0.f;
+        xn[i][j] = (r < n && c < W && l >= 0) ? hs[l * nw + (size_t)r * W + c] : 0.f;
       }
-      const float inv = row_inverse_rms(x, W, lane);
+    }
+  };
+  load_inputs(depth - 1);
+  for (int l = depth - 1; l >= 0; --l) {
+    const int s = strides[l];
+    const float* w = wts + (size_t)l * pw;
+    float* mine = contrib + warp * pw;
+    for (int t = lane; t < pw; t += 32) mine[t] = 0.f;
+    float xc[kBwdRows][J];
+#pragma unroll
+    for (int i = 0; i < kBwdRows; ++i)
+#pragma unroll
+      for (int j = 0; j < J; ++j) xc[i][j] = xn[i][j];
+    load_inputs(l - 1);
+#pragma unroll
+    for (int i = 0; i < kBwdRows; ++i) {
+      const float inv = row_inverse_rms<J>(xc[i], W, lane);
       __syncwarp();
 #pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
+      for (int j = 0; j < J; ++j) {
         const int c = lane + 32 * j;
-        if (c < W) nrow[c] = x[j] * inv;
+        if (c < W) nrow[c] = xc[i][j] * inv;
       }
       __syncwarp();
 #pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
+      for (int j = 0; j < J; ++j) {
         const int c = lane + 32 * j;
         if (c < W) {
           const float z = fmaf(nrow[(c + s) % W], w[3 * c + 1], nrow[c] * w[3 * c]) + w[3 * c + 2];
@@ -508,9 +566,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
         }
       }
       __syncwarp();
-      float dn[kMaxJ], dot = 0.f;
+      float dn[J], dot = 0.f;
 #pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
+      for (int j = 0; j < J; ++j) {
         const int c = lane + 32 * j;
         dn[j] = 0.f;
         if (c < W) {
@@ -525,7 +583,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
       }
       dot = warp_sum(dot) / (float)W;
 #pragma unroll
-      for (int j = 0; j < kMaxJ; ++j) {
+      for (int j = 0; j < J; ++j) {
         const int c = lane + 32 * j;
         if (c < W) dh[i][j] += inv * (dn[j] - nrow[c] * dot);
       }
@@ -543,55 +601,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
     const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
     if (r >= n) continue;
 #pragma unroll
-    for (int j = 0; j < kMaxJ; ++j) {
+    for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
       if (c < W) dh0[(size_t)r * W + c] = dh[i][j];
     }
-  }
-}
-
-// Chain backward over the class rows: dv = dE[k]; for l = ed-1 .. 0 the
-// chain weights' gradient sums dv[c] v_l[c] and dv[c] v_l[c+1] over the
-// class rows (fixed order: warp-strided rows, then warps in order), and
-// dv <- dv[c] w0[c] + dv[c-1] w1[c-1].  One CTA; dv lives in `dvbuf`.
-constexpr int kChainWarps = 16;
-__global__ void __launch_bounds__(kChainWarps * 32)
-    chain_backward(int m, int W, int ed, const float* __restrict__ chain, const float* __restrict__ states,
-                   const float* __restrict__ dE, float* __restrict__ dvbuf, float* __restrict__ grad) {
-  extern __shared__ float sm[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* vrow = sm + warp * 2 * W;
-  float* drow = vrow + W;
-  float* contrib = sm + kChainWarps * 2 * W;
-  float* mine = contrib + warp * 2 * W;
-  const size_t mw = (size_t)m * W;
-  for (int k = warp; k < m; k += kChainWarps)
-    for (int c = lane; c < W; c += 32) dvbuf[(size_t)k * W + c] = dE[(size_t)k * W + c];
-  for (int l = ed - 1; l >= 0; --l) {
-    const float* w = chain + (size_t)l * 2 * W;
-    for (int t = lane; t < 2 * W; t += 32) mine[t] = 0.f;
-    for (int k = warp; k < m; k += kChainWarps) {
-      __syncwarp();
-      for (int c = lane; c < W; c += 32) {
-        vrow[c] = states[l * mw + (size_t)k * W + c];
-        drow[c] = dvbuf[(size_t)k * W + c];
-      }
-      __syncwarp();
-      for (int c = lane; c < W; c += 32) {
-        const float d = drow[c];
-        mine[2 * c] += d * vrow[c];
-        mine[2 * c + 1] += d * vrow[(c + 1) % W];
-        const int q = (c + W - 1) % W;
-        dvbuf[(size_t)k * W + c] = fmaf(drow[q], w[2 * q + 1], d * w[2 * c]);
-      }
-    }
-    __syncthreads();
-    for (int t = threadIdx.x; t < 2 * W; t += blockDim.x) {
-      float sum = 0.f;
-      for (int q = 0; q < kChainWarps; ++q) sum += contrib[q * 2 * W + t];
-      grad[(size_t)l * 2 * W + t] = sum;
-    }
-    __syncthreads();
   }
 }
 
@@ -775,7 +788,7 @@ struct Workspace {
   float *logits, *dlog;
   float *h, *act, *dact, *dh0, *part;  // mesh-mlp
   float *hs, *ns, *invs, *zs, *dh, *dz, *dn, *dhf, *dEread, *gemm_part;
-  float *hf, *invf, *states, *dEemb, *dv;  // shared-Neighbor
+  float *hf, *invf, *states, *dEemb, *dv, *dv2;  // shared-Neighbor
   int bwd_ctas = 0;
   cudaGraphExec_t step_graph = nullptr;
   uint32_t step_launches = 0;
@@ -1024,16 +1037,41 @@ class SimpleModel {
   uint32_t step_launches() const { return last_launches_; }
 
  private:
+  // Row values per lane (J) of the templated row kernels for this width.
+  template <class F>
+  static void with_j(int W, F&& f) {
+    if (W <= 128)
+      f(std::integral_constant<int, 4>{});
+    else if (W <= 256)
+      f(std::integral_constant<int, 8>{});
+    else if (W <= 384)
+      f(std::integral_constant<int, 12>{});
+    else
+      f(std::integral_constant<int, 16>{});
+  }
+  int core_smem_floats() const {
+    const int f = (int)c_.depth * 3 * (int)c_.width;
+    return c_.architecture == kSharedNeighbor && f <= kCoreSmemFloats ? f : 0;
+  }
+  int fwd_smem() const { return (core_smem_floats() + kFwdWarps * (int)c_.width) * 4; }
+  int bwd_smem() const { return (core_smem_floats() + kBwdWarps * 5 * (int)c_.width) * 4; }
+
+  template <int ACT>
+  void set_attributes_impl() {
+    const int fs = fwd_smem(), bs = bwd_smem();
+    with_j((int)c_.width, [&](auto jc) {
+      constexpr int J = decltype(jc)::value;
+      SIMPLE_CUDA(cudaFuncSetAttribute(&mlp_forward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, fs));
+      SIMPLE_CUDA(cudaFuncSetAttribute(&mlp_backward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, bs));
+      SIMPLE_CUDA(cudaFuncSetAttribute(&shared_forward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, fs));
+      SIMPLE_CUDA(cudaFuncSetAttribute(&shared_backward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, bs));
+    });
+  }
   void set_attributes() {
-    const int W = (int)c_.width;
-    const int bwd_smem = (kBwdWarps * 2 * W + kBwdWarps * 3 * W) * 4;
-    const int chain_smem = (kChainWarps * 2 * W + kChainWarps * 2 * W) * 4;
-    SIMPLE_CUDA(cudaFuncSetAttribute(&mlp_backward<kRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem));
-    SIMPLE_CUDA(cudaFuncSetAttribute(&mlp_backward<kSquare>, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem));
-    SIMPLE_CUDA(cudaFuncSetAttribute(&shared_backward<kRelu>, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem));
-    SIMPLE_CUDA(
-        cudaFuncSetAttribute(&shared_backward<kSquare>, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem));
-    SIMPLE_CUDA(cudaFuncSetAttribute(&chain_backward, cudaFuncAttributeMaxDynamicSharedMemorySize, chain_smem));
+    if (c_.activation == kRelu)
+      set_attributes_impl<kRelu>();
+    else
+      set_attributes_impl<kSquare>();
   }
 
   void check_table(const mb_simple_table* t) const {
@@ -1103,6 +1141,7 @@ class SimpleModel {
       w->dEemb = M.alloc<float>(m * W);
       w->dEread = M.alloc<float>(m * W);
       w->dv = M.alloc<float>(m * W);
+      w->dv2 = M.alloc<float>(m * W);
       part = gemm_partial_floats((int)m, (int)W, n, kSplitK);
     }
     w->gemm_part = M.alloc<float>(std::max<size_t>(part, 1));
@@ -1125,6 +1164,11 @@ class SimpleModel {
 
   template <int ACT>
   void forward_impl(Workspace& ws) {
+    with_j((int)c_.width, [&](auto jc) { forward_j<ACT, decltype(jc)::value>(ws); });
+  }
+
+  template <int ACT, int J>
+  void forward_j(Workspace& ws) {
     const int n = ws.n, W = (int)c_.width, m = (int)c_.modulus;
     const size_t nw = (size_t)n * W;
     const int fgrid = (n + kFwdWarps - 1) / kFwdWarps;
@@ -1132,18 +1176,18 @@ class SimpleModel {
     if (c_.architecture == kMeshMlp) {
       const int L = mesh_layers(c_), p = parents(c_);
       const float* R = w + offsets_[1];
-      mlp_forward<ACT><<<fgrid, kFwdWarps * 32, kFwdWarps * W * 4, stream_>>>(
+      mlp_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
           n, W, m, L, p, strides_, ws.a, ws.b, w + offsets_[0], w + (L > 0 ? offsets_[2] : 0), ws.h, ws.act); ++launches_;
       // logits = act . R  (R [W][m]: B element (j, c) at R[c * m + j])
       gemm({ws.act, W, false}, {R, m, true}, ws.logits, m, n, m, W, nullptr);
     } else if (c_.architecture == kRotaryDense) {
       const float* E = w + offsets_[0];
-      rotary_embed<<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.a, ws.b, E, ws.hs, ws.ns, ws.invs); ++launches_;
+      rotary_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.a, ws.b, E, ws.hs, ws.ns, ws.invs); ++launches_;
       for (uint32_t l = 0; l < c_.depth; ++l) {
         const float* D = w + offsets_[1 + l];
         // z = n_l . D  (D [in][out]: B element (out, in) at D[in * W + out])
         gemm({ws.ns + l * nw, W, false}, {D, W, true}, ws.zs + l * nw, W, n, W, W, nullptr);
-        residual_norm<ACT><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.hs + l * nw, ws.zs + l * nw,
+        residual_norm<ACT, J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.hs + l * nw, ws.zs + l * nw,
                                                                   ws.hs + (l + 1) * nw, ws.ns + (l + 1) * nw,
                                                                   ws.invs + (l + 1) * n); ++launches_;
       }
@@ -1153,10 +1197,9 @@ class SimpleModel {
       const int ed = (int)c_.embedding_mesh_depth;
       const float* chain = w;
       const float* core = w + offsets_[ed];
-      chain_forward<<<(m + kFwdWarps - 1) / kFwdWarps, kFwdWarps * 32, kFwdWarps * W * 4, stream_>>>(m, W, ed, chain,
-                                                                                                    ws.states); ++launches_;
+      chain_forward<<<1, kChainThreads, 0, stream_>>>(m, W, ed, chain, ws.states); ++launches_;
       const float* E = ws.states + (size_t)ed * m * W;
-      shared_forward<ACT><<<fgrid, kFwdWarps * 32, kFwdWarps * W * 4, stream_>>>(
+      shared_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
           n, W, (int)c_.depth, strides_, ws.a, ws.b, E, core, ws.hs, ws.hf, ws.invf); ++launches_;
       gemm({ws.hf, W, false}, {E, W, false}, ws.logits, m, n, m, W, nullptr);
     }
@@ -1179,10 +1222,15 @@ class SimpleModel {
 
   template <int ACT>
   void backward_impl(Workspace& ws) {
+    with_j((int)c_.width, [&](auto jc) { backward_j<ACT, decltype(jc)::value>(ws); });
+  }
+
+  template <int ACT, int J>
+  void backward_j(Workspace& ws) {
     const int n = ws.n, W = (int)c_.width, m = (int)c_.modulus;
     const size_t nw = (size_t)n * W;
     const int fgrid = (n + kFwdWarps - 1) / kFwdWarps;
-    const int bwd_smem = (kBwdWarps * 2 * W + kBwdWarps * 3 * W) * 4;
+    const int bsm = bwd_smem();
     float* g = grad_;
     const float* w = w_;
     if (c_.architecture == kMeshMlp) {
@@ -1193,7 +1241,7 @@ class SimpleModel {
       // dact = dlog . R^T  (B element (c, j) at R[c * m + j])
       gemm({ws.dlog, m, false}, {R, m, false}, ws.dact, W, n, W, m, nullptr);
       if (L > 0) {
-        mlp_backward<ACT><<<ws.bwd_ctas, kBwdWarps * 32, bwd_smem, stream_>>>(n, W, L, p, strides_, w + offsets_[2],
+        mlp_backward<ACT, J><<<ws.bwd_ctas, kBwdWarps * 32, bsm, stream_>>>(n, W, L, p, strides_, w + offsets_[2],
                                                                             ws.h, ws.dact, ws.dh0, ws.part); ++launches_;
         const size_t cnt = (size_t)L * p * W;
         reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
@@ -1210,7 +1258,7 @@ class SimpleModel {
       // dE (readout share) = dlog^T . hf ; dhf = dlog . E
       gemm({ws.dlog, m, true}, {hf, W, true}, ws.dEread, W, m, W, n, ws.gemm_part, kSplitK);
       gemm({ws.dlog, m, false}, {E, W, true}, ws.dhf, W, n, W, m, nullptr);
-      rms_backward<<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, hf, ws.invs + d * n, ws.dhf, nullptr, ws.dh); ++launches_;
+      rms_backward<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, hf, ws.invs + d * n, ws.dhf, nullptr, ws.dh); ++launches_;
       for (int l = d - 1; l >= 0; --l) {
         const float* D = w + offsets_[1 + l];
         activation_gradient<ACT><<<(int)std::min<size_t>((nw + 255) / 256, 1184), 256, 0, stream_>>>(
@@ -1218,7 +1266,7 @@ class SimpleModel {
         // dD = n_l^T . dz ; dn = dz . D^T
         gemm({ws.ns + l * nw, W, true}, {ws.dz, W, true}, g + offsets_[1 + l], W, W, W, n, ws.gemm_part, kSplitK);
         gemm({ws.dz, W, false}, {D, W, false}, ws.dn, W, n, W, W, nullptr);
-        rms_backward<<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.ns + l * nw, ws.invs + l * n, ws.dn, ws.dh,
+        rms_backward<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.ns + l * nw, ws.invs + l * n, ws.dn, ws.dh,
                                                              ws.dh); ++launches_;
       }
       class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 1, ws.a, ws.b, ws.dh, ws.dEread, g + offsets_[0]); ++launches_;
@@ -1227,14 +1275,13 @@ class SimpleModel {
       const float* E = ws.states + (size_t)ed * m * W;
       gemm({ws.dlog, m, true}, {ws.hf, W, true}, ws.dEread, W, m, W, n, ws.gemm_part, kSplitK);
       gemm({ws.dlog, m, false}, {E, W, true}, ws.dhf, W, n, W, m, nullptr);
-      shared_backward<ACT><<<ws.bwd_ctas, kBwdWarps * 32, bwd_smem, stream_>>>(
+      shared_backward<ACT, J><<<ws.bwd_ctas, kBwdWarps * 32, bsm, stream_>>>(
           n, W, d, strides_, w + offsets_[ed], ws.hs, ws.hf, ws.invf, ws.dhf, ws.dh0, ws.part); ++launches_;
       const size_t cnt = (size_t)d * 3 * W;
       reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
           ws.part, ws.bwd_ctas, cnt, g + offsets_[ed]); ++launches_;
       class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 1, ws.a, ws.b, ws.dh0, ws.dEread, ws.dEemb); ++launches_;
-      const int chain_smem = (kChainWarps * 2 * W + kChainWarps * 2 * W) * 4;
-      chain_backward<<<1, kChainWarps * 32, chain_smem, stream_>>>(m, W, ed, w, ws.states, ws.dEemb, ws.dv, g); ++launches_;
+      chain_backward<<<1, kChainThreads, 0, stream_>>>(m, W, ed, w, ws.states, ws.dEemb, ws.dv, ws.dv2, g); ++launches_;
     }
     SIMPLE_CUDA(cudaGetLastError());
   }
