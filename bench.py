@@ -530,6 +530,18 @@ def grok_main(args):
     from grokking_abmod_b200.simple import GpuSimpleModel, SimpleConfig
 
     torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     config = SimpleConfig(modulus=97, **gcfg["model"])
     dataset, order = _grok_problem(gcfg, 11)
     eq = np.asarray(dataset.split(False), dtype=np.uint32)
@@ -550,6 +562,8 @@ def grok_main(args):
     clocks.start()
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     with torch.cuda.stream(stream):
         for s in range(args.steps):
             flush.zero_()
@@ -559,7 +573,7 @@ def grok_main(args):
     torch.cuda.synchronize()
     clock_info = clocks.stop()
     model.check()
-    ms = sum(a.elapsed_time(b) for a, b in events)
+    ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in events))
     value = world * args.steps / (ms / 1000.0)
 
     # end to end through the public API, as grok-simple's loop does: the
@@ -576,7 +590,7 @@ def grok_main(args):
             model.evaluate(table, valid)
             evals += 1
     model.check()
-    e_wall = time.perf_counter() - t0
+    e_wall = max_over_ranks(time.perf_counter() - t0)
     e2e = world * e2e_steps / e_wall
     d2h = evals * 2 * GROK_ROWS * (97 * 4 + 4) / e2e_steps
 
@@ -615,6 +629,8 @@ def grok_main(args):
         print(json.dumps(line), flush=True)
     del batches, table, valid
     model.close()
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def _summarize(times):

@@ -46,31 +46,74 @@ struct TcFmt {
   static constexpr int QTILE = 8 * QPART + 2 * kTcQ;  // Q, Q', dO, dO', Qt, Qt', dOt, dOt', lse2, delta
   static constexpr int K_HI = 0, K_LO = 1, VT_HI = 2, VT_LO = 3, V_HI = 4, V_LO = 5, KT_HI = 6, KT_LO = 7;
   static constexpr int Q_HI = 0, Q_LO = 1, D_HI = 2, D_LO = 3, QT_HI = 4, QT_LO = 5, DT_HI = 6, DT_LO = 7;
+  static_assert(QT_HI == 4 && DT_HI == 6, "dK/dV streams parts 0-3 and 4-7 (+ lse2, delta) as two rings");
 };
 
-__device__ __forceinline__ void split_store(float* base, int part_stride, int hi_part, int off, float x) {
-  const float h = tc::tf32_hi(x);
-  base[hi_part * part_stride + off] = h;
-  base[(hi_part + 1) * part_stride + off] = x - h;
+// Writes parts of one operand tile in the blocked K-major layout from a
+// shared-memory copy `x` ([R][HD], row stride HD + 2).  Part kind 0 is the
+// tile itself ([R rows][HD columns]), kind 1 its transpose ([HD rows][R
+// columns]); each part is written as its TF32 hi and lo halves (parts `p`,
+// `p + 1` of `tile`).  Every thread writes whole 16-byte groups of the
+// blocked layout (4 consecutive columns of one core-matrix row), so the
+// stores of a warp cover contiguous 512-byte runs.
+template <int R, int HD>
+__device__ __forceinline__ void store_parts(float* __restrict__ tile, int part_floats, int p, bool transposed,
+                                            const float* x) {
+  constexpr int XS = HD + 2;
+  const int rows = transposed ? HD : R, cols = transposed ? R : HD;
+  float* hi = tile + (size_t)p * part_floats;
+  float* lo = hi + part_floats;
+  for (int q = threadIdx.x; q < rows * cols / 4; q += blockDim.x) {
+    const int rl = q & 7, c4 = (q >> 3) % (cols / 4), rg = (q >> 3) / (cols / 4);
+    const int r = rg * 8 + rl, c = c4 * 4;
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = transposed ? x[(c + e) * XS + r] : x[r * XS + c + e];
+    float4 h, l;
+    h.x = tc::tf32_hi(v[0]);
+    h.y = tc::tf32_hi(v[1]);
+    h.z = tc::tf32_hi(v[2]);
+    h.w = tc::tf32_hi(v[3]);
+    l = make_float4(v[0] - h.x, v[1] - h.y, v[2] - h.z, v[3] - h.w);
+    reinterpret_cast<float4*>(hi)[q] = h;
+    reinterpret_cast<float4*>(lo)[q] = l;
+  }
 }
 
-// Key tiles of K and V: grid (ceil(rows/64), H), 256 threads.
+// Rows [row0, row0 + R) of head h of a row-major [rows][W] tensor into
+// shared memory ([R][HD], stride HD + 2), zero past the last row.
+template <int R, int HD>
+__device__ __forceinline__ void load_rows(float* x, const float* __restrict__ g, int row0, int rows, int W, int h) {
+  constexpr int XS = HD + 2;
+  for (int i = threadIdx.x; i < R * HD / 4; i += blockDim.x) {
+    const int r = i / (HD / 4), c = (i % (HD / 4)) * 4, row = row0 + r;
+    const float4 v = row < rows ? __ldg(reinterpret_cast<const float4*>(g + (size_t)row * W + h * HD + c))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+    x[r * XS + c] = v.x;
+    x[r * XS + c + 1] = v.y;
+    x[r * XS + c + 2] = v.z;
+    x[r * XS + c + 3] = v.w;
+  }
+}
+
+// Key tiles of K and V: grid (ceil(rows/64), H), 256 threads.  `parts` is a
+// bit mask over the hi parts of TcFmt's key tile (K_HI, VT_HI, V_HI, KT_HI):
+// only the parts the following kernel reads are written.
 template <int HD>
 __global__ void __launch_bounds__(256) attention_format_keys(int rows, int W, const float* __restrict__ k,
-                                                               const float* __restrict__ v, float* __restrict__ fmt) {
+                                                               const float* __restrict__ v, float* __restrict__ fmt,
+                                                               unsigned parts) {
   using F = TcFmt<HD>;
+  __shared__ float xk[kTcK * (HD + 2)], xv[kTcK * (HD + 2)];
   const int t = blockIdx.x, h = blockIdx.y;
   float* tile = fmt + ((size_t)h * gridDim.x + t) * F::KTILE;
-  for (int i = threadIdx.x; i < kTcK * HD; i += 256) {
-    const int r = i / HD, c = i % HD, row = t * kTcK + r;
-    const float kv = row < rows ? k[(size_t)row * W + h * HD + c] : 0.f;
-    const float vv = row < rows ? v[(size_t)row * W + h * HD + c] : 0.f;
-    const int rowmajor = tc::blk(r, c, HD), transposed = tc::blk(c, r, kTcK);
-    split_store(tile, F::KPART, F::K_HI, rowmajor, kv);
-    split_store(tile, F::KPART, F::V_HI, rowmajor, vv);
-    split_store(tile, F::KPART, F::KT_HI, transposed, kv);
-    split_store(tile, F::KPART, F::VT_HI, transposed, vv);
-  }
+  load_rows<kTcK, HD>(xk, k, t * kTcK, rows, W, h);
+  load_rows<kTcK, HD>(xv, v, t * kTcK, rows, W, h);
+  __syncthreads();
+  if (parts & (1u << F::K_HI)) store_parts<kTcK, HD>(tile, F::KPART, F::K_HI, false, xk);
+  if (parts & (1u << F::VT_HI)) store_parts<kTcK, HD>(tile, F::KPART, F::VT_HI, true, xv);
+  if (parts & (1u << F::V_HI)) store_parts<kTcK, HD>(tile, F::KPART, F::V_HI, false, xv);
+  if (parts & (1u << F::KT_HI)) store_parts<kTcK, HD>(tile, F::KPART, F::KT_HI, true, xk);
 }
 
 // Query tiles of Q and dO with their LSE and delta: grid (ceil(rows/32), H).
@@ -81,18 +124,16 @@ __global__ void __launch_bounds__(256) attention_format_queries(int rows, int W,
                                                                   const float* __restrict__ delta,
                                                                   float* __restrict__ fmt) {
   using F = TcFmt<HD>;
+  __shared__ float xq[kTcQ * (HD + 2)], xd[kTcQ * (HD + 2)];
   const int t = blockIdx.x, h = blockIdx.y;
   float* tile = fmt + ((size_t)h * gridDim.x + t) * F::QTILE;
-  for (int i = threadIdx.x; i < kTcQ * HD; i += 256) {
-    const int r = i / HD, c = i % HD, row = t * kTcQ + r;
-    const float qv = row < rows ? q[(size_t)row * W + h * HD + c] : 0.f;
-    const float dv = row < rows ? dout[(size_t)row * W + h * HD + c] : 0.f;
-    const int rowmajor = tc::blk(r, c, HD), transposed = tc::blk(c, r, kTcQ);
-    split_store(tile, F::QPART, F::Q_HI, rowmajor, qv);
-    split_store(tile, F::QPART, F::D_HI, rowmajor, dv);
-    split_store(tile, F::QPART, F::QT_HI, transposed, qv);
-    split_store(tile, F::QPART, F::DT_HI, transposed, dv);
-  }
+  load_rows<kTcQ, HD>(xq, q, t * kTcQ, rows, W, h);
+  load_rows<kTcQ, HD>(xd, dout, t * kTcQ, rows, W, h);
+  __syncthreads();
+  store_parts<kTcQ, HD>(tile, F::QPART, F::Q_HI, false, xq);
+  store_parts<kTcQ, HD>(tile, F::QPART, F::D_HI, false, xd);
+  store_parts<kTcQ, HD>(tile, F::QPART, F::QT_HI, true, xq);
+  store_parts<kTcQ, HD>(tile, F::QPART, F::DT_HI, true, xd);
   if (threadIdx.x < kTcQ) {
     const int row = t * kTcQ + threadIdx.x;
     tile[8 * F::QPART + threadIdx.x] = row < rows ? lse2[(size_t)h * rows + row] : 0.f;
@@ -191,11 +232,8 @@ struct TcAtt {
   static constexpr int FWD_STAGE = 4 * F::KPART;  // K, K', Vt, Vt'
   static constexpr int DQ_STAGES = 2;
   static constexpr int DQ_STAGE = 6 * F::KPART;  // K, K', V, V', Kt, Kt'
-  static constexpr int KV_STAGES = 3;
-  static constexpr int KV_STAGE = F::QTILE;  // a whole query tile
   static constexpr size_t smem_forward = (size_t)FWD_STAGES * FWD_STAGE * sizeof(float);
   static constexpr size_t smem_dq = (size_t)DQ_STAGES * DQ_STAGE * sizeof(float);
-  static constexpr size_t smem_dkdv = (size_t)KV_STAGES * KV_STAGE * sizeof(float);
 };
 
 struct TcShared {
@@ -564,21 +602,58 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 // ------------------------------------------------------------------- dK/dV
 // A CTA owns 128 keys of one head and walks the later queries 32 at a time.
-// TMEM: K hi | K lo | V hi | V lo (64 each) | S^T then P^T hi | dP^T then
-// dS^T hi | P^T lo | dS^T lo (32 each) | dV | dK (64 each).
+// Threads 0-255 compute (key row = tid % 128 = TMEM lane, half = tid / 128
+// takes query columns [16 half, 16 half + 16)), warp 8 streams the A ring
+// (Q, dO), warp 9 issues the MMAs, warp 10 streams the B ring (Q^T, dO^T,
+// LSE, delta).  K lives in TMEM, V in shared memory; S/dP and their P/dS
+// successors are double-buffered in TMEM, so the MMAs of query step j+1 run
+// while the compute warps turn step j's scores into P and dS.
+// TMEM: K hi | K lo | dV | dK (64 each) | buffer 0 | buffer 1, each buffer
+// S^T then P^T hi | dP^T then dS^T hi | P^T lo | dS^T lo (32 each).
 // Per query step: S^T = K Q^T, dP^T = V dO^T (keys on lanes); P^T, dS^T;
 // dV += P^T dO, dK += dS^T Q (B = dO^T / Q^T tiles).
+constexpr int kTcKvThreads = 352;
+constexpr int kKvProducerA = 256, kKvIssuer = 288, kKvProducerB = 320;
+
 template <int HD>
-__global__ void __launch_bounds__(kTcThreads, 1)
+struct TcKv {
+  using F = TcFmt<HD>;
+  static constexpr int NA = 3, NB = 2;
+  static constexpr int A_FLOATS = 4 * F::QPART;             // Q, Q', dO, dO'
+  static constexpr int B_FLOATS = 4 * F::QPART + 2 * kTcQ;  // Q^T, Q^T', dO^T, dO^T', lse2, delta
+  static constexpr int V_FLOATS = 2 * kTcRows * HD;         // V hi, V lo
+  static constexpr size_t smem = (size_t)(V_FLOATS + NA * A_FLOATS + NB * B_FLOATS) * sizeof(float);
+};
+
+// D (+)= A . B^T with A a K-major hi/lo shared tile [128 rows][KC columns].
+template <int KC>
+__device__ __forceinline__ void mma_smem_a(uint32_t d, const float* ah, const float* al, const float* bh,
+                                           const float* bl, uint32_t idesc, bool accumulate) {
+#pragma unroll
+  for (int s = 0; s < KC / 8; ++s) {
+    const uint64_t a_h = tc::desc_kmajor(ah, KC, s), a_l = tc::desc_kmajor(al, KC, s);
+    const uint64_t b_h = tc::desc_kmajor(bh, KC, s), b_l = tc::desc_kmajor(bl, KC, s);
+    tc::mma_ss(d, a_h, b_h, idesc, (accumulate || s > 0) ? 1u : 0u);
+    tc::mma_ss(d, a_h, b_l, idesc, 1u);
+    tc::mma_ss(d, a_l, b_h, idesc, 1u);
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kTcKvThreads, 1)
     attention_backward_dkdv_tc(int rows, int W, int T, float scale, const float* __restrict__ k,
                                const float* __restrict__ v, const float* __restrict__ qfmt,
                                const float* __restrict__ dv_add, float* __restrict__ dk, float* __restrict__ dv,
                                int* __restrict__ err) {
-  using A = TcAtt<HD>;
   using F = TcFmt<HD>;
-  constexpr int NS = A::KV_STAGES;
+  using S = TcKv<HD>;
+  constexpr int NA = S::NA, NB = S::NB;
   extern __shared__ __align__(128) float sm[];
-  __shared__ uint64_t q_full[NS], q_empty[NS], s_full, d_full, g_done;
+  float* Vh = sm;
+  float* Vl = sm + kTcRows * HD;
+  float* ring_a = sm + S::V_FLOATS;
+  float* ring_b = ring_a + NA * S::A_FLOATS;
+  __shared__ uint64_t a_full[NA], a_empty[NA], b_full[NB], b_empty[NB], s_full[2], d_full[2], g_done[2];
   __shared__ TcShared sh;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int k0 = blockIdx.x * kTcRows;
@@ -586,13 +661,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nqt = (rows + kTcQ - 1) / kTcQ;
   if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
   if (tid == 0) {
-    for (int b = 0; b < NS; ++b) {
-      tc::bar_init(&q_full[b], 1);
-      tc::bar_init(&q_empty[b], 1);
+    for (int i = 0; i < NA; ++i) {
+      tc::bar_init(&a_full[i], 1);
+      tc::bar_init(&a_empty[i], 1);
     }
-    tc::bar_init(&s_full, 1);
-    tc::bar_init(&d_full, kTcCompute);
-    tc::bar_init(&g_done, 1);
+    for (int i = 0; i < NB; ++i) {
+      tc::bar_init(&b_full[i], 1);
+      tc::bar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      tc::bar_init(&s_full[i], 1);
+      tc::bar_init(&d_full[i], kTcCompute);
+      tc::bar_init(&g_done[i], 1);
+    }
     tc::bar_init_fence();
     sh.failed = 0;
   }
@@ -600,8 +681,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t t0 = sh.tmem_base;
-  const uint32_t tKh = t0, tKl = t0 + 64, tVh = t0 + 128, tVl = t0 + 192, tS = t0 + 256, tP = t0 + 288,
-                 tPl = t0 + 320, tSl = t0 + 352, tdV = t0 + 384, tdK = t0 + 448;
+  const uint32_t tKh = t0, tKl = t0 + 64, tdV = t0 + 128, tdK = t0 + 192;
+  auto tS = [&](int b) { return t0 + 256 + 128 * b; };
+  auto tP = [&](int b) { return t0 + 256 + 128 * b + 32; };
+  auto tPl = [&](int b) { return t0 + 256 + 128 * b + 64; };
+  auto tSl = [&](int b) { return t0 + 256 + 128 * b + 96; };
   const int last = min(rows, k0 + kTcRows) - 1;
   const int qend = min(rows, (last / T + 1) * T);
   const int n = (qend - k0 + kTcQ - 1) / kTcQ;
@@ -609,17 +693,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp < 4) {
     const uint32_t lane = (uint32_t)(warp * 32) << 16;
     row_to_tmem<HD>(k, k0 + tid, rows, W, h, tKh + lane, tKl + lane);
-    row_to_tmem<HD>(v, k0 + tid, rows, W, h, tVh + lane, tVl + lane);
     tc::tmem_st_wait();
   }
+  if (tid < kTcCompute) {
+    // V rows of the CTA, split and stored in the blocked K-major layout.
+    for (int i = tid; i < kTcRows * HD; i += kTcCompute) {
+      const int r = i / HD, c = i % HD;
+      const float x = k0 + r < rows ? v[(size_t)(k0 + r) * W + h * HD + c] : 0.f;
+      const float hi = tc::tf32_hi(x);
+      Vh[tc::blk(r, c, HD)] = hi;
+      Vl[tc::blk(r, c, HD)] = x - hi;
+    }
+  }
+  tc::fence_async_smem();
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
 
   if (tid < kTcCompute) {
-    // Thread (key row, half) handles query columns [16 half, 16 half + 16).
+    // ---------------------------------------------------------- softmax
     const int row = tid & (kTcRows - 1), half = tid >> 7;
-    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t lane = (uint32_t)(((tid >> 5) & 3) * 32) << 16;
     const float scale2 = scale * 1.4426950408889634f;
     const int kr = k0 + row;
     const int ke = (kr / T + 1) * T;  // end of the key's sequence
@@ -629,15 +723,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool one_seq = (k0 + kTcRows - 1) / T == k0 / T && k0 + kTcRows <= rows;
     bool done = false;
     for (int j = 0; j < n; ++j) {
-      const int st = j % NS;
-      TC_WAIT_OR_FAIL(&s_full, j & 1);
+      const int b = j & 1, sb = j % NB;
+      TC_WAIT_OR_FAIL(&s_full[b], (j >> 1) & 1);
+      TC_WAIT_OR_FAIL(&b_full[sb], (j / NB) & 1);
       tc::fence_after_sync();
-      const float* stage = sm + st * A::KV_STAGE;
-      const float* Ls = stage + 8 * F::QPART + 16 * half;  // lse2 of the query step
-      const float* Es = Ls + kTcQ;                         // delta of the query step
+      const float* Ls = ring_b + sb * S::B_FLOATS + 4 * F::QPART + 16 * half;  // lse2 of the query step
+      const float* Es = Ls + kTcQ;                                              // delta of the query step
       float s[16], dp[16];
-      tc::tmem_ld16(tS + 16 * half + lane, s);
-      tc::tmem_ld16(tP + 16 * half + lane, dp);
+      tc::tmem_ld16(tS(b) + 16 * half + lane, s);
+      tc::tmem_ld16(tP(b) + 16 * half + lane, dp);
       const int qt = k0 + j * kTcQ;
       const bool full = one_seq && qt >= k0 + kTcRows - 1 && qt + kTcQ <= min(kseq_end, rows);
       const int qh = qt + 16 * half;
@@ -649,14 +743,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         s[c] = p;
         dp[c] = p * (dp[c] - Es[c]) * scale;
       }
-      tc_st_split<16>(tS + 16 * half + lane, tPl + 16 * half + lane, s);   // P^T hi over S^T
-      tc_st_split<16>(tP + 16 * half + lane, tSl + 16 * half + lane, dp);  // dS^T hi over dP^T
+      tc_st_split<16>(tS(b) + 16 * half + lane, tPl(b) + 16 * half + lane, s);   // P^T hi over S^T
+      tc_st_split<16>(tP(b) + 16 * half + lane, tSl(b) + 16 * half + lane, dp);  // dS^T hi over dP^T
       tc::tmem_st_wait();
       tc::fence_before_sync();
-      tc::bar_arrive(&d_full);
+      tc::bar_arrive(&d_full[b]);
       if (j + 1 == n) done = true;
     }
-    if (done && !tc::bar_wait(&g_done, (n - 1) & 1)) sh.failed = 1;
+    if (done && !tc::bar_wait(&g_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
     tc::fence_after_sync();
     if (done && !sh.failed) {
       const bool in = kr < rows;
@@ -676,36 +770,57 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
     }
-  } else if (tid == kTcProducer) {
+  } else if (tid == kKvProducerA) {
+    // ---------------------------------------------------------- A ring: Q, dO
     for (int j = 0; j < n; ++j) {
-      const int st = j % NS;
-      if (j >= NS) {
-        TC_WAIT_OR_FAIL(&q_empty[st], ((j - NS) / NS) & 1);
+      const int st = j % NA;
+      if (j >= NA) {
+        TC_WAIT_OR_FAIL(&a_empty[st], ((j - NA) / NA) & 1);
       }
-      tc::bar_expect_tx(&q_full[st], A::KV_STAGE * 4);
-      tc::bulk_g2s(sm + st * A::KV_STAGE, qfmt + ((size_t)h * nqt + qt0 + j) * F::QTILE, A::KV_STAGE * 4,
-                   &q_full[st]);
+      tc::bar_expect_tx(&a_full[st], S::A_FLOATS * 4);
+      tc::bulk_g2s(ring_a + st * S::A_FLOATS, qfmt + ((size_t)h * nqt + qt0 + j) * F::QTILE, S::A_FLOATS * 4,
+                   &a_full[st]);
     }
-  } else if (tid == kTcIssuer) {
+  } else if (tid == kKvProducerB) {
+    // ---------------------------------------------------------- B ring: Q^T, dO^T, lse2, delta
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NB;
+      if (j >= NB) {
+        TC_WAIT_OR_FAIL(&b_empty[st], ((j - NB) / NB) & 1);
+      }
+      tc::bar_expect_tx(&b_full[st], S::B_FLOATS * 4);
+      tc::bulk_g2s(ring_b + st * S::B_FLOATS, qfmt + ((size_t)h * nqt + qt0 + j) * F::QTILE + 4 * F::QPART,
+                   S::B_FLOATS * 4, &b_full[st]);
+    }
+  } else if (tid == kKvIssuer) {
+    // ---------------------------------------------------------- MMA issuer
     constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcQ, false, false);
     constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
-    for (int j = 0; j < n; ++j) {
-      const int st = j % NS;
-      const float* stage = sm + st * A::KV_STAGE;
-      TC_WAIT_OR_FAIL(&q_full[st], (j / NS) & 1);
-      if (j >= 1) {
-        TC_WAIT_OR_FAIL(&g_done, (j - 1) & 1);  // dV/dK of step j-1 have read P^T / dS^T
+    for (int j = 0; j <= n; ++j) {
+      if (j < n) {
+        const int sa = j % NA, b = j & 1;
+        TC_WAIT_OR_FAIL(&a_full[sa], (j / NA) & 1);
+        if (j >= 2) {
+          TC_WAIT_OR_FAIL(&g_done[b], ((j - 2) >> 1) & 1);  // dV/dK of step j-2 have read buffer b
+        }
+        tc::fence_after_sync();
+        const float* A = ring_a + sa * S::A_FLOATS;
+        mma_tmem_a<HD>(tS(b), tKh, tKl, A + F::Q_HI * F::QPART, A + F::Q_LO * F::QPART, idS, false);  // S^T
+        mma_smem_a<HD>(tP(b), Vh, Vl, A + F::D_HI * F::QPART, A + F::D_LO * F::QPART, idS, false);    // dP^T
+        tc::commit(&s_full[b]);
+        tc::commit(&a_empty[sa]);
       }
-      tc::fence_after_sync();
-      mma_tmem_a<HD>(tS, tKh, tKl, stage + F::Q_HI * F::QPART, stage + F::Q_LO * F::QPART, idS, false);  // S^T
-      mma_tmem_a<HD>(tP, tVh, tVl, stage + F::D_HI * F::QPART, stage + F::D_LO * F::QPART, idS, false);  // dP^T
-      tc::commit(&s_full);
-      TC_WAIT_OR_FAIL(&d_full, j & 1);
-      tc::fence_after_sync();
-      mma_tmem_a<kTcQ>(tdV, tS, tPl, stage + F::DT_HI * F::QPART, stage + F::DT_LO * F::QPART, idG, j > 0);
-      mma_tmem_a<kTcQ>(tdK, tP, tSl, stage + F::QT_HI * F::QPART, stage + F::QT_LO * F::QPART, idG, j > 0);
-      tc::commit(&g_done);
-      tc::commit(&q_empty[st]);
+      if (j >= 1) {
+        const int pj = j - 1, sb = pj % NB, pb = pj & 1;
+        TC_WAIT_OR_FAIL(&b_full[sb], (pj / NB) & 1);
+        TC_WAIT_OR_FAIL(&d_full[pb], (pj >> 1) & 1);
+        tc::fence_after_sync();
+        const float* B = ring_b + sb * S::B_FLOATS;  // Q^T, Q^T', dO^T, dO^T'
+        mma_tmem_a<kTcQ>(tdV, tS(pb), tPl(pb), B + 2 * F::QPART, B + 3 * F::QPART, idG, pj > 0);  // dV += P^T dO
+        mma_tmem_a<kTcQ>(tdK, tP(pb), tSl(pb), B, B + F::QPART, idG, pj > 0);                     // dK += dS^T Q
+        tc::commit(&g_done[pb]);
+        tc::commit(&b_empty[sb]);
+      }
     }
   }
   tc::fence_before_sync();

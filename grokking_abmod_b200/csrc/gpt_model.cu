@@ -209,19 +209,20 @@ struct AttentionOpsTc final : AttentionOps {
     MB_CUDA(cudaFuncSetAttribute(&attention_backward_dq_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)K::smem_dq));
     MB_CUDA(cudaFuncSetAttribute(&attention_backward_dkdv_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)K::smem_dkdv));
+                                 (int)TcKv<HD>::smem));
   }
   static size_t key_floats(int rows, int H) { return (size_t)H * ((rows + kTcK - 1) / kTcK) * F::KTILE; }
   static size_t query_floats(int rows, int H) { return (size_t)H * ((rows + kTcQ - 1) / kTcQ) * F::QTILE; }
   size_t scratch_floats(int rows, int H) const override { return key_floats(rows, H) + query_floats(rows, H); }
   float* kfmt() const { return scratch; }
   float* qfmt(int rows, int H) const { return scratch + key_floats(rows, H); }
-  void format_keys(cudaStream_t s, int rows, int W, int H, const float* k, const float* v) {
-    attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), 256, 0, s>>>(rows, W, k, v, kfmt());
+  // Writes the key-tile parts (bit mask over TcFmt's hi parts) the next kernel reads.
+  void format_keys(cudaStream_t s, int rows, int W, int H, const float* k, const float* v, unsigned parts) {
+    attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), 256, 0, s>>>(rows, W, k, v, kfmt(), parts);
   }
   void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                const float* v, float* o, float* lse) override {
-    format_keys(s, rows, W, H, k, v);
+    format_keys(s, rows, W, H, k, v, (1u << F::K_HI) | (1u << F::VT_HI));
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
     attention_forward_tc<HD><<<grid, kTcThreads, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
                                                                         kfmt(), o, lse, err);
@@ -232,12 +233,12 @@ struct AttentionOpsTc final : AttentionOps {
     attention_format_queries<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), 256, 0, s>>>(rows, W, q, dout, lse, delta,
                                                                                    qfmt(rows, H));
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dkdv_tc<HD><<<grid, kTcThreads, K::smem_dkdv, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), k, v,
+    attention_backward_dkdv_tc<HD><<<grid, kTcKvThreads, TcKv<HD>::smem, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), k, v,
                                                                            qfmt(rows, H), dv_add, dk, dv, err);
   }
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
-    format_keys(s, rows, W, H, k, v);
+    format_keys(s, rows, W, H, k, v, (1u << F::K_HI) | (1u << F::V_HI) | (1u << F::KT_HI));
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
     attention_backward_dq_tc<HD><<<grid, kTcThreads, K::smem_dq, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, dout,
                                                                        kfmt(), lse, delta, dq, err);
