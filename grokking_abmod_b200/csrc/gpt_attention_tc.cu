@@ -17,13 +17,14 @@
 //    one query tile (dK/dV) is 8 parts x 32 rows x hd plus its LSE and delta.
 //    Operands needed with rows along N are stored transposed (K-major), since
 //    TF32 MMAs read a transposed (MN-major) operand as zeros here.
-//  * A single producer thread streams each step's tile into a multi-stage
-//    shared-memory ring with cp.async.bulk (plain, no multicast); the tile
-//    arrives as mbarrier transactions.
+//  * Producer threads stream each step's tile into multi-stage shared-memory
+//    rings with cp.async.bulk (plain, no multicast); the tiles arrive as
+//    mbarrier transactions.
 //  * The 128-row operand owned by the CTA (Q in the forward, Q and dO in dQ,
-//    K and V in dK/dV) is split by the compute threads into TMEM, and every
-//    MMA uses the A-from-TMEM form; score / probability tiles also live in
-//    TMEM (thread i of the compute warps owns lane i = row i).
+//    K in dK/dV) is split by the compute threads into TMEM and used through
+//    the A-from-TMEM form (dK/dV keeps V in shared memory); score /
+//    probability tiles also live in TMEM (thread i of the compute warps owns
+//    lane i = row i).
 //  * One thread issues all MMAs and commits them to mbarriers; all waits are
 //    bounded and report through `err` instead of hanging.
 
@@ -138,6 +139,43 @@ __global__ void __launch_bounds__(256) attention_format_queries(int rows, int W,
     const int row = t * kTcQ + threadIdx.x;
     tile[8 * F::QPART + threadIdx.x] = row < rows ? lse2[(size_t)h * rows + row] : 0.f;
     tile[8 * F::QPART + kTcQ + threadIdx.x] = row < rows ? delta[(size_t)h * rows + row] : 0.f;
+  }
+}
+
+// The CTA's 128 rows of head h, loaded by all `nthreads` threads with
+// coalesced float4 reads into a staging area ([128][HD + 4]) of shared memory.
+template <int HD>
+__device__ __forceinline__ void stage_rows(float* stage, const float* __restrict__ g, int row0, int rows, int W,
+                                           int h, int nthreads) {
+  constexpr int XS = HD + 4, PER = kTcRows * HD / 4;
+  for (int i = threadIdx.x; i < PER; i += nthreads) {
+    const int r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+    const float4 x = row0 + r < rows ? __ldg(reinterpret_cast<const float4*>(g + (size_t)(row0 + r) * W + h * HD + c))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(stage + r * XS + c) = x;
+  }
+}
+
+// Row `r` of a staging area split into hi/lo TMEM columns of this thread's
+// lane (threads 0-127, row = TMEM lane).
+template <int HD>
+__device__ __forceinline__ void staged_row_to_tmem(const float* stage, int r, uint32_t thi, uint32_t tlo) {
+  constexpr int XS = HD + 4;
+#pragma unroll
+  for (int c = 0; c < HD; c += 16) {
+    float hi[16], lo[16];
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      const float4 x = *reinterpret_cast<const float4*>(stage + r * XS + c + e);
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        hi[e + u] = tc::tf32_hi(xs[u]);
+        lo[e + u] = xs[u] - hi[e + u];
+      }
+    }
+    tc::tmem_st16(thi + c, hi);
+    tc::tmem_st16(tlo + c, lo);
   }
 }
 
@@ -690,19 +728,33 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
   const int qend = min(rows, (last / T + 1) * T);
   const int n = (qend - k0 + kTcQ - 1) / kTcQ;
   const int qt0 = k0 / kTcQ;
+  // K through the (still idle) A ring into TMEM.
+  stage_rows<HD>(ring_a, k, k0, rows, W, h, kTcKvThreads);
+  __syncthreads();
   if (warp < 4) {
     const uint32_t lane = (uint32_t)(warp * 32) << 16;
-    row_to_tmem<HD>(k, k0 + tid, rows, W, h, tKh + lane, tKl + lane);
+    staged_row_to_tmem<HD>(ring_a, tid, tKh + lane, tKl + lane);
     tc::tmem_st_wait();
   }
   if (tid < kTcCompute) {
-    // V rows of the CTA, split and stored in the blocked K-major layout.
-    for (int i = tid; i < kTcRows * HD; i += kTcCompute) {
-      const int r = i / HD, c = i % HD;
-      const float x = k0 + r < rows ? v[(size_t)(k0 + r) * W + h * HD + c] : 0.f;
-      const float hi = tc::tf32_hi(x);
-      Vh[tc::blk(r, c, HD)] = hi;
-      Vl[tc::blk(r, c, HD)] = x - hi;
+    // V rows of the CTA, split and stored in the blocked K-major layout.  All
+    // loads are issued before the first shared-memory store, so they overlap.
+    constexpr int PER = kTcRows * HD / 4 / kTcCompute;  // float4 per thread
+    float4 x[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int i = tid + kTcCompute * j, r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+      x[j] = k0 + r < rows ? __ldg(reinterpret_cast<const float4*>(v + (size_t)(k0 + r) * W + h * HD + c))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int i = tid + kTcCompute * j, r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+      const float4 h = make_float4(tc::tf32_hi(x[j].x), tc::tf32_hi(x[j].y), tc::tf32_hi(x[j].z),
+                                   tc::tf32_hi(x[j].w));
+      *reinterpret_cast<float4*>(Vh + tc::blk(r, c, HD)) = h;
+      *reinterpret_cast<float4*>(Vl + tc::blk(r, c, HD)) =
+          make_float4(x[j].x - h.x, x[j].y - h.y, x[j].z - h.z, x[j].w - h.w);
     }
   }
   tc::fence_async_smem();
