@@ -202,6 +202,18 @@ __device__ __forceinline__ void row_to_tmem(const float* __restrict__ g, int row
   }
 }
 
+// The 128-row tile CTA b works on, ordered by causal work (most first) so the
+// last wave of the grid holds the shortest CTAs.  With sequences made of
+// whole tiles, all sequences' tiles at one position come together; a query
+// tile's work grows with its position (more keys before it), a key tile's
+// shrinks (fewer queries after it).  Other shapes keep a plain order.
+__device__ __forceinline__ int tile_by_work(int b, int nt, int rows, int T, bool queries) {
+  if (T % kTcRows != 0 || rows % T != 0) return queries ? nt - 1 - b : b;
+  const int per_seq = T / kTcRows, nseq = nt / per_seq;
+  const int i = b / nseq, seq = b % nseq;
+  return seq * per_seq + (queries ? per_seq - 1 - i : i);
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -310,7 +322,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ float xm[2][kTcRows], xl[2][kTcRows];
   const int tid = threadIdx.x, warp = tid >> 5;
   const int nt = (rows + kTcRows - 1) / kTcRows;
-  const int q0 = (nt - 1 - (int)blockIdx.x) * kTcRows;  // longest causal spans first
+  const int q0 = tile_by_work(blockIdx.x, nt, rows, T, true) * kTcRows;  // longest causal spans first
   const int h = blockIdx.y;
   const int nkt = (rows + kTcK - 1) / kTcK;
   if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
@@ -515,7 +527,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ TcShared sh;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int nt = (rows + kTcRows - 1) / kTcRows;
-  const int q0 = (nt - 1 - (int)blockIdx.x) * kTcRows;
+  const int q0 = tile_by_work(blockIdx.x, nt, rows, T, true) * kTcRows;
   const int h = blockIdx.y;
   const int nkt = (rows + kTcK - 1) / kTcK;
   if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
@@ -694,7 +706,7 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
   __shared__ uint64_t a_full[NA], a_empty[NA], b_full[NB], b_empty[NB], s_full[2], d_full[2], g_done[2];
   __shared__ TcShared sh;
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int k0 = blockIdx.x * kTcRows;
+  const int k0 = tile_by_work(blockIdx.x, gridDim.x, rows, T, false) * kTcRows;
   const int h = blockIdx.y;
   const int nqt = (rows + kTcQ - 1) / kTcQ;
   if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
