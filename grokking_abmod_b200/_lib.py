@@ -104,6 +104,10 @@ SIGNATURES = {
                                                    ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
                                                    ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
                                                    ctypes.c_void_p]),
+    "mb_gpt_checkpoint_write": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(GptConfigC), c_u32_p, ctypes.c_size_t,
+                                               c_float_p, ctypes.c_size_t]),
+    "mb_gpt_checkpoint_read": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(GptConfigC), c_u32_p, c_size_p,
+                                              c_float_p, c_size_p]),
     "mb_random_units": (ctypes.c_int, [ctypes.c_uint64, c_float_p, ctypes.c_size_t]),
     "mb_equation_dataset": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_double, ctypes.c_uint64,
                                            c_u32_p, c_u32_p, c_size_p, c_u32_p, c_size_p]),

@@ -14,7 +14,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libmeshb200.so")
 
 SOURCES = ["gpt_model.cu", "mesh_ops.cu", "gemm_tc.cu", "simple_model.cu", "config.cpp", "data.cpp",
-           "simple_config.cpp"]
+           "simple_config.cpp", "checkpoint.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -187,6 +187,20 @@ int mb_op_mesh_backward_noalloc(const float* x, const float* dy, float* dx, floa
                                 uint32_t width, uint32_t depth, uint32_t connectivity, const float* weights,
                                 void* stream);
 
+/* ---- checkpoints (src/gpt/checkpoint.rs:25-196) --------------------------
+ * MSHGPT07 (default architecture) / MSHGPT08 (butterfly connectivity) files:
+ * magic, config as LE u32, the tokenizer's characters as u32 code points,
+ * the parameters as LE f32, no trailing bytes.  Write from host arrays
+ * (parameters from mb_gpt_get_parameters); read with NULL arrays to query
+ * *n_characters / *n_parameters, then again with buffers.  Load into a model
+ * with mb_gpt_create + mb_gpt_set_parameters (which resets AdamW, as
+ * Checkpoint::load's callers do).  MSHGPT09 geometry ablations and table
+ * embeddings return MB_ERR_UNSUPPORTED. */
+int mb_gpt_checkpoint_write(const char* path, const mb_gpt_config* config, const uint32_t* characters,
+                            size_t n_characters, const float* parameters, size_t n_parameters);
+int mb_gpt_checkpoint_read(const char* path, mb_gpt_config* config, uint32_t* characters, size_t* n_characters,
+                           float* parameters, size_t* n_parameters);
+
 /* ---- seeded data (src/mesh.rs:256-288, src/gpt/grokking.rs:128-306) ---- */
 /* SplitMix64 Random::unit() draws (f32). */
 int mb_random_units(uint64_t seed, float* out, size_t count);
