@@ -85,8 +85,8 @@ struct BlockOps {
                             const float* wv, const float2* rope, float* dx, float* pq, float* pk, float* pv) = 0;
 };
 
-constexpr int kRptForward = 8;
-constexpr int kRptBackward = 4;
+constexpr int kRptForward = 4;
+constexpr int kRptBackward = 2;
 
 template <int W>
 struct BlockOpsW final : BlockOps {
