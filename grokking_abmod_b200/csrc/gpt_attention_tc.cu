@@ -34,7 +34,7 @@ namespace mb {
 
 constexpr int kTcRows = 128;     // CTA tile rows = TMEM lanes
 constexpr int kTcK = 64;         // key-tile rows (forward, dQ)
-constexpr int kTcQ = 32;         // query-tile rows (dK/dV)
+constexpr int kTcQ = 64;         // query-tile rows (dK/dV)
 constexpr int kTcThreads = 320;  // 8 compute warps + producer warp + MMA warp
 constexpr int kTcCompute = 256;  // compute threads: row = tid % 128, column half = tid / 128
 constexpr int kTcProducer = 256, kTcIssuer = 288;
@@ -651,28 +651,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ------------------------------------------------------------------- dK/dV
-// A CTA owns 128 keys of one head and walks the later queries 32 at a time.
-// Threads 0-255 compute (key row = tid % 128 = TMEM lane, half = tid / 128
-// takes query columns [16 half, 16 half + 16)), warp 8 streams the A ring
-// (Q, dO), warp 9 issues the MMAs, warp 10 streams the B ring (Q^T, dO^T,
-// LSE, delta).  K lives in TMEM, V in shared memory; S/dP and their P/dS
-// successors are double-buffered in TMEM, so the MMAs of query step j+1 run
-// while the compute warps turn step j's scores into P and dS.
-// TMEM: K hi | K lo | dV | dK (64 each) | buffer 0 | buffer 1, each buffer
-// S^T then P^T hi | dP^T then dS^T hi | P^T lo | dS^T lo (32 each).
-// Per query step: S^T = K Q^T, dP^T = V dO^T (keys on lanes); P^T, dS^T;
-// dV += P^T dO, dK += dS^T Q (B = dO^T / Q^T tiles).
+// A CTA owns 128 keys of one head and walks the later queries 64 at a time.
+// Threads 0-255 compute (key row = tid % 128 = TMEM lane; thread half
+// tid / 128 takes 16 of each 32-query half), warp 8 streams the A tile
+// (Q, dO), warp 9 issues the MMAs, warp 10 streams the B tile (Q^T, dO^T,
+// LSE, delta).  K lives in TMEM, V in shared memory.  Per query step:
+//   S^T = K Q^T and dP^T = V dO^T (keys on lanes, N = 64 queries);
+//   P^T and dS^T, produced in two 32-query halves: while the compute warps
+//   finish the second half, dV += P^T dO and dK += dS^T Q already run for the
+//   first (K steps 0-3 of the B tiles), then for the second (K steps 4-7).
+// TMEM: K hi | K lo | dV | dK | S^T then P^T hi | dP^T then dS^T hi | P^T lo
+// | dS^T lo (64 columns each).
 constexpr int kTcKvThreads = 352;
 constexpr int kKvProducerA = 256, kKvIssuer = 288, kKvProducerB = 320;
 
 template <int HD>
 struct TcKv {
   using F = TcFmt<HD>;
-  static constexpr int NA = 3, NB = 2;
   static constexpr int A_FLOATS = 4 * F::QPART;             // Q, Q', dO, dO'
   static constexpr int B_FLOATS = 4 * F::QPART + 2 * kTcQ;  // Q^T, Q^T', dO^T, dO^T', lse2, delta
   static constexpr int V_FLOATS = 2 * kTcRows * HD;         // V hi, V lo
-  static constexpr size_t smem = (size_t)(V_FLOATS + NA * A_FLOATS + NB * B_FLOATS) * sizeof(float);
+  static constexpr size_t smem = (size_t)(V_FLOATS + A_FLOATS + B_FLOATS) * sizeof(float);
 };
 
 // D (+)= A . B^T with A a K-major hi/lo shared tile [128 rows][KC columns].
@@ -697,13 +696,12 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
                                int* __restrict__ err) {
   using F = TcFmt<HD>;
   using S = TcKv<HD>;
-  constexpr int NA = S::NA, NB = S::NB;
   extern __shared__ __align__(128) float sm[];
   float* Vh = sm;
   float* Vl = sm + kTcRows * HD;
-  float* ring_a = sm + S::V_FLOATS;
-  float* ring_b = ring_a + NA * S::A_FLOATS;
-  __shared__ uint64_t a_full[NA], a_empty[NA], b_full[NB], b_empty[NB], s_full[2], d_full[2], g_done[2];
+  float* tile_a = sm + S::V_FLOATS;
+  float* tile_b = tile_a + S::A_FLOATS;
+  __shared__ uint64_t a_full, a_empty, b_full, b_empty, s_full, d_full[2], g_done;
   __shared__ TcShared sh;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int k0 = tile_by_work(blockIdx.x, gridDim.x, rows, T, false) * kTcRows;
@@ -711,19 +709,14 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
   const int nqt = (rows + kTcQ - 1) / kTcQ;
   if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
   if (tid == 0) {
-    for (int i = 0; i < NA; ++i) {
-      tc::bar_init(&a_full[i], 1);
-      tc::bar_init(&a_empty[i], 1);
-    }
-    for (int i = 0; i < NB; ++i) {
-      tc::bar_init(&b_full[i], 1);
-      tc::bar_init(&b_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      tc::bar_init(&s_full[i], 1);
-      tc::bar_init(&d_full[i], kTcCompute);
-      tc::bar_init(&g_done[i], 1);
-    }
+    tc::bar_init(&a_full, 1);
+    tc::bar_init(&a_empty, 1);
+    tc::bar_init(&b_full, 1);
+    tc::bar_init(&b_empty, 1);
+    tc::bar_init(&s_full, 1);
+    tc::bar_init(&d_full[0], kTcCompute);
+    tc::bar_init(&d_full[1], kTcCompute);
+    tc::bar_init(&g_done, 1);
     tc::bar_init_fence();
     sh.failed = 0;
   }
@@ -731,21 +724,18 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t t0 = sh.tmem_base;
-  const uint32_t tKh = t0, tKl = t0 + 64, tdV = t0 + 128, tdK = t0 + 192;
-  auto tS = [&](int b) { return t0 + 256 + 128 * b; };
-  auto tP = [&](int b) { return t0 + 256 + 128 * b + 32; };
-  auto tPl = [&](int b) { return t0 + 256 + 128 * b + 64; };
-  auto tSl = [&](int b) { return t0 + 256 + 128 * b + 96; };
+  const uint32_t tKh = t0, tKl = t0 + 64, tdV = t0 + 128, tdK = t0 + 192, tS = t0 + 256, tP = t0 + 320,
+                 tPl = t0 + 384, tSl = t0 + 448;
   const int last = min(rows, k0 + kTcRows) - 1;
   const int qend = min(rows, (last / T + 1) * T);
   const int n = (qend - k0 + kTcQ - 1) / kTcQ;
   const int qt0 = k0 / kTcQ;
-  // K through the (still idle) A ring into TMEM.
-  stage_rows<HD>(ring_a, k, k0, rows, W, h, kTcKvThreads);
+  // K through the (still idle) A tile into TMEM.
+  stage_rows<HD>(tile_a, k, k0, rows, W, h, kTcKvThreads);
   __syncthreads();
   if (warp < 4) {
     const uint32_t lane = (uint32_t)(warp * 32) << 16;
-    staged_row_to_tmem<HD>(ring_a, tid, tKh + lane, tKl + lane);
+    staged_row_to_tmem<HD>(tile_a, tid, tKh + lane, tKl + lane);
     tc::tmem_st_wait();
   }
   if (tid < kTcCompute) {
@@ -762,11 +752,11 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
       const int i = tid + kTcCompute * j, r = i / (HD / 4), c = (i % (HD / 4)) * 4;
-      const float4 h = make_float4(tc::tf32_hi(x[j].x), tc::tf32_hi(x[j].y), tc::tf32_hi(x[j].z),
-                                   tc::tf32_hi(x[j].w));
-      *reinterpret_cast<float4*>(Vh + tc::blk(r, c, HD)) = h;
+      const float4 hv = make_float4(tc::tf32_hi(x[j].x), tc::tf32_hi(x[j].y), tc::tf32_hi(x[j].z),
+                                    tc::tf32_hi(x[j].w));
+      *reinterpret_cast<float4*>(Vh + tc::blk(r, c, HD)) = hv;
       *reinterpret_cast<float4*>(Vl + tc::blk(r, c, HD)) =
-          make_float4(x[j].x - h.x, x[j].y - h.y, x[j].z - h.z, x[j].w - h.w);
+          make_float4(x[j].x - hv.x, x[j].y - hv.y, x[j].z - hv.z, x[j].w - hv.w);
     }
   }
   tc::fence_async_smem();
@@ -781,40 +771,46 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
     const float scale2 = scale * 1.4426950408889634f;
     const int kr = k0 + row;
     const int ke = (kr / T + 1) * T;  // end of the key's sequence
-    // Every key row of the CTA in one sequence, so query steps wholly above
+    // Every key row of the CTA in one sequence, so query halves wholly above
     // the diagonal and inside the sequence need no mask.
     const int kseq_end = (k0 / T + 1) * T;
     const bool one_seq = (k0 + kTcRows - 1) / T == k0 / T && k0 + kTcRows <= rows;
+    const float* Ls0 = tile_b + 4 * F::QPART;  // lse2 of the query step
+    const float* Es0 = Ls0 + kTcQ;             // delta of the query step
     bool done = false;
     for (int j = 0; j < n; ++j) {
-      const int b = j & 1, sb = j % NB;
-      TC_WAIT_OR_FAIL(&s_full[b], (j >> 1) & 1);
-      TC_WAIT_OR_FAIL(&b_full[sb], (j / NB) & 1);
+      TC_WAIT_OR_FAIL(&s_full, j & 1);
+      TC_WAIT_OR_FAIL(&b_full, j & 1);
       tc::fence_after_sync();
-      const float* Ls = ring_b + sb * S::B_FLOATS + 4 * F::QPART + 16 * half;  // lse2 of the query step
-      const float* Es = Ls + kTcQ;                                              // delta of the query step
-      float s[16], dp[16];
-      tc::tmem_ld16(tS(b) + 16 * half + lane, s);
-      tc::tmem_ld16(tP(b) + 16 * half + lane, dp);
-      const int qt = k0 + j * kTcQ;
-      const bool full = one_seq && qt >= k0 + kTcRows - 1 && qt + kTcQ <= min(kseq_end, rows);
-      const int qh = qt + 16 * half;
+      for (int q2 = 0; q2 < 2; ++q2) {
+        // Columns [32 q2 + 16 half, +16) of this query step.
+        const int col = 32 * q2 + 16 * half;
+        const float* Ls = Ls0 + col;
+        const float* Es = Es0 + col;
+        float s[16], dp[16];
+        tc::tmem_ld16(tS + col + lane, s);
+        tc::tmem_ld16(tP + col + lane, dp);
+        const int qh = k0 + j * kTcQ + col;
+        const bool full = one_seq && k0 + j * kTcQ + 32 * q2 >= k0 + kTcRows - 1 &&
+                          k0 + j * kTcQ + 32 * q2 + 32 <= min(kseq_end, rows);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const int qj = qh + c;
-        const bool ok = full || (qj >= kr && qj < ke && qj < rows && kr < rows);
-        const float p = ok ? ex2(fmaf(s[c], scale2, -Ls[c])) : 0.f;
-        s[c] = p;
-        dp[c] = p * (dp[c] - Es[c]) * scale;
+        for (int c = 0; c < 16; ++c) {
+          const int qj = qh + c;
+          const bool ok = full || (qj >= kr && qj < ke && qj < rows && kr < rows);
+          const float p = ok ? ex2(fmaf(s[c], scale2, -Ls[c])) : 0.f;
+          s[c] = p;
+          dp[c] = p * (dp[c] - Es[c]) * scale;
+        }
+        tc_st_split<16>(tS + col + lane, tPl + col + lane, s);   // P^T hi over S^T
+        tc_st_split<16>(tP + col + lane, tSl + col + lane, dp);  // dS^T hi over dP^T
+        tc::tmem_st_wait();
+        tc::fence_before_sync();
+        tc::bar_arrive(&d_full[q2]);
       }
-      tc_st_split<16>(tS(b) + 16 * half + lane, tPl(b) + 16 * half + lane, s);   // P^T hi over S^T
-      tc_st_split<16>(tP(b) + 16 * half + lane, tSl(b) + 16 * half + lane, dp);  // dS^T hi over dP^T
-      tc::tmem_st_wait();
-      tc::fence_before_sync();
-      tc::bar_arrive(&d_full[b]);
+      // The next step's S^T / dP^T overwrite these columns: wait for dV/dK.
+      TC_WAIT_OR_FAIL(&g_done, j & 1);
       if (j + 1 == n) done = true;
     }
-    if (done && !tc::bar_wait(&g_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
     tc::fence_after_sync();
     if (done && !sh.failed) {
       const bool in = kr < rows;
@@ -835,56 +831,50 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
       }
     }
   } else if (tid == kKvProducerA) {
-    // ---------------------------------------------------------- A ring: Q, dO
+    // ---------------------------------------------------------- A tile: Q, dO
     for (int j = 0; j < n; ++j) {
-      const int st = j % NA;
-      if (j >= NA) {
-        TC_WAIT_OR_FAIL(&a_empty[st], ((j - NA) / NA) & 1);
+      if (j >= 1) {
+        TC_WAIT_OR_FAIL(&a_empty, (j - 1) & 1);
       }
-      tc::bar_expect_tx(&a_full[st], S::A_FLOATS * 4);
-      tc::bulk_g2s(ring_a + st * S::A_FLOATS, qfmt + ((size_t)h * nqt + qt0 + j) * F::QTILE, S::A_FLOATS * 4,
-                   &a_full[st]);
+      tc::bar_expect_tx(&a_full, S::A_FLOATS * 4);
+      tc::bulk_g2s(tile_a, qfmt + ((size_t)h * nqt + qt0 + j) * F::QTILE, S::A_FLOATS * 4, &a_full);
     }
   } else if (tid == kKvProducerB) {
-    // ---------------------------------------------------------- B ring: Q^T, dO^T, lse2, delta
+    // ---------------------------------------------------------- B tile: Q^T, dO^T, lse2, delta
     for (int j = 0; j < n; ++j) {
-      const int st = j % NB;
-      if (j >= NB) {
-        TC_WAIT_OR_FAIL(&b_empty[st], ((j - NB) / NB) & 1);
+      if (j >= 1) {
+        TC_WAIT_OR_FAIL(&b_empty, (j - 1) & 1);
       }
-      tc::bar_expect_tx(&b_full[st], S::B_FLOATS * 4);
-      tc::bulk_g2s(ring_b + st * S::B_FLOATS, qfmt + ((size_t)h * nqt + qt0 + j) * F::QTILE + 4 * F::QPART,
-                   S::B_FLOATS * 4, &b_full[st]);
+      tc::bar_expect_tx(&b_full, S::B_FLOATS * 4);
+      tc::bulk_g2s(tile_b, qfmt + ((size_t)h * nqt + qt0 + j) * F::QTILE + 4 * F::QPART, S::B_FLOATS * 4,
+                   &b_full);
     }
   } else if (tid == kKvIssuer) {
     // ---------------------------------------------------------- MMA issuer
     constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcQ, false, false);
     constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
-    for (int j = 0; j <= n; ++j) {
-      if (j < n) {
-        const int sa = j % NA, b = j & 1;
-        TC_WAIT_OR_FAIL(&a_full[sa], (j / NA) & 1);
-        if (j >= 2) {
-          TC_WAIT_OR_FAIL(&g_done[b], ((j - 2) >> 1) & 1);  // dV/dK of step j-2 have read buffer b
-        }
-        tc::fence_after_sync();
-        const float* A = ring_a + sa * S::A_FLOATS;
-        mma_tmem_a<HD>(tS(b), tKh, tKl, A + F::Q_HI * F::QPART, A + F::Q_LO * F::QPART, idS, false);  // S^T
-        mma_smem_a<HD>(tP(b), Vh, Vl, A + F::D_HI * F::QPART, A + F::D_LO * F::QPART, idS, false);    // dP^T
-        tc::commit(&s_full[b]);
-        tc::commit(&a_empty[sa]);
-      }
+    for (int j = 0; j < n; ++j) {
+      TC_WAIT_OR_FAIL(&a_full, j & 1);
       if (j >= 1) {
-        const int pj = j - 1, sb = pj % NB, pb = pj & 1;
-        TC_WAIT_OR_FAIL(&b_full[sb], (pj / NB) & 1);
-        TC_WAIT_OR_FAIL(&d_full[pb], (pj >> 1) & 1);
-        tc::fence_after_sync();
-        const float* B = ring_b + sb * S::B_FLOATS;  // Q^T, Q^T', dO^T, dO^T'
-        mma_tmem_a<kTcQ>(tdV, tS(pb), tPl(pb), B + 2 * F::QPART, B + 3 * F::QPART, idG, pj > 0);  // dV += P^T dO
-        mma_tmem_a<kTcQ>(tdK, tP(pb), tSl(pb), B, B + F::QPART, idG, pj > 0);                     // dK += dS^T Q
-        tc::commit(&g_done[pb]);
-        tc::commit(&b_empty[sb]);
+        TC_WAIT_OR_FAIL(&g_done, (j - 1) & 1);  // dV/dK of step j-1 have read P^T / dS^T
       }
+      tc::fence_after_sync();
+      mma_tmem_a<HD>(tS, tKh, tKl, tile_a + F::Q_HI * F::QPART, tile_a + F::Q_LO * F::QPART, idS, false);  // S^T
+      mma_smem_a<HD>(tP, Vh, Vl, tile_a + F::D_HI * F::QPART, tile_a + F::D_LO * F::QPART, idS, false);    // dP^T
+      tc::commit(&s_full);
+      tc::commit(&a_empty);
+      TC_WAIT_OR_FAIL(&b_full, j & 1);
+      const float* qt = tile_b;                   // Q^T, Q^T'
+      const float* dot = tile_b + 2 * F::QPART;   // dO^T, dO^T'
+      for (int q2 = 0; q2 < 2; ++q2) {
+        TC_WAIT_OR_FAIL(&d_full[q2], j & 1);
+        tc::fence_after_sync();
+        // dV += P^T dO, dK += dS^T Q over queries [32 q2, 32 q2 + 32) (K steps 4 q2 .. 4 q2 + 3)
+        mma_tmem_a_steps<kTcQ, 4>(tdV, tS, tPl, dot, dot + F::QPART, idG, j > 0 || q2 > 0, 4 * q2);
+        mma_tmem_a_steps<kTcQ, 4>(tdK, tP, tSl, qt, qt + F::QPART, idG, j > 0 || q2 > 0, 4 * q2);
+      }
+      tc::commit(&g_done);
+      tc::commit(&b_empty);
     }
   }
   tc::fence_before_sync();
