@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   using F = TcFmt<HD>;
   constexpr int NS = A::DQ_STAGES;
   extern __shared__ __align__(128) float sm[];
-  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full, d_full, q_done;
+  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full, d_full[2], q_done;
   __shared__ TcShared sh;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int nt = (rows + kTcRows - 1) / kTcRows;
@@ -537,7 +537,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::bar_init(&kv_empty[b], 1);
     }
     tc::bar_init(&s_full, 1);
-    tc::bar_init(&d_full, kTcCompute);
+    tc::bar_init(&d_full[0], kTcCompute);
+    tc::bar_init(&d_full[1], kTcCompute);
     tc::bar_init(&q_done, 1);
     tc::bar_init_fence();
     sh.failed = 0;
@@ -577,23 +578,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int j = 0; j < n; ++j) {
       TC_WAIT_OR_FAIL(&s_full, j & 1);
       tc::fence_after_sync();
-      float s[32], dp[32];
-      tc::tmem_ld32(tS + 32 * half + lane, s);
-      tc::tmem_ld32(tP + 32 * half + lane, dp);
       const int kt = kbeg + j * kTcK;
-      const bool full = one_seq && kt >= seq0 && kt + kTcK - 1 <= q0;
-      const int kh = kt + 32 * half;
+      // Key columns [32 k2 + 16 half, +16): the first 32 keys are handed to
+      // the MMA thread (dQ += dS K) while the second 32 are computed.
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int col = 32 * k2 + 16 * half;
+        float s[16], dp[16];
+        tc::tmem_ld16(tS + col + lane, s);
+        tc::tmem_ld16(tP + col + lane, dp);
+        const bool full = one_seq && kt + 32 * k2 >= seq0 && kt + 32 * k2 + 31 <= q0;
+        const int kh = kt + col;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int kr = kh + c;
-        const bool ok = full || (kr <= qr && kr >= qs && kr < rows);
-        const float p = ok ? ex2(fmaf(s[c], scale2, -L)) : 0.f;
-        s[c] = p * (dp[c] - dl) * scale;
+        for (int c = 0; c < 16; ++c) {
+          const int kr = kh + c;
+          const bool ok = full || (kr <= qr && kr >= qs && kr < rows);
+          const float p = ok ? ex2(fmaf(s[c], scale2, -L)) : 0.f;
+          s[c] = p * (dp[c] - dl) * scale;
+        }
+        tc_st_split<16>(tS + col + lane, tSl + col + lane, s);  // dS hi over S
+        tc::tmem_st_wait();
+        tc::fence_before_sync();
+        tc::bar_arrive(&d_full[k2]);
       }
-      tc_st_split<32>(tS + 32 * half + lane, tSl + 32 * half + lane, s);  // dS hi over S
-      tc::tmem_st_wait();
-      tc::fence_before_sync();
-      tc::bar_arrive(&d_full);
       if (j + 1 == n) done = true;
     }
     if (done && !tc::bar_wait(&q_done, (n - 1) & 1)) sh.failed = 1;
@@ -637,9 +643,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mma_tmem_a<HD>(tS, tQh, tQl, stage, stage + F::KPART, idS, false);                     // S  = Q K^T
       mma_tmem_a<HD>(tP, tDh, tDl, stage + 2 * F::KPART, stage + 3 * F::KPART, idS, false);  // dP = dO V^T
       tc::commit(&s_full);
-      TC_WAIT_OR_FAIL(&d_full, j & 1);
-      tc::fence_after_sync();
-      mma_tmem_a<kTcK>(tG, tS, tSl, stage + 4 * F::KPART, stage + 5 * F::KPART, idG, j > 0);  // dQ += dS K
+      bool ok = true;
+      for (int k2 = 0; k2 < 2 && ok; ++k2) {
+        ok = tc::bar_wait(&d_full[k2], j & 1);
+        tc::fence_after_sync();
+        // dQ += dS K over keys [32 k2, 32 k2 + 32) (K steps 4 k2 .. 4 k2 + 3)
+        if (ok)
+          mma_tmem_a_steps<kTcK, 4>(tG, tS, tSl, stage + 4 * F::KPART, stage + 5 * F::KPART, idG,
+                                    j > 0 || k2 > 0, 4 * k2);
+      }
+      if (!ok) {
+        sh.failed = 1;
+        break;
+      }
       tc::commit(&q_done);
       tc::commit(&kv_empty[st]);
     }
