@@ -58,105 +58,80 @@ __global__ void embedding_backward(int W, int V, int depth, int connectivity, in
   }
 }
 
-// ---- fused head: final RMSNorm, logits = n E^T, cross-entropy, dlogits,
-// dn = dlogits E and the RMSNorm adjoint -> dx.  One CTA handles HR rows with
-// one warp per row for the row reductions.
-constexpr int kHeadRows = 16;
-constexpr int kHeadThreads = 256;
+// ---- the head as row kernels around two tensor-core GEMMs (gemm_tc.cu):
+// head_norm (final RMSNorm), logits = nf E^T, head_loss (cross-entropy and
+// dlogits), dn = dlogits E, head_norm_backward (the RMSNorm adjoint -> dx).
+// One warp per row.
+constexpr int kHeadWarps = 8;
 
-__global__ void __launch_bounds__(kHeadThreads)
-    head_forward_backward(int rows, int W, int V, const float* __restrict__ x, const float* __restrict__ E,
-                          const float* __restrict__ Et, const uint32_t* __restrict__ targets,
-                          const float* __restrict__ supervised, float* __restrict__ logits_out,
-                          float* __restrict__ nf_out, float* __restrict__ dlogits_out,
-                          float* __restrict__ loss_rows, float* __restrict__ dx_out) {
-  extern __shared__ float sm[];
-  float* n = sm;                        // [HR][W]
-  float* dn = n + kHeadRows * W;        // [HR][W]
-  float* lg = dn + kHeadRows * W;       // [HR][V]
-  float* inv = lg + kHeadRows * V;      // [HR]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r0 = blockIdx.x * kHeadRows;
-  // targets == nullptr: inference, logits only.
-  const float sup = targets != nullptr ? *supervised : 1.0f;
-  // 1. RMSNorm (heads = 1)
-  for (int rr = warp; rr < kHeadRows; rr += kHeadThreads / 32) {
-    const int r = r0 + rr;
-    float s = 0.f;
-    for (int ch = lane; ch < W; ch += 32) {
-      float v = r < rows ? x[(size_t)r * W + ch] : 0.f;
-      n[rr * W + ch] = v;
-      s += v * v;
-    }
-    s = group_sum<32>(s);
-    float iv = 1.0f / sqrtf(s / (float)W + kRmsEpsilon);
-    if (lane == 0) inv[rr] = iv;
-    for (int ch = lane; ch < W; ch += 32) {
-      float v = n[rr * W + ch] * iv;
-      n[rr * W + ch] = v;
-      if (r < rows && nf_out != nullptr) nf_out[(size_t)r * W + ch] = v;
-    }
+__global__ void __launch_bounds__(kHeadWarps * 32)
+    head_norm(int rows, int W, const float* __restrict__ x, float* __restrict__ nf, float* __restrict__ inv_out) {
+  const int lane = threadIdx.x & 31, r = blockIdx.x * kHeadWarps + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float* xr = x + (size_t)r * W;
+  float s = 0.f;
+  for (int ch = lane * 4; ch < W; ch += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + ch);
+    s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
-  __syncthreads();
-  // 2. logits
-  for (int i = threadIdx.x; i < kHeadRows * V; i += kHeadThreads) {
-    const int rr = i / V, t = i % V;
-    const float* nr = n + rr * W;
-    float acc = 0.f;
-    for (int ch = 0; ch < W; ++ch) acc += nr[ch] * __ldg(Et + (size_t)ch * V + t);
-    lg[i] = acc;
-    if (logits_out != nullptr && r0 + rr < rows) logits_out[(size_t)(r0 + rr) * V + t] = acc;
+  s = group_sum<32>(s);
+  const float iv = 1.0f / sqrtf(s / (float)W + kRmsEpsilon);
+  if (lane == 0) inv_out[r] = iv;
+  for (int ch = lane * 4; ch < W; ch += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + ch);
+    *reinterpret_cast<float4*>(nf + (size_t)r * W + ch) = make_float4(v.x * iv, v.y * iv, v.z * iv, v.w * iv);
   }
-  if (targets == nullptr) return;
-  __syncthreads();
-  // 3. cross-entropy per row (src/gpt/gpu.rs:955-994)
-  for (int rr = warp; rr < kHeadRows; rr += kHeadThreads / 32) {
-    const int r = r0 + rr;
-    float* l = lg + rr * V;
-    const uint32_t tg = r < rows ? targets[r] : kIgnoreTarget;
-    if (tg == kIgnoreTarget) {
-      for (int t = lane; t < V; t += 32) l[t] = 0.f;
-      if (lane == 0 && r < rows) loss_rows[r] = 0.f;
-    } else {
-      float m = -INFINITY;
-      for (int t = lane; t < V; t += 32) m = fmaxf(m, l[t]);
+}
+
+// Cross-entropy per row (src/gpt/gpu.rs:955-994): loss_rows and
+// dlogits = (softmax - onehot) / supervised; ignored rows get zeros.
+__global__ void __launch_bounds__(kHeadWarps * 32)
+    head_loss(int rows, int V, const float* __restrict__ logits, const uint32_t* __restrict__ targets,
+              const float* __restrict__ supervised, float* __restrict__ loss_rows, float* __restrict__ dlogits) {
+  const int lane = threadIdx.x & 31, r = blockIdx.x * kHeadWarps + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float* l = logits + (size_t)r * V;
+  float* d = dlogits + (size_t)r * V;
+  const uint32_t tg = targets[r];
+  if (tg == kIgnoreTarget) {
+    for (int t = lane; t < V; t += 32) d[t] = 0.f;
+    if (lane == 0) loss_rows[r] = 0.f;
+    return;
+  }
+  const float sup = *supervised;
+  float m = -INFINITY;
+  for (int t = lane; t < V; t += 32) m = fmaxf(m, l[t]);
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      float s = 0.f;
-      for (int t = lane; t < V; t += 32) s += expf(l[t] - m);
-      s = group_sum<32>(s);
-      const float lt = l[tg < (uint32_t)V ? tg : 0];
-      __syncwarp();
-      if (lane == 0) loss_rows[r] = logf(s) + m - lt;
-      for (int t = lane; t < V; t += 32) {
-        float p = expf(l[t] - m) / s;
-        l[t] = (p - (t == (int)tg ? 1.0f : 0.0f)) / sup;
-      }
-    }
-    __syncwarp();
-    if (r < rows)
-      for (int t = lane; t < V; t += 32) dlogits_out[(size_t)r * V + t] = l[t];
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float s = 0.f;
+  for (int t = lane; t < V; t += 32) s += expf(l[t] - m);
+  s = group_sum<32>(s);
+  if (lane == 0) loss_rows[r] = logf(s) + m - l[tg < (uint32_t)V ? tg : 0];
+  for (int t = lane; t < V; t += 32) {
+    const float p = expf(l[t] - m) / s;
+    d[t] = (p - (t == (int)tg ? 1.0f : 0.0f)) / sup;
   }
-  __syncthreads();
-  // 4. dn = dlogits E
-  for (int i = threadIdx.x; i < kHeadRows * W; i += kHeadThreads) {
-    const int rr = i / W, ch = i % W;
-    const float* l = lg + rr * V;
-    float acc = 0.f;
-    for (int t = 0; t < V; ++t) acc += l[t] * __ldg(E + (size_t)t * W + ch);
-    dn[i] = acc;
+}
+
+// dx = inv (dn - n mean(dn n)), the RMSNorm adjoint of the final norm.
+__global__ void __launch_bounds__(kHeadWarps * 32)
+    head_norm_backward(int rows, int W, const float* __restrict__ nf, const float* __restrict__ inv,
+                       const float* __restrict__ dn, float* __restrict__ dx) {
+  const int lane = threadIdx.x & 31, r = blockIdx.x * kHeadWarps + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const float* nr = nf + (size_t)r * W;
+  const float* gr = dn + (size_t)r * W;
+  float s = 0.f;
+  for (int ch = lane * 4; ch < W; ch += 128) {
+    const float4 n = *reinterpret_cast<const float4*>(nr + ch), g = *reinterpret_cast<const float4*>(gr + ch);
+    s += g.x * n.x + g.y * n.y + g.z * n.z + g.w * n.w;
   }
-  __syncthreads();
-  // 5. RMSNorm adjoint
-  for (int rr = warp; rr < kHeadRows; rr += kHeadThreads / 32) {
-    const int r = r0 + rr;
-    if (r >= rows) continue;
-    float s = 0.f;
-    for (int ch = lane; ch < W; ch += 32) s += dn[rr * W + ch] * n[rr * W + ch];
-    s = group_sum<32>(s) / (float)W;
-    const float iv = inv[rr];
-    for (int ch = lane; ch < W; ch += 32)
-      dx_out[(size_t)r * W + ch] = iv * (dn[rr * W + ch] - n[rr * W + ch] * s);
+  s = group_sum<32>(s) / (float)W;
+  const float iv = inv[r];
+  for (int ch = lane * 4; ch < W; ch += 128) {
+    const float4 n = *reinterpret_cast<const float4*>(nr + ch), g = *reinterpret_cast<const float4*>(gr + ch);
+    *reinterpret_cast<float4*>(dx + (size_t)r * W + ch) =
+        make_float4(iv * (g.x - n.x * s), iv * (g.y - n.y * s), iv * (g.z - n.z * s), iv * (g.w - n.w * s));
   }
 }
 

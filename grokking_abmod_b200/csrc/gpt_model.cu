@@ -28,6 +28,7 @@
 #include <mutex>
 #include <string>
 
+#include "gemm_tc.h"
 #include "host.h"
 
 #include "gpt_attention.cu"
@@ -154,6 +155,9 @@ struct AttentionOps {
   // Device scratch (floats) the kernels need for `rows` token rows; the model
   // allocates it per workspace and sets `scratch` before enqueueing.
   virtual size_t scratch_floats(int rows, int H) const { return 0; }
+  // Kernel launches of one forward / one backward (dK/dV + dQ) call.
+  virtual int forward_launches() const { return 1; }
+  virtual int backward_launches() const { return 2; }
   float* scratch = nullptr;
   virtual void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                        const float* v, float* o, float* lse) = 0;
@@ -214,6 +218,8 @@ struct AttentionOpsTc final : AttentionOps {
   static size_t key_floats(int rows, int H) { return (size_t)H * ((rows + kTcK - 1) / kTcK) * F::KTILE; }
   static size_t query_floats(int rows, int H) { return (size_t)H * ((rows + kTcQ - 1) / kTcQ) * F::QTILE; }
   size_t scratch_floats(int rows, int H) const override { return key_floats(rows, H) + query_floats(rows, H); }
+  int forward_launches() const override { return 2; }   // key format + forward
+  int backward_launches() const override { return 4; }  // query format + dK/dV, key format + dQ
   float* kfmt() const { return scratch; }
   float* qfmt(int rows, int H) const { return scratch + key_floats(rows, H); }
   // Writes the key-tile parts (bit mask over TcFmt's hi parts) the next kernel reads.
@@ -298,6 +304,7 @@ struct Workspace {
   std::vector<float*> x;  // L + 1
   std::vector<float*> q, k, v, o, xm, lse;
   float *nf, *dlog, *logits, *loss_rows, *g, *dO, *dvx, *dxm, *delta, *dq, *dk, *dv, *emb_partial, *dE;
+  float *head_inv, *head_dn;  // final RMSNorm's 1/rms per row and the head's dn = dlogits E
   float* emb_mesh_partial;
   float* att_scratch;
   float2* rope;
@@ -340,9 +347,7 @@ class GptModel {
     tc_err_ = mem_.alloc<int>(1);
     MB_CUDA(cudaMemset(tc_err_, 0, sizeof(int)));
     attention_ = make_attention_ops(cfg.width / cfg.heads, tc_err_);
-    head_smem_ = (size_t)(2 * kHeadRows * cfg.width + kHeadRows * cfg.vocab_size + kHeadRows) * sizeof(float);
-    MB_CUDA(cudaFuncSetAttribute(&head_forward_backward, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)head_smem_));
+    gemm_prepare();
     const size_t P = layout_.count();
     w_ = mem_.alloc<float>(P);
     m_ = mem_.alloc<float>(P);
@@ -529,10 +534,13 @@ class GptModel {
   }
 
   size_t step_launches() const {
-    // count + embedding fwd + 3 per block fwd + head + loss + 4 per block bwd
-    // (attention backward is two kernels) + embedding partials + 2 reduces +
-    // embedding bwd + optimizer advance + AdamW
-    return 1 + 1 + 3 * (size_t)cfg_.layers + 1 + 1 + 4 * (size_t)cfg_.layers + 1 + 2 + 1 + 2;
+    // count + embedding fwd + per block (qkv, attention, post) forward + head
+    // (norm, GEMM, loss, GEMM, norm adjoint) + loss + per block (post,
+    // attention, qkv) backward + embedding partials + 2 reduces + embedding
+    // bwd + optimizer advance + AdamW
+    const size_t L = cfg_.layers;
+    return 1 + 1 + L * (2 + attention_->forward_launches()) + 5 + 1 + L * (2 + attention_->backward_launches()) + 1 +
+           2 + 1 + 2;
   }
 
   // ---- data parallelism
@@ -607,6 +615,8 @@ class GptModel {
     ws->nf = a.alloc<float>(NW);
     ws->dlog = a.alloc<float>((size_t)rows * V);
     ws->logits = a.alloc<float>((size_t)rows * V);
+    ws->head_inv = a.alloc<float>(rows);
+    ws->head_dn = a.alloc<float>((size_t)rows * W);
     ws->loss_rows = a.alloc<float>(rows);
     ws->g = a.alloc<float>(NW);
     ws->dO = a.alloc<float>(NW);
@@ -708,10 +718,19 @@ class GptModel {
       blocks_->post_forward(stream_, ws.grid_pf, d, ws.o[b], ws.v[b], ws.x[b], group(bg.projection), group(bg.ffn),
                             ws.xm[b], ws.x[b + 1]);
     }
+    // Head: final RMSNorm, logits = nf E^T on the tensor cores; in training
+    // also the cross-entropy, dn = dlogits E and the RMSNorm adjoint into g.
     mark("head_forward_backward");
-    head_forward_backward<<<(ws.rows + kHeadRows - 1) / kHeadRows, kHeadThreads, head_smem_, stream_>>>(
-        ws.rows, W, V, ws.x[L], final_embedding(), et_, with_targets ? ws.targets : nullptr, ws.supervised,
-        with_targets ? nullptr : ws.logits, ws.nf, ws.dlog, ws.loss_rows, ws.g);
+    const int hgrid = (ws.rows + kHeadWarps - 1) / kHeadWarps;
+    const float* E = final_embedding();
+    head_norm<<<hgrid, kHeadWarps * 32, 0, stream_>>>(ws.rows, W, ws.x[L], ws.nf, ws.head_inv);
+    launch_gemm({ws.nf, W, false}, {E, W, false}, ws.logits, V, ws.rows, V, W, 0, nullptr, tc_err_, stream_);
+    if (with_targets) {
+      head_loss<<<hgrid, kHeadWarps * 32, 0, stream_>>>(ws.rows, V, ws.logits, ws.targets, ws.supervised,
+                                                          ws.loss_rows, ws.dlog);
+      launch_gemm({ws.dlog, V, false}, {E, W, true}, ws.head_dn, W, ws.rows, W, V, 0, nullptr, tc_err_, stream_);
+      head_norm_backward<<<hgrid, kHeadWarps * 32, 0, stream_>>>(ws.rows, W, ws.nf, ws.head_inv, ws.head_dn, ws.g);
+    }
     MB_CUDA(cudaGetLastError());
   }
 
@@ -822,7 +841,6 @@ class GptModel {
 
   mb_gpt_config cfg_;
   int device_ = 0, sms_ = 1;
-  size_t head_smem_ = 0;
   Layout layout_;
   cudaStream_t stream_ = nullptr;
   DeviceArena mem_;
