@@ -56,9 +56,6 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
   int phase = 0;
   const int hp = d.head_width / 2;
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
-  const float4* wgs[3] = {reinterpret_cast<const float4*>(wq), reinterpret_cast<const float4*>(wk),
-                          reinterpret_cast<const float4*>(wv)};
-  float* outs[3] = {q_out, k_out, v_out};
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     float2 n[RPT];
     float inv[RPT];
@@ -80,10 +77,13 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
     }
     rmsnorm_rows<T>(c, n, inv, red, phase, W);
     for (int m = 0; m < 3; ++m) {
+      // Selected, not indexed: a pointer array indexed by m would live in local memory.
+      const float4* wg = reinterpret_cast<const float4*>(m == 0 ? wq : (m == 1 ? wk : wv));
+      float* out = m == 0 ? q_out : (m == 1 ? k_out : v_out);
       float2 a[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = n[k];
-      mesh_forward<W, T>(c, d, a, wgs[m], d.attn_depth, bufs, false);
+      mesh_forward<W, T>(c, d, a, wg, d.attn_depth, bufs, false);
 #pragma unroll
       for (int k = 0; k < RPT; ++k) {
         const int r = tile * T::TR + c.row(k);
@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
           head_rmsnorm(v, hp);
           v = rope_pair(v, c.cp, hp, r % d.sequence, rope_cs, false);
         }
-        st2(outs[m], r, d.rows, W, c.cp, v);
+        st2(out, r, d.rows, W, c.cp, v);
       }
       __syncthreads();
     }
@@ -274,9 +274,6 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
   int phase = 0;
   const int hp = d.head_width / 2;
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
-  const float4* wgs[3] = {reinterpret_cast<const float4*>(wq), reinterpret_cast<const float4*>(wk),
-                          reinterpret_cast<const float4*>(wv)};
-  const float* grads[3] = {dq, dk, dv};
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     float2 n1[RPT], dn[RPT];
     float inv1[RPT];
@@ -287,16 +284,18 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
     }
     rmsnorm_rows<T>(c, n1, inv1, red, phase, W);
     for (int m = 0; m < 3; ++m) {
+      const float4* wg = reinterpret_cast<const float4*>(m == 0 ? wq : (m == 1 ? wk : wv));
+      const float* grad = m == 0 ? dq : (m == 1 ? dk : dv);
       float2 a[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = n1[k];
       __syncthreads();  // the previous mesh backward may still read bufs
-      mesh_forward<W, T>(c, d, a, wgs[m], A, bufs, true);
+      mesh_forward<W, T>(c, d, a, wg, A, bufs, true);
       float2 gm[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) {
         const int r = tile * T::TR + c.row(k);
-        float2 gg = ld2<T>(grads[m], r, d.rows, W, c.cp);
+        float2 gg = ld2<T>(grad, r, d.rows, W, c.cp);
         if (m < 2) {
           // QK-Norm then RoPE in forward; backward: inverse RoPE, then the
           // per-head RMSNorm adjoint.
@@ -308,7 +307,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
         }
         gm[k] = gg;
       }
-      mesh_backward<W, T>(c, d, gm, wgs[m], A, bufs, xch, accs + m * A * T::NT);
+      mesh_backward<W, T>(c, d, gm, wg, A, bufs, xch, accs + m * A * T::NT);
 #pragma unroll
       for (int k = 0; k < RPT; ++k) dn[k] = dn[k] + gm[k];
     }

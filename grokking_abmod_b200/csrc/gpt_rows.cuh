@@ -6,6 +6,11 @@
 // once per mesh layer.  Per-edge weight gradients accumulate per thread (no
 // atomics) and are written as per-(CTA, row-lane) partials that a separate
 // kernel reduces in a fixed order, so every result is bitwise reproducible.
+//
+// Shared-memory row buffers hold the even channels of a row in its first
+// W/2 floats and the odd channels in the second W/2 (see Planes), so each
+// thread's pair and every neighbour read of any stride are unit-stride,
+// bank-conflict-free accesses.
 #pragma once
 
 #include "common.cuh"
@@ -55,15 +60,27 @@ struct Ctx {
   __device__ __forceinline__ int row(int k) const { return k * T::RL + rl; }
 };
 
-// Value pair at channels (2cp+shift, 2cp+1+shift) mod W of one shared row.
+// One shared row of W channels as an even plane (row[cp] = x[2cp]) and an
+// odd plane (row[P + cp] = x[2cp + 1]).
 template <int W>
-__device__ __forceinline__ float2 gather_pair(const float* srow, int cp, int shift) {
-  int c0 = 2 * cp + shift;
-  c0 = ((c0 % W) + W) % W;
-  if ((c0 & 1) == 0) return *reinterpret_cast<const float2*>(srow + c0);
-  int c1 = c0 + 1 == W ? 0 : c0 + 1;
-  return make_float2(srow[c0], srow[c1]);
-}
+struct Planes {
+  static constexpr int P = W / 2;
+  __device__ static __forceinline__ void put(float* row, int cp, float2 v) {
+    row[cp] = v.x;
+    row[P + cp] = v.y;
+  }
+  __device__ static __forceinline__ float2 get(const float* row, int cp) { return make_float2(row[cp], row[P + cp]); }
+  // Even channel of pair cp + 1 (mod P): the stride-1 neighbour of 2cp + 1.
+  __device__ static __forceinline__ float next_even(const float* row, int cp) { return row[cp + 1 == P ? 0 : cp + 1]; }
+  // Odd channel of pair cp - 1 (mod P): the stride -1 neighbour of 2cp.
+  __device__ static __forceinline__ float prev_odd(const float* row, int cp) { return row[P + (cp == 0 ? P - 1 : cp - 1)]; }
+  // Channels (2cp + s, 2cp + 1 + s) mod W for an even shift |s| <= W / 2.
+  __device__ static __forceinline__ float2 shifted_even(const float* row, int cp, int s) {
+    int h = cp + s / 2;
+    h = h >= P ? h - P : (h < 0 ? h + P : h);
+    return get(row, h);
+  }
+};
 
 // Full-row sums (heads = 1) of one value per owned row.  `red` holds
 // 2 * TR * WPR floats; `phase` alternates the halves so back-to-back
@@ -110,18 +127,13 @@ template <int W, class T>
 __device__ __forceinline__ void mesh_layer_forward(const Ctx<T>& c, float2 (&a)[T::RPT], float4 w, int stride,
                                                    bool activated, float* buf) {
 #pragma unroll
-  for (int k = 0; k < T::RPT; ++k) *reinterpret_cast<float2*>(buf + c.row(k) * W + 2 * c.cp) = a[k];
+  for (int k = 0; k < T::RPT; ++k) Planes<W>::put(buf + c.row(k) * W, c.cp, a[k]);
   __syncthreads();
 #pragma unroll
   for (int k = 0; k < T::RPT; ++k) {
     const float* srow = buf + c.row(k) * W;
-    float2 nb;
-    if (stride == 1) {
-      int c2 = 2 * c.cp + 2 == W ? 0 : 2 * c.cp + 2;
-      nb = make_float2(a[k].y, srow[c2]);
-    } else {
-      nb = gather_pair<W>(srow, c.cp, stride);
-    }
+    const float2 nb = stride == 1 ? make_float2(a[k].y, Planes<W>::next_even(srow, c.cp))
+                                  : Planes<W>::shifted_even(srow, c.cp, stride);
     float z0 = a[k].x * w.x + nb.x * w.y;
     float z1 = a[k].y * w.z + nb.y * w.w;
     a[k] = activated ? make_float2(elu(z0), elu(z1)) : make_float2(z0, z1);
@@ -160,18 +172,24 @@ __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, fl
       const int r = c.row(k);
       float2 dz = dy[k];
       if (l + 1 != depth) {
-        float2 y = *reinterpret_cast<const float2*>(yout + r * W + 2 * c.cp);
+        const float2 y = Planes<W>::get(yout + r * W, c.cp);
         dz.x *= elu_slope(y.x);
         dz.y *= elu_slope(y.y);
       }
-      float2 x = *reinterpret_cast<const float2*>(xin + r * W + 2 * c.cp);
-      float2 nb = gather_pair<W>(xin + r * W, c.cp, s);
+      const float2 x = Planes<W>::get(xin + r * W, c.cp);
+      const float2 nb = s == 1 ? make_float2(x.y, Planes<W>::next_even(xin + r * W, c.cp))
+                               : Planes<W>::shifted_even(xin + r * W, c.cp, s);
       g.x += dz.x * x.x;
       g.y += dz.x * nb.x;
       g.z += dz.y * x.y;
       g.w += dz.y * nb.y;
       dy[k] = dz;
-      *reinterpret_cast<float2*>(ex + r * W + 2 * c.cp) = make_float2(dz.x * w.y, dz.y * w.w);
+      // Channel c's neighbour term dz*w1 flows back to channel c + s.
+      if (s == 1) {
+        ex[r * W + Planes<W>::P + c.cp] = dz.y * w.w;
+      } else {
+        Planes<W>::put(ex + r * W, c.cp, make_float2(dz.x * w.y, dz.y * w.w));
+      }
     }
     float4& slot = acc[l * T::NT + c.tid];
     slot.x += g.x;
@@ -181,7 +199,9 @@ __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, fl
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < T::RPT; ++k) {
-      float2 t = gather_pair<W>(ex + c.row(k) * W, c.cp, -s);
+      const float* erow = ex + c.row(k) * W;
+      const float2 t = s == 1 ? make_float2(Planes<W>::prev_odd(erow, c.cp), dy[k].x * w.y)
+                              : Planes<W>::shifted_even(erow, c.cp, -s);
       dy[k] = make_float2(dy[k].x * w.x + t.x, dy[k].y * w.z + t.y);
     }
   }
