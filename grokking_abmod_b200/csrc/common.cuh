@@ -10,8 +10,12 @@ constexpr uint32_t kIgnoreTarget = 0xFFFFFFFFu;  // src/gpt/mod.rs:26
 constexpr float kRmsEpsilon = 1e-5f;              // src/gpt/mod.rs:39
 constexpr float kXsaEpsilon = 1e-12f;             // src/gpt/mod.rs:41
 
-// ELU with alpha 1, written like the reference kernel (src/gpt/gpu.rs:135-139).
-__device__ __forceinline__ float elu(float z) { return z < 0.0f ? expf(z) - 1.0f : z; }
+// ELU with alpha 1 as in the reference kernel (src/gpt/gpu.rs:135-139):
+// exp(z) - 1 for z < 0.  The exponential is the __expf intrinsic (one
+// multiply and the hardware base-2 exponential); its error, a few ulp of
+// exp(z) on the negative branch, sits far inside the model's tolerances and
+// keeps the mesh layers' instruction count low.
+__device__ __forceinline__ float elu(float z) { return z < 0.0f ? __expf(z) - 1.0f : z; }
 
 // ELU derivative from the activated output y (src/gpt/gpu.rs:28-34).
 __device__ __forceinline__ float elu_slope(float y) { return y >= 0.0f ? 1.0f : y + 1.0f; }

@@ -122,12 +122,20 @@ __device__ __forceinline__ float head_sum(float v, int hp) {
 
 // One forward mesh layer over the owned rows: y = f(x[c] w0 + x[c+s] w1).
 // `buf` is a tile buffer the layer input is published into; the caller
-// guarantees no thread still reads it from an earlier phase.
+// guarantees no thread still reads it from an earlier phase.  With `keep`
+// the whole input is published (a backward pass reads it later); otherwise
+// a stride-1 layer publishes only the even plane its neighbours read.
 template <int W, class T>
 __device__ __forceinline__ void mesh_layer_forward(const Ctx<T>& c, float2 (&a)[T::RPT], float4 w, int stride,
-                                                   bool activated, float* buf) {
+                                                   bool activated, float* buf, bool keep) {
 #pragma unroll
-  for (int k = 0; k < T::RPT; ++k) Planes<W>::put(buf + c.row(k) * W, c.cp, a[k]);
+  for (int k = 0; k < T::RPT; ++k) {
+    if (keep || stride != 1) {
+      Planes<W>::put(buf + c.row(k) * W, c.cp, a[k]);
+    } else {
+      buf[c.row(k) * W + c.cp] = a[k].x;
+    }
+  }
   __syncthreads();
 #pragma unroll
   for (int k = 0; k < T::RPT; ++k) {
@@ -148,7 +156,7 @@ __device__ __forceinline__ void mesh_forward(const Ctx<T>& c, const Dims& d, flo
   for (int l = 0; l < depth; ++l) {
     float4 w = __ldg(wg + l * T::PAIRS + c.cp);
     float* buf = bufs + (keep ? l : (l & 1)) * T::BUF;
-    mesh_layer_forward<W, T>(c, a, w, mesh_stride(d, l), l + 1 != depth, buf);
+    mesh_layer_forward<W, T>(c, a, w, mesh_stride(d, l), l + 1 != depth, buf, keep);
   }
 }
 
