@@ -152,7 +152,7 @@ __device__ __forceinline__ void flush_partials(const Ctx<T>& c, const float4* ac
   if (partial == nullptr) return;
   const int slot = blockIdx.x * T::RL + c.rl;
   float4* out = reinterpret_cast<float4*>(partial) + (size_t)slot * depth * T::PAIRS;
-  for (int l = 0; l < depth; ++l) out[l * T::PAIRS + c.cp] = acc[l * T::NT + c.tid];
+  for (int l = 0; l < depth; ++l) out[l * T::PAIRS + c.cp] = slot_to_params(acc[l * T::NT + c.tid]);
 }
 
 template <class T>

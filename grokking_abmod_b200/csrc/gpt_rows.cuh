@@ -142,11 +142,15 @@ __device__ __forceinline__ void mesh_layer_forward(const Ctx<T>& c, float2 (&a)[
     const float* srow = buf + c.row(k) * W;
     const float2 nb = stride == 1 ? make_float2(a[k].y, Planes<W>::next_even(srow, c.cp))
                                   : Planes<W>::shifted_even(srow, c.cp, stride);
-    float z0 = a[k].x * w.x + nb.x * w.y;
-    float z1 = a[k].y * w.z + nb.y * w.w;
-    a[k] = activated ? make_float2(elu(z0), elu(z1)) : make_float2(z0, z1);
+    const float2 z = fma2(nb, make_float2(w.y, w.w), mul2(a[k], make_float2(w.x, w.z)));
+    a[k] = activated ? elu2(z) : z;
   }
 }
+
+// Edge-gradient slots hold (self c0, self c1, neighbour c0, neighbour c1) of
+// a channel pair so the packed updates pair up; parameters are stored per
+// channel as (self, neighbour) (src/gpt/config.rs:440-444).
+__device__ __forceinline__ float4 slot_to_params(float4 g) { return make_float4(g.x, g.z, g.y, g.w); }
 
 // Forward through a whole mesh stack.  With `keep`, layer l's input stays in
 // bufs[l] for a later backward pass; otherwise two buffers alternate.
@@ -171,46 +175,41 @@ __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, fl
   for (int l = depth - 1; l >= 0; --l) {
     const int s = mesh_stride(d, l);
     const float4 w = __ldg(wg + l * T::PAIRS + c.cp);
+    const float2 w0 = make_float2(w.x, w.z), w1 = make_float2(w.y, w.w);
     const float* xin = bufs + l * T::BUF;
     const float* yout = bufs + (l + 1) * T::BUF;  // valid when l + 1 < depth
     float* ex = xch + (l & 1) * T::BUF;
-    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+    float2 gs = make_float2(0.f, 0.f), gn = make_float2(0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < T::RPT; ++k) {
       const int r = c.row(k);
       float2 dz = dy[k];
-      if (l + 1 != depth) {
-        const float2 y = Planes<W>::get(yout + r * W, c.cp);
-        dz.x *= elu_slope(y.x);
-        dz.y *= elu_slope(y.y);
-      }
+      if (l + 1 != depth) dz = mul2(dz, elu_slope2(Planes<W>::get(yout + r * W, c.cp)));
       const float2 x = Planes<W>::get(xin + r * W, c.cp);
       const float2 nb = s == 1 ? make_float2(x.y, Planes<W>::next_even(xin + r * W, c.cp))
                                : Planes<W>::shifted_even(xin + r * W, c.cp, s);
-      g.x += dz.x * x.x;
-      g.y += dz.x * nb.x;
-      g.z += dz.y * x.y;
-      g.w += dz.y * nb.y;
+      gs = fma2(dz, x, gs);
+      gn = fma2(dz, nb, gn);
       dy[k] = dz;
       // Channel c's neighbour term dz*w1 flows back to channel c + s.
+      const float2 back = mul2(dz, w1);
       if (s == 1) {
-        ex[r * W + Planes<W>::P + c.cp] = dz.y * w.w;
+        ex[r * W + Planes<W>::P + c.cp] = back.y;
       } else {
-        Planes<W>::put(ex + r * W, c.cp, make_float2(dz.x * w.y, dz.y * w.w));
+        Planes<W>::put(ex + r * W, c.cp, back);
       }
     }
     float4& slot = acc[l * T::NT + c.tid];
-    slot.x += g.x;
-    slot.y += g.y;
-    slot.z += g.z;
-    slot.w += g.w;
+    const float2 ss = add2(make_float2(slot.x, slot.y), gs);
+    const float2 sn = add2(make_float2(slot.z, slot.w), gn);
+    slot = make_float4(ss.x, ss.y, sn.x, sn.y);
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < T::RPT; ++k) {
       const float* erow = ex + c.row(k) * W;
       const float2 t = s == 1 ? make_float2(Planes<W>::prev_odd(erow, c.cp), dy[k].x * w.y)
                               : Planes<W>::shifted_even(erow, c.cp, -s);
-      dy[k] = make_float2(dy[k].x * w.x + t.x, dy[k].y * w.z + t.y);
+      dy[k] = fma2(dy[k], w0, t);
     }
   }
 }

@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(RowTile<W, kOpRpt>::NT)
   }
   const int slot = blockIdx.x * T::RL + c.rl;
   float4* out = reinterpret_cast<float4*>(partial) + (size_t)slot * depth * T::PAIRS;
-  for (int l = 0; l < depth; ++l) out[l * T::PAIRS + c.cp] = acc[l * T::NT + c.tid];
+  for (int l = 0; l < depth; ++l) out[l * T::PAIRS + c.cp] = slot_to_params(acc[l * T::NT + c.tid]);
 }
 
 // out[p] = sum over slots of partial[slot][p], in slot order.
