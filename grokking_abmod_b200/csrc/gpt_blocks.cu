@@ -33,12 +33,17 @@ __device__ __forceinline__ void st2(float* p, int row, int rows, int W, int cp, 
 }
 
 // Per-head RMS (QK-Norm): returns 1/rms of the owned pair's head, and the
-// normalized pair in v.
-__device__ __forceinline__ float head_rmsnorm(float2& v, int hp) {
+// normalized pair in v.  inv_hw = 1 / head width.
+__device__ __forceinline__ float head_rmsnorm(float2& v, int hp, float inv_hw) {
   float s = head_sum(v.x * v.x + v.y * v.y, hp);
-  float inv = 1.0f / sqrtf(s / (float)(2 * hp) + kRmsEpsilon);
+  float inv = rms_scale(s, inv_hw);
   v = v * inv;
   return inv;
+}
+
+// XSA's 1 / max(|v|, eps) from |v|^2 (src/gpt/gpu.rs:781-822).
+__device__ __forceinline__ float xsa_scale(float sq) {
+  return sq >= kXsaEpsilon * kXsaEpsilon ? rsqrtf(sq) : 1.0f / kXsaEpsilon;
 }
 
 template <int W, int RPT>
@@ -55,10 +60,14 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
   Ctx<T> c;
   int phase = 0;
   const int hp = d.head_width / 2;
+  const float inv_hw = 1.0f / (float)d.head_width;
+  const RopeLane rope(c.cp, hp);
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     float2 n[RPT];
     float inv[RPT];
+    int pos[RPT];
+    tile_positions<T>(c, tile, d.sequence, pos);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
       const int r = tile * T::TR + c.row(k);
@@ -89,8 +98,8 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
         const int r = tile * T::TR + c.row(k);
         float2 v = a[k];
         if (m < 2) {
-          head_rmsnorm(v, hp);
-          v = rope_pair(v, c.cp, hp, r % d.sequence, rope_cs, false);
+          head_rmsnorm(v, hp, inv_hw);
+          v = rope.apply(v, pos[k], rope_cs, false);
         }
         st2(out, r, d.rows, W, c.cp, v);
       }
@@ -123,7 +132,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
       res[k] = ld2<T>(x, r, d.rows, W, c.cp);
       // XSA: z = y - (y.u)u, u = v / max(|v|, eps)   (src/gpt/gpu.rs:829-853)
       float sq = head_sum(vv.x * vv.x + vv.y * vv.y, hp);
-      float iv = 1.0f / fmaxf(sqrtf(sq), kXsaEpsilon);
+      float iv = xsa_scale(sq);
       float2 u = vv * iv;
       float proj = head_sum(y.x * u.x + y.y * u.y, hp);
       a[k] = make_float2(y.x - proj * u.x, y.y - proj * u.y);
@@ -213,7 +222,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
       y[k] = ld2<T>(o, r, d.rows, W, c.cp);
       float2 vv = ld2<T>(v, r, d.rows, W, c.cp);
       sq[k] = head_sum(vv.x * vv.x + vv.y * vv.y, hp);
-      iv[k] = 1.0f / fmaxf(sqrtf(sq[k]), kXsaEpsilon);
+      iv[k] = xsa_scale(sq[k]);
       u[k] = vv * iv[k];
       proj[k] = head_sum(y[k].x * u[k].x + y[k].y * u[k].y, hp);
     }
@@ -273,10 +282,14 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
   zero_slots<T>(c, accs, 3 * A);
   int phase = 0;
   const int hp = d.head_width / 2;
+  const float inv_hw = 1.0f / (float)d.head_width;
+  const RopeLane rope(c.cp, hp);
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     float2 n1[RPT], dn[RPT];
     float inv1[RPT];
+    int pos[RPT];
+    tile_positions<T>(c, tile, d.sequence, pos);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
       n1[k] = ld2<T>(x, tile * T::TR + c.row(k), d.rows, W, c.cp);
@@ -300,9 +313,9 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
           // QK-Norm then RoPE in forward; backward: inverse RoPE, then the
           // per-head RMSNorm adjoint.
           float2 qn = a[k];
-          float ih = head_rmsnorm(qn, hp);
-          gg = rope_pair(gg, c.cp, hp, r % d.sequence, rope_cs, true);
-          float dot = head_sum(gg.x * qn.x + gg.y * qn.y, hp) / (float)(2 * hp);
+          float ih = head_rmsnorm(qn, hp, inv_hw);
+          gg = rope.apply(gg, pos[k], rope_cs, true);
+          float dot = head_sum(gg.x * qn.x + gg.y * qn.y, hp) * inv_hw;
           gg = make_float2(ih * (gg.x - qn.x * dot), ih * (gg.y - qn.y * dot));
         }
         gm[k] = gg;

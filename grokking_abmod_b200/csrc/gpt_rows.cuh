@@ -108,6 +108,13 @@ __device__ __forceinline__ void row_sums(const Ctx<T>& c, float (&v)[T::RPT], fl
   }
 }
 
+// 1 / sqrt(mean + eps) of a sum of squares over `count` values, with
+// inv_count = 1 / count (src/gpt/gpu.rs:65-94).  rsqrtf is the hardware
+// reciprocal square root (a couple of ulp), well inside the tolerances.
+__device__ __forceinline__ float rms_scale(float sum_sq, float inv_count) {
+  return rsqrtf(sum_sq * inv_count + kRmsEpsilon);
+}
+
 // Per-head sums over hp = head_width/2 consecutive lanes (hp a power of two <= 32).
 __device__ __forceinline__ float head_sum(float v, int hp) {
   switch (hp) {
@@ -224,7 +231,7 @@ __device__ __forceinline__ void rmsnorm_rows(const Ctx<T>& c, float2 (&x)[T::RPT
   row_sums<T>(c, s, red, phase);
 #pragma unroll
   for (int k = 0; k < T::RPT; ++k) {
-    inv[k] = 1.0f / sqrtf(s[k] / (float)width + kRmsEpsilon);
+    inv[k] = rms_scale(s[k], 1.0f / (float)width);
     x[k] = x[k] * inv[k];
   }
 }
@@ -245,23 +252,44 @@ __device__ __forceinline__ void rmsnorm_rows_backward(const Ctx<T>& c, const flo
   }
 }
 
-// Slice RoPE on one owned pair of one row (split-half pairs within a head).
-// `inverse` rotates by -angle (backward).  cs: table [T][hd/2] of (cos, sin).
-__device__ __forceinline__ float2 rope_pair(float2 v, int cp, int hp, int pos, const float2* cs, bool inverse) {
-  const int j = cp % hp;  // lane within the head
-  if (hp == 1) {
-    float2 t = __ldg(cs + pos);
-    float sn = inverse ? -t.y : t.y;
-    return make_float2(v.x * t.x - v.y * sn, v.y * t.x + v.x * sn);
+// Slice RoPE (src/gpt/gpu.rs:175-208) for one thread's channel pair: the
+// split-half partner sits hp/2 lanes away within the head.  The lane
+// constants are fixed per thread; `apply` rotates one row's pair.
+struct RopeLane {
+  int hp, half, i0;
+  float sign;  // -1 on the first half of the head (x0 cos - x1 sin)
+  __device__ RopeLane(int cp, int hp_) : hp(hp_) {
+    const int j = cp % hp;
+    half = hp / 2;
+    const bool left = j < half;
+    i0 = left ? 2 * j : 2 * j - hp;
+    sign = left ? -1.0f : 1.0f;
   }
-  const int half = hp / 2;
-  float2 p = shfl_xor2(v, half);
-  const bool left = j < half;
-  const int i0 = left ? 2 * j : 2 * j - hp;
-  float2 t0 = __ldg(cs + pos * hp + i0);
-  float2 t1 = __ldg(cs + pos * hp + i0 + 1);
-  float sg = (left ? -1.0f : 1.0f) * (inverse ? -1.0f : 1.0f);
-  return make_float2(v.x * t0.x + sg * p.x * t0.y, v.y * t1.x + sg * p.y * t1.y);
+  // cs: table [T][hd/2] of (cos, sin); `inverse` rotates by -angle.
+  __device__ __forceinline__ float2 apply(float2 v, int pos, const float2* cs, bool inverse) const {
+    if (hp == 1) {
+      const float2 t = __ldg(cs + pos);
+      const float sn = inverse ? -t.y : t.y;
+      return make_float2(v.x * t.x - v.y * sn, v.y * t.x + v.x * sn);
+    }
+    const float2 p = shfl_xor2(v, half);
+    // (cos, sin) of the pair's two frequencies, one 16-byte load (i0 and hp are even).
+    const float4 t = __ldg(reinterpret_cast<const float4*>(cs + pos * hp + i0));
+    const float sg = inverse ? -sign : sign;
+    return fma2(v, make_float2(t.x, t.z), mul2(p * sg, make_float2(t.y, t.w)));
+  }
+};
+
+// Position within its sequence of each owned row of a tile.
+template <class T>
+__device__ __forceinline__ void tile_positions(const Ctx<T>& c, int tile, int sequence, int (&pos)[T::RPT]) {
+  const int base = (tile * T::TR) % sequence;
+#pragma unroll
+  for (int k = 0; k < T::RPT; ++k) {
+    int p = base + c.row(k);
+    while (p >= sequence) p -= sequence;
+    pos[k] = p;
+  }
 }
 
 }  // namespace mb
