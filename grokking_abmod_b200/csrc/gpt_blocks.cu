@@ -170,7 +170,7 @@ __device__ __forceinline__ void zero_slots(const Ctx<T>& c, float4* acc, int lay
 }
 
 template <int W, int RPT>
-__global__ void __launch_bounds__(RowTile<W, RPT>::NT)
+__global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
     post_backward(Dims d, const float* __restrict__ dxn, const float* __restrict__ xmid, const float* __restrict__ o,
                   const float* __restrict__ v, const float* __restrict__ wo, const float* __restrict__ wf,
                   float* __restrict__ do_out, float* __restrict__ dvx_out, float* __restrict__ dxm_out,
@@ -263,8 +263,11 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
   flush_partials<T>(c, acc_o, d.attn_depth, part_o);
 }
 
+// Register budget: shared memory limits the backward kernels to three CTAs
+// of 256 threads per SM at width 512, so ptxas gets the registers three CTAs
+// allow (85) instead of spilling to fit CTAs that shared memory would not admit.
 template <int W, int RPT>
-__global__ void __launch_bounds__(RowTile<W, RPT>::NT)
+__global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
     qkv_backward(Dims d, const float* __restrict__ dq, const float* __restrict__ dk, const float* __restrict__ dv,
                  const float* __restrict__ x, const float* __restrict__ dxm, const float* __restrict__ wq,
                  const float* __restrict__ wk, const float* __restrict__ wv, const float2* __restrict__ rope_cs,
