@@ -152,13 +152,15 @@ std::unique_ptr<BlockOps> make_block_ops(int W, int A, int F) {
 // ------------------------------------------------- head-width attention ops
 struct AttentionOps {
   virtual ~AttentionOps() = default;
-  // Device scratch (floats) the kernels need for `rows` token rows; the model
-  // allocates it per workspace and sets `scratch` before enqueueing.
-  virtual size_t scratch_floats(int rows, int H) const { return 0; }
+  // Device scratch (floats) the kernels need for `rows` token rows of a
+  // `layers`-block model; the model allocates it per workspace and sets
+  // `scratch` (and `layer`, the block being enqueued) before enqueueing.
+  virtual size_t scratch_floats(int rows, int H, int layers) const { return 0; }
   // Kernel launches of one forward / one backward (dK/dV + dQ) call.
   virtual int forward_launches() const { return 1; }
   virtual int backward_launches() const { return 2; }
   float* scratch = nullptr;
+  int layer = 0;
   virtual void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                        const float* v, float* o, float* lse) = 0;
   virtual void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q,
@@ -217,37 +219,37 @@ struct AttentionOpsTc final : AttentionOps {
   }
   static size_t key_floats(int rows, int H) { return (size_t)H * ((rows + kTcK - 1) / kTcK) * F::KTILE; }
   static size_t query_floats(int rows, int H) { return (size_t)H * ((rows + kTcQ - 1) / kTcQ) * F::QTILE; }
-  size_t scratch_floats(int rows, int H) const override { return key_floats(rows, H) + query_floats(rows, H); }
-  int forward_launches() const override { return 2; }   // key format + forward
-  int backward_launches() const override { return 4; }  // query format + dK/dV, key format + dQ
-  float* kfmt() const { return scratch; }
-  float* qfmt(int rows, int H) const { return scratch + key_floats(rows, H); }
-  // Writes the key-tile parts (bit mask over TcFmt's hi parts) the next kernel reads.
-  void format_keys(cudaStream_t s, int rows, int W, int H, const float* k, const float* v, unsigned parts) {
-    attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), 256, 0, s>>>(rows, W, k, v, kfmt(), parts);
+  // One query-tile set (rebuilt per backward block) and one key-tile set per
+  // block: the forward formats every key part once and dQ reuses them.
+  size_t scratch_floats(int rows, int H, int layers) const override {
+    return query_floats(rows, H) + (size_t)layers * key_floats(rows, H);
   }
+  int forward_launches() const override { return 2; }   // key format + forward
+  int backward_launches() const override { return 3; }  // query format + dK/dV, dQ
+  float* qfmt() const { return scratch; }
+  float* kfmt(int rows, int H) const { return scratch + query_floats(rows, H) + (size_t)layer * key_floats(rows, H); }
   void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                const float* v, float* o, float* lse) override {
-    format_keys(s, rows, W, H, k, v, (1u << F::K_HI) | (1u << F::VT_HI));
+    attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), 256, 0, s>>>(
+        rows, W, k, v, kfmt(rows, H), (1u << F::K_HI) | (1u << F::VT_HI) | (1u << F::V_HI) | (1u << F::KT_HI));
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
     attention_forward_tc<HD><<<grid, kTcThreads, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
-                                                                        kfmt(), o, lse, err);
+                                                                        kfmt(rows, H), o, lse, err);
   }
   void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                      const float* v, const float* dout, const float* lse, const float* delta, const float* dv_add,
                      float* dk, float* dv) override {
     attention_format_queries<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), 256, 0, s>>>(rows, W, q, dout, lse, delta,
-                                                                                   qfmt(rows, H));
+                                                                                   qfmt());
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
     attention_backward_dkdv_tc<HD><<<grid, kTcKvThreads, TcKv<HD>::smem, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), k, v,
-                                                                           qfmt(rows, H), dv_add, dk, dv, err);
+                                                                           qfmt(), dv_add, dk, dv, err);
   }
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
-    format_keys(s, rows, W, H, k, v, (1u << F::K_HI) | (1u << F::V_HI) | (1u << F::KT_HI));
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
     attention_backward_dq_tc<HD><<<grid, kTcThreads, K::smem_dq, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, dout,
-                                                                       kfmt(), lse, delta, dq, err);
+                                                                       kfmt(rows, H), lse, delta, dq, err);
   }
 };
 
@@ -629,7 +631,7 @@ class GptModel {
     ws->emb_chunks = (rows + kEmbChunk - 1) / kEmbChunk;
     ws->emb_partial = a.alloc<float>((size_t)ws->emb_chunks * V * W);
     ws->dE = a.alloc<float>((size_t)V * W);
-    ws->att_scratch = a.alloc<float>(attention_->scratch_floats(rows, H));
+    ws->att_scratch = a.alloc<float>(attention_->scratch_floats(rows, H, cfg_.layers));
     ws->emb_mesh_partial = a.alloc<float>((size_t)V * layout_.groups[layout_.embedding].size);
     ws->tokens = a.alloc<uint32_t>(rows);
     ws->targets = a.alloc<uint32_t>(rows);
@@ -713,6 +715,7 @@ class GptModel {
                            b == 0 ? ws.x[0] : nullptr, group(bg.query), group(bg.key), group(bg.value), ws.rope,
                            ws.q[b], ws.k[b], ws.v[b]);
       mark("attention_forward");
+      attention_->layer = b;
       attention_->forward(stream_, ws.rows, W, ws.seq, H, W / H, ws.q[b], ws.k[b], ws.v[b], ws.o[b], ws.lse[b]);
       mark("post_forward");
       blocks_->post_forward(stream_, ws.grid_pf, d, ws.o[b], ws.v[b], ws.x[b], group(bg.projection), group(bg.ffn),
@@ -750,6 +753,7 @@ class GptModel {
                              group(bg.ffn), ws.dO, ws.dvx, ws.dxm, ws.delta, ws.part[bg.projection],
                              ws.part[bg.ffn]);
       mark("attention_backward_dkdv");
+      attention_->layer = b;
       attention_->backward_dkdv(stream_, ws.rows, W, ws.seq, H, W / H, ws.q[b], ws.k[b], ws.v[b], ws.dO, ws.lse[b],
                                 ws.delta, ws.dvx, ws.dk, ws.dv);
       mark("attention_backward_dq");
