@@ -223,6 +223,25 @@ def roofline(times, cfg, rows, peaks):
     return out
 
 
+def step_roofline(cfg, rows, ms_per_step, peaks):
+    """Whole-step HBM roofline of a Mesh GPT training step.  Algorithmic bytes:
+    every op reads its inputs and writes its outputs once, and backward reads
+    the saved forward tensors it needs: per token per block W(21 + 2(4A+F))
+    floats forward and W(50 + 4(4A+F)) backward, 12W + 6V floats per token
+    outside the blocks, and 32 bytes per parameter per step (AdamW state and
+    the gradient)."""
+    W, V, L = cfg["width"], cfg["vocab_size"], cfg["layers"]
+    A, F = cfg["attention_mesh_depth"], cfg["ffn_mesh_depth"]
+    P = 2 * W * (A + L * (4 * A + F))
+    per_token = 4 * (L * W * ((21 + 2 * (4 * A + F)) + (50 + 4 * (4 * A + F))) + 12 * W + 6 * V)
+    step_bytes = per_token * rows + 32 * P
+    achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
+    peak = peaks.get("hbm_gbs")
+    return {"bound": "hbm", "algorithmic_bytes_per_token": per_token, "algorithmic_bytes_per_step": step_bytes,
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak if peak else None,
+            "peak_source": "measured (MEASURED_PEAKS.json)" if peaks.get("_measured") else "fallback"}
+
+
 def traffic_from_profiles(kernel):
     """DRAM bytes per launch of `kernel` from the committed ncu summary, if any
     (a line 'traffic_bytes_per_launch <kernel> <bytes>')."""
@@ -422,6 +441,7 @@ def main():
                     "h2d_bytes_per_step": 2 * rows * 4, "d2h_bytes_per_step": 8,
                     "api": "MeshGpt.train_batch_with_optimizer (mb_gpt_train_step), pinned host batches"},
             "roofline": roofline(times, cfg, rows, peaks),
+            "step_roofline": step_roofline(cfg, rows, ms / args.steps, peaks),
             "cpu_baseline": base,
             "gpu_launches": model.step_launches(rows, T) * args.steps,
             "clocks": clock_info,
