@@ -237,9 +237,12 @@ __device__ __forceinline__ void tc_st_split(uint32_t thi, uint32_t tlo, const fl
   for (int c = 0; c < NC; c += 16) {
     float hi[16], lo[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < 16; j += 2) {
       hi[j] = tc::tf32_hi(v[c + j]);
-      lo[j] = v[c + j] - hi[j];
+      hi[j + 1] = tc::tf32_hi(v[c + j + 1]);
+      const float2 l2 = add2(make_float2(v[c + j], v[c + j + 1]), make_float2(-hi[j], -hi[j + 1]));
+      lo[j] = l2.x;
+      lo[j + 1] = l2.y;
     }
     tc::tmem_st16(thi + c, hi);
     tc::tmem_st16(tlo + c, lo);
@@ -382,18 +385,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int kt = kbeg + j * kTcK;
       const bool full = one_seq && kt >= seq0 && kt + kTcK - 1 <= q0;
       const int kh = kt + 32 * half;
-      float mx = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) mx = fmaxf(mx, s[c]);
-      } else {
+      if (!full) {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           const int kr = kh + c;
           s[c] = (kr <= qr && kr >= qs && kr < rows) ? s[c] : -INFINITY;
-          mx = fmaxf(mx, s[c]);
         }
       }
+      // Row maximum over four independent chains (max is exact in any order).
+      float m4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+      for (int c = 4; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
+      float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       mx *= scale2;
       const bool need = mx > m + 8.0f;  // false while every key so far is masked
       float alpha = 1.0f;
@@ -401,14 +404,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         alpha = ex2(m - mx);  // 0 when m = -inf
         m = mx;
       }
-      float rs = 0.f;
       const float nm = m == -INFINITY ? 0.f : -m;
+      float2 rs2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        s[c] = ex2(fmaf(s[c], scale2, nm));  // ex2(-inf) = 0 for masked keys
-        rs += s[c];
+      for (int c = 0; c < 32; c += 2) {
+        const float2 t = fma2(make_float2(s[c], s[c + 1]), splat2(scale2), splat2(nm));
+        s[c] = ex2(t.x);  // ex2(-inf) = 0 for masked keys
+        s[c + 1] = ex2(t.y);
+        rs2 = add2(rs2, make_float2(s[c], s[c + 1]));
       }
-      l = l * alpha + rs;
+      l = l * alpha + (rs2.x + rs2.y);
       if (j > 0) {
         // P.V of step j-1 complete: O is stable and the P buffer is free.
         TC_WAIT_OR_FAIL(&o_done, (j - 1) & 1);
@@ -589,11 +594,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const bool full = one_seq && kt + 32 * k2 >= seq0 && kt + 32 * k2 + 31 <= q0;
         const int kh = kt + col;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int kr = kh + c;
-          const bool ok = full || (kr <= qr && kr >= qs && kr < rows);
-          const float p = ok ? ex2(fmaf(s[c], scale2, -L)) : 0.f;
-          s[c] = p * (dp[c] - dl) * scale;
+        for (int c = 0; c < 16; c += 2) {
+          const float2 t = fma2(make_float2(s[c], s[c + 1]), splat2(scale2), splat2(-L));
+          const bool ok0 = full || (kh + c <= qr && kh + c >= qs && kh + c < rows);
+          const bool ok1 = full || (kh + c + 1 <= qr && kh + c + 1 >= qs && kh + c + 1 < rows);
+          const float2 p = make_float2(ok0 ? ex2(t.x) : 0.f, ok1 ? ex2(t.y) : 0.f);
+          const float2 g = mul2(mul2(p, add2(make_float2(dp[c], dp[c + 1]), splat2(-dl))), splat2(scale));
+          s[c] = g.x;
+          s[c + 1] = g.y;
         }
         tc_st_split<16>(tS + col + lane, tSl + col + lane, s);  // dS hi over S
         tc::tmem_st_wait();
@@ -810,12 +818,25 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
         const bool full = one_seq && k0 + j * kTcQ + 32 * q2 >= k0 + kTcRows - 1 &&
                           k0 + j * kTcQ + 32 * q2 + 32 <= min(kseq_end, rows);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int qj = qh + c;
-          const bool ok = full || (qj >= kr && qj < ke && qj < rows && kr < rows);
-          const float p = ok ? ex2(fmaf(s[c], scale2, -Ls[c])) : 0.f;
-          s[c] = p;
-          dp[c] = p * (dp[c] - Es[c]) * scale;
+        for (int c = 0; c < 16; c += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(Ls + c);
+          const float4 e4 = *reinterpret_cast<const float4*>(Es + c);
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {
+            const float2 lv = u == 0 ? make_float2(l4.x, l4.y) : make_float2(l4.z, l4.w);
+            const float2 ev = u == 0 ? make_float2(e4.x, e4.y) : make_float2(e4.z, e4.w);
+            const int q0j = qh + c + u;
+            const float2 t = fma2(make_float2(s[c + u], s[c + u + 1]), splat2(scale2), make_float2(-lv.x, -lv.y));
+            const bool ok0 = full || (q0j >= kr && q0j < ke && q0j < rows && kr < rows);
+            const bool ok1 = full || (q0j + 1 >= kr && q0j + 1 < ke && q0j + 1 < rows && kr < rows);
+            const float2 p = make_float2(ok0 ? ex2(t.x) : 0.f, ok1 ? ex2(t.y) : 0.f);
+            const float2 g = mul2(mul2(p, add2(make_float2(dp[c + u], dp[c + u + 1]), make_float2(-ev.x, -ev.y))),
+                                  splat2(scale));
+            s[c + u] = p.x;
+            s[c + u + 1] = p.y;
+            dp[c + u] = g.x;
+            dp[c + u + 1] = g.y;
+          }
         }
         tc_st_split<16>(tS + col + lane, tPl + col + lane, s);   // P^T hi over S^T
         tc_st_split<16>(tP + col + lane, tSl + col + lane, dp);  // dS^T hi over dP^T
