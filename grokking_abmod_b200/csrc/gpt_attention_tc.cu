@@ -28,6 +28,7 @@
 //  * One thread issues all MMAs and commits them to mbarriers; all waits are
 //    bounded and report through `err` instead of hanging.
 
+#include "common.cuh"
 #include "tc05.cuh"
 
 namespace mb {
@@ -452,8 +453,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int c = 0; c < HD / 2; c += 16) {
         const int col = (HD / 2) * half + c;
         float a[16], bb[16];
-        tc::tmem_ld16(o0 + col, a);
-        tc::tmem_ld16(o1 + col, bb);
+        tc::tmem_ld16_pair(o0 + col, a, o1 + col, bb);
         if (qr < rows) {
           float4* dst = reinterpret_cast<float4*>(o + (size_t)qr * W + h * HD + col);
 #pragma unroll
@@ -515,9 +515,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ---------------------------------------------------------------------- dQ
-// TMEM: Q hi | Q lo | dO hi | dO lo | S then dS hi | dP | dS lo | dQ
+// TMEM: Q hi | Q lo | dO hi | dO lo | S | dP then dS hi | dS lo | dQ
 // Per key step: S = Q K^T, dP = dO V^T; dS = P (dP - delta) scale; dQ += dS K.
-// S and dS hi share columns, so S_{j+1} is issued once dQ_j has completed.
+// dS hi overwrites dP, so S_{j+1} is issued as soon as the compute warps have
+// read S_j, ahead of dQ_j's second half completing; only dP_{j+1} waits for
+// dQ_j.
 template <int HD>
 __global__ void __launch_bounds__(kTcThreads, 1)
     attention_backward_dq_tc(int rows, int W, int T, float scale, const float* __restrict__ q,
@@ -589,8 +591,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int k2 = 0; k2 < 2; ++k2) {
         const int col = 32 * k2 + 16 * half;
         float s[16], dp[16];
-        tc::tmem_ld16(tS + col + lane, s);
-        tc::tmem_ld16(tP + col + lane, dp);
+        tc::tmem_ld16_pair(tS + col + lane, s, tP + col + lane, dp);
         const bool full = one_seq && kt + 32 * k2 >= seq0 && kt + 32 * k2 + 31 <= q0;
         const int kh = kt + col;
 #pragma unroll
@@ -603,7 +604,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           s[c] = g.x;
           s[c + 1] = g.y;
         }
-        tc_st_split<16>(tS + col + lane, tSl + col + lane, s);  // dS hi over S
+        tc_st_split<16>(tP + col + lane, tSl + col + lane, s);  // dS hi over dP
         tc::tmem_st_wait();
         tc::fence_before_sync();
         tc::bar_arrive(&d_full[k2]);
@@ -640,24 +641,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (tid == kTcIssuer) {
     constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcK, false, false);
     constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
-    for (int j = 0; j < n; ++j) {
+    // Step j: S_j and dP_j were issued by the previous iteration (or the
+    // prologue); the loop issues dQ_j, then S_{j+1}, then (after dQ_j has
+    // consumed dS_j from the dP columns) dP_{j+1}.
+    if (n > 0 && !tc::bar_wait(&kv_full[0], 0)) sh.failed = 1;
+    if (n > 0 && !sh.failed) {
+      tc::fence_after_sync();
+      mma_tmem_a<HD>(tS, tQh, tQl, sm, sm + F::KPART, idS, false);                     // S_0  = Q K_0^T
+      mma_tmem_a<HD>(tP, tDh, tDl, sm + 2 * F::KPART, sm + 3 * F::KPART, idS, false);  // dP_0 = dO V_0^T
+      tc::commit(&s_full);
+    }
+    for (int j = 0; j < n && !sh.failed; ++j) {
       const int st = j % NS;
       const float* stage = sm + st * A::DQ_STAGE;  // K, K', V, V', Kt, Kt'
-      TC_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
-      if (j >= 1) {
-        TC_WAIT_OR_FAIL(&q_done, (j - 1) & 1);  // dQ_{j-1} has read dS (the S columns)
-      }
-      tc::fence_after_sync();
-      mma_tmem_a<HD>(tS, tQh, tQl, stage, stage + F::KPART, idS, false);                     // S  = Q K^T
-      mma_tmem_a<HD>(tP, tDh, tDl, stage + 2 * F::KPART, stage + 3 * F::KPART, idS, false);  // dP = dO V^T
-      tc::commit(&s_full);
       bool ok = true;
       for (int k2 = 0; k2 < 2 && ok; ++k2) {
         ok = tc::bar_wait(&d_full[k2], j & 1);
         tc::fence_after_sync();
         // dQ += dS K over keys [32 k2, 32 k2 + 32) (K steps 4 k2 .. 4 k2 + 3)
         if (ok)
-          mma_tmem_a_steps<kTcK, 4>(tG, tS, tSl, stage + 4 * F::KPART, stage + 5 * F::KPART, idG,
+          mma_tmem_a_steps<kTcK, 4>(tG, tP, tSl, stage + 4 * F::KPART, stage + 5 * F::KPART, idG,
                                     j > 0 || k2 > 0, 4 * k2);
       }
       if (!ok) {
@@ -666,6 +669,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc::commit(&q_done);
       tc::commit(&kv_empty[st]);
+      if (j + 1 < n) {
+        const int sn = (j + 1) % NS;
+        const float* next = sm + sn * A::DQ_STAGE;
+        TC_WAIT_OR_FAIL(&kv_full[sn], ((j + 1) / NS) & 1);
+        tc::fence_after_sync();
+        // The compute warps have read S_j (they arrived on d_full[1]).
+        mma_tmem_a<HD>(tS, tQh, tQl, next, next + F::KPART, idS, false);  // S_{j+1}
+        TC_WAIT_OR_FAIL(&q_done, j & 1);  // dQ_j has read dS_j hi (the dP columns)
+        tc::fence_after_sync();
+        mma_tmem_a<HD>(tP, tDh, tDl, next + 2 * F::KPART, next + 3 * F::KPART, idS, false);  // dP_{j+1}
+        tc::commit(&s_full);
+      }
     }
   }
   tc::fence_before_sync();
@@ -812,8 +827,7 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
         const float* Ls = Ls0 + col;
         const float* Es = Es0 + col;
         float s[16], dp[16];
-        tc::tmem_ld16(tS + col + lane, s);
-        tc::tmem_ld16(tP + col + lane, dp);
+        tc::tmem_ld16_pair(tS + col + lane, s, tP + col + lane, dp);
         const int qh = k0 + j * kTcQ + col;
         const bool full = one_seq && k0 + j * kTcQ + 32 * q2 >= k0 + kTcRows - 1 &&
                           k0 + j * kTcQ + 32 * q2 + 32 <= min(kseq_end, rows);
@@ -855,8 +869,7 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
       for (int c = 0; c < HD / 2; c += 16) {
         const int col = (HD / 2) * half + c;
         float gk[16], gv[16];
-        tc::tmem_ld16(tdK + lane + col, gk);
-        tc::tmem_ld16(tdV + lane + col, gv);
+        tc::tmem_ld16_pair(tdK + lane + col, gk, tdV + lane + col, gv);
         if (in) {
           const size_t base = (size_t)kr * W + h * HD + col;
 #pragma unroll
