@@ -871,11 +871,18 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
         float gk[16], gv[16];
         tc::tmem_ld16_pair(tdK + lane + col, gk, tdV + lane + col, gv);
         if (in) {
-          const size_t base = (size_t)kr * W + h * HD + col;
+          const size_t base = (size_t)kr * W + h * HD + col;  // 16-float aligned
+          float4* dk4 = reinterpret_cast<float4*>(dk + base);
+          float4* dv4 = reinterpret_cast<float4*>(dv + base);
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            dk[base + e] = gk[e];
-            dv[base + e] = gv[e] + (dv_add != nullptr ? dv_add[base + e] : 0.f);
+          for (int e = 0; e < 4; ++e) {
+            float4 a = make_float4(gv[4 * e], gv[4 * e + 1], gv[4 * e + 2], gv[4 * e + 3]);
+            if (dv_add != nullptr) {
+              const float4 x = __ldg(reinterpret_cast<const float4*>(dv_add + base) + e);
+              a = make_float4(a.x + x.x, a.y + x.y, a.z + x.z, a.w + x.w);
+            }
+            dk4[e] = make_float4(gk[4 * e], gk[4 * e + 1], gk[4 * e + 2], gk[4 * e + 3]);
+            dv4[e] = a;
           }
         }
       }
