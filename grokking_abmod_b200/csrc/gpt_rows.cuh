@@ -164,10 +164,14 @@ __device__ __forceinline__ float4 slot_to_params(float4 g) { return make_float4(
 template <int W, class T>
 __device__ __forceinline__ void mesh_forward(const Ctx<T>& c, const Dims& d, float2 (&a)[T::RPT],
                                              const float4* wg, int depth, float* bufs, bool keep) {
+  // Each layer's weights are requested one layer ahead: with the row
+  // buffers filling shared memory, L1 holds little and they come from L2.
+  float4 w = __ldg(wg + c.cp);
   for (int l = 0; l < depth; ++l) {
-    float4 w = __ldg(wg + l * T::PAIRS + c.cp);
+    const float4 wn = l + 1 < depth ? __ldg(wg + (l + 1) * T::PAIRS + c.cp) : w;
     float* buf = bufs + (keep ? l : (l & 1)) * T::BUF;
     mesh_layer_forward<W, T>(c, a, w, mesh_stride(d, l), l + 1 != depth, buf, keep);
+    w = wn;
   }
 }
 
@@ -179,9 +183,11 @@ template <int W, class T>
 __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, float2 (&dy)[T::RPT],
                                               const float4* wg, int depth, const float* bufs, float* xch,
                                               float4* acc) {
+  float4 wnext = __ldg(wg + (depth - 1) * T::PAIRS + c.cp);
   for (int l = depth - 1; l >= 0; --l) {
     const int s = mesh_stride(d, l);
-    const float4 w = __ldg(wg + l * T::PAIRS + c.cp);
+    const float4 w = wnext;
+    if (l > 0) wnext = __ldg(wg + (l - 1) * T::PAIRS + c.cp);  // one layer ahead
     const float2 w0 = make_float2(w.x, w.z), w1 = make_float2(w.y, w.w);
     const float* xin = bufs + l * T::BUF;
     const float* yout = bufs + (l + 1) * T::BUF;  // valid when l + 1 < depth
