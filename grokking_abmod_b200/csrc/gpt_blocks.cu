@@ -207,23 +207,27 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       for (int k = 0; k < RPT; ++k) a[k] = n2[k];
       mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(wf), d.ffn_depth, bufs, true);
     }
+    // O and V of the attention path, in flight during the FFN backward.
+    float2 y[RPT], vv[RPT];
 #pragma unroll
-    for (int k = 0; k < RPT; ++k) dy[k] = g[k];
+    for (int k = 0; k < RPT; ++k) {
+      const int r = tile * T::TR + c.row(k);
+      y[k] = ld2<T>(o, r, d.rows, W, c.cp);
+      vv[k] = ld2<T>(v, r, d.rows, W, c.cp);
+      dy[k] = g[k];
+    }
     mesh_backward<W, T>(c, d, dy, reinterpret_cast<const float4*>(wf), d.ffn_depth, bufs, xch, acc_f);
     rmsnorm_rows_backward<T>(c, n2, inv2, dy, red, phase, W);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) g[k] = g[k] + dy[k];  // dx_mid
     // Attention output path: x_mid = x + Omesh(XSA(O, V)).
-    float2 y[RPT], u[RPT];
+    float2 u[RPT];
     float proj[RPT], iv[RPT], sq[RPT];
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
-      const int r = tile * T::TR + c.row(k);
-      y[k] = ld2<T>(o, r, d.rows, W, c.cp);
-      float2 vv = ld2<T>(v, r, d.rows, W, c.cp);
-      sq[k] = head_sum(vv.x * vv.x + vv.y * vv.y, hp);
+      sq[k] = head_sum(vv[k].x * vv[k].x + vv[k].y * vv[k].y, hp);
       iv[k] = xsa_scale(sq[k]);
-      u[k] = vv * iv[k];
+      u[k] = vv[k] * iv[k];
       proj[k] = head_sum(y[k].x * u[k].x + y[k].y * u[k].y, hp);
     }
     __syncthreads();  // the FFN backward may still read bufs
