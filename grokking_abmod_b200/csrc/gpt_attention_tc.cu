@@ -51,6 +51,8 @@ struct TcFmt {
   static_assert(QT_HI == 4 && DT_HI == 6, "dK/dV streams parts 0-3 and 4-7 (+ lse2, delta) as two rings");
 };
 
+constexpr int kFmtThreads = 256;  // threads of the format kernels
+
 // Writes parts of one operand tile in the blocked K-major layout from a
 // shared-memory copy `x` ([R][HD], row stride HD + 2).  Part kind 0 is the
 // tile itself ([R rows][HD columns]), kind 1 its transpose ([HD rows][R
@@ -65,7 +67,8 @@ __device__ __forceinline__ void store_parts(float* __restrict__ tile, int part_f
   const int rows = transposed ? HD : R, cols = transposed ? R : HD;
   float* hi = tile + (size_t)p * part_floats;
   float* lo = hi + part_floats;
-  for (int q = threadIdx.x; q < rows * cols / 4; q += blockDim.x) {
+#pragma unroll
+  for (int q = threadIdx.x; q < R * HD / 4; q += kFmtThreads) {
     const int rl = q & 7, c4 = (q >> 3) % (cols / 4), rg = (q >> 3) / (cols / 4);
     const int r = rg * 8 + rl, c = c4 * 4;
     float v[4];
@@ -82,19 +85,30 @@ __device__ __forceinline__ void store_parts(float* __restrict__ tile, int part_f
   }
 }
 
-// Rows [row0, row0 + R) of head h of a row-major [rows][W] tensor into
-// shared memory ([R][HD], stride HD + 2), zero past the last row.
+// Rows [row0, row0 + R) of head h of two row-major [rows][W] tensors into
+// shared memory ([R][HD], stride HD + 2), zero past the last row.  Every
+// load of the thread is issued before the first store, so a CTA keeps all
+// of its 2 R HD floats in flight.
 template <int R, int HD>
-__device__ __forceinline__ void load_rows(float* x, const float* __restrict__ g, int row0, int rows, int W, int h) {
-  constexpr int XS = HD + 2;
-  for (int i = threadIdx.x; i < R * HD / 4; i += blockDim.x) {
-    const int r = i / (HD / 4), c = (i % (HD / 4)) * 4, row = row0 + r;
-    const float4 v = row < rows ? __ldg(reinterpret_cast<const float4*>(g + (size_t)row * W + h * HD + c))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-    x[r * XS + c] = v.x;
-    x[r * XS + c + 1] = v.y;
-    x[r * XS + c + 2] = v.z;
-    x[r * XS + c + 3] = v.w;
+__device__ __forceinline__ void load_rows2(float* xa, const float* __restrict__ ga, float* xb,
+                                           const float* __restrict__ gb, int row0, int rows, int W, int h) {
+  constexpr int XS = HD + 2, PER = R * HD / 4 / kFmtThreads;
+  static_assert(PER * kFmtThreads * 4 == R * HD, "tile must split evenly over the threads");
+  float4 va[PER], vb[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = threadIdx.x + kFmtThreads * j, r = i / (HD / 4), c = (i % (HD / 4)) * 4, row = row0 + r;
+    const size_t off = (size_t)row * W + h * HD + c;
+    va[j] = row < rows ? __ldg(reinterpret_cast<const float4*>(ga + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    vb[j] = row < rows ? __ldg(reinterpret_cast<const float4*>(gb + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = threadIdx.x + kFmtThreads * j, r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+    float* a = xa + r * XS + c;
+    float* b = xb + r * XS + c;
+    a[0] = va[j].x, a[1] = va[j].y, a[2] = va[j].z, a[3] = va[j].w;
+    b[0] = vb[j].x, b[1] = vb[j].y, b[2] = vb[j].z, b[3] = vb[j].w;
   }
 }
 
@@ -102,15 +116,14 @@ __device__ __forceinline__ void load_rows(float* x, const float* __restrict__ g,
 // bit mask over the hi parts of TcFmt's key tile (K_HI, VT_HI, V_HI, KT_HI):
 // only the parts the following kernel reads are written.
 template <int HD>
-__global__ void __launch_bounds__(256) attention_format_keys(int rows, int W, const float* __restrict__ k,
+__global__ void __launch_bounds__(kFmtThreads) attention_format_keys(int rows, int W, const float* __restrict__ k,
                                                                const float* __restrict__ v, float* __restrict__ fmt,
                                                                unsigned parts) {
   using F = TcFmt<HD>;
   __shared__ float xk[kTcK * (HD + 2)], xv[kTcK * (HD + 2)];
   const int t = blockIdx.x, h = blockIdx.y;
   float* tile = fmt + ((size_t)h * gridDim.x + t) * F::KTILE;
-  load_rows<kTcK, HD>(xk, k, t * kTcK, rows, W, h);
-  load_rows<kTcK, HD>(xv, v, t * kTcK, rows, W, h);
+  load_rows2<kTcK, HD>(xk, k, xv, v, t * kTcK, rows, W, h);
   __syncthreads();
   if (parts & (1u << F::K_HI)) store_parts<kTcK, HD>(tile, F::KPART, F::K_HI, false, xk);
   if (parts & (1u << F::VT_HI)) store_parts<kTcK, HD>(tile, F::KPART, F::VT_HI, true, xv);
@@ -120,7 +133,7 @@ __global__ void __launch_bounds__(256) attention_format_keys(int rows, int W, co
 
 // Query tiles of Q and dO with their LSE and delta: grid (ceil(rows/32), H).
 template <int HD>
-__global__ void __launch_bounds__(256) attention_format_queries(int rows, int W, const float* __restrict__ q,
+__global__ void __launch_bounds__(kFmtThreads) attention_format_queries(int rows, int W, const float* __restrict__ q,
                                                                   const float* __restrict__ dout,
                                                                   const float* __restrict__ lse2,
                                                                   const float* __restrict__ delta,
@@ -129,8 +142,7 @@ __global__ void __launch_bounds__(256) attention_format_queries(int rows, int W,
   __shared__ float xq[kTcQ * (HD + 2)], xd[kTcQ * (HD + 2)];
   const int t = blockIdx.x, h = blockIdx.y;
   float* tile = fmt + ((size_t)h * gridDim.x + t) * F::QTILE;
-  load_rows<kTcQ, HD>(xq, q, t * kTcQ, rows, W, h);
-  load_rows<kTcQ, HD>(xd, dout, t * kTcQ, rows, W, h);
+  load_rows2<kTcQ, HD>(xq, q, xd, dout, t * kTcQ, rows, W, h);
   __syncthreads();
   store_parts<kTcQ, HD>(tile, F::QPART, F::Q_HI, false, xq);
   store_parts<kTcQ, HD>(tile, F::QPART, F::D_HI, false, xd);

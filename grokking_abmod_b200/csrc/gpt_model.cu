@@ -230,7 +230,7 @@ struct AttentionOpsTc final : AttentionOps {
   float* kfmt(int rows, int H) const { return scratch + query_floats(rows, H) + (size_t)layer * key_floats(rows, H); }
   void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                const float* v, float* o, float* lse) override {
-    attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), 256, 0, s>>>(
+    attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), kFmtThreads, 0, s>>>(
         rows, W, k, v, kfmt(rows, H), (1u << F::K_HI) | (1u << F::VT_HI) | (1u << F::V_HI) | (1u << F::KT_HI));
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
     attention_forward_tc<HD><<<grid, kTcThreads, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
@@ -239,7 +239,7 @@ struct AttentionOpsTc final : AttentionOps {
   void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                      const float* v, const float* dout, const float* lse, const float* delta, const float* dv_add,
                      float* dk, float* dv) override {
-    attention_format_queries<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), 256, 0, s>>>(rows, W, q, dout, lse, delta,
+    attention_format_queries<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), kFmtThreads, 0, s>>>(rows, W, q, dout, lse, delta,
                                                                                    qfmt());
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
     attention_backward_dkdv_tc<HD><<<grid, kTcKvThreads, TcKv<HD>::smem, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), k, v,
