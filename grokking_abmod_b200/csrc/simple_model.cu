@@ -425,6 +425,109 @@ __global__ void __launch_bounds__(kChainThreads)
   }
 }
 
+// The same chain with the row state in shared memory (used when 2 m W floats
+// fit in kChainSmemFloats and every thread holds at most kChainRows rows):
+// each layer reads its input from one buffer and writes the other plus the
+// states[] copy the backward pass and the readout GEMMs use.  The arithmetic
+// and its order are those of chain_forward / chain_backward, so the results
+// are identical; only the memory the layers exchange through changes.
+constexpr int kChainSmemFloats = 40960;  // 160 KiB
+constexpr int kChainRows = 16;
+__global__ void __launch_bounds__(kChainThreads)
+    chain_forward_smem(int m, int W, int ed, const float* __restrict__ chain, float* __restrict__ states) {
+  extern __shared__ float csm[];
+  const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
+  const int mw = m * W;
+  if (rg < RG)
+    for (int k = rg; k < m; k += RG) {
+      const float e = c == k ? 1.f : 0.f;
+      csm[k * W + c] = e;
+      states[(size_t)k * W + c] = e;
+    }
+  __syncthreads();
+  const int cn = c + 1 == W ? 0 : c + 1;
+  for (int l = 0; l < ed; ++l) {
+    const float w0 = chain[(size_t)l * 2 * W + 2 * c], w1 = chain[(size_t)l * 2 * W + 2 * c + 1];
+    const float* in = csm + (l & 1) * mw;
+    float* out = csm + ((l + 1) & 1) * mw;
+    float* st = states + (size_t)(l + 1) * mw;
+    if (rg < RG) {
+      float val[kChainRows];
+#pragma unroll
+      for (int i = 0; i < kChainRows; ++i) {
+        const int k = rg + i * RG;
+        if (k < m) val[i] = fmaf(in[k * W + cn], w1, in[k * W + c] * w0);
+      }
+#pragma unroll
+      for (int i = 0; i < kChainRows; ++i) {
+        const int k = rg + i * RG;
+        if (k < m) {
+          out[k * W + c] = val[i];
+          st[(size_t)k * W + c] = val[i];
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kChainThreads)
+    chain_backward_smem(int m, int W, int ed, const float* __restrict__ chain, const float* __restrict__ states,
+                        const float* __restrict__ dE, float* __restrict__ grad) {
+  extern __shared__ float csm[];  // dv double buffer, 2 m W floats
+  __shared__ float part[2][kChainThreads];
+  const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
+  const int cp = c == 0 ? W - 1 : c - 1, cn = c + 1 == W ? 0 : c + 1;
+  const int mw = m * W;
+  for (int i = threadIdx.x; i < mw; i += kChainThreads) csm[i] = dE[i];
+  __syncthreads();
+  for (int l = ed - 1; l >= 0; --l) {
+    const float w0 = chain[(size_t)l * 2 * W + 2 * c], w1p = chain[(size_t)l * 2 * W + 2 * cp + 1];
+    const float* v = states + (size_t)l * mw;
+    const float* dv = csm + ((ed - 1 - l) & 1) * mw;
+    float* out = csm + ((ed - l) & 1) * mw;
+    float g0 = 0.f, g1 = 0.f;
+    if (rg < RG) {
+      // The layer's saved states come from L2: each group of 8 rows issues
+      // all its loads first.
+      for (int i0 = 0; i0 < kChainRows; i0 += 8) {
+        float vc[8], vn[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int k = rg + (i0 + i) * RG;
+          if (k < m) {
+            vc[i] = v[(size_t)k * W + c];
+            vn[i] = v[(size_t)k * W + cn];
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int k = rg + (i0 + i) * RG;
+          if (k < m) {
+            const float d = dv[k * W + c];
+            g0 = fmaf(d, vc[i], g0);
+            g1 = fmaf(d, vn[i], g1);
+            if (l > 0) out[k * W + c] = fmaf(dv[k * W + cp], w1p, d * w0);
+          }
+        }
+      }
+    }
+    part[0][threadIdx.x] = g0;
+    part[1][threadIdx.x] = g1;
+    __syncthreads();
+    if (threadIdx.x < W) {
+      float s0 = 0.f, s1 = 0.f;
+      for (int q = 0; q < RG; ++q) {
+        s0 += part[0][q * W + threadIdx.x];
+        s1 += part[1][q * W + threadIdx.x];
+      }
+      grad[(size_t)l * 2 * W + 2 * threadIdx.x] = s0;
+      grad[(size_t)l * 2 * W + 2 * threadIdx.x + 1] = s1;
+    }
+    __syncthreads();
+  }
+}
+
 // The core's weights, staged in shared memory when they fit (depth x 3W).
 constexpr int kCoreSmemFloats = 24576;  // 96 KiB
 __device__ __forceinline__ const float* stage_core(const float* __restrict__ core, int n_floats, float* sm) {
@@ -1054,6 +1157,11 @@ class SimpleModel {
     return c_.architecture == kSharedNeighbor && f <= kCoreSmemFloats ? f : 0;
   }
   int fwd_smem() const { return (core_smem_floats() + kFwdWarps * (int)c_.width) * 4; }
+  // The shared-memory chain kernels apply (see chain_forward_smem).
+  bool chain_in_smem(int m) const {
+    const int W = (int)c_.width, RG = kChainThreads / W;
+    return RG >= 1 && 2 * m * W <= kChainSmemFloats && m <= kChainRows * RG;
+  }
   int bwd_smem() const { return (core_smem_floats() + kBwdWarps * 5 * (int)c_.width) * 4; }
 
   template <int ACT>
@@ -1068,6 +1176,10 @@ class SimpleModel {
     });
   }
   void set_attributes() {
+    SIMPLE_CUDA(cudaFuncSetAttribute(&chain_forward_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kChainSmemFloats * 4));
+    SIMPLE_CUDA(cudaFuncSetAttribute(&chain_backward_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kChainSmemFloats * 4));
     if (c_.activation == kRelu)
       set_attributes_impl<kRelu>();
     else
@@ -1197,7 +1309,11 @@ class SimpleModel {
       const int ed = (int)c_.embedding_mesh_depth;
       const float* chain = w;
       const float* core = w + offsets_[ed];
-      chain_forward<<<1, kChainThreads, 0, stream_>>>(m, W, ed, chain, ws.states); ++launches_;
+      if (chain_in_smem(m))
+        chain_forward_smem<<<1, kChainThreads, 2 * m * W * 4, stream_>>>(m, W, ed, chain, ws.states);
+      else
+        chain_forward<<<1, kChainThreads, 0, stream_>>>(m, W, ed, chain, ws.states);
+      ++launches_;
       const float* E = ws.states + (size_t)ed * m * W;
       shared_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
           n, W, (int)c_.depth, strides_, ws.a, ws.b, E, core, ws.hs, ws.hf, ws.invf); ++launches_;
@@ -1281,7 +1397,11 @@ class SimpleModel {
       reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
           ws.part, ws.bwd_ctas, cnt, g + offsets_[ed]); ++launches_;
       class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 1, ws.a, ws.b, ws.dh0, ws.dEread, ws.dEemb); ++launches_;
-      chain_backward<<<1, kChainThreads, 0, stream_>>>(m, W, ed, w, ws.states, ws.dEemb, ws.dv, ws.dv2, g); ++launches_;
+      if (chain_in_smem(m))
+        chain_backward_smem<<<1, kChainThreads, 2 * m * W * 4, stream_>>>(m, W, ed, w, ws.states, ws.dEemb, g);
+      else
+        chain_backward<<<1, kChainThreads, 0, stream_>>>(m, W, ed, w, ws.states, ws.dEemb, ws.dv, ws.dv2, g);
+      ++launches_;
     }
     SIMPLE_CUDA(cudaGetLastError());
   }
