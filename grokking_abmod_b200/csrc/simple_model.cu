@@ -58,6 +58,11 @@ constexpr float kEps = 1e-5f;         // RMSNORM_EPSILON, src/gpt/mod.rs:39
 constexpr int kFwdWarps = 8;          // forward row kernels: warps (= rows) per CTA
 constexpr int kBwdWarps = 16;         // backward row kernels: warps per CTA ...
 constexpr int kBwdRows = 2;           // ... each walking this many rows per layer
+
+// (c + s) mod W and (c - s) mod W for 0 <= c, s < W: a compare and a
+// subtract instead of an integer division in the per-element loops.
+__device__ __forceinline__ int wrap_up(int c, int s, int W) { return c + s >= W ? c + s - W : c + s; }
+__device__ __forceinline__ int wrap_down(int c, int s, int W) { return c < s ? c - s + W : c - s; }
 constexpr int kMaxJ = kMaxKernelWidth / 32;  // row values per lane at the widest row
 constexpr int kSplitK = 256;          // batch rows per weight-gradient GEMM chunk
 constexpr unsigned kFull = 0xffffffffu;
@@ -144,7 +149,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
       const int c = lane + 32 * j;
       if (c < W) {
         float y = row[c] * w[c * p];
-        if (p == 2) y = fmaf(row[(c + s) % W], w[c * p + 1], y);
+        if (p == 2) y = fmaf(row[wrap_up(c, s, W)], w[c * p + 1], y);
         v[j] = y;
       }
     }
@@ -215,8 +220,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
           mine[c * p] += d * arow[c];
           float da = d * w[c * p];
           if (p == 2) {
-            mine[c * p + 1] += d * arow[(c + s) % W];
-            const int q = (c - s + W) % W;
+            mine[c * p + 1] += d * arow[wrap_up(c, s, W)];
+            const int q = wrap_down(c, s, W);
             da = fmaf(drow[q], w[q * p + 1], da);
           }
           dh[i][j] = da * act_g<ACT>(hl[j]);
@@ -577,7 +582,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     for (int j = 0; j < J; ++j) {
       const int c = lane + 32 * j;
       if (c < W) {
-        const float z = fmaf(row[(c + s) % W], w[3 * c + 1], row[c] * w[3 * c]) + w[3 * c + 2];
+        const float z = fmaf(row[wrap_up(c, s, W)], w[3 * c + 1], row[c] * w[3 * c]) + w[3 * c + 2];
         h[j] += act_f<ACT>(z);
       }
     }
@@ -664,7 +669,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
       for (int j = 0; j < J; ++j) {
         const int c = lane + 32 * j;
         if (c < W) {
-          const float z = fmaf(nrow[(c + s) % W], w[3 * c + 1], nrow[c] * w[3 * c]) + w[3 * c + 2];
+          const float z = fmaf(nrow[wrap_up(c, s, W)], w[3 * c + 1], nrow[c] * w[3 * c]) + w[3 * c + 2];
           zrow[c] = dh[i][j] * act_g<ACT>(z);
         }
       }
@@ -677,9 +682,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
         if (c < W) {
           const float dz = zrow[c];
           mine[3 * c] += dz * nrow[c];
-          mine[3 * c + 1] += dz * nrow[(c + s) % W];
+          mine[3 * c + 1] += dz * nrow[wrap_up(c, s, W)];
           mine[3 * c + 2] += dz;
-          const int q = (c - s + W) % W;
+          const int q = wrap_down(c, s, W);
           dn[j] = fmaf(zrow[q], w[3 * q + 1], dz * w[3 * c]);
           dot = fmaf(dn[j], nrow[c], dot);
         }
