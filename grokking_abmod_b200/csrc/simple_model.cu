@@ -195,7 +195,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
     const int s = strides[l];
     const float* w = mesh + (size_t)l * pw;
     float* mine = contrib + warp * pw;
-    for (int t = lane; t < pw; t += 32) mine[t] = 0.f;
+    // This warp's weight contributions over its rows, summed in registers in
+    // row order and written once per layer.
+    float g0[J], g1[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) g0[j] = g1[j] = 0.f;
 #pragma unroll
     for (int i = 0; i < kBwdRows; ++i) {
       const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
@@ -217,15 +221,23 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
         const int c = lane + 32 * j;
         if (c < W) {
           const float d = drow[c];
-          mine[c * p] += d * arow[c];
+          g0[j] += d * arow[c];
           float da = d * w[c * p];
           if (p == 2) {
-            mine[c * p + 1] += d * arow[wrap_up(c, s, W)];
+            g1[j] += d * arow[wrap_up(c, s, W)];
             const int q = wrap_down(c, s, W);
             da = fmaf(drow[q], w[q * p + 1], da);
           }
           dh[i][j] = da * act_g<ACT>(hl[j]);
         }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) {
+        mine[c * p] = g0[j];
+        if (p == 2) mine[c * p + 1] = g1[j];
       }
     }
     __syncthreads();
@@ -648,7 +660,11 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
     const int s = strides[l];
     const float* w = wts + (size_t)l * pw;
     float* mine = contrib + warp * pw;
-    for (int t = lane; t < pw; t += 32) mine[t] = 0.f;
+    // Weight contributions (w0, w1, bias) over this warp's rows, summed in
+    // registers in row order and written once per layer.
+    float g0[J], g1[J], g2[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) g0[j] = g1[j] = g2[j] = 0.f;
     float xc[kBwdRows][J];
 #pragma unroll
     for (int i = 0; i < kBwdRows; ++i)
@@ -681,9 +697,9 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
         dn[j] = 0.f;
         if (c < W) {
           const float dz = zrow[c];
-          mine[3 * c] += dz * nrow[c];
-          mine[3 * c + 1] += dz * nrow[wrap_up(c, s, W)];
-          mine[3 * c + 2] += dz;
+          g0[j] += dz * nrow[c];
+          g1[j] += dz * nrow[wrap_up(c, s, W)];
+          g2[j] += dz;
           const int q = wrap_down(c, s, W);
           dn[j] = fmaf(zrow[q], w[3 * q + 1], dz * w[3 * c]);
           dot = fmaf(dn[j], nrow[c], dot);
@@ -694,6 +710,15 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
       for (int j = 0; j < J; ++j) {
         const int c = lane + 32 * j;
         if (c < W) dh[i][j] += inv * (dn[j] - nrow[c] * dot);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) {
+        mine[3 * c] = g0[j];
+        mine[3 * c + 1] = g1[j];
+        mine[3 * c + 2] = g2[j];
       }
     }
     __syncthreads();
