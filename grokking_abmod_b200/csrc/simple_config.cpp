@@ -41,6 +41,16 @@ std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& 
   } else if (c.architecture == kRotaryDense) {
     l.push_back({c.modulus, c.width});
     for (uint32_t i = 0; i < c.depth; ++i) l.push_back({c.width, c.width});
+  } else if (c.architecture == kMlp) {
+    // src/simple/mod.rs:716-721: input layer, depth - 1 hidden layers, readout
+    l.push_back({2 * c.modulus, c.width});
+    for (uint32_t i = 1; i < c.depth; ++i) l.push_back({c.width, c.width});
+    l.push_back({c.width, c.modulus});
+  } else if (c.architecture == kBilinear) {
+    // src/simple/mod.rs:745-749: the a embedding, the b embedding, readout
+    l.push_back({c.modulus, c.width});
+    l.push_back({c.modulus, c.width});
+    l.push_back({c.width, c.modulus});
   }
   return l;
 }
@@ -64,20 +74,21 @@ size_t parameter_count(const mb_simple_config& c) {
 }
 
 void validate(const mb_simple_config& c) {
-  require(c.architecture <= kSharedNeighbor,
-          "architecture must be 0 (mesh-mlp), 1 (tied-rotary-residual-dense-mlp) or 2 (shared-neighbor-mesh-mlp)",
+  require(c.architecture <= kBilinear,
+          "architecture must be 0 (mesh-mlp), 1 (tied-rotary-residual-dense-mlp), 2 (shared-neighbor-mesh-mlp), "
+          "3 (mlp) or 4 (bilinear)",
           MB_ERR_UNSUPPORTED);
   require(c.activation <= kSquare, "activation must be 0 (relu) or 1 (square)");
   require(c.connectivity <= kButterfly, "connectivity must be 0 (own), 1 (neighbor) or 2 (butterfly)");
   require(c.full_mesh_initialization <= 1, "full-mesh initialization must be 0 (kaiming) or 1 (identity-hidden)");
   require(c.modulus >= 2 && c.modulus <= kMaxClasses, "modulus must be in 2..=1024");
   require(c.width >= 1 && c.width <= kMaxWidth, "width must be in 1..=16384");
-  require(c.depth >= 1 && c.depth <= kMaxDepth, "depth must be in 1..=64");
+  if (c.architecture != kBilinear) require(c.depth >= 1 && c.depth <= kMaxDepth, "depth must be in 1..=64");
   if (c.architecture == kSharedNeighbor)
     require(c.embedding_mesh_depth >= 1 && c.embedding_mesh_depth <= kMaxDepth,
             "shared Neighbor embedding depth must be in 1..=64");
   if (mesh_layers(c) > 0 && parents(c) == 2) require(c.width >= 2, "a second mesh parent needs a width of at least 2");
-  if (c.architecture != kMeshMlp)
+  if (c.architecture == kRotaryDense || c.architecture == kSharedNeighbor)
     require(c.width >= 2 && c.width % 2 == 0, "rotary roles need one-hot encoding and a positive even width");
   if (c.full_mesh_initialization != 0)
     require(c.architecture == kSharedNeighbor, "only a full mesh configures its mesh initialization");

@@ -1,5 +1,6 @@
 // grok-simple executor (host C++) and its kernels: mesh-mlp,
-// tied-rotary-residual-dense-mlp and shared-neighbor-mesh-mlp.
+// tied-rotary-residual-dense-mlp, shared-neighbor-mesh-mlp, mlp and
+// bilinear.
 //
 // Replaces GpuSimpleModel (src/simple/gpu.rs:1757-2073) and its op-by-op
 // plans (forward_with / backward_with, :2140-2700).  One training step is a
@@ -20,8 +21,9 @@
 //    fixed warp order into one partial per CTA; a second pass sums the CTA
 //    partials in order.  No atomics: results are bitwise reproducible.
 //  * Every dense contraction (readouts, their input and weight gradients, the
-//    residual dense projections) is a tcgen05 3xTF32 GEMM (gemm_tc.cu), with
-//    split-K over batch rows for weight gradients.
+//    residual dense projections, mlp's hidden layers) is a tcgen05 3xTF32
+//    GEMM (gemm_tc.cu), with split-K over batch rows for weight gradients.
+//    Embedding-row gradients of one-hot inputs are ordered per-class sums.
 //  * The shared-Neighbor readout (the transposed Neighbor chain,
 //    src/simple/reference.rs:257-268) equals h . E^T with E[k] the chain
 //    applied to class k's one-hot row (the reference's own identity,
@@ -741,6 +743,52 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
   }
 }
 
+// ------------------------------------------------------- mlp, bilinear
+// mlp input layer on one-hot rows (src/simple/reference.rs:292-299): x W0
+// with x one-hot at a and at m + b is W0[a] + W0[m + b]; z keeps the
+// pre-activation for the backward pass and act = act(z) feeds layer 1.
+template <int ACT>
+__global__ void mlp_input(int n, int W, int m, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                          const float* __restrict__ w0, float* __restrict__ z, float* __restrict__ act) {
+  const size_t count = (size_t)n * W;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / W, c = i % W;
+    const float v = w0[(size_t)a[r] * W + c] + w0[(size_t)(m + b[r]) * W + c];
+    z[i] = v;
+    act[i] = act_f<ACT>(v);
+  }
+}
+
+template <int ACT>
+__global__ void activate(size_t count, const float* __restrict__ z, float* __restrict__ act) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
+    act[i] = act_f<ACT>(z[i]);
+}
+
+// bilinear (src/simple/reference.rs:434-444): left = E_a[a], right = E_b[b]
+// (one-hot rows), p = left * right elementwise.
+__global__ void bilinear_input(int n, int W, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                               const float* __restrict__ ea, const float* __restrict__ eb, float* __restrict__ p) {
+  const size_t count = (size_t)n * W;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / W, c = i % W;
+    p[i] = ea[(size_t)a[r] * W + c] * eb[(size_t)b[r] * W + c];
+  }
+}
+
+// dleft = dp * right, dright = dp * left (the embeddings gathered again).
+__global__ void bilinear_gradient(int n, int W, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                                  const float* __restrict__ ea, const float* __restrict__ eb,
+                                  const float* __restrict__ dp, float* __restrict__ dleft,
+                                  float* __restrict__ dright) {
+  const size_t count = (size_t)n * W;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / W, c = i % W;
+    dleft[i] = dp[i] * eb[(size_t)b[r] * W + c];
+    dright[i] = dp[i] * ea[(size_t)a[r] * W + c];
+  }
+}
+
 // ------------------------------------------------------------ embedding
 // Per class k (one CTA each): the ordered sum over batch rows of the
 // operand-embedding gradients that use row k of the embedding.
@@ -748,6 +796,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
 //         k >= m rows with b == k - m, both as dh0[r][c].
 //  mode 1 (rotary): rows with a == k add dh0[r][c]; rows with b == k add
 //         the transposed rotation of dh0[r] (dh0[r][c^1], negated for odd c).
+//  mode 2 / 3 (bilinear, m rows of one operand's embedding): rows with
+//         a == k (mode 2) or b == k (mode 3) add dh0[r][c].
 // `extra` ([rows][W], may be null) is added (the readout's share of dE).
 constexpr int kClassThreads = 256;
 __global__ void __launch_bounds__(kClassThreads)
@@ -768,6 +818,8 @@ __global__ void __launch_bounds__(kClassThreads)
     if (r < n) {
       if (mode == 0) {
         kind = (k < m) ? (a[r] == (uint32_t)k ? 1 : 0) : (b[r] == (uint32_t)(k - m) ? 1 : 0);
+      } else if (mode >= 2) {
+        kind = (mode == 2 ? a[r] : b[r]) == (uint32_t)k ? 1 : 0;
       } else {
         kind = (a[r] == (uint32_t)k ? 1 : 0) | (b[r] == (uint32_t)k ? 2 : 0);
       }
@@ -977,7 +1029,7 @@ class SimpleModel {
     scalars_ = mem_.alloc<StepScalars>(1);
     SIMPLE_CUDA(cudaMemsetAsync(flags_, 0, kFlags * sizeof(int), stream_));
     SIMPLE_CUDA(cudaMemsetAsync(grad_, 0, P_ * sizeof(float), stream_));
-    const int nstr = c.architecture == kMeshMlp ? std::max(1, mesh_layers(c)) : (int)c.depth;
+    const int nstr = c.architecture == kMeshMlp ? std::max(1, mesh_layers(c)) : std::max(1, (int)c.depth);
     std::vector<int> st(nstr);
     for (int l = 0; l < nstr; ++l) st[l] = stride(c, l);
     strides_ = mem_.alloc<int>(nstr);
@@ -1262,6 +1314,20 @@ class SimpleModel {
       w->dact = w->dhf;
       w->part = M.alloc<float>((size_t)ctas * std::max(L, 1) * parents(c_) * W);
       part = gemm_partial_floats((int)W, (int)m, n, kSplitK);
+    } else if (c_.architecture == kMlp) {
+      // zs: pre-activations of layers 0..depth-1, hs: their activations
+      const size_t d = c_.depth;
+      w->zs = M.alloc<float>(d * nw);
+      w->hs = M.alloc<float>(d * nw);
+      w->dh = M.alloc<float>(nw);
+      w->dz = M.alloc<float>(nw);
+      part = std::max(gemm_partial_floats((int)W, (int)m, n, kSplitK), gemm_partial_floats((int)W, (int)W, n, kSplitK));
+    } else if (c_.architecture == kBilinear) {
+      w->hs = M.alloc<float>(nw);  // p = left * right
+      w->dn = M.alloc<float>(nw);  // dp
+      w->dh = M.alloc<float>(nw);  // dleft
+      w->dz = M.alloc<float>(nw);  // dright
+      part = gemm_partial_floats((int)W, (int)m, n, kSplitK);
     } else if (c_.architecture == kRotaryDense) {
       const size_t d = c_.depth;
       w->hs = M.alloc<float>((d + 1) * nw);
@@ -1322,6 +1388,21 @@ class SimpleModel {
           n, W, m, L, p, strides_, ws.a, ws.b, w + offsets_[0], w + (L > 0 ? offsets_[2] : 0), ws.h, ws.act); ++launches_;
       // logits = act . R  (R [W][m]: B element (j, c) at R[c * m + j])
       gemm({ws.act, W, false}, {R, m, true}, ws.logits, m, n, m, W, nullptr);
+    } else if (c_.architecture == kMlp) {
+      const int d = (int)c_.depth;
+      const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
+      mlp_input<ACT><<<eg, 256, 0, stream_>>>(n, W, m, ws.a, ws.b, w + offsets_[0], ws.zs, ws.hs); ++launches_;
+      for (int l = 1; l < d; ++l) {
+        // z_l = act_{l-1} . W_l  (W_l [in][out]: B element (out, in) at W_l[in * W + out])
+        gemm({ws.hs + (l - 1) * nw, W, false}, {w + offsets_[l], W, true}, ws.zs + l * nw, W, n, W, W, nullptr);
+        activate<ACT><<<eg, 256, 0, stream_>>>(nw, ws.zs + l * nw, ws.hs + l * nw); ++launches_;
+      }
+      // logits = act_{d-1} . R  (R [W][m])
+      gemm({ws.hs + (d - 1) * nw, W, false}, {w + offsets_[d], m, true}, ws.logits, m, n, m, W, nullptr);
+    } else if (c_.architecture == kBilinear) {
+      const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
+      bilinear_input<<<eg, 256, 0, stream_>>>(n, W, ws.a, ws.b, w + offsets_[0], w + offsets_[1], ws.hs); ++launches_;
+      gemm({ws.hs, W, false}, {w + offsets_[2], m, true}, ws.logits, m, n, m, W, nullptr);
     } else if (c_.architecture == kRotaryDense) {
       const float* E = w + offsets_[0];
       rotary_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.a, ws.b, E, ws.hs, ws.ns, ws.invs); ++launches_;
@@ -1397,6 +1478,31 @@ class SimpleModel {
             nw, ws.dact, ws.h, ws.dh0); ++launches_;
       }
       class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr, g + offsets_[0]); ++launches_;
+    } else if (c_.architecture == kMlp) {
+      const int d = (int)c_.depth;
+      const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
+      const float* R = w + offsets_[d];
+      // dR = act_{d-1}^T . dlog ; da = dlog . R^T
+      gemm({ws.hs + (d - 1) * nw, W, true}, {ws.dlog, m, true}, g + offsets_[d], m, W, m, n, ws.gemm_part, kSplitK);
+      gemm({ws.dlog, m, false}, {R, m, false}, ws.dh, W, n, W, m, nullptr);
+      for (int l = d - 1; l >= 1; --l) {
+        activation_gradient<ACT><<<eg, 256, 0, stream_>>>(nw, ws.dh, ws.zs + l * nw, ws.dz); ++launches_;
+        // dW_l = act_{l-1}^T . dz ; da = dz . W_l^T
+        gemm({ws.hs + (l - 1) * nw, W, true}, {ws.dz, W, true}, g + offsets_[l], W, W, W, n, ws.gemm_part, kSplitK);
+        gemm({ws.dz, W, false}, {w + offsets_[l], W, false}, ws.dh, W, n, W, W, nullptr);
+      }
+      activation_gradient<ACT><<<eg, 256, 0, stream_>>>(nw, ws.dh, ws.zs, ws.dh0); ++launches_;
+      class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr, g + offsets_[0]); ++launches_;
+    } else if (c_.architecture == kBilinear) {
+      const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
+      const float* R = w + offsets_[2];
+      // dR = p^T . dlog ; dp = dlog . R^T
+      gemm({ws.hs, W, true}, {ws.dlog, m, true}, g + offsets_[2], m, W, m, n, ws.gemm_part, kSplitK);
+      gemm({ws.dlog, m, false}, {R, m, false}, ws.dn, W, n, W, m, nullptr);
+      bilinear_gradient<<<eg, 256, 0, stream_>>>(n, W, ws.a, ws.b, w + offsets_[0], w + offsets_[1], ws.dn, ws.dh,
+                                                 ws.dz); ++launches_;
+      class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 2, ws.a, ws.b, ws.dh, nullptr, g + offsets_[0]); ++launches_;
+      class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 3, ws.a, ws.b, ws.dz, nullptr, g + offsets_[1]); ++launches_;
     } else if (c_.architecture == kRotaryDense) {
       const float* E = w + offsets_[0];
       const int d = (int)c_.depth;

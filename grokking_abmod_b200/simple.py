@@ -3,9 +3,9 @@
 Python mirror of the reference's ``SimpleConfig`` (src/simple/mod.rs:500-1055)
 and ``GpuSimpleModel`` (src/simple/gpu.rs:1757-2073): same names, argument
 meaning and error behaviour (a nonzero library status raises
-``MeshError``).  Three architectures run on this path: ``mesh-mlp``,
-``tied-rotary-residual-dense-mlp`` and ``shared-neighbor-mesh-mlp``, with
-one-hot operands.  There is no CPU fallback.
+``MeshError``).  Five architectures run on this path: ``mesh-mlp``,
+``tied-rotary-residual-dense-mlp``, ``shared-neighbor-mesh-mlp``, ``mlp``
+and ``bilinear``, with one-hot operands.  There is no CPU fallback.
 """
 
 import ctypes
@@ -19,7 +19,7 @@ from ._lib import AdamWC, SimpleConfigC, check, ptr
 from .data import EquationDataset, EquationSampler
 from .gpt import AdamWOptions
 
-ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp")
+ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear")
 ACTIVATIONS = ("relu", "square")
 CONNECTIVITIES = ("own", "neighbor", "butterfly")
 INITIALIZATIONS = ("kaiming", "identity-hidden")
@@ -27,7 +27,7 @@ INITIALIZATIONS = ("kaiming", "identity-hidden")
 
 @dataclass(frozen=True)
 class SimpleConfig:
-    """``SimpleConfig`` fields read by the three architectures (reference
+    """``SimpleConfig`` fields read by the five architectures (reference
     defaults)."""
     architecture: str = "mesh-mlp"
     activation: str = "relu"

@@ -2,7 +2,8 @@
 restatement of the forward pass, loss and gradients (test infrastructure
 only: the checker of the CUDA path, never the product).
 
-Covers the three architectures of the benchmark configurations:
+Covers the three architectures of the benchmark configurations and the two
+dense-only ones:
 
 * ``mesh-mlp`` (``src/simple/mod.rs:42-46``): dense input layer, ``depth-1``
   two-parent mesh layers with the activation on their inputs, dense readout.
@@ -13,6 +14,10 @@ Covers the three architectures of the benchmark configurations:
 * ``shared-neighbor-mesh-mlp`` (``:51-53``): a linear Neighbor embedding
   chain shared by a, b and the transposed readout, Rotate90 roles,
   pre-RMSNorm residual two-parent blocks with biases, final RMSNorm.
+* ``mlp`` (``:36-37``): concatenated operands, ``depth`` activated
+  bias-free dense layers, dense readout.
+* ``bilinear`` (``:77-78``): the elementwise product of separate ``a`` and
+  ``b`` embeddings, read out by a dense layer.
 
 Sources: ``SimpleConfig`` validation / layout / init / encode
 (``src/simple/mod.rs:500-1055``), the f64 tape model
@@ -37,7 +42,7 @@ from .rng import Random
 RMSNORM_EPSILON = 1e-5  # src/gpt/mod.rs:39 (f32 1e-5 widened)
 EPS = float(np.float32(RMSNORM_EPSILON))
 MAX_WIDTH, MAX_DEPTH, MAX_CLASSES = 16384, 64, 1024  # src/simple/mod.rs:25-31
-ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp")
+ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear")
 
 
 def butterfly_stride(width: int, layer: int) -> int:
@@ -48,7 +53,9 @@ def butterfly_stride(width: int, layer: int) -> int:
 @dataclass(frozen=True)
 class SimpleConfig:
     """The subset of ``SimpleConfig`` (``src/simple/mod.rs:500-558``) these
-    architectures read.  Encoding is one-hot; the embedding initializers are
+    architectures read.  Encoding is one-hot (``scalar``, one feature per
+    operand, is accepted by the dense architectures so that the reference's
+    tiny known-answer models can be stated); the embedding initializers are
     the reference defaults (uniform fan-in E, near-identity shared chain)."""
     architecture: str = "mesh-mlp"
     activation: str = "relu"  # or "square"
@@ -59,6 +66,7 @@ class SimpleConfig:
     embedding_mesh_depth: int = 4
     full_mesh_initialization: str = "kaiming"  # or "identity-hidden"
     mesh_learning_rate_multiplier: int = 1
+    encoding: str = "one-hot"  # or "scalar"
 
     def with_(self, **kw):
         return replace(self, **kw)
@@ -77,13 +85,18 @@ class SimpleConfig:
             raise ValueError(f"modulus must be in 2..={MAX_CLASSES}")
         if not 1 <= self.width <= MAX_WIDTH:
             raise ValueError(f"width must be in 1..={MAX_WIDTH}")
-        if not 1 <= self.depth <= MAX_DEPTH:
+        if a != "bilinear" and not 1 <= self.depth <= MAX_DEPTH:
             raise ValueError(f"depth must be in 1..={MAX_DEPTH}")
+        if self.encoding not in ("one-hot", "scalar"):
+            raise ValueError("unknown encoding")
+        if self.encoding != "one-hot" and a not in ("mesh-mlp", "mlp", "bilinear"):
+            raise ValueError("rotary roles need one-hot encoding and a positive even width")
         if a == "shared-neighbor-mesh-mlp" and not 1 <= self.embedding_mesh_depth <= MAX_DEPTH:
             raise ValueError("shared Neighbor embedding depth must be in 1..=64")
         if self.mesh_layers() > 0 and self.parents() == 2 and self.width < 2:
             raise ValueError("a second mesh parent needs a width of at least 2")
-        if a != "mesh-mlp" and (self.width < 2 or self.width % 2):
+        if a in ("tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp") and (
+                self.width < 2 or self.width % 2):
             raise ValueError("rotary roles need one-hot encoding and a positive even width")
         if self.full_mesh_initialization not in ("kaiming", "identity-hidden"):
             raise ValueError("unknown full-mesh initialization")
@@ -111,14 +124,21 @@ class SimpleConfig:
             return 1
         return butterfly_stride(self.width, layer)
 
+    def operand_features(self) -> int:
+        return self.modulus if self.encoding == "one-hot" else 1
+
     def input_features(self) -> int:
-        return 2 * self.modulus
+        return 2 * self.operand_features()
 
     def layers(self):
-        """Dense (inputs, outputs) layers in parameter order (``:720-756``)."""
-        m, w = self.modulus, self.width
+        """Dense (inputs, outputs) layers in parameter order (``:710-756``)."""
+        m, w, f = self.modulus, self.width, self.operand_features()
         if self.architecture == "mesh-mlp":
-            return [(2 * m, w), (w, m)]
+            return [(2 * f, w), (w, m)]
+        if self.architecture == "mlp":
+            return [(2 * f, w)] + [(w, w)] * (self.depth - 1) + [(w, m)]
+        if self.architecture == "bilinear":
+            return [(f, w), (f, w), (w, m)]
         if self.architecture == "tied-rotary-residual-dense-mlp":
             return [(m, w)] + [(w, w)] * self.depth
         return []
@@ -199,6 +219,8 @@ def initial_parameters(config: SimpleConfig, seed: int) -> np.ndarray:
 
 def encode(config: SimpleConfig, equations):
     """One-hot ``[a | b]`` feature rows and answer classes (``:1039-1055``)."""
+    if config.encoding != "one-hot":
+        raise ValueError("this restatement encodes one-hot rows only")
     m = config.modulus
     rows = len(equations)
     features = np.zeros((rows, 2 * m), dtype=np.float32)
@@ -264,8 +286,23 @@ class ReferenceSimpleModel:
         x = np.asarray(features, dtype=np.float64)
         g = _split(c, self.parameters)
         m, w = c.modulus, c.width
+        if c.architecture == "mlp":
+            # src/simple/reference.rs:292-299
+            zs = [x @ g[0].reshape(-1, w)]
+            acts = []
+            for layer in range(1, c.depth + 1):
+                acts.append(_act(c, zs[-1]))
+                out = c.layers()[layer][1]
+                zs.append(acts[-1] @ g[layer].reshape(-1, out))
+            return zs[-1], dict(x=x, zs=zs, acts=acts)
+        if c.architecture == "bilinear":
+            # src/simple/reference.rs:434-444
+            f = c.operand_features()
+            left, right = x[:, :f] @ g[0].reshape(f, w), x[:, f:] @ g[1].reshape(f, w)
+            prod = left * right
+            return prod @ g[2].reshape(w, m), dict(x=x, left=left, right=right, prod=prod)
         if c.architecture == "mesh-mlp":
-            w0 = g[0].reshape(2 * m, w)
+            w0 = g[0].reshape(-1, w)
             readout = g[1].reshape(w, m)
             h = [x @ w0]
             for layer in range(c.mesh_layers()):
@@ -347,6 +384,21 @@ class ReferenceSimpleModel:
         g = _split(c, self.parameters)
         grads = [np.zeros_like(x) for x in g]
         m, w = c.modulus, c.width
+        if c.architecture == "mlp":
+            dz = dlog
+            for layer in range(c.depth, 0, -1):
+                out = c.layers()[layer][1]
+                grads[layer] = (s["acts"][layer - 1].T @ dz).reshape(-1)
+                dz = (dz @ g[layer].reshape(-1, out).T) * _act_grad(c, s["zs"][layer - 1])
+            grads[0] = (s["x"].T @ dz).reshape(-1)
+            return loss, np.concatenate(grads)
+        if c.architecture == "bilinear":
+            f = c.operand_features()
+            grads[2] = (s["prod"].T @ dlog).reshape(-1)
+            dp = dlog @ g[2].reshape(w, m).T
+            grads[0] = (s["x"][:, :f].T @ (dp * s["right"])).reshape(-1)
+            grads[1] = (s["x"][:, f:].T @ (dp * s["left"])).reshape(-1)
+            return loss, np.concatenate(grads)
         if c.architecture == "mesh-mlp":
             readout = g[1].reshape(w, m)
             grads[1] = (s["act"].T @ dlog).reshape(-1)

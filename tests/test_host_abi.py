@@ -163,6 +163,10 @@ def test_simple_validation_mirrors_the_reference():
         with pytest.raises(MeshError):
             SimpleConfig(**kw).validate()
     with pytest.raises(ValueError):
-        SimpleConfig(architecture="bilinear").to_c()
+        SimpleConfig(architecture="residual-mlp").to_c()
+    # the library's own counts for the two dense-only architectures
+    assert SimpleConfig(architecture="mlp", modulus=97, width=128, depth=2).parameter_count() == 53632
+    assert SimpleConfig(architecture="bilinear", modulus=97, width=16, depth=0).validate().parameter_count() == 4656
+    assert SimpleConfig(architecture="mlp", modulus=7, width=9, depth=3).groups() == [14 * 9, 81, 81, 9 * 7]
     with pytest.raises(MeshError):
         SimpleConfig(modulus=7, width=8).encode([(7, 0, 0)])

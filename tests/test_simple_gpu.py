@@ -32,6 +32,9 @@ SMALL = [
     dict(architecture="shared-neighbor-mesh-mlp", modulus=7, width=32, depth=5, embedding_mesh_depth=4),
     dict(architecture="shared-neighbor-mesh-mlp", modulus=11, width=48, depth=6, embedding_mesh_depth=3,
          connectivity="butterfly", full_mesh_initialization="identity-hidden"),
+    dict(architecture="mlp", modulus=7, width=32, depth=3),
+    dict(architecture="mlp", modulus=11, width=20, depth=1, activation="square"),
+    dict(architecture="bilinear", modulus=13, width=24),
 ]
 FULL = [dict(GROK[name]["config"], modulus=97) for name in ("cfg0", "cfg1", "cfg2")]
 
@@ -77,7 +80,7 @@ def test_loss_and_gradient_match_oracle(kw):
         assert np.abs(seg - ref_seg).max() <= 1e-4 * np.abs(ref_grad).max() + 1e-4 * np.abs(ref_seg).max()
 
 
-@pytest.mark.parametrize("kw", SMALL[:1] + SMALL[3:4] + SMALL[5:6] + FULL)
+@pytest.mark.parametrize("kw", SMALL[:1] + SMALL[3:4] + SMALL[5:6] + SMALL[7:] + FULL)
 def test_logits_and_predictions_match_oracle(kw):
     config, features, targets, _ = _problem(kw, 0)
     params = _perturbed(config, 7)
@@ -189,3 +192,20 @@ def test_invalid_inputs_fail_before_launch():
         GpuSimpleModel(0, SimpleConfig(architecture="mesh-mlp", width=1024), seed=1)
     with pytest.raises(MeshError):
         model.set_parameters(np.full(config.parameter_count(), np.nan, np.float32))
+
+
+@pytest.mark.parametrize("case", PINS["grok_simple_models"]["cases"],
+                         ids=lambda c: "-".join(str(v) for v in c["config"].values()))
+def test_archived_mlp_and_bilinear_accuracies(case):
+    """The archived accuracy histories of the mlp and bilinear runs, replayed
+    on the device: step 0 (seeded split, init and forward) to one row, step
+    250 (25 warmed epochs of AdamW) to 2e-3."""
+    opt = PINS["grok_simple_models"]["optimizer"]
+    config = SimpleConfig(modulus=97, **case["config"])
+    records = train_records(config, 0, opt["operation"], opt["train_fraction"], opt["seed"], steps=250,
+                            batch=opt["batch"],
+                            optimizer=AdamWOptions(learning_rate=opt["learning_rate"],
+                                                   weight_decay=opt["weight_decay"], beta1=opt["beta1"],
+                                                   beta2=opt["beta2"], epsilon=opt["epsilon"]))
+    assert abs(records[0][2] - case["step0"][0]) <= 1.5 / 4656 and abs(records[0][3] - case["step0"][1]) <= 1.5 / 4656
+    assert abs(records[1][2] - case["step250"][0]) <= 2e-3 and abs(records[1][3] - case["step250"][1]) <= 2e-3

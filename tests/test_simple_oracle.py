@@ -3,8 +3,10 @@ unit-test constants (no GPU).
 
 ``oracle/simple_ref.py`` is pinned here to the archived ``loss.csv`` lines of
 the three benchmark configurations (seeded init, split and forward at step
-0; one warmed AdamW epoch at step 10), to the reference's parameter-count
-unit tests, and to finite differences of its own loss."""
+0; one warmed AdamW epoch at step 10), to the archived accuracy histories of
+the mlp and bilinear runs (step 0 and step 250), to the reference's
+known-answer models and parameter-count unit tests, and to finite
+differences of its own loss."""
 
 import json
 import math
@@ -45,11 +47,45 @@ def test_validation_rejects_what_the_reference_rejects():
         SimpleConfig("mesh-mlp", depth=0),
         SimpleConfig("mesh-mlp", depth=65),
         SimpleConfig("mesh-mlp", modulus=1),
-        SimpleConfig("bilinear"),
+        SimpleConfig("residual-mlp"),  # outside this restatement
+        SimpleConfig("tied-rotary-residual-dense-mlp", encoding="scalar"),
+        SimpleConfig("mlp", depth=0),
     ]
     for config in bad:
         with pytest.raises(ValueError):
             config.validate()
+
+
+def test_bilinear_ignores_depth_and_mlp_counts_its_layers():
+    # src/simple/mod.rs:593-597 (no depth rule for bilinear), :716-749 (layers)
+    assert SimpleConfig("bilinear", modulus=97, width=16, depth=0).validate().parameter_count() == 4656
+    assert SimpleConfig("mlp", modulus=97, width=128, depth=1).parameter_count() == 37248
+    assert SimpleConfig("mlp", modulus=97, width=128, depth=2).parameter_count() == 53632
+
+
+def test_known_answer_models():
+    """The reference's tiny models with hand-computed logits."""
+    for case in PINS["simple_kats"]["cases"]:
+        model = ReferenceSimpleModel(SimpleConfig(**case["config"]), parameters=case["parameters"])
+        got = model.logits(np.array([case["features"]], dtype=np.float32))[0]
+        assert np.allclose(got, case["logits"], atol=1e-12), (case, got)
+
+
+@pytest.mark.parametrize("case", PINS["grok_simple_models"]["cases"],
+                         ids=lambda c: "-".join(str(v) for v in c["config"].values()))
+def test_simple_models_match_archived_accuracies(case):
+    """Seeded split, init and forward reproduce the archived step-0
+    accuracies exactly; 250 warmed AdamW steps (25 epochs of 9 x 512 + 48)
+    reproduce step 250 to 2e-3 (the depth-2 MLP's FP32 run and this f64
+    restatement end 7 training rows apart; the others agree exactly)."""
+    opt = PINS["grok_simple_models"]["optimizer"]
+    config = SimpleConfig(modulus=97, **case["config"])
+    records = train_records(config, opt["operation"], opt["train_fraction"], opt["seed"], steps=250,
+                            batch=opt["batch"], learning_rate=opt["learning_rate"],
+                            weight_decay=opt["weight_decay"], beta1=opt["beta1"], beta2=opt["beta2"],
+                            epsilon=opt["epsilon"])
+    assert abs(records[0][2] - case["step0"][0]) < 1e-9 and abs(records[0][3] - case["step0"][1]) < 1e-9
+    assert abs(records[1][2] - case["step250"][0]) <= 2e-3 and abs(records[1][3] - case["step250"][1]) <= 2e-3
 
 
 def test_encode_is_one_hot_a_then_b():
@@ -111,6 +147,9 @@ def test_step10_record_matches_archive(name, tolerance):
     SimpleConfig("shared-neighbor-mesh-mlp", modulus=7, width=8, depth=3, embedding_mesh_depth=4),
     SimpleConfig("shared-neighbor-mesh-mlp", modulus=7, width=8, depth=3, embedding_mesh_depth=2,
                  connectivity="butterfly", full_mesh_initialization="identity-hidden"),
+    SimpleConfig("mlp", modulus=7, width=8, depth=3),
+    SimpleConfig("mlp", modulus=7, width=6, depth=1, activation="square"),
+    SimpleConfig("bilinear", modulus=7, width=8),
 ])
 def test_gradient_matches_finite_differences(config):
     rng = np.random.default_rng(0)
