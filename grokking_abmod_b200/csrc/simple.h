@@ -11,7 +11,8 @@
 namespace mb {
 namespace simple {
 
-enum Architecture : uint32_t { kMeshMlp = 0, kRotaryDense = 1, kSharedNeighbor = 2, kMlp = 3, kBilinear = 4 };
+enum Architecture : uint32_t { kMeshMlp = 0, kRotaryDense = 1, kSharedNeighbor = 2, kMlp = 3, kBilinear = 4,
+                               kResidualMlp = 5 };
 enum Activation : uint32_t { kRelu = 0, kSquare = 1 };
 enum Connectivity : uint32_t { kOwn = 0, kNeighbor = 1, kButterfly = 2 };
 

@@ -46,6 +46,16 @@ std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& 
     l.push_back({2 * c.modulus, c.width});
     for (uint32_t i = 1; i < c.depth; ++i) l.push_back({c.width, c.width});
     l.push_back({c.width, c.modulus});
+  } else if (c.architecture == kResidualMlp) {
+    // src/simple/mod.rs:735-744: input layer, per block (width -> hidden,
+    // hidden -> width), readout
+    const uint32_t hidden = c.width * c.expansion;
+    l.push_back({2 * c.modulus, c.width});
+    for (uint32_t i = 0; i < c.depth; ++i) {
+      l.push_back({c.width, hidden});
+      l.push_back({hidden, c.width});
+    }
+    l.push_back({c.width, c.modulus});
   } else if (c.architecture == kBilinear) {
     // src/simple/mod.rs:745-749: the a embedding, the b embedding, readout
     l.push_back({c.modulus, c.width});
@@ -74,9 +84,9 @@ size_t parameter_count(const mb_simple_config& c) {
 }
 
 void validate(const mb_simple_config& c) {
-  require(c.architecture <= kBilinear,
+  require(c.architecture <= kResidualMlp,
           "architecture must be 0 (mesh-mlp), 1 (tied-rotary-residual-dense-mlp), 2 (shared-neighbor-mesh-mlp), "
-          "3 (mlp) or 4 (bilinear)",
+          "3 (mlp), 4 (bilinear) or 5 (residual-mlp)",
           MB_ERR_UNSUPPORTED);
   require(c.activation <= kSquare, "activation must be 0 (relu) or 1 (square)");
   require(c.connectivity <= kButterfly, "connectivity must be 0 (own), 1 (neighbor) or 2 (butterfly)");
@@ -84,6 +94,9 @@ void validate(const mb_simple_config& c) {
   require(c.modulus >= 2 && c.modulus <= kMaxClasses, "modulus must be in 2..=1024");
   require(c.width >= 1 && c.width <= kMaxWidth, "width must be in 1..=16384");
   if (c.architecture != kBilinear) require(c.depth >= 1 && c.depth <= kMaxDepth, "depth must be in 1..=64");
+  if (c.architecture == kResidualMlp)
+    require(c.expansion >= 1 && (uint64_t)c.width * c.expansion <= kMaxWidth,
+            "residual hidden width must be in 1..=16384");
   if (c.architecture == kSharedNeighbor)
     require(c.embedding_mesh_depth >= 1 && c.embedding_mesh_depth <= kMaxDepth,
             "shared Neighbor embedding depth must be in 1..=64");

@@ -1,6 +1,6 @@
 // grok-simple executor (host C++) and its kernels: mesh-mlp,
-// tied-rotary-residual-dense-mlp, shared-neighbor-mesh-mlp, mlp and
-// bilinear.
+// tied-rotary-residual-dense-mlp, shared-neighbor-mesh-mlp, mlp, bilinear
+// and residual-mlp.
 //
 // Replaces GpuSimpleModel (src/simple/gpu.rs:1757-2073) and its op-by-op
 // plans (forward_with / backward_with, :2140-2700).  One training step is a
@@ -81,13 +81,16 @@ struct StepScalars {
 // Device status flags: [0] a tensor-core wait gave up, [1] nonfinite logits.
 enum { kFlagTc = 0, kFlagNonfinite = 1, kFlags = 2 };
 
+// kLinear: the identity, for residual sums whose branch ends without an
+// activation (residual-mlp); it is not a model activation.
+constexpr int kLinear = 2;
 template <int ACT>
 __device__ __forceinline__ float act_f(float x) {
-  return ACT == kRelu ? fmaxf(x, 0.f) : x * x;
+  return ACT == kRelu ? fmaxf(x, 0.f) : (ACT == kSquare ? x * x : x);
 }
 template <int ACT>
 __device__ __forceinline__ float act_g(float x) {
-  return ACT == kRelu ? (x > 0.f ? 1.f : 0.f) : 2.f * x;
+  return ACT == kRelu ? (x > 0.f ? 1.f : 0.f) : (ACT == kSquare ? 2.f * x : 1.f);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -338,6 +341,36 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     }
   }
   if (lane == 0) inv_out[r] = inv;
+}
+
+// residual-mlp input (src/simple/reference.rs:418-419): h0 = x W0 with x
+// one-hot at a and m + b, i.e. W0[a] + W0[m + b], and n0 = RMSNorm(h0).
+template <int J>
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    concat_embed(int n, int W, int m, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                 const float* __restrict__ w0, float* __restrict__ h0, float* __restrict__ n0,
+                 float* __restrict__ inv0) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  if (r >= n) return;
+  const float* ra = w0 + (size_t)a[r] * W;
+  const float* rb = w0 + (size_t)(m + b[r]) * W;
+  float v[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = lane + 32 * j;
+    v[j] = c < W ? ra[c] + rb[c] : 0.f;
+  }
+  const float inv = row_inverse_rms(v, W, lane);
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = lane + 32 * j;
+    if (c < W) {
+      h0[(size_t)r * W + c] = v[j];
+      n0[(size_t)r * W + c] = v[j] * inv;
+    }
+  }
+  if (lane == 0) inv0[r] = inv;
 }
 
 // dx = add + inv (dy - y <dy, y> / W) with y the normalised row.
@@ -974,6 +1007,7 @@ struct Workspace {
   float *h, *act, *dact, *dh0, *part;  // mesh-mlp
   float *hs, *ns, *invs, *zs, *dh, *dz, *dn, *dhf, *dEread, *gemm_part;
   float *hf, *invf, *states, *dEemb, *dv, *dv2;  // shared-Neighbor
+  float *es, *as, *dex, *dax;                     // residual-mlp expansion
   int bwd_ctas = 0;
   cudaGraphExec_t step_graph = nullptr;
   uint32_t step_launches = 0;
@@ -1322,6 +1356,22 @@ class SimpleModel {
       w->dh = M.alloc<float>(nw);
       w->dz = M.alloc<float>(nw);
       part = std::max(gemm_partial_floats((int)W, (int)m, n, kSplitK), gemm_partial_floats((int)W, (int)W, n, kSplitK));
+    } else if (c_.architecture == kResidualMlp) {
+      // per block l: hs/ns/invs the residual stream and its RMSNorm, es the
+      // expanded pre-activation, as its activation, zs the branch output
+      const size_t d = c_.depth, H = (size_t)W * c_.expansion, nh = N * H;
+      w->hs = M.alloc<float>((d + 1) * nw);
+      w->ns = M.alloc<float>((d + 1) * nw);
+      w->invs = M.alloc<float>((d + 1) * N);
+      w->es = M.alloc<float>(d * nh);
+      w->as = M.alloc<float>(d * nh);
+      w->zs = M.alloc<float>(d * nw);
+      w->dh = M.alloc<float>(nw);
+      w->dn = M.alloc<float>(nw);
+      w->dex = M.alloc<float>(nh);
+      w->dax = M.alloc<float>(nh);
+      part = std::max({gemm_partial_floats((int)H, (int)W, n, kSplitK), gemm_partial_floats((int)W, (int)H, n, kSplitK),
+                       gemm_partial_floats((int)W, (int)m, n, kSplitK)});
     } else if (c_.architecture == kBilinear) {
       w->hs = M.alloc<float>(nw);  // p = left * right
       w->dn = M.alloc<float>(nw);  // dp
@@ -1399,6 +1449,24 @@ class SimpleModel {
       }
       // logits = act_{d-1} . R  (R [W][m])
       gemm({ws.hs + (d - 1) * nw, W, false}, {w + offsets_[d], m, true}, ws.logits, m, n, m, W, nullptr);
+    } else if (c_.architecture == kResidualMlp) {
+      // src/simple/reference.rs:418-433
+      const int d = (int)c_.depth, H = W * (int)c_.expansion;
+      const size_t nh = (size_t)n * H;
+      const int hg = (int)std::min<size_t>((nh + 255) / 256, 1184);
+      concat_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, m, ws.a, ws.b, w + offsets_[0], ws.hs, ws.ns,
+                                                            ws.invs); ++launches_;
+      for (int l = 0; l < d; ++l) {
+        const float* U = w + offsets_[1 + 2 * l];  // [W][H]
+        const float* D = w + offsets_[2 + 2 * l];  // [H][W]
+        gemm({ws.ns + l * nw, W, false}, {U, H, true}, ws.es + l * nh, H, n, H, W, nullptr);
+        activate<ACT><<<hg, 256, 0, stream_>>>(nh, ws.es + l * nh, ws.as + l * nh); ++launches_;
+        gemm({ws.as + l * nh, H, false}, {D, W, true}, ws.zs + l * nw, W, n, W, H, nullptr);
+        residual_norm<kLinear, J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.hs + l * nw, ws.zs + l * nw,
+                                                                     ws.hs + (l + 1) * nw, ws.ns + (l + 1) * nw,
+                                                                     ws.invs + (l + 1) * n); ++launches_;
+      }
+      gemm({ws.ns + d * nw, W, false}, {w + offsets_[1 + 2 * d], m, true}, ws.logits, m, n, m, W, nullptr);
     } else if (c_.architecture == kBilinear) {
       const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
       bilinear_input<<<eg, 256, 0, stream_>>>(n, W, ws.a, ws.b, w + offsets_[0], w + offsets_[1], ws.hs); ++launches_;
@@ -1493,6 +1561,33 @@ class SimpleModel {
       }
       activation_gradient<ACT><<<eg, 256, 0, stream_>>>(nw, ws.dh, ws.zs, ws.dh0); ++launches_;
       class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr, g + offsets_[0]); ++launches_;
+    } else if (c_.architecture == kResidualMlp) {
+      const int d = (int)c_.depth, H = W * (int)c_.expansion;
+      const size_t nh = (size_t)n * H;
+      const int hg = (int)std::min<size_t>((nh + 255) / 256, 1184);
+      const float* R = w + offsets_[1 + 2 * d];
+      // dR = n_d^T . dlog ; dn_d = dlog . R^T ; dh = RMSNorm adjoint
+      gemm({ws.ns + d * nw, W, true}, {ws.dlog, m, true}, g + offsets_[1 + 2 * d], m, W, m, n, ws.gemm_part,
+           kSplitK);
+      gemm({ws.dlog, m, false}, {R, m, false}, ws.dn, W, n, W, m, nullptr);
+      rms_backward<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.ns + d * nw, ws.invs + d * n, ws.dn, nullptr,
+                                                           ws.dh); ++launches_;
+      for (int l = d - 1; l >= 0; --l) {
+        const float* U = w + offsets_[1 + 2 * l];
+        const float* D = w + offsets_[2 + 2 * l];
+        // the branch output's gradient is dh: dD = a^T dh, da = dh D^T
+        gemm({ws.as + l * nh, H, true}, {ws.dh, W, true}, g + offsets_[2 + 2 * l], W, H, W, n, ws.gemm_part,
+             kSplitK);
+        gemm({ws.dh, W, false}, {D, W, false}, ws.dax, H, n, H, W, nullptr);
+        activation_gradient<ACT><<<hg, 256, 0, stream_>>>(nh, ws.dax, ws.es + l * nh, ws.dex); ++launches_;
+        // dU = n_l^T de, dn = de U^T, dh += RMSNorm adjoint of dn
+        gemm({ws.ns + l * nw, W, true}, {ws.dex, H, true}, g + offsets_[1 + 2 * l], H, W, H, n, ws.gemm_part,
+             kSplitK);
+        gemm({ws.dex, H, false}, {U, H, false}, ws.dn, W, n, W, H, nullptr);
+        rms_backward<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.ns + l * nw, ws.invs + l * n, ws.dn, ws.dh,
+                                                             ws.dh); ++launches_;
+      }
+      class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh, nullptr, g + offsets_[0]); ++launches_;
     } else if (c_.architecture == kBilinear) {
       const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
       const float* R = w + offsets_[2];

@@ -3,9 +3,10 @@
 Python mirror of the reference's ``SimpleConfig`` (src/simple/mod.rs:500-1055)
 and ``GpuSimpleModel`` (src/simple/gpu.rs:1757-2073): same names, argument
 meaning and error behaviour (a nonzero library status raises
-``MeshError``).  Five architectures run on this path: ``mesh-mlp``,
-``tied-rotary-residual-dense-mlp``, ``shared-neighbor-mesh-mlp``, ``mlp``
-and ``bilinear``, with one-hot operands.  There is no CPU fallback.
+``MeshError``).  Six architectures run on this path: ``mesh-mlp``,
+``tied-rotary-residual-dense-mlp``, ``shared-neighbor-mesh-mlp``, ``mlp``,
+``bilinear`` and ``residual-mlp``, with one-hot operands.  There is no CPU
+fallback.
 """
 
 import ctypes
@@ -19,7 +20,8 @@ from ._lib import AdamWC, SimpleConfigC, check, ptr
 from .data import EquationDataset, EquationSampler
 from .gpt import AdamWOptions
 
-ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear")
+ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear",
+                 "residual-mlp")
 ACTIVATIONS = ("relu", "square")
 CONNECTIVITIES = ("own", "neighbor", "butterfly")
 INITIALIZATIONS = ("kaiming", "identity-hidden")
@@ -27,7 +29,7 @@ INITIALIZATIONS = ("kaiming", "identity-hidden")
 
 @dataclass(frozen=True)
 class SimpleConfig:
-    """``SimpleConfig`` fields read by the five architectures (reference
+    """``SimpleConfig`` fields read by the six architectures (reference
     defaults)."""
     architecture: str = "mesh-mlp"
     activation: str = "relu"
@@ -38,6 +40,7 @@ class SimpleConfig:
     embedding_mesh_depth: int = 4
     full_mesh_initialization: str = "kaiming"
     mesh_learning_rate_multiplier: int = 1
+    expansion: int = 4
 
     def with_(self, **kw):
         return replace(self, **kw)
@@ -52,7 +55,7 @@ class SimpleConfig:
                              self.depth, index(CONNECTIVITIES, self.connectivity, "mesh connectivity"),
                              self.embedding_mesh_depth,
                              index(INITIALIZATIONS, self.full_mesh_initialization, "full-mesh initialization"),
-                             self.mesh_learning_rate_multiplier)
+                             self.mesh_learning_rate_multiplier, self.expansion)
 
     def validate(self):
         c = self.to_c()

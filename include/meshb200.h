@@ -225,10 +225,12 @@ int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t seque
 /* ---- grok-simple models (src/simple/mod.rs, src/simple/gpu.rs) ----------
  * Replaces GpuSimpleModel::{new, parameters, set_parameters, upload_table,
  * upload_batches, logits, evaluate, loss_and_gradient, train_batch}
- * (src/simple/gpu.rs:1757-2073) for five architectures of SimpleConfig
+ * (src/simple/gpu.rs:1757-2073) for six architectures of SimpleConfig
  * (src/simple/mod.rs:500-558); the encoding is one-hot.
  *   architecture 0 = mesh-mlp, 1 = tied-rotary-residual-dense-mlp,
- *                2 = shared-neighbor-mesh-mlp, 3 = mlp, 4 = bilinear
+ *                2 = shared-neighbor-mesh-mlp, 3 = mlp, 4 = bilinear,
+ *                5 = residual-mlp
+ *   expansion    residual-mlp's hidden width / width (reference default 4)
  *   activation   0 = relu, 1 = square
  *   connectivity 0 = own, 1 = neighbor, 2 = butterfly
  *   full_mesh_initialization 0 = kaiming, 1 = identity-hidden
@@ -243,6 +245,7 @@ typedef struct mb_simple_config {
   uint32_t embedding_mesh_depth;
   uint32_t full_mesh_initialization;
   uint32_t mesh_learning_rate_multiplier;
+  uint32_t expansion;
 } mb_simple_config;
 
 typedef struct mb_simple mb_simple;

@@ -2,8 +2,8 @@
 restatement of the forward pass, loss and gradients (test infrastructure
 only: the checker of the CUDA path, never the product).
 
-Covers the three architectures of the benchmark configurations and the two
-dense-only ones:
+Covers the three architectures of the benchmark configurations and three
+more:
 
 * ``mesh-mlp`` (``src/simple/mod.rs:42-46``): dense input layer, ``depth-1``
   two-parent mesh layers with the activation on their inputs, dense readout.
@@ -18,6 +18,9 @@ dense-only ones:
   bias-free dense layers, dense readout.
 * ``bilinear`` (``:77-78``): the elementwise product of separate ``a`` and
   ``b`` embeddings, read out by a dense layer.
+* ``residual-mlp`` (``:60-62``): a dense operand embedding, ``depth``
+  pre-RMSNorm feed-forward blocks (width -> width * expansion -> width)
+  with residual sums, a final RMSNorm and a dense readout.
 
 Sources: ``SimpleConfig`` validation / layout / init / encode
 (``src/simple/mod.rs:500-1055``), the f64 tape model
@@ -42,7 +45,8 @@ from .rng import Random
 RMSNORM_EPSILON = 1e-5  # src/gpt/mod.rs:39 (f32 1e-5 widened)
 EPS = float(np.float32(RMSNORM_EPSILON))
 MAX_WIDTH, MAX_DEPTH, MAX_CLASSES = 16384, 64, 1024  # src/simple/mod.rs:25-31
-ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear")
+ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear",
+                 "residual-mlp")
 
 
 def butterfly_stride(width: int, layer: int) -> int:
@@ -67,6 +71,7 @@ class SimpleConfig:
     full_mesh_initialization: str = "kaiming"  # or "identity-hidden"
     mesh_learning_rate_multiplier: int = 1
     encoding: str = "one-hot"  # or "scalar"
+    expansion: int = 4  # residual-mlp hidden width / width
 
     def with_(self, **kw):
         return replace(self, **kw)
@@ -89,7 +94,9 @@ class SimpleConfig:
             raise ValueError(f"depth must be in 1..={MAX_DEPTH}")
         if self.encoding not in ("one-hot", "scalar"):
             raise ValueError("unknown encoding")
-        if self.encoding != "one-hot" and a not in ("mesh-mlp", "mlp", "bilinear"):
+        if a == "residual-mlp" and not 1 <= self.width * self.expansion <= MAX_WIDTH:
+            raise ValueError(f"residual hidden width must be in 1..={MAX_WIDTH}")
+        if self.encoding != "one-hot" and a not in ("mesh-mlp", "mlp", "bilinear", "residual-mlp"):
             raise ValueError("rotary roles need one-hot encoding and a positive even width")
         if a == "shared-neighbor-mesh-mlp" and not 1 <= self.embedding_mesh_depth <= MAX_DEPTH:
             raise ValueError("shared Neighbor embedding depth must be in 1..=64")
@@ -139,6 +146,9 @@ class SimpleConfig:
             return [(2 * f, w)] + [(w, w)] * (self.depth - 1) + [(w, m)]
         if self.architecture == "bilinear":
             return [(f, w), (f, w), (w, m)]
+        if self.architecture == "residual-mlp":
+            hidden = w * self.expansion
+            return [(2 * f, w)] + [(w, hidden), (hidden, w)] * self.depth + [(w, m)]
         if self.architecture == "tied-rotary-residual-dense-mlp":
             return [(m, w)] + [(w, w)] * self.depth
         return []
@@ -295,6 +305,19 @@ class ReferenceSimpleModel:
                 out = c.layers()[layer][1]
                 zs.append(acts[-1] @ g[layer].reshape(-1, out))
             return zs[-1], dict(x=x, zs=zs, acts=acts)
+        if c.architecture == "residual-mlp":
+            # src/simple/reference.rs:418-433
+            hidden = w * c.expansion
+            h = x @ g[0].reshape(-1, w)
+            blocks = []
+            for block in range(c.depth):
+                n, inv = _rmsnorm(h)
+                e = n @ g[1 + 2 * block].reshape(w, hidden)
+                act = _act(c, e)
+                blocks.append((n, inv, e, act))
+                h = h + act @ g[2 + 2 * block].reshape(hidden, w)
+            hf, invf = _rmsnorm(h)
+            return hf @ g[1 + 2 * c.depth].reshape(w, m), dict(x=x, blocks=blocks, hf=hf, invf=invf)
         if c.architecture == "bilinear":
             # src/simple/reference.rs:434-444
             f = c.operand_features()
@@ -391,6 +414,21 @@ class ReferenceSimpleModel:
                 grads[layer] = (s["acts"][layer - 1].T @ dz).reshape(-1)
                 dz = (dz @ g[layer].reshape(-1, out).T) * _act_grad(c, s["zs"][layer - 1])
             grads[0] = (s["x"].T @ dz).reshape(-1)
+            return loss, np.concatenate(grads)
+        if c.architecture == "residual-mlp":
+            hidden, d = w * c.expansion, c.depth
+            readout = g[1 + 2 * d].reshape(w, m)
+            grads[1 + 2 * d] = (s["hf"].T @ dlog).reshape(-1)
+            dh = _rmsnorm_backward(s["hf"], s["invf"], dlog @ readout.T)
+            for block in reversed(range(d)):
+                n, inv, e, act = s["blocks"][block]
+                down = g[2 + 2 * block].reshape(hidden, w)
+                up = g[1 + 2 * block].reshape(w, hidden)
+                grads[2 + 2 * block] = (act.T @ dh).reshape(-1)
+                de = (dh @ down.T) * _act_grad(c, e)
+                grads[1 + 2 * block] = (n.T @ de).reshape(-1)
+                dh = dh + _rmsnorm_backward(n, inv, de @ up.T)
+            grads[0] = (s["x"].T @ dh).reshape(-1)
             return loss, np.concatenate(grads)
         if c.architecture == "bilinear":
             f = c.operand_features()

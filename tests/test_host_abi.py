@@ -163,7 +163,7 @@ def test_simple_validation_mirrors_the_reference():
         with pytest.raises(MeshError):
             SimpleConfig(**kw).validate()
     with pytest.raises(ValueError):
-        SimpleConfig(architecture="residual-mlp").to_c()
+        SimpleConfig(architecture="residual-mesh-mlp").to_c()
     # the library's own counts for the two dense-only architectures
     assert SimpleConfig(architecture="mlp", modulus=97, width=128, depth=2).parameter_count() == 53632
     assert SimpleConfig(architecture="bilinear", modulus=97, width=16, depth=0).validate().parameter_count() == 4656

@@ -35,6 +35,8 @@ SMALL = [
     dict(architecture="mlp", modulus=7, width=32, depth=3),
     dict(architecture="mlp", modulus=11, width=20, depth=1, activation="square"),
     dict(architecture="bilinear", modulus=13, width=24),
+    dict(architecture="residual-mlp", modulus=7, width=32, depth=2, expansion=3),
+    dict(architecture="residual-mlp", modulus=11, width=40, depth=1, expansion=2, activation="square"),
 ]
 FULL = [dict(GROK[name]["config"], modulus=97) for name in ("cfg0", "cfg1", "cfg2")]
 
@@ -197,9 +199,10 @@ def test_invalid_inputs_fail_before_launch():
 @pytest.mark.parametrize("case", PINS["grok_simple_models"]["cases"],
                          ids=lambda c: "-".join(str(v) for v in c["config"].values()))
 def test_archived_mlp_and_bilinear_accuracies(case):
-    """The archived accuracy histories of the mlp and bilinear runs, replayed
-    on the device: step 0 (seeded split, init and forward) to one row, step
-    250 (25 warmed epochs of AdamW) to 2e-3."""
+    """The archived accuracy histories of the mlp, bilinear and residual-mlp
+    runs, replayed on the device: step 0 (seeded split, init and forward) to
+    one row, step 250 (25 warmed epochs of AdamW) to 2e-3 (5e-3 for
+    residual-mlp, see the oracle test)."""
     opt = PINS["grok_simple_models"]["optimizer"]
     config = SimpleConfig(modulus=97, **case["config"])
     records = train_records(config, 0, opt["operation"], opt["train_fraction"], opt["seed"], steps=250,
@@ -208,4 +211,5 @@ def test_archived_mlp_and_bilinear_accuracies(case):
                                                    weight_decay=opt["weight_decay"], beta1=opt["beta1"],
                                                    beta2=opt["beta2"], epsilon=opt["epsilon"]))
     assert abs(records[0][2] - case["step0"][0]) <= 1.5 / 4656 and abs(records[0][3] - case["step0"][1]) <= 1.5 / 4656
-    assert abs(records[1][2] - case["step250"][0]) <= 2e-3 and abs(records[1][3] - case["step250"][1]) <= 2e-3
+    tol = case.get("step250_tolerance", 2e-3)
+    assert abs(records[1][2] - case["step250"][0]) <= tol and abs(records[1][3] - case["step250"][1]) <= tol

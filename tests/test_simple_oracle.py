@@ -47,7 +47,8 @@ def test_validation_rejects_what_the_reference_rejects():
         SimpleConfig("mesh-mlp", depth=0),
         SimpleConfig("mesh-mlp", depth=65),
         SimpleConfig("mesh-mlp", modulus=1),
-        SimpleConfig("residual-mlp"),  # outside this restatement
+        SimpleConfig("residual-mesh-mlp"),  # outside this restatement
+        SimpleConfig("residual-mlp", width=8, expansion=0),
         SimpleConfig("tied-rotary-residual-dense-mlp", encoding="scalar"),
         SimpleConfig("mlp", depth=0),
     ]
@@ -61,6 +62,9 @@ def test_bilinear_ignores_depth_and_mlp_counts_its_layers():
     assert SimpleConfig("bilinear", modulus=97, width=16, depth=0).validate().parameter_count() == 4656
     assert SimpleConfig("mlp", modulus=97, width=128, depth=1).parameter_count() == 37248
     assert SimpleConfig("mlp", modulus=97, width=128, depth=2).parameter_count() == 53632
+    # the archived residual-mlp runs' counts (summary.json settings.parameters)
+    assert SimpleConfig("residual-mlp", modulus=97, width=128, depth=1).parameter_count() == 168320
+    assert SimpleConfig("residual-mlp", modulus=97, width=64, depth=2).parameter_count() == 84160
 
 
 def test_known_answer_models():
@@ -68,7 +72,7 @@ def test_known_answer_models():
     for case in PINS["simple_kats"]["cases"]:
         model = ReferenceSimpleModel(SimpleConfig(**case["config"]), parameters=case["parameters"])
         got = model.logits(np.array([case["features"]], dtype=np.float32))[0]
-        assert np.allclose(got, case["logits"], atol=1e-12), (case, got)
+        assert np.allclose(got, case["logits"], atol=case.get("tolerance", 1e-12)), (case, got)
 
 
 @pytest.mark.parametrize("case", PINS["grok_simple_models"]["cases"],
@@ -76,8 +80,10 @@ def test_known_answer_models():
 def test_simple_models_match_archived_accuracies(case):
     """Seeded split, init and forward reproduce the archived step-0
     accuracies exactly; 250 warmed AdamW steps (25 epochs of 9 x 512 + 48)
-    reproduce step 250 to 2e-3 (the depth-2 MLP's FP32 run and this f64
-    restatement end 7 training rows apart; the others agree exactly)."""
+    reproduce step 250 to 2e-3 for mlp and bilinear (the depth-2 MLP's FP32
+    run and this f64 restatement end 7 training rows apart, the others
+    agree exactly) and to 5e-3 for residual-mlp, whose fast memorisation
+    amplifies the FP32 / f64 difference to at most 16 of 4656 rows."""
     opt = PINS["grok_simple_models"]["optimizer"]
     config = SimpleConfig(modulus=97, **case["config"])
     records = train_records(config, opt["operation"], opt["train_fraction"], opt["seed"], steps=250,
@@ -85,7 +91,8 @@ def test_simple_models_match_archived_accuracies(case):
                             weight_decay=opt["weight_decay"], beta1=opt["beta1"], beta2=opt["beta2"],
                             epsilon=opt["epsilon"])
     assert abs(records[0][2] - case["step0"][0]) < 1e-9 and abs(records[0][3] - case["step0"][1]) < 1e-9
-    assert abs(records[1][2] - case["step250"][0]) <= 2e-3 and abs(records[1][3] - case["step250"][1]) <= 2e-3
+    tol = case.get("step250_tolerance", 2e-3)
+    assert abs(records[1][2] - case["step250"][0]) <= tol and abs(records[1][3] - case["step250"][1]) <= tol
 
 
 def test_encode_is_one_hot_a_then_b():
@@ -150,6 +157,8 @@ def test_step10_record_matches_archive(name, tolerance):
     SimpleConfig("mlp", modulus=7, width=8, depth=3),
     SimpleConfig("mlp", modulus=7, width=6, depth=1, activation="square"),
     SimpleConfig("bilinear", modulus=7, width=8),
+    SimpleConfig("residual-mlp", modulus=7, width=8, depth=2, expansion=2),
+    SimpleConfig("residual-mlp", modulus=7, width=6, depth=1, expansion=3, activation="square"),
 ])
 def test_gradient_matches_finite_differences(config):
     rng = np.random.default_rng(0)
