@@ -706,11 +706,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // Threads 0-255 compute (key row = tid % 128 = TMEM lane; thread half
 // tid / 128 takes 16 of each 32-query half), warp 8 streams the A tile
 // (Q, dO), warp 9 issues the MMAs, warp 10 streams the B tile (Q^T, dO^T,
-// LSE, delta).  K lives in TMEM, V in shared memory.  Per query step:
-//   S^T = K Q^T and dP^T = V dO^T (keys on lanes, N = 64 queries);
-//   P^T and dS^T, produced in two 32-query halves: while the compute warps
-//   finish the second half, dV += P^T dO and dK += dS^T Q already run for the
-//   first (K steps 0-3 of the B tiles), then for the second (K steps 4-7).
+// LSE, delta).  K lives in TMEM, V in shared memory.  Per query step the
+// tensor pipe runs S^T = K Q^T, dP^T = V dO^T (keys on lanes, N = 64
+// queries), dV += P^T dO and dK += dS^T Q, and the softmax hides behind it:
+//   * the P phase (P^T from S^T and LSE) runs while dP^T executes;
+//   * the dS phase (dS^T from P^T, dP^T and delta, two 32-query halves)
+//     runs while dV and the first half's dK execute;
+//   * dV and dK complete on separate barriers, so the next step's S^T (over
+//     the P^T columns) queues behind dK and only dP^T (over the dS^T
+//     columns) waits for dK.
 // TMEM: K hi | K lo | dV | dK | S^T then P^T hi | dP^T then dS^T hi | P^T lo
 // | dS^T lo (64 columns each).
 constexpr int kTcKvThreads = 352;
@@ -752,7 +756,7 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
   float* Vl = sm + kTcRows * HD;
   float* tile_a = sm + S::V_FLOATS;
   float* tile_b = tile_a + S::A_FLOATS;
-  __shared__ uint64_t a_full, a_empty, b_full, b_empty, s_full, d_full[2], g_done;
+  __shared__ uint64_t a_full, a_empty, b_full, b_empty, s_full, dp_full, p_full, ds_full[2], v_done, g_done;
   __shared__ TcShared sh;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int k0 = tile_by_work(blockIdx.x, gridDim.x, rows, T, false) * kTcRows;
@@ -765,8 +769,11 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
     tc::bar_init(&b_full, 1);
     tc::bar_init(&b_empty, 1);
     tc::bar_init(&s_full, 1);
-    tc::bar_init(&d_full[0], kTcCompute);
-    tc::bar_init(&d_full[1], kTcCompute);
+    tc::bar_init(&dp_full, 1);
+    tc::bar_init(&p_full, kTcCompute);
+    tc::bar_init(&ds_full[0], kTcCompute);
+    tc::bar_init(&ds_full[1], kTcCompute);
+    tc::bar_init(&v_done, 1);
     tc::bar_init(&g_done, 1);
     tc::bar_init_fence();
     sh.failed = 0;
@@ -830,50 +837,73 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
     const float* Es0 = Ls0 + kTcQ;             // delta of the query step
     bool done = false;
     for (int j = 0; j < n; ++j) {
+      // P phase: P^T = exp2(S^T scale - lse) as soon as S^T is done, while
+      // the tensor cores run dP^T; P stays in registers for the dS phase.
       TC_WAIT_OR_FAIL(&s_full, j & 1);
       TC_WAIT_OR_FAIL(&b_full, j & 1);
       tc::fence_after_sync();
+      float pv[32];
       for (int q2 = 0; q2 < 2; ++q2) {
         // Columns [32 q2 + 16 half, +16) of this query step.
         const int col = 32 * q2 + 16 * half;
         const float* Ls = Ls0 + col;
-        const float* Es = Es0 + col;
-        float s[16], dp[16];
-        tc::tmem_ld16_pair(tS + col + lane, s, tP + col + lane, dp);
+        float s[16];
+        tc::tmem_ld16(tS + col + lane, s);
         const int qh = k0 + j * kTcQ + col;
         const bool full = one_seq && k0 + j * kTcQ + 32 * q2 >= k0 + kTcRows - 1 &&
                           k0 + j * kTcQ + 32 * q2 + 32 <= min(kseq_end, rows);
 #pragma unroll
         for (int c = 0; c < 16; c += 4) {
           const float4 l4 = *reinterpret_cast<const float4*>(Ls + c);
-          const float4 e4 = *reinterpret_cast<const float4*>(Es + c);
 #pragma unroll
           for (int u = 0; u < 4; u += 2) {
             const float2 lv = u == 0 ? make_float2(l4.x, l4.y) : make_float2(l4.z, l4.w);
-            const float2 ev = u == 0 ? make_float2(e4.x, e4.y) : make_float2(e4.z, e4.w);
             const int q0j = qh + c + u;
             const float2 t = fma2(make_float2(s[c + u], s[c + u + 1]), splat2(scale2), make_float2(-lv.x, -lv.y));
             const bool ok0 = full || (q0j >= kr && q0j < ke && q0j < rows && kr < rows);
             const bool ok1 = full || (q0j + 1 >= kr && q0j + 1 < ke && q0j + 1 < rows && kr < rows);
-            const float2 p = make_float2(ok0 ? ex2(t.x) : 0.f, ok1 ? ex2(t.y) : 0.f);
-            const float2 g = mul2(mul2(p, add2(make_float2(dp[c + u], dp[c + u + 1]), make_float2(-ev.x, -ev.y))),
+            s[c + u] = ok0 ? ex2(t.x) : 0.f;
+            s[c + u + 1] = ok1 ? ex2(t.y) : 0.f;
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 16; ++c) pv[16 * q2 + c] = s[c];
+        tc_st_split<16>(tS + col + lane, tPl + col + lane, s);  // P^T hi over S^T
+      }
+      tc::tmem_st_wait();
+      tc::fence_before_sync();
+      tc::bar_arrive(&p_full);
+      // dS phase: dS^T = P^T (dP^T - delta) scale, one 32-query half at a
+      // time, while the tensor cores run dV and the first half's dK.
+      TC_WAIT_OR_FAIL(&dp_full, j & 1);
+      tc::fence_after_sync();
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const int col = 32 * q2 + 16 * half;
+        const float* Es = Es0 + col;
+        float dp[16];
+        tc::tmem_ld16(tP + col + lane, dp);
+#pragma unroll
+        for (int c = 0; c < 16; c += 4) {
+          const float4 e4 = *reinterpret_cast<const float4*>(Es + c);
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {
+            const float2 ev = u == 0 ? make_float2(e4.x, e4.y) : make_float2(e4.z, e4.w);
+            const float2 pp = make_float2(pv[16 * q2 + c + u], pv[16 * q2 + c + u + 1]);
+            const float2 g = mul2(mul2(pp, add2(make_float2(dp[c + u], dp[c + u + 1]), make_float2(-ev.x, -ev.y))),
                                   splat2(scale));
-            s[c + u] = p.x;
-            s[c + u + 1] = p.y;
             dp[c + u] = g.x;
             dp[c + u + 1] = g.y;
           }
         }
-        tc_st_split<16>(tS + col + lane, tPl + col + lane, s);   // P^T hi over S^T
         tc_st_split<16>(tP + col + lane, tSl + col + lane, dp);  // dS^T hi over dP^T
         tc::tmem_st_wait();
         tc::fence_before_sync();
-        tc::bar_arrive(&d_full[q2]);
+        tc::bar_arrive(&ds_full[q2]);
       }
-      // The next step's S^T / dP^T overwrite these columns: wait for dV/dK.
-      TC_WAIT_OR_FAIL(&g_done, j & 1);
       if (j + 1 == n) done = true;
     }
+    // dV and dK of the last step complete before the accumulators are read.
+    if (done && !tc::bar_wait(&g_done, (n - 1) & 1)) sh.failed = 1;
     tc::fence_after_sync();
     if (done && !sh.failed) {
       const bool in = kr < rows;
@@ -925,22 +955,36 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
     for (int j = 0; j < n; ++j) {
       TC_WAIT_OR_FAIL(&a_full, j & 1);
       if (j >= 1) {
-        TC_WAIT_OR_FAIL(&g_done, (j - 1) & 1);  // dV/dK of step j-1 have read P^T / dS^T
+        TC_WAIT_OR_FAIL(&v_done, (j - 1) & 1);  // dV of step j-1 has read P^T (the S^T columns)
       }
       tc::fence_after_sync();
       mma_tmem_a<HD>(tS, tKh, tKl, tile_a + F::Q_HI * F::QPART, tile_a + F::Q_LO * F::QPART, idS, false);  // S^T
-      mma_smem_a<HD>(tP, Vh, Vl, tile_a + F::D_HI * F::QPART, tile_a + F::D_LO * F::QPART, idS, false);    // dP^T
       tc::commit(&s_full);
+      if (j >= 1) {
+        TC_WAIT_OR_FAIL(&g_done, (j - 1) & 1);  // dK of step j-1 has read dS^T (the dP^T columns)
+      }
+      tc::fence_after_sync();
+      mma_smem_a<HD>(tP, Vh, Vl, tile_a + F::D_HI * F::QPART, tile_a + F::D_LO * F::QPART, idS, false);    // dP^T
+      tc::commit(&dp_full);
       tc::commit(&a_empty);
       TC_WAIT_OR_FAIL(&b_full, j & 1);
       const float* qt = tile_b;                   // Q^T, Q^T'
       const float* dot = tile_b + 2 * F::QPART;   // dO^T, dO^T'
-      for (int q2 = 0; q2 < 2; ++q2) {
-        TC_WAIT_OR_FAIL(&d_full[q2], j & 1);
+      TC_WAIT_OR_FAIL(&p_full, j & 1);
+      tc::fence_after_sync();
+      // dV += P^T dO over the step's 64 queries
+      mma_tmem_a_steps<kTcQ, 8>(tdV, tS, tPl, dot, dot + F::QPART, idG, j > 0, 0);
+      tc::commit(&v_done);
+      bool ok = true;
+      for (int q2 = 0; q2 < 2 && ok; ++q2) {
+        ok = tc::bar_wait(&ds_full[q2], j & 1);
         tc::fence_after_sync();
-        // dV += P^T dO, dK += dS^T Q over queries [32 q2, 32 q2 + 32) (K steps 4 q2 .. 4 q2 + 3)
-        mma_tmem_a_steps<kTcQ, 4>(tdV, tS, tPl, dot, dot + F::QPART, idG, j > 0 || q2 > 0, 4 * q2);
-        mma_tmem_a_steps<kTcQ, 4>(tdK, tP, tSl, qt, qt + F::QPART, idG, j > 0 || q2 > 0, 4 * q2);
+        // dK += dS^T Q over queries [32 q2, 32 q2 + 32) (K steps 4 q2 .. 4 q2 + 3)
+        if (ok) mma_tmem_a_steps<kTcQ, 4>(tdK, tP, tSl, qt, qt + F::QPART, idG, j > 0 || q2 > 0, 4 * q2);
+      }
+      if (!ok) {
+        sh.failed = 1;
+        break;
       }
       tc::commit(&g_done);
       tc::commit(&b_empty);
