@@ -28,7 +28,7 @@ c_u8_p = ctypes.POINTER(ctypes.c_uint8)
 class GptConfigC(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint32) for n in (
         "vocab_size", "context", "width", "heads", "layers",
-        "attention_mesh_depth", "ffn_mesh_depth", "connectivity")]
+        "attention_mesh_depth", "ffn_mesh_depth", "connectivity", "embedding")]
 
 
 class SimpleConfigC(ctypes.Structure):

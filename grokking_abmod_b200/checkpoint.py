@@ -1,7 +1,7 @@
 """Weight checkpoints in the reference's formats.
 
 ``Checkpoint`` mirrors ``src/gpt/checkpoint.rs`` (MSHGPT07 for the default
-architecture, MSHGPT08 for butterfly connectivity): the configuration, the
+architecture, MSHGPT08 for a table embedding or butterfly connectivity): the configuration, the
 character tokenizer and the FP32 parameters, read and written by the C ABI
 (``mb_gpt_checkpoint_write`` / ``mb_gpt_checkpoint_read``).  Loading into a
 model goes through ``set_parameters``, which resets AdamW as the reference's
@@ -52,7 +52,8 @@ class Checkpoint:
         check(lib.mb_gpt_checkpoint_read(os.fsencode(path), ctypes.byref(c), ptr(codes, ctypes.c_uint32),
                                          ctypes.byref(nc), ptr(params, ctypes.c_float), ctypes.byref(npar)))
         config = GptConfig(c.vocab_size, c.context, c.width, c.heads, c.layers, c.attention_mesh_depth,
-                           c.ffn_mesh_depth, "butterfly" if c.connectivity else "neighbor")
+                           c.ffn_mesh_depth, "butterfly" if c.connectivity else "neighbor",
+                           "table" if c.embedding else "mesh")
         return cls(config, "".join(chr(int(x)) for x in codes), params)
 
     @classmethod

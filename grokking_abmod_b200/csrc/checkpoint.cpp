@@ -4,8 +4,8 @@
 // and the parameters as little-endian f32, with nothing after them.
 // MSHGPT07 is the default architecture (mesh token embedding, Neighbor
 // connectivity); MSHGPT08 adds the (embedding, connectivity) fields.  The
-// MSHGPT09 geometry ablations and table embeddings are outside this build's
-// kernels and load as MB_ERR_UNSUPPORTED.  Loading a checkpoint into a model
+// MSHGPT09 geometry ablations are outside this build's kernels and load as
+// MB_ERR_UNSUPPORTED.  Loading a checkpoint into a model
 // goes through set_parameters, which resets AdamW as the reference's loader
 // does.
 
@@ -59,7 +59,7 @@ void write_checkpoint(const std::string& path, const mb_gpt_config& c, const uin
   validate_characters(chars, n_chars);
   for (size_t i = 0; i < n_params; ++i)
     require(std::isfinite(params[i]), "checkpoint parameters must be finite", MB_ERR_NONFINITE);
-  const bool default_layout = c.connectivity == 0;
+  const bool default_layout = c.connectivity == 0 && c.embedding == 0;
   std::vector<unsigned char> out;
   out.reserve(8 + 4 * (9 + n_chars + n_params));
   const char* magic = default_layout ? "MSHGPT07" : "MSHGPT08";
@@ -67,7 +67,7 @@ void write_checkpoint(const std::string& path, const mb_gpt_config& c, const uin
   for (uint32_t f : {c.vocab_size, c.context, c.width, c.heads, c.layers, c.attention_mesh_depth, c.ffn_mesh_depth})
     put_u32(out, f);
   if (!default_layout) {
-    put_u32(out, 0);  // mesh token embedding
+    put_u32(out, c.embedding);
     put_u32(out, c.connectivity);
   }
   for (size_t i = 0; i < n_chars; ++i) put_u32(out, chars[i]);
@@ -117,13 +117,14 @@ void read_checkpoint(const std::string& path, mb_gpt_config& c, std::vector<uint
   c.attention_mesh_depth = get_u32(in, pos);
   c.ffn_mesh_depth = get_u32(in, pos);
   c.connectivity = 0;
+  c.embedding = 0;
   if (magic == "MSHGPT08") {
     const uint32_t embedding = get_u32(in, pos);
     const uint32_t connectivity = get_u32(in, pos);
     require(embedding <= 1, "unknown checkpoint token embedding");
     require(connectivity <= 1, "unknown checkpoint mesh connectivity");
     require(!(embedding == 0 && connectivity == 0), "the default architecture must use the MSHGPT07 layout");
-    require(embedding == 0, "table token embeddings are outside this build", MB_ERR_UNSUPPORTED);
+    c.embedding = embedding;
     c.connectivity = connectivity;
   }
   validate_config(c);

@@ -30,6 +30,7 @@ void validate_config(const mb_gpt_config& c) {
               c.ffn_mesh_depth <= 256,
           "mesh depths must be in 1..256");
   require(c.connectivity <= 1, "connectivity must be 0 (neighbor) or 1 (butterfly)");
+  require(c.embedding <= 1, "embedding must be 0 (mesh) or 1 (table)");
 }
 
 void validate_kernel_shapes(const mb_gpt_config& c) {
@@ -59,7 +60,9 @@ Layout make_layout(const mb_gpt_config& c) {
     return (int)l.groups.size() - 1;
   };
   const size_t w = c.width;
-  l.embedding = push(2 * w * c.attention_mesh_depth, c.attention_mesh_depth);
+  // A table has no mesh layers (src/gpt/config.rs:366-372).
+  l.embedding = c.embedding == 0 ? push(2 * w * c.attention_mesh_depth, c.attention_mesh_depth)
+                                 : push((size_t)c.vocab_size * w, 0);
   for (uint32_t b = 0; b < c.layers; ++b) {
     BlockGroups g;
     g.query = push(2 * w * c.attention_mesh_depth, c.attention_mesh_depth);
@@ -72,7 +75,16 @@ Layout make_layout(const mb_gpt_config& c) {
   return l;
 }
 
+std::vector<float> tabulated(const mb_gpt_config& mesh, const std::vector<float>& params);
+
 std::vector<float> initial_parameters(const mb_gpt_config& c, uint64_t seed) {
+  if (c.embedding == 1) {
+    // A table draws the mesh model's stream and stores its tabulated
+    // embedding, so both start as one function (src/gpt/config.rs:416-433).
+    mb_gpt_config mesh = c;
+    mesh.embedding = 0;
+    return tabulated(mesh, initial_parameters(mesh, seed));
+  }
   const Layout layout = make_layout(c);
   Random random(seed);
   std::vector<float> p(layout.count(), 0.0f);
@@ -92,6 +104,31 @@ std::vector<float> initial_parameters(const mb_gpt_config& c, uint64_t seed) {
     }
   }
   return p;
+}
+
+// The mesh embedding of every token code in f64 (ELU through expm1), cast to
+// f32, followed by the block parameters (src/gpt/config.rs:515-546).
+std::vector<float> tabulated(const mb_gpt_config& mesh, const std::vector<float>& params) {
+  const uint32_t v = mesh.vocab_size, w = mesh.width, depth = mesh.attention_mesh_depth;
+  const std::vector<float> codes = token_codes(mesh);
+  std::vector<double> cur(codes.begin(), codes.end()), next((size_t)v * w);
+  for (uint32_t layer = 0; layer < depth; ++layer) {
+    const uint32_t stride = (uint32_t)mesh_stride(mesh, (int)layer);
+    for (uint32_t t = 0; t < v; ++t) {
+      const double* in = cur.data() + (size_t)t * w;
+      for (uint32_t ch = 0; ch < w; ++ch) {
+        const size_t p = (size_t)layer * 2 * w + 2 * ch;
+        const double sum = in[ch] * (double)params[p] + in[(ch + stride) % w] * (double)params[p + 1];
+        next[(size_t)t * w + ch] = layer + 1 != depth && sum < 0.0 ? std::expm1(sum) : sum;
+      }
+    }
+    cur.swap(next);
+  }
+  std::vector<float> out;
+  out.reserve((size_t)v * w + params.size() - (size_t)2 * w * depth);
+  for (double x : cur) out.push_back((float)x);
+  out.insert(out.end(), params.begin() + (size_t)2 * w * depth, params.end());
+  return out;
 }
 
 std::vector<float> token_codes(const mb_gpt_config& c) {

@@ -457,9 +457,8 @@ class GptModel {
     const size_t VW = (size_t)cfg_.vocab_size * cfg_.width;
     require(n == VW, "token embedding buffer must hold vocab * width floats");
     MB_CUDA(cudaSetDevice(device_));
-    launch_embedding_forward();
-    MB_CUDA(cudaMemcpyAsync(out, emb_acts_ + VW * cfg_.attention_mesh_depth, VW * sizeof(float),
-                            cudaMemcpyDeviceToHost, stream_));
+    if (!table()) launch_embedding_forward();
+    MB_CUDA(cudaMemcpyAsync(out, final_embedding(), VW * sizeof(float), cudaMemcpyDeviceToHost, stream_));
     MB_CUDA(cudaStreamSynchronize(stream_));
   }
 
@@ -540,9 +539,10 @@ class GptModel {
     // (norm, GEMM, loss, GEMM, norm adjoint) + loss + per block (post,
     // attention, qkv) backward + embedding partials + 2 reduces + embedding
     // bwd + optimizer advance + AdamW
-    const size_t L = cfg_.layers;
-    return 1 + 1 + L * (2 + attention_->forward_launches()) + 5 + 1 + L * (2 + attention_->backward_launches()) + 1 +
-           2 + 1 + 2;
+    // (a table embedding has no embedding mesh forward or backward)
+    const size_t L = cfg_.layers, mesh = table() ? 0 : 1;
+    return 1 + mesh + L * (2 + attention_->forward_launches()) + 5 + 1 + L * (2 + attention_->backward_launches()) +
+           1 + 1 + mesh + mesh + 2;
   }
 
   // ---- data parallelism
@@ -632,7 +632,7 @@ class GptModel {
     ws->emb_partial = a.alloc<float>((size_t)ws->emb_chunks * V * W);
     ws->dE = a.alloc<float>((size_t)V * W);
     ws->att_scratch = a.alloc<float>(attention_->scratch_floats(rows, H, cfg_.layers));
-    ws->emb_mesh_partial = a.alloc<float>((size_t)V * layout_.groups[layout_.embedding].size);
+    if (!table()) ws->emb_mesh_partial = a.alloc<float>((size_t)V * layout_.groups[layout_.embedding].size);
     ws->tokens = a.alloc<uint32_t>(rows);
     ws->targets = a.alloc<uint32_t>(rows);
     ws->supervised = a.alloc<float>(1);
@@ -666,7 +666,9 @@ class GptModel {
     for (size_t gi = 0; gi < layout_.groups.size(); ++gi) {
       const Group& g = layout_.groups[gi];
       int slots;
-      if ((int)gi == layout_.embedding) {
+      if ((int)gi == layout_.embedding && table()) {
+        continue;  // the embedding reduction writes the table's gradient directly
+      } else if ((int)gi == layout_.embedding) {
         ws->part[gi] = ws->emb_mesh_partial;
         slots = V;
       } else {
@@ -680,7 +682,8 @@ class GptModel {
     ws->njobs = (int)jobs.size();
     ws->d_jobs = a.alloc<ReduceJob>(jobs.size());
     MB_CUDA(cudaMemcpy(ws->d_jobs, jobs.data(), jobs.size() * sizeof(ReduceJob), cudaMemcpyHostToDevice));
-    ReduceJob ej{ws->emb_partial, ws->dE, ws->emb_chunks, V * W};
+    ReduceJob ej{ws->emb_partial, table() ? grad_ + layout_.groups[layout_.embedding].offset : ws->dE,
+                 ws->emb_chunks, V * W};
     ws->d_jobs_emb = a.alloc<ReduceJob>(1);
     MB_CUDA(cudaMemcpy(ws->d_jobs_emb, &ej, sizeof(ej), cudaMemcpyHostToDevice));
     return ws;
@@ -695,7 +698,11 @@ class GptModel {
                                                             emb_acts_, et_);
   }
 
+  // A table embedding is the parameter group itself; a mesh embedding is the
+  // last layer of the embedding mesh over the token codes.
+  bool table() const { return cfg_.embedding == 1; }
   const float* final_embedding() const {
+    if (table()) return group(layout_.embedding);
     return emb_acts_ + (size_t)cfg_.vocab_size * cfg_.width * cfg_.attention_mesh_depth;
   }
 
@@ -707,7 +714,7 @@ class GptModel {
     if (with_targets)
       count_supervised<<<1, 1024, 0, stream_>>>(ws.rows, V, ws.tokens, ws.targets, ws.supervised, ws.flags);
     mark("embedding_forward");
-    launch_embedding_forward();
+    if (!table()) launch_embedding_forward();
     for (int b = 0; b < L; ++b) {
       const BlockGroups& bg = layout_.blocks[b];
       mark("qkv_forward");
@@ -772,9 +779,10 @@ class GptModel {
     mark("reduce_partials");
     reduce_partials<<<dim3((V * W + 255) / 256, 1), 256, 0, stream_>>>(ws.d_jobs_emb, 1);
     mark("embedding_backward");
-    embedding_backward<<<V, W, W * sizeof(float), stream_>>>(W, V, cfg_.attention_mesh_depth, cfg_.connectivity,
-                                                             31 - __builtin_clz(W), group(layout_.embedding),
-                                                             emb_acts_, ws.dE, ws.emb_mesh_partial);
+    if (!table())
+      embedding_backward<<<V, W, W * sizeof(float), stream_>>>(W, V, cfg_.attention_mesh_depth, cfg_.connectivity,
+                                                               31 - __builtin_clz(W), group(layout_.embedding),
+                                                               emb_acts_, ws.dE, ws.emb_mesh_partial);
     mark("reduce_partials");
     reduce_partials<<<dim3((ws.max_job + 255) / 256, ws.njobs), 256, 0, stream_>>>(ws.d_jobs, ws.njobs);
     mark("end");

@@ -20,7 +20,8 @@ __all__ = ["GptConfig", "AdamWOptions", "MeshGpt", "IGNORE_TARGET", "parameter_c
 
 @dataclass(frozen=True)
 class GptConfig:
-    """``GptConfig`` (src/gpt/config.rs:22-56); connectivity "neighbor" or "butterfly"."""
+    """``GptConfig`` (src/gpt/config.rs:22-56); connectivity "neighbor" or
+    "butterfly"; embedding "mesh" or "table" (src/gpt/config.rs:60-67)."""
     vocab_size: int = 32
     context: int = 32
     width: int = 32
@@ -29,13 +30,16 @@ class GptConfig:
     attention_mesh_depth: int = 4
     ffn_mesh_depth: int = 6
     connectivity: str = "neighbor"
+    embedding: str = "mesh"
 
     def to_c(self) -> GptConfigC:
         if self.connectivity not in ("neighbor", "butterfly"):
             raise ValueError(f"unknown mesh connectivity: {self.connectivity}")
+        if self.embedding not in ("mesh", "table"):
+            raise ValueError(f"unknown token embedding: {self.embedding}")
         return GptConfigC(self.vocab_size, self.context, self.width, self.heads, self.layers,
                           self.attention_mesh_depth, self.ffn_mesh_depth,
-                          0 if self.connectivity == "neighbor" else 1)
+                          0 if self.connectivity == "neighbor" else 1, 0 if self.embedding == "mesh" else 1)
 
     def with_(self, **kw):
         return replace(self, **kw)

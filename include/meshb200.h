@@ -40,9 +40,12 @@ extern "C" {
 
 #define MB_IGNORE_TARGET 0xFFFFFFFFu /* src/gpt/mod.rs:26 */
 
-/* GptConfig (src/gpt/config.rs:22-56); connectivity 0 = neighbor, 1 = butterfly.
- * The default geometry (parity codes, token order, no normalisation) is the
- * only embedding geometry on this path. */
+/* GptConfig (src/gpt/config.rs:22-56); connectivity 0 = neighbor, 1 = butterfly;
+ * embedding 0 = mesh (fixed token codes through the embedding mesh), 1 = table
+ * (a learned [vocab][width] table, initialised as the tabulated mesh
+ * embedding; src/gpt/config.rs:60-67,416-433).  The default geometry (parity
+ * codes, token order, no normalisation) is the only embedding geometry on
+ * this path. */
 typedef struct mb_gpt_config {
   uint32_t vocab_size;
   uint32_t context;
@@ -52,6 +55,7 @@ typedef struct mb_gpt_config {
   uint32_t attention_mesh_depth;
   uint32_t ffn_mesh_depth;
   uint32_t connectivity;
+  uint32_t embedding;
 } mb_gpt_config;
 
 /* AdamWOptions (src/gpt/config.rs:258-295). */
@@ -188,14 +192,15 @@ int mb_op_mesh_backward_noalloc(const float* x, const float* dy, float* dx, floa
                                 void* stream);
 
 /* ---- checkpoints (src/gpt/checkpoint.rs:25-196) --------------------------
- * MSHGPT07 (default architecture) / MSHGPT08 (butterfly connectivity) files:
+ * MSHGPT07 (default architecture) / MSHGPT08 (table embedding or butterfly
+ * connectivity) files:
  * magic, config as LE u32, the tokenizer's characters as u32 code points,
  * the parameters as LE f32, no trailing bytes.  Write from host arrays
  * (parameters from mb_gpt_get_parameters); read with NULL arrays to query
  * *n_characters / *n_parameters, then again with buffers.  Load into a model
  * with mb_gpt_create + mb_gpt_set_parameters (which resets AdamW, as
- * Checkpoint::load's callers do).  MSHGPT09 geometry ablations and table
- * embeddings return MB_ERR_UNSUPPORTED. */
+ * Checkpoint::load's callers do).  MSHGPT09 geometry ablations return
+ * MB_ERR_UNSUPPORTED. */
 int mb_gpt_checkpoint_write(const char* path, const mb_gpt_config* config, const uint32_t* characters,
                             size_t n_characters, const float* parameters, size_t n_parameters);
 int mb_gpt_checkpoint_read(const char* path, mb_gpt_config* config, uint32_t* characters, size_t* n_characters,

@@ -3,8 +3,9 @@
 
 Restates ``src/gpt/config.rs``: ``GptConfig`` defaults (``:38-56``),
 validation (``:144-172``), connectivity strides (``:117-122``), ``Layout``
-(``:358-414``), ``Layout::initialize`` (``:416-459``, mesh embedding, default
-parity geometry) and ``token_codes`` (``:552-591``).
+(``:358-414``), ``Layout::initialize`` (``:416-459``, default parity
+geometry; a table embedding starts as the tabulated mesh embedding,
+``tabulated`` at ``:515-546``) and ``token_codes`` (``:552-591``).
 """
 
 from dataclasses import dataclass, replace
@@ -28,6 +29,7 @@ class GptConfig:
     attention_mesh_depth: int = 4
     ffn_mesh_depth: int = 6
     connectivity: str = "neighbor"  # or "butterfly"
+    embedding: str = "mesh"  # or "table" (src/gpt/config.rs:60-67)
 
     def validate(self):
         # src/gpt/config.rs:144-172
@@ -47,6 +49,8 @@ class GptConfig:
             raise ValueError("layers must be in 1..64")
         if not (1 <= self.attention_mesh_depth <= 256 and 1 <= self.ffn_mesh_depth <= 256):
             raise ValueError("mesh depths must be in 1..256")
+        if self.embedding not in ("mesh", "table"):
+            raise ValueError("unknown token embedding")
         return self
 
     def stride(self, layer: int) -> int:
@@ -76,7 +80,9 @@ class Layout:
         self.config = config
         self.groups = []
         w, a, f = config.width, config.attention_mesh_depth, config.ffn_mesh_depth
-        self.embedding = self._push(2 * w * a, a)
+        # A table has no mesh layers (src/gpt/config.rs:366-372).
+        self.embedding = (self._push(2 * w * a, a) if config.embedding == "mesh"
+                          else self._push(config.vocab_size * w, 0))
         self.blocks = []
         for _ in range(config.layers):
             q = self._push(2 * w * a, a)
@@ -101,7 +107,12 @@ class Layout:
 
     def initialize(self, seed: int) -> np.ndarray:
         """``src/gpt/config.rs:416-459`` in f32 arithmetic, draw order
-        group -> layer -> channel -> (self, neighbor)."""
+        group -> layer -> channel -> (self, neighbor).  A table embedding
+        draws the mesh model's stream and stores its tabulated embedding, so
+        both start as one function."""
+        if self.config.embedding == "table":
+            mesh = self.config.with_(embedding="mesh")
+            return tabulated(mesh, Layout(mesh).initialize(seed))
         random = Random(seed)
         out = np.zeros(self.count(), dtype=np.float32)
         w = self.config.width
@@ -117,6 +128,21 @@ class Layout:
                         b = b * f(0.3)
                     out[o], out[o + 1] = a, b
         return out
+
+
+def tabulated(config: GptConfig, parameters) -> np.ndarray:
+    """``src/gpt/config.rs:515-546``: the mesh embedding of every token code in
+    f64 (ELU through expm1), cast to f32, followed by the block parameters."""
+    w, depth = config.width, config.attention_mesh_depth
+    p = np.asarray(parameters, dtype=np.float32)
+    vectors = token_codes(config).astype(np.float64)
+    for layer in range(depth):
+        s = config.stride(layer)
+        w0 = p[layer * 2 * w:(layer + 1) * 2 * w:2].astype(np.float64)
+        w1 = p[layer * 2 * w + 1:(layer + 1) * 2 * w:2].astype(np.float64)
+        total = vectors * w0 + np.roll(vectors, -s, axis=1) * w1
+        vectors = np.where(total < 0.0, np.expm1(total), total) if layer + 1 != depth else total
+    return np.concatenate([vectors.astype(np.float32).reshape(-1), p[2 * w * depth:]])
 
 
 def parameter_count(config: GptConfig) -> int:

@@ -200,9 +200,13 @@ class ReferenceGpt:
             raise ValueError("token ID is outside the vocabulary")
         A, F, H = c.attention_mesh_depth, c.ffn_mesh_depth, c.heads
         cache = {"tokens": tokens, "sequence": sequence, "blocks": []}
-        emb_acts = mesh_forward(self.codes, self._w(self.layout.embedding), self._strides(A))
-        E = emb_acts[-1]
-        cache["emb_acts"] = emb_acts
+        if c.embedding == "table":
+            emb_acts = None
+            E = self._table()
+        else:
+            emb_acts = mesh_forward(self.codes, self._w(self.layout.embedding), self._strides(A))
+            E = emb_acts[-1]
+        cache["emb_acts"], cache["E"] = emb_acts, E
         x = E[tokens]
         for block in self.layout.blocks:
             bc = {"x": x}
@@ -238,7 +242,14 @@ class ReferenceGpt:
     def hidden_states(self, tokens, sequence):
         return self.forward(tokens, sequence)[1]["x_final"]
 
+    def _table(self):
+        g = self.layout.groups[self.layout.embedding]
+        return self.parameters[g.offset:g.offset + g.size].astype(np.float64).reshape(
+            self.config.vocab_size, self.config.width)
+
     def token_embeddings(self):
+        if self.config.embedding == "table":
+            return self._table()
         return mesh_forward(self.codes, self._w(self.layout.embedding),
                             self._strides(self.config.attention_mesh_depth))[-1]
 
@@ -276,8 +287,7 @@ class ReferenceGpt:
         t = np.where(sup, targets, 0)
         p[np.arange(len(t)), t] -= 1.0
         dlogits = np.where(sup[:, None], p / count, 0.0)
-        emb_acts = cache["emb_acts"]
-        E = emb_acts[-1]
+        emb_acts, E = cache["emb_acts"], cache["E"]
         dE = dlogits.T @ cache["nf"]
         dx = rmsnorm_backward(cache["nf"], cache["invf"], dlogits @ E, 1)
         H, A, F = c.heads, c.attention_mesh_depth, c.ffn_mesh_depth
@@ -300,8 +310,11 @@ class ReferenceGpt:
                 dn1 += dni
             dx = dxm + rmsnorm_backward(bc["n1"], bc["inv1"], dn1, 1)
         np.add.at(dE, cache["tokens"], dx)
-        _, dw = mesh_backward(emb_acts, self._w(self.layout.embedding), self._strides(A), dE)
-        self._add(grad, self.layout.embedding, dw)
+        if c.embedding == "table":
+            self._add(grad, self.layout.embedding, dE)  # the table's gradient is dE itself
+        else:
+            _, dw = mesh_backward(emb_acts, self._w(self.layout.embedding), self._strides(A), dE)
+            self._add(grad, self.layout.embedding, dw)
         return loss, grad
 
     def _add(self, grad, gid, dw):

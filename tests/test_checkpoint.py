@@ -19,11 +19,12 @@ def _expected_bytes(config, characters, params, magic, extra=()):
     return head + np.asarray(params, dtype="<f4").tobytes()
 
 
-@pytest.mark.parametrize("connectivity,magic,extra", [("neighbor", b"MSHGPT07", ()),
-                                                      ("butterfly", b"MSHGPT08", (0, 1))])
-def test_layout_and_round_trip(tmp_path, connectivity, magic, extra):
+@pytest.mark.parametrize("connectivity,embedding,magic,extra", [
+    ("neighbor", "mesh", b"MSHGPT07", ()), ("butterfly", "mesh", b"MSHGPT08", (0, 1)),
+    ("neighbor", "table", b"MSHGPT08", (1, 0)), ("butterfly", "table", b"MSHGPT08", (1, 1))])
+def test_layout_and_round_trip(tmp_path, connectivity, embedding, magic, extra):
     config = GptConfig(vocab_size=7, context=5, width=8, heads=2, layers=2, attention_mesh_depth=3,
-                       ffn_mesh_depth=2, connectivity=connectivity)
+                       ffn_mesh_depth=2, connectivity=connectivity, embedding=embedding)
     chars = "abc=+\U0001F600"
     params = initial_parameters(config, 7)
     path = tmp_path / "model.ckpt"
@@ -61,8 +62,11 @@ def test_reference_rejections(tmp_path):
         Checkpoint.load(_write(tmp_path / "f", _expected_bytes(config, "abc", bad, b"MSHGPT07")))
     with pytest.raises(MeshError, match="MSHGPT07"):
         Checkpoint.load(_write(tmp_path / "8", _expected_bytes(config, "abc", params, b"MSHGPT08", (0, 0))))
-    with pytest.raises(UnsupportedShape):
+    # a table header over mesh-sized parameters: the table layout is shorter
+    with pytest.raises(MeshError, match="trailing"):
         Checkpoint.load(_write(tmp_path / "tab", _expected_bytes(config, "abc", params, b"MSHGPT08", (1, 0))))
+    with pytest.raises(MeshError, match="embedding"):
+        Checkpoint.load(_write(tmp_path / "e", _expected_bytes(config, "abc", params, b"MSHGPT08", (2, 0))))
     with pytest.raises(UnsupportedShape):
         Checkpoint.load(_write(tmp_path / "9", b"MSHGPT09" + good[8:]))
     surrogate = good[:36] + struct.pack("<I", 0xD800) + good[40:]

@@ -31,6 +31,9 @@ CASES = [
     (dict(vocab_size=64, context=70, width=256, heads=4, layers=2), 3, 70),
     (dict(vocab_size=64, context=130, width=512, heads=8, layers=1), 2, 130),
     (dict(vocab_size=33, context=64, width=384, heads=6, layers=1, attention_mesh_depth=2, ffn_mesh_depth=3), 2, 64),
+    (dict(vocab_size=17, context=8, width=128, heads=4, layers=1, embedding="table"), 6, 8),
+    (dict(vocab_size=64, context=70, width=256, heads=4, layers=2, embedding="table", connectivity="butterfly"), 3,
+     70),
 ]
 
 

@@ -170,3 +170,15 @@ def test_simple_validation_mirrors_the_reference():
     assert SimpleConfig(architecture="mlp", modulus=7, width=9, depth=3).groups() == [14 * 9, 81, 81, 9 * 7]
     with pytest.raises(MeshError):
         SimpleConfig(modulus=7, width=8).encode([(7, 0, 0)])
+
+
+def test_table_embedding_init_matches_the_oracle_bitwise():
+    from oracle.gpt_config import GptConfig as OracleConfig, Layout
+    for connectivity in ("neighbor", "butterfly"):
+        kw = dict(vocab_size=64, context=70, width=256, heads=4, layers=2, connectivity=connectivity)
+        got = initial_parameters(GptConfig(**kw, embedding="table"), 5)
+        want = Layout(OracleConfig(**kw, embedding="table")).initialize(5)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        assert parameter_count(GptConfig(**kw, embedding="table")) == want.size
+    with pytest.raises(ValueError):
+        GptConfig(embedding="dense").to_c()

@@ -251,3 +251,49 @@ def test_grok_epoch_reproduces_archived_reference_run():
     for got, want in zip(start + end, pin["train_cross_entropy"][:1] + pin["validation_cross_entropy"][:1]
                          + pin["train_cross_entropy"][1:] + pin["validation_cross_entropy"][1:]):
         assert abs(got - want) < 1e-6 * abs(want), (got, want)
+
+
+def test_table_embedding_starts_as_the_tabulated_mesh():
+    """src/gpt/config.rs:810-840: a table has vocab * width embedding
+    parameters and no embedding mesh, its initial table is the mesh model's
+    embedding tabulated over the token codes, and the blocks are the mesh
+    model's own; so the two models start as one function."""
+    from oracle.gpt_config import Layout, parameter_count, tabulated
+    for connectivity in ("neighbor", "butterfly"):
+        mesh = GptConfig(vocab_size=99, width=16, attention_mesh_depth=6, connectivity=connectivity)
+        table = mesh.with_(embedding="table")
+        blocks = parameter_count(mesh) - 2 * 16 * 6
+        assert parameter_count(table) == 99 * 16 + blocks
+        layout = Layout(table)
+        assert layout.groups[layout.embedding].size == 99 * 16 and layout.groups[layout.embedding].depth == 0
+        assert all(g.size == 2 * 16 * g.depth for g in layout.groups[1:])
+        init_mesh = Layout(mesh).initialize(5)
+        init_table = layout.initialize(5)
+        assert np.array_equal(init_table, tabulated(mesh, init_mesh))
+        assert np.array_equal(init_table[99 * 16:], init_mesh[2 * 16 * 6:])
+        rm, rt = ReferenceGpt(mesh, init_mesh), ReferenceGpt(table, init_table)
+        assert np.abs(rm.token_embeddings() - rt.token_embeddings()).max() < 1e-7
+        tokens = np.arange(24) % 99
+        targets = (tokens * 7 + 3) % 99
+        lm, gm = rm.loss_and_gradient(tokens, targets, 8)
+        lt, gt = rt.loss_and_gradient(tokens, targets, 8)
+        assert abs(lm - lt) < 1e-7 and np.abs(gm[2 * 16 * 6:] - gt[99 * 16:]).max() < 1e-7
+
+
+def test_table_gradient_matches_finite_differences():
+    from oracle.gpt_config import Layout
+    config = GptConfig(vocab_size=7, context=4, width=8, heads=2, layers=1, attention_mesh_depth=2,
+                       ffn_mesh_depth=2, embedding="table")
+    model = ReferenceGpt(config, seed=3)
+    tokens = np.array([1, 2, 3, 4, 5, 6, 0, 1])
+    targets = np.array([2, 3, 4, 5, 6, 0, 1, 2])
+    _, grad = model.loss_and_gradient(tokens, targets, 4)
+    p0 = model.parameters.astype(np.float64).copy()
+    for i in range(0, 7 * 8, 5):  # table entries
+        h = 1e-4
+        model.parameters = p0.copy(); model.parameters[i] += h
+        lp = model.loss_and_gradient(tokens, targets, 4)[0]
+        model.parameters = p0.copy(); model.parameters[i] -= h
+        lm = model.loss_and_gradient(tokens, targets, 4)[0]
+        model.parameters = p0.copy()
+        assert abs((lp - lm) / (2 * h) - grad[i]) <= 1e-6 + 1e-4 * abs(grad[i])
