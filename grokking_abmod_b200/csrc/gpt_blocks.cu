@@ -46,7 +46,7 @@ __device__ __forceinline__ float xsa_scale(float sq) {
   return sq >= kXsaEpsilon * kXsaEpsilon ? rsqrtf(sq) : 1.0f / kXsaEpsilon;
 }
 
-template <int W, int RPT>
+template <int W, int RPT, class S>
 __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
     qkv_forward(Dims d, const float* __restrict__ x, const uint32_t* __restrict__ tokens,
                 const float* __restrict__ emb, float* __restrict__ x_out, const float* __restrict__ wq,
@@ -85,6 +85,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
       }
     }
     rmsnorm_rows<T>(c, n, inv, red, phase, W);
+#pragma unroll 1
     for (int m = 0; m < 3; ++m) {
       // Selected, not indexed: a pointer array indexed by m would live in local memory.
       const float4* wg = reinterpret_cast<const float4*>(m == 0 ? wq : (m == 1 ? wk : wv));
@@ -92,7 +93,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
       float2 a[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = n[k];
-      mesh_forward<W, T>(c, d, a, wg, d.attn_depth, bufs, false);
+      mesh_forward<W, T, S::A, S::CONN>(c, d, a, wg, S::attn(d), bufs, false);
 #pragma unroll
       for (int k = 0; k < RPT; ++k) {
         const int r = tile * T::TR + c.row(k);
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
   }
 }
 
-template <int W, int RPT>
+template <int W, int RPT, class S>
 __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
     post_forward(Dims d, const float* __restrict__ o, const float* __restrict__ v, const float* __restrict__ x,
                  const float* __restrict__ wo, const float* __restrict__ wf, float* __restrict__ xmid_out,
@@ -137,7 +138,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
       float proj = head_sum(y.x * u.x + y.y * u.y, hp);
       a[k] = make_float2(y.x - proj * u.x, y.y - proj * u.y);
     }
-    mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(wo), d.attn_depth, bufs, false);
+    mesh_forward<W, T, S::A, S::CONN>(c, d, a, reinterpret_cast<const float4*>(wo), S::attn(d), bufs, false);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
       res[k] = res[k] + a[k];
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
     float inv[RPT];
     __syncthreads();
     rmsnorm_rows<T>(c, a, inv, red, phase, W);
-    mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(wf), d.ffn_depth, bufs, false);
+    mesh_forward<W, T, S::F, S::CONN>(c, d, a, reinterpret_cast<const float4*>(wf), S::ffn(d), bufs, false);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) st2(xnext_out, tile * T::TR + c.row(k), d.rows, W, c.cp, res[k] + a[k]);
     __syncthreads();
@@ -169,7 +170,7 @@ __device__ __forceinline__ void zero_slots(const Ctx<T>& c, float4* acc, int lay
   for (int l = 0; l < layers; ++l) acc[l * T::NT + c.tid] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-template <int W, int RPT>
+template <int W, int RPT, class S>
 __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
     post_backward(Dims d, const float* __restrict__ dxn, const float* __restrict__ xmid, const float* __restrict__ o,
                   const float* __restrict__ v, const float* __restrict__ wo, const float* __restrict__ wf,
@@ -177,16 +178,17 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
                   float* __restrict__ delta_out, float* __restrict__ part_o, float* __restrict__ part_f) {
   using T = RowTile<W, RPT>;
   extern __shared__ float4 smem4[];
-  const int dmax = d.ffn_depth > d.attn_depth ? d.ffn_depth : d.attn_depth;
-  float4* acc_f = smem4;                           // ffn_depth * NT slots
-  float4* acc_o = smem4 + d.ffn_depth * T::NT;     // attn_depth * NT slots
-  float* smem = reinterpret_cast<float*>(smem4 + (d.ffn_depth + d.attn_depth) * T::NT);
+  const int A = S::attn(d), F = S::ffn(d);
+  const int dmax = F > A ? F : A;
+  float4* acc_f = smem4;                 // F * NT slots
+  float4* acc_o = smem4 + F * T::NT;     // A * NT slots
+  float* smem = reinterpret_cast<float*>(smem4 + (F + A) * T::NT);
   float* bufs = smem;                              // dmax activation buffers
   float* xch = smem + dmax * T::BUF;               // 2 exchange buffers
   float* red = xch + 2 * T::BUF;
   Ctx<T> c;
-  zero_slots<T>(c, acc_f, d.ffn_depth);
-  zero_slots<T>(c, acc_o, d.attn_depth);
+  zero_slots<T>(c, acc_f, F);
+  zero_slots<T>(c, acc_o, A);
   int phase = 0;
   const int hp = d.head_width / 2;
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
@@ -205,7 +207,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       float2 a[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = n2[k];
-      mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(wf), d.ffn_depth, bufs, true);
+      mesh_forward<W, T, S::F, S::CONN>(c, d, a, reinterpret_cast<const float4*>(wf), S::ffn(d), bufs, true);
     }
     // O and V of the attention path, in flight during the FFN backward.
     float2 y[RPT], vv[RPT];
@@ -216,7 +218,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       vv[k] = ld2<T>(v, r, d.rows, W, c.cp);
       dy[k] = g[k];
     }
-    mesh_backward<W, T>(c, d, dy, reinterpret_cast<const float4*>(wf), d.ffn_depth, bufs, xch, acc_f);
+    mesh_backward<W, T, S::F, S::CONN>(c, d, dy, reinterpret_cast<const float4*>(wf), S::ffn(d), bufs, xch, acc_f);
     rmsnorm_rows_backward<T>(c, n2, inv2, dy, red, phase, W);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) g[k] = g[k] + dy[k];  // dx_mid
@@ -235,11 +237,11 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       float2 a[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = make_float2(y[k].x - proj[k] * u[k].x, y[k].y - proj[k] * u[k].y);
-      mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(wo), d.attn_depth, bufs, true);
+      mesh_forward<W, T, S::A, S::CONN>(c, d, a, reinterpret_cast<const float4*>(wo), S::attn(d), bufs, true);
     }
 #pragma unroll
     for (int k = 0; k < RPT; ++k) dy[k] = g[k];
-    mesh_backward<W, T>(c, d, dy, reinterpret_cast<const float4*>(wo), d.attn_depth, bufs, xch, acc_o);
+    mesh_backward<W, T, S::A, S::CONN>(c, d, dy, reinterpret_cast<const float4*>(wo), S::attn(d), bufs, xch, acc_o);
     // XSA backward (src/gpt/gpu.rs:861-897); dy is dL/dz.
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
@@ -263,14 +265,14 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
     }
     __syncthreads();
   }
-  flush_partials<T>(c, acc_f, d.ffn_depth, part_f);
-  flush_partials<T>(c, acc_o, d.attn_depth, part_o);
+  flush_partials<T>(c, acc_f, F, part_f);
+  flush_partials<T>(c, acc_o, A, part_o);
 }
 
 // Register budget: shared memory limits the backward kernels to three CTAs
 // of 256 threads per SM at width 512, so ptxas gets the registers three CTAs
 // allow (85) instead of spilling to fit CTAs that shared memory would not admit.
-template <int W, int RPT>
+template <int W, int RPT, class S>
 __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
     qkv_backward(Dims d, const float* __restrict__ dq, const float* __restrict__ dk, const float* __restrict__ dv,
                  const float* __restrict__ x, const float* __restrict__ dxm, const float* __restrict__ wq,
@@ -279,7 +281,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
                  float* __restrict__ part_v) {
   using T = RowTile<W, RPT>;
   extern __shared__ float4 smem4[];
-  const int A = d.attn_depth;
+  const int A = S::attn(d);
   float4* accs = smem4;  // 3 * A * NT slots
   float* smem = reinterpret_cast<float*>(smem4 + 3 * A * T::NT);
   float* bufs = smem;
@@ -303,6 +305,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       dn[k] = make_float2(0.f, 0.f);
     }
     rmsnorm_rows<T>(c, n1, inv1, red, phase, W);
+#pragma unroll 1
     for (int m = 0; m < 3; ++m) {
       const float4* wg = reinterpret_cast<const float4*>(m == 0 ? wq : (m == 1 ? wk : wv));
       const float* grad = m == 0 ? dq : (m == 1 ? dk : dv);
@@ -310,7 +313,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = n1[k];
       __syncthreads();  // the previous mesh backward may still read bufs
-      mesh_forward<W, T>(c, d, a, wg, A, bufs, true);
+      mesh_forward<W, T, S::A, S::CONN>(c, d, a, wg, A, bufs, true);
       float2 gm[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) {
@@ -327,7 +330,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
         }
         gm[k] = gg;
       }
-      mesh_backward<W, T>(c, d, gm, wg, A, bufs, xch, accs + m * A * T::NT);
+      mesh_backward<W, T, S::A, S::CONN>(c, d, gm, wg, A, bufs, xch, accs + m * A * T::NT);
 #pragma unroll
       for (int k = 0; k < RPT; ++k) dn[k] = dn[k] + gm[k];
     }

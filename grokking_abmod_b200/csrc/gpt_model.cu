@@ -89,7 +89,7 @@ struct BlockOps {
 constexpr int kRptForward = 4;
 constexpr int kRptBackward = 2;
 
-template <int W>
+template <int W, class S>
 struct BlockOpsW final : BlockOps {
   using TF = RowTile<W, kRptForward>;
   using TB = RowTile<W, kRptBackward>;
@@ -111,40 +111,50 @@ struct BlockOpsW final : BlockOps {
     require(occ_qf > 0 && occ_pf > 0 && occ_pb > 0 && occ_qb > 0,
             "fused block kernels do not fit on this device for these mesh depths", MB_ERR_UNSUPPORTED);
   }
-  static auto qkv_forward_k() { return &mb::qkv_forward<W, kRptForward>; }
-  static auto post_forward_k() { return &mb::post_forward<W, kRptForward>; }
-  static auto post_backward_k() { return &mb::post_backward<W, kRptBackward>; }
-  static auto qkv_backward_k() { return &mb::qkv_backward<W, kRptBackward>; }
+  static auto qkv_forward_k() { return &mb::qkv_forward<W, kRptForward, S>; }
+  static auto post_forward_k() { return &mb::post_forward<W, kRptForward, S>; }
+  static auto post_backward_k() { return &mb::post_backward<W, kRptBackward, S>; }
+  static auto qkv_backward_k() { return &mb::qkv_backward<W, kRptBackward, S>; }
   void qkv_forward(cudaStream_t s, int grid, const Dims& d, const float* x, const uint32_t* tokens,
                    const float* emb, float* x_out, const float* wq, const float* wk, const float* wv,
                    const float2* rope, float* q, float* k, float* v) override {
-    mb::qkv_forward<W, kRptForward><<<grid, TF::NT, smem_f, s>>>(d, x, tokens, emb, x_out, wq, wk, wv, rope, q, k, v);
+    qkv_forward_k()<<<grid, TF::NT, smem_f, s>>>(d, x, tokens, emb, x_out, wq, wk, wv, rope, q, k, v);
   }
   void post_forward(cudaStream_t s, int grid, const Dims& d, const float* o, const float* v, const float* x,
                     const float* wo, const float* wf, float* xm, float* xn) override {
-    mb::post_forward<W, kRptForward><<<grid, TF::NT, smem_f, s>>>(d, o, v, x, wo, wf, xm, xn);
+    post_forward_k()<<<grid, TF::NT, smem_f, s>>>(d, o, v, x, wo, wf, xm, xn);
   }
   void post_backward(cudaStream_t s, int grid, const Dims& d, const float* dxn, const float* xm, const float* o,
                      const float* v, const float* wo, const float* wf, float* dO, float* dvx, float* dxm,
                      float* delta, float* part_o, float* part_f) override {
-    mb::post_backward<W, kRptBackward><<<grid, TB::NT, smem_pb, s>>>(d, dxn, xm, o, v, wo, wf, dO, dvx, dxm, delta,
+    post_backward_k()<<<grid, TB::NT, smem_pb, s>>>(d, dxn, xm, o, v, wo, wf, dO, dvx, dxm, delta,
                                                                      part_o, part_f);
   }
   void qkv_backward(cudaStream_t s, int grid, const Dims& d, const float* dq, const float* dk, const float* dv,
                     const float* x, const float* dxm, const float* wq, const float* wk, const float* wv,
                     const float2* rope, float* dx, float* pq, float* pk, float* pv) override {
-    mb::qkv_backward<W, kRptBackward><<<grid, TB::NT, smem_qb, s>>>(d, dq, dk, dv, x, dxm, wq, wk, wv, rope, dx, pq,
+    qkv_backward_k()<<<grid, TB::NT, smem_qb, s>>>(d, dq, dk, dv, x, dxm, wq, wk, wv, rope, dx, pq,
                                                                     pk, pv);
   }
 };
 
-std::unique_ptr<BlockOps> make_block_ops(int W, int A, int F) {
+// The reference's default mesh depths (attention 4, FFN 6; src/gpt/config.rs:46-47)
+// get kernels with the shape compiled in; other depths run the same kernels
+// with the shape read at run time.
+template <int W>
+std::unique_ptr<BlockOps> make_block_ops_w(int A, int F, int conn) {
+  if (A == 4 && F == 6 && conn == 0) return std::make_unique<BlockOpsW<W, MeshShape<4, 6, 0>>>(A, F);
+  if (A == 4 && F == 6 && conn == 1) return std::make_unique<BlockOpsW<W, MeshShape<4, 6, 1>>>(A, F);
+  return std::make_unique<BlockOpsW<W, RuntimeShape>>(A, F);
+}
+
+std::unique_ptr<BlockOps> make_block_ops(int W, int A, int F, int conn) {
   switch (W) {
-    case 64: return std::make_unique<BlockOpsW<64>>(A, F);
-    case 128: return std::make_unique<BlockOpsW<128>>(A, F);
-    case 256: return std::make_unique<BlockOpsW<256>>(A, F);
-    case 384: return std::make_unique<BlockOpsW<384>>(A, F);
-    case 512: return std::make_unique<BlockOpsW<512>>(A, F);
+    case 64: return make_block_ops_w<64>(A, F, conn);
+    case 128: return make_block_ops_w<128>(A, F, conn);
+    case 256: return make_block_ops_w<256>(A, F, conn);
+    case 384: return make_block_ops_w<384>(A, F, conn);
+    case 512: return make_block_ops_w<512>(A, F, conn);
   }
   throw Error(MB_ERR_UNSUPPORTED, "unsupported width");
 }
@@ -345,7 +355,7 @@ class GptModel {
     require(prop.major >= 10, "this library is built for sm_100a (B200)", MB_ERR_UNSUPPORTED);
     sms_ = prop.multiProcessorCount;
     MB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
-    blocks_ = make_block_ops(cfg.width, cfg.attention_mesh_depth, cfg.ffn_mesh_depth);
+    blocks_ = make_block_ops(cfg.width, cfg.attention_mesh_depth, cfg.ffn_mesh_depth, (int)cfg.connectivity);
     tc_err_ = mem_.alloc<int>(1);
     MB_CUDA(cudaMemset(tc_err_, 0, sizeof(int)));
     attention_ = make_attention_ops(cfg.width / cfg.heads, tc_err_);

@@ -47,6 +47,50 @@ __device__ __forceinline__ int mesh_stride(const Dims& d, int layer) {
   return d.connectivity == 0 ? 1 : (1 << (layer % d.log2w));
 }
 
+// Mesh-stack shape fixed at compile time: attention and FFN depths (0 = read
+// from Dims at run time) and connectivity (-1 = read from Dims).  With a
+// fixed shape the layer loops unroll, so every stride, shared-memory offset
+// and weight address is a constant instead of per-layer integer work.
+template <int A_, int F_, int CONN_>
+struct MeshShape {
+  static constexpr int A = A_, F = F_, CONN = CONN_;
+  __device__ static __forceinline__ int attn(const Dims& d) { return A > 0 ? A : d.attn_depth; }
+  __device__ static __forceinline__ int ffn(const Dims& d) { return F > 0 ? F : d.ffn_depth; }
+};
+using RuntimeShape = MeshShape<0, 0, -1>;
+
+// floor(log2 W), the butterfly period (Dims::log2w).
+template <int W>
+__host__ __device__ constexpr int floor_log2() {
+  int r = 0;
+  while ((2 << r) <= W) ++r;
+  return r;
+}
+
+template <int W, int CONN>
+__device__ __forceinline__ int layer_stride(const Dims& d, int layer) {
+  if constexpr (CONN == 0) {
+    return 1;
+  } else if constexpr (CONN == 1) {
+    return 1 << (layer % floor_log2<W>());
+  } else {
+    return mesh_stride(d, layer);
+  }
+}
+
+// body(l) for l = 0 .. n-1 (or n-1 .. 0 with `reverse`): unrolled when the
+// count N is a compile-time constant, a rolled loop otherwise.
+template <int N, bool reverse, class F>
+__device__ __forceinline__ void layer_loop(int n, F&& body) {
+  if constexpr (N > 0) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) body(reverse ? N - 1 - i : i);
+  } else {
+#pragma unroll 1
+    for (int i = 0; i < n; ++i) body(reverse ? n - 1 - i : i);
+  }
+}
+
 template <class T>
 struct Ctx {
   int tid, rl, cp, lane, warp;
@@ -161,31 +205,35 @@ __device__ __forceinline__ float4 slot_to_params(float4 g) { return make_float4(
 
 // Forward through a whole mesh stack.  With `keep`, layer l's input stays in
 // bufs[l] for a later backward pass; otherwise two buffers alternate.
-template <int W, class T>
+// DEPTH and CONN fix the depth and connectivity at compile time (see
+// MeshShape); `depth` is used when DEPTH is 0.
+template <int W, class T, int DEPTH, int CONN>
 __device__ __forceinline__ void mesh_forward(const Ctx<T>& c, const Dims& d, float2 (&a)[T::RPT],
                                              const float4* wg, int depth, float* bufs, bool keep) {
   // Each layer's weights are requested one layer ahead: with the row
   // buffers filling shared memory, L1 holds little and they come from L2.
+  if constexpr (DEPTH > 0) depth = DEPTH;
   float4 w = __ldg(wg + c.cp);
-  for (int l = 0; l < depth; ++l) {
+  layer_loop<DEPTH, false>(depth, [&](int l) {
     const float4 wn = l + 1 < depth ? __ldg(wg + (l + 1) * T::PAIRS + c.cp) : w;
     float* buf = bufs + (keep ? l : (l & 1)) * T::BUF;
-    mesh_layer_forward<W, T>(c, a, w, mesh_stride(d, l), l + 1 != depth, buf, keep);
+    mesh_layer_forward<W, T>(c, a, w, layer_stride<W, CONN>(d, l), l + 1 != depth, buf, keep);
     w = wn;
-  }
+  });
 }
 
 // Backward through a mesh stack whose layer inputs sit in bufs[0..depth-1]
 // (written by mesh_forward with keep = true).  dy enters as the gradient of
 // the stack output and leaves as the gradient of its input.  Edge gradients
 // add into the thread's private accumulator slots acc[l * NT + tid].
-template <int W, class T>
+template <int W, class T, int DEPTH, int CONN>
 __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, float2 (&dy)[T::RPT],
                                               const float4* wg, int depth, const float* bufs, float* xch,
                                               float4* acc) {
+  if constexpr (DEPTH > 0) depth = DEPTH;
   float4 wnext = __ldg(wg + (depth - 1) * T::PAIRS + c.cp);
-  for (int l = depth - 1; l >= 0; --l) {
-    const int s = mesh_stride(d, l);
+  layer_loop<DEPTH, true>(depth, [&](int l) {
+    const int s = layer_stride<W, CONN>(d, l);
     const float4 w = wnext;
     if (l > 0) wnext = __ldg(wg + (l - 1) * T::PAIRS + c.cp);  // one layer ahead
     const float2 w0 = make_float2(w.x, w.z), w1 = make_float2(w.y, w.w);
@@ -224,7 +272,7 @@ __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, fl
                               : Planes<W>::shifted_even(erow, c.cp, -s);
       dy[k] = fma2(dy[k], w0, t);
     }
-  }
+  });
 }
 
 // RMSNorm over the full row: returns normalized values and 1/rms per row.

@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(RowTile<W, kOpRpt>::NT)
       const int r = tile * T::TR + c.row(k);
       a[k] = r < d.rows ? __ldg(reinterpret_cast<const float2*>(x + (size_t)r * W) + c.cp) : make_float2(0.f, 0.f);
     }
-    mesh_forward<W, T>(c, d, a, reinterpret_cast<const float4*>(weights), d.attn_depth, bufs, false);
+    mesh_forward<W, T, 0, -1>(c, d, a, reinterpret_cast<const float4*>(weights), d.attn_depth, bufs, false);
 #pragma unroll
     for (int k = 0; k < kOpRpt; ++k) {
       const int r = tile * T::TR + c.row(k);
@@ -77,8 +77,8 @@ __global__ void __launch_bounds__(RowTile<W, kOpRpt>::NT)
       a[k] = in ? __ldg(reinterpret_cast<const float2*>(x + (size_t)r * W) + c.cp) : make_float2(0.f, 0.f);
       g[k] = in ? __ldg(reinterpret_cast<const float2*>(dy + (size_t)r * W) + c.cp) : make_float2(0.f, 0.f);
     }
-    mesh_forward<W, T>(c, d, a, wg, depth, bufs, true);
-    mesh_backward<W, T>(c, d, g, wg, depth, bufs, xch, acc);
+    mesh_forward<W, T, 0, -1>(c, d, a, wg, depth, bufs, true);
+    mesh_backward<W, T, 0, -1>(c, d, g, wg, depth, bufs, xch, acc);
 #pragma unroll
     for (int k = 0; k < kOpRpt; ++k) {
       const int r = tile * T::TR + c.row(k);
