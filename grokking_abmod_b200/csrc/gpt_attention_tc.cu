@@ -39,6 +39,8 @@ constexpr int kTcQ = 64;         // query-tile rows (dK/dV)
 constexpr int kTcThreads = 320;  // 8 compute warps + producer warp + MMA warp
 constexpr int kTcCompute = 256;  // compute threads: row = tid % 128, column half = tid / 128
 constexpr int kTcProducer = 256, kTcIssuer = 288;
+// The forward adds an eleventh warp whose thread 320 issues the P.V MMAs.
+constexpr int kTcFwdThreads = 352, kTcPvIssuer = 320;
 
 template <int HD>
 struct TcFmt {
@@ -318,14 +320,18 @@ struct TcShared {
 // Threads 0-255 compute (row r = tid % 128 owns TMEM lane r; half = tid / 128
 // takes keys [32 half, 32 half + 32) of every 64-key step and keeps its own
 // online-softmax stream with its own O accumulator), thread 256 producer,
-// thread 288 MMA issuer.  The two streams merge once at the end, so no
+// thread 288 issues the S = Q K^T MMAs and thread 320 (an eleventh warp) the
+// P.V MMAs: with TMEM loads and stores of the softmax warps in flight every
+// mbarrier wait of an issuing thread takes hundreds of cycles, and two
+// issuers let one keep the tensor pipe fed while the other waits.  The two
+// softmax streams merge once at the end, so no
 // per-step cross-warp reduction is needed.  O is rescaled lazily (only when a
 // row's running maximum grows by more than 2^8), as in FlashAttention-4.
 // TMEM: Q hi | Q lo | S0 | S1 | P hi | P lo | O0 | O1   (64 columns each).
 // mbarriers (parity = use index & 1): kv_full/kv_empty per stage, s_full /
 // s_empty per S buffer, p_full (256 arrivals), o_done (commit after P.V).
 template <int HD>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcFwdThreads, 1)
     attention_forward_tc(int rows, int W, int T, float scale, const float* __restrict__ q,
                          const float* __restrict__ kfmt, float* __restrict__ o, float* __restrict__ lse2,
                          int* __restrict__ err) {
@@ -489,35 +495,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                    &kv_full[st]);
     }
   } else if (tid == kTcIssuer) {
-    // ---------------------------------------------------------- MMA issuer
+    // ---------------------------------------------------------- S issuer
     constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcK, false, false);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS, b = j & 1;
+      const float* stage = sm + st * A::FWD_STAGE;
+      TC_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
+      if (j >= 2) {
+        TC_WAIT_OR_FAIL(&s_empty[b], ((j - 2) >> 1) & 1);
+      }
+      tc::fence_after_sync();
+      // S_j = Q K_j^T
+      mma_tmem_a<HD>(tS + 64 * b, tQh, tQl, stage + F::K_HI * F::KPART, stage + F::K_LO * F::KPART, idS, false);
+      tc::commit(&s_full[b]);
+    }
+  } else if (tid == kTcPvIssuer) {
+    // ---------------------------------------------------------- P.V issuer
     constexpr uint32_t idO = tc::idesc_tf32(kTcRows, HD, false, false);
-    for (int j = 0; j <= n; ++j) {
-      if (j < n) {
-        const int st = j % NS, b = j & 1;
-        const float* stage = sm + st * A::FWD_STAGE;
-        TC_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
-        if (j >= 2) {
-          TC_WAIT_OR_FAIL(&s_empty[b], ((j - 2) >> 1) & 1);
-        }
-        tc::fence_after_sync();
-        // S_j = Q K_j^T
-        mma_tmem_a<HD>(tS + 64 * b, tQh, tQl, stage + F::K_HI * F::KPART, stage + F::K_LO * F::KPART, idS, false);
-        tc::commit(&s_full[b]);
-      }
-      if (j >= 1) {
-        const int pj = j - 1, pst = pj % NS;
-        const float* stage = sm + pst * A::FWD_STAGE;
-        TC_WAIT_OR_FAIL(&p_full, pj & 1);
-        tc::fence_after_sync();
-        // O_half += P[:, half] V[half keys]   (B = V^T tile, K-major over keys)
-        const float* vh = stage + F::VT_HI * F::KPART;
-        const float* vl = stage + F::VT_LO * F::KPART;
-        mma_tmem_a_steps<kTcK, 4>(tO, tPh, tPl, vh, vl, idO, pj > 0, 0);
-        mma_tmem_a_steps<kTcK, 4>(tO + 64, tPh, tPl, vh, vl, idO, pj > 0, 4);
-        tc::commit(&o_done);
-        tc::commit(&kv_empty[pst]);
-      }
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      const float* stage = sm + st * A::FWD_STAGE;
+      TC_WAIT_OR_FAIL(&p_full, j & 1);
+      // Already complete (S_j read this stage); observed here as well so
+      // the Vt bytes are ordered before this thread's MMAs.
+      TC_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
+      tc::fence_after_sync();
+      // O_half += P[:, half] V[half keys]   (B = V^T tile, K-major over keys)
+      const float* vh = stage + F::VT_HI * F::KPART;
+      const float* vl = stage + F::VT_LO * F::KPART;
+      mma_tmem_a_steps<kTcK, 4>(tO, tPh, tPl, vh, vl, idO, j > 0, 0);
+      mma_tmem_a_steps<kTcK, 4>(tO + 64, tPh, tPl, vh, vl, idO, j > 0, 4);
+      tc::commit(&o_done);
+      tc::commit(&kv_empty[st]);
     }
   }
   tc::fence_before_sync();
