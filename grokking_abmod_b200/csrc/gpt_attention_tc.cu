@@ -36,11 +36,11 @@ namespace mb {
 constexpr int kTcRows = 128;     // CTA tile rows = TMEM lanes
 constexpr int kTcK = 64;         // key-tile rows (forward, dQ)
 constexpr int kTcQ = 64;         // query-tile rows (dK/dV)
-constexpr int kTcThreads = 320;  // 8 compute warps + producer warp + MMA warp
 constexpr int kTcCompute = 256;  // compute threads: row = tid % 128, column half = tid / 128
+// Forward and dQ: 8 compute warps, a producer warp (thread 256), and two MMA
+// issuers in separate warps (threads 288 and 320).
 constexpr int kTcProducer = 256, kTcIssuer = 288;
-// The forward adds an eleventh warp whose thread 320 issues the P.V MMAs.
-constexpr int kTcFwdThreads = 352, kTcPvIssuer = 320;
+constexpr int kTcThreads2 = 352, kTcIssuer2 = 320;
 
 template <int HD>
 struct TcFmt {
@@ -331,7 +331,7 @@ struct TcShared {
 // mbarriers (parity = use index & 1): kv_full/kv_empty per stage, s_full /
 // s_empty per S buffer, p_full (256 arrivals), o_done (commit after P.V).
 template <int HD>
-__global__ void __launch_bounds__(kTcFwdThreads, 1)
+__global__ void __launch_bounds__(kTcThreads2, 1)
     attention_forward_tc(int rows, int W, int T, float scale, const float* __restrict__ q,
                          const float* __restrict__ kfmt, float* __restrict__ o, float* __restrict__ lse2,
                          int* __restrict__ err) {
@@ -509,7 +509,7 @@ __global__ void __launch_bounds__(kTcFwdThreads, 1)
       mma_tmem_a<HD>(tS + 64 * b, tQh, tQl, stage + F::K_HI * F::KPART, stage + F::K_LO * F::KPART, idS, false);
       tc::commit(&s_full[b]);
     }
-  } else if (tid == kTcPvIssuer) {
+  } else if (tid == kTcIssuer2) {
     // ---------------------------------------------------------- P.V issuer
     constexpr uint32_t idO = tc::idesc_tf32(kTcRows, HD, false, false);
     for (int j = 0; j < n; ++j) {
@@ -540,9 +540,10 @@ __global__ void __launch_bounds__(kTcFwdThreads, 1)
 // Per key step: S = Q K^T, dP = dO V^T; dS = P (dP - delta) scale; dQ += dS K.
 // dS hi overwrites dP, so S_{j+1} is issued as soon as the compute warps have
 // read S_j, ahead of dQ_j's second half completing; only dP_{j+1} waits for
-// dQ_j.
+// dQ_j.  Thread 288 issues S and dP, thread 320 (an eleventh warp) dQ, so
+// each issuer's mbarrier waits overlap the other's MMAs.
 template <int HD>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads2, 1)
     attention_backward_dq_tc(int rows, int W, int T, float scale, const float* __restrict__ q,
                              const float* __restrict__ dout, const float* __restrict__ kfmt,
                              const float* __restrict__ lse2, const float* __restrict__ delta, float* __restrict__ dq,
@@ -660,21 +661,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc::bulk_g2s(stage + 2 * F::KPART, tile + F::V_HI * F::KPART, 4 * F::KPART * 4, &kv_full[st]);  // V, V', Kt, Kt'
     }
   } else if (tid == kTcIssuer) {
+    // ---------------------------------------------------------- S / dP issuer
     constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcK, false, false);
-    constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
-    // Step j: S_j and dP_j were issued by the previous iteration (or the
-    // prologue); the loop issues dQ_j, then S_{j+1}, then (after dQ_j has
-    // consumed dS_j from the dP columns) dP_{j+1}.
-    if (n > 0 && !tc::bar_wait(&kv_full[0], 0)) sh.failed = 1;
-    if (n > 0 && !sh.failed) {
-      tc::fence_after_sync();
-      mma_tmem_a<HD>(tS, tQh, tQl, sm, sm + F::KPART, idS, false);                     // S_0  = Q K_0^T
-      mma_tmem_a<HD>(tP, tDh, tDl, sm + 2 * F::KPART, sm + 3 * F::KPART, idS, false);  // dP_0 = dO V_0^T
-      tc::commit(&s_full);
-    }
-    for (int j = 0; j < n && !sh.failed; ++j) {
+    for (int j = 0; j < n; ++j) {
       const int st = j % NS;
       const float* stage = sm + st * A::DQ_STAGE;  // K, K', V, V', Kt, Kt'
+      TC_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
+      if (j > 0) {
+        TC_WAIT_OR_FAIL(&d_full[1], (j - 1) & 1);  // the compute warps have read S_{j-1}
+      }
+      tc::fence_after_sync();
+      mma_tmem_a<HD>(tS, tQh, tQl, stage, stage + F::KPART, idS, false);  // S_j = Q K_j^T
+      if (j > 0) {
+        TC_WAIT_OR_FAIL(&q_done, (j - 1) & 1);  // dQ_{j-1} has read dS_{j-1} hi (the dP columns)
+      }
+      tc::fence_after_sync();
+      mma_tmem_a<HD>(tP, tDh, tDl, stage + 2 * F::KPART, stage + 3 * F::KPART, idS, false);  // dP_j = dO V_j^T
+      tc::commit(&s_full);
+    }
+  } else if (tid == kTcIssuer2) {
+    // ---------------------------------------------------------- dQ issuer
+    constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      const float* stage = sm + st * A::DQ_STAGE;
+      // Complete since S_j read this stage; observed so the Kt bytes are
+      // ordered before this thread's MMAs.
+      TC_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
       bool ok = true;
       for (int k2 = 0; k2 < 2 && ok; ++k2) {
         ok = tc::bar_wait(&d_full[k2], j & 1);
@@ -690,18 +703,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       tc::commit(&q_done);
       tc::commit(&kv_empty[st]);
-      if (j + 1 < n) {
-        const int sn = (j + 1) % NS;
-        const float* next = sm + sn * A::DQ_STAGE;
-        TC_WAIT_OR_FAIL(&kv_full[sn], ((j + 1) / NS) & 1);
-        tc::fence_after_sync();
-        // The compute warps have read S_j (they arrived on d_full[1]).
-        mma_tmem_a<HD>(tS, tQh, tQl, next, next + F::KPART, idS, false);  // S_{j+1}
-        TC_WAIT_OR_FAIL(&q_done, j & 1);  // dQ_j has read dS_j hi (the dP columns)
-        tc::fence_after_sync();
-        mma_tmem_a<HD>(tP, tDh, tDl, next + 2 * F::KPART, next + 3 * F::KPART, idS, false);  // dP_{j+1}
-        tc::commit(&s_full);
-      }
     }
   }
   tc::fence_before_sync();

@@ -243,7 +243,7 @@ struct AttentionOpsTc final : AttentionOps {
     attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), kFmtThreads, 0, s>>>(
         rows, W, k, v, kfmt(rows, H), (1u << F::K_HI) | (1u << F::VT_HI) | (1u << F::V_HI) | (1u << F::KT_HI));
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_forward_tc<HD><<<grid, kTcFwdThreads, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
+    attention_forward_tc<HD><<<grid, kTcThreads2, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
                                                                         kfmt(rows, H), o, lse, err);
   }
   void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
@@ -258,7 +258,7 @@ struct AttentionOpsTc final : AttentionOps {
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dq_tc<HD><<<grid, kTcThreads, K::smem_dq, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, dout,
+    attention_backward_dq_tc<HD><<<grid, kTcThreads2, K::smem_dq, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, dout,
                                                                        kfmt(rows, H), lse, delta, dq, err);
   }
 };
