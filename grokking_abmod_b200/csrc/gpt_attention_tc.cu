@@ -715,8 +715,9 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
 // A CTA owns 128 keys of one head and walks the later queries 64 at a time.
 // Threads 0-255 compute (key row = tid % 128 = TMEM lane; thread half
 // tid / 128 takes 16 of each 32-query half), warp 8 streams the A tile
-// (Q, dO), warp 9 issues the MMAs, warp 10 streams the B tile (Q^T, dO^T,
-// LSE, delta).  K lives in TMEM, V in shared memory.  Per query step the
+// (Q, dO), warp 9 issues S^T and dP^T, warp 10 streams the B tile (Q^T,
+// dO^T, LSE, delta), warp 11 issues dV and dK (two issuers, so each one's
+// mbarrier waits overlap the other's MMAs).  K lives in TMEM, V in shared memory.  Per query step the
 // tensor pipe runs S^T = K Q^T, dP^T = V dO^T (keys on lanes, N = 64
 // queries), dV += P^T dO and dK += dS^T Q, and the softmax hides behind it:
 //   * the P phase (P^T from S^T and LSE) runs while dP^T executes;
@@ -727,8 +728,8 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
 //     columns) waits for dK.
 // TMEM: K hi | K lo | dV | dK | S^T then P^T hi | dP^T then dS^T hi | P^T lo
 // | dS^T lo (64 columns each).
-constexpr int kTcKvThreads = 352;
-constexpr int kKvProducerA = 256, kKvIssuer = 288, kKvProducerB = 320;
+constexpr int kTcKvThreads = 384;
+constexpr int kKvProducerA = 256, kKvIssuer = 288, kKvProducerB = 320, kKvIssuer2 = 352;
 
 template <int HD>
 struct TcKv {
@@ -959,9 +960,8 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
                    &b_full);
     }
   } else if (tid == kKvIssuer) {
-    // ---------------------------------------------------------- MMA issuer
+    // ---------------------------------------------------------- S^T / dP^T issuer
     constexpr uint32_t idS = tc::idesc_tf32(kTcRows, kTcQ, false, false);
-    constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
     for (int j = 0; j < n; ++j) {
       TC_WAIT_OR_FAIL(&a_full, j & 1);
       if (j >= 1) {
@@ -977,9 +977,14 @@ __global__ void __launch_bounds__(kTcKvThreads, 1)
       mma_smem_a<HD>(tP, Vh, Vl, tile_a + F::D_HI * F::QPART, tile_a + F::D_LO * F::QPART, idS, false);    // dP^T
       tc::commit(&dp_full);
       tc::commit(&a_empty);
+    }
+  } else if (tid == kKvIssuer2) {
+    // ---------------------------------------------------------- dV / dK issuer
+    constexpr uint32_t idG = tc::idesc_tf32(kTcRows, HD, false, false);
+    const float* qt = tile_b;                   // Q^T, Q^T'
+    const float* dot = tile_b + 2 * F::QPART;   // dO^T, dO^T'
+    for (int j = 0; j < n; ++j) {
       TC_WAIT_OR_FAIL(&b_full, j & 1);
-      const float* qt = tile_b;                   // Q^T, Q^T'
-      const float* dot = tile_b + 2 * F::QPART;   // dO^T, dO^T'
       TC_WAIT_OR_FAIL(&p_full, j & 1);
       tc::fence_after_sync();
       // dV += P^T dO over the step's 64 queries
