@@ -203,11 +203,12 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
     }
     // FFN: x_next = x_mid + FFN(RMSNorm(x_mid)).
     rmsnorm_rows<T>(c, n2, inv2, red, phase, W);
+    KeptInputs<T, S::F, S::CONN> kept_f;
     {
       float2 a[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = n2[k];
-      mesh_forward<W, T, S::F, S::CONN>(c, d, a, reinterpret_cast<const float4*>(wf), S::ffn(d), bufs, true);
+      mesh_forward_kept<W, T, S::F, S::CONN>(c, d, a, reinterpret_cast<const float4*>(wf), F, bufs, kept_f);
     }
     // O and V of the attention path, in flight during the FFN backward.
     float2 y[RPT], vv[RPT];
@@ -218,7 +219,8 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       vv[k] = ld2<T>(v, r, d.rows, W, c.cp);
       dy[k] = g[k];
     }
-    mesh_backward<W, T, S::F, S::CONN>(c, d, dy, reinterpret_cast<const float4*>(wf), S::ffn(d), bufs, xch, acc_f);
+    mesh_backward_kept<W, T, S::F, S::CONN>(c, d, dy, reinterpret_cast<const float4*>(wf), F, bufs, xch, acc_f,
+                                            kept_f);
     rmsnorm_rows_backward<T>(c, n2, inv2, dy, red, phase, W);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) g[k] = g[k] + dy[k];  // dx_mid
@@ -233,15 +235,17 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       proj[k] = head_sum(y[k].x * u[k].x + y[k].y * u[k].y, hp);
     }
     __syncthreads();  // the FFN backward may still read bufs
+    KeptInputs<T, S::A, S::CONN> kept_o;
     {
       float2 a[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = make_float2(y[k].x - proj[k] * u[k].x, y[k].y - proj[k] * u[k].y);
-      mesh_forward<W, T, S::A, S::CONN>(c, d, a, reinterpret_cast<const float4*>(wo), S::attn(d), bufs, true);
+      mesh_forward_kept<W, T, S::A, S::CONN>(c, d, a, reinterpret_cast<const float4*>(wo), A, bufs, kept_o);
     }
 #pragma unroll
     for (int k = 0; k < RPT; ++k) dy[k] = g[k];
-    mesh_backward<W, T, S::A, S::CONN>(c, d, dy, reinterpret_cast<const float4*>(wo), S::attn(d), bufs, xch, acc_o);
+    mesh_backward_kept<W, T, S::A, S::CONN>(c, d, dy, reinterpret_cast<const float4*>(wo), A, bufs, xch, acc_o,
+                                            kept_o);
     // XSA backward (src/gpt/gpu.rs:861-897); dy is dL/dz.
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
@@ -313,7 +317,8 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = n1[k];
       __syncthreads();  // the previous mesh backward may still read bufs
-      mesh_forward<W, T, S::A, S::CONN>(c, d, a, wg, A, bufs, true);
+      KeptInputs<T, S::A, S::CONN> kept;
+      mesh_forward_kept<W, T, S::A, S::CONN>(c, d, a, wg, A, bufs, kept);
       float2 gm[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) {
@@ -330,7 +335,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
         }
         gm[k] = gg;
       }
-      mesh_backward<W, T, S::A, S::CONN>(c, d, gm, wg, A, bufs, xch, accs + m * A * T::NT);
+      mesh_backward_kept<W, T, S::A, S::CONN>(c, d, gm, wg, A, bufs, xch, accs + m * A * T::NT, kept);
 #pragma unroll
       for (int k = 0; k < RPT; ++k) dn[k] = dn[k] + gm[k];
     }

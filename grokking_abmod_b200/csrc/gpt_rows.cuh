@@ -275,6 +275,79 @@ __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, fl
   });
 }
 
+// Layer inputs of a mesh stack kept for its backward pass.  With the shape
+// compiled in and stride-1 (neighbor) layers, each thread keeps its own
+// channel pairs in registers and only the even plane, which the neighbours
+// read, goes to shared memory: the backward then reads one shared value per
+// row and layer instead of five.  Other shapes keep whole layer inputs in
+// shared memory (mesh_forward with keep = true).
+template <class T, int DEPTH, int CONN>
+struct KeptInputs {
+  static constexpr bool kRegs = DEPTH > 0 && CONN == 0;
+  float2 x[kRegs ? DEPTH : 1][T::RPT];
+};
+
+template <int W, class T, int DEPTH, int CONN>
+__device__ __forceinline__ void mesh_forward_kept(const Ctx<T>& c, const Dims& d, float2 (&a)[T::RPT],
+                                                  const float4* wg, int depth, float* bufs,
+                                                  KeptInputs<T, DEPTH, CONN>& kept) {
+  if constexpr (KeptInputs<T, DEPTH, CONN>::kRegs) {
+    float4 w = __ldg(wg + c.cp);
+    layer_loop<DEPTH, false>(DEPTH, [&](int l) {
+      const float4 wn = l + 1 < DEPTH ? __ldg(wg + (l + 1) * T::PAIRS + c.cp) : w;
+#pragma unroll
+      for (int k = 0; k < T::RPT; ++k) kept.x[l][k] = a[k];
+      mesh_layer_forward<W, T>(c, a, w, 1, l + 1 != DEPTH, bufs + l * T::BUF, false);
+      w = wn;
+    });
+  } else {
+    mesh_forward<W, T, DEPTH, CONN>(c, d, a, wg, depth, bufs, true);
+  }
+}
+
+// mesh_backward over inputs kept by mesh_forward_kept.
+template <int W, class T, int DEPTH, int CONN>
+__device__ __forceinline__ void mesh_backward_kept(const Ctx<T>& c, const Dims& d, float2 (&dy)[T::RPT],
+                                                   const float4* wg, int depth, const float* bufs, float* xch,
+                                                   float4* acc, const KeptInputs<T, DEPTH, CONN>& kept) {
+  if constexpr (KeptInputs<T, DEPTH, CONN>::kRegs) {
+    float4 wnext = __ldg(wg + (DEPTH - 1) * T::PAIRS + c.cp);
+    layer_loop<DEPTH, true>(DEPTH, [&](int l) {
+      const float4 w = wnext;
+      if (l > 0) wnext = __ldg(wg + (l - 1) * T::PAIRS + c.cp);  // one layer ahead
+      const float2 w0 = make_float2(w.x, w.z), w1 = make_float2(w.y, w.w);
+      const float* xin = bufs + l * T::BUF;  // even plane of layer l's input
+      float* ex = xch + (l & 1) * T::BUF;
+      float2 gs = make_float2(0.f, 0.f), gn = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < T::RPT; ++k) {
+        const int r = c.row(k);
+        float2 dz = dy[k];
+        if (l + 1 != DEPTH) dz = mul2(dz, elu_slope2(kept.x[l + 1 < DEPTH ? l + 1 : l][k]));
+        const float2 x = kept.x[l][k];
+        const float2 nb = make_float2(x.y, Planes<W>::next_even(xin + r * W, c.cp));
+        gs = fma2(dz, x, gs);
+        gn = fma2(dz, nb, gn);
+        dy[k] = dz;
+        // Channel c's neighbour term dz*w1 flows back to channel c + 1.
+        ex[r * W + Planes<W>::P + c.cp] = dz.y * w1.y;
+      }
+      float4& slot = acc[l * T::NT + c.tid];
+      const float2 ss = add2(make_float2(slot.x, slot.y), gs);
+      const float2 sn = add2(make_float2(slot.z, slot.w), gn);
+      slot = make_float4(ss.x, ss.y, sn.x, sn.y);
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < T::RPT; ++k) {
+        const float2 t = make_float2(Planes<W>::prev_odd(ex + c.row(k) * W, c.cp), dy[k].x * w.y);
+        dy[k] = fma2(dy[k], w0, t);
+      }
+    });
+  } else {
+    mesh_backward<W, T, DEPTH, CONN>(c, d, dy, wg, depth, bufs, xch, acc);
+  }
+}
+
 // RMSNorm over the full row: returns normalized values and 1/rms per row.
 template <class T>
 __device__ __forceinline__ void rmsnorm_rows(const Ctx<T>& c, float2 (&x)[T::RPT], float (&inv)[T::RPT], float* red,
