@@ -21,6 +21,16 @@ more:
 * ``residual-mlp`` (``:60-62``): a dense operand embedding, ``depth``
   pre-RMSNorm feed-forward blocks (width -> width * expansion -> width)
   with residual sums, a final RMSNorm and a dense readout.
+* the residual mesh family (``:57-70``): ``depth`` pre-RMSNorm residual
+  blocks whose branches are ``mesh_depth`` fixed-width mesh layers
+  (activated between layers, and after the last with
+  ``mesh_output_activation``), a final RMSNorm and a readout; the operand
+  embedding is a dense layer over ``[a | b]`` (``residual-mesh-mlp``), the
+  concatenation ``[E a | E b]`` projected to ``width``
+  (``tied-concat-residual-mesh-mlp``) or E's Rotate90 roles
+  (``tied-rotary-residual-mesh-mlp``); the tied ones read out through E.
+* ``tied-concat-mesh-mlp`` (``:54-56``): the tied concatenation embedding,
+  ``depth-1`` mesh layers as in ``mesh-mlp``, readout through E.
 
 Sources: ``SimpleConfig`` validation / layout / init / encode
 (``src/simple/mod.rs:500-1055``), the f64 tape model
@@ -46,7 +56,11 @@ RMSNORM_EPSILON = 1e-5  # src/gpt/mod.rs:39 (f32 1e-5 widened)
 EPS = float(np.float32(RMSNORM_EPSILON))
 MAX_WIDTH, MAX_DEPTH, MAX_CLASSES = 16384, 64, 1024  # src/simple/mod.rs:25-31
 ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear",
-                 "residual-mlp")
+                 "residual-mlp", "residual-mesh-mlp", "tied-concat-residual-mesh-mlp",
+                 "tied-rotary-residual-mesh-mlp", "tied-concat-mesh-mlp")
+RESIDUAL_MESH = ("residual-mesh-mlp", "tied-concat-residual-mesh-mlp", "tied-rotary-residual-mesh-mlp")
+TIED_CONCAT = ("tied-concat-residual-mesh-mlp", "tied-concat-mesh-mlp")
+ROTARY = ("tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "tied-rotary-residual-mesh-mlp")
 
 
 def butterfly_stride(width: int, layer: int) -> int:
@@ -72,6 +86,8 @@ class SimpleConfig:
     mesh_learning_rate_multiplier: int = 1
     encoding: str = "one-hot"  # or "scalar"
     expansion: int = 4  # residual-mlp hidden width / width
+    mesh_depth: int = 4  # mesh layers per residual mesh branch
+    mesh_output_activation: bool = False  # activate the branch output too
 
     def with_(self, **kw):
         return replace(self, **kw)
@@ -96,14 +112,20 @@ class SimpleConfig:
             raise ValueError("unknown encoding")
         if a == "residual-mlp" and not 1 <= self.width * self.expansion <= MAX_WIDTH:
             raise ValueError(f"residual hidden width must be in 1..={MAX_WIDTH}")
-        if self.encoding != "one-hot" and a not in ("mesh-mlp", "mlp", "bilinear", "residual-mlp"):
+        if a in RESIDUAL_MESH and not 1 <= self.mesh_depth <= MAX_DEPTH:
+            raise ValueError(f"mesh depth must be in 1..={MAX_DEPTH}")
+        if self.mesh_output_activation and a not in RESIDUAL_MESH:
+            raise ValueError("only residual mesh branches activate their final mesh output")
+        if a in TIED_CONCAT and (self.encoding != "one-hot" or 2 * self.width > MAX_WIDTH):
+            raise ValueError(f"tied concatenation needs one-hot encoding and width <= {MAX_WIDTH // 2}")
+        if self.encoding != "one-hot" and a not in ("mesh-mlp", "mlp", "bilinear", "residual-mlp",
+                                                     "residual-mesh-mlp"):
             raise ValueError("rotary roles need one-hot encoding and a positive even width")
         if a == "shared-neighbor-mesh-mlp" and not 1 <= self.embedding_mesh_depth <= MAX_DEPTH:
             raise ValueError("shared Neighbor embedding depth must be in 1..=64")
         if self.mesh_layers() > 0 and self.parents() == 2 and self.width < 2:
             raise ValueError("a second mesh parent needs a width of at least 2")
-        if a in ("tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp") and (
-                self.width < 2 or self.width % 2):
+        if a in ROTARY and (self.width < 2 or self.width % 2):
             raise ValueError("rotary roles need one-hot encoding and a positive even width")
         if self.full_mesh_initialization not in ("kaiming", "identity-hidden"):
             raise ValueError("unknown full-mesh initialization")
@@ -140,8 +162,12 @@ class SimpleConfig:
     def layers(self):
         """Dense (inputs, outputs) layers in parameter order (``:710-756``)."""
         m, w, f = self.modulus, self.width, self.operand_features()
-        if self.architecture == "mesh-mlp":
+        if self.architecture in ("mesh-mlp", "residual-mesh-mlp"):
             return [(2 * f, w), (w, m)]
+        if self.architecture in TIED_CONCAT:
+            return [(m, w), (2 * w, w)]
+        if self.architecture == "tied-rotary-residual-mesh-mlp":
+            return [(m, w)]
         if self.architecture == "mlp":
             return [(2 * f, w)] + [(w, w)] * (self.depth - 1) + [(w, m)]
         if self.architecture == "bilinear":
@@ -155,8 +181,10 @@ class SimpleConfig:
 
     def mesh_layers(self) -> int:
         """``:758-765``."""
-        if self.architecture == "mesh-mlp":
+        if self.architecture in ("mesh-mlp", "tied-concat-mesh-mlp"):
             return self.depth - 1
+        if self.architecture in RESIDUAL_MESH:
+            return self.depth * self.mesh_depth
         if self.architecture == "shared-neighbor-mesh-mlp":
             return self.embedding_mesh_depth + self.depth
         return 0
@@ -337,6 +365,22 @@ class ReferenceSimpleModel:
                 h.append(y)
             act = _act(c, h[-1])
             return act @ readout, dict(x=x, h=h, act=act)
+        if c.architecture == "tied-concat-mesh-mlp":
+            # src/simple/reference.rs:300-335 (tied)
+            emb = g[0].reshape(m, w)
+            j = np.concatenate([x[:, :m] @ emb, x[:, m:] @ emb], axis=1)
+            h = [j @ g[1].reshape(2 * w, w)]
+            for layer in range(c.mesh_layers()):
+                mw = g[2 + layer].reshape(w, c.parents())
+                act = _act(c, h[-1])
+                y = act * mw[:, 0]
+                if c.parents() == 2:
+                    y = y + np.roll(act, -c.stride(layer), axis=1) * mw[:, 1]
+                h.append(y)
+            act = _act(c, h[-1])
+            return act @ emb.T, dict(x=x, j=j, h=h, act=act, emb=emb)
+        if c.architecture in RESIDUAL_MESH:
+            return self._residual_mesh_forward(x, g)
         perm, sign = _rotation(w)
         if c.architecture == "tied-rotary-residual-dense-mlp":
             emb = g[0].reshape(m, w)
@@ -382,6 +426,82 @@ class ReferenceSimpleModel:
             y = y * chain[layer][:, 0] + np.roll(y * chain[layer][:, 1], 1, axis=1)
         return y[:, :m], dict(x=x, ls=ls, rs=rs, blocks=blocks, hf=hf, invf=invf, reads=reads,
                               chain=chain, core=core)
+
+    def _residual_mesh_forward(self, x, g):
+        """``src/simple/reference.rs:337-407`` for the residual mesh family."""
+        c = self.config
+        m, w, md, nd = c.modulus, c.width, c.mesh_depth, len(c.layers())
+        emb = j = None
+        if c.architecture == "tied-rotary-residual-mesh-mlp":
+            perm, sign = _rotation(w)
+            emb = g[0].reshape(m, w)
+            h = x[:, :m] @ emb + (x[:, m:] @ emb)[:, perm] * sign
+        elif c.architecture == "tied-concat-residual-mesh-mlp":
+            emb = g[0].reshape(m, w)
+            j = np.concatenate([x[:, :m] @ emb, x[:, m:] @ emb], axis=1)
+            h = j @ g[1].reshape(2 * w, w)
+        else:
+            h = x @ g[0].reshape(-1, w)
+        blocks = []
+        for block in range(c.depth):
+            n, inv = _rmsnorm(h)
+            branch, zs = n, []
+            for layer in range(md):
+                if layer > 0:
+                    branch = _act(c, branch)
+                mesh = block * md + layer
+                mw = g[nd + mesh].reshape(w, c.parents())
+                z = branch * mw[:, 0]
+                if c.parents() == 2:
+                    z = z + np.roll(branch, -c.stride(mesh), axis=1) * mw[:, 1]
+                zs.append(z)
+                branch = z
+            if c.mesh_output_activation:
+                branch = _act(c, branch)
+            blocks.append((n, inv, zs))
+            h = h + branch
+        hf, invf = _rmsnorm(h)
+        logits = hf @ emb.T if emb is not None else hf @ g[1].reshape(w, m)
+        return logits, dict(x=x, j=j, emb=emb, blocks=blocks, hf=hf, invf=invf)
+
+    def _residual_mesh_backward(self, s, g, grads, dlog):
+        c = self.config
+        m, w, md, nd = c.modulus, c.width, c.mesh_depth, len(c.layers())
+        x, emb = s["x"], s["emb"]
+        if emb is not None:
+            demb = dlog.T @ s["hf"]
+            dh = _rmsnorm_backward(s["hf"], s["invf"], dlog @ emb)
+        else:
+            grads[1] = (s["hf"].T @ dlog).reshape(-1)
+            dh = _rmsnorm_backward(s["hf"], s["invf"], dlog @ g[1].reshape(w, m).T)
+        for block in reversed(range(c.depth)):
+            n, inv, zs = s["blocks"][block]
+            dz = dh * _act_grad(c, zs[-1]) if c.mesh_output_activation else dh
+            for layer in reversed(range(md)):
+                mesh = block * md + layer
+                xin = n if layer == 0 else _act(c, zs[layer - 1])
+                mw = g[nd + mesh].reshape(w, c.parents())
+                gw = np.zeros((w, c.parents()))
+                gw[:, 0] = (dz * xin).sum(axis=0)
+                dx = dz * mw[:, 0]
+                if c.parents() == 2:
+                    st = c.stride(mesh)
+                    gw[:, 1] = (dz * np.roll(xin, -st, axis=1)).sum(axis=0)
+                    dx = dx + np.roll(dz * mw[:, 1], st, axis=1)
+                grads[nd + mesh] = gw.reshape(-1)
+                dz = dx * _act_grad(c, zs[layer - 1]) if layer > 0 else dx
+            dh = dh + _rmsnorm_backward(n, inv, dz)
+        if c.architecture == "tied-rotary-residual-mesh-mlp":
+            perm, sign = _rotation(w)
+            dright = np.empty_like(dh)
+            dright[:, perm] = dh * sign
+            grads[0] = (demb + x[:, :m].T @ dh + x[:, m:].T @ dright).reshape(-1)
+        elif c.architecture == "tied-concat-residual-mesh-mlp":
+            grads[1] = (s["j"].T @ dh).reshape(-1)
+            dj = dh @ g[1].reshape(2 * w, w).T
+            grads[0] = (demb + x[:, :m].T @ dj[:, :w] + x[:, m:].T @ dj[:, w:]).reshape(-1)
+        else:
+            grads[0] = (x.T @ dh).reshape(-1)
 
     def logits(self, features) -> np.ndarray:
         return self._forward(features)[0]
@@ -455,6 +575,31 @@ class ReferenceSimpleModel:
                 grads[2 + layer] = gw.reshape(-1)
                 dh = dact * _act_grad(c, hin)
             grads[0] = (s["x"].T @ dh).reshape(-1)
+            return loss, np.concatenate(grads)
+        if c.architecture == "tied-concat-mesh-mlp":
+            emb = s["emb"]
+            demb = dlog.T @ s["act"]
+            dh = (dlog @ emb) * _act_grad(c, s["h"][-1])
+            for layer in reversed(range(c.mesh_layers())):
+                mw = g[2 + layer].reshape(w, c.parents())
+                hin = s["h"][layer]
+                act = _act(c, hin)
+                gw = np.zeros((w, c.parents()))
+                gw[:, 0] = (dh * act).sum(axis=0)
+                dact = dh * mw[:, 0]
+                if c.parents() == 2:
+                    st = c.stride(layer)
+                    gw[:, 1] = (dh * np.roll(act, -st, axis=1)).sum(axis=0)
+                    dact = dact + np.roll(dh * mw[:, 1], st, axis=1)
+                grads[2 + layer] = gw.reshape(-1)
+                dh = dact * _act_grad(c, hin)
+            grads[1] = (s["j"].T @ dh).reshape(-1)
+            dj = dh @ g[1].reshape(2 * w, w).T
+            x = s["x"]
+            grads[0] = (demb + x[:, :m].T @ dj[:, :w] + x[:, m:].T @ dj[:, w:]).reshape(-1)
+            return loss, np.concatenate(grads)
+        if c.architecture in RESIDUAL_MESH:
+            self._residual_mesh_backward(s, g, grads, dlog)
             return loss, np.concatenate(grads)
         perm, sign = _rotation(w)
         x = s["x"]

@@ -47,7 +47,13 @@ def test_validation_rejects_what_the_reference_rejects():
         SimpleConfig("mesh-mlp", depth=0),
         SimpleConfig("mesh-mlp", depth=65),
         SimpleConfig("mesh-mlp", modulus=1),
-        SimpleConfig("residual-mesh-mlp"),  # outside this restatement
+        SimpleConfig("residual-mesh-mlp", mesh_depth=0),
+        SimpleConfig("residual-mesh-mlp", mesh_depth=65),
+        SimpleConfig("tied-rotary-residual-mesh-mlp", width=127),
+        SimpleConfig("tied-concat-residual-mesh-mlp", encoding="scalar"),
+        SimpleConfig("tied-concat-mesh-mlp", width=16384),
+        SimpleConfig("mesh-mlp", mesh_output_activation=True),
+        SimpleConfig("tied-concat-mesh-mlp", mesh_output_activation=True),
         SimpleConfig("residual-mlp", width=8, expansion=0),
         SimpleConfig("tied-rotary-residual-dense-mlp", encoding="scalar"),
         SimpleConfig("mlp", depth=0),
@@ -159,6 +165,16 @@ def test_step10_record_matches_archive(name, tolerance):
     SimpleConfig("bilinear", modulus=7, width=8),
     SimpleConfig("residual-mlp", modulus=7, width=8, depth=2, expansion=2),
     SimpleConfig("residual-mlp", modulus=7, width=6, depth=1, expansion=3, activation="square"),
+    SimpleConfig("residual-mesh-mlp", modulus=7, width=8, depth=2, mesh_depth=3),
+    SimpleConfig("residual-mesh-mlp", modulus=7, width=8, depth=2, mesh_depth=2, connectivity="butterfly",
+                 activation="square", mesh_output_activation=True),
+    SimpleConfig("residual-mesh-mlp", modulus=7, width=6, depth=1, mesh_depth=2, connectivity="own"),
+    SimpleConfig("tied-concat-residual-mesh-mlp", modulus=7, width=8, depth=2, mesh_depth=2),
+    SimpleConfig("tied-rotary-residual-mesh-mlp", modulus=7, width=8, depth=2, mesh_depth=3, activation="square"),
+    SimpleConfig("tied-rotary-residual-mesh-mlp", modulus=7, width=8, depth=1, mesh_depth=1,
+                 mesh_output_activation=True),
+    SimpleConfig("tied-concat-mesh-mlp", modulus=7, width=8, depth=3),
+    SimpleConfig("tied-concat-mesh-mlp", modulus=7, width=8, depth=3, connectivity="own", activation="square"),
 ])
 def test_gradient_matches_finite_differences(config):
     rng = np.random.default_rng(0)
@@ -199,3 +215,51 @@ def test_shared_neighbor_readout_is_the_embedding_transpose():
             e = np.array([w[2 * (layer * 8 + c)] * e[c] + w[2 * (layer * 8 + c) + 1] * e[(c + 1) % 8]
                           for c in range(8)])
         assert math.isclose(readout[k], float(e @ h), rel_tol=1e-12, abs_tol=1e-14)
+
+
+def test_mesh_parameter_counts_match_reference_tests():
+    """``src/simple/mod.rs:1446-1760``: counts and groups of the residual mesh
+    family and the tied-concat mesh MLP."""
+    c = SimpleConfig("residual-mesh-mlp", width=64, depth=2, mesh_depth=4).validate()
+    assert c.parameter_count() == 19_648 and c.mesh_layers() == 8
+    c = SimpleConfig("tied-rotary-residual-mesh-mlp", activation="square", width=128, depth=2,
+                     mesh_depth=3).validate()
+    assert c.parameter_count() == 13_952 and c.groups() == [12_416] + [256] * 6
+    assert initial_parameters(c, 11).size == 13_952
+    plain = SimpleConfig("tied-rotary-residual-mesh-mlp", activation="square", width=128, depth=1, mesh_depth=1)
+    activated = plain.with_(mesh_output_activation=True).validate()
+    assert activated.parameter_count() == 12_672 and activated.groups() == plain.groups()
+    assert np.array_equal(initial_parameters(activated, 11), initial_parameters(plain, 11))
+    c = SimpleConfig("tied-concat-residual-mesh-mlp", activation="square", width=128, depth=2,
+                     mesh_depth=3).validate()
+    assert c.parameter_count() == 46_720 and c.groups() == [12_416, 32_768] + [256] * 6 and c.mesh_layers() == 6
+    c = SimpleConfig("tied-concat-mesh-mlp", connectivity="own", width=64, depth=5).validate()
+    assert c.parameter_count() == 14_656 and c.groups() == [97 * 64, 128 * 64, 64, 64, 64, 64]
+    assert initial_parameters(c, 7).size == 14_656
+
+
+@pytest.mark.parametrize("case", PINS["grok_simple_mesh_models"]["cases"],
+                         ids=lambda c: "-".join(str(v) for v in c["config"].values()))
+def test_mesh_models_match_archived_records(case):
+    """Seeded split, identity-mesh / uniform fan-in init and forward against
+    the archived step-0 line (CE to 1e-8 relative, accuracies exactly, the
+    weight norm to 1e-9), then the archived later line after warmed AdamW
+    steps (CE and weight norm to 2e-5 relative, accuracies to four rows:
+    the FP32 run and this f64 restatement drift apart over 250 steps, by
+    up to 2.4e-6 in train CE, 7.5e-6 in held-out CE and three rows of
+    train accuracy for the 16-layer W128 model, while the shallower models
+    agree to 1e-8 and exactly)."""
+    opt = case["optimizer"]
+    config = SimpleConfig(modulus=97, **case["config"])
+    records = train_records(config, opt["operation"], opt["train_fraction"], opt["seed"], steps=case["steps"],
+                            batch=opt["batch"], learning_rate=opt["learning_rate"],
+                            weight_decay=opt["weight_decay"], beta1=opt["beta1"], beta2=opt["beta2"],
+                            epsilon=opt["epsilon"])
+    got, want = records[0], case["step0"]
+    assert abs(got[0] - want[0]) <= 1e-8 * want[0] and abs(got[1] - want[1]) <= 1e-8 * want[1], (got, want)
+    assert abs(got[2] - want[2]) < 1e-9 and abs(got[3] - want[3]) < 1e-9
+    assert abs(got[4] - want[4]) <= 1e-9 * want[4]
+    got, want = records[1], case["later"]
+    assert abs(got[0] - want[0]) <= 2e-5 * want[0] and abs(got[1] - want[1]) <= 2e-5 * want[1], (got, want)
+    assert abs(got[2] - want[2]) <= 4.5 / 4656 and abs(got[3] - want[3]) <= 4.5 / 4656
+    assert abs(got[4] - want[4]) <= 2e-5 * want[4]
