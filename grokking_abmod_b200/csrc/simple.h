@@ -12,7 +12,8 @@ namespace mb {
 namespace simple {
 
 enum Architecture : uint32_t { kMeshMlp = 0, kRotaryDense = 1, kSharedNeighbor = 2, kMlp = 3, kBilinear = 4,
-                               kResidualMlp = 5 };
+                               kResidualMlp = 5, kResidualMesh = 6, kTiedConcatResidualMesh = 7,
+                               kTiedRotaryResidualMesh = 8, kTiedConcatMesh = 9 };
 enum Activation : uint32_t { kRelu = 0, kSquare = 1 };
 enum Connectivity : uint32_t { kOwn = 0, kNeighbor = 1, kButterfly = 2 };
 
@@ -21,6 +22,15 @@ constexpr size_t kMaxRows = 131072;
 constexpr size_t kMaxParameters = (size_t)1 << 28;
 // This build's fused row kernels keep a row per warp in shared memory.
 constexpr uint32_t kMaxKernelWidth = 512;
+
+// src/simple/mod.rs:113-147
+inline bool residual_mesh(const mb_simple_config& c) {
+  return c.architecture == kResidualMesh || c.architecture == kTiedConcatResidualMesh ||
+         c.architecture == kTiedRotaryResidualMesh;
+}
+inline bool tied_concat(const mb_simple_config& c) {
+  return c.architecture == kTiedConcatResidualMesh || c.architecture == kTiedConcatMesh;
+}
 
 void validate(const mb_simple_config& c);                // the reference's rules (MB_ERR_INVALID)
 void validate_kernel_shapes(const mb_simple_config& c);  // this build's kernels (MB_ERR_UNSUPPORTED)

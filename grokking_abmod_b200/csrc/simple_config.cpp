@@ -2,8 +2,8 @@
 // initialisation and one-hot decoding (host side of the C ABI).
 //
 // Restates src/simple/mod.rs: SimpleConfig::validate :561-694 (the rules that
-// concern mesh-mlp, tied-rotary-residual-dense-mlp and
-// shared-neighbor-mesh-mlp), layers :720-756, mesh_layers :758-765, groups
+// concern the ten architectures of this build; full-mesh-mlp and non-one-hot
+// encodings are out), layers :720-756, mesh_layers :758-765, groups
 // :871-889, initial_parameters :938-1036 (default near-identity shared
 // chain, uniform fan-in embedding) and encode :1039-1055.  Compiled with
 // -ffp-contract=off: the f32 uniform draws and the f64 Box-Muller draws
@@ -28,16 +28,24 @@ int stride(const mb_simple_config& c, int layer) {
 }
 
 int mesh_layers(const mb_simple_config& c) {
-  if (c.architecture == kMeshMlp) return (int)c.depth - 1;
+  // src/simple/mod.rs:754-765
+  if (c.architecture == kMeshMlp || c.architecture == kTiedConcatMesh) return (int)c.depth - 1;
+  if (residual_mesh(c)) return (int)(c.depth * c.mesh_depth);
   if (c.architecture == kSharedNeighbor) return (int)(c.embedding_mesh_depth + c.depth);
   return 0;
 }
 
 std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& c) {
   std::vector<std::pair<uint32_t, uint32_t>> l;
-  if (c.architecture == kMeshMlp) {
+  if (c.architecture == kMeshMlp || c.architecture == kResidualMesh) {
     l.push_back({2 * c.modulus, c.width});
     l.push_back({c.width, c.modulus});
+  } else if (tied_concat(c)) {
+    // src/simple/mod.rs:727-729: the shared embedding E, the projection of [E a | E b]
+    l.push_back({c.modulus, c.width});
+    l.push_back({2 * c.width, c.width});
+  } else if (c.architecture == kTiedRotaryResidualMesh) {
+    l.push_back({c.modulus, c.width});
   } else if (c.architecture == kRotaryDense) {
     l.push_back({c.modulus, c.width});
     for (uint32_t i = 0; i < c.depth; ++i) l.push_back({c.width, c.width});
@@ -84,9 +92,10 @@ size_t parameter_count(const mb_simple_config& c) {
 }
 
 void validate(const mb_simple_config& c) {
-  require(c.architecture <= kResidualMlp,
+  require(c.architecture <= kTiedConcatMesh,
           "architecture must be 0 (mesh-mlp), 1 (tied-rotary-residual-dense-mlp), 2 (shared-neighbor-mesh-mlp), "
-          "3 (mlp), 4 (bilinear) or 5 (residual-mlp)",
+          "3 (mlp), 4 (bilinear), 5 (residual-mlp), 6 (residual-mesh-mlp), 7 (tied-concat-residual-mesh-mlp), "
+          "8 (tied-rotary-residual-mesh-mlp) or 9 (tied-concat-mesh-mlp)",
           MB_ERR_UNSUPPORTED);
   require(c.activation <= kSquare, "activation must be 0 (relu) or 1 (square)");
   require(c.connectivity <= kButterfly, "connectivity must be 0 (own), 1 (neighbor) or 2 (butterfly)");
@@ -97,11 +106,17 @@ void validate(const mb_simple_config& c) {
   if (c.architecture == kResidualMlp)
     require(c.expansion >= 1 && (uint64_t)c.width * c.expansion <= kMaxWidth,
             "residual hidden width must be in 1..=16384");
+  if (residual_mesh(c)) require(c.mesh_depth >= 1 && c.mesh_depth <= kMaxDepth, "mesh depth must be in 1..=64");
   if (c.architecture == kSharedNeighbor)
     require(c.embedding_mesh_depth >= 1 && c.embedding_mesh_depth <= kMaxDepth,
             "shared Neighbor embedding depth must be in 1..=64");
+  require(c.mesh_output_activation <= 1, "mesh output activation must be 0 or 1");
+  if (c.mesh_output_activation)
+    require(residual_mesh(c), "only residual mesh branches activate their final mesh output");
   if (mesh_layers(c) > 0 && parents(c) == 2) require(c.width >= 2, "a second mesh parent needs a width of at least 2");
-  if (c.architecture == kRotaryDense || c.architecture == kSharedNeighbor)
+  if (tied_concat(c))
+    require(2 * (uint64_t)c.width <= kMaxWidth, "tied concatenation needs one-hot encoding and width <= 8192");
+  if (c.architecture == kRotaryDense || c.architecture == kSharedNeighbor || c.architecture == kTiedRotaryResidualMesh)
     require(c.width >= 2 && c.width % 2 == 0, "rotary roles need one-hot encoding and a positive even width");
   if (c.full_mesh_initialization != 0)
     require(c.architecture == kSharedNeighbor, "only a full mesh configures its mesh initialization");

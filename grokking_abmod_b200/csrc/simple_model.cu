@@ -1,6 +1,8 @@
 // grok-simple executor (host C++) and its kernels: mesh-mlp,
-// tied-rotary-residual-dense-mlp, shared-neighbor-mesh-mlp, mlp, bilinear
-// and residual-mlp.
+// tied-rotary-residual-dense-mlp, shared-neighbor-mesh-mlp, mlp, bilinear,
+// residual-mlp, the residual mesh family (residual-mesh-mlp,
+// tied-concat-residual-mesh-mlp, tied-rotary-residual-mesh-mlp) and
+// tied-concat-mesh-mlp.
 //
 // Replaces GpuSimpleModel (src/simple/gpu.rs:1757-2073) and its op-by-op
 // plans (forward_with / backward_with, :2140-2700).  One training step is a
@@ -123,24 +125,22 @@ __global__ void gather_batch(int n, const StepScalars* __restrict__ sc, const ui
 }
 
 // ------------------------------------------------------------- mesh-mlp
-// h0 = W0[a] + W0[m + b]; per mesh layer h' = act(h)[c] w0 + act(h)[c+s] w1;
-// act = act(h_L) feeds the readout GEMM.  h[l] (l = 0..L) is kept for the
-// backward.
+// h0 = W0[a] + W0[m + b] (or h0_in, the tied-concat projection, when given);
+// per mesh layer h' = act(h)[c] w0 + act(h)[c+s] w1; act = act(h_L) feeds the
+// readout GEMM.  h[l] (l = 0..L) is kept for the backward.
 template <int ACT, int J>
 __global__ void __launch_bounds__(kFwdWarps * 32)
     mlp_forward(int n, int W, int m, int L, int p, const int* __restrict__ strides, const uint32_t* __restrict__ a,
-                const uint32_t* __restrict__ b, const float* __restrict__ w0, const float* __restrict__ mesh,
-                float* __restrict__ h, float* __restrict__ act) {
+                const uint32_t* __restrict__ b, const float* __restrict__ w0, const float* __restrict__ h0_in,
+                const float* __restrict__ mesh, float* __restrict__ h, float* __restrict__ act) {
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
   if (r >= n) return;
   float* row = sm + warp * W;
-  const float* ea = w0 + (size_t)a[r] * W;
-  const float* eb = w0 + (size_t)(m + b[r]) * W;
   const size_t nw = (size_t)n * W;
   for (int c = lane; c < W; c += 32) {
-    const float v = ea[c] + eb[c];
+    const float v = h0_in != nullptr ? h0_in[(size_t)r * W + c] : w0[(size_t)a[r] * W + c] + w0[(size_t)(m + b[r]) * W + c];
     h[(size_t)r * W + c] = v;
     row[c] = act_f<ACT>(v);
   }
@@ -367,10 +367,10 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     const int c = lane + 32 * j;
     if (c < W) {
       h0[(size_t)r * W + c] = v[j];
-      n0[(size_t)r * W + c] = v[j] * inv;
+      if (n0 != nullptr) n0[(size_t)r * W + c] = v[j] * inv;
     }
   }
-  if (lane == 0) inv0[r] = inv;
+  if (inv0 != nullptr && lane == 0) inv0[r] = inv;
 }
 
 // dx = add + inv (dy - y <dy, y> / W) with y the normalised row.
@@ -582,6 +582,7 @@ __global__ void __launch_bounds__(kChainThreads)
 
 // The core's weights, staged in shared memory when they fit (depth x 3W).
 constexpr int kCoreSmemFloats = 24576;  // 96 KiB
+constexpr int kSmemFloats = 57344;      // 224 KiB: the dynamic shared memory a CTA may use
 __device__ __forceinline__ const float* stage_core(const float* __restrict__ core, int n_floats, float* sm) {
   if (n_floats > kCoreSmemFloats) return core;
   for (int i = threadIdx.x; i < n_floats; i += blockDim.x) sm[i] = core[i];
@@ -776,6 +777,244 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
   }
 }
 
+// ------------------------------------------------------- residual mesh
+// residual-mesh-mlp, tied-concat-residual-mesh-mlp and
+// tied-rotary-residual-mesh-mlp blocks (src/simple/reference.rs:337-407):
+// per block n = RMSNorm(h); the branch runs md mesh layers
+//   z_l[c] = x_l[c] w0 + x_l[c+s] w1   (w1 only with two parents)
+// with x_0 = n and x_l = act(z_{l-1}), ends in act(z) with the output
+// activation, else z, and h += branch.  The mesh weights of all depth * md
+// layers are staged in shared memory when `staged` is nonzero.  Kept for the
+// backward: ns[b] / invs[b] (each block's normalised input and 1/rms),
+// zs[b * md + l] (every pre-activation), hf / invf (the final RMSNorm).
+template <int ACT, int J, int P>
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    resmesh_forward(int n, int W, int depth, int md, int moa, int staged, const int* __restrict__ strides,
+                    const float* __restrict__ mesh, const float* __restrict__ h0, float* __restrict__ ns,
+                    float* __restrict__ invs, float* __restrict__ zs, float* __restrict__ hf,
+                    float* __restrict__ invf) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  const float* wts = mesh;
+  if (staged) {
+    for (int i = threadIdx.x; i < staged; i += blockDim.x) sm[i] = mesh[i];
+    __syncthreads();
+    wts = sm;
+  }
+  if (r >= n) return;
+  float* row = sm + staged + warp * W;
+  const size_t nw = (size_t)n * W;
+  float h[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = lane + 32 * j;
+    h[j] = c < W ? h0[(size_t)r * W + c] : 0.f;
+  }
+  for (int blk = 0; blk < depth; ++blk) {
+    const float inv = row_inverse_rms<J>(h, W, lane);
+    float x[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = lane + 32 * j;
+      x[j] = h[j] * inv;
+      if (c < W) ns[blk * nw + (size_t)r * W + c] = x[j];
+    }
+    if (lane == 0) invs[(size_t)blk * n + r] = inv;
+    for (int l = 0; l < md; ++l) {
+      const int layer = blk * md + l;
+      const int s = strides[layer];
+      const float* w = wts + (size_t)layer * P * W;
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int c = lane + 32 * j;
+        if (c < W) row[c] = x[j];
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int c = lane + 32 * j;
+        if (c < W) {
+          float z = x[j] * w[P * c];
+          if (P == 2) z = fmaf(row[wrap_up(c, s, W)], w[P * c + 1], z);
+          zs[layer * nw + (size_t)r * W + c] = z;
+          x[j] = (l + 1 < md || moa) ? act_f<ACT>(z) : z;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) h[j] += x[j];
+  }
+  const float inv = row_inverse_rms<J>(h, W, lane);
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int c = lane + 32 * j;
+    if (c < W) hf[(size_t)r * W + c] = h[j] * inv;
+  }
+  if (lane == 0) invf[r] = inv;
+}
+
+// Backward of the residual mesh blocks: dhf (gradient of the final RMSNorm
+// output) in, dh0 out; per-CTA weight partials [gridDim.x][depth * md][P W]
+// in parameter order.  Each warp walks its kBwdRows rows through every
+// layer; the layer's weight contributions are summed per warp in registers
+// in row order, then over the warps in order.
+template <int ACT, int J, int P>
+__global__ void __launch_bounds__(kBwdWarps * 32)
+    resmesh_backward(int n, int W, int depth, int md, int moa, int staged, const int* __restrict__ strides,
+                     const float* __restrict__ mesh, const float* __restrict__ ns, const float* __restrict__ invs,
+                     const float* __restrict__ zs, const float* __restrict__ hf, const float* __restrict__ invf,
+                     const float* __restrict__ dhf, float* __restrict__ dh0, float* __restrict__ partials) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pw = P * W;
+  const float* wts = mesh;
+  if (staged) {
+    for (int i = threadIdx.x; i < staged; i += blockDim.x) sm[i] = mesh[i];
+    __syncthreads();
+    wts = sm;
+  }
+  float* xrow = sm + staged + warp * 2 * W;  // the layer input x_l of the current row
+  float* zrow = xrow + W;                    // dz of the current row
+  float* contrib = sm + staged + kBwdWarps * 2 * W;
+  const size_t nw = (size_t)n * W;
+  const int layers = depth * md;
+  float dh[kBwdRows][J], dz[kBwdRows][J];
+#pragma unroll
+  for (int i = 0; i < kBwdRows; ++i) {
+    const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+    const bool active = r < n;
+    float yv[J], dv[J], dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = lane + 32 * j;
+      yv[j] = (active && c < W) ? hf[(size_t)r * W + c] : 0.f;
+      dv[j] = (active && c < W) ? dhf[(size_t)r * W + c] : 0.f;
+      dot = fmaf(dv[j], yv[j], dot);
+    }
+    dot = warp_sum(dot) / (float)W;
+    const float iv = active ? invf[r] : 0.f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) dh[i][j] = iv * (dv[j] - yv[j] * dot);
+  }
+  for (int blk = depth - 1; blk >= 0; --blk) {
+    // The branch output's gradient is dh (through the output activation).
+#pragma unroll
+    for (int i = 0; i < kBwdRows; ++i) {
+      const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int c = lane + 32 * j;
+        dz[i][j] = dh[i][j];
+        if (moa && r < n && c < W) dz[i][j] *= act_g<ACT>(zs[(blk * md + md - 1) * nw + (size_t)r * W + c]);
+      }
+    }
+    for (int l = md - 1; l >= 0; --l) {
+      const int layer = blk * md + l;
+      const int s = strides[layer];
+      const float* w = wts + (size_t)layer * pw;
+      float* mine = contrib + warp * pw;
+      float g0[J], g1[J];
+#pragma unroll
+      for (int j = 0; j < J; ++j) g0[j] = g1[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < kBwdRows; ++i) {
+        const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+        const bool active = r < n;
+        float zp[J];  // z_{l-1}: the layer input is act(z_{l-1}) (n for l = 0)
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+          const int c = lane + 32 * j;
+          if (c < W) {
+            float x;
+            if (l > 0) {
+              zp[j] = active ? zs[(layer - 1) * nw + (size_t)r * W + c] : 0.f;
+              x = act_f<ACT>(zp[j]);
+            } else {
+              zp[j] = 0.f;
+              x = active ? ns[blk * nw + (size_t)r * W + c] : 0.f;
+            }
+            xrow[c] = x;
+            zrow[c] = dz[i][j];
+          }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+          const int c = lane + 32 * j;
+          if (c < W) {
+            const float d = zrow[c];
+            g0[j] += d * xrow[c];
+            float dx = d * w[P * c];
+            if (P == 2) {
+              g1[j] += d * xrow[wrap_up(c, s, W)];
+              const int q = wrap_down(c, s, W);
+              dx = fmaf(zrow[q], w[P * q + 1], dx);
+            }
+            dz[i][j] = l > 0 ? dx * act_g<ACT>(zp[j]) : dx;
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int c = lane + 32 * j;
+        if (c < W) {
+          mine[P * c] = g0[j];
+          if (P == 2) mine[P * c + 1] = g1[j];
+        }
+      }
+      __syncthreads();
+      for (int t = threadIdx.x; t < pw; t += blockDim.x) {
+        float sum = 0.f;
+        for (int q = 0; q < kBwdWarps; ++q) sum += contrib[q * pw + t];
+        partials[((size_t)blockIdx.x * layers + layer) * pw + t] = sum;
+      }
+      __syncthreads();
+    }
+    // dz now holds dn: dh += inv (dn - n <dn, n> / W)
+#pragma unroll
+    for (int i = 0; i < kBwdRows; ++i) {
+      const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+      const bool active = r < n;
+      float nv[J], dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int c = lane + 32 * j;
+        nv[j] = (active && c < W) ? ns[blk * nw + (size_t)r * W + c] : 0.f;
+        dot = fmaf(dz[i][j], nv[j], dot);
+      }
+      dot = warp_sum(dot) / (float)W;
+      const float iv = active ? invs[(size_t)blk * n + r] : 0.f;
+#pragma unroll
+      for (int j = 0; j < J; ++j) dh[i][j] += iv * (dz[i][j] - nv[j] * dot);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kBwdRows; ++i) {
+    const int r = (blockIdx.x * kBwdWarps + warp) * kBwdRows + i;
+    if (r >= n) continue;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int c = lane + 32 * j;
+      if (c < W) dh0[(size_t)r * W + c] = dh[i][j];
+    }
+  }
+}
+
+// Tied concatenation (src/simple/reference.rs:303-306, :355-359): the row
+// [E a | E b] of each batch row, [n][2W].
+__global__ void concat_rows(int n, int W, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
+                            const float* __restrict__ E, float* __restrict__ cat) {
+  const size_t total = (size_t)n * 2 * W;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / (2 * W);
+    const int c = (int)(i % (2 * W));
+    cat[i] = c < W ? E[(size_t)a[r] * W + c] : E[(size_t)b[r] * W + (c - W)];
+  }
+}
+
 // ------------------------------------------------------- mlp, bilinear
 // mlp input layer on one-hot rows (src/simple/reference.rs:292-299): x W0
 // with x one-hot at a and at m + b is W0[a] + W0[m + b]; z keeps the
@@ -831,6 +1070,8 @@ __global__ void bilinear_gradient(int n, int W, const uint32_t* __restrict__ a, 
 //         the transposed rotation of dh0[r] (dh0[r][c^1], negated for odd c).
 //  mode 2 / 3 (bilinear, m rows of one operand's embedding): rows with
 //         a == k (mode 2) or b == k (mode 3) add dh0[r][c].
+//  mode 4 (tied concatenation, dh0 rows of 2W): rows with a == k add
+//         dh0[r][c], rows with b == k add dh0[r][W + c].
 // `extra` ([rows][W], may be null) is added (the readout's share of dE).
 constexpr int kClassThreads = 256;
 __global__ void __launch_bounds__(kClassThreads)
@@ -851,9 +1092,9 @@ __global__ void __launch_bounds__(kClassThreads)
     if (r < n) {
       if (mode == 0) {
         kind = (k < m) ? (a[r] == (uint32_t)k ? 1 : 0) : (b[r] == (uint32_t)(k - m) ? 1 : 0);
-      } else if (mode >= 2) {
+      } else if (mode == 2 || mode == 3) {
         kind = (mode == 2 ? a[r] : b[r]) == (uint32_t)k ? 1 : 0;
-      } else {
+      } else {  // modes 1 and 4
         kind = (a[r] == (uint32_t)k ? 1 : 0) | (b[r] == (uint32_t)k ? 2 : 0);
       }
     }
@@ -878,13 +1119,13 @@ __global__ void __launch_bounds__(kClassThreads)
     __syncthreads();
     for (int e = 0; e < total; ++e) {
       const int rr = list[e], kd = kinds[e];
-      const float* g = dh0 + (size_t)rr * W;
+      const float* g = dh0 + (size_t)rr * (mode == 4 ? 2 * W : W);
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
         const int c = tid + kClassThreads * j;
         if (c < W) {
           if (kd & 1) acc[j] += g[c];
-          if (kd & 2) acc[j] += (c & 1) ? -g[c ^ 1] : g[c ^ 1];
+          if (kd & 2) acc[j] += mode == 4 ? g[W + c] : ((c & 1) ? -g[c ^ 1] : g[c ^ 1]);
         }
       }
     }
@@ -1002,12 +1243,15 @@ class DeviceBuffers {
 struct Workspace {
   int n = 0;
   DeviceBuffers mem;
-  uint32_t *a, *b, *y;
-  float *logits, *dlog;
-  float *h, *act, *dact, *dh0, *part;  // mesh-mlp
-  float *hs, *ns, *invs, *zs, *dh, *dz, *dn, *dhf, *dEread, *gemm_part;
-  float *hf, *invf, *states, *dEemb, *dv, *dv2;  // shared-Neighbor
-  float *es, *as, *dex, *dax;                     // residual-mlp expansion
+  uint32_t *a = nullptr, *b = nullptr, *y = nullptr;
+  float *logits = nullptr, *dlog = nullptr;
+  float *h = nullptr, *act = nullptr, *dact = nullptr, *dh0 = nullptr, *part = nullptr;  // mesh-mlp
+  float *hs = nullptr, *ns = nullptr, *invs = nullptr, *zs = nullptr, *dh = nullptr, *dz = nullptr, *dn = nullptr,
+        *dhf = nullptr, *dEread = nullptr, *gemm_part = nullptr;
+  float *hf = nullptr, *invf = nullptr, *states = nullptr, *dEemb = nullptr, *dv = nullptr,
+        *dv2 = nullptr;                                           // shared-Neighbor
+  float *es = nullptr, *as = nullptr, *dex = nullptr, *dax = nullptr;  // residual-mlp expansion
+  float *cat = nullptr, *dcat = nullptr;  // tied concatenation [E a | E b] and its gradient
   int bwd_ctas = 0;
   cudaGraphExec_t step_graph = nullptr;
   uint32_t step_launches = 0;
@@ -1063,7 +1307,9 @@ class SimpleModel {
     scalars_ = mem_.alloc<StepScalars>(1);
     SIMPLE_CUDA(cudaMemsetAsync(flags_, 0, kFlags * sizeof(int), stream_));
     SIMPLE_CUDA(cudaMemsetAsync(grad_, 0, P_ * sizeof(float), stream_));
-    const int nstr = c.architecture == kMeshMlp ? std::max(1, mesh_layers(c)) : std::max(1, (int)c.depth);
+    // Strides per mesh layer (mesh stacks) or per core layer (shared-Neighbor).
+    const bool per_mesh = c.architecture == kMeshMlp || c.architecture == kTiedConcatMesh || residual_mesh(c);
+    const int nstr = per_mesh ? std::max(1, mesh_layers(c)) : std::max(1, (int)c.depth);
     std::vector<int> st(nstr);
     for (int l = 0; l < nstr; ++l) st[l] = stride(c, l);
     strides_ = mem_.alloc<int>(nstr);
@@ -1279,6 +1525,18 @@ class SimpleModel {
     return RG >= 1 && 2 * m * W <= kChainSmemFloats && m <= kChainRows * RG;
   }
   int bwd_smem() const { return (core_smem_floats() + kBwdWarps * 5 * (int)c_.width) * 4; }
+  // Residual mesh kernels: all mesh weights staged in shared memory when
+  // they fit beside the backward's per-warp rows and contributions.
+  int resmesh_staged() const {
+    if (!residual_mesh(c_)) return 0;
+    const int f = mesh_layers(c_) * parents(c_) * (int)c_.width;
+    const int rows = kBwdWarps * (2 + parents(c_)) * (int)c_.width;
+    return f <= kCoreSmemFloats && f + rows <= kSmemFloats ? f : 0;
+  }
+  int resmesh_fwd_smem() const { return (resmesh_staged() + kFwdWarps * (int)c_.width) * 4; }
+  int resmesh_bwd_smem() const {
+    return (resmesh_staged() + kBwdWarps * (2 + parents(c_)) * (int)c_.width) * 4;
+  }
 
   template <int ACT>
   void set_attributes_impl() {
@@ -1289,6 +1547,13 @@ class SimpleModel {
       SIMPLE_CUDA(cudaFuncSetAttribute(&mlp_backward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, bs));
       SIMPLE_CUDA(cudaFuncSetAttribute(&shared_forward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, fs));
       SIMPLE_CUDA(cudaFuncSetAttribute(&shared_backward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, bs));
+      if (residual_mesh(c_)) {
+        const int rf = resmesh_fwd_smem(), rb = resmesh_bwd_smem();
+        SIMPLE_CUDA(cudaFuncSetAttribute(&resmesh_forward<ACT, J, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, rf));
+        SIMPLE_CUDA(cudaFuncSetAttribute(&resmesh_forward<ACT, J, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, rf));
+        SIMPLE_CUDA(cudaFuncSetAttribute(&resmesh_backward<ACT, J, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, rb));
+        SIMPLE_CUDA(cudaFuncSetAttribute(&resmesh_backward<ACT, J, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, rb));
+      }
     });
   }
   void set_attributes() {
@@ -1341,13 +1606,33 @@ class SimpleModel {
     const int ctas = (int)((N + kBwdWarps * kBwdRows - 1) / (kBwdWarps * kBwdRows));
     w->bwd_ctas = ctas;
     size_t part = 0;
-    if (c_.architecture == kMeshMlp) {
+    if (tied_concat(c_)) {
+      w->cat = M.alloc<float>(2 * nw);
+      w->dcat = M.alloc<float>(2 * nw);
+      w->dEread = M.alloc<float>(m * W);
+      part = std::max(gemm_partial_floats((int)(2 * W), (int)W, n, kSplitK),
+                      gemm_partial_floats((int)m, (int)W, n, kSplitK));
+    }
+    if (c_.architecture == kMeshMlp || c_.architecture == kTiedConcatMesh) {
       const int L = mesh_layers(c_);
       w->h = M.alloc<float>((L + 1) * nw);
       w->act = M.alloc<float>(nw);
       w->dact = w->dhf;
       w->part = M.alloc<float>((size_t)ctas * std::max(L, 1) * parents(c_) * W);
-      part = gemm_partial_floats((int)W, (int)m, n, kSplitK);
+      part = std::max(part, gemm_partial_floats((int)W, (int)m, n, kSplitK));
+    } else if (residual_mesh(c_)) {
+      // h0, per block ns / invs, every mesh pre-activation zs, hf / invf
+      const size_t d = c_.depth, L = (size_t)mesh_layers(c_);
+      w->h = M.alloc<float>(nw);
+      w->ns = M.alloc<float>(d * nw);
+      w->invs = M.alloc<float>(d * N);
+      w->zs = M.alloc<float>(L * nw);
+      w->hf = M.alloc<float>(nw);
+      w->invf = M.alloc<float>(N);
+      w->part = M.alloc<float>((size_t)ctas * L * parents(c_) * W);
+      if (w->dEread == nullptr) w->dEread = M.alloc<float>(m * W);
+      part = std::max({part, gemm_partial_floats((int)W, (int)m, n, kSplitK),
+                       gemm_partial_floats((int)m, (int)W, n, kSplitK)});
     } else if (c_.architecture == kMlp) {
       // zs: pre-activations of layers 0..depth-1, hs: their activations
       const size_t d = c_.depth;
@@ -1420,6 +1705,25 @@ class SimpleModel {
     SIMPLE_CUDA(cudaGetLastError());
   }
 
+  // h0 = [E a | E b] . Pj (Pj [2W][W]); ws.cat keeps the concatenation.
+  void enqueue_concat(Workspace& ws, const float* E, const float* Pj, float* h0) {
+    const int n = ws.n, W = (int)c_.width;
+    const size_t total = (size_t)n * 2 * W;
+    concat_rows<<<(int)std::min<size_t>((total + 255) / 256, 1184), 256, 0, stream_>>>(n, W, ws.a, ws.b, E,
+                                                                                      ws.cat); ++launches_;
+    gemm({ws.cat, 2 * W, false}, {Pj, W, true}, h0, W, n, W, 2 * W, nullptr);
+  }
+
+  // Gradients of the tied concatenation from dh0: dPj = cat^T dh0, dcat =
+  // dh0 Pj^T, and dE = the per-class sums of dcat's halves plus `extra`.
+  void enqueue_concat_backward(Workspace& ws, const float* dh0, const float* extra) {
+    const int n = ws.n, W = (int)c_.width, m = (int)c_.modulus;
+    const float* Pj = w_ + offsets_[1];
+    gemm({ws.cat, 2 * W, true}, {dh0, W, true}, grad_ + offsets_[1], W, 2 * W, W, n, ws.gemm_part, kSplitK);
+    gemm({dh0, W, false}, {Pj, W, false}, ws.dcat, 2 * W, n, 2 * W, W, nullptr);
+    class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 4, ws.a, ws.b, ws.dcat, extra, grad_ + offsets_[0]); ++launches_;
+  }
+
   template <int ACT>
   void forward_impl(Workspace& ws) {
     with_j((int)c_.width, [&](auto jc) { forward_j<ACT, decltype(jc)::value>(ws); });
@@ -1435,9 +1739,43 @@ class SimpleModel {
       const int L = mesh_layers(c_), p = parents(c_);
       const float* R = w + offsets_[1];
       mlp_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
-          n, W, m, L, p, strides_, ws.a, ws.b, w + offsets_[0], w + (L > 0 ? offsets_[2] : 0), ws.h, ws.act); ++launches_;
+          n, W, m, L, p, strides_, ws.a, ws.b, w + offsets_[0], nullptr, w + (L > 0 ? offsets_[2] : 0), ws.h,
+          ws.act); ++launches_;
       // logits = act . R  (R [W][m]: B element (j, c) at R[c * m + j])
       gemm({ws.act, W, false}, {R, m, true}, ws.logits, m, n, m, W, nullptr);
+    } else if (c_.architecture == kTiedConcatMesh) {
+      // src/simple/reference.rs:300-335: h0 = [E a | E b] Pj, the mesh stack
+      // of mesh-mlp, logits = act(h_L) E^T
+      const int L = mesh_layers(c_), p = parents(c_);
+      const float* E = w + offsets_[0];
+      enqueue_concat(ws, E, w + offsets_[1], ws.h);
+      mlp_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
+          n, W, m, L, p, strides_, ws.a, ws.b, nullptr, ws.h, w + (L > 0 ? offsets_[2] : 0), ws.h, ws.act); ++launches_;
+      gemm({ws.act, W, false}, {E, W, false}, ws.logits, m, n, m, W, nullptr);
+    } else if (residual_mesh(c_)) {
+      // src/simple/reference.rs:337-407
+      const float* E = w + offsets_[0];
+      if (c_.architecture == kResidualMesh) {
+        concat_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, m, ws.a, ws.b, E, ws.h, nullptr, nullptr); ++launches_;
+      } else if (c_.architecture == kTiedRotaryResidualMesh) {
+        rotary_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.a, ws.b, E, ws.h, nullptr, nullptr); ++launches_;
+      } else {
+        enqueue_concat(ws, E, w + offsets_[1], ws.h);
+      }
+      const float* mesh = w + offsets_[dense_layers(c_).size()];
+      const int d = (int)c_.depth, md = (int)c_.mesh_depth, moa = (int)c_.mesh_output_activation;
+      const int st = resmesh_staged();
+      if (parents(c_) == 2)
+        resmesh_forward<ACT, J, 2><<<fgrid, kFwdWarps * 32, resmesh_fwd_smem(), stream_>>>(
+            n, W, d, md, moa, st, strides_, mesh, ws.h, ws.ns, ws.invs, ws.zs, ws.hf, ws.invf);
+      else
+        resmesh_forward<ACT, J, 1><<<fgrid, kFwdWarps * 32, resmesh_fwd_smem(), stream_>>>(
+            n, W, d, md, moa, st, strides_, mesh, ws.h, ws.ns, ws.invs, ws.zs, ws.hf, ws.invf);
+      ++launches_;
+      if (c_.architecture == kResidualMesh)  // logits = hf . R  (R [W][m])
+        gemm({ws.hf, W, false}, {w + offsets_[1], m, true}, ws.logits, m, n, m, W, nullptr);
+      else  // logits = hf . E^T
+        gemm({ws.hf, W, false}, {E, W, false}, ws.logits, m, n, m, W, nullptr);
     } else if (c_.architecture == kMlp) {
       const int d = (int)c_.depth;
       const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
@@ -1546,6 +1884,60 @@ class SimpleModel {
             nw, ws.dact, ws.h, ws.dh0); ++launches_;
       }
       class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr, g + offsets_[0]); ++launches_;
+    } else if (c_.architecture == kTiedConcatMesh) {
+      const int L = mesh_layers(c_), p = parents(c_);
+      const float* E = w + offsets_[0];
+      // dE (readout share) = dlog^T . act ; dact = dlog . E
+      gemm({ws.dlog, m, true}, {ws.act, W, true}, ws.dEread, W, m, W, n, ws.gemm_part, kSplitK);
+      gemm({ws.dlog, m, false}, {E, W, true}, ws.dact, W, n, W, m, nullptr);
+      if (L > 0) {
+        mlp_backward<ACT, J><<<ws.bwd_ctas, kBwdWarps * 32, bsm, stream_>>>(n, W, L, p, strides_, w + offsets_[2],
+                                                                            ws.h, ws.dact, ws.dh0, ws.part); ++launches_;
+        const size_t cnt = (size_t)L * p * W;
+        reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
+            ws.part, ws.bwd_ctas, cnt, g + offsets_[2]); ++launches_;
+      } else {
+        activation_gradient<ACT><<<(int)std::min<size_t>((nw + 255) / 256, 1184), 256, 0, stream_>>>(
+            nw, ws.dact, ws.h, ws.dh0); ++launches_;
+      }
+      enqueue_concat_backward(ws, ws.dh0, ws.dEread);
+    } else if (residual_mesh(c_)) {
+      const float* E = w + offsets_[0];
+      const bool tied = c_.architecture != kResidualMesh;
+      if (tied) {
+        // dE (readout share) = dlog^T . hf ; dhf = dlog . E
+        gemm({ws.dlog, m, true}, {ws.hf, W, true}, ws.dEread, W, m, W, n, ws.gemm_part, kSplitK);
+        gemm({ws.dlog, m, false}, {E, W, true}, ws.dhf, W, n, W, m, nullptr);
+      } else {
+        const float* R = w + offsets_[1];
+        // dR = hf^T . dlog ; dhf = dlog . R^T
+        gemm({ws.hf, W, true}, {ws.dlog, m, true}, g + offsets_[1], m, W, m, n, ws.gemm_part, kSplitK);
+        gemm({ws.dlog, m, false}, {R, m, false}, ws.dhf, W, n, W, m, nullptr);
+      }
+      const size_t mesh_off = offsets_[dense_layers(c_).size()];
+      const int d = (int)c_.depth, md = (int)c_.mesh_depth, moa = (int)c_.mesh_output_activation;
+      const int st = resmesh_staged(), p = parents(c_);
+      if (p == 2)
+        resmesh_backward<ACT, J, 2><<<ws.bwd_ctas, kBwdWarps * 32, resmesh_bwd_smem(), stream_>>>(
+            n, W, d, md, moa, st, strides_, w + mesh_off, ws.ns, ws.invs, ws.zs, ws.hf, ws.invf, ws.dhf, ws.dh0,
+            ws.part);
+      else
+        resmesh_backward<ACT, J, 1><<<ws.bwd_ctas, kBwdWarps * 32, resmesh_bwd_smem(), stream_>>>(
+            n, W, d, md, moa, st, strides_, w + mesh_off, ws.ns, ws.invs, ws.zs, ws.hf, ws.invf, ws.dhf, ws.dh0,
+            ws.part);
+      ++launches_;
+      const size_t cnt = (size_t)mesh_layers(c_) * p * W;
+      reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
+          ws.part, ws.bwd_ctas, cnt, g + mesh_off); ++launches_;
+      if (c_.architecture == kResidualMesh) {
+        class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr,
+                                                             g + offsets_[0]); ++launches_;
+      } else if (c_.architecture == kTiedRotaryResidualMesh) {
+        class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 1, ws.a, ws.b, ws.dh0, ws.dEread,
+                                                         g + offsets_[0]); ++launches_;
+      } else {
+        enqueue_concat_backward(ws, ws.dh0, ws.dEread);
+      }
     } else if (c_.architecture == kMlp) {
       const int d = (int)c_.depth;
       const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);

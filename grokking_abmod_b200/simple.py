@@ -3,9 +3,11 @@
 Python mirror of the reference's ``SimpleConfig`` (src/simple/mod.rs:500-1055)
 and ``GpuSimpleModel`` (src/simple/gpu.rs:1757-2073): same names, argument
 meaning and error behaviour (a nonzero library status raises
-``MeshError``).  Six architectures run on this path: ``mesh-mlp``,
+``MeshError``).  Ten architectures run on this path: ``mesh-mlp``,
 ``tied-rotary-residual-dense-mlp``, ``shared-neighbor-mesh-mlp``, ``mlp``,
-``bilinear`` and ``residual-mlp``, with one-hot operands.  There is no CPU
+``bilinear``, ``residual-mlp``, ``residual-mesh-mlp``,
+``tied-concat-residual-mesh-mlp``, ``tied-rotary-residual-mesh-mlp`` and
+``tied-concat-mesh-mlp``, with one-hot operands.  There is no CPU
 fallback.
 """
 
@@ -21,7 +23,8 @@ from .data import EquationDataset, EquationSampler
 from .gpt import AdamWOptions
 
 ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear",
-                 "residual-mlp")
+                 "residual-mlp", "residual-mesh-mlp", "tied-concat-residual-mesh-mlp",
+                 "tied-rotary-residual-mesh-mlp", "tied-concat-mesh-mlp")
 ACTIVATIONS = ("relu", "square")
 CONNECTIVITIES = ("own", "neighbor", "butterfly")
 INITIALIZATIONS = ("kaiming", "identity-hidden")
@@ -29,7 +32,7 @@ INITIALIZATIONS = ("kaiming", "identity-hidden")
 
 @dataclass(frozen=True)
 class SimpleConfig:
-    """``SimpleConfig`` fields read by the six architectures (reference
+    """``SimpleConfig`` fields read by the ten architectures (reference
     defaults)."""
     architecture: str = "mesh-mlp"
     activation: str = "relu"
@@ -41,6 +44,8 @@ class SimpleConfig:
     full_mesh_initialization: str = "kaiming"
     mesh_learning_rate_multiplier: int = 1
     expansion: int = 4
+    mesh_depth: int = 4
+    mesh_output_activation: bool = False
 
     def with_(self, **kw):
         return replace(self, **kw)
@@ -55,7 +60,8 @@ class SimpleConfig:
                              self.depth, index(CONNECTIVITIES, self.connectivity, "mesh connectivity"),
                              self.embedding_mesh_depth,
                              index(INITIALIZATIONS, self.full_mesh_initialization, "full-mesh initialization"),
-                             self.mesh_learning_rate_multiplier, self.expansion)
+                             self.mesh_learning_rate_multiplier, self.expansion, self.mesh_depth,
+                             int(self.mesh_output_activation))
 
     def validate(self):
         c = self.to_c()

@@ -251,6 +251,8 @@ typedef struct mb_simple_config {
   uint32_t full_mesh_initialization;
   uint32_t mesh_learning_rate_multiplier;
   uint32_t expansion;
+  uint32_t mesh_depth;             /* mesh layers per residual mesh branch (6-8) */
+  uint32_t mesh_output_activation; /* 1: activate a residual mesh branch's output (6-8) */
 } mb_simple_config;
 
 typedef struct mb_simple mb_simple;

@@ -132,7 +132,14 @@ def _simple_pairs():
                dict(architecture="shared-neighbor-mesh-mlp", width=128, depth=64, embedding_mesh_depth=32,
                     full_mesh_initialization="identity-hidden"),
                dict(architecture="shared-neighbor-mesh-mlp", modulus=7, width=8, depth=3, embedding_mesh_depth=2,
-                    connectivity="butterfly", mesh_learning_rate_multiplier=3)):
+                    connectivity="butterfly", mesh_learning_rate_multiplier=3),
+               dict(architecture="residual-mesh-mlp", width=64, depth=2, mesh_depth=4),
+               dict(architecture="residual-mesh-mlp", modulus=7, width=6, depth=3, mesh_depth=2, connectivity="own"),
+               dict(architecture="tied-concat-residual-mesh-mlp", width=128, depth=2, mesh_depth=3,
+                    activation="square", connectivity="butterfly"),
+               dict(architecture="tied-rotary-residual-mesh-mlp", width=128, depth=1, mesh_depth=1,
+                    mesh_output_activation=True, mesh_learning_rate_multiplier=2),
+               dict(architecture="tied-concat-mesh-mlp", width=64, depth=5, connectivity="own")):
         yield OracleSimpleConfig(**kw), SimpleConfig(**kw)
 
 
@@ -158,12 +165,25 @@ def test_simple_validation_mirrors_the_reference():
            dict(architecture="mesh-mlp", full_mesh_initialization="identity-hidden"),
            dict(architecture="mesh-mlp", depth=1, mesh_learning_rate_multiplier=2),
            dict(architecture="mesh-mlp", depth=0), dict(architecture="mesh-mlp", depth=65),
-           dict(architecture="mesh-mlp", modulus=1), dict(architecture="mesh-mlp", modulus=1025)]
+           dict(architecture="mesh-mlp", modulus=1), dict(architecture="mesh-mlp", modulus=1025),
+           dict(architecture="residual-mesh-mlp", mesh_depth=0), dict(architecture="residual-mesh-mlp", mesh_depth=65),
+           dict(architecture="mesh-mlp", mesh_output_activation=True),
+           dict(architecture="tied-concat-mesh-mlp", mesh_output_activation=True),
+           dict(architecture="tied-rotary-residual-mesh-mlp", width=127),
+           dict(architecture="tied-concat-residual-mesh-mlp", width=8193)]
     for kw in bad:
         with pytest.raises(MeshError):
             SimpleConfig(**kw).validate()
     with pytest.raises(ValueError):
-        SimpleConfig(architecture="residual-mesh-mlp").to_c()
+        SimpleConfig(architecture="full-mesh-mlp").to_c()
+    # src/simple/mod.rs:1446-1760 (parameter counts of the mesh architectures)
+    assert SimpleConfig(architecture="residual-mesh-mlp", width=64, depth=2, mesh_depth=4).parameter_count() == 19648
+    assert SimpleConfig(architecture="tied-rotary-residual-mesh-mlp", width=128, depth=2,
+                        mesh_depth=3).groups() == [12416] + [256] * 6
+    assert SimpleConfig(architecture="tied-concat-residual-mesh-mlp", width=128, depth=2,
+                        mesh_depth=3).groups() == [12416, 32768] + [256] * 6
+    assert SimpleConfig(architecture="tied-concat-mesh-mlp", width=64, depth=5,
+                        connectivity="own").groups() == [97 * 64, 128 * 64, 64, 64, 64, 64]
     # the library's own counts for the two dense-only architectures
     assert SimpleConfig(architecture="mlp", modulus=97, width=128, depth=2).parameter_count() == 53632
     assert SimpleConfig(architecture="bilinear", modulus=97, width=16, depth=0).validate().parameter_count() == 4656

@@ -37,6 +37,18 @@ SMALL = [
     dict(architecture="bilinear", modulus=13, width=24),
     dict(architecture="residual-mlp", modulus=7, width=32, depth=2, expansion=3),
     dict(architecture="residual-mlp", modulus=11, width=40, depth=1, expansion=2, activation="square"),
+    dict(architecture="residual-mesh-mlp", modulus=7, width=32, depth=2, mesh_depth=3),
+    dict(architecture="residual-mesh-mlp", modulus=11, width=64, depth=2, mesh_depth=2, connectivity="butterfly",
+         activation="square", mesh_output_activation=True),
+    dict(architecture="residual-mesh-mlp", modulus=7, width=40, depth=3, mesh_depth=2, connectivity="own"),
+    dict(architecture="tied-concat-residual-mesh-mlp", modulus=13, width=48, depth=2, mesh_depth=2),
+    dict(architecture="tied-rotary-residual-mesh-mlp", modulus=7, width=32, depth=2, mesh_depth=3,
+         activation="square"),
+    dict(architecture="tied-rotary-residual-mesh-mlp", modulus=11, width=64, depth=1, mesh_depth=1,
+         mesh_output_activation=True, mesh_learning_rate_multiplier=2),
+    dict(architecture="tied-concat-mesh-mlp", modulus=7, width=32, depth=3),
+    dict(architecture="tied-concat-mesh-mlp", modulus=11, width=40, depth=4, connectivity="own", activation="square"),
+    dict(architecture="tied-concat-mesh-mlp", modulus=7, width=24, depth=1),
 ]
 FULL = [dict(GROK[name]["config"], modulus=97) for name in ("cfg0", "cfg1", "cfg2")]
 
@@ -213,3 +225,28 @@ def test_archived_mlp_and_bilinear_accuracies(case):
     assert abs(records[0][2] - case["step0"][0]) <= 1.5 / 4656 and abs(records[0][3] - case["step0"][1]) <= 1.5 / 4656
     tol = case.get("step250_tolerance", 2e-3)
     assert abs(records[1][2] - case["step250"][0]) <= tol and abs(records[1][3] - case["step250"][1]) <= tol
+
+
+@pytest.mark.parametrize("case", PINS["grok_simple_mesh_models"]["cases"],
+                         ids=lambda c: "-".join(str(v) for v in c["config"].values()))
+def test_archived_mesh_records(case):
+    """The archived records of the residual mesh family and the tied-concat
+    mesh MLP replayed on the device: step 0 (seeded split, init and forward:
+    the weight norm exactly, CE to 1e-6, accuracies to one row), then the
+    later line after warmed AdamW steps (CE to 1e-3 relative, accuracies to
+    2e-3, the weight norm to 1e-4)."""
+    opt = case["optimizer"]
+    config = SimpleConfig(modulus=97, **case["config"])
+    records = train_records(config, 0, opt["operation"], opt["train_fraction"], opt["seed"], steps=case["steps"],
+                            batch=opt["batch"],
+                            optimizer=AdamWOptions(learning_rate=opt["learning_rate"],
+                                                   weight_decay=opt["weight_decay"], beta1=opt["beta1"],
+                                                   beta2=opt["beta2"], epsilon=opt["epsilon"]))
+    got, want = records[0], case["step0"]
+    assert abs(got[0] - want[0]) <= 1e-6 * want[0] and abs(got[1] - want[1]) <= 1e-6 * want[1], (got, want)
+    assert abs(got[2] - want[2]) <= 1.5 / 4656 and abs(got[3] - want[3]) <= 1.5 / 4656, (got, want)
+    assert got[4] == pytest.approx(want[4], rel=1e-8)
+    got, want = records[1], case["later"]
+    assert abs(got[0] - want[0]) <= 1e-3 * want[0] and abs(got[1] - want[1]) <= 1e-3 * want[1], (got, want)
+    assert abs(got[2] - want[2]) <= 2e-3 and abs(got[3] - want[3]) <= 2e-3, (got, want)
+    assert abs(got[4] - want[4]) <= 1e-4 * want[4], (got, want)
