@@ -230,12 +230,16 @@ int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t seque
 /* ---- grok-simple models (src/simple/mod.rs, src/simple/gpu.rs) ----------
  * Replaces GpuSimpleModel::{new, parameters, set_parameters, upload_table,
  * upload_batches, logits, evaluate, loss_and_gradient, train_batch}
- * (src/simple/gpu.rs:1757-2073) for six architectures of SimpleConfig
+ * (src/simple/gpu.rs:1757-2073) for ten architectures of SimpleConfig
  * (src/simple/mod.rs:500-558); the encoding is one-hot.
  *   architecture 0 = mesh-mlp, 1 = tied-rotary-residual-dense-mlp,
  *                2 = shared-neighbor-mesh-mlp, 3 = mlp, 4 = bilinear,
- *                5 = residual-mlp
+ *                5 = residual-mlp, 6 = residual-mesh-mlp,
+ *                7 = tied-concat-residual-mesh-mlp,
+ *                8 = tied-rotary-residual-mesh-mlp, 9 = tied-concat-mesh-mlp
  *   expansion    residual-mlp's hidden width / width (reference default 4)
+ *   mesh_depth   mesh layers per residual mesh branch (reference default 4)
+ *   mesh_output_activation  1: activate a residual mesh branch's output
  *   activation   0 = relu, 1 = square
  *   connectivity 0 = own, 1 = neighbor, 2 = butterfly
  *   full_mesh_initialization 0 = kaiming, 1 = identity-hidden
