@@ -37,6 +37,9 @@ void validate_kernel_shapes(const mb_simple_config& c);  // this build's kernels
 int parents(const mb_simple_config& c);
 int stride(const mb_simple_config& c, int layer);
 int mesh_layers(const mb_simple_config& c);
+// Mesh layers with their own weights: at most one when they are tied
+// (src/simple/mod.rs:880-893).
+int stored_mesh_layers(const mb_simple_config& c);
 // Dense (inputs, outputs) layers in parameter order.
 std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& c);
 std::vector<size_t> groups(const mb_simple_config& c);

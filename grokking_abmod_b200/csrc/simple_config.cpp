@@ -9,6 +9,7 @@
 // -ffp-contract=off: the f32 uniform draws and the f64 Box-Muller draws
 // round exactly as the reference's.
 
+#include <algorithm>
 #include <cmath>
 #include <string>
 
@@ -33,6 +34,10 @@ int mesh_layers(const mb_simple_config& c) {
   if (residual_mesh(c)) return (int)(c.depth * c.mesh_depth);
   if (c.architecture == kSharedNeighbor) return (int)(c.embedding_mesh_depth + c.depth);
   return 0;
+}
+
+int stored_mesh_layers(const mb_simple_config& c) {
+  return c.tied_mesh ? std::min(mesh_layers(c), 1) : mesh_layers(c);
 }
 
 std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& c) {
@@ -81,7 +86,7 @@ std::vector<size_t> groups(const mb_simple_config& c) {
     return g;
   }
   for (auto& d : dense_layers(c)) g.push_back((size_t)d.first * d.second);
-  for (int i = 0; i < mesh_layers(c); ++i) g.push_back((size_t)parents(c) * c.width);
+  for (int i = 0; i < stored_mesh_layers(c); ++i) g.push_back((size_t)parents(c) * c.width);
   return g;
 }
 
@@ -113,6 +118,9 @@ void validate(const mb_simple_config& c) {
   require(c.mesh_output_activation <= 1, "mesh output activation must be 0 or 1");
   if (c.mesh_output_activation)
     require(residual_mesh(c), "only residual mesh branches activate their final mesh output");
+  require(c.tied_mesh <= 1, "tied mesh must be 0 or 1");
+  if (c.tied_mesh)
+    require(c.architecture == kMeshMlp || c.architecture == kTiedConcatMesh, "only mesh MLPs tie mesh layers");
   if (mesh_layers(c) > 0 && parents(c) == 2) require(c.width >= 2, "a second mesh parent needs a width of at least 2");
   if (tied_concat(c))
     require(2 * (uint64_t)c.width <= kMaxWidth, "tied concatenation needs one-hot encoding and width <= 8192");
@@ -191,7 +199,7 @@ std::vector<float> initial_parameters(const mb_simple_config& c, uint64_t seed) 
     const float bound = 1.0f / std::sqrt((float)layers[index].first);
     for (size_t i = 0; i < count; ++i) p.push_back((2.0f * r.unit() - 1.0f) * bound);
   }
-  for (size_t i = 0; i < (size_t)mesh_layers(c) * w; ++i) {
+  for (size_t i = 0; i < (size_t)stored_mesh_layers(c) * w; ++i) {
     p.push_back(1.0f);
     if (parents(c) == 2) p.push_back(0.0f);
   }

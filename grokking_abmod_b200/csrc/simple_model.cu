@@ -127,10 +127,12 @@ __global__ void gather_batch(int n, const StepScalars* __restrict__ sc, const ui
 // ------------------------------------------------------------- mesh-mlp
 // h0 = W0[a] + W0[m + b] (or h0_in, the tied-concat projection, when given);
 // per mesh layer h' = act(h)[c] w0 + act(h)[c+s] w1; act = act(h_L) feeds the
-// readout GEMM.  h[l] (l = 0..L) is kept for the backward.
+// readout GEMM.  h[l] (l = 0..L) is kept for the backward.  Layer l's weights
+// start at mesh + l * lstride (lstride 0: tied mesh layers).
 template <int ACT, int J>
 __global__ void __launch_bounds__(kFwdWarps * 32)
-    mlp_forward(int n, int W, int m, int L, int p, const int* __restrict__ strides, const uint32_t* __restrict__ a,
+    mlp_forward(int n, int W, int m, int L, int p, int lstride, const int* __restrict__ strides,
+                const uint32_t* __restrict__ a,
                 const uint32_t* __restrict__ b, const float* __restrict__ w0, const float* __restrict__ h0_in,
                 const float* __restrict__ mesh, float* __restrict__ h, float* __restrict__ act) {
   extern __shared__ float sm[];
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
   for (int l = 0; l < L; ++l) {
     __syncwarp();
     const int s = strides[l];
-    const float* w = mesh + (size_t)l * W * p;
+    const float* w = mesh + (size_t)l * lstride;
     float v[J];
 #pragma unroll
     for (int j = 0; j < J; ++j) {
@@ -176,7 +178,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
 // [gridDim.x][L][p*W].
 template <int ACT, int J>
 __global__ void __launch_bounds__(kBwdWarps * 32)
-    mlp_backward(int n, int W, int L, int p, const int* __restrict__ strides, const float* __restrict__ mesh,
+    mlp_backward(int n, int W, int L, int p, int lstride, const int* __restrict__ strides, const float* __restrict__ mesh,
                  const float* __restrict__ h, const float* __restrict__ dact, float* __restrict__ dh0,
                  float* __restrict__ partials) {
   extern __shared__ float sm[];
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
   }
   for (int l = L - 1; l >= 0; --l) {
     const int s = strides[l];
-    const float* w = mesh + (size_t)l * pw;
+    const float* w = mesh + (size_t)l * lstride;
     float* mine = contrib + warp * pw;
     // This warp's weight contributions over its rows, summed in registers in
     // row order and written once per layer.
@@ -262,6 +264,22 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
       const int c = lane + 32 * j;
       if (c < W) dh0[(size_t)r * W + c] = dh[i][j];
     }
+  }
+}
+
+// Tied mesh layers: out[t] = sum over layers l = L-1 .. 0 of the in-order
+// CTA sums of partials[cta][l][t] (the reference adds each lower layer's
+// gradient to the last one's, src/simple/gpu.rs:2771-2792).
+__global__ void reduce_layer_partials(const float* __restrict__ partials, int ctas, int L, int count,
+                                      float* __restrict__ out) {
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < count; t += gridDim.x * blockDim.x) {
+    float total = 0.f;
+    for (int l = L - 1; l >= 0; --l) {
+      float s = 0.f;
+      for (int q = 0; q < ctas; ++q) s += partials[((size_t)q * L + l) * count + t];
+      total += s;
+    }
+    out[t] = total;
   }
 }
 
@@ -1705,6 +1723,22 @@ class SimpleModel {
     SIMPLE_CUDA(cudaGetLastError());
   }
 
+  // Floats between consecutive mesh layers' weights (0: tied mesh layers).
+  int mesh_lstride() const { return c_.tied_mesh ? 0 : parents(c_) * (int)c_.width; }
+
+  // Mesh weight gradients from per-CTA partials [ctas][L][pw]: per layer, or
+  // summed over the layers into the one stored layer when they are tied.
+  void reduce_mesh_partials(Workspace& ws, int L, int pw, float* out) {
+    if (c_.tied_mesh) {
+      reduce_layer_partials<<<(pw + 255) / 256, 256, 0, stream_>>>(ws.part, ws.bwd_ctas, L, pw, out);
+    } else {
+      const size_t cnt = (size_t)L * pw;
+      reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
+          ws.part, ws.bwd_ctas, cnt, out);
+    }
+    ++launches_;
+  }
+
   // h0 = [E a | E b] . Pj (Pj [2W][W]); ws.cat keeps the concatenation.
   void enqueue_concat(Workspace& ws, const float* E, const float* Pj, float* h0) {
     const int n = ws.n, W = (int)c_.width;
@@ -1739,8 +1773,8 @@ class SimpleModel {
       const int L = mesh_layers(c_), p = parents(c_);
       const float* R = w + offsets_[1];
       mlp_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
-          n, W, m, L, p, strides_, ws.a, ws.b, w + offsets_[0], nullptr, w + (L > 0 ? offsets_[2] : 0), ws.h,
-          ws.act); ++launches_;
+          n, W, m, L, p, mesh_lstride(), strides_, ws.a, ws.b, w + offsets_[0], nullptr,
+          w + (L > 0 ? offsets_[2] : 0), ws.h, ws.act); ++launches_;
       // logits = act . R  (R [W][m]: B element (j, c) at R[c * m + j])
       gemm({ws.act, W, false}, {R, m, true}, ws.logits, m, n, m, W, nullptr);
     } else if (c_.architecture == kTiedConcatMesh) {
@@ -1750,7 +1784,8 @@ class SimpleModel {
       const float* E = w + offsets_[0];
       enqueue_concat(ws, E, w + offsets_[1], ws.h);
       mlp_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
-          n, W, m, L, p, strides_, ws.a, ws.b, nullptr, ws.h, w + (L > 0 ? offsets_[2] : 0), ws.h, ws.act); ++launches_;
+          n, W, m, L, p, mesh_lstride(), strides_, ws.a, ws.b, nullptr, ws.h, w + (L > 0 ? offsets_[2] : 0), ws.h,
+          ws.act); ++launches_;
       gemm({ws.act, W, false}, {E, W, false}, ws.logits, m, n, m, W, nullptr);
     } else if (residual_mesh(c_)) {
       // src/simple/reference.rs:337-407
@@ -1874,11 +1909,10 @@ class SimpleModel {
       // dact = dlog . R^T  (B element (c, j) at R[c * m + j])
       gemm({ws.dlog, m, false}, {R, m, false}, ws.dact, W, n, W, m, nullptr);
       if (L > 0) {
-        mlp_backward<ACT, J><<<ws.bwd_ctas, kBwdWarps * 32, bsm, stream_>>>(n, W, L, p, strides_, w + offsets_[2],
-                                                                            ws.h, ws.dact, ws.dh0, ws.part); ++launches_;
-        const size_t cnt = (size_t)L * p * W;
-        reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
-            ws.part, ws.bwd_ctas, cnt, g + offsets_[2]); ++launches_;
+        mlp_backward<ACT, J><<<ws.bwd_ctas, kBwdWarps * 32, bsm, stream_>>>(n, W, L, p, mesh_lstride(), strides_,
+                                                                            w + offsets_[2], ws.h, ws.dact, ws.dh0,
+                                                                            ws.part); ++launches_;
+        reduce_mesh_partials(ws, L, p * W, g + offsets_[2]);
       } else {
         activation_gradient<ACT><<<(int)std::min<size_t>((nw + 255) / 256, 1184), 256, 0, stream_>>>(
             nw, ws.dact, ws.h, ws.dh0); ++launches_;
@@ -1891,11 +1925,10 @@ class SimpleModel {
       gemm({ws.dlog, m, true}, {ws.act, W, true}, ws.dEread, W, m, W, n, ws.gemm_part, kSplitK);
       gemm({ws.dlog, m, false}, {E, W, true}, ws.dact, W, n, W, m, nullptr);
       if (L > 0) {
-        mlp_backward<ACT, J><<<ws.bwd_ctas, kBwdWarps * 32, bsm, stream_>>>(n, W, L, p, strides_, w + offsets_[2],
-                                                                            ws.h, ws.dact, ws.dh0, ws.part); ++launches_;
-        const size_t cnt = (size_t)L * p * W;
-        reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
-            ws.part, ws.bwd_ctas, cnt, g + offsets_[2]); ++launches_;
+        mlp_backward<ACT, J><<<ws.bwd_ctas, kBwdWarps * 32, bsm, stream_>>>(n, W, L, p, mesh_lstride(), strides_,
+                                                                            w + offsets_[2], ws.h, ws.dact, ws.dh0,
+                                                                            ws.part); ++launches_;
+        reduce_mesh_partials(ws, L, p * W, g + offsets_[2]);
       } else {
         activation_gradient<ACT><<<(int)std::min<size_t>((nw + 255) / 256, 1184), 256, 0, stream_>>>(
             nw, ws.dact, ws.h, ws.dh0); ++launches_;

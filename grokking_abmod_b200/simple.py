@@ -46,6 +46,7 @@ class SimpleConfig:
     expansion: int = 4
     mesh_depth: int = 4
     mesh_output_activation: bool = False
+    tied_mesh: bool = False
 
     def with_(self, **kw):
         return replace(self, **kw)
@@ -61,7 +62,7 @@ class SimpleConfig:
                              self.embedding_mesh_depth,
                              index(INITIALIZATIONS, self.full_mesh_initialization, "full-mesh initialization"),
                              self.mesh_learning_rate_multiplier, self.expansion, self.mesh_depth,
-                             int(self.mesh_output_activation))
+                             int(self.mesh_output_activation), int(self.tied_mesh))
 
     def validate(self):
         c = self.to_c()

@@ -240,6 +240,8 @@ int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t seque
  *   expansion    residual-mlp's hidden width / width (reference default 4)
  *   mesh_depth   mesh layers per residual mesh branch (reference default 4)
  *   mesh_output_activation  1: activate a residual mesh branch's output
+ *   tied_mesh    1: mesh-mlp / tied-concat-mesh-mlp store one mesh layer that
+ *                every mesh layer uses (its gradient sums over the layers)
  *   activation   0 = relu, 1 = square
  *   connectivity 0 = own, 1 = neighbor, 2 = butterfly
  *   full_mesh_initialization 0 = kaiming, 1 = identity-hidden
@@ -257,6 +259,7 @@ typedef struct mb_simple_config {
   uint32_t expansion;
   uint32_t mesh_depth;             /* mesh layers per residual mesh branch (6-8) */
   uint32_t mesh_output_activation; /* 1: activate a residual mesh branch's output (6-8) */
+  uint32_t tied_mesh;              /* 1: every mesh layer uses one stored layer (0, 9) */
 } mb_simple_config;
 
 typedef struct mb_simple mb_simple;

@@ -88,6 +88,7 @@ class SimpleConfig:
     expansion: int = 4  # residual-mlp hidden width / width
     mesh_depth: int = 4  # mesh layers per residual mesh branch
     mesh_output_activation: bool = False  # activate the branch output too
+    tied_mesh: bool = False  # every mesh layer uses the first one's weights
 
     def with_(self, **kw):
         return replace(self, **kw)
@@ -116,6 +117,8 @@ class SimpleConfig:
             raise ValueError(f"mesh depth must be in 1..={MAX_DEPTH}")
         if self.mesh_output_activation and a not in RESIDUAL_MESH:
             raise ValueError("only residual mesh branches activate their final mesh output")
+        if self.tied_mesh and a not in ("mesh-mlp", "tied-concat-mesh-mlp"):
+            raise ValueError("only mesh MLPs tie mesh layers")
         if a in TIED_CONCAT and (self.encoding != "one-hot" or 2 * self.width > MAX_WIDTH):
             raise ValueError(f"tied concatenation needs one-hot encoding and width <= {MAX_WIDTH // 2}")
         if self.encoding != "one-hot" and a not in ("mesh-mlp", "mlp", "bilinear", "residual-mlp",
@@ -189,12 +192,19 @@ class SimpleConfig:
             return self.embedding_mesh_depth + self.depth
         return 0
 
+    def stored_mesh_layers(self) -> int:
+        """``:880-893``: one stored layer when the mesh layers are tied."""
+        return min(self.mesh_layers(), 1) if self.tied_mesh else self.mesh_layers()
+
+    def stored_mesh_layer(self, layer: int) -> int:
+        return 0 if self.tied_mesh else layer
+
     def groups(self):
         """Parameter group sizes in storage order (``:871-889``)."""
         if self.architecture == "shared-neighbor-mesh-mlp":
             return [2 * self.width] * self.embedding_mesh_depth + [3 * self.width] * self.depth
         g = [i * o for i, o in self.layers()]
-        return g + [self.parents() * self.width] * self.mesh_layers()
+        return g + [self.parents() * self.width] * self.stored_mesh_layers()
 
     def parameter_count(self) -> int:
         return sum(self.groups())
@@ -250,7 +260,7 @@ def initial_parameters(config: SimpleConfig, seed: int) -> np.ndarray:
         for _ in range(count):
             out.append((np.float32(2.0) * random.unit() - np.float32(1.0)) * bound)
     unit = [1.0, 0.0][:config.parents()]
-    for _ in range(config.mesh_layers() * w):
+    for _ in range(config.stored_mesh_layers() * w):
         out += unit
     return np.array(out, dtype=np.float32)
 
@@ -357,7 +367,7 @@ class ReferenceSimpleModel:
             readout = g[1].reshape(w, m)
             h = [x @ w0]
             for layer in range(c.mesh_layers()):
-                mw = g[2 + layer].reshape(w, c.parents())
+                mw = g[2 + c.stored_mesh_layer(layer)].reshape(w, c.parents())
                 act = _act(c, h[-1])
                 y = act * mw[:, 0]
                 if c.parents() == 2:
@@ -371,7 +381,7 @@ class ReferenceSimpleModel:
             j = np.concatenate([x[:, :m] @ emb, x[:, m:] @ emb], axis=1)
             h = [j @ g[1].reshape(2 * w, w)]
             for layer in range(c.mesh_layers()):
-                mw = g[2 + layer].reshape(w, c.parents())
+                mw = g[2 + c.stored_mesh_layer(layer)].reshape(w, c.parents())
                 act = _act(c, h[-1])
                 y = act * mw[:, 0]
                 if c.parents() == 2:
@@ -562,7 +572,7 @@ class ReferenceSimpleModel:
             grads[1] = (s["act"].T @ dlog).reshape(-1)
             dh = (dlog @ readout.T) * _act_grad(c, s["h"][-1])
             for layer in reversed(range(c.mesh_layers())):
-                mw = g[2 + layer].reshape(w, c.parents())
+                mw = g[2 + c.stored_mesh_layer(layer)].reshape(w, c.parents())
                 hin = s["h"][layer]
                 act = _act(c, hin)
                 gw = np.zeros((w, c.parents()))
@@ -572,7 +582,7 @@ class ReferenceSimpleModel:
                     st = c.stride(layer)
                     gw[:, 1] = (dh * np.roll(act, -st, axis=1)).sum(axis=0)
                     dact = dact + np.roll(dh * mw[:, 1], st, axis=1)
-                grads[2 + layer] = gw.reshape(-1)
+                grads[2 + c.stored_mesh_layer(layer)] = grads[2 + c.stored_mesh_layer(layer)] + gw.reshape(-1)
                 dh = dact * _act_grad(c, hin)
             grads[0] = (s["x"].T @ dh).reshape(-1)
             return loss, np.concatenate(grads)
@@ -581,7 +591,7 @@ class ReferenceSimpleModel:
             demb = dlog.T @ s["act"]
             dh = (dlog @ emb) * _act_grad(c, s["h"][-1])
             for layer in reversed(range(c.mesh_layers())):
-                mw = g[2 + layer].reshape(w, c.parents())
+                mw = g[2 + c.stored_mesh_layer(layer)].reshape(w, c.parents())
                 hin = s["h"][layer]
                 act = _act(c, hin)
                 gw = np.zeros((w, c.parents()))
@@ -591,7 +601,7 @@ class ReferenceSimpleModel:
                     st = c.stride(layer)
                     gw[:, 1] = (dh * np.roll(act, -st, axis=1)).sum(axis=0)
                     dact = dact + np.roll(dh * mw[:, 1], st, axis=1)
-                grads[2 + layer] = gw.reshape(-1)
+                grads[2 + c.stored_mesh_layer(layer)] = grads[2 + c.stored_mesh_layer(layer)] + gw.reshape(-1)
                 dh = dact * _act_grad(c, hin)
             grads[1] = (s["j"].T @ dh).reshape(-1)
             dj = dh @ g[1].reshape(2 * w, w).T

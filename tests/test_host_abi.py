@@ -139,7 +139,9 @@ def _simple_pairs():
                     activation="square", connectivity="butterfly"),
                dict(architecture="tied-rotary-residual-mesh-mlp", width=128, depth=1, mesh_depth=1,
                     mesh_output_activation=True, mesh_learning_rate_multiplier=2),
-               dict(architecture="tied-concat-mesh-mlp", width=64, depth=5, connectivity="own")):
+               dict(architecture="tied-concat-mesh-mlp", width=64, depth=5, connectivity="own"),
+               dict(architecture="mesh-mlp", width=64, depth=3, connectivity="own", tied_mesh=True),
+               dict(architecture="tied-concat-mesh-mlp", modulus=7, width=8, depth=4, tied_mesh=True)):
         yield OracleSimpleConfig(**kw), SimpleConfig(**kw)
 
 
@@ -170,7 +172,8 @@ def test_simple_validation_mirrors_the_reference():
            dict(architecture="mesh-mlp", mesh_output_activation=True),
            dict(architecture="tied-concat-mesh-mlp", mesh_output_activation=True),
            dict(architecture="tied-rotary-residual-mesh-mlp", width=127),
-           dict(architecture="tied-concat-residual-mesh-mlp", width=8193)]
+           dict(architecture="tied-concat-residual-mesh-mlp", width=8193),
+           dict(architecture="residual-mesh-mlp", tied_mesh=True), dict(architecture="mlp", tied_mesh=True)]
     for kw in bad:
         with pytest.raises(MeshError):
             SimpleConfig(**kw).validate()

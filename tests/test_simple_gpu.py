@@ -49,6 +49,9 @@ SMALL = [
     dict(architecture="tied-concat-mesh-mlp", modulus=7, width=32, depth=3),
     dict(architecture="tied-concat-mesh-mlp", modulus=11, width=40, depth=4, connectivity="own", activation="square"),
     dict(architecture="tied-concat-mesh-mlp", modulus=7, width=24, depth=1),
+    dict(architecture="mesh-mlp", modulus=7, width=32, depth=4, connectivity="butterfly", tied_mesh=True),
+    dict(architecture="tied-concat-mesh-mlp", modulus=11, width=32, depth=3, connectivity="own", tied_mesh=True,
+         activation="square"),
 ]
 FULL = [dict(GROK[name]["config"], modulus=97) for name in ("cfg0", "cfg1", "cfg2")]
 

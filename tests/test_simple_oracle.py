@@ -54,6 +54,8 @@ def test_validation_rejects_what_the_reference_rejects():
         SimpleConfig("tied-concat-mesh-mlp", width=16384),
         SimpleConfig("mesh-mlp", mesh_output_activation=True),
         SimpleConfig("tied-concat-mesh-mlp", mesh_output_activation=True),
+        SimpleConfig("residual-mesh-mlp", tied_mesh=True),
+        SimpleConfig("mlp", tied_mesh=True),
         SimpleConfig("residual-mlp", width=8, expansion=0),
         SimpleConfig("tied-rotary-residual-dense-mlp", encoding="scalar"),
         SimpleConfig("mlp", depth=0),
@@ -175,6 +177,8 @@ def test_step10_record_matches_archive(name, tolerance):
                  mesh_output_activation=True),
     SimpleConfig("tied-concat-mesh-mlp", modulus=7, width=8, depth=3),
     SimpleConfig("tied-concat-mesh-mlp", modulus=7, width=8, depth=3, connectivity="own", activation="square"),
+    SimpleConfig("mesh-mlp", modulus=7, width=8, depth=4, connectivity="butterfly", tied_mesh=True),
+    SimpleConfig("tied-concat-mesh-mlp", modulus=7, width=8, depth=3, tied_mesh=True, activation="square"),
 ])
 def test_gradient_matches_finite_differences(config):
     rng = np.random.default_rng(0)
@@ -263,3 +267,21 @@ def test_mesh_models_match_archived_records(case):
     assert abs(got[0] - want[0]) <= 2e-5 * want[0] and abs(got[1] - want[1]) <= 2e-5 * want[1], (got, want)
     assert abs(got[2] - want[2]) <= 4.5 / 4656 and abs(got[3] - want[3]) <= 4.5 / 4656
     assert abs(got[4] - want[4]) <= 2e-5 * want[4]
+
+
+def test_tied_meshes_repeat_their_one_stored_layer():
+    """``src/simple/reference.rs:765-800``: a tied mesh MLP computes the
+    untied model whose every mesh layer holds the one stored layer."""
+    for connectivity in ("own", "butterfly"):
+        tied = SimpleConfig("mesh-mlp", modulus=7, width=5, depth=5, connectivity=connectivity,
+                            tied_mesh=True).validate()
+        untied = tied.with_(tied_mesh=False)
+        assert tied.groups() == untied.groups()[:3]
+        rng = np.random.default_rng(1)
+        shared = rng.normal(size=tied.parameter_count()).astype(np.float32)
+        k = tied.parents() * 5
+        repeated = np.concatenate([shared[:-k]] + [shared[-k:]] * untied.mesh_layers())
+        features, _ = encode(tied, [(1, 2, 0), (3, 0, 1), (6, 6, 2)])
+        a = ReferenceSimpleModel(tied, parameters=shared).logits(features)
+        b = ReferenceSimpleModel(untied, parameters=repeated).logits(features)
+        assert np.array_equal(a, b)
