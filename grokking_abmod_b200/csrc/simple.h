@@ -15,6 +15,7 @@ enum Architecture : uint32_t { kMeshMlp = 0, kRotaryDense = 1, kSharedNeighbor =
                                kResidualMlp = 5, kResidualMesh = 6, kTiedConcatResidualMesh = 7,
                                kTiedRotaryResidualMesh = 8, kTiedConcatMesh = 9 };
 enum Activation : uint32_t { kRelu = 0, kSquare = 1 };
+enum Encoding : uint32_t { kOneHot = 0, kBinary = 1, kScalar = 2, kDiscreteLog = 3 };
 enum Connectivity : uint32_t { kOwn = 0, kNeighbor = 1, kButterfly = 2 };
 
 constexpr uint32_t kMaxWidth = 16384, kMaxDepth = 64, kMaxClasses = 1024;  // src/simple/mod.rs:25-31
@@ -45,9 +46,15 @@ std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& 
 std::vector<size_t> groups(const mb_simple_config& c);
 size_t parameter_count(const mb_simple_config& c);
 std::vector<float> initial_parameters(const mb_simple_config& c, uint64_t seed);
-// One-hot rows -> operand classes; throws MB_ERR_INVALID on other features.
-void decode_one_hot(const mb_simple_config& c, const float* features, const uint32_t* targets, size_t rows,
-                    std::vector<uint32_t>& a, std::vector<uint32_t>& b);
+// Features per operand (Encoding::features, src/simple/mod.rs:362-370).
+uint32_t operand_features(const mb_simple_config& c);
+// One feature row per residue, [modulus][operand_features]
+// (Encoding::table, src/simple/mod.rs:373-414).
+std::vector<float> encoding_table(const mb_simple_config& c);
+// Encoded rows -> operand residues: each operand block must equal one row
+// of the encoding table (MB_ERR_UNSUPPORTED otherwise).
+void decode_operands(const mb_simple_config& c, const float* features, const uint32_t* targets, size_t rows,
+                     std::vector<uint32_t>& a, std::vector<uint32_t>& b);
 
 }  // namespace simple
 }  // namespace mb

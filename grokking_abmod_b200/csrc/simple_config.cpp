@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <string>
 
 #include "simple.h"
@@ -40,10 +41,75 @@ int stored_mesh_layers(const mb_simple_config& c) {
   return c.tied_mesh ? std::min(mesh_layers(c), 1) : mesh_layers(c);
 }
 
+uint32_t operand_features(const mb_simple_config& c) {
+  switch (c.encoding) {
+    case kBinary: {
+      uint32_t bits = 0;
+      while ((c.modulus - 1) >> bits) ++bits;
+      return std::max(bits, 1u);
+    }
+    case kScalar: return 1;
+    case kDiscreteLog: return 2;
+    default: return c.modulus;
+  }
+}
+
+namespace {
+// The smallest primitive root (src/simple/mod.rs:444-456), or 0 without one.
+uint32_t primitive_root(uint32_t m) {
+  std::vector<char> seen(m);
+  for (uint32_t root = 1; root < m; ++root) {
+    std::fill(seen.begin(), seen.end(), 0);
+    uint64_t v = 1;
+    for (uint32_t i = 0; i + 1 < m; ++i) {
+      seen[v] = 1;
+      v = v * root % m;
+    }
+    bool all = true;
+    for (uint32_t k = 1; k < m && all; ++k) all = seen[k] != 0;
+    if (all) return root;
+  }
+  return 0;
+}
+}  // namespace
+
+std::vector<float> encoding_table(const mb_simple_config& c) {
+  const uint32_t m = c.modulus, f = operand_features(c);
+  std::vector<float> t((size_t)m * f, 0.0f);
+  if (c.encoding == kOneHot) {
+    for (uint32_t v = 0; v < m; ++v) t[(size_t)v * f + v] = 1.0f;
+  } else if (c.encoding == kBinary) {
+    for (uint32_t v = 0; v < m; ++v)
+      for (uint32_t bit = 0; bit < f; ++bit) t[(size_t)v * f + bit] = ((v >> bit) & 1u) ? 1.0f : -1.0f;
+  } else if (c.encoding == kScalar) {
+    const double middle = (double)(m - 1) / 2.0;
+    for (uint32_t v = 0; v < m; ++v) t[v] = (float)(((double)v - middle) / middle);
+  } else {
+    const uint32_t root = primitive_root(m);
+    require(root != 0, "discrete logarithms require a prime modulus");
+    std::vector<uint32_t> logs(m, 0);
+    uint64_t v = 1;
+    for (uint32_t e = 0; e + 1 < m; ++e) {
+      logs[v] = e;
+      v = v * root % m;
+    }
+    const double middle = (double)(m - 2) / 2.0;
+    for (uint32_t k = 0; k < m; ++k) {
+      if (k == 0) {
+        t[0] = 1.0f;
+      } else if (middle != 0.0) {
+        t[(size_t)k * 2 + 1] = (float)(((double)logs[k] - middle) / middle);
+      }
+    }
+  }
+  return t;
+}
+
 std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& c) {
   std::vector<std::pair<uint32_t, uint32_t>> l;
+  const uint32_t F = operand_features(c);
   if (c.architecture == kMeshMlp || c.architecture == kResidualMesh) {
-    l.push_back({2 * c.modulus, c.width});
+    l.push_back({2 * F, c.width});
     l.push_back({c.width, c.modulus});
   } else if (tied_concat(c)) {
     // src/simple/mod.rs:727-729: the shared embedding E, the projection of [E a | E b]
@@ -56,14 +122,14 @@ std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& 
     for (uint32_t i = 0; i < c.depth; ++i) l.push_back({c.width, c.width});
   } else if (c.architecture == kMlp) {
     // src/simple/mod.rs:716-721: input layer, depth - 1 hidden layers, readout
-    l.push_back({2 * c.modulus, c.width});
+    l.push_back({2 * F, c.width});
     for (uint32_t i = 1; i < c.depth; ++i) l.push_back({c.width, c.width});
     l.push_back({c.width, c.modulus});
   } else if (c.architecture == kResidualMlp) {
     // src/simple/mod.rs:735-744: input layer, per block (width -> hidden,
     // hidden -> width), readout
     const uint32_t hidden = c.width * c.expansion;
-    l.push_back({2 * c.modulus, c.width});
+    l.push_back({2 * F, c.width});
     for (uint32_t i = 0; i < c.depth; ++i) {
       l.push_back({c.width, hidden});
       l.push_back({hidden, c.width});
@@ -71,8 +137,8 @@ std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& 
     l.push_back({c.width, c.modulus});
   } else if (c.architecture == kBilinear) {
     // src/simple/mod.rs:745-749: the a embedding, the b embedding, readout
-    l.push_back({c.modulus, c.width});
-    l.push_back({c.modulus, c.width});
+    l.push_back({F, c.width});
+    l.push_back({F, c.width});
     l.push_back({c.width, c.modulus});
   }
   return l;
@@ -119,6 +185,12 @@ void validate(const mb_simple_config& c) {
   if (c.mesh_output_activation)
     require(residual_mesh(c), "only residual mesh branches activate their final mesh output");
   require(c.tied_mesh <= 1, "tied mesh must be 0 or 1");
+  require(c.encoding <= kDiscreteLog, "encoding must be 0 (one-hot), 1 (binary), 2 (scalar) or 3 (discrete-log)");
+  if (c.encoding != kOneHot)
+    require(c.architecture == kMlp || c.architecture == kMeshMlp || c.architecture == kBilinear ||
+                c.architecture == kResidualMlp || c.architecture == kResidualMesh,
+            "this architecture needs one-hot operand encoding");
+  if (c.encoding == kDiscreteLog) require(primitive_root(c.modulus) != 0, "discrete logarithms require a prime modulus");
   if (c.tied_mesh)
     require(c.architecture == kMeshMlp || c.architecture == kTiedConcatMesh, "only mesh MLPs tie mesh layers");
   if (mesh_layers(c) > 0 && parents(c) == 2) require(c.width >= 2, "a second mesh parent needs a width of at least 2");
@@ -206,26 +278,33 @@ std::vector<float> initial_parameters(const mb_simple_config& c, uint64_t seed) 
   return p;
 }
 
-void decode_one_hot(const mb_simple_config& c, const float* features, const uint32_t* targets, size_t rows,
-                    std::vector<uint32_t>& a, std::vector<uint32_t>& b) {
-  const uint32_t m = c.modulus;
+void decode_operands(const mb_simple_config& c, const float* features, const uint32_t* targets, size_t rows,
+                     std::vector<uint32_t>& a, std::vector<uint32_t>& b) {
+  const uint32_t m = c.modulus, f = operand_features(c);
+  const std::vector<float> table = encoding_table(c);
   a.resize(rows);
   b.resize(rows);
   for (size_t r = 0; r < rows; ++r) {
     require(targets[r] < m, "answer classes must be below the modulus");
     for (int half = 0; half < 2; ++half) {
-      const float* f = features + r * 2 * m + half * m;
-      uint32_t hot = m;
-      for (uint32_t k = 0; k < m; ++k) {
-        require(std::isfinite(f[k]), "features must contain only finite values", MB_ERR_NONFINITE);
-        if (f[k] == 1.0f && hot == m) {
-          hot = k;
-        } else {
-          require(f[k] == 0.0f, "this build's kernels read one-hot operand rows", MB_ERR_UNSUPPORTED);
+      const float* x = features + r * 2 * f + half * f;
+      for (uint32_t k = 0; k < f; ++k)
+        require(std::isfinite(x[k]), "features must contain only finite values", MB_ERR_NONFINITE);
+      uint32_t hit = m;
+      if (c.encoding == kOneHot) {
+        for (uint32_t k = 0; k < m; ++k) {
+          if (x[k] == 1.0f && hit == m) {
+            hit = k;
+          } else {
+            require(x[k] == 0.0f, "this build's kernels read encoded operand rows", MB_ERR_UNSUPPORTED);
+          }
         }
+      } else {
+        for (uint32_t v = 0; v < m && hit == m; ++v)
+          if (std::memcmp(x, table.data() + (size_t)v * f, f * sizeof(float)) == 0) hit = v;
       }
-      require(hot < m, "this build's kernels read one-hot operand rows", MB_ERR_UNSUPPORTED);
-      (half == 0 ? a : b)[r] = hot;
+      require(hit < m, "this build's kernels read encoded operand rows", MB_ERR_UNSUPPORTED);
+      (half == 0 ? a : b)[r] = hit;
     }
   }
 }

@@ -1033,6 +1033,39 @@ __global__ void concat_rows(int n, int W, const uint32_t* __restrict__ a, const 
   }
 }
 
+// Non-one-hot encodings: the first dense layer's output for every residue,
+// out[k][c] = sum_f table[k mod m][f] Wx[f][c] with Wx the a half (k < m) or
+// the b half (k >= m) of the layer (or the a and b embeddings of bilinear).
+// One-hot gathers then read these 2m rows exactly as they read the layer's
+// own rows for one-hot operands: x W0 = T[a] W0a + T[b] W0b.
+__global__ void encoded_embedding(int m, int F, int W, const float* __restrict__ table, const float* __restrict__ wa,
+                                  const float* __restrict__ wb, float* __restrict__ out) {
+  const int total = 2 * m * W;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int k = i / W, c = i % W;
+    const float* x = table + (size_t)(k < m ? k : k - m) * F;
+    const float* w = k < m ? wa : wb;
+    float s = 0.f;
+    for (int f = 0; f < F; ++f) s = fmaf(x[f], w[(size_t)f * W + c], s);
+    out[i] = s;
+  }
+}
+
+// Its gradient: ga[f][c] = sum over residues k (in order) of table[k][f]
+// dE[k][c], gb[f][c] the same over dE[m + k][c].
+__global__ void encoded_embedding_gradient(int m, int F, int W, const float* __restrict__ table,
+                                           const float* __restrict__ dE, float* __restrict__ ga,
+                                           float* __restrict__ gb) {
+  const int total = 2 * F * W;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int half = i / (F * W), rem = i % (F * W), f = rem / W, c = rem % W;
+    const float* d = dE + (size_t)half * m * W;
+    float s = 0.f;
+    for (int k = 0; k < m; ++k) s = fmaf(table[(size_t)k * F + f], d[(size_t)k * W + c], s);
+    (half == 0 ? ga : gb)[(size_t)f * W + c] = s;
+  }
+}
+
 // ------------------------------------------------------- mlp, bilinear
 // mlp input layer on one-hot rows (src/simple/reference.rs:292-299): x W0
 // with x one-hot at a and at m + b is W0[a] + W0[m + b]; z keeps the
@@ -1332,6 +1365,16 @@ class SimpleModel {
     for (int l = 0; l < nstr; ++l) st[l] = stride(c, l);
     strides_ = mem_.alloc<int>(nstr);
     SIMPLE_CUDA(cudaMemcpy(strides_, st.data(), nstr * sizeof(int), cudaMemcpyHostToDevice));
+    if (c.encoding != kOneHot) {
+      // Encoded operands: the residues' rows through the first layer are
+      // formed per step (encoded_embedding) and gathered like one-hot rows.
+      const std::vector<float> t = encoding_table(c);
+      const size_t mw = (size_t)c.modulus * c.width;
+      enc_table_ = mem_.alloc<float>(t.size());
+      enc_rows_ = mem_.alloc<float>(2 * mw);
+      enc_grad_ = mem_.alloc<float>(2 * mw);
+      SIMPLE_CUDA(cudaMemcpy(enc_table_, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice));
+    }
     set_parameters(initial_parameters(c, seed).data(), P_);
     set_attributes();
   }
@@ -1367,7 +1410,7 @@ class SimpleModel {
   mb_simple_table* upload_table(const float* features, const uint32_t* targets, size_t rows) {
     require(rows >= 1 && rows <= kMaxRows, "tables need 1..=131072 rows");
     std::vector<uint32_t> a, b;
-    decode_one_hot(c_, features, targets, rows, a, b);
+    decode_operands(c_, features, targets, rows, a, b);
     std::vector<uint32_t> ident(rows);
     for (size_t i = 0; i < rows; ++i) ident[i] = (uint32_t)i;
     SIMPLE_CUDA(cudaSetDevice(device_));
@@ -1723,6 +1766,30 @@ class SimpleModel {
     SIMPLE_CUDA(cudaGetLastError());
   }
 
+  // The first layer's rows per operand residue, [2m][W] (a rows, then b
+  // rows): the layer's own weights for one-hot operands, else the encoded
+  // embeddings formed here from the current weights.
+  const float* operand_rows() {
+    if (enc_rows_ == nullptr) return w_ + offsets_[0];
+    const int m = (int)c_.modulus, W = (int)c_.width, F = (int)operand_features(c_);
+    const float* wa = w_ + offsets_[0];
+    const float* wb = c_.architecture == kBilinear ? w_ + offsets_[1] : wa + (size_t)F * W;
+    encoded_embedding<<<(2 * m * W + 255) / 256, 256, 0, stream_>>>(m, F, W, enc_table_, wa, wb, enc_rows_);
+    ++launches_;
+    return enc_rows_;
+  }
+  // Where the per-residue row gradients go: the first layer's gradient for
+  // one-hot operands, else a scratch that operand_rows_gradient maps back.
+  float* operand_rows_grad() { return enc_grad_ != nullptr ? enc_grad_ : grad_ + offsets_[0]; }
+  void operand_rows_gradient() {
+    if (enc_grad_ == nullptr) return;
+    const int m = (int)c_.modulus, W = (int)c_.width, F = (int)operand_features(c_);
+    float* ga = grad_ + offsets_[0];
+    float* gb = c_.architecture == kBilinear ? grad_ + offsets_[1] : ga + (size_t)F * W;
+    encoded_embedding_gradient<<<(2 * F * W + 255) / 256, 256, 0, stream_>>>(m, F, W, enc_table_, enc_grad_, ga, gb);
+    ++launches_;
+  }
+
   // Floats between consecutive mesh layers' weights (0: tied mesh layers).
   int mesh_lstride() const { return c_.tied_mesh ? 0 : parents(c_) * (int)c_.width; }
 
@@ -1773,7 +1840,7 @@ class SimpleModel {
       const int L = mesh_layers(c_), p = parents(c_);
       const float* R = w + offsets_[1];
       mlp_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
-          n, W, m, L, p, mesh_lstride(), strides_, ws.a, ws.b, w + offsets_[0], nullptr,
+          n, W, m, L, p, mesh_lstride(), strides_, ws.a, ws.b, operand_rows(), nullptr,
           w + (L > 0 ? offsets_[2] : 0), ws.h, ws.act); ++launches_;
       // logits = act . R  (R [W][m]: B element (j, c) at R[c * m + j])
       gemm({ws.act, W, false}, {R, m, true}, ws.logits, m, n, m, W, nullptr);
@@ -1791,7 +1858,8 @@ class SimpleModel {
       // src/simple/reference.rs:337-407
       const float* E = w + offsets_[0];
       if (c_.architecture == kResidualMesh) {
-        concat_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, m, ws.a, ws.b, E, ws.h, nullptr, nullptr); ++launches_;
+        concat_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, m, ws.a, ws.b, operand_rows(), ws.h, nullptr,
+                                                              nullptr); ++launches_;
       } else if (c_.architecture == kTiedRotaryResidualMesh) {
         rotary_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.a, ws.b, E, ws.h, nullptr, nullptr); ++launches_;
       } else {
@@ -1814,7 +1882,7 @@ class SimpleModel {
     } else if (c_.architecture == kMlp) {
       const int d = (int)c_.depth;
       const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
-      mlp_input<ACT><<<eg, 256, 0, stream_>>>(n, W, m, ws.a, ws.b, w + offsets_[0], ws.zs, ws.hs); ++launches_;
+      mlp_input<ACT><<<eg, 256, 0, stream_>>>(n, W, m, ws.a, ws.b, operand_rows(), ws.zs, ws.hs); ++launches_;
       for (int l = 1; l < d; ++l) {
         // z_l = act_{l-1} . W_l  (W_l [in][out]: B element (out, in) at W_l[in * W + out])
         gemm({ws.hs + (l - 1) * nw, W, false}, {w + offsets_[l], W, true}, ws.zs + l * nw, W, n, W, W, nullptr);
@@ -1827,7 +1895,7 @@ class SimpleModel {
       const int d = (int)c_.depth, H = W * (int)c_.expansion;
       const size_t nh = (size_t)n * H;
       const int hg = (int)std::min<size_t>((nh + 255) / 256, 1184);
-      concat_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, m, ws.a, ws.b, w + offsets_[0], ws.hs, ws.ns,
+      concat_embed<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, m, ws.a, ws.b, operand_rows(), ws.hs, ws.ns,
                                                             ws.invs); ++launches_;
       for (int l = 0; l < d; ++l) {
         const float* U = w + offsets_[1 + 2 * l];  // [W][H]
@@ -1842,7 +1910,9 @@ class SimpleModel {
       gemm({ws.ns + d * nw, W, false}, {w + offsets_[1 + 2 * d], m, true}, ws.logits, m, n, m, W, nullptr);
     } else if (c_.architecture == kBilinear) {
       const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
-      bilinear_input<<<eg, 256, 0, stream_>>>(n, W, ws.a, ws.b, w + offsets_[0], w + offsets_[1], ws.hs); ++launches_;
+      const float* rows = operand_rows();
+      const float* eb = enc_rows_ != nullptr ? rows + (size_t)m * W : w + offsets_[1];
+      bilinear_input<<<eg, 256, 0, stream_>>>(n, W, ws.a, ws.b, rows, eb, ws.hs); ++launches_;
       gemm({ws.hs, W, false}, {w + offsets_[2], m, true}, ws.logits, m, n, m, W, nullptr);
     } else if (c_.architecture == kRotaryDense) {
       const float* E = w + offsets_[0];
@@ -1917,7 +1987,9 @@ class SimpleModel {
         activation_gradient<ACT><<<(int)std::min<size_t>((nw + 255) / 256, 1184), 256, 0, stream_>>>(
             nw, ws.dact, ws.h, ws.dh0); ++launches_;
       }
-      class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr, g + offsets_[0]); ++launches_;
+      class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr,
+                                                           operand_rows_grad()); ++launches_;
+      operand_rows_gradient();
     } else if (c_.architecture == kTiedConcatMesh) {
       const int L = mesh_layers(c_), p = parents(c_);
       const float* E = w + offsets_[0];
@@ -1964,7 +2036,8 @@ class SimpleModel {
           ws.part, ws.bwd_ctas, cnt, g + mesh_off); ++launches_;
       if (c_.architecture == kResidualMesh) {
         class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr,
-                                                             g + offsets_[0]); ++launches_;
+                                                             operand_rows_grad()); ++launches_;
+        operand_rows_gradient();
       } else if (c_.architecture == kTiedRotaryResidualMesh) {
         class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 1, ws.a, ws.b, ws.dh0, ws.dEread,
                                                          g + offsets_[0]); ++launches_;
@@ -1985,7 +2058,9 @@ class SimpleModel {
         gemm({ws.dz, W, false}, {w + offsets_[l], W, false}, ws.dh, W, n, W, W, nullptr);
       }
       activation_gradient<ACT><<<eg, 256, 0, stream_>>>(nw, ws.dh, ws.zs, ws.dh0); ++launches_;
-      class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr, g + offsets_[0]); ++launches_;
+      class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh0, nullptr,
+                                                           operand_rows_grad()); ++launches_;
+      operand_rows_gradient();
     } else if (c_.architecture == kResidualMlp) {
       const int d = (int)c_.depth, H = W * (int)c_.expansion;
       const size_t nh = (size_t)n * H;
@@ -2012,17 +2087,24 @@ class SimpleModel {
         rms_backward<J><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, W, ws.ns + l * nw, ws.invs + l * n, ws.dn, ws.dh,
                                                              ws.dh); ++launches_;
       }
-      class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh, nullptr, g + offsets_[0]); ++launches_;
+      class_gradient<<<2 * m, kClassThreads, 0, stream_>>>(n, W, m, 0, ws.a, ws.b, ws.dh, nullptr,
+                                                           operand_rows_grad()); ++launches_;
+      operand_rows_gradient();
     } else if (c_.architecture == kBilinear) {
       const int eg = (int)std::min<size_t>((nw + 255) / 256, 1184);
       const float* R = w + offsets_[2];
       // dR = p^T . dlog ; dp = dlog . R^T
       gemm({ws.hs, W, true}, {ws.dlog, m, true}, g + offsets_[2], m, W, m, n, ws.gemm_part, kSplitK);
       gemm({ws.dlog, m, false}, {R, m, false}, ws.dn, W, n, W, m, nullptr);
-      bilinear_gradient<<<eg, 256, 0, stream_>>>(n, W, ws.a, ws.b, w + offsets_[0], w + offsets_[1], ws.dn, ws.dh,
+      const float* ea = enc_rows_ != nullptr ? enc_rows_ : w + offsets_[0];
+      const float* eb = enc_rows_ != nullptr ? enc_rows_ + (size_t)m * W : w + offsets_[1];
+      bilinear_gradient<<<eg, 256, 0, stream_>>>(n, W, ws.a, ws.b, ea, eb, ws.dn, ws.dh,
                                                  ws.dz); ++launches_;
-      class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 2, ws.a, ws.b, ws.dh, nullptr, g + offsets_[0]); ++launches_;
-      class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 3, ws.a, ws.b, ws.dz, nullptr, g + offsets_[1]); ++launches_;
+      float* ga = operand_rows_grad();
+      float* gb = enc_grad_ != nullptr ? enc_grad_ + (size_t)m * W : g + offsets_[1];
+      class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 2, ws.a, ws.b, ws.dh, nullptr, ga); ++launches_;
+      class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 3, ws.a, ws.b, ws.dz, nullptr, gb); ++launches_;
+      operand_rows_gradient();
     } else if (c_.architecture == kRotaryDense) {
       const float* E = w + offsets_[0];
       const int d = (int)c_.depth;
@@ -2084,6 +2166,7 @@ class SimpleModel {
   float *w_, *m1_, *m2_, *grad_;
   int* flags_;
   int* strides_;
+  float *enc_table_ = nullptr, *enc_rows_ = nullptr, *enc_grad_ = nullptr;  // non-one-hot encodings
   StepScalars* scalars_;
   float beta1_power_ = 1.0f, beta2_power_ = 1.0f;
   std::vector<std::unique_ptr<Workspace>> workspaces_;
@@ -2152,14 +2235,14 @@ int mb_simple_encode(const mb_simple_config* config, const uint32_t* equations, 
     need(features, "features");
     need(targets, "targets");
     mb::simple::validate(*config);
-    const uint32_t m = config->modulus;
+    const uint32_t m = config->modulus, f = mb::simple::operand_features(*config);
     for (size_t r = 0; r < n; ++r)
       for (int j = 0; j < 3; ++j)
         require(equations[3 * r + j] < m, "equation residue is outside the model's modulus");
-    std::memset(features, 0, n * 2 * m * sizeof(float));
+    const std::vector<float> table = mb::simple::encoding_table(*config);
     for (size_t r = 0; r < n; ++r) {
-      features[r * 2 * m + equations[3 * r]] = 1.0f;
-      features[r * 2 * m + m + equations[3 * r + 1]] = 1.0f;
+      std::memcpy(features + r * 2 * f, table.data() + (size_t)equations[3 * r] * f, f * sizeof(float));
+      std::memcpy(features + r * 2 * f + f, table.data() + (size_t)equations[3 * r + 1] * f, f * sizeof(float));
       targets[r] = equations[3 * r + 2];
     }
   });

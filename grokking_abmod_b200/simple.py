@@ -26,6 +26,7 @@ ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-
                  "residual-mlp", "residual-mesh-mlp", "tied-concat-residual-mesh-mlp",
                  "tied-rotary-residual-mesh-mlp", "tied-concat-mesh-mlp")
 ACTIVATIONS = ("relu", "square")
+ENCODINGS = ("one-hot", "binary", "scalar", "discrete-log")
 CONNECTIVITIES = ("own", "neighbor", "butterfly")
 INITIALIZATIONS = ("kaiming", "identity-hidden")
 
@@ -47,9 +48,18 @@ class SimpleConfig:
     mesh_depth: int = 4
     mesh_output_activation: bool = False
     tied_mesh: bool = False
+    encoding: str = "one-hot"
 
     def with_(self, **kw):
         return replace(self, **kw)
+
+    def operand_features(self) -> int:
+        """Features per operand of the encoding (``Encoding::features``)."""
+        if self.encoding == "one-hot":
+            return self.modulus
+        if self.encoding == "binary":
+            return max((self.modulus - 1).bit_length(), 1)
+        return 1 if self.encoding == "scalar" else 2
 
     def to_c(self) -> SimpleConfigC:
         def index(names, value, what):
@@ -62,7 +72,8 @@ class SimpleConfig:
                              self.embedding_mesh_depth,
                              index(INITIALIZATIONS, self.full_mesh_initialization, "full-mesh initialization"),
                              self.mesh_learning_rate_multiplier, self.expansion, self.mesh_depth,
-                             int(self.mesh_output_activation), int(self.tied_mesh))
+                             int(self.mesh_output_activation), int(self.tied_mesh),
+                             index(ENCODINGS, self.encoding, "encoding"))
 
     def validate(self):
         c = self.to_c()
@@ -91,7 +102,7 @@ class SimpleConfig:
         """One-hot ``[a | b]`` rows and answer classes of (a, b, answer) triples."""
         eq = np.ascontiguousarray(np.asarray(equations, dtype=np.uint32).reshape(-1, 3))
         c = self.to_c()
-        features = np.empty((len(eq), 2 * self.modulus), dtype=np.float32)
+        features = np.empty((len(eq), 2 * self.operand_features()), dtype=np.float32)
         targets = np.empty(len(eq), dtype=np.uint32)
         check(_lib.load().mb_simple_encode(ctypes.byref(c), ptr(eq, ctypes.c_uint32), len(eq),
                                            ptr(features, ctypes.c_float), ptr(targets, ctypes.c_uint32)))
@@ -158,7 +169,7 @@ class GpuSimpleModel:
     def upload_table(self, features, targets) -> DeviceTable:
         f = np.ascontiguousarray(features, dtype=np.float32)
         t = np.ascontiguousarray(targets, dtype=np.uint32)
-        if f.size != t.size * 2 * self.config.modulus:
+        if f.size != t.size * 2 * self.config.operand_features():
             raise ValueError("each table row needs the model's input features")
         h = ctypes.c_void_p()
         check(self._lib.mb_simple_upload_table(self._h, ptr(f, ctypes.c_float), ptr(t, ctypes.c_uint32), t.size,

@@ -231,7 +231,9 @@ int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t seque
  * Replaces GpuSimpleModel::{new, parameters, set_parameters, upload_table,
  * upload_batches, logits, evaluate, loss_and_gradient, train_batch}
  * (src/simple/gpu.rs:1757-2073) for ten architectures of SimpleConfig
- * (src/simple/mod.rs:500-558); the encoding is one-hot.
+ * (src/simple/mod.rs:500-558).  Operand encodings (src/simple/mod.rs:348-414):
+ * one-hot for every architecture; binary, scalar and discrete-log for mlp,
+ * mesh-mlp, bilinear, residual-mlp and residual-mesh-mlp.
  *   architecture 0 = mesh-mlp, 1 = tied-rotary-residual-dense-mlp,
  *                2 = shared-neighbor-mesh-mlp, 3 = mlp, 4 = bilinear,
  *                5 = residual-mlp, 6 = residual-mesh-mlp,
@@ -260,6 +262,7 @@ typedef struct mb_simple_config {
   uint32_t mesh_depth;             /* mesh layers per residual mesh branch (6-8) */
   uint32_t mesh_output_activation; /* 1: activate a residual mesh branch's output (6-8) */
   uint32_t tied_mesh;              /* 1: every mesh layer uses one stored layer (0, 9) */
+  uint32_t encoding;               /* 0 one-hot, 1 binary, 2 scalar, 3 discrete-log */
 } mb_simple_config;
 
 typedef struct mb_simple mb_simple;
@@ -275,7 +278,8 @@ int mb_simple_groups(const mb_simple_config* config, uint32_t* groups, size_t* n
 /* SimpleConfig::initial_parameters (:938-1036), host out[count]. */
 int mb_simple_initial_parameters(const mb_simple_config* config, uint64_t seed, float* out, size_t count);
 /* SimpleConfig::encode (:1039-1055): host equations [n][3] (a, b, answer)
- * -> host features [n][2*modulus], targets [n]. */
+ * -> host features [n][2*F] (F = features per operand of the encoding),
+ * targets [n]. */
 int mb_simple_encode(const mb_simple_config* config, const uint32_t* equations, size_t n, float* features,
                      uint32_t* targets);
 

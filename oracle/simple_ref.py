@@ -58,6 +58,7 @@ MAX_WIDTH, MAX_DEPTH, MAX_CLASSES = 16384, 64, 1024  # src/simple/mod.rs:25-31
 ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear",
                  "residual-mlp", "residual-mesh-mlp", "tied-concat-residual-mesh-mlp",
                  "tied-rotary-residual-mesh-mlp", "tied-concat-mesh-mlp")
+ENCODINGS = ("one-hot", "binary", "scalar", "discrete-log")
 RESIDUAL_MESH = ("residual-mesh-mlp", "tied-concat-residual-mesh-mlp", "tied-rotary-residual-mesh-mlp")
 TIED_CONCAT = ("tied-concat-residual-mesh-mlp", "tied-concat-mesh-mlp")
 ROTARY = ("tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "tied-rotary-residual-mesh-mlp")
@@ -84,7 +85,7 @@ class SimpleConfig:
     embedding_mesh_depth: int = 4
     full_mesh_initialization: str = "kaiming"  # or "identity-hidden"
     mesh_learning_rate_multiplier: int = 1
-    encoding: str = "one-hot"  # or "scalar"
+    encoding: str = "one-hot"  # binary | scalar | discrete-log
     expansion: int = 4  # residual-mlp hidden width / width
     mesh_depth: int = 4  # mesh layers per residual mesh branch
     mesh_output_activation: bool = False  # activate the branch output too
@@ -109,8 +110,10 @@ class SimpleConfig:
             raise ValueError(f"width must be in 1..={MAX_WIDTH}")
         if a != "bilinear" and not 1 <= self.depth <= MAX_DEPTH:
             raise ValueError(f"depth must be in 1..={MAX_DEPTH}")
-        if self.encoding not in ("one-hot", "scalar"):
+        if self.encoding not in ENCODINGS:
             raise ValueError("unknown encoding")
+        if self.encoding == "discrete-log":
+            primitive_root(self.modulus)
         if a == "residual-mlp" and not 1 <= self.width * self.expansion <= MAX_WIDTH:
             raise ValueError(f"residual hidden width must be in 1..={MAX_WIDTH}")
         if a in RESIDUAL_MESH and not 1 <= self.mesh_depth <= MAX_DEPTH:
@@ -157,7 +160,12 @@ class SimpleConfig:
         return butterfly_stride(self.width, layer)
 
     def operand_features(self) -> int:
-        return self.modulus if self.encoding == "one-hot" else 1
+        """``Encoding::features`` (``src/simple/mod.rs:362-370``)."""
+        if self.encoding == "one-hot":
+            return self.modulus
+        if self.encoding == "binary":
+            return max((self.modulus - 1).bit_length(), 1)
+        return 1 if self.encoding == "scalar" else 2
 
     def input_features(self) -> int:
         return 2 * self.operand_features()
@@ -265,19 +273,59 @@ def initial_parameters(config: SimpleConfig, seed: int) -> np.ndarray:
     return np.array(out, dtype=np.float32)
 
 
+def primitive_root(modulus: int) -> int:
+    """The smallest primitive root (``src/simple/mod.rs:444-456``)."""
+    for root in range(1, modulus):
+        seen, value = [False] * modulus, 1
+        for _ in range(modulus - 1):
+            seen[value] = True
+            value = value * root % modulus
+        if all(seen[1:]):
+            return root
+    raise ValueError("discrete logarithms require a prime modulus")
+
+
+def encoding_table(config: SimpleConfig) -> np.ndarray:
+    """``Encoding::table`` (``src/simple/mod.rs:373-414``): one feature row
+    per residue, float32 [modulus][operand_features]."""
+    m, f = config.modulus, config.operand_features()
+    table = np.zeros((m, f), dtype=np.float32)
+    if config.encoding == "one-hot":
+        table[np.arange(m), np.arange(m)] = 1.0
+    elif config.encoding == "binary":
+        for value in range(m):
+            table[value] = [1.0 if value >> bit & 1 else -1.0 for bit in range(f)]
+    elif config.encoding == "scalar":
+        middle = (m - 1) / 2.0
+        table[:, 0] = [np.float32((value - middle) / middle) for value in range(m)]
+    else:
+        root, logs, value = primitive_root(m), [0] * m, 1
+        for exponent in range(m - 1):
+            logs[value] = exponent
+            value = value * root % m
+        middle = (m - 2) / 2.0
+        for value in range(m):
+            if value == 0:
+                table[value] = [1.0, 0.0]
+            elif middle == 0.0:
+                table[value] = [0.0, 0.0]
+            else:
+                table[value] = [0.0, np.float32((logs[value] - middle) / middle)]
+    return table
+
+
 def encode(config: SimpleConfig, equations):
-    """One-hot ``[a | b]`` feature rows and answer classes (``:1039-1055``)."""
-    if config.encoding != "one-hot":
-        raise ValueError("this restatement encodes one-hot rows only")
+    """``[a | b]`` feature rows of the configured encoding and answer
+    classes (``:1039-1055``)."""
     m = config.modulus
+    table = encoding_table(config)
     rows = len(equations)
-    features = np.zeros((rows, 2 * m), dtype=np.float32)
+    features = np.zeros((rows, 2 * table.shape[1]), dtype=np.float32)
     targets = np.zeros(rows, dtype=np.uint32)
     for r, (a, b, answer) in enumerate(equations):
         if a >= m or b >= m or answer >= m:
             raise ValueError("equation residue is outside the model's modulus")
-        features[r, a] = 1.0
-        features[r, m + b] = 1.0
+        features[r] = np.concatenate([table[a], table[b]])
         targets[r] = answer
     return features, targets
 

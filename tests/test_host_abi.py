@@ -141,7 +141,13 @@ def _simple_pairs():
                     mesh_output_activation=True, mesh_learning_rate_multiplier=2),
                dict(architecture="tied-concat-mesh-mlp", width=64, depth=5, connectivity="own"),
                dict(architecture="mesh-mlp", width=64, depth=3, connectivity="own", tied_mesh=True),
-               dict(architecture="tied-concat-mesh-mlp", modulus=7, width=8, depth=4, tied_mesh=True)):
+               dict(architecture="tied-concat-mesh-mlp", modulus=7, width=8, depth=4, tied_mesh=True),
+               dict(architecture="mlp", width=512, depth=2, encoding="binary"),
+               dict(architecture="residual-mlp", width=128, depth=1, encoding="discrete-log"),
+               dict(architecture="bilinear", modulus=13, width=16, encoding="scalar"),
+               dict(architecture="mesh-mlp", modulus=3, width=8, depth=2, encoding="discrete-log"),
+               dict(architecture="residual-mesh-mlp", modulus=11, width=32, depth=2, mesh_depth=2,
+                    encoding="binary")):
         yield OracleSimpleConfig(**kw), SimpleConfig(**kw)
 
 
@@ -173,7 +179,9 @@ def test_simple_validation_mirrors_the_reference():
            dict(architecture="tied-concat-mesh-mlp", mesh_output_activation=True),
            dict(architecture="tied-rotary-residual-mesh-mlp", width=127),
            dict(architecture="tied-concat-residual-mesh-mlp", width=8193),
-           dict(architecture="residual-mesh-mlp", tied_mesh=True), dict(architecture="mlp", tied_mesh=True)]
+           dict(architecture="residual-mesh-mlp", tied_mesh=True), dict(architecture="mlp", tied_mesh=True),
+           dict(architecture="tied-rotary-residual-mesh-mlp", encoding="binary"),
+           dict(architecture="mlp", modulus=15, encoding="discrete-log")]
     for kw in bad:
         with pytest.raises(MeshError):
             SimpleConfig(**kw).validate()

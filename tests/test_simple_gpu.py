@@ -52,6 +52,11 @@ SMALL = [
     dict(architecture="mesh-mlp", modulus=7, width=32, depth=4, connectivity="butterfly", tied_mesh=True),
     dict(architecture="tied-concat-mesh-mlp", modulus=11, width=32, depth=3, connectivity="own", tied_mesh=True,
          activation="square"),
+    dict(architecture="mlp", modulus=11, width=32, depth=2, encoding="binary"),
+    dict(architecture="mesh-mlp", modulus=7, width=32, depth=3, encoding="scalar", activation="square"),
+    dict(architecture="bilinear", modulus=13, width=24, encoding="discrete-log"),
+    dict(architecture="residual-mlp", modulus=7, width=32, depth=1, expansion=2, encoding="binary"),
+    dict(architecture="residual-mesh-mlp", modulus=11, width=32, depth=2, mesh_depth=2, encoding="discrete-log"),
 ]
 FULL = [dict(GROK[name]["config"], modulus=97) for name in ("cfg0", "cfg1", "cfg2")]
 
@@ -214,10 +219,12 @@ def test_invalid_inputs_fail_before_launch():
 @pytest.mark.parametrize("case", PINS["grok_simple_models"]["cases"],
                          ids=lambda c: "-".join(str(v) for v in c["config"].values()))
 def test_archived_mlp_and_bilinear_accuracies(case):
-    """The archived accuracy histories of the mlp, bilinear and residual-mlp
-    runs, replayed on the device: step 0 (seeded split, init and forward) to
-    one row, step 250 (25 warmed epochs of AdamW) to 2e-3 (5e-3 for
-    residual-mlp, see the oracle test)."""
+    """The archived accuracy histories of the mlp, bilinear, residual-mlp and
+    tied mesh-mlp runs (one-hot, binary and discrete-log operands), replayed
+    on the device: step 0 (seeded split, init and forward) to one row, step
+    250 (25 warmed epochs of AdamW) to 2e-3 (5e-3 for residual-mlp and the
+    two-layer encoded MLPs, whose fast memorisation amplifies FP32 summation
+    order: the binary one ends 10 training rows from the archive)."""
     opt = PINS["grok_simple_models"]["optimizer"]
     config = SimpleConfig(modulus=97, **case["config"])
     records = train_records(config, 0, opt["operation"], opt["train_fraction"], opt["seed"], steps=250,

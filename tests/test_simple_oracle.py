@@ -16,8 +16,8 @@ import numpy as np
 import pytest
 
 from oracle.data import EquationDataset
-from oracle.simple_ref import (ReferenceSimpleModel, SimpleConfig, encode, initial_parameters,
-                               record, train_records)
+from oracle.simple_ref import (ReferenceSimpleModel, SimpleConfig, encode, encoding_table, initial_parameters,
+                               primitive_root, record, train_records)
 
 PINS = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_pins.json")))
 GROK = PINS["grok_simple"]
@@ -56,6 +56,10 @@ def test_validation_rejects_what_the_reference_rejects():
         SimpleConfig("tied-concat-mesh-mlp", mesh_output_activation=True),
         SimpleConfig("residual-mesh-mlp", tied_mesh=True),
         SimpleConfig("mlp", tied_mesh=True),
+        SimpleConfig("tied-rotary-residual-mesh-mlp", encoding="binary"),
+        SimpleConfig("tied-concat-mesh-mlp", encoding="scalar"),
+        SimpleConfig("mlp", modulus=15, encoding="discrete-log"),
+        SimpleConfig("mlp", encoding="ternary"),
         SimpleConfig("residual-mlp", width=8, expansion=0),
         SimpleConfig("tied-rotary-residual-dense-mlp", encoding="scalar"),
         SimpleConfig("mlp", depth=0),
@@ -179,6 +183,11 @@ def test_step10_record_matches_archive(name, tolerance):
     SimpleConfig("tied-concat-mesh-mlp", modulus=7, width=8, depth=3, connectivity="own", activation="square"),
     SimpleConfig("mesh-mlp", modulus=7, width=8, depth=4, connectivity="butterfly", tied_mesh=True),
     SimpleConfig("tied-concat-mesh-mlp", modulus=7, width=8, depth=3, tied_mesh=True, activation="square"),
+    SimpleConfig("mlp", modulus=7, width=8, depth=2, encoding="binary"),
+    SimpleConfig("mesh-mlp", modulus=7, width=8, depth=3, encoding="scalar", activation="square"),
+    SimpleConfig("bilinear", modulus=7, width=8, encoding="discrete-log"),
+    SimpleConfig("residual-mlp", modulus=7, width=6, depth=1, expansion=2, encoding="binary"),
+    SimpleConfig("residual-mesh-mlp", modulus=7, width=8, depth=2, mesh_depth=2, encoding="discrete-log"),
 ])
 def test_gradient_matches_finite_differences(config):
     rng = np.random.default_rng(0)
@@ -285,3 +294,24 @@ def test_tied_meshes_repeat_their_one_stored_layer():
         a = ReferenceSimpleModel(tied, parameters=shared).logits(features)
         b = ReferenceSimpleModel(untied, parameters=repeated).logits(features)
         assert np.array_equal(a, b)
+
+
+def test_encodings_present_identities_bits_values_and_logarithms():
+    """``src/simple/mod.rs:1765-1800`` and ``:2092-2123``."""
+    one_hot = encoding_table(SimpleConfig("mlp", modulus=97))
+    assert one_hot.shape == (97, 97) and np.array_equal(one_hot, np.eye(97, dtype=np.float32))
+    binary = encoding_table(SimpleConfig("mlp", modulus=97, encoding="binary"))
+    assert binary[5].tolist() == [1.0, -1.0, 1.0, -1.0, -1.0, -1.0, -1.0]
+    assert binary[96].tolist() == [-1.0, -1.0, -1.0, -1.0, -1.0, 1.0, 1.0]
+    scalar = encoding_table(SimpleConfig("mlp", modulus=97, encoding="scalar"))
+    assert [scalar[0][0], scalar[48][0], scalar[96][0]] == [-1.0, 0.0, 1.0]
+    assert primitive_root(97) == 5
+    logs = encoding_table(SimpleConfig("mlp", modulus=97, encoding="discrete-log"))
+    assert logs[0].tolist() == [1.0, 0.0] and logs[1].tolist() == [0.0, -1.0]
+    assert logs[5][1] == np.float32(-46.5 / 47.5)
+    assert SimpleConfig("mlp", modulus=2, encoding="binary").operand_features() == 1
+    assert encoding_table(SimpleConfig("mlp", modulus=2, encoding="discrete-log")).tolist() == [[1.0, 0.0], [0.0, 0.0]]
+    with pytest.raises(ValueError):
+        primitive_root(8)
+    features, targets = encode(SimpleConfig("mlp", modulus=5, encoding="scalar"), [(4, 2, 2), (0, 1, 0)])
+    assert features.reshape(-1).tolist() == [1.0, 0.0, -1.0, -0.5] and targets.tolist() == [2, 0]
