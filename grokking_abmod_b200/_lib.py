@@ -35,7 +35,7 @@ class SimpleConfigC(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint32) for n in (
         "architecture", "activation", "modulus", "width", "depth", "connectivity",
         "embedding_mesh_depth", "full_mesh_initialization", "mesh_learning_rate_multiplier", "expansion",
-        "mesh_depth", "mesh_output_activation", "tied_mesh", "encoding")]
+        "mesh_depth", "mesh_output_activation", "tied_mesh", "encoding", "decay_factors")]
 
 
 class AdamWC(ctypes.Structure):

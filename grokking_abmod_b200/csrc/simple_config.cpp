@@ -191,6 +191,9 @@ void validate(const mb_simple_config& c) {
                 c.architecture == kResidualMlp || c.architecture == kResidualMesh,
             "this architecture needs one-hot operand encoding");
   if (c.encoding == kDiscreteLog) require(primitive_root(c.modulus) != 0, "discrete logarithms require a prime modulus");
+  require(c.decay_factors >= 2, "weight decay imitates at least two factors per channel");
+  if (c.decay_factors != 2)
+    require(c.architecture == kMlp && c.depth == 1, "only one-layer MLPs decay as more factors per channel");
   if (c.tied_mesh)
     require(c.architecture == kMeshMlp || c.architecture == kTiedConcatMesh, "only mesh MLPs tie mesh layers");
   if (mesh_layers(c) > 0 && parents(c) == 2) require(c.width >= 2, "a second mesh parent needs a width of at least 2");

@@ -1254,13 +1254,18 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
 
 // simple_adam (src/simple/gpu.rs:787-812) over the flat parameters; groups
 // from index `mesh_start` on train at lr_mesh.
+// With `channel` (one-layer mlp, decay_factors != 2) the decay of the input
+// layer's weight i (< n_in, channel i % W) and of the readout's weight i
+// (channel (i - n_in) / m) is channel[c] instead of the uniform decay
+// (simple_adam_channels, src/simple/gpu.rs:846-881).
 __global__ void adamw(size_t count, size_t mesh_start, const StepScalars* __restrict__ sc,
                       const float* __restrict__ grad, float* __restrict__ w, float* __restrict__ m1,
-                      float* __restrict__ m2) {
-  const float b1 = sc->beta1, b2 = sc->beta2, eps = sc->epsilon, wd = sc->weight_decay;
+                      float* __restrict__ m2, const float* __restrict__ channel, int W, int m, size_t n_in) {
+  const float b1 = sc->beta1, b2 = sc->beta2, eps = sc->epsilon;
   const float c1 = sc->correction1, c2 = sc->correction2;
   const float ob1 = __fsub_rn(1.0f, b1), ob2 = __fsub_rn(1.0f, b2);
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+    const float wd = channel == nullptr ? sc->weight_decay : channel[i < n_in ? i % W : (i - n_in) / m];
     const float lr = i < mesh_start ? sc->lr_dense : sc->lr_mesh;
     const float g = grad[i];
     const float mm = __fadd_rn(__fmul_rn(b1, m1[i]), __fmul_rn(ob1, g));
@@ -1271,6 +1276,27 @@ __global__ void adamw(size_t count, size_t mesh_start, const StepScalars* __rest
     const float upd = __fadd_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), __fmul_rn(wd, w[i]));
     w[i] = __fsub_rn(w[i], __fmul_rn(lr, upd));
   }
+}
+
+// Channel decay of a one-layer mlp (simple_channel_decay, src/simple/gpu.rs:
+// 814-844): out[c] = min(wd max(s_c, FLT_MIN)^exponent, 1 / lr) with
+// s_c = (sum_i E[i][c]^2 + sum_k R[c][k]^2) / 2 over the weights before
+// the step (E input-major [inputs][W], R [W][m]).
+__global__ void channel_decay(int inputs, int W, int m, float exponent, const StepScalars* __restrict__ sc,
+                              const float* __restrict__ E, const float* __restrict__ R, float* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= W) return;
+  float squares = 0.f;
+  for (int i = 0; i < inputs; ++i) {
+    const float x = E[(size_t)i * W + c];
+    squares = __fadd_rn(squares, __fmul_rn(x, x));
+  }
+  for (int k = 0; k < m; ++k) {
+    const float x = R[(size_t)c * m + k];
+    squares = __fadd_rn(squares, __fmul_rn(x, x));
+  }
+  const float scale = powf(fmaxf(0.5f * squares, 1.17549435e-38f), exponent);
+  out[c] = fminf(sc->weight_decay * scale, 1.0f / sc->lr_dense);
 }
 
 // ================================================================ executor
@@ -1375,6 +1401,7 @@ class SimpleModel {
       enc_grad_ = mem_.alloc<float>(2 * mw);
       SIMPLE_CUDA(cudaMemcpy(enc_table_, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice));
     }
+    if (c.decay_factors != 2) chan_decay_ = mem_.alloc<float>(c.width);
     set_parameters(initial_parameters(c, seed).data(), P_);
     set_attributes();
   }
@@ -2152,8 +2179,16 @@ class SimpleModel {
   }
 
   void enqueue_update() {
+    const int W = (int)c_.width, m = (int)c_.modulus;
+    const size_t n_in = groups_[0];
+    if (chan_decay_ != nullptr) {
+      const float exponent = (float)(2.0 / (double)c_.decay_factors - 1.0);
+      channel_decay<<<(W + 127) / 128, 128, 0, stream_>>>((int)(n_in / W), W, m, exponent, scalars_, w_,
+                                                          w_ + offsets_[1], chan_decay_); ++launches_;
+    }
     adamw<<<(int)std::min<size_t>((P_ + 255) / 256, 1184), 256, 0, stream_>>>(P_, mesh_start_, scalars_, grad_, w_,
-                                                                               m1_, m2_); ++launches_;
+                                                                               m1_, m2_, chan_decay_, W, m, n_in);
+    ++launches_;
     SIMPLE_CUDA(cudaGetLastError());
   }
 
@@ -2167,6 +2202,7 @@ class SimpleModel {
   int* flags_;
   int* strides_;
   float *enc_table_ = nullptr, *enc_rows_ = nullptr, *enc_grad_ = nullptr;  // non-one-hot encodings
+  float* chan_decay_ = nullptr;  // per-channel decay (decay_factors != 2)
   StepScalars* scalars_;
   float beta1_power_ = 1.0f, beta2_power_ = 1.0f;
   std::vector<std::unique_ptr<Workspace>> workspaces_;

@@ -49,6 +49,7 @@ class SimpleConfig:
     mesh_output_activation: bool = False
     tied_mesh: bool = False
     encoding: str = "one-hot"
+    decay_factors: int = 2
 
     def with_(self, **kw):
         return replace(self, **kw)
@@ -73,7 +74,7 @@ class SimpleConfig:
                              index(INITIALIZATIONS, self.full_mesh_initialization, "full-mesh initialization"),
                              self.mesh_learning_rate_multiplier, self.expansion, self.mesh_depth,
                              int(self.mesh_output_activation), int(self.tied_mesh),
-                             index(ENCODINGS, self.encoding, "encoding"))
+                             index(ENCODINGS, self.encoding, "encoding"), self.decay_factors)
 
     def validate(self):
         c = self.to_c()

@@ -244,6 +244,9 @@ int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t seque
  *   mesh_output_activation  1: activate a residual mesh branch's output
  *   tied_mesh    1: mesh-mlp / tied-concat-mesh-mlp store one mesh layer that
  *                every mesh layer uses (its gradient sums over the layers)
+ *   decay_factors  n != 2 (one-layer mlp only): AdamW decays hidden channel
+ *                c's input column and readout row at min(wd s_c^(2/n-1), 1/lr),
+ *                s_c = (|E_c|^2 + |R_c|^2) / 2 (src/simple/gpu.rs:814-881)
  *   activation   0 = relu, 1 = square
  *   connectivity 0 = own, 1 = neighbor, 2 = butterfly
  *   full_mesh_initialization 0 = kaiming, 1 = identity-hidden
@@ -263,6 +266,7 @@ typedef struct mb_simple_config {
   uint32_t mesh_output_activation; /* 1: activate a residual mesh branch's output (6-8) */
   uint32_t tied_mesh;              /* 1: every mesh layer uses one stored layer (0, 9) */
   uint32_t encoding;               /* 0 one-hot, 1 binary, 2 scalar, 3 discrete-log */
+  uint32_t decay_factors;          /* 2, or more for a one-layer mlp's channel decay */
 } mb_simple_config;
 
 typedef struct mb_simple mb_simple;

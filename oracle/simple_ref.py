@@ -90,6 +90,7 @@ class SimpleConfig:
     mesh_depth: int = 4  # mesh layers per residual mesh branch
     mesh_output_activation: bool = False  # activate the branch output too
     tied_mesh: bool = False  # every mesh layer uses the first one's weights
+    decay_factors: int = 2  # factors per hidden channel the weight decay imitates
 
     def with_(self, **kw):
         return replace(self, **kw)
@@ -122,6 +123,10 @@ class SimpleConfig:
             raise ValueError("only residual mesh branches activate their final mesh output")
         if self.tied_mesh and a not in ("mesh-mlp", "tied-concat-mesh-mlp"):
             raise ValueError("only mesh MLPs tie mesh layers")
+        if self.decay_factors < 2:
+            raise ValueError("weight decay imitates at least two factors per channel")
+        if self.decay_factors != 2 and (a != "mlp" or self.depth != 1):
+            raise ValueError("only one-layer MLPs decay as more factors per channel")
         if a in TIED_CONCAT and (self.encoding != "one-hot" or 2 * self.width > MAX_WIDTH):
             raise ValueError(f"tied concatenation needs one-hot encoding and width <= {MAX_WIDTH // 2}")
         if self.encoding != "one-hot" and a not in ("mesh-mlp", "mlp", "bilinear", "residual-mlp",
@@ -712,6 +717,28 @@ class ReferenceSimpleModel:
         return loss, np.concatenate(grads)
 
 
+def channel_decays(config: SimpleConfig, parameters, learning_rate, weight_decay):
+    """Per-parameter decay of a one-layer MLP with ``decay_factors`` n != 2
+    (``src/simple/gpu.rs:814-881``, checked on the host at ``:3800-3820``):
+    channel c's input column and readout row decay at
+    min(wd s_c^(2/n - 1), 1 / lr) with s_c = (|E_c|^2 + |R_c|^2) / 2 over the
+    weights before the step, all in f32."""
+    f = np.float32
+    w, m = config.width, config.modulus
+    p = np.asarray(parameters, dtype=np.float32)
+    n_in = config.layers()[0][0] * w
+    inputs, readout = p[:n_in].reshape(-1, w), p[n_in:].reshape(w, m)
+    squares = np.zeros(w, dtype=np.float32)
+    for row in inputs:
+        squares = squares + row * row
+    for k in range(m):
+        squares = squares + readout[:, k] * readout[:, k]
+    exponent = f(2.0 / config.decay_factors - 1.0)
+    scale = np.power(np.maximum(f(0.5) * squares, f(np.finfo(np.float32).tiny)), exponent).astype(np.float32)
+    channel = np.minimum(f(weight_decay) * scale, f(1.0) / f(learning_rate)).astype(np.float32)
+    return np.concatenate([np.tile(channel, inputs.shape[0]), np.repeat(channel, m)]).astype(np.float32)
+
+
 # ------------------------------------------------------------------ records
 def row_metrics(logits, targets):
     """Per-row f64 cross-entropy from (f32) logits and the first maximum
@@ -767,7 +794,10 @@ def train_records(config: SimpleConfig, operation: str = "div", train_fraction: 
         _, grad = model.loss_and_gradient(features[rows], targets[rows])
         b1p, b2p = np.float32(b1p * np.float32(beta1)), np.float32(b2p * np.float32(beta2))
         p = model.parameters
-        if np.all(scales == 1):
+        if config.decay_factors != 2:
+            decays = channel_decays(config, p, lr, weight_decay)
+            adamw_step(p, m, v, grad, step, lr, decays, beta1, beta2, epsilon, (b1p, b2p))
+        elif np.all(scales == 1):
             adamw_step(p, m, v, grad, step, lr, weight_decay, beta1, beta2, epsilon, (b1p, b2p))
         else:
             for scale in np.unique(scales):

@@ -181,7 +181,9 @@ def test_simple_validation_mirrors_the_reference():
            dict(architecture="tied-concat-residual-mesh-mlp", width=8193),
            dict(architecture="residual-mesh-mlp", tied_mesh=True), dict(architecture="mlp", tied_mesh=True),
            dict(architecture="tied-rotary-residual-mesh-mlp", encoding="binary"),
-           dict(architecture="mlp", modulus=15, encoding="discrete-log")]
+           dict(architecture="mlp", modulus=15, encoding="discrete-log"),
+           dict(architecture="mlp", decay_factors=1), dict(architecture="mlp", depth=2, decay_factors=3),
+           dict(architecture="bilinear", decay_factors=4)]
     for kw in bad:
         with pytest.raises(MeshError):
             SimpleConfig(**kw).validate()

@@ -57,6 +57,7 @@ SMALL = [
     dict(architecture="bilinear", modulus=13, width=24, encoding="discrete-log"),
     dict(architecture="residual-mlp", modulus=7, width=32, depth=1, expansion=2, encoding="binary"),
     dict(architecture="residual-mesh-mlp", modulus=11, width=32, depth=2, mesh_depth=2, encoding="discrete-log"),
+    dict(architecture="mlp", modulus=11, width=32, depth=1, decay_factors=3),
 ]
 FULL = [dict(GROK[name]["config"], modulus=97) for name in ("cfg0", "cfg1", "cfg2")]
 
@@ -133,10 +134,12 @@ def test_one_adamw_step_matches_oracle(kw):
     _, g = osr.ReferenceSimpleModel(oc, parameters=params).loss_and_gradient(features[idx], targets[idx])
     want, m, v = params.copy(), np.zeros_like(params), np.zeros_like(params)
     scales = np.repeat(np.array(oc.group_learning_rate_scale(), np.float32), oc.groups())
+    decay = (osr.channel_decays(oc, params, opt.learning_rate, opt.weight_decay) if oc.decay_factors != 2
+             else np.full(params.size, opt.weight_decay, np.float32))
     for scale in np.unique(scales):
         sel = scales == scale
         ws, ms, vs = want[sel], m[sel], v[sel]
-        adamw_step(ws, ms, vs, g[sel], 1, np.float32(opt.learning_rate * scale), opt.weight_decay, opt.beta1,
+        adamw_step(ws, ms, vs, g[sel], 1, np.float32(opt.learning_rate * scale), decay[sel], opt.beta1,
                    opt.beta2, opt.epsilon, (np.float32(opt.beta1), np.float32(opt.beta2)))
         want[sel] = ws
     # AdamW maps any gradient well above epsilon to a full +-lr step, so

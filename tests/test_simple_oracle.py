@@ -60,6 +60,9 @@ def test_validation_rejects_what_the_reference_rejects():
         SimpleConfig("tied-concat-mesh-mlp", encoding="scalar"),
         SimpleConfig("mlp", modulus=15, encoding="discrete-log"),
         SimpleConfig("mlp", encoding="ternary"),
+        SimpleConfig("mlp", decay_factors=1),
+        SimpleConfig("mlp", depth=2, decay_factors=3),
+        SimpleConfig("mesh-mlp", depth=1, decay_factors=3),
         SimpleConfig("residual-mlp", width=8, expansion=0),
         SimpleConfig("tied-rotary-residual-dense-mlp", encoding="scalar"),
         SimpleConfig("mlp", depth=0),
