@@ -13,7 +13,7 @@ namespace simple {
 
 enum Architecture : uint32_t { kMeshMlp = 0, kRotaryDense = 1, kSharedNeighbor = 2, kMlp = 3, kBilinear = 4,
                                kResidualMlp = 5, kResidualMesh = 6, kTiedConcatResidualMesh = 7,
-                               kTiedRotaryResidualMesh = 8, kTiedConcatMesh = 9 };
+                               kTiedRotaryResidualMesh = 8, kTiedConcatMesh = 9, kFullMesh = 10 };
 enum Activation : uint32_t { kRelu = 0, kSquare = 1 };
 enum Encoding : uint32_t { kOneHot = 0, kBinary = 1, kScalar = 2, kDiscreteLog = 3 };
 enum Connectivity : uint32_t { kOwn = 0, kNeighbor = 1, kButterfly = 2 };
@@ -41,6 +41,13 @@ int mesh_layers(const mb_simple_config& c);
 // Mesh layers with their own weights: at most one when they are tied
 // (src/simple/mod.rs:880-893).
 int stored_mesh_layers(const mb_simple_config& c);
+// A full mesh layer: unit o reads inputs o * inputs / outputs and that plus
+// stride (mod inputs) (TwoParentLayer, src/simple/mod.rs:486-501).
+struct TwoParentLayer {
+  uint32_t inputs, outputs, stride;
+};
+// The full mesh's layers, input layer to readout (src/simple/mod.rs:766-800).
+std::vector<TwoParentLayer> two_parent_layers(const mb_simple_config& c);
 // Dense (inputs, outputs) layers in parameter order.
 std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& c);
 std::vector<size_t> groups(const mb_simple_config& c);

@@ -33,6 +33,7 @@ int mesh_layers(const mb_simple_config& c) {
   // src/simple/mod.rs:754-765
   if (c.architecture == kMeshMlp || c.architecture == kTiedConcatMesh) return (int)c.depth - 1;
   if (residual_mesh(c)) return (int)(c.depth * c.mesh_depth);
+  if (c.architecture == kFullMesh) return (int)c.depth + 1;
   if (c.architecture == kSharedNeighbor) return (int)(c.embedding_mesh_depth + c.depth);
   return 0;
 }
@@ -144,8 +145,22 @@ std::vector<std::pair<uint32_t, uint32_t>> dense_layers(const mb_simple_config& 
   return l;
 }
 
+std::vector<TwoParentLayer> two_parent_layers(const mb_simple_config& c) {
+  std::vector<TwoParentLayer> l;
+  if (c.architecture != kFullMesh) return l;
+  const uint32_t F = operand_features(c);
+  l.push_back({2 * F, c.width, F});
+  for (uint32_t layer = 1; layer < c.depth; ++layer) l.push_back({c.width, c.width, (uint32_t)stride(c, layer - 1)});
+  l.push_back({c.width, c.modulus, (uint32_t)stride(c, c.depth - 1)});
+  return l;
+}
+
 std::vector<size_t> groups(const mb_simple_config& c) {
   std::vector<size_t> g;
+  if (c.architecture == kFullMesh) {
+    for (const auto& l : two_parent_layers(c)) g.push_back(3 * (size_t)l.outputs);
+    return g;
+  }
   if (c.architecture == kSharedNeighbor) {
     for (uint32_t i = 0; i < c.embedding_mesh_depth; ++i) g.push_back(2 * (size_t)c.width);
     for (uint32_t i = 0; i < c.depth; ++i) g.push_back(3 * (size_t)c.width);
@@ -163,10 +178,10 @@ size_t parameter_count(const mb_simple_config& c) {
 }
 
 void validate(const mb_simple_config& c) {
-  require(c.architecture <= kTiedConcatMesh,
+  require(c.architecture <= kFullMesh,
           "architecture must be 0 (mesh-mlp), 1 (tied-rotary-residual-dense-mlp), 2 (shared-neighbor-mesh-mlp), "
           "3 (mlp), 4 (bilinear), 5 (residual-mlp), 6 (residual-mesh-mlp), 7 (tied-concat-residual-mesh-mlp), "
-          "8 (tied-rotary-residual-mesh-mlp) or 9 (tied-concat-mesh-mlp)",
+          "8 (tied-rotary-residual-mesh-mlp), 9 (tied-concat-mesh-mlp) or 10 (full-mesh-mlp)",
           MB_ERR_UNSUPPORTED);
   require(c.activation <= kSquare, "activation must be 0 (relu) or 1 (square)");
   require(c.connectivity <= kButterfly, "connectivity must be 0 (own), 1 (neighbor) or 2 (butterfly)");
@@ -188,7 +203,7 @@ void validate(const mb_simple_config& c) {
   require(c.encoding <= kDiscreteLog, "encoding must be 0 (one-hot), 1 (binary), 2 (scalar) or 3 (discrete-log)");
   if (c.encoding != kOneHot)
     require(c.architecture == kMlp || c.architecture == kMeshMlp || c.architecture == kBilinear ||
-                c.architecture == kResidualMlp || c.architecture == kResidualMesh,
+                c.architecture == kResidualMlp || c.architecture == kResidualMesh || c.architecture == kFullMesh,
             "this architecture needs one-hot operand encoding");
   if (c.encoding == kDiscreteLog) require(primitive_root(c.modulus) != 0, "discrete logarithms require a prime modulus");
   require(c.decay_factors >= 2, "weight decay imitates at least two factors per channel");
@@ -202,7 +217,11 @@ void validate(const mb_simple_config& c) {
   if (c.architecture == kRotaryDense || c.architecture == kSharedNeighbor || c.architecture == kTiedRotaryResidualMesh)
     require(c.width >= 2 && c.width % 2 == 0, "rotary roles need one-hot encoding and a positive even width");
   if (c.full_mesh_initialization != 0)
-    require(c.architecture == kSharedNeighbor, "only a full mesh configures its mesh initialization");
+    require(c.architecture == kSharedNeighbor || c.architecture == kFullMesh,
+            "only a full mesh configures its mesh initialization");
+  if (c.architecture == kFullMesh)
+    require(c.encoding == kBinary && c.connectivity != kOwn,
+            "a full mesh needs ordinary binary inputs and two-parent connectivity");
   if (c.architecture == kSharedNeighbor)
     require(c.width >= c.modulus && c.width % 2 == 0 && c.connectivity != kOwn,
             "shared Neighbor meshes need one-hot inputs, even width >= classes, two core parents and "
@@ -216,6 +235,9 @@ void validate(const mb_simple_config& c) {
 void validate_kernel_shapes(const mb_simple_config& c) {
   validate(c);
   require(c.width <= kMaxKernelWidth, "this build's fused row kernels support widths up to 512", MB_ERR_UNSUPPORTED);
+  if (c.architecture == kFullMesh)
+    require(c.width <= 256 && c.modulus <= 256, "this build's full mesh kernels support widths and moduli up to 256",
+            MB_ERR_UNSUPPORTED);
 }
 
 namespace {
@@ -253,6 +275,27 @@ std::vector<float> initial_parameters(const mb_simple_config& c, uint64_t seed) 
           const Normal n = box_muller(r);
           p.push_back((float)(n.radius * std::cos(n.angle)));
           p.push_back((float)(n.radius * std::sin(n.angle)));
+        }
+        p.push_back(0.0f);
+      }
+    }
+    return p;
+  }
+  if (c.architecture == kFullMesh) {
+    // src/simple/mod.rs:979-1003: Box-Muller pairs (deviation sqrt(1/2) on
+    // the readout), identity hidden layers on request, zero biases.
+    const auto tl = two_parent_layers(c);
+    for (size_t index = 0; index < tl.size(); ++index) {
+      const bool identity = c.full_mesh_initialization == 1 && index > 0 && index < c.depth;
+      const double deviation = index == c.depth ? std::sqrt(0.5) : 1.0;
+      for (uint32_t u = 0; u < tl[index].outputs; ++u) {
+        if (identity) {
+          p.push_back(1.0f);
+          p.push_back(0.0f);
+        } else {
+          const Normal n = box_muller(r);
+          p.push_back((float)(deviation * n.radius * std::cos(n.angle)));
+          p.push_back((float)(deviation * n.radius * std::sin(n.angle)));
         }
         p.push_back(0.0f);
       }

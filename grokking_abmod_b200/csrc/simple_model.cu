@@ -1066,6 +1066,161 @@ __global__ void encoded_embedding_gradient(int m, int F, int W, const float* __r
   }
 }
 
+// ------------------------------------------------------------- full mesh
+// full-mesh-mlp (src/simple/reference.rs:271-290): every layer's unit o
+// computes x[p0] w0 + x[p1] w1 + bias with p0 = o * in / out and p1 = (p0 +
+// stride) mod in; layer 0 reads the binary operand bits, later layers the
+// activated outputs of the layer before.  FmLayer describes one layer: its
+// shape, parameter offset (3 floats per unit) and pre-activation offset
+// (floats per row of the workspace's zs, laid out [layer][row][outputs]).
+struct FmLayer {
+  int inputs, outputs, stride, param, z;
+};
+constexpr int kFmMax = 256;  // widest layer input or output of the full mesh kernels
+
+__device__ __forceinline__ int fm_first(int o, const FmLayer& L) { return (int)((long long)o * L.inputs / L.outputs); }
+
+// One warp per row; two row buffers per warp alternate as layer inputs.
+template <int ACT>
+__global__ void __launch_bounds__(kFwdWarps * 32)
+    fullmesh_forward(int n, int F, int nl, const FmLayer* __restrict__ layers, const float* __restrict__ table,
+                     const uint32_t* __restrict__ a, const uint32_t* __restrict__ b, const float* __restrict__ w,
+                     float* __restrict__ zs, float* __restrict__ logits) {
+  __shared__ float bufs[kFwdWarps][2][kFmMax];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kFwdWarps + warp;
+  if (r >= n) return;
+  for (int i = lane; i < 2 * F; i += 32)
+    bufs[warp][0][i] = i < F ? table[(size_t)a[r] * F + i] : table[(size_t)b[r] * F + i - F];
+  __syncwarp();
+  for (int l = 0; l < nl; ++l) {
+    const FmLayer L = layers[l];
+    const float* x = bufs[warp][l & 1];
+    float* y = bufs[warp][(l + 1) & 1];
+    const bool last = l + 1 == nl;
+    float* z = last ? logits + (size_t)r * L.outputs : zs + (size_t)n * L.z + (size_t)r * L.outputs;
+    for (int o = lane; o < L.outputs; o += 32) {
+      const int p0 = fm_first(o, L);
+      int p1 = p0 + L.stride;
+      if (p1 >= L.inputs) p1 -= L.inputs;
+      const float* u = w + L.param + 3 * o;
+      const float v = fmaf(x[p1], u[1], x[p0] * u[0]) + u[2];
+      z[o] = v;
+      if (!last) y[o] = act_f<ACT>(v);
+    }
+    __syncwarp();
+  }
+}
+
+// Backward: dlogits in; per-CTA weight partials [gridDim.x][P] in parameter
+// order.  Each warp walks kBwdRows rows per layer: the layer's input is
+// rebuilt (bits or act(z)), its output gradient dz sits in shared memory,
+// unit o's contributions (dz x[p0], dz x[p1], dz) are summed per warp in
+// registers in row order, and the input gradient of input i gathers the
+// units whose first or second parent is i — contiguous output ranges, since
+// p0(o) = o * in / out is monotone — in output order (no atomics).
+template <int ACT, int J>
+__global__ void __launch_bounds__(kBwdWarps * 32)
+    fullmesh_backward(int n, int F, int nl, const FmLayer* __restrict__ layers, const float* __restrict__ table,
+                      const uint32_t* __restrict__ a, const uint32_t* __restrict__ b, const float* __restrict__ w,
+                      const float* __restrict__ zs, const float* __restrict__ dlog, int P,
+                      float* __restrict__ partials) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* xrow = sm + warp * (kBwdRows + 1) * kFmMax;  // the layer input of the current row
+  float* drow = xrow + kFmMax;                        // kBwdRows output gradients
+  float* contrib = sm + kBwdWarps * (kBwdRows + 1) * kFmMax;
+  const int row0 = (blockIdx.x * kBwdWarps + warp) * kBwdRows;
+  const FmLayer top = layers[nl - 1];
+  for (int i = 0; i < kBwdRows; ++i) {
+    const int r = row0 + i;
+    for (int o = lane; o < top.outputs; o += 32) drow[i * kFmMax + o] = r < n ? dlog[(size_t)r * top.outputs + o] : 0.f;
+  }
+  __syncwarp();
+  for (int l = nl - 1; l >= 0; --l) {
+    const FmLayer L = layers[l];
+    float g0[J], g1[J], g2[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) g0[j] = g1[j] = g2[j] = 0.f;
+    for (int i = 0; i < kBwdRows; ++i) {
+      const int r = row0 + i;
+      const bool active = r < n;
+      float* d = drow + i * kFmMax;
+      __syncwarp();
+      for (int k = lane; k < L.inputs; k += 32) {
+        float x = 0.f;
+        if (active) {
+          if (l == 0)
+            x = k < F ? table[(size_t)a[r] * F + k] : table[(size_t)b[r] * F + k - F];
+          else
+            x = act_f<ACT>(zs[(size_t)n * layers[l - 1].z + (size_t)r * L.inputs + k]);
+        }
+        xrow[k] = x;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int o = lane + 32 * j;
+        if (o < L.outputs) {
+          const int p0 = fm_first(o, L);
+          int p1 = p0 + L.stride;
+          if (p1 >= L.inputs) p1 -= L.inputs;
+          const float dz = d[o];
+          g0[j] += dz * xrow[p0];
+          g1[j] += dz * xrow[p1];
+          g2[j] += dz;
+        }
+      }
+      if (l > 0) {
+        // dx[k] over the units whose first parent is k, then those whose
+        // second parent is k (first parent (k - stride) mod in).
+        float dx[kFmMax / 32];
+#pragma unroll
+        for (int q = 0; q < kFmMax / 32; ++q) {
+          const int k = lane + 32 * q;
+          dx[q] = 0.f;
+          if (k < L.inputs) {
+            float s = 0.f;
+            for (int pass = 0; pass < 2; ++pass) {
+              int first = k - (pass ? L.stride : 0);
+              if (first < 0) first += L.inputs;
+              // units o with o * in / out == first: o in [ceil(first out / in), ceil((first + 1) out / in))
+              const int lo = (int)(((long long)first * L.outputs + L.inputs - 1) / L.inputs);
+              const int hi = (int)(((long long)(first + 1) * L.outputs + L.inputs - 1) / L.inputs);
+              for (int o = lo; o < hi && o < L.outputs; ++o) s = fmaf(d[o], w[L.param + 3 * o + pass], s);
+            }
+            const float zp = active ? zs[(size_t)n * layers[l - 1].z + (size_t)r * L.inputs + k] : 0.f;
+            dx[q] = s * act_g<ACT>(zp);
+          }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < kFmMax / 32; ++q) {
+          const int k = lane + 32 * q;
+          if (k < L.inputs) d[k] = dx[q];
+        }
+      }
+    }
+    float* mine = contrib + warp * 3 * kFmMax;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int o = lane + 32 * j;
+      if (o < L.outputs) {
+        mine[3 * o] = g0[j];
+        mine[3 * o + 1] = g1[j];
+        mine[3 * o + 2] = g2[j];
+      }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < 3 * L.outputs; t += blockDim.x) {
+      float sum = 0.f;
+      for (int q = 0; q < kBwdWarps; ++q) sum += contrib[q * 3 * kFmMax + t];
+      partials[(size_t)blockIdx.x * P + L.param + t] = sum;
+    }
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------- mlp, bilinear
 // mlp input layer on one-hot rows (src/simple/reference.rs:292-299): x W0
 // with x one-hot at a and at m + b is W0[a] + W0[m + b]; z keeps the
@@ -1402,6 +1557,18 @@ class SimpleModel {
       SIMPLE_CUDA(cudaMemcpy(enc_table_, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice));
     }
     if (c.decay_factors != 2) chan_decay_ = mem_.alloc<float>(c.width);
+    if (c.architecture == kFullMesh) {
+      std::vector<FmLayer> fl;
+      int param = 0, z = 0;
+      for (const auto& l : two_parent_layers(c)) {
+        fl.push_back({(int)l.inputs, (int)l.outputs, (int)l.stride, param, z});
+        param += 3 * (int)l.outputs;
+        z += (int)l.outputs;
+      }
+      fm_z_ = z - (int)c.modulus;  // the readout writes the logits
+      fm_layers_ = mem_.alloc<FmLayer>(fl.size());
+      SIMPLE_CUDA(cudaMemcpy(fm_layers_, fl.data(), fl.size() * sizeof(FmLayer), cudaMemcpyHostToDevice));
+    }
     set_parameters(initial_parameters(c, seed).data(), P_);
     set_attributes();
   }
@@ -1622,6 +1789,7 @@ class SimpleModel {
     return f <= kCoreSmemFloats && f + rows <= kSmemFloats ? f : 0;
   }
   int resmesh_fwd_smem() const { return (resmesh_staged() + kFwdWarps * (int)c_.width) * 4; }
+  static int fullmesh_bwd_smem() { return (kBwdWarps * (kBwdRows + 1) * kFmMax + kBwdWarps * 3 * kFmMax) * 4; }
   int resmesh_bwd_smem() const {
     return (resmesh_staged() + kBwdWarps * (2 + parents(c_)) * (int)c_.width) * 4;
   }
@@ -1629,12 +1797,15 @@ class SimpleModel {
   template <int ACT>
   void set_attributes_impl() {
     const int fs = fwd_smem(), bs = bwd_smem();
-    with_j((int)c_.width, [&](auto jc) {
+    with_j(j_width(), [&](auto jc) {
       constexpr int J = decltype(jc)::value;
       SIMPLE_CUDA(cudaFuncSetAttribute(&mlp_forward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, fs));
       SIMPLE_CUDA(cudaFuncSetAttribute(&mlp_backward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, bs));
       SIMPLE_CUDA(cudaFuncSetAttribute(&shared_forward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, fs));
       SIMPLE_CUDA(cudaFuncSetAttribute(&shared_backward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize, bs));
+      if (c_.architecture == kFullMesh)
+        SIMPLE_CUDA(cudaFuncSetAttribute(&fullmesh_backward<ACT, J>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         fullmesh_bwd_smem()));
       if (residual_mesh(c_)) {
         const int rf = resmesh_fwd_smem(), rb = resmesh_bwd_smem();
         SIMPLE_CUDA(cudaFuncSetAttribute(&resmesh_forward<ACT, J, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, rf));
@@ -1701,7 +1872,10 @@ class SimpleModel {
       part = std::max(gemm_partial_floats((int)(2 * W), (int)W, n, kSplitK),
                       gemm_partial_floats((int)m, (int)W, n, kSplitK));
     }
-    if (c_.architecture == kMeshMlp || c_.architecture == kTiedConcatMesh) {
+    if (c_.architecture == kFullMesh) {
+      w->zs = M.alloc<float>((size_t)fm_z_ * N);
+      w->part = M.alloc<float>((size_t)ctas * P_);
+    } else if (c_.architecture == kMeshMlp || c_.architecture == kTiedConcatMesh) {
       const int L = mesh_layers(c_);
       w->h = M.alloc<float>((L + 1) * nw);
       w->act = M.alloc<float>(nw);
@@ -1852,9 +2026,15 @@ class SimpleModel {
     class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 4, ws.a, ws.b, ws.dcat, extra, grad_ + offsets_[0]); ++launches_;
   }
 
+  // Row values per lane of the templated kernels: the width, or for the full
+  // mesh the widest layer (its readout may be wider than the hidden layers).
+  int j_width() const {
+    return c_.architecture == kFullMesh ? (int)std::max(c_.width, c_.modulus) : (int)c_.width;
+  }
+
   template <int ACT>
   void forward_impl(Workspace& ws) {
-    with_j((int)c_.width, [&](auto jc) { forward_j<ACT, decltype(jc)::value>(ws); });
+    with_j(j_width(), [&](auto jc) { forward_j<ACT, decltype(jc)::value>(ws); });
   }
 
   template <int ACT, int J>
@@ -1863,7 +2043,11 @@ class SimpleModel {
     const size_t nw = (size_t)n * W;
     const int fgrid = (n + kFwdWarps - 1) / kFwdWarps;
     const float* w = w_;
-    if (c_.architecture == kMeshMlp) {
+    if (c_.architecture == kFullMesh) {
+      fullmesh_forward<ACT><<<fgrid, kFwdWarps * 32, 0, stream_>>>(n, (int)operand_features(c_),
+                                                                   mesh_layers(c_), fm_layers_, enc_table_, ws.a,
+                                                                   ws.b, w, ws.zs, ws.logits); ++launches_;
+    } else if (c_.architecture == kMeshMlp) {
       const int L = mesh_layers(c_), p = parents(c_);
       const float* R = w + offsets_[1];
       mlp_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
@@ -1987,7 +2171,7 @@ class SimpleModel {
 
   template <int ACT>
   void backward_impl(Workspace& ws) {
-    with_j((int)c_.width, [&](auto jc) { backward_j<ACT, decltype(jc)::value>(ws); });
+    with_j(j_width(), [&](auto jc) { backward_j<ACT, decltype(jc)::value>(ws); });
   }
 
   template <int ACT, int J>
@@ -1998,7 +2182,13 @@ class SimpleModel {
     const int bsm = bwd_smem();
     float* g = grad_;
     const float* w = w_;
-    if (c_.architecture == kMeshMlp) {
+    if (c_.architecture == kFullMesh) {
+      fullmesh_backward<ACT, J><<<ws.bwd_ctas, kBwdWarps * 32, fullmesh_bwd_smem(), stream_>>>(
+          n, (int)operand_features(c_), mesh_layers(c_), fm_layers_, enc_table_, ws.a, ws.b, w, ws.zs, ws.dlog,
+          (int)P_, ws.part); ++launches_;
+      reduce_cta_partials<<<(int)std::min<size_t>((P_ + 255) / 256, 1184), 256, 0, stream_>>>(ws.part, ws.bwd_ctas, P_,
+                                                                                              g); ++launches_;
+    } else if (c_.architecture == kMeshMlp) {
       const int L = mesh_layers(c_), p = parents(c_);
       const float* R = w + offsets_[1];
       // dR = act^T . dlog  (split-K over rows)
@@ -2203,6 +2393,8 @@ class SimpleModel {
   int* strides_;
   float *enc_table_ = nullptr, *enc_rows_ = nullptr, *enc_grad_ = nullptr;  // non-one-hot encodings
   float* chan_decay_ = nullptr;  // per-channel decay (decay_factors != 2)
+  FmLayer* fm_layers_ = nullptr;  // full mesh layer descriptors
+  int fm_z_ = 0;                  // full mesh pre-activation floats per row (all but the readout)
   StepScalars* scalars_;
   float beta1_power_ = 1.0f, beta2_power_ = 1.0f;
   std::vector<std::unique_ptr<Workspace>> workspaces_;

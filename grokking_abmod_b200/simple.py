@@ -3,11 +3,11 @@
 Python mirror of the reference's ``SimpleConfig`` (src/simple/mod.rs:500-1055)
 and ``GpuSimpleModel`` (src/simple/gpu.rs:1757-2073): same names, argument
 meaning and error behaviour (a nonzero library status raises
-``MeshError``).  Ten architectures run on this path: ``mesh-mlp``,
+``MeshError``).  Eleven architectures run on this path: ``mesh-mlp``,
 ``tied-rotary-residual-dense-mlp``, ``shared-neighbor-mesh-mlp``, ``mlp``,
 ``bilinear``, ``residual-mlp``, ``residual-mesh-mlp``,
 ``tied-concat-residual-mesh-mlp``, ``tied-rotary-residual-mesh-mlp`` and
-``tied-concat-mesh-mlp``, with one-hot operands.  There is no CPU
+``tied-concat-mesh-mlp`` and ``full-mesh-mlp``, with one-hot or encoded operands.  There is no CPU
 fallback.
 """
 
@@ -24,7 +24,7 @@ from .gpt import AdamWOptions
 
 ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear",
                  "residual-mlp", "residual-mesh-mlp", "tied-concat-residual-mesh-mlp",
-                 "tied-rotary-residual-mesh-mlp", "tied-concat-mesh-mlp")
+                 "tied-rotary-residual-mesh-mlp", "tied-concat-mesh-mlp", "full-mesh-mlp")
 ACTIVATIONS = ("relu", "square")
 ENCODINGS = ("one-hot", "binary", "scalar", "discrete-log")
 CONNECTIVITIES = ("own", "neighbor", "butterfly")
@@ -33,7 +33,7 @@ INITIALIZATIONS = ("kaiming", "identity-hidden")
 
 @dataclass(frozen=True)
 class SimpleConfig:
-    """``SimpleConfig`` fields read by the ten architectures (reference
+    """``SimpleConfig`` fields read by the eleven architectures (reference
     defaults)."""
     architecture: str = "mesh-mlp"
     activation: str = "relu"

@@ -230,15 +230,17 @@ int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t seque
 /* ---- grok-simple models (src/simple/mod.rs, src/simple/gpu.rs) ----------
  * Replaces GpuSimpleModel::{new, parameters, set_parameters, upload_table,
  * upload_batches, logits, evaluate, loss_and_gradient, train_batch}
- * (src/simple/gpu.rs:1757-2073) for ten architectures of SimpleConfig
+ * (src/simple/gpu.rs:1757-2073) for the eleven architectures of SimpleConfig
  * (src/simple/mod.rs:500-558).  Operand encodings (src/simple/mod.rs:348-414):
- * one-hot for every architecture; binary, scalar and discrete-log for mlp,
- * mesh-mlp, bilinear, residual-mlp and residual-mesh-mlp.
+ * one-hot for every architecture but the full mesh; binary, scalar and
+ * discrete-log for mlp, mesh-mlp, bilinear, residual-mlp and
+ * residual-mesh-mlp; binary for full-mesh-mlp.
  *   architecture 0 = mesh-mlp, 1 = tied-rotary-residual-dense-mlp,
  *                2 = shared-neighbor-mesh-mlp, 3 = mlp, 4 = bilinear,
  *                5 = residual-mlp, 6 = residual-mesh-mlp,
  *                7 = tied-concat-residual-mesh-mlp,
- *                8 = tied-rotary-residual-mesh-mlp, 9 = tied-concat-mesh-mlp
+ *                8 = tied-rotary-residual-mesh-mlp, 9 = tied-concat-mesh-mlp,
+ *                10 = full-mesh-mlp (binary operands, widths and moduli <= 256)
  *   expansion    residual-mlp's hidden width / width (reference default 4)
  *   mesh_depth   mesh layers per residual mesh branch (reference default 4)
  *   mesh_output_activation  1: activate a residual mesh branch's output

@@ -31,6 +31,9 @@ more:
   (``tied-rotary-residual-mesh-mlp``); the tied ones read out through E.
 * ``tied-concat-mesh-mlp`` (``:54-56``): the tied concatenation embedding,
   ``depth-1`` mesh layers as in ``mesh-mlp``, readout through E.
+* ``full-mesh-mlp`` (``:47-49``): an entirely two-parent network over the
+  binary operand bits, every unit ``x[a] w0 + x[b] w1 + bias`` with the
+  activation on the inputs of every layer after the first.
 
 Sources: ``SimpleConfig`` validation / layout / init / encode
 (``src/simple/mod.rs:500-1055``), the f64 tape model
@@ -57,11 +60,19 @@ EPS = float(np.float32(RMSNORM_EPSILON))
 MAX_WIDTH, MAX_DEPTH, MAX_CLASSES = 16384, 64, 1024  # src/simple/mod.rs:25-31
 ARCHITECTURES = ("mesh-mlp", "tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "mlp", "bilinear",
                  "residual-mlp", "residual-mesh-mlp", "tied-concat-residual-mesh-mlp",
-                 "tied-rotary-residual-mesh-mlp", "tied-concat-mesh-mlp")
+                 "tied-rotary-residual-mesh-mlp", "tied-concat-mesh-mlp", "full-mesh-mlp")
 ENCODINGS = ("one-hot", "binary", "scalar", "discrete-log")
 RESIDUAL_MESH = ("residual-mesh-mlp", "tied-concat-residual-mesh-mlp", "tied-rotary-residual-mesh-mlp")
 TIED_CONCAT = ("tied-concat-residual-mesh-mlp", "tied-concat-mesh-mlp")
 ROTARY = ("tied-rotary-residual-dense-mlp", "shared-neighbor-mesh-mlp", "tied-rotary-residual-mesh-mlp")
+
+
+def two_parents(inputs: int, outputs: int, stride: int):
+    """``TwoParentLayer::parents`` (``src/simple/mod.rs:493-496``) for every
+    output: the first parent o * inputs / outputs and (first + stride) mod
+    inputs."""
+    first = np.arange(outputs) * inputs // outputs
+    return first, (first + stride) % inputs
 
 
 def butterfly_stride(width: int, layer: int) -> int:
@@ -130,7 +141,7 @@ class SimpleConfig:
         if a in TIED_CONCAT and (self.encoding != "one-hot" or 2 * self.width > MAX_WIDTH):
             raise ValueError(f"tied concatenation needs one-hot encoding and width <= {MAX_WIDTH // 2}")
         if self.encoding != "one-hot" and a not in ("mesh-mlp", "mlp", "bilinear", "residual-mlp",
-                                                     "residual-mesh-mlp"):
+                                                     "residual-mesh-mlp", "full-mesh-mlp"):
             raise ValueError("rotary roles need one-hot encoding and a positive even width")
         if a == "shared-neighbor-mesh-mlp" and not 1 <= self.embedding_mesh_depth <= MAX_DEPTH:
             raise ValueError("shared Neighbor embedding depth must be in 1..=64")
@@ -140,7 +151,9 @@ class SimpleConfig:
             raise ValueError("rotary roles need one-hot encoding and a positive even width")
         if self.full_mesh_initialization not in ("kaiming", "identity-hidden"):
             raise ValueError("unknown full-mesh initialization")
-        if self.full_mesh_initialization != "kaiming" and a != "shared-neighbor-mesh-mlp":
+        if a == "full-mesh-mlp" and (self.encoding != "binary" or self.connectivity == "own"):
+            raise ValueError("a full mesh needs ordinary binary inputs and two-parent connectivity")
+        if self.full_mesh_initialization != "kaiming" and a not in ("shared-neighbor-mesh-mlp", "full-mesh-mlp"):
             raise ValueError("only a full mesh configures its mesh initialization")
         if a == "shared-neighbor-mesh-mlp" and (
                 self.width < self.modulus or self.width % 2 or self.connectivity == "own"):
@@ -195,12 +208,23 @@ class SimpleConfig:
             return [(m, w)] + [(w, w)] * self.depth
         return []
 
+    def two_parent_layers(self):
+        """Full mesh layers as (inputs, outputs, stride) (``:766-800``)."""
+        if self.architecture != "full-mesh-mlp":
+            return []
+        w = self.width
+        layers = [(self.input_features(), w, self.operand_features())]
+        layers += [(w, w, self.stride(layer - 1)) for layer in range(1, self.depth)]
+        return layers + [(w, self.modulus, self.stride(self.depth - 1))]
+
     def mesh_layers(self) -> int:
         """``:758-765``."""
         if self.architecture in ("mesh-mlp", "tied-concat-mesh-mlp"):
             return self.depth - 1
         if self.architecture in RESIDUAL_MESH:
             return self.depth * self.mesh_depth
+        if self.architecture == "full-mesh-mlp":
+            return self.depth + 1
         if self.architecture == "shared-neighbor-mesh-mlp":
             return self.embedding_mesh_depth + self.depth
         return 0
@@ -216,6 +240,8 @@ class SimpleConfig:
         """Parameter group sizes in storage order (``:871-889``)."""
         if self.architecture == "shared-neighbor-mesh-mlp":
             return [2 * self.width] * self.embedding_mesh_depth + [3 * self.width] * self.depth
+        if self.architecture == "full-mesh-mlp":
+            return [3 * o for _, o, _ in self.two_parent_layers()]
         g = [i * o for i, o in self.layers()]
         return g + [self.parents() * self.width] * self.stored_mesh_layers()
 
@@ -224,6 +250,8 @@ class SimpleConfig:
 
     def group_learning_rate_scale(self):
         """Per group: the learning-rate multiple (``src/simple/gpu.rs:2051-2064``)."""
+        if self.architecture == "full-mesh-mlp":
+            return [self.mesh_learning_rate_multiplier] * len(self.groups())
         n_dense = len(self.layers())
         return [1 if i < n_dense else self.mesh_learning_rate_multiplier
                 for i in range(len(self.groups()))]
@@ -257,6 +285,19 @@ def initial_parameters(config: SimpleConfig, seed: int) -> np.ndarray:
                 else:
                     radius, angle = _box_muller(random)
                     pair = [radius * math.cos(angle), radius * math.sin(angle)]
+                out += [np.float32(pair[0]), np.float32(pair[1]), np.float32(0.0)]
+        return np.array(out, dtype=np.float32)
+    if config.architecture == "full-mesh-mlp":
+        # src/simple/mod.rs:979-1003
+        for index, (_, outputs, _) in enumerate(config.two_parent_layers()):
+            identity = config.full_mesh_initialization == "identity-hidden" and 0 < index < config.depth
+            deviation = math.sqrt(0.5) if index == config.depth else 1.0
+            for _ in range(outputs):
+                if identity:
+                    pair = [1.0, 0.0]
+                else:
+                    radius, angle = _box_muller(random)
+                    pair = [deviation * radius * math.cos(angle), deviation * radius * math.sin(angle)]
                 out += [np.float32(pair[0]), np.float32(pair[1]), np.float32(0.0)]
         return np.array(out, dtype=np.float32)
     for index, (inputs, outputs) in enumerate(config.layers()):
@@ -444,6 +485,16 @@ class ReferenceSimpleModel:
             return act @ emb.T, dict(x=x, j=j, h=h, act=act, emb=emb)
         if c.architecture in RESIDUAL_MESH:
             return self._residual_mesh_forward(x, g)
+        if c.architecture == "full-mesh-mlp":
+            # src/simple/reference.rs:271-290
+            zs, h = [], x
+            for index, (inputs, outputs, stride) in enumerate(c.two_parent_layers()):
+                xin = h if index == 0 else _act(c, h)
+                p = g[index].reshape(outputs, 3)
+                a, b = two_parents(inputs, outputs, stride)
+                h = xin[:, a] * p[:, 0] + xin[:, b] * p[:, 1] + p[:, 2]
+                zs.append(h)
+            return h, dict(x=x, zs=zs)
         perm, sign = _rotation(w)
         if c.architecture == "tied-rotary-residual-dense-mlp":
             emb = g[0].reshape(m, w)
@@ -663,6 +714,21 @@ class ReferenceSimpleModel:
             return loss, np.concatenate(grads)
         if c.architecture in RESIDUAL_MESH:
             self._residual_mesh_backward(s, g, grads, dlog)
+            return loss, np.concatenate(grads)
+        if c.architecture == "full-mesh-mlp":
+            layers, dz = c.two_parent_layers(), dlog
+            for index in reversed(range(len(layers))):
+                inputs, outputs, stride = layers[index]
+                xin = s["x"] if index == 0 else _act(c, s["zs"][index - 1])
+                p = g[index].reshape(outputs, 3)
+                a, b = two_parents(inputs, outputs, stride)
+                grads[index] = np.stack([(dz * xin[:, a]).sum(axis=0), (dz * xin[:, b]).sum(axis=0),
+                                         dz.sum(axis=0)], axis=1).reshape(-1)
+                if index > 0:
+                    dx = np.zeros_like(xin)
+                    np.add.at(dx.T, a, (dz * p[:, 0]).T)
+                    np.add.at(dx.T, b, (dz * p[:, 1]).T)
+                    dz = dx * _act_grad(c, s["zs"][index - 1])
             return loss, np.concatenate(grads)
         perm, sign = _rotation(w)
         x = s["x"]

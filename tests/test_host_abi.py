@@ -147,7 +147,10 @@ def _simple_pairs():
                dict(architecture="bilinear", modulus=13, width=16, encoding="scalar"),
                dict(architecture="mesh-mlp", modulus=3, width=8, depth=2, encoding="discrete-log"),
                dict(architecture="residual-mesh-mlp", modulus=11, width=32, depth=2, mesh_depth=2,
-                    encoding="binary")):
+                    encoding="binary"),
+               dict(architecture="full-mesh-mlp", width=128, depth=8, connectivity="butterfly", encoding="binary"),
+               dict(architecture="full-mesh-mlp", modulus=7, width=8, depth=3, encoding="binary",
+                    full_mesh_initialization="identity-hidden")):
         yield OracleSimpleConfig(**kw), SimpleConfig(**kw)
 
 
@@ -183,12 +186,13 @@ def test_simple_validation_mirrors_the_reference():
            dict(architecture="tied-rotary-residual-mesh-mlp", encoding="binary"),
            dict(architecture="mlp", modulus=15, encoding="discrete-log"),
            dict(architecture="mlp", decay_factors=1), dict(architecture="mlp", depth=2, decay_factors=3),
-           dict(architecture="bilinear", decay_factors=4)]
+           dict(architecture="bilinear", decay_factors=4),
+           dict(architecture="full-mesh-mlp"), dict(architecture="full-mesh-mlp", encoding="binary", connectivity="own")]
     for kw in bad:
         with pytest.raises(MeshError):
             SimpleConfig(**kw).validate()
     with pytest.raises(ValueError):
-        SimpleConfig(architecture="full-mesh-mlp").to_c()
+        SimpleConfig(architecture="sparse-mesh-mlp").to_c()
     # src/simple/mod.rs:1446-1760 (parameter counts of the mesh architectures)
     assert SimpleConfig(architecture="residual-mesh-mlp", width=64, depth=2, mesh_depth=4).parameter_count() == 19648
     assert SimpleConfig(architecture="tied-rotary-residual-mesh-mlp", width=128, depth=2,

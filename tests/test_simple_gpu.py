@@ -58,6 +58,10 @@ SMALL = [
     dict(architecture="residual-mlp", modulus=7, width=32, depth=1, expansion=2, encoding="binary"),
     dict(architecture="residual-mesh-mlp", modulus=11, width=32, depth=2, mesh_depth=2, encoding="discrete-log"),
     dict(architecture="mlp", modulus=11, width=32, depth=1, decay_factors=3),
+    dict(architecture="full-mesh-mlp", modulus=7, width=32, depth=3, encoding="binary"),
+    dict(architecture="full-mesh-mlp", modulus=13, width=24, depth=2, encoding="binary", connectivity="butterfly",
+         activation="square", full_mesh_initialization="identity-hidden"),
+    dict(architecture="full-mesh-mlp", modulus=97, width=64, depth=4, encoding="binary", connectivity="butterfly"),
 ]
 FULL = [dict(GROK[name]["config"], modulus=97) for name in ("cfg0", "cfg1", "cfg2")]
 

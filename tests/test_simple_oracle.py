@@ -17,7 +17,7 @@ import pytest
 
 from oracle.data import EquationDataset
 from oracle.simple_ref import (ReferenceSimpleModel, SimpleConfig, encode, encoding_table, initial_parameters,
-                               primitive_root, record, train_records)
+                               primitive_root, record, train_records, two_parents)
 
 PINS = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_pins.json")))
 GROK = PINS["grok_simple"]
@@ -63,6 +63,9 @@ def test_validation_rejects_what_the_reference_rejects():
         SimpleConfig("mlp", decay_factors=1),
         SimpleConfig("mlp", depth=2, decay_factors=3),
         SimpleConfig("mesh-mlp", depth=1, decay_factors=3),
+        SimpleConfig("full-mesh-mlp"),  # one-hot
+        SimpleConfig("full-mesh-mlp", encoding="binary", connectivity="own"),
+        SimpleConfig("full-mesh-mlp", encoding="binary", tied_mesh=True),
         SimpleConfig("residual-mlp", width=8, expansion=0),
         SimpleConfig("tied-rotary-residual-dense-mlp", encoding="scalar"),
         SimpleConfig("mlp", depth=0),
@@ -191,6 +194,9 @@ def test_step10_record_matches_archive(name, tolerance):
     SimpleConfig("bilinear", modulus=7, width=8, encoding="discrete-log"),
     SimpleConfig("residual-mlp", modulus=7, width=6, depth=1, expansion=2, encoding="binary"),
     SimpleConfig("residual-mesh-mlp", modulus=7, width=8, depth=2, mesh_depth=2, encoding="discrete-log"),
+    SimpleConfig("full-mesh-mlp", modulus=7, width=8, depth=3, encoding="binary"),
+    SimpleConfig("full-mesh-mlp", modulus=11, width=12, depth=2, connectivity="butterfly", activation="square",
+                 encoding="binary", full_mesh_initialization="identity-hidden"),
 ])
 def test_gradient_matches_finite_differences(config):
     rng = np.random.default_rng(0)
@@ -318,3 +324,39 @@ def test_encodings_present_identities_bits_values_and_logarithms():
         primitive_root(8)
     features, targets = encode(SimpleConfig("mlp", modulus=5, encoding="scalar"), [(4, 2, 2), (0, 1, 0)])
     assert features.reshape(-1).tolist() == [1.0, 0.0, -1.0, -0.5] and targets.tolist() == [2, 0]
+
+
+def test_full_mesh_has_two_distinct_parents_including_input_and_readout():
+    """``src/simple/mod.rs:1337-1397``."""
+    config = SimpleConfig("full-mesh-mlp", encoding="binary", width=128, depth=8, connectivity="butterfly").validate()
+    assert config.layers() == []
+    layers = config.two_parent_layers()
+    assert len(layers) == 9 and layers[0][:2] == (14, 128) and layers[8][:2] == (128, 97)
+    assert config.parameter_count() == 3 * (8 * 128 + 97)
+    for inputs, outputs, stride in layers:
+        a, b = two_parents(inputs, outputs, stride)
+        assert (a < inputs).all() and (b < inputs).all() and (a != b).all()
+
+    def fields(c):
+        f = [1 << bit for bit in range(c.input_features())]
+        for inputs, outputs, stride in c.two_parent_layers():
+            a, b = two_parents(inputs, outputs, stride)
+            f = [f[x] | f[y] for x, y in zip(a, b)]
+        return f
+    every = (1 << 14) - 1
+    assert all(v == every for v in fields(config))
+    assert all(v != every for v in fields(config.with_(connectivity="neighbor")))
+    assert all(v == every for v in fields(config.with_(connectivity="neighbor", depth=64)))
+
+
+def test_full_mesh_initialization_is_seeded_and_identity_applies_only_to_hidden_layers():
+    """``src/simple/mod.rs:1399-1445``."""
+    config = SimpleConfig("full-mesh-mlp", encoding="binary", modulus=7, width=8, depth=3)
+    w = initial_parameters(config, 11)
+    assert w.size == config.parameter_count() and np.array_equal(w, initial_parameters(config, 11))
+    assert not np.array_equal(w, initial_parameters(config, 7))
+    units = w.reshape(-1, 3)
+    assert (units[:, 2] == 0).all() and (units[:, 1] != 0).any()
+    identity = initial_parameters(config.with_(full_mesh_initialization="identity-hidden").validate(), 11)
+    assert (identity[24:72].reshape(-1, 3) == [1.0, 0.0, 0.0]).all()
+    assert (identity[:24].reshape(-1, 3)[:, 1] != 0).any() and (identity[72:].reshape(-1, 3)[:, 1] != 0).any()
