@@ -70,9 +70,9 @@ class DeviceArena {
 // ------------------------------------------------- width-specialised blocks
 struct BlockOps {
   virtual ~BlockOps() = default;
-  int row_lanes = 1, tile_rows = 1, tile_rows_bwd = 1;
+  int row_lanes = 1, tile_rows = 1, tile_rows_post = 1, tile_rows_bwd = 1;
   int occ_qf = 1, occ_pf = 1, occ_pb = 1, occ_qb = 1;
-  size_t smem_f = 0, smem_pb = 0, smem_qb = 0;
+  size_t smem_f = 0, smem_pf = 0, smem_pb = 0, smem_qb = 0;
   virtual void qkv_forward(cudaStream_t s, int grid, const Dims& d, const float* x, const uint32_t* tokens,
                            const float* emb, float* x_out, const float* wq, const float* wk, const float* wv,
                            const float2* rope, float* q, float* k, float* v) = 0;
@@ -86,33 +86,39 @@ struct BlockOps {
                             const float* wv, const float2* rope, float* dx, float* pq, float* pk, float* pv) = 0;
 };
 
+// Rows per thread of the block kernels, from measured sweeps: qkv_forward
+// runs fastest with 4, post_forward with 2, the backward kernels with 2.
 constexpr int kRptForward = 4;
+constexpr int kRptPostForward = 2;
 constexpr int kRptBackward = 2;
 
 template <int W, class S>
 struct BlockOpsW final : BlockOps {
   using TF = RowTile<W, kRptForward>;
+  using TP = RowTile<W, kRptPostForward>;
   using TB = RowTile<W, kRptBackward>;
   explicit BlockOpsW(int A, int F) {
     row_lanes = TB::RL;
     tile_rows = TF::TR;
+    tile_rows_post = TP::TR;
     tile_rows_bwd = TB::TR;
     smem_f = BlockKernels<W, kRptForward>::smem_forward();
+    smem_pf = BlockKernels<W, kRptPostForward>::smem_forward();
     smem_pb = BlockKernels<W, kRptBackward>::smem_post_backward(A, F);
     smem_qb = BlockKernels<W, kRptBackward>::smem_qkv_backward(A);
     MB_CUDA(cudaFuncSetAttribute(qkv_forward_k(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_f));
-    MB_CUDA(cudaFuncSetAttribute(post_forward_k(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_f));
+    MB_CUDA(cudaFuncSetAttribute(post_forward_k(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_pf));
     MB_CUDA(cudaFuncSetAttribute(post_backward_k(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_pb));
     MB_CUDA(cudaFuncSetAttribute(qkv_backward_k(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_qb));
     MB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_qf, qkv_forward_k(), TF::NT, smem_f));
-    MB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_pf, post_forward_k(), TF::NT, smem_f));
+    MB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_pf, post_forward_k(), TP::NT, smem_pf));
     MB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_pb, post_backward_k(), TB::NT, smem_pb));
     MB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_qb, qkv_backward_k(), TB::NT, smem_qb));
     require(occ_qf > 0 && occ_pf > 0 && occ_pb > 0 && occ_qb > 0,
             "fused block kernels do not fit on this device for these mesh depths", MB_ERR_UNSUPPORTED);
   }
   static auto qkv_forward_k() { return &mb::qkv_forward<W, kRptForward, S>; }
-  static auto post_forward_k() { return &mb::post_forward<W, kRptForward, S>; }
+  static auto post_forward_k() { return &mb::post_forward<W, kRptPostForward, S>; }
   static auto post_backward_k() { return &mb::post_backward<W, kRptBackward, S>; }
   static auto qkv_backward_k() { return &mb::qkv_backward<W, kRptBackward, S>; }
   void qkv_forward(cudaStream_t s, int grid, const Dims& d, const float* x, const uint32_t* tokens,
@@ -122,7 +128,7 @@ struct BlockOpsW final : BlockOps {
   }
   void post_forward(cudaStream_t s, int grid, const Dims& d, const float* o, const float* v, const float* x,
                     const float* wo, const float* wf, float* xm, float* xn) override {
-    post_forward_k()<<<grid, TF::NT, smem_f, s>>>(d, o, v, x, wo, wf, xm, xn);
+    post_forward_k()<<<grid, TP::NT, smem_pf, s>>>(d, o, v, x, wo, wf, xm, xn);
   }
   void post_backward(cudaStream_t s, int grid, const Dims& d, const float* dxn, const float* xm, const float* o,
                      const float* v, const float* wo, const float* wf, float* dO, float* dvx, float* dxm,
@@ -666,7 +672,7 @@ class GptModel {
       return std::max(1, std::min(tiles, sms_ * occ));
     };
     ws->grid_qf = grid(blocks_->tile_rows, blocks_->occ_qf);
-    ws->grid_pf = grid(blocks_->tile_rows, blocks_->occ_pf);
+    ws->grid_pf = grid(blocks_->tile_rows_post, blocks_->occ_pf);
     ws->grid_pb = grid(blocks_->tile_rows_bwd, blocks_->occ_pb);
     ws->grid_qb = grid(blocks_->tile_rows_bwd, blocks_->occ_qb);
     const int slots_pb = ws->grid_pb * blocks_->row_lanes;
