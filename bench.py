@@ -281,12 +281,24 @@ class ClockSampler:
         self.proc = None
         self.file = None
 
+    def _lines(self):
+        with open(self.file.name) as f:
+            return [r for r in f.read().splitlines() if r.strip()]
+
     def start(self):
+        """Starts nvidia-smi (a sample every 50 ms) and waits, at most 5 s,
+        for its first row, so that it is sampling when the timed region
+        begins; rows before that are not counted."""
+        self.mark = 0
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.device)], stdout=self.file,
+                                          "-lms", "50", "-i", str(self.device)], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
+            deadline = time.time() + 5.0
+            while time.time() < deadline and not self._lines():
+                time.sleep(0.02)
+            self.mark = len(self._lines())
         except Exception:
             self.proc = None
 
@@ -299,9 +311,12 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.file.flush()
-        self.file.seek(0)
-        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        lines = self._lines()
         os.unlink(self.file.name)
+        # rows sampled during the timed region (the last earlier one if the
+        # region ended before the next sample)
+        kept = lines[self.mark:] or lines[max(self.mark - 1, 0):self.mark]
+        rows = [r.split(",") for r in kept]
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
