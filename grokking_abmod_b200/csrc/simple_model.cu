@@ -1323,15 +1323,29 @@ __global__ void __launch_bounds__(kClassThreads)
       kinds[pos] = kind;
     }
     __syncthreads();
-    for (int e = 0; e < total; ++e) {
-      const int rr = list[e], kd = kinds[e];
-      const float* g = dh0 + (size_t)rr * (mode == 4 ? 2 * W : W);
+    // Rows in list order; each group of kBatch rows issues all of its loads
+    // before the adds, which keep the same order (one dependent add chain).
+    constexpr int kBatch = 8;
+    const int stride = mode == 4 ? 2 * W : W;
+    for (int e0 = 0; e0 < total; e0 += kBatch) {
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
         const int c = tid + kClassThreads * j;
-        if (c < W) {
-          if (kd & 1) acc[j] += g[c];
-          if (kd & 2) acc[j] += mode == 4 ? g[W + c] : ((c & 1) ? -g[c ^ 1] : g[c ^ 1]);
+        if (c >= W) continue;
+        const int c2 = mode == 4 ? W + c : (c ^ 1);
+        float v1[kBatch], v2[kBatch];
+        int kd[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          kd[i] = e0 + i < total ? kinds[e0 + i] : 0;
+          const float* g = dh0 + (size_t)(e0 + i < total ? list[e0 + i] : 0) * stride;
+          v1[i] = (kd[i] & 1) ? g[c] : 0.f;
+          v2[i] = (kd[i] & 2) ? g[c2] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          if (kd[i] & 1) acc[j] += v1[i];
+          if (kd[i] & 2) acc[j] += (mode == 4 || !(c & 1)) ? v2[i] : -v2[i];
         }
       }
     }
