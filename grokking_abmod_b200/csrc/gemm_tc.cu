@@ -10,8 +10,9 @@
 // FP32 columns).  Per 32-wide K block every thread loads and splits one slice
 // of A and B into hi/lo TF32 shared tiles (K-major: a K-outer operand is
 // transposed while staging, since TF32 MMAs read a transposed descriptor as
-// zeros here); thread 0 issues 4 K-steps x 3 MMAs and commits them to an
-// mbarrier that all threads wait on (bounded).  Long reductions (K = batch
+// zeros here); thread 0 issues 4 K-steps x 3 MMAs and commits them to the
+// stage's mbarrier.  Two stages alternate, so the next block loads while the
+// current block's MMAs run; all waits are bounded.  Long reductions (K = batch
 // rows in a weight gradient) split K over grid.z; each chunk writes its own
 // partial tile and a second kernel sums the chunks in a fixed order, so the
 // result is bitwise reproducible.
@@ -27,6 +28,8 @@ namespace mb {
 namespace {
 
 constexpr int kGemmBM = 128, kGemmBN = 64, kGemmBK = 32;
+constexpr int kGemmStages = 2;
+constexpr int kGemmStageFloats = 2 * kGemmBM * kGemmBK + 2 * kGemmBN * kGemmBK;  // A hi/lo, B hi/lo
 
 // Rows [r0, r0+R) x K columns [k0, k0+BK) of a K-major operand
 // (element (r, k) at g[r * ld + k]) into hi / lo blocked tiles, zero outside.
@@ -76,20 +79,19 @@ __global__ void __launch_bounds__(128, 1)
     gemm_tf32x3_kernel(GemmOperand A, GemmOperand B, float* __restrict__ C, int ldc, size_t chunk_stride, int M,
                        int N, int K, int k_chunk, bool a_tmem, int* __restrict__ err) {
   extern __shared__ __align__(128) float sm[];
-  float* Ah = sm;
-  float* Al = Ah + kGemmBM * kGemmBK;
-  float* Bh = Al + kGemmBM * kGemmBK;
-  float* Bl = Bh + kGemmBN * kGemmBK;
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bar[kGemmStages];
   __shared__ uint32_t tmem_base;
   __shared__ int failed;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * kGemmBN;
   const int kbeg = blockIdx.z * k_chunk, kend = min(K, kbeg + k_chunk);
+  const int nb = kend > kbeg ? (kend - kbeg + kGemmBK - 1) / kGemmBK : 0;
   C += blockIdx.z * chunk_stride;  // split-K: this chunk's own partial tile
-  if (warp == 0) tc::tmem_alloc(&tmem_base, 128);
+  // TMEM: the 64-column accumulator, then per stage 32 hi + 32 lo columns of
+  // a TMEM-staged A block.
+  if (warp == 0) tc::tmem_alloc(&tmem_base, 256);
   if (tid == 0) {
-    tc::bar_init(&bar, 1);
+    for (int st = 0; st < kGemmStages; ++st) tc::bar_init(&bar[st], 1);
     tc::bar_init_fence();
     failed = 0;
   }
@@ -99,11 +101,16 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t tmem = tmem_base;
   const uint32_t idesc = tc::idesc_tf32(kGemmBM, kGemmBN, false, false);
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-  uint32_t phase = 0;
-  for (int k0 = kbeg; k0 < kend; k0 += kGemmBK) {
+  // K block i into stage st (shared-memory tiles, or TMEM columns for A).
+  auto load = [&](int i, int st) {
+    const int k0 = kbeg + i * kGemmBK;
+    float* Ah = sm + st * kGemmStageFloats;
+    float* Al = Ah + kGemmBM * kGemmBK;
+    float* Bh = Al + kGemmBM * kGemmBK;
+    float* Bl = Bh + kGemmBN * kGemmBK;
     if (a_tmem) {
-      // This thread's row of the A block, split and stored to TMEM columns
-      // [64, 96) (hi) and [96, 128) (lo) of its lane.
+      // This thread's row of the A block, split and stored to the stage's
+      // TMEM columns of its lane.
       float hi[16], lo[16];
       for (int half = 0; half < 2; ++half) {
 #pragma unroll
@@ -113,8 +120,8 @@ __global__ void __launch_bounds__(128, 1)
           hi[j] = tc::tf32_hi(x);
           lo[j] = x - hi[j];
         }
-        tc::tmem_st16(tmem + lane_off + 64 + half * 16, hi);
-        tc::tmem_st16(tmem + lane_off + 96 + half * 16, lo);
+        tc::tmem_st16(tmem + lane_off + 64 + 64 * st + half * 16, hi);
+        tc::tmem_st16(tmem + lane_off + 96 + 64 * st + half * 16, lo);
       }
       tc::tmem_st_wait();
     } else if (A.k_outer) {
@@ -128,45 +135,78 @@ __global__ void __launch_bounds__(128, 1)
       load_kmajor<kGemmBN>(Bh, Bl, B.p, B.ld, n0, N, k0, kend);
     tc::fence_async_smem();
     tc::fence_before_sync();
-    __syncthreads();
+  };
+  // Two stages: block i + 1 is loaded while block i's MMAs run.  A stage is
+  // refilled only after the MMAs that read it (block i - 1) have completed.
+  uint32_t phase[kGemmStages] = {0, 0};
+  if (nb > 0) load(0, 0);
+  __syncthreads();
+  for (int i = 0; i < nb; ++i) {
+    const int st = i & 1;
     if (tid == 0) {
       tc::fence_after_sync();
+      const float* Ah = sm + st * kGemmStageFloats;
+      const float* Al = Ah + kGemmBM * kGemmBK;
+      const float* Bh = Al + kGemmBM * kGemmBK;
+      const float* Bl = Bh + kGemmBN * kGemmBK;
 #pragma unroll
       for (int s = 0; s < kGemmBK / 8; ++s) {
         const uint64_t ah = tc::desc_kmajor(Ah, kGemmBK, s), al = tc::desc_kmajor(Al, kGemmBK, s);
         const uint64_t bh = tc::desc_kmajor(Bh, kGemmBK, s), bl = tc::desc_kmajor(Bl, kGemmBK, s);
-        const uint32_t acc = (k0 > kbeg || s > 0) ? 1u : 0u;
+        const uint32_t acc = (i > 0 || s > 0) ? 1u : 0u;
         if (a_tmem) {
-          tc::mma_ts(tmem, tmem + 64 + 8 * s, bh, idesc, acc);
-          tc::mma_ts(tmem, tmem + 64 + 8 * s, bl, idesc, 1u);
-          tc::mma_ts(tmem, tmem + 96 + 8 * s, bh, idesc, 1u);
+          const uint32_t a0 = tmem + 64 + 64 * st;
+          tc::mma_ts(tmem, a0 + 8 * s, bh, idesc, acc);
+          tc::mma_ts(tmem, a0 + 8 * s, bl, idesc, 1u);
+          tc::mma_ts(tmem, a0 + 32 + 8 * s, bh, idesc, 1u);
         } else {
           tc::mma_ss(tmem, ah, bh, idesc, acc);
           tc::mma_ss(tmem, ah, bl, idesc, 1u);
           tc::mma_ss(tmem, al, bh, idesc, 1u);
         }
       }
-      tc::commit(&bar);
+      tc::commit(&bar[st]);
     }
-    if (!tc::bar_wait(&bar, phase)) failed = 1;
-    phase ^= 1;
+    if (i + 1 < nb) {
+      const int nx = st ^ 1;
+      if (i >= 1) {
+        if (!tc::bar_wait(&bar[nx], phase[nx])) failed = 1;
+        phase[nx] ^= 1;
+        tc::fence_after_sync();
+      }
+      load(i + 1, nx);
+    }
     __syncthreads();
     if (failed) break;
   }
+  // The last block's commit covers every MMA this thread issued.
+  if (nb > 0 && !failed) {
+    const int st = (nb - 1) & 1;
+    if (!tc::bar_wait(&bar[st], phase[st])) failed = 1;
+  }
   tc::fence_after_sync();
+  __syncthreads();
   if (!failed) {
     const int r = m0 + tid;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + lane_off;
     // An empty K range (a trailing chunk) never wrote TMEM: its tile is zero.
-    const bool empty = kbeg >= kend;
+    const bool empty = nb == 0;
 #pragma unroll
     for (int c0 = 0; c0 < kGemmBN; c0 += 16) {
       float v[16];
       tc::tmem_ld16(lane_base + c0, v);
       if (r < M) {
+        float* dst = C + (size_t)r * ldc + n0 + c0;
+        if (n0 + c0 + 16 <= N && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (n0 + c0 + j < N) C[(size_t)r * ldc + n0 + c0 + j] = empty ? 0.f : v[j];
+          for (int q = 0; q < 4; ++q)
+            reinterpret_cast<float4*>(dst)[q] = empty ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                                      : make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (n0 + c0 + j < N) dst[j] = empty ? 0.f : v[j];
+        }
       }
     }
   } else if (tid == 0) {
@@ -174,7 +214,7 @@ __global__ void __launch_bounds__(128, 1)
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, 128);
+  if (warp == 0) tc::tmem_dealloc(tmem, 256);
 }
 
 // C[m][n] = sum over chunks (in order) of partial[chunk][m][n].
@@ -188,7 +228,7 @@ __global__ void gemm_reduce_chunks(const float* __restrict__ partial, int chunks
   }
 }
 
-size_t gemm_smem() { return (size_t)(2 * kGemmBM * kGemmBK + 2 * kGemmBN * kGemmBK) * sizeof(float); }
+size_t gemm_smem() { return (size_t)kGemmStages * kGemmStageFloats * sizeof(float); }
 
 }  // namespace
 
