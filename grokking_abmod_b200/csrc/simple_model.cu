@@ -428,159 +428,69 @@ __global__ void activation_gradient(size_t count, const float* __restrict__ dh, 
 }
 
 // ---------------------------------------------------- shared-Neighbor
-// The shared linear Neighbor chain over the class rows, one CTA: thread t
-// owns channel c = t % W of the rows k = t / W, t / W + RG, ... (RG = row
-// groups), and every layer ends with a block barrier.
+// The shared linear Neighbor chain over the class rows.  The rows are
+// independent through the chain, so CTA b owns rows [b RG, b RG + RG) (RG =
+// 1024 / W row groups) and thread (rg, c) channel c of row b RG + rg; the
+// row moves between two shared-memory buffers, one barrier per layer:
 //   states[0][k] = e_k
 //   states[l+1][k][c] = states[l][k][c] w0[c] + states[l][k][c+1] w1[c]
 // states[ed] is the embedding E of the operands and of the readout.
 constexpr int kChainThreads = 1024;
 __global__ void __launch_bounds__(kChainThreads)
     chain_forward(int m, int W, int ed, const float* __restrict__ chain, float* __restrict__ states) {
+  __shared__ float buf[2][kChainThreads];
   const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
+  const int k = blockIdx.x * RG + rg;
+  const bool active = rg < RG && k < m;
+  const int cn = c + 1 == W ? 0 : c + 1;
   const size_t mw = (size_t)m * W;
-  if (rg < RG)
-    for (int k = rg; k < m; k += RG) states[(size_t)k * W + c] = c == k ? 1.f : 0.f;
+  if (active) {
+    const float e = c == k ? 1.f : 0.f;
+    buf[0][rg * W + c] = e;
+    states[(size_t)k * W + c] = e;
+  }
   __syncthreads();
   for (int l = 0; l < ed; ++l) {
     const float w0 = chain[(size_t)l * 2 * W + 2 * c], w1 = chain[(size_t)l * 2 * W + 2 * c + 1];
-    const float* in = states + l * mw;
-    float* out = states + (l + 1) * mw;
-    if (rg < RG)
-      for (int k = rg; k < m; k += RG)
-        out[(size_t)k * W + c] = fmaf(in[(size_t)k * W + (c + 1) % W], w1, in[(size_t)k * W + c] * w0);
+    const float* in = buf[l & 1];
+    float* out = buf[(l + 1) & 1];
+    if (active) {
+      const float v = fmaf(in[rg * W + cn], w1, in[rg * W + c] * w0);
+      out[rg * W + c] = v;
+      states[(l + 1) * mw + (size_t)k * W + c] = v;
+    }
     __syncthreads();
   }
 }
 
-// Chain backward over the class rows (one CTA, same thread layout): dv = dE;
-// for l = ed-1 .. 0 the chain weights' gradient sums dv[k][c] v_l[k][c] and
-// dv[k][c] v_l[k][c+1] over the rows (each thread over its rows in order,
-// then the row groups in order), and dv <- dv[c] w0[c] + dv[c-1] w1[c-1]
-// (double-buffered in dva / dvb).
+// Chain backward over the class rows (same layout): dv = dE; for l = ed-1
+// .. 0 the chain weights' gradient sums dv[k][c] v_l[k][c] and dv[k][c]
+// v_l[k][c+1] over the CTA's rows (in row order) into partials[cta][l][2W],
+// which reduce_cta_partials sums over the CTAs in order, and dv <- dv[c] w0[c]
+// + dv[c-1] w1[c-1].
 __global__ void __launch_bounds__(kChainThreads)
     chain_backward(int m, int W, int ed, const float* __restrict__ chain, const float* __restrict__ states,
-                   const float* __restrict__ dE, float* dva, float* dvb, float* __restrict__ grad) {
+                   const float* __restrict__ dE, float* __restrict__ partials) {
+  __shared__ float buf[2][kChainThreads];
   __shared__ float part[2][kChainThreads];
   const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
-  const int cp = (c + W - 1) % W;
-  const size_t mw = (size_t)m * W;
-  const float* dv = dE;
-  for (int l = ed - 1; l >= 0; --l) {
-    const float w0 = chain[(size_t)l * 2 * W + 2 * c], w1p = chain[(size_t)l * 2 * W + 2 * cp + 1];
-    const float* v = states + l * mw;
-    float* out = (l & 1) ? dva : dvb;
-    float g0 = 0.f, g1 = 0.f;
-    if (rg < RG)
-      for (int k = rg; k < m; k += RG) {
-        const float d = dv[(size_t)k * W + c];
-        g0 = fmaf(d, v[(size_t)k * W + c], g0);
-        g1 = fmaf(d, v[(size_t)k * W + (c + 1) % W], g1);
-        if (l > 0) out[(size_t)k * W + c] = fmaf(dv[(size_t)k * W + cp], w1p, d * w0);
-      }
-    part[0][threadIdx.x] = g0;
-    part[1][threadIdx.x] = g1;
-    __syncthreads();
-    if (threadIdx.x < W) {
-      float s0 = 0.f, s1 = 0.f;
-      for (int q = 0; q < RG; ++q) {
-        s0 += part[0][q * W + threadIdx.x];
-        s1 += part[1][q * W + threadIdx.x];
-      }
-      grad[(size_t)l * 2 * W + 2 * threadIdx.x] = s0;
-      grad[(size_t)l * 2 * W + 2 * threadIdx.x + 1] = s1;
-    }
-    __syncthreads();
-    dv = out;
-  }
-}
-
-// The same chain with the row state in shared memory (used when 2 m W floats
-// fit in kChainSmemFloats and every thread holds at most kChainRows rows):
-// each layer reads its input from one buffer and writes the other plus the
-// states[] copy the backward pass and the readout GEMMs use.  The arithmetic
-// and its order are those of chain_forward / chain_backward, so the results
-// are identical; only the memory the layers exchange through changes.
-constexpr int kChainSmemFloats = 40960;  // 160 KiB
-constexpr int kChainRows = 16;
-__global__ void __launch_bounds__(kChainThreads)
-    chain_forward_smem(int m, int W, int ed, const float* __restrict__ chain, float* __restrict__ states) {
-  extern __shared__ float csm[];
-  const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
-  const int mw = m * W;
-  if (rg < RG)
-    for (int k = rg; k < m; k += RG) {
-      const float e = c == k ? 1.f : 0.f;
-      csm[k * W + c] = e;
-      states[(size_t)k * W + c] = e;
-    }
-  __syncthreads();
-  const int cn = c + 1 == W ? 0 : c + 1;
-  for (int l = 0; l < ed; ++l) {
-    const float w0 = chain[(size_t)l * 2 * W + 2 * c], w1 = chain[(size_t)l * 2 * W + 2 * c + 1];
-    const float* in = csm + (l & 1) * mw;
-    float* out = csm + ((l + 1) & 1) * mw;
-    float* st = states + (size_t)(l + 1) * mw;
-    if (rg < RG) {
-      float val[kChainRows];
-#pragma unroll
-      for (int i = 0; i < kChainRows; ++i) {
-        const int k = rg + i * RG;
-        if (k < m) val[i] = fmaf(in[k * W + cn], w1, in[k * W + c] * w0);
-      }
-#pragma unroll
-      for (int i = 0; i < kChainRows; ++i) {
-        const int k = rg + i * RG;
-        if (k < m) {
-          out[k * W + c] = val[i];
-          st[(size_t)k * W + c] = val[i];
-        }
-      }
-    }
-    __syncthreads();
-  }
-}
-
-__global__ void __launch_bounds__(kChainThreads)
-    chain_backward_smem(int m, int W, int ed, const float* __restrict__ chain, const float* __restrict__ states,
-                        const float* __restrict__ dE, float* __restrict__ grad) {
-  extern __shared__ float csm[];  // dv double buffer, 2 m W floats
-  __shared__ float part[2][kChainThreads];
-  const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
+  const int k = blockIdx.x * RG + rg;
+  const bool active = rg < RG && k < m;
   const int cp = c == 0 ? W - 1 : c - 1, cn = c + 1 == W ? 0 : c + 1;
-  const int mw = m * W;
-  for (int i = threadIdx.x; i < mw; i += kChainThreads) csm[i] = dE[i];
+  const size_t mw = (size_t)m * W;
+  if (active) buf[0][rg * W + c] = dE[(size_t)k * W + c];
   __syncthreads();
   for (int l = ed - 1; l >= 0; --l) {
     const float w0 = chain[(size_t)l * 2 * W + 2 * c], w1p = chain[(size_t)l * 2 * W + 2 * cp + 1];
-    const float* v = states + (size_t)l * mw;
-    const float* dv = csm + ((ed - 1 - l) & 1) * mw;
-    float* out = csm + ((ed - l) & 1) * mw;
+    const float* dv = buf[(ed - 1 - l) & 1];
+    float* out = buf[(ed - l) & 1];
     float g0 = 0.f, g1 = 0.f;
-    if (rg < RG) {
-      // The layer's saved states come from L2: each group of 8 rows issues
-      // all its loads first.
-      for (int i0 = 0; i0 < kChainRows; i0 += 8) {
-        float vc[8], vn[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int k = rg + (i0 + i) * RG;
-          if (k < m) {
-            vc[i] = v[(size_t)k * W + c];
-            vn[i] = v[(size_t)k * W + cn];
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int k = rg + (i0 + i) * RG;
-          if (k < m) {
-            const float d = dv[k * W + c];
-            g0 = fmaf(d, vc[i], g0);
-            g1 = fmaf(d, vn[i], g1);
-            if (l > 0) out[k * W + c] = fmaf(dv[k * W + cp], w1p, d * w0);
-          }
-        }
-      }
+    if (active) {
+      const float* v = states + l * mw + (size_t)k * W;
+      const float d = dv[rg * W + c];
+      g0 = d * v[c];
+      g1 = d * v[cn];
+      if (l > 0) out[rg * W + c] = fmaf(dv[rg * W + cp], w1p, d * w0);
     }
     part[0][threadIdx.x] = g0;
     part[1][threadIdx.x] = g1;
@@ -591,8 +501,9 @@ __global__ void __launch_bounds__(kChainThreads)
         s0 += part[0][q * W + threadIdx.x];
         s1 += part[1][q * W + threadIdx.x];
       }
-      grad[(size_t)l * 2 * W + 2 * threadIdx.x] = s0;
-      grad[(size_t)l * 2 * W + 2 * threadIdx.x + 1] = s1;
+      float* out_g = partials + ((size_t)blockIdx.x * ed + l) * 2 * W;
+      out_g[2 * threadIdx.x] = s0;
+      out_g[2 * threadIdx.x + 1] = s1;
     }
     __syncthreads();
   }
@@ -1494,8 +1405,8 @@ struct Workspace {
   float *h = nullptr, *act = nullptr, *dact = nullptr, *dh0 = nullptr, *part = nullptr;  // mesh-mlp
   float *hs = nullptr, *ns = nullptr, *invs = nullptr, *zs = nullptr, *dh = nullptr, *dz = nullptr, *dn = nullptr,
         *dhf = nullptr, *dEread = nullptr, *gemm_part = nullptr;
-  float *hf = nullptr, *invf = nullptr, *states = nullptr, *dEemb = nullptr, *dv = nullptr,
-        *dv2 = nullptr;                                           // shared-Neighbor
+  float *hf = nullptr, *invf = nullptr, *states = nullptr, *dEemb = nullptr,
+        *dv = nullptr;  // shared-Neighbor (dv: the chain's per-CTA weight partials)
   float *es = nullptr, *as = nullptr, *dex = nullptr, *dax = nullptr;  // residual-mlp expansion
   float *cat = nullptr, *dcat = nullptr;  // tied concatenation [E a | E b] and its gradient
   int bwd_ctas = 0;
@@ -1788,10 +1699,10 @@ class SimpleModel {
     return c_.architecture == kSharedNeighbor && f <= kCoreSmemFloats ? f : 0;
   }
   int fwd_smem() const { return (core_smem_floats() + kFwdWarps * (int)c_.width) * 4; }
-  // The shared-memory chain kernels apply (see chain_forward_smem).
-  bool chain_in_smem(int m) const {
-    const int W = (int)c_.width, RG = kChainThreads / W;
-    return RG >= 1 && 2 * m * W <= kChainSmemFloats && m <= kChainRows * RG;
+  // CTAs of the chain kernels: kChainThreads / W class rows each.
+  int chain_ctas() const {
+    const int RG = kChainThreads / (int)c_.width;
+    return ((int)c_.modulus + RG - 1) / RG;
   }
   int bwd_smem() const { return (core_smem_floats() + kBwdWarps * 5 * (int)c_.width) * 4; }
   // Residual mesh kernels: all mesh weights staged in shared memory when
@@ -1830,10 +1741,6 @@ class SimpleModel {
     });
   }
   void set_attributes() {
-    SIMPLE_CUDA(cudaFuncSetAttribute(&chain_forward_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kChainSmemFloats * 4));
-    SIMPLE_CUDA(cudaFuncSetAttribute(&chain_backward_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kChainSmemFloats * 4));
     if (c_.activation == kRelu)
       set_attributes_impl<kRelu>();
     else
@@ -1959,8 +1866,7 @@ class SimpleModel {
       w->states = M.alloc<float>((ed + 1) * m * W);
       w->dEemb = M.alloc<float>(m * W);
       w->dEread = M.alloc<float>(m * W);
-      w->dv = M.alloc<float>(m * W);
-      w->dv2 = M.alloc<float>(m * W);
+      w->dv = M.alloc<float>((size_t)chain_ctas() * ed * 2 * W);  // chain weight partials
       part = gemm_partial_floats((int)m, (int)W, n, kSplitK);
     }
     w->gemm_part = M.alloc<float>(std::max<size_t>(part, 1));
@@ -2156,11 +2062,7 @@ class SimpleModel {
       const int ed = (int)c_.embedding_mesh_depth;
       const float* chain = w;
       const float* core = w + offsets_[ed];
-      if (chain_in_smem(m))
-        chain_forward_smem<<<1, kChainThreads, 2 * m * W * 4, stream_>>>(m, W, ed, chain, ws.states);
-      else
-        chain_forward<<<1, kChainThreads, 0, stream_>>>(m, W, ed, chain, ws.states);
-      ++launches_;
+      chain_forward<<<chain_ctas(), kChainThreads, 0, stream_>>>(m, W, ed, chain, ws.states); ++launches_;
       const float* E = ws.states + (size_t)ed * m * W;
       shared_forward<ACT, J><<<fgrid, kFwdWarps * 32, fwd_smem(), stream_>>>(
           n, W, (int)c_.depth, strides_, ws.a, ws.b, E, core, ws.hs, ws.hf, ws.invf); ++launches_;
@@ -2366,11 +2268,11 @@ class SimpleModel {
       reduce_cta_partials<<<(int)std::min<size_t>((cnt + 255) / 256, 1184), 256, 0, stream_>>>(
           ws.part, ws.bwd_ctas, cnt, g + offsets_[ed]); ++launches_;
       class_gradient<<<m, kClassThreads, 0, stream_>>>(n, W, m, 1, ws.a, ws.b, ws.dh0, ws.dEread, ws.dEemb); ++launches_;
-      if (chain_in_smem(m))
-        chain_backward_smem<<<1, kChainThreads, 2 * m * W * 4, stream_>>>(m, W, ed, w, ws.states, ws.dEemb, g);
-      else
-        chain_backward<<<1, kChainThreads, 0, stream_>>>(m, W, ed, w, ws.states, ws.dEemb, ws.dv, ws.dv2, g);
+      chain_backward<<<chain_ctas(), kChainThreads, 0, stream_>>>(m, W, ed, w, ws.states, ws.dEemb, ws.dv);
       ++launches_;
+      const size_t ccnt = (size_t)ed * 2 * W;
+      reduce_cta_partials<<<(int)std::min<size_t>((ccnt + 255) / 256, 1184), 256, 0, stream_>>>(
+          ws.dv, chain_ctas(), ccnt, g); ++launches_;
     }
     SIMPLE_CUDA(cudaGetLastError());
   }
