@@ -6,16 +6,22 @@
 // 161-232 forward / input gradient, :234-318 weight gradient) and the
 // building-block check of the tcgen05 path used by the attention kernels.
 //
-// A CTA of 128 threads owns a 128 x 64 tile of C in TMEM (128 lanes x 64
-// FP32 columns).  Per 32-wide K block every thread loads and splits one slice
-// of A and B into hi/lo TF32 shared tiles (K-major: a K-outer operand is
-// transposed while staging, since TF32 MMAs read a transposed descriptor as
-// zeros here); thread 0 issues 4 K-steps x 3 MMAs and commits them to the
-// stage's mbarrier.  Two stages alternate, so the next block loads while the
-// current block's MMAs run; all waits are bounded.  Long reductions (K = batch
+// A CTA of 256 threads owns a 128 x 64 tile of C in TMEM (128 lanes x 64
+// FP32 columns).  The raw fp32 tiles of each 32-wide K block of A and B are
+// copied into shared memory four blocks ahead by TMA tensor copies (cp.async
+// pieces where an operand's alignment rules a tensor map out); every thread then
+// splits one slice of a landed block into hi/lo TF32 K-major tiles (a
+// K-outer operand is transposed while splitting, since TF32 MMAs read a
+// transposed descriptor as zeros here) and thread 0 issues 4 K-steps x 3
+// MMAs, committed to the hi/lo stage's mbarrier.  Two hi/lo stages
+// alternate, so one block is split while the previous block's MMAs run; all
+// waits are bounded.  Long reductions (K = batch
 // rows in a weight gradient) split K over grid.z; each chunk writes its own
 // partial tile and a second kernel sums the chunks in a fixed order, so the
 // result is bitwise reproducible.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <string>
 
@@ -31,27 +37,104 @@ constexpr int kGemmBM = 128, kGemmBN = 64, kGemmBK = 32;
 constexpr int kGemmStages = 2;
 constexpr int kGemmStageFloats = 2 * kGemmBM * kGemmBK + 2 * kGemmBN * kGemmBK;  // A hi/lo, B hi/lo
 
-// Rows [r0, r0+R) x K columns [k0, k0+BK) of a K-major operand
-// (element (r, k) at g[r * ld + k]) into hi / lo blocked tiles, zero outside.
+// Eight warps: the copy and split work of a K block is spread over all of
+// them; warp w reads TMEM lane quarter w % 4, column half w / 4.
+constexpr int kGemmThreads = 256;
+// Raw fp32 operand tiles staged ahead of the split: kGemmRaw stages, all in
+// flight while the tensor cores work on earlier blocks.  A K-major tile is
+// raw[r][BK] with the 16-byte pieces of row r at piece c ^ (r & 7) (the TMA
+// 128-byte swizzle, so the split's row-wise reads are conflict-free); a
+// K-outer tile is raw[k][R].  Tiles come from TMA tensor copies where the
+// operand allows one (16-byte aligned base and row stride), else cp.async.
+constexpr int kGemmRaw = 4;
+constexpr int kRawFloats = (kGemmBM + kGemmBN) * kGemmBK;
+constexpr int kTmaA = 1, kTmaB = 2;
+
+__device__ __forceinline__ int raw_kmajor(int r, int c) { return r * kGemmBK + (((c >> 2) ^ (r & 7)) << 2); }
+
+// One 2D tensor copy (box at coordinates x inner, y outer) into shared
+// memory, completing its bytes on the mbarrier.  x is a multiple of 32
+// (K-major) or of 64 (K-outer) elements: every copy starts 16-byte aligned.
+__device__ __forceinline__ void tma_load_2d(float* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(tc::smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc::smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tc::smem_addr(dst)), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, int bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(tc::smem_addr(dst)), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Starts the copy of rows [r0, r0+R) x K columns [k0, k0+BK) of an operand
+// into a raw tile; bytes outside the matrix are zero-filled (and not read).
+// `vec`: 16-byte copies are aligned (base 16-byte aligned, ld a multiple of 4).
 template <int R>
-__device__ __forceinline__ void load_kmajor(float* hi, float* lo, const float* __restrict__ g, int ld, int r0,
-                                            int rows, int k0, int K) {
-  constexpr int C4 = kGemmBK / 4;
-  for (int i = threadIdx.x; i < R * C4; i += blockDim.x) {
-    const int rl = i & 7, c4 = (i >> 3) % C4, rh = (i >> 3) / C4;
-    const int r = rh * 8 + rl, c = c4 * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int gr = r0 + r, gc = k0 + c;
-    if (gr < rows) {
-      const float* p = g + (size_t)gr * ld + gc;
-      if (gc + 3 < K && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
-        v = *reinterpret_cast<const float4*>(p);
-      } else {
-        v.x = gc < K ? p[0] : 0.f;
-        v.y = gc + 1 < K ? p[1] : 0.f;
-        v.z = gc + 2 < K ? p[2] : 0.f;
-        v.w = gc + 3 < K ? p[3] : 0.f;
-      }
+__device__ __forceinline__ void stage_raw(float* raw, const GemmOperand& op, bool vec, int r0, int rows, int k0,
+                                          int K) {
+  constexpr int kPer = R * (kGemmBK / 4) / kGemmThreads;
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int i = threadIdx.x + u * kGemmThreads;
+    int gr, gk, rlim, klim;
+    float* dst;
+    if (!op.k_outer) {  // 16-byte pieces along k
+      const int r = i >> 3, c = (i & 7) * 4;
+      gr = r0 + r;
+      gk = k0 + c;
+      dst = raw + raw_kmajor(r, c);
+      rlim = gr < rows ? 1 : 0;
+      klim = K - gk;
+    } else {  // 16-byte pieces along r
+      const int kk = i / (R / 4), r = (i % (R / 4)) * 4;
+      gr = r0 + r;
+      gk = k0 + kk;
+      dst = raw + kk * R + r;
+      rlim = rows - gr;
+      klim = gk < K ? 1 : 0;
+    }
+    const int n = op.k_outer ? (klim > 0 ? min(4, max(0, rlim)) : 0) : (rlim > 0 ? min(4, max(0, klim)) : 0);
+    const float* src = n > 0 ? op.p + (op.k_outer ? (size_t)gk * op.ld + gr : (size_t)gr * op.ld + gk) : op.p;
+    if (vec) {
+      cp_async16(dst, src, 4 * n);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cp_async4(dst + j, j < n ? src + j : op.p, j < n ? 4 : 0);
+    }
+  }
+}
+
+// Splits a landed raw tile into hi / lo TF32 K-major blocked tiles.  A
+// thread takes one row and one 4-wide K group; consecutive threads take
+// consecutive rows, so the 16-byte stores of a quarter warp fill one
+// contiguous core-matrix run and the raw reads are conflict-free.
+template <int R>
+__device__ __forceinline__ void split_raw(float* hi, float* lo, const float* raw, bool k_outer) {
+  constexpr int kPer = R * (kGemmBK / 4) / kGemmThreads;
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int i = threadIdx.x + u * kGemmThreads;
+    int r, c;
+    float4 v;
+    if (!k_outer) {
+      r = (i >> 3) / (kGemmBK / 4) * 8 + (i & 7);
+      c = ((i >> 3) % (kGemmBK / 4)) * 4;
+      v = *reinterpret_cast<const float4*>(raw + raw_kmajor(r, c));
+    } else {
+      r = i % R;
+      c = (i / R) * 4;
+      v = make_float4(raw[c * R + r], raw[(c + 1) * R + r], raw[(c + 2) * R + r], raw[(c + 3) * R + r]);
     }
     const float4 h = make_float4(tc::tf32_hi(v.x), tc::tf32_hi(v.y), tc::tf32_hi(v.z), tc::tf32_hi(v.w));
     const int off = tc::blk(r, c, kGemmBK);
@@ -60,26 +143,13 @@ __device__ __forceinline__ void load_kmajor(float* hi, float* lo, const float* _
   }
 }
 
-// The same from a K-outer operand (element (r, k) at g[k * ld + r]): reads
-// coalesce along r and the tile is transposed into K-major blocks.
-template <int R>
-__device__ __forceinline__ void load_kouter(float* hi, float* lo, const float* __restrict__ g, int ld, int r0,
-                                            int rows, int k0, int K) {
-  for (int i = threadIdx.x; i < kGemmBK * R; i += blockDim.x) {
-    const int r = i % R, kk = i / R;
-    const float x = (k0 + kk < K && r0 + r < rows) ? g[(size_t)(k0 + kk) * ld + r0 + r] : 0.f;
-    const float h = tc::tf32_hi(x);
-    const int off = tc::blk(r, kk, kGemmBK);
-    hi[off] = h;
-    lo[off] = x - h;
-  }
-}
-
-__global__ void __launch_bounds__(128, 1)
-    gemm_tf32x3_kernel(GemmOperand A, GemmOperand B, float* __restrict__ C, int ldc, size_t chunk_stride, int M,
-                       int N, int K, int k_chunk, bool a_tmem, int* __restrict__ err) {
-  extern __shared__ __align__(128) float sm[];
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tf32x3_kernel(GemmOperand A, GemmOperand B, const __grid_constant__ CUtensorMap tma_a,
+                       const __grid_constant__ CUtensorMap tma_b, int tma, float* __restrict__ C, int ldc,
+                       size_t chunk_stride, int M, int N, int K, int k_chunk, bool a_tmem, int* __restrict__ err) {
+  extern __shared__ __align__(1024) float sm[];
   __shared__ uint64_t bar[kGemmStages];
+  __shared__ uint64_t full[kGemmRaw];  // TMA completion per raw stage
   __shared__ uint32_t tmem_base;
   __shared__ int failed;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -92,6 +162,7 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) tc::tmem_alloc(&tmem_base, 256);
   if (tid == 0) {
     for (int st = 0; st < kGemmStages; ++st) tc::bar_init(&bar[st], 1);
+    for (int st = 0; st < kGemmRaw; ++st) tc::bar_init(&full[st], 1);
     tc::bar_init_fence();
     failed = 0;
   }
@@ -100,17 +171,45 @@ __global__ void __launch_bounds__(128, 1)
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base;
   const uint32_t idesc = tc::idesc_tf32(kGemmBM, kGemmBN, false, false);
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-  // K block i into stage st (shared-memory tiles, or TMEM columns for A).
-  auto load = [&](int i, int st) {
-    const int k0 = kbeg + i * kGemmBK;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  // Raw tiles start on a 1024-byte boundary (the 128-byte swizzle's period).
+  float* raw_base = sm + kGemmStages * kGemmStageFloats;
+  raw_base += ((1024u - (tc::smem_addr(raw_base) & 1023u)) & 1023u) / 4;
+  const bool vec_a = A.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(A.p) & 15) == 0;
+  const bool vec_b = B.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(B.p) & 15) == 0;
+  // Starts the copies of K block i into raw stage i % kGemmRaw: thread 0
+  // issues the tensor copies, every thread its cp.async pieces (one commit
+  // group per block, empty past the end so the group count stays uniform).
+  auto stage = [&](int i) {
+    if (i < nb) {
+      const int s = i % kGemmRaw;
+      float* raw = raw_base + s * kRawFloats;
+      const int k0 = kbeg + i * kGemmBK;
+      if (tma && tid == 0) {
+        const uint32_t bytes = ((tma & kTmaA) ? kGemmBM * kGemmBK * 4 : 0) + ((tma & kTmaB) ? kGemmBN * kGemmBK * 4 : 0);
+        tc::bar_expect_tx(&full[s], bytes);
+        if (tma & kTmaA) tma_load_2d(raw, &tma_a, A.k_outer ? m0 : k0, A.k_outer ? k0 : m0, &full[s]);
+        if (tma & kTmaB)
+          tma_load_2d(raw + kGemmBM * kGemmBK, &tma_b, B.k_outer ? n0 : k0, B.k_outer ? k0 : n0, &full[s]);
+      }
+      if (!a_tmem && !(tma & kTmaA)) stage_raw<kGemmBM>(raw, A, vec_a, m0, M, k0, kend);
+      if (!(tma & kTmaB)) stage_raw<kGemmBN>(raw + kGemmBM * kGemmBK, B, vec_b, n0, N, k0, kend);
+    }
+    cp_async_commit();
+  };
+  uint32_t full_phase = 0;  // bit s: parity of raw stage s's next completion
+  int landed = 0;           // blocks whose tensor copies have been waited for
+  // Splits landed K block i into hi/lo stage i & 1 (A of a TMEM-staged
+  // operand is read from global memory straight into its TMEM columns).
+  auto split = [&](int i) {
+    const int st = i & 1;
+    const float* raw = raw_base + (i % kGemmRaw) * kRawFloats;
     float* Ah = sm + st * kGemmStageFloats;
     float* Al = Ah + kGemmBM * kGemmBK;
     float* Bh = Al + kGemmBM * kGemmBK;
     float* Bl = Bh + kGemmBN * kGemmBK;
-    if (a_tmem) {
-      // This thread's row of the A block, split and stored to the stage's
-      // TMEM columns of its lane.
+    if (a_tmem && tid < kGemmBM) {  // warps 0-3: one TMEM lane (A row) per thread
+      const int k0 = kbeg + i * kGemmBK;
       float hi[16], lo[16];
       for (int half = 0; half < 2; ++half) {
 #pragma unroll
@@ -124,25 +223,37 @@ __global__ void __launch_bounds__(128, 1)
         tc::tmem_st16(tmem + lane_off + 96 + 64 * st + half * 16, lo);
       }
       tc::tmem_st_wait();
-    } else if (A.k_outer) {
-      load_kouter<kGemmBM>(Ah, Al, A.p, A.ld, m0, M, k0, kend);
-    } else {
-      load_kmajor<kGemmBM>(Ah, Al, A.p, A.ld, m0, M, k0, kend);
+    } else if (!a_tmem) {
+      split_raw<kGemmBM>(Ah, Al, raw, A.k_outer);
     }
-    if (B.k_outer)
-      load_kouter<kGemmBN>(Bh, Bl, B.p, B.ld, n0, N, k0, kend);
-    else
-      load_kmajor<kGemmBN>(Bh, Bl, B.p, B.ld, n0, N, k0, kend);
+    split_raw<kGemmBN>(Bh, Bl, raw + kGemmBM * kGemmBK, B.k_outer);
     tc::fence_async_smem();
     tc::fence_before_sync();
   };
-  // Two stages: block i + 1 is loaded while block i's MMAs run.  A stage is
-  // refilled only after the MMAs that read it (block i - 1) have completed.
+  // Pipeline: raw copies run kGemmRaw blocks ahead; block i is split
+  // into hi/lo stage i & 1 once the MMAs of block i - 2 (the stage's last
+  // reader) have completed, and its MMAs then run while block i + 1 is
+  // split.
   uint32_t phase[kGemmStages] = {0, 0};
-  if (nb > 0) load(0, 0);
-  __syncthreads();
+  for (int p = 0; p < kGemmRaw; ++p) stage(p);
   for (int i = 0; i < nb; ++i) {
     const int st = i & 1;
+    cp_async_wait<kGemmRaw - 1>();  // block i's group has landed
+    if (tma) {
+      const int s = i % kGemmRaw;
+      if (!tc::bar_wait(&full[s], (full_phase >> s) & 1u)) failed = 1;
+      full_phase ^= 1u << s;
+      landed = i + 1;
+    }
+    __syncthreads();
+    if (i >= 2) {
+      if (!tc::bar_wait(&bar[st], phase[st])) failed = 1;
+      phase[st] ^= 1;
+      tc::fence_after_sync();
+    }
+    split(i);
+    __syncthreads();
+    if (failed) break;
     if (tid == 0) {
       tc::fence_after_sync();
       const float* Ah = sm + st * kGemmStageFloats;
@@ -167,17 +278,20 @@ __global__ void __launch_bounds__(128, 1)
       }
       tc::commit(&bar[st]);
     }
-    if (i + 1 < nb) {
-      const int nx = st ^ 1;
-      if (i >= 1) {
-        if (!tc::bar_wait(&bar[nx], phase[nx])) failed = 1;
-        phase[nx] ^= 1;
-        tc::fence_after_sync();
-      }
-      load(i + 1, nx);
+    // Raw stage i % kGemmRaw was consumed by the split above (all threads
+    // passed the barrier since): refill it with block i + kGemmRaw.
+    stage(i + kGemmRaw);
+  }
+  cp_async_wait<0>();
+  // After a failed wait, let the tensor copies still in flight land (bounded)
+  // before the shared memory is released.
+  if (tma) {
+    const int issued = min(nb, landed + kGemmRaw - 1);
+    for (int j = landed; j < issued; ++j) {
+      const int s = j % kGemmRaw;
+      tc::bar_wait(&full[s], (full_phase >> s) & 1u);
+      full_phase ^= 1u << s;
     }
-    __syncthreads();
-    if (failed) break;
   }
   // The last block's commit covers every MMA this thread issued.
   if (nb > 0 && !failed) {
@@ -187,12 +301,13 @@ __global__ void __launch_bounds__(128, 1)
   tc::fence_after_sync();
   __syncthreads();
   if (!failed) {
-    const int r = m0 + tid;
+    const int r = m0 + (warp & 3) * 32 + (tid & 31);
     const uint32_t lane_base = tmem + lane_off;
     // An empty K range (a trailing chunk) never wrote TMEM: its tile is zero.
     const bool empty = nb == 0;
 #pragma unroll
-    for (int c0 = 0; c0 < kGemmBN; c0 += 16) {
+    for (int h = 0; h < kGemmBN / 32; ++h) {
+      const int c0 = (warp >> 2) * (kGemmBN / 2) + h * 16;
       float v[16];
       tc::tmem_ld16(lane_base + c0, v);
       if (r < M) {
@@ -228,7 +343,51 @@ __global__ void gemm_reduce_chunks(const float* __restrict__ partial, int chunks
   }
 }
 
-size_t gemm_smem() { return (size_t)kGemmStages * kGemmStageFloats * sizeof(float); }
+size_t gemm_smem() {
+  return ((size_t)kGemmStages * kGemmStageFloats + (size_t)kGemmRaw * kRawFloats) * sizeof(float) + 1024;
+}
+
+// cuTensorMapEncodeTiled from the driver (null if unavailable).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Tensor map of an operand's (rows x K) matrix with an R x BK box: K-major as
+// [rows][K] with the 128-byte swizzle, K-outer as [K][rows] unswizzled.
+// False (the kernel then stages with cp.async) when the operand's base or
+// row stride is not 16-byte aligned or the driver refuses the map.
+bool encode_operand(CUtensorMap* map, const GemmOperand& op, int rows, int K, int R) {
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr || (reinterpret_cast<uintptr_t>(op.p) & 15) != 0 || op.ld % 4 != 0) return false;
+  cuuint64_t dims[2];
+  cuuint32_t box[2];
+  const cuuint32_t elem[2] = {1, 1};
+  if (op.k_outer) {
+    dims[0] = (cuuint64_t)rows;
+    dims[1] = (cuuint64_t)K;
+    box[0] = (cuuint32_t)R;
+    box[1] = kGemmBK;
+  } else {
+    dims[0] = (cuuint64_t)K;
+    dims[1] = (cuuint64_t)rows;
+    box[0] = kGemmBK;
+    box[1] = (cuuint32_t)R;
+  }
+  const cuuint64_t stride[1] = {(cuuint64_t)op.ld * sizeof(float)};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(op.p), dims, stride, box,
+                            elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            op.k_outer ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
 
 }  // namespace
 
@@ -255,11 +414,16 @@ void launch_gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, 
   require(chunks == 1 || kc % kGemmBK == 0, "split-K chunks must be multiples of 32");
   require(chunks == 1 || partial != nullptr, "split-K needs a partial buffer");
   dim3 grid((M + kGemmBM - 1) / kGemmBM, (N + kGemmBN - 1) / kGemmBN, chunks);
+  CUtensorMap ta{}, tb{};
+  int tma = 0;
+  if (!a_tmem && encode_operand(&ta, A, M, K, kGemmBM)) tma |= kTmaA;
+  if (encode_operand(&tb, B, N, K, kGemmBN)) tma |= kTmaB;
   if (chunks == 1) {
-    gemm_tf32x3_kernel<<<grid, 128, gemm_smem(), st>>>(A, B, C, ldc, 0, M, N, K, kc, a_tmem, err);
+    gemm_tf32x3_kernel<<<grid, kGemmThreads, gemm_smem(), st>>>(A, B, ta, tb, tma, C, ldc, 0, M, N, K, kc, a_tmem,
+                                                                err);
   } else {
-    gemm_tf32x3_kernel<<<grid, 128, gemm_smem(), st>>>(A, B, partial, N, (size_t)M * N, M, N, K, kc, a_tmem,
-                                                       err);
+    gemm_tf32x3_kernel<<<grid, kGemmThreads, gemm_smem(), st>>>(A, B, ta, tb, tma, partial, N, (size_t)M * N, M, N,
+                                                                K, kc, a_tmem, err);
     const size_t mn = (size_t)M * N;
     const int blocks = (int)std::min<size_t>((mn + 255) / 256, 148 * 8);
     gemm_reduce_chunks<<<blocks, 256, 0, st>>>(partial, chunks, M, N, C, ldc);

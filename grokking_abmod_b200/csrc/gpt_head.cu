@@ -1,11 +1,13 @@
-// Tied embedding mesh, vocabulary head, cross-entropy, embedding gradient,
-// gradient reduction and AdamW for Mesh GPT on sm_100a.
+// Tied embedding mesh, vocabulary head, cross-entropy, gradient reduction and
+// AdamW for Mesh GPT on sm_100a.  The embedding gradient itself
+// (gpt_embedding_gradient_partials / _reduce, src/gpt/gpu.rs:1159-1218) is
+// one split-K tensor-core GEMM over the head's dlogits and the token
+// indicator written here (see the gradient pass of gpt_model.cu).
 //
 // Reference kernels restated: gpt_embed / gpt_embedding_transpose / gpt_head /
 // gpt_cross_entropy / gpt_head_backward (src/gpt/gpu.rs:41-56, :904-1021),
-// gpt_embedding_gradient_partials / _reduce (:1159-1218), the embedding mesh
-// forward/backward over the vocabulary (:2094-2156, :2564-2605),
-// gpt_mesh_gradient_reduce (:1126-1149) and gpt_adam (:1369-1391).
+// the embedding mesh forward/backward over the vocabulary (:2094-2156,
+// :2564-2605), gpt_mesh_gradient_reduce (:1126-1149) and gpt_adam (:1369-1391).
 
 #include "common.cuh"
 
@@ -84,14 +86,19 @@ __global__ void __launch_bounds__(kHeadWarps * 32)
 }
 
 // Cross-entropy per row (src/gpt/gpu.rs:955-994): loss_rows and
-// dlogits = (softmax - onehot) / supervised; ignored rows get zeros.
+// dlogits = (softmax - onehot) / supervised; ignored rows get zeros.  Also
+// writes the row's input-token indicator (1 at tokens[r], else 0), the
+// second half of the embedding-gradient contraction's left operand.
 __global__ void __launch_bounds__(kHeadWarps * 32)
     head_loss(int rows, int V, const float* __restrict__ logits, const uint32_t* __restrict__ targets,
-              const float* __restrict__ supervised, float* __restrict__ loss_rows, float* __restrict__ dlogits) {
+              const float* __restrict__ supervised, const uint32_t* __restrict__ tokens,
+              float* __restrict__ loss_rows, float* __restrict__ dlogits, float* __restrict__ indicator) {
   const int lane = threadIdx.x & 31, r = blockIdx.x * kHeadWarps + (threadIdx.x >> 5);
   if (r >= rows) return;
   const float* l = logits + (size_t)r * V;
   float* d = dlogits + (size_t)r * V;
+  const uint32_t tok = tokens[r];
+  for (int t = lane; t < V; t += 32) indicator[(size_t)r * V + t] = (uint32_t)t == tok ? 1.f : 0.f;
   const uint32_t tg = targets[r];
   if (tg == kIgnoreTarget) {
     for (int t = lane; t < V; t += 32) d[t] = 0.f;
@@ -132,63 +139,6 @@ __global__ void __launch_bounds__(kHeadWarps * 32)
     const float4 n = *reinterpret_cast<const float4*>(nr + ch), g = *reinterpret_cast<const float4*>(gr + ch);
     *reinterpret_cast<float4*>(dx + (size_t)r * W + ch) =
         make_float4(iv * (g.x - n.x * s), iv * (g.y - n.y * s), iv * (g.z - n.z * s), iv * (g.w - n.w * s));
-  }
-}
-
-// ---- embedding gradient partials: dE[t][c] = sum_r dlogits[r][t] nf[r][c]
-// + [tok_r == t] dx0[r][c] over a chunk of rows.  Grid (W / 64, chunks);
-// 256 threads own a 4 x 4 (token, channel) patch of a 64-channel slab, for
-// V up to 64 per pass (larger vocabularies loop over token slabs).
-constexpr int kEmbChunk = 256;
-
-__global__ void __launch_bounds__(256)
-    embedding_gradient_partials(int rows, int W, int V, const uint32_t* __restrict__ tokens,
-                                const float* __restrict__ dlogits, const float* __restrict__ nf,
-                                const float* __restrict__ dx0, float* __restrict__ partial) {
-  __shared__ float sl[32][64 + 1];   // dlogits rows x tokens
-  __shared__ float sn[32][64 + 1];   // nf rows x channels
-  __shared__ float sx[32][64 + 1];   // dx0 rows x channels
-  __shared__ int stok[32];
-  const int c0 = blockIdx.x * 64;
-  const int r0 = blockIdx.y * kEmbChunk;
-  const int r1 = min(rows, r0 + kEmbChunk);
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;  // channels tx*4.., tokens ty*4..
-  for (int t0 = 0; t0 < V; t0 += 64) {
-    float acc[4][4] = {};
-    for (int rb = r0; rb < r1; rb += 32) {
-      __syncthreads();
-      for (int i = threadIdx.x; i < 32 * 64; i += 256) {
-        const int rr = i / 64, j = i % 64;
-        const int r = rb + rr;
-        const bool ok = r < r1;
-        sl[rr][j] = ok && t0 + j < V ? dlogits[(size_t)r * V + t0 + j] : 0.f;
-        sn[rr][j] = ok && c0 + j < W ? nf[(size_t)r * W + c0 + j] : 0.f;
-        sx[rr][j] = ok && c0 + j < W ? dx0[(size_t)r * W + c0 + j] : 0.f;
-      }
-      if (threadIdx.x < 32) stok[threadIdx.x] = rb + (int)threadIdx.x < r1 ? (int)tokens[rb + threadIdx.x] : -1;
-      __syncthreads();
-      for (int rr = 0; rr < 32; ++rr) {
-        const int tok = stok[rr] - t0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float a = sl[rr][ty * 4 + i];
-          const bool hit = tok == ty * 4 + i;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            acc[i][j] += a * sn[rr][tx * 4 + j];
-            if (hit) acc[i][j] += sx[rr][tx * 4 + j];
-          }
-        }
-      }
-    }
-    for (int i = 0; i < 4; ++i) {
-      const int t = t0 + ty * 4 + i;
-      if (t >= V) continue;
-      for (int j = 0; j < 4; ++j) {
-        const int ch = c0 + tx * 4 + j;
-        if (ch < W) partial[((size_t)blockIdx.y * V + t) * W + ch] = acc[i][j];
-      }
-    }
   }
 }
 

@@ -321,7 +321,9 @@ struct Workspace {
   DeviceArena mem;
   std::vector<float*> x;  // L + 1
   std::vector<float*> q, k, v, o, xm, lse;
-  float *nf, *dlog, *logits, *loss_rows, *g, *dO, *dvx, *dxm, *delta, *dq, *dk, *dv, *emb_partial, *dE;
+  // nf and g are one allocation ([2][rows][W]), as are dlog and indicator
+  // ([2][rows][V]): the embedding gradient contracts both halves in one GEMM.
+  float *nf, *dlog, *indicator, *logits, *loss_rows, *g, *dO, *dvx, *dxm, *delta, *dq, *dk, *dv, *emb_partial, *dE;
   float *head_inv, *head_dn;  // final RMSNorm's 1/rms per row and the head's dn = dlogits E
   float* emb_mesh_partial;
   float* att_scratch;
@@ -331,9 +333,8 @@ struct Workspace {
   int* flags;
   double* loss;
   std::vector<float*> part;  // per parameter group
-  ReduceJob* d_jobs_emb;     // dE reduction
-  ReduceJob* d_jobs;         // group reductions
-  int njobs = 0, max_job = 0, emb_chunks = 0;
+  ReduceJob* d_jobs;  // group reductions
+  int njobs = 0, max_job = 0, emb_k_chunk = 0;
   int grid_qf = 1, grid_pf = 1, grid_pb = 1, grid_qb = 1;
   cudaGraphExec_t graph = nullptr;
   // Kernel boundary events captured into the graph when timing is enabled:
@@ -550,15 +551,26 @@ class GptModel {
     return b;
   }
 
-  size_t step_launches() const {
+  // K chunk of the embedding-gradient GEMM (K = 2 rows): one CTA per SM
+  // (the GEMM's shared-memory pipeline fills an SM) over its V x W output
+  // tiles, chunks a multiple of 32 and at least 256.
+  int embedding_k_chunk(int rows) const {
+    const int K = 2 * rows;
+    const int tiles = ((cfg_.vocab_size + 127) / 128) * ((cfg_.width + 63) / 64);
+    const int chunks = std::max(1, sms_ / tiles);
+    const int kc = ((K + chunks - 1) / chunks + 31) / 32 * 32;
+    return std::max(256, kc);
+  }
+
+  size_t step_launches(int rows) const {
     // count + embedding fwd + per block (qkv, attention, post) forward + head
     // (norm, GEMM, loss, GEMM, norm adjoint) + loss + per block (post,
-    // attention, qkv) backward + embedding partials + 2 reduces + embedding
-    // bwd + optimizer advance + AdamW
+    // attention, qkv) backward + embedding-gradient GEMM (+ its chunk sum) +
+    // group reduce + embedding bwd + optimizer advance + AdamW
     // (a table embedding has no embedding mesh forward or backward)
     const size_t L = cfg_.layers, mesh = table() ? 0 : 1;
     return 1 + mesh + L * (2 + attention_->forward_launches()) + 5 + 1 + L * (2 + attention_->backward_launches()) +
-           1 + 1 + mesh + mesh + 2;
+           gemm_launches(2 * rows, embedding_k_chunk(rows)) + 1 + mesh + mesh + 2;
   }
 
   // ---- data parallelism
@@ -630,13 +642,14 @@ class GptModel {
       ws->xm.push_back(a.alloc<float>(NW));
       ws->lse.push_back(a.alloc<float>((size_t)H * rows));
     }
-    ws->nf = a.alloc<float>(NW);
-    ws->dlog = a.alloc<float>((size_t)rows * V);
+    ws->nf = a.alloc<float>(2 * NW);
+    ws->g = ws->nf + NW;
+    ws->dlog = a.alloc<float>((size_t)2 * rows * V);
+    ws->indicator = ws->dlog + (size_t)rows * V;
     ws->logits = a.alloc<float>((size_t)rows * V);
     ws->head_inv = a.alloc<float>(rows);
     ws->head_dn = a.alloc<float>((size_t)rows * W);
     ws->loss_rows = a.alloc<float>(rows);
-    ws->g = a.alloc<float>(NW);
     ws->dO = a.alloc<float>(NW);
     ws->dvx = a.alloc<float>(NW);
     ws->dxm = a.alloc<float>(NW);
@@ -644,8 +657,8 @@ class GptModel {
     ws->dq = a.alloc<float>(NW);
     ws->dk = a.alloc<float>(NW);
     ws->dv = a.alloc<float>(NW);
-    ws->emb_chunks = (rows + kEmbChunk - 1) / kEmbChunk;
-    ws->emb_partial = a.alloc<float>((size_t)ws->emb_chunks * V * W);
+    ws->emb_k_chunk = embedding_k_chunk(rows);
+    ws->emb_partial = a.alloc<float>(std::max<size_t>(1, gemm_partial_floats(V, W, 2 * rows, ws->emb_k_chunk)));
     ws->dE = a.alloc<float>((size_t)V * W);
     ws->att_scratch = a.alloc<float>(attention_->scratch_floats(rows, H, cfg_.layers));
     if (!table()) ws->emb_mesh_partial = a.alloc<float>((size_t)V * layout_.groups[layout_.embedding].size);
@@ -698,10 +711,6 @@ class GptModel {
     ws->njobs = (int)jobs.size();
     ws->d_jobs = a.alloc<ReduceJob>(jobs.size());
     MB_CUDA(cudaMemcpy(ws->d_jobs, jobs.data(), jobs.size() * sizeof(ReduceJob), cudaMemcpyHostToDevice));
-    ReduceJob ej{ws->emb_partial, table() ? grad_ + layout_.groups[layout_.embedding].offset : ws->dE,
-                 ws->emb_chunks, V * W};
-    ws->d_jobs_emb = a.alloc<ReduceJob>(1);
-    MB_CUDA(cudaMemcpy(ws->d_jobs_emb, &ej, sizeof(ej), cudaMemcpyHostToDevice));
     return ws;
   }
 
@@ -753,7 +762,7 @@ class GptModel {
     launch_gemm({ws.nf, W, false}, {E, W, false}, ws.logits, V, ws.rows, V, W, 0, nullptr, tc_err_, stream_);
     if (with_targets) {
       head_loss<<<hgrid, kHeadWarps * 32, 0, stream_>>>(ws.rows, V, ws.logits, ws.targets, ws.supervised,
-                                                          ws.loss_rows, ws.dlog);
+                                                          ws.tokens, ws.loss_rows, ws.dlog, ws.indicator);
       launch_gemm({ws.dlog, V, false}, {E, W, true}, ws.head_dn, W, ws.rows, W, V, 0, nullptr, tc_err_, stream_);
       head_norm_backward<<<hgrid, kHeadWarps * 32, 0, stream_>>>(ws.rows, W, ws.nf, ws.head_inv, ws.head_dn, ws.g);
     }
@@ -787,13 +796,13 @@ class GptModel {
                             group(bg.key), group(bg.value), ws.rope, ws.g, ws.part[bg.query], ws.part[bg.key],
                             ws.part[bg.value]);
     }
-    // Tied embedding: input-lookup and head contributions, then the mesh.
-    dim3 eg((W + 63) / 64, ws.emb_chunks);
-    mark("embedding_gradient_partials");
-    embedding_gradient_partials<<<eg, 256, 0, stream_>>>(ws.rows, W, V, ws.tokens, ws.dlog, ws.nf, ws.g,
-                                                         ws.emb_partial);
-    mark("reduce_partials");
-    reduce_partials<<<dim3((V * W + 255) / 256, 1), 256, 0, stream_>>>(ws.d_jobs_emb, 1);
+    // Tied embedding: head and input-lookup contributions in one contraction
+    // over K = 2 rows, dE[t][c] = sum_r dlogits[r][t] nf[r][c]
+    // + sum_r [tok_r == t] dx0[r][c], split over K chunks summed in order.
+    mark("embedding_gradient");
+    launch_gemm({ws.dlog, V, true}, {ws.nf, W, true},
+                table() ? grad_ + layout_.groups[layout_.embedding].offset : ws.dE, W, V, W, 2 * ws.rows,
+                ws.emb_k_chunk, ws.emb_partial, tc_err_, stream_);
     mark("embedding_backward");
     if (!table())
       embedding_backward<<<V, W, W * sizeof(float), stream_>>>(W, V, cfg_.attention_mesh_depth, cfg_.connectivity,
@@ -1107,9 +1116,9 @@ int mb_gpt_allocated_device_bytes(mb_gpt* m, size_t* bytes) {
 int mb_gpt_step_launches(mb_gpt* m, size_t rows, size_t sequence, size_t* launches) {
   return guarded([&] {
     need(launches, "launches");
-    (void)rows;
     (void)sequence;
-    *launches = model_of(m).step_launches();
+    mb::require(rows >= 1 && rows <= (size_t)INT32_MAX / 2, "rows out of range");
+    *launches = model_of(m).step_launches((int)rows);
   });
 }
 
