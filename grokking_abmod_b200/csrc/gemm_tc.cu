@@ -143,16 +143,47 @@ __device__ __forceinline__ void split_raw(float* hi, float* lo, const float* raw
   }
 }
 
-__global__ void __launch_bounds__(kGemmThreads, 1)
+// Bounded wait on an mbarrier phase that also gives up as soon as another
+// warp of the CTA has flagged a failure.
+__device__ __forceinline__ bool wait_or_failed(uint64_t* bar, uint32_t parity, volatile int* failed) {
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    if (tc::bar_wait(bar, parity, 4)) return true;
+    if (*failed) return false;
+  }
+  return false;
+}
+
+// Named barrier 1 over the worker warps only (the MMA warp never joins it);
+// workers_any also ORs a flag over them, so all workers take the same branch.
+__device__ __forceinline__ void workers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kGemmThreads) : "memory"); }
+__device__ __forceinline__ bool workers_any(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kGemmThreads)
+      : "memory");
+  return r != 0;
+}
+
+// Warps 0-7 (workers) stage raw tiles, split them into hi/lo stages and run
+// the epilogue; warp 8 issues the MMAs.  Per hi/lo stage st: ready[st] (one
+// arrival per worker warp) publishes a split block to the MMA warp, and
+// done[st] (tcgen05.commit) hands the stage back once its MMAs completed.
+__global__ void __launch_bounds__(kGemmThreads + 32, 1)
     gemm_tf32x3_kernel(GemmOperand A, GemmOperand B, const __grid_constant__ CUtensorMap tma_a,
                        const __grid_constant__ CUtensorMap tma_b, int tma, float* __restrict__ C, int ldc,
                        size_t chunk_stride, int M, int N, int K, int k_chunk, bool a_tmem, int* __restrict__ err) {
   extern __shared__ __align__(1024) float sm[];
-  __shared__ uint64_t bar[kGemmStages];
+  __shared__ uint64_t ready[kGemmStages], done[kGemmStages];
   __shared__ uint64_t full[kGemmRaw];  // TMA completion per raw stage
   __shared__ uint32_t tmem_base;
   __shared__ int failed;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  constexpr int kWorkerWarps = kGemmThreads / 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * kGemmBN;
   const int kbeg = blockIdx.z * k_chunk, kend = min(K, kbeg + k_chunk);
   const int nb = kend > kbeg ? (kend - kbeg + kGemmBK - 1) / kGemmBK : 0;
@@ -161,7 +192,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // a TMEM-staged A block.
   if (warp == 0) tc::tmem_alloc(&tmem_base, 256);
   if (tid == 0) {
-    for (int st = 0; st < kGemmStages; ++st) tc::bar_init(&bar[st], 1);
+    for (int st = 0; st < kGemmStages; ++st) {
+      tc::bar_init(&ready[st], kWorkerWarps);
+      tc::bar_init(&done[st], 1);
+    }
     for (int st = 0; st < kGemmRaw; ++st) tc::bar_init(&full[st], 1);
     tc::bar_init_fence();
     failed = 0;
@@ -170,138 +204,157 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = tmem_base;
-  const uint32_t idesc = tc::idesc_tf32(kGemmBM, kGemmBN, false, false);
   const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
   // Raw tiles start on a 1024-byte boundary (the 128-byte swizzle's period).
   float* raw_base = sm + kGemmStages * kGemmStageFloats;
   raw_base += ((1024u - (tc::smem_addr(raw_base) & 1023u)) & 1023u) / 4;
-  const bool vec_a = A.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(A.p) & 15) == 0;
-  const bool vec_b = B.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(B.p) & 15) == 0;
-  // Starts the copies of K block i into raw stage i % kGemmRaw: thread 0
-  // issues the tensor copies, every thread its cp.async pieces (one commit
-  // group per block, empty past the end so the group count stays uniform).
-  auto stage = [&](int i) {
-    if (i < nb) {
-      const int s = i % kGemmRaw;
-      float* raw = raw_base + s * kRawFloats;
-      const int k0 = kbeg + i * kGemmBK;
-      if (tma && tid == 0) {
-        const uint32_t bytes = ((tma & kTmaA) ? kGemmBM * kGemmBK * 4 : 0) + ((tma & kTmaB) ? kGemmBN * kGemmBK * 4 : 0);
-        tc::bar_expect_tx(&full[s], bytes);
-        if (tma & kTmaA) tma_load_2d(raw, &tma_a, A.k_outer ? m0 : k0, A.k_outer ? k0 : m0, &full[s]);
-        if (tma & kTmaB)
-          tma_load_2d(raw + kGemmBM * kGemmBK, &tma_b, B.k_outer ? n0 : k0, B.k_outer ? k0 : n0, &full[s]);
-      }
-      if (!a_tmem && !(tma & kTmaA)) stage_raw<kGemmBM>(raw, A, vec_a, m0, M, k0, kend);
-      if (!(tma & kTmaB)) stage_raw<kGemmBN>(raw + kGemmBM * kGemmBK, B, vec_b, n0, N, k0, kend);
-    }
-    cp_async_commit();
-  };
-  uint32_t full_phase = 0;  // bit s: parity of raw stage s's next completion
-  int landed = 0;           // blocks whose tensor copies have been waited for
-  // Splits landed K block i into hi/lo stage i & 1 (A of a TMEM-staged
-  // operand is read from global memory straight into its TMEM columns).
-  auto split = [&](int i) {
-    const int st = i & 1;
-    const float* raw = raw_base + (i % kGemmRaw) * kRawFloats;
-    float* Ah = sm + st * kGemmStageFloats;
-    float* Al = Ah + kGemmBM * kGemmBK;
-    float* Bh = Al + kGemmBM * kGemmBK;
-    float* Bl = Bh + kGemmBN * kGemmBK;
-    if (a_tmem && tid < kGemmBM) {  // warps 0-3: one TMEM lane (A row) per thread
-      const int k0 = kbeg + i * kGemmBK;
-      float hi[16], lo[16];
-      for (int half = 0; half < 2; ++half) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int r = m0 + tid, c = k0 + half * 16 + j;
-          const float x = (r < M && c < kend) ? A.p[(size_t)r * A.ld + c] : 0.f;
-          hi[j] = tc::tf32_hi(x);
-          lo[j] = x - hi[j];
+  volatile int* vfailed = &failed;
+
+  if (warp < kWorkerWarps) {
+    const bool vec_a = A.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(A.p) & 15) == 0;
+    const bool vec_b = B.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(B.p) & 15) == 0;
+    const bool cp_a = !a_tmem && !(tma & kTmaA), cp_b = !(tma & kTmaB);
+    // Starts the copies of K block i into raw stage i % kGemmRaw: thread 0
+    // issues the tensor copies, every worker its cp.async pieces (one commit
+    // group per block, empty past the end so the group count stays uniform).
+    auto stage = [&](int i) {
+      if (i < nb) {
+        const int s = i % kGemmRaw;
+        float* raw = raw_base + s * kRawFloats;
+        const int k0 = kbeg + i * kGemmBK;
+        if (tma && tid == 0) {
+          const uint32_t bytes =
+              ((tma & kTmaA) ? kGemmBM * kGemmBK * 4 : 0) + ((tma & kTmaB) ? kGemmBN * kGemmBK * 4 : 0);
+          tc::bar_expect_tx(&full[s], bytes);
+          if (tma & kTmaA) tma_load_2d(raw, &tma_a, A.k_outer ? m0 : k0, A.k_outer ? k0 : m0, &full[s]);
+          if (tma & kTmaB)
+            tma_load_2d(raw + kGemmBM * kGemmBK, &tma_b, B.k_outer ? n0 : k0, B.k_outer ? k0 : n0, &full[s]);
         }
-        tc::tmem_st16(tmem + lane_off + 64 + 64 * st + half * 16, hi);
-        tc::tmem_st16(tmem + lane_off + 96 + 64 * st + half * 16, lo);
+        if (cp_a) stage_raw<kGemmBM>(raw, A, vec_a, m0, M, k0, kend);
+        if (cp_b) stage_raw<kGemmBN>(raw + kGemmBM * kGemmBK, B, vec_b, n0, N, k0, kend);
       }
-      tc::tmem_st_wait();
-    } else if (!a_tmem) {
-      split_raw<kGemmBM>(Ah, Al, raw, A.k_outer);
+      cp_async_commit();
+    };
+    uint32_t full_phase = 0, done_phase = 0;  // bit s: parity of the barrier's next completion
+    int landed = 0;                           // blocks whose tensor copies have been waited for
+    for (int p = 0; p < kGemmRaw; ++p) stage(p);
+    for (int i = 0; i < nb; ++i) {
+      const int st = i & 1, s = i % kGemmRaw;
+      cp_async_wait<kGemmRaw - 1>();  // this thread's pieces of block i have landed
+      bool bad = false;
+      if (tma) {
+        bad |= !wait_or_failed(&full[s], (full_phase >> s) & 1u, vfailed);
+        full_phase ^= 1u << s;
+        landed = i + 1;
+      }
+      // hi/lo stage st was last read by the MMAs of block i - 2.
+      if (i >= 2) {
+        bad |= !wait_or_failed(&done[st], (done_phase >> st) & 1u, vfailed);
+        done_phase ^= 1u << st;
+        tc::fence_after_sync();
+      }
+      // One decision for all workers (and every worker's cp.async pieces
+      // have landed once all have passed this barrier).
+      if (workers_any(bad || *vfailed)) {
+        failed = 1;
+        break;
+      }
+      const float* raw = raw_base + s * kRawFloats;
+      float* Ah = sm + st * kGemmStageFloats;
+      float* Al = Ah + kGemmBM * kGemmBK;
+      float* Bh = Al + kGemmBM * kGemmBK;
+      float* Bl = Bh + kGemmBN * kGemmBK;
+      if (a_tmem) {
+        if (tid < kGemmBM) {  // warps 0-3: one TMEM lane (A row) per thread, read straight from global
+          const int k0 = kbeg + i * kGemmBK;
+          float hi[16], lo[16];
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int r = m0 + tid, c = k0 + half * 16 + j;
+              const float x = (r < M && c < kend) ? A.p[(size_t)r * A.ld + c] : 0.f;
+              hi[j] = tc::tf32_hi(x);
+              lo[j] = x - hi[j];
+            }
+            tc::tmem_st16(tmem + lane_off + 64 + 64 * st + half * 16, hi);
+            tc::tmem_st16(tmem + lane_off + 96 + 64 * st + half * 16, lo);
+          }
+          tc::tmem_st_wait();
+        }
+      } else {
+        split_raw<kGemmBM>(Ah, Al, raw, A.k_outer);
+      }
+      split_raw<kGemmBN>(Bh, Bl, raw + kGemmBM * kGemmBK, B.k_outer);
+      tc::fence_async_smem();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::bar_arrive(&ready[st]);
+      // Every worker has read raw stage s: refill it with block i + kGemmRaw.
+      workers_sync();
+      stage(i + kGemmRaw);
     }
-    split_raw<kGemmBN>(Bh, Bl, raw + kGemmBM * kGemmBK, B.k_outer);
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-  };
-  // Pipeline: raw copies run kGemmRaw blocks ahead; block i is split
-  // into hi/lo stage i & 1 once the MMAs of block i - 2 (the stage's last
-  // reader) have completed, and its MMAs then run while block i + 1 is
-  // split.
-  uint32_t phase[kGemmStages] = {0, 0};
-  for (int p = 0; p < kGemmRaw; ++p) stage(p);
-  for (int i = 0; i < nb; ++i) {
-    const int st = i & 1;
-    cp_async_wait<kGemmRaw - 1>();  // block i's group has landed
+    cp_async_wait<0>();
+    // After a failure, let the tensor copies still in flight land (bounded)
+    // before the shared memory is released.
     if (tma) {
-      const int s = i % kGemmRaw;
-      if (!tc::bar_wait(&full[s], (full_phase >> s) & 1u)) failed = 1;
-      full_phase ^= 1u << s;
-      landed = i + 1;
-    }
-    __syncthreads();
-    if (i >= 2) {
-      if (!tc::bar_wait(&bar[st], phase[st])) failed = 1;
-      phase[st] ^= 1;
-      tc::fence_after_sync();
-    }
-    split(i);
-    __syncthreads();
-    if (failed) break;
-    if (tid == 0) {
-      tc::fence_after_sync();
-      const float* Ah = sm + st * kGemmStageFloats;
-      const float* Al = Ah + kGemmBM * kGemmBK;
-      const float* Bh = Al + kGemmBM * kGemmBK;
-      const float* Bl = Bh + kGemmBN * kGemmBK;
-#pragma unroll
-      for (int s = 0; s < kGemmBK / 8; ++s) {
-        const uint64_t ah = tc::desc_kmajor(Ah, kGemmBK, s), al = tc::desc_kmajor(Al, kGemmBK, s);
-        const uint64_t bh = tc::desc_kmajor(Bh, kGemmBK, s), bl = tc::desc_kmajor(Bl, kGemmBK, s);
-        const uint32_t acc = (i > 0 || s > 0) ? 1u : 0u;
-        if (a_tmem) {
-          const uint32_t a0 = tmem + 64 + 64 * st;
-          tc::mma_ts(tmem, a0 + 8 * s, bh, idesc, acc);
-          tc::mma_ts(tmem, a0 + 8 * s, bl, idesc, 1u);
-          tc::mma_ts(tmem, a0 + 32 + 8 * s, bh, idesc, 1u);
-        } else {
-          tc::mma_ss(tmem, ah, bh, idesc, acc);
-          tc::mma_ss(tmem, ah, bl, idesc, 1u);
-          tc::mma_ss(tmem, al, bh, idesc, 1u);
-        }
+      const int issued = min(nb, landed + kGemmRaw - 1);
+      for (int j = landed; j < issued; ++j) {
+        const int s = j % kGemmRaw;
+        tc::bar_wait(&full[s], (full_phase >> s) & 1u);
+        full_phase ^= 1u << s;
       }
-      tc::commit(&bar[st]);
     }
-    // Raw stage i % kGemmRaw was consumed by the split above (all threads
-    // passed the barrier since): refill it with block i + kGemmRaw.
-    stage(i + kGemmRaw);
-  }
-  cp_async_wait<0>();
-  // After a failed wait, let the tensor copies still in flight land (bounded)
-  // before the shared memory is released.
-  if (tma) {
-    const int issued = min(nb, landed + kGemmRaw - 1);
-    for (int j = landed; j < issued; ++j) {
-      const int s = j % kGemmRaw;
-      tc::bar_wait(&full[s], (full_phase >> s) & 1u);
-      full_phase ^= 1u << s;
+  } else {
+    // MMA warp: block i's 4 K-steps x 3 MMAs (hi.hi + hi.lo + lo.hi) once its
+    // stage is split, committed to done[st]; then the last commit is awaited
+    // (it covers every MMA this thread issued) before the epilogue.
+    const uint32_t idesc = tc::idesc_tf32(kGemmBM, kGemmBN, false, false);
+    uint32_t ready_phase = 0;
+    int committed = 0;
+    for (int i = 0; lane == 0 && i < nb; ++i) {
+      const int st = i & 1;
+      if (!wait_or_failed(&ready[st], (ready_phase >> st) & 1u, vfailed)) {
+        failed = 1;
+        break;
+      }
+      ready_phase ^= 1u << st;
+      tc::fence_after_sync();
+      {
+        const float* Ah = sm + st * kGemmStageFloats;
+        const float* Al = Ah + kGemmBM * kGemmBK;
+        const float* Bh = Al + kGemmBM * kGemmBK;
+        const float* Bl = Bh + kGemmBN * kGemmBK;
+#pragma unroll
+        for (int s = 0; s < kGemmBK / 8; ++s) {
+          const uint64_t ah = tc::desc_kmajor(Ah, kGemmBK, s), al = tc::desc_kmajor(Al, kGemmBK, s);
+          const uint64_t bh = tc::desc_kmajor(Bh, kGemmBK, s), bl = tc::desc_kmajor(Bl, kGemmBK, s);
+          const uint32_t acc = (i > 0 || s > 0) ? 1u : 0u;
+          if (a_tmem) {
+            const uint32_t a0 = tmem + 64 + 64 * st;
+            tc::mma_ts(tmem, a0 + 8 * s, bh, idesc, acc);
+            tc::mma_ts(tmem, a0 + 8 * s, bl, idesc, 1u);
+            tc::mma_ts(tmem, a0 + 32 + 8 * s, bh, idesc, 1u);
+          } else {
+            tc::mma_ss(tmem, ah, bh, idesc, acc);
+            tc::mma_ss(tmem, ah, bl, idesc, 1u);
+            tc::mma_ss(tmem, al, bh, idesc, 1u);
+          }
+        }
+        tc::commit(&done[st]);
+      }
+      committed = i + 1;
+    }
+    // The k-th commit on done[st] completes the barrier's phase k (parity k & 1).
+    if (committed > 0) {
+      const int j = committed - 1;
+      if (!tc::bar_wait(&done[j & 1], (uint32_t)(j >> 1) & 1u)) failed = 1;
     }
   }
-  // The last block's commit covers every MMA this thread issued.
-  if (nb > 0 && !failed) {
-    const int st = (nb - 1) & 1;
-    if (!tc::bar_wait(&bar[st], phase[st])) failed = 1;
-  }
-  tc::fence_after_sync();
+  tc::fence_before_sync();
   __syncthreads();
-  if (!failed) {
-    const int r = m0 + (warp & 3) * 32 + (tid & 31);
+  tc::fence_after_sync();
+  if (warp < kWorkerWarps && !failed) {
+    const int r = m0 + (warp & 3) * 32 + lane;
     const uint32_t lane_base = tmem + lane_off;
     // An empty K range (a trailing chunk) never wrote TMEM: its tile is zero.
     const bool empty = nb == 0;
@@ -324,7 +377,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
-  } else if (tid == 0) {
+  } else if (tid == 0 && failed) {
     atomicExch(err, 1);
   }
   tc::fence_before_sync();
@@ -419,10 +472,10 @@ void launch_gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, 
   if (!a_tmem && encode_operand(&ta, A, M, K, kGemmBM)) tma |= kTmaA;
   if (encode_operand(&tb, B, N, K, kGemmBN)) tma |= kTmaB;
   if (chunks == 1) {
-    gemm_tf32x3_kernel<<<grid, kGemmThreads, gemm_smem(), st>>>(A, B, ta, tb, tma, C, ldc, 0, M, N, K, kc, a_tmem,
+    gemm_tf32x3_kernel<<<grid, kGemmThreads + 32, gemm_smem(), st>>>(A, B, ta, tb, tma, C, ldc, 0, M, N, K, kc, a_tmem,
                                                                 err);
   } else {
-    gemm_tf32x3_kernel<<<grid, kGemmThreads, gemm_smem(), st>>>(A, B, ta, tb, tma, partial, N, (size_t)M * N, M, N,
+    gemm_tf32x3_kernel<<<grid, kGemmThreads + 32, gemm_smem(), st>>>(A, B, ta, tb, tma, partial, N, (size_t)M * N, M, N,
                                                                 K, kc, a_tmem, err);
     const size_t mn = (size_t)M * N;
     const int blocks = (int)std::min<size_t>((mn + 255) / 256, 148 * 8);
