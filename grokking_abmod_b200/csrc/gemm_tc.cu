@@ -9,13 +9,13 @@
 // A CTA of 256 threads owns a 128 x 64 tile of C in TMEM (128 lanes x 64
 // FP32 columns).  The raw fp32 tiles of each 32-wide K block of A and B are
 // copied into shared memory four blocks ahead by TMA tensor copies (cp.async
-// pieces where an operand's alignment rules a tensor map out); every thread then
-// splits one slice of a landed block into hi/lo TF32 K-major tiles (a
-// K-outer operand is transposed while splitting, since TF32 MMAs read a
-// transposed descriptor as zeros here) and thread 0 issues 4 K-steps x 3
-// MMAs, committed to the hi/lo stage's mbarrier.  Two hi/lo stages
-// alternate, so one block is split while the previous block's MMAs run; all
-// waits are bounded.  Long reductions (K = batch
+// pieces where an operand's alignment rules a tensor map out).  Worker warps
+// split a landed block into hi/lo TF32: A rows straight into TMEM columns
+// (one lane per row), B into K-major shared tiles (a K-outer operand is
+// transposed while splitting, since TF32 MMAs read a transposed descriptor
+// as zeros here).  A separate MMA warp issues 4 K-steps x 3 MMAs (A from
+// TMEM, B from shared memory) per block.  Two hi/lo stages alternate, so one
+// block is split while the previous block's MMAs run; all waits are bounded.  Long reductions (K = batch
 // rows in a weight gradient) split K over grid.z; each chunk writes its own
 // partial tile and a second kernel sums the chunks in a fixed order, so the
 // result is bitwise reproducible.
@@ -35,7 +35,7 @@ namespace {
 
 constexpr int kGemmBM = 128, kGemmBN = 64, kGemmBK = 32;
 constexpr int kGemmStages = 2;
-constexpr int kGemmStageFloats = 2 * kGemmBM * kGemmBK + 2 * kGemmBN * kGemmBK;  // A hi/lo, B hi/lo
+constexpr int kGemmStageFloats = 2 * kGemmBN * kGemmBK;  // B hi/lo (A hi/lo live in TMEM)
 
 // Eight warps: the copy and split work of a K block is spread over all of
 // them; warp w reads TMEM lane quarter w % 4, column half w / 4.
@@ -119,12 +119,12 @@ __device__ __forceinline__ void stage_raw(float* raw, const GemmOperand& op, boo
 // thread takes one row and one 4-wide K group; consecutive threads take
 // consecutive rows, so the 16-byte stores of a quarter warp fill one
 // contiguous core-matrix run and the raw reads are conflict-free.
-template <int R>
-__device__ __forceinline__ void split_raw(float* hi, float* lo, const float* raw, bool k_outer) {
-  constexpr int kPer = R * (kGemmBK / 4) / kGemmThreads;
+template <int R, int T>
+__device__ __forceinline__ void split_raw(float* hi, float* lo, const float* raw, bool k_outer, int t) {
+  constexpr int kPer = R * (kGemmBK / 4) / T;
 #pragma unroll
   for (int u = 0; u < kPer; ++u) {
-    const int i = threadIdx.x + u * kGemmThreads;
+    const int i = t + u * T;
     int r, c;
     float4 v;
     if (!k_outer) {
@@ -141,6 +141,37 @@ __device__ __forceinline__ void split_raw(float* hi, float* lo, const float* raw
     *reinterpret_cast<float4*>(hi + off) = h;
     *reinterpret_cast<float4*>(lo + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
   }
+}
+
+// Splits row r of a landed raw A tile into hi / lo TF32 and stores them to
+// this thread's TMEM lane: 32 hi columns at col_hi, 32 lo columns at col_lo.
+__device__ __forceinline__ void split_a_row(const float* raw, bool k_outer, int r, uint32_t col_hi,
+                                            uint32_t col_lo) {
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    float x[16], hi[16], lo[16];
+    if (!k_outer) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(raw + raw_kmajor(r, half * 16 + q * 4));
+        x[4 * q] = v.x;
+        x[4 * q + 1] = v.y;
+        x[4 * q + 2] = v.z;
+        x[4 * q + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) x[j] = raw[(half * 16 + j) * kGemmBM + r];
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      hi[j] = tc::tf32_hi(x[j]);
+      lo[j] = x[j] - hi[j];
+    }
+    tc::tmem_st16(col_hi + half * 16, hi);
+    tc::tmem_st16(col_lo + half * 16, lo);
+  }
+  tc::tmem_st_wait();
 }
 
 // Bounded wait on an mbarrier phase that also gives up as soon as another
@@ -176,7 +207,7 @@ __device__ __forceinline__ bool workers_any(bool v) {
 __global__ void __launch_bounds__(kGemmThreads + 32, 1)
     gemm_tf32x3_kernel(GemmOperand A, GemmOperand B, const __grid_constant__ CUtensorMap tma_a,
                        const __grid_constant__ CUtensorMap tma_b, int tma, float* __restrict__ C, int ldc,
-                       size_t chunk_stride, int M, int N, int K, int k_chunk, bool a_tmem, int* __restrict__ err) {
+                       size_t chunk_stride, int M, int N, int K, int k_chunk, int* __restrict__ err) {
   extern __shared__ __align__(1024) float sm[];
   __shared__ uint64_t ready[kGemmStages], done[kGemmStages];
   __shared__ uint64_t full[kGemmRaw];  // TMA completion per raw stage
@@ -213,7 +244,7 @@ __global__ void __launch_bounds__(kGemmThreads + 32, 1)
   if (warp < kWorkerWarps) {
     const bool vec_a = A.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(A.p) & 15) == 0;
     const bool vec_b = B.ld % 4 == 0 && (reinterpret_cast<uintptr_t>(B.p) & 15) == 0;
-    const bool cp_a = !a_tmem && !(tma & kTmaA), cp_b = !(tma & kTmaB);
+    const bool cp_a = !(tma & kTmaA), cp_b = !(tma & kTmaB);
     // Starts the copies of K block i into raw stage i % kGemmRaw: thread 0
     // issues the tensor copies, every worker its cp.async pieces (one commit
     // group per block, empty past the end so the group count stays uniform).
@@ -260,31 +291,14 @@ __global__ void __launch_bounds__(kGemmThreads + 32, 1)
         break;
       }
       const float* raw = raw_base + s * kRawFloats;
-      float* Ah = sm + st * kGemmStageFloats;
-      float* Al = Ah + kGemmBM * kGemmBK;
-      float* Bh = Al + kGemmBM * kGemmBK;
+      float* Bh = sm + st * kGemmStageFloats;
       float* Bl = Bh + kGemmBN * kGemmBK;
-      if (a_tmem) {
-        if (tid < kGemmBM) {  // warps 0-3: one TMEM lane (A row) per thread, read straight from global
-          const int k0 = kbeg + i * kGemmBK;
-          float hi[16], lo[16];
-          for (int half = 0; half < 2; ++half) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int r = m0 + tid, c = k0 + half * 16 + j;
-              const float x = (r < M && c < kend) ? A.p[(size_t)r * A.ld + c] : 0.f;
-              hi[j] = tc::tf32_hi(x);
-              lo[j] = x - hi[j];
-            }
-            tc::tmem_st16(tmem + lane_off + 64 + 64 * st + half * 16, hi);
-            tc::tmem_st16(tmem + lane_off + 96 + 64 * st + half * 16, lo);
-          }
-          tc::tmem_st_wait();
-        }
-      } else {
-        split_raw<kGemmBM>(Ah, Al, raw, A.k_outer);
-      }
-      split_raw<kGemmBN>(Bh, Bl, raw + kGemmBM * kGemmBK, B.k_outer);
+      // Warps 0-3: A row tid into TMEM lane tid (stage st's hi/lo columns);
+      // warps 4-7: the B tile into shared hi/lo tiles.
+      if (warp < 4)
+        split_a_row(raw, A.k_outer, tid, tmem + lane_off + 64 + 64 * st, tmem + lane_off + 96 + 64 * st);
+      else
+        split_raw<kGemmBN, kGemmThreads / 2>(Bh, Bl, raw + kGemmBM * kGemmBK, B.k_outer, tid - kGemmThreads / 2);
       tc::fence_async_smem();
       tc::fence_before_sync();
       __syncwarp();
@@ -320,25 +334,16 @@ __global__ void __launch_bounds__(kGemmThreads + 32, 1)
       ready_phase ^= 1u << st;
       tc::fence_after_sync();
       {
-        const float* Ah = sm + st * kGemmStageFloats;
-        const float* Al = Ah + kGemmBM * kGemmBK;
-        const float* Bh = Al + kGemmBM * kGemmBK;
+        const float* Bh = sm + st * kGemmStageFloats;
         const float* Bl = Bh + kGemmBN * kGemmBK;
+        const uint32_t a0 = tmem + 64 + 64 * st;  // A hi at a0, lo at a0 + 32
 #pragma unroll
         for (int s = 0; s < kGemmBK / 8; ++s) {
-          const uint64_t ah = tc::desc_kmajor(Ah, kGemmBK, s), al = tc::desc_kmajor(Al, kGemmBK, s);
           const uint64_t bh = tc::desc_kmajor(Bh, kGemmBK, s), bl = tc::desc_kmajor(Bl, kGemmBK, s);
           const uint32_t acc = (i > 0 || s > 0) ? 1u : 0u;
-          if (a_tmem) {
-            const uint32_t a0 = tmem + 64 + 64 * st;
-            tc::mma_ts(tmem, a0 + 8 * s, bh, idesc, acc);
-            tc::mma_ts(tmem, a0 + 8 * s, bl, idesc, 1u);
-            tc::mma_ts(tmem, a0 + 32 + 8 * s, bh, idesc, 1u);
-          } else {
-            tc::mma_ss(tmem, ah, bh, idesc, acc);
-            tc::mma_ss(tmem, ah, bl, idesc, 1u);
-            tc::mma_ss(tmem, al, bh, idesc, 1u);
-          }
+          tc::mma_ts(tmem, a0 + 8 * s, bh, idesc, acc);
+          tc::mma_ts(tmem, a0 + 8 * s, bl, idesc, 1u);
+          tc::mma_ts(tmem, a0 + 32 + 8 * s, bh, idesc, 1u);
         }
         tc::commit(&done[st]);
       }
@@ -461,7 +466,7 @@ int gemm_launches(int K, int k_chunk) { return gemm_chunks(K, k_chunk) > 1 ? 2 :
 
 void launch_gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, int M, int N, int K, int k_chunk,
                  float* partial, int* err, cudaStream_t st, bool a_tmem) {
-  require(!(a_tmem && A.k_outer), "an A operand staged through TMEM must be K-major");
+  (void)a_tmem;  // A is always staged through tensor memory
   const int chunks = gemm_chunks(K, k_chunk);
   const int kc = chunks > 1 ? k_chunk : K;
   require(chunks == 1 || kc % kGemmBK == 0, "split-K chunks must be multiples of 32");
@@ -469,14 +474,13 @@ void launch_gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, 
   dim3 grid((M + kGemmBM - 1) / kGemmBM, (N + kGemmBN - 1) / kGemmBN, chunks);
   CUtensorMap ta{}, tb{};
   int tma = 0;
-  if (!a_tmem && encode_operand(&ta, A, M, K, kGemmBM)) tma |= kTmaA;
+  if (encode_operand(&ta, A, M, K, kGemmBM)) tma |= kTmaA;
   if (encode_operand(&tb, B, N, K, kGemmBN)) tma |= kTmaB;
   if (chunks == 1) {
-    gemm_tf32x3_kernel<<<grid, kGemmThreads + 32, gemm_smem(), st>>>(A, B, ta, tb, tma, C, ldc, 0, M, N, K, kc, a_tmem,
-                                                                err);
+    gemm_tf32x3_kernel<<<grid, kGemmThreads + 32, gemm_smem(), st>>>(A, B, ta, tb, tma, C, ldc, 0, M, N, K, kc, err);
   } else {
     gemm_tf32x3_kernel<<<grid, kGemmThreads + 32, gemm_smem(), st>>>(A, B, ta, tb, tma, partial, N, (size_t)M * N, M, N,
-                                                                K, kc, a_tmem, err);
+                                                                K, kc, err);
     const size_t mn = (size_t)M * N;
     const int blocks = (int)std::min<size_t>((mn + 255) / 256, 148 * 8);
     gemm_reduce_chunks<<<blocks, 256, 0, st>>>(partial, chunks, M, N, C, ldc);

@@ -21,7 +21,8 @@ void gemm_prepare();
 // C[M][N] (row stride ldc) = A . B^T over K.  k_chunk > 0 and < K splits K
 // into chunks of that many (a multiple of 32) with partial tiles in
 // `partial` (gemm_partial_floats floats) summed in chunk order.  `err` is a
-// device flag set if an mbarrier wait gave up.
+// device flag set if an mbarrier wait gave up.  A is always staged through
+// tensor memory; `a_tmem` is accepted for callers that ask for it.
 void launch_gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, int M, int N, int K, int k_chunk,
                  float* partial, int* err, cudaStream_t st, bool a_tmem = false);
 int gemm_chunks(int K, int k_chunk);

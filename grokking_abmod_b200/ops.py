@@ -48,7 +48,8 @@ def mesh_backward(x, dy, weights, connectivity: int = 0):
 
 def gemm_tf32x3(a, b, layout: int = 0):
     """FP32 GEMM via tcgen05 3xTF32, C [m][n] = A . B^T over k.  Layout bits:
-    1 = b given [k][n] (else [n][k]); 2 = A staged through tensor memory;
+    1 = b given [k][n] (else [n][k]); 2 = accepted, the same as 0 (A is always
+    staged through tensor memory);
     4 = a given [k][m] (else [m][k]; not with 2)."""
     import torch
     m, k = (a.shape[1], a.shape[0]) if layout & 4 else a.shape

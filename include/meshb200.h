@@ -167,8 +167,8 @@ int mb_op_mesh_backward(const float* x, const float* dy, float* dx, float* dweig
  * 3xTF32 split (hi.hi + hi.lo + lo.hi), the dense contraction of the
  * reference's FP32 blocked_product GEMMs (src/simple/dense_tiled.rs:161-232).
  * layout 0: B is [n][k] (C = A B^T); 1: B is [k][n] (C = A B, transposed
- * while staged); 2: as 0 with A staged through tensor memory (A-from-TMEM
- * form).  All row-major FP32 device arrays.  d_status (device
+ * while staged); 2: the same as 0 (A is always staged through tensor
+ * memory, the A-from-TMEM MMA form).  All row-major FP32 device arrays.  d_status (device
  * int) is set to 1 if a tensor-core completion wait gave up. */
 int mb_op_gemm_tf32x3(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k, uint32_t layout,
                       int* d_status, void* stream);

@@ -1,6 +1,7 @@
 """tcgen05 3xTF32 GEMM (the tensor-core building blocks) against f64 numpy:
-K-major operands, K-outer (transposed) A and B operands staged K-major, and A
-staged through tensor memory."""
+K-major and K-outer (transposed) A and B operands, including strides that
+rule out a TMA tensor map (the cp.async staging path); A is staged through
+tensor memory."""
 
 import numpy as np
 import pytest
