@@ -151,12 +151,45 @@ struct ReduceJob {
   int size;
 };
 
+// A thread sums four consecutive parameters (one float4 per slot), with the
+// loads of eight slots in flight before they are added in slot order.
 __global__ void reduce_partials(const ReduceJob* __restrict__ jobs, int njobs) {
   const ReduceJob job = jobs[blockIdx.y];
-  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < job.size; p += gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int k = 0; k < job.slots; ++k) s += job.partial[(size_t)k * job.size + p];
-    job.out[p] = s;
+  const bool vec = (job.size & 3) == 0 && (reinterpret_cast<uintptr_t>(job.partial) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(job.out) & 15) == 0;
+  if (!vec) {
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < job.size; p += gridDim.x * blockDim.x) {
+      float s = 0.f;
+      for (int k = 0; k < job.slots; ++k) s += job.partial[(size_t)k * job.size + p];
+      job.out[p] = s;
+    }
+    return;
+  }
+  const int n4 = job.size >> 2;
+  const float4* part = reinterpret_cast<const float4*>(job.partial);
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n4; p += gridDim.x * blockDim.x) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    int k = 0;
+    for (; k + 8 <= job.slots; k += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = part[(size_t)(k + j) * n4 + p];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        s.x += v[j].x;
+        s.y += v[j].y;
+        s.z += v[j].z;
+        s.w += v[j].w;
+      }
+    }
+    for (; k < job.slots; ++k) {
+      const float4 v = part[(size_t)k * n4 + p];
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    reinterpret_cast<float4*>(job.out)[p] = s;
   }
 }
 

@@ -809,7 +809,8 @@ class GptModel {
                                                                31 - __builtin_clz(W), group(layout_.embedding),
                                                                emb_acts_, ws.dE, ws.emb_mesh_partial);
     mark("reduce_partials");
-    reduce_partials<<<dim3((ws.max_job + 255) / 256, ws.njobs), 256, 0, stream_>>>(ws.d_jobs, ws.njobs);
+    reduce_partials<<<dim3(std::max(1, (ws.max_job / 4 + 255) / 256), ws.njobs), 256, 0, stream_>>>(ws.d_jobs,
+                                                                                               ws.njobs);
     mark("end");
     MB_CUDA(cudaGetLastError());
   }
