@@ -92,6 +92,7 @@ SIGNATURES = {
     "mb_gpt_kernel_times": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, c_float_p, c_size_p]),
     "mb_nccl_unique_id": (ctypes.c_int, [c_u8_p]),
     "mb_gpt_attach_nccl": (ctypes.c_int, [ctypes.c_void_p, c_u8_p, ctypes.c_int, ctypes.c_int]),
+    "mb_gpt_attach_nccl_comm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]),
     "mb_gpt_detach_nccl": (ctypes.c_int, [ctypes.c_void_p]),
     "mb_op_mesh_forward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
                                           ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p]),

@@ -161,7 +161,7 @@ std::vector<float> token_codes(const mb_gpt_config& c) {
 }
 
 size_t validate_batch(const mb_gpt_config& c, const uint32_t* inputs, const uint32_t* targets, size_t rows,
-                      size_t sequence) {
+                      size_t sequence, bool allow_unsupervised) {
   require(sequence >= 1 && sequence <= c.context && rows >= 1 && rows % sequence == 0 && rows <= kMaxRows,
           "tokens must form a nonempty batch of equal sequences within context and 131072 rows");
   require(inputs != nullptr, "inputs must not be null");
@@ -174,7 +174,7 @@ size_t validate_batch(const mb_gpt_config& c, const uint32_t* inputs, const uint
       ++supervised;
     }
   }
-  require(supervised > 0, "batch must contain at least one supervised target");
+  require(supervised > 0 || allow_unsupervised, "batch must contain at least one supervised target");
   return supervised;
 }
 

@@ -203,8 +203,11 @@ struct OptimizerState {
 };
 
 // Sets this step's hyperparameters and advances the bias-correction powers
-// (beta_power *= beta in f32, once per update).
-__global__ void optimizer_set(OptimizerState* st, OptimizerState h) {
+// (beta_power *= beta in f32, once per update).  A step whose batch the
+// device rejected (step_flags != 0) changes nothing: neither the powers nor,
+// in adamw, the weights and moments.
+__global__ void optimizer_set(OptimizerState* st, OptimizerState h, const int* __restrict__ step_flags) {
+  if (*step_flags != 0) return;
   st->learning_rate = h.learning_rate;
   st->weight_decay = h.weight_decay;
   st->beta1 = h.beta1;
@@ -216,7 +219,9 @@ __global__ void optimizer_set(OptimizerState* st, OptimizerState h) {
 }
 
 __global__ void adamw(int n, const OptimizerState* __restrict__ st, const float* __restrict__ grad,
-                      float* __restrict__ w, float* __restrict__ m, float* __restrict__ v) {
+                      float* __restrict__ w, float* __restrict__ m, float* __restrict__ v,
+                      const int* __restrict__ step_flags) {
+  if (*step_flags != 0) return;
   const float lr = st->learning_rate, wd = st->weight_decay, b1 = st->beta1, b2 = st->beta2, eps = st->epsilon;
   const float c1 = __fsub_rn(1.0f, st->beta1_power), c2 = __fsub_rn(1.0f, st->beta2_power);
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -236,10 +241,17 @@ __global__ void adamw(int n, const OptimizerState* __restrict__ st, const float*
 // ---- batch validation and supervised count (src/gpt/config.rs:230-253), on
 // the device so device-resident batches need no host round trip.  flags bit 0:
 // token outside the vocabulary; bit 1: target outside the vocabulary; bit 2: no
-// supervised target.
+// supervised target.  stats[4] = (supervised count, bad token, bad target, 0)
+// as floats, so that data-parallel ranks can sum them in one all-reduce; the
+// count is what the cross-entropy divides by.  step_flags holds this step's
+// flags (read by the optimizer), flags accumulates them until the host
+// reads them.
+//   dp == 0: the count and flags are final (a count of 0 becomes 1, flag 4).
+//   dp != 0: stats holds this rank's raw values; finish_supervised turns
+//            their sum over ranks into the final count and flags.
 __global__ void count_supervised(int rows, int V, const uint32_t* __restrict__ tokens,
-                                 const uint32_t* __restrict__ targets, float* __restrict__ supervised,
-                                 int* __restrict__ flags) {
+                                 const uint32_t* __restrict__ targets, float* __restrict__ stats,
+                                 int* __restrict__ step_flags, int* __restrict__ flags, int dp) {
   __shared__ int s_count[32];
   __shared__ int s_flags[32];
   int cnt = 0, fl = 0;
@@ -267,10 +279,28 @@ __global__ void count_supervised(int rows, int V, const uint32_t* __restrict__ t
       c += s_count[w];
       f |= s_flags[w];
     }
+    if (dp) {
+      stats[0] = (float)c;
+      stats[1] = (float)(f & 1);
+      stats[2] = (float)((f >> 1) & 1);
+      stats[3] = 0.f;
+      return;
+    }
     if (c == 0) f |= 4;
-    *supervised = (float)(c > 0 ? c : 1);
+    stats[0] = (float)(c > 0 ? c : 1);
+    *step_flags = f;
     *flags |= f;
   }
+}
+
+// The data-parallel end of count_supervised: stats now holds the sums over
+// ranks (counts stay exact in f32 up to 2^24 rows), so every rank divides by
+// the global supervised count and takes the same flags.
+__global__ void finish_supervised(float* __restrict__ stats, int* __restrict__ step_flags, int* __restrict__ flags) {
+  const int f = (stats[1] > 0.f ? 1 : 0) | (stats[2] > 0.f ? 2 : 0) | (stats[0] == 0.f ? 4 : 0);
+  if (stats[0] == 0.f) stats[0] = 1.f;
+  *step_flags = f;
+  *flags |= f;
 }
 
 // ---- mean cross-entropy: f64 sum of the f32 per-row losses in a fixed

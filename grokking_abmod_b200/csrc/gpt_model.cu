@@ -287,6 +287,7 @@ struct NcclApi {
                              cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_count)(const ncclComm_t, int*) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
 };
 
@@ -303,6 +304,7 @@ NcclApi& nccl() {
     api.all_reduce = (decltype(api.all_reduce))dlsym(h, "ncclAllReduce");
     api.comm_destroy = (decltype(api.comm_destroy))dlsym(h, "ncclCommDestroy");
     api.comm_abort = (decltype(api.comm_abort))dlsym(h, "ncclCommAbort");
+    api.comm_count = (decltype(api.comm_count))dlsym(h, "ncclCommCount");
     api.error_string = (decltype(api.error_string))dlsym(h, "ncclGetErrorString");
   });
   require(api.handle != nullptr && api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy,
@@ -329,14 +331,16 @@ struct Workspace {
   float* att_scratch;
   float2* rope;
   uint32_t *tokens, *targets;
-  float* supervised;
-  int* flags;
+  float* stats;     // [4]: supervised count (the loss divisor), bad-token and bad-target indicators
+  int* step_flags;  // this step's batch flags (the optimizer skips a flagged step)
+  int* flags;       // flags accumulated until mb_gpt_check reads them
   double* loss;
   std::vector<float*> part;  // per parameter group
   ReduceJob* d_jobs;  // group reductions
   int njobs = 0, max_job = 0, emb_k_chunk = 0;
   int grid_qf = 1, grid_pf = 1, grid_pb = 1, grid_qb = 1;
   cudaGraphExec_t graph = nullptr;
+  bool graph_dp = false;  // captured for data parallelism (the batch count runs outside the graph)
   // Kernel boundary events captured into the graph when timing is enabled:
   // marks[i] precedes launch i, marks.back() follows the last one.
   std::vector<cudaEvent_t> marks;
@@ -418,25 +422,25 @@ class GptModel {
   // ---- host-batch entry points (validate on the host like the reference)
   double train_step(const uint32_t* in, const uint32_t* tgt, size_t rows, size_t seq, const mb_adamw* opt) {
     validate_optimizer(*opt);
-    validate_batch(cfg_, in, tgt, rows, seq);
+    validate_batch(cfg_, in, tgt, rows, seq, data_parallel());
     MB_CUDA(cudaSetDevice(device_));
     Workspace& ws = workspace(rows, seq);
     MB_CUDA(cudaMemcpyAsync(ws.tokens, in, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
     MB_CUDA(cudaMemcpyAsync(ws.targets, tgt, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
-    run_gradient_graph(ws);
-    allreduce_and_update(opt);
+    gradient_pass(ws);
+    update(ws, opt);
     return read_loss(ws);
   }
 
   double loss_and_gradient(const uint32_t* in, const uint32_t* tgt, size_t rows, size_t seq, float* grad,
                            size_t n) {
     require(n == count(), "gradient length does not match GPT configuration");
-    validate_batch(cfg_, in, tgt, rows, seq);
+    validate_batch(cfg_, in, tgt, rows, seq, data_parallel());
     MB_CUDA(cudaSetDevice(device_));
     Workspace& ws = workspace(rows, seq);
     MB_CUDA(cudaMemcpyAsync(ws.tokens, in, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
     MB_CUDA(cudaMemcpyAsync(ws.targets, tgt, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
-    run_gradient_graph(ws);
+    gradient_pass(ws);
     const double loss = read_loss(ws);
     MB_CUDA(cudaMemcpyAsync(grad, grad_, n * sizeof(float), cudaMemcpyDeviceToHost, stream_));
     MB_CUDA(cudaStreamSynchronize(stream_));
@@ -451,7 +455,7 @@ class GptModel {
     Workspace& ws = workspace(rows, seq);
     MB_CUDA(cudaMemcpyAsync(ws.tokens, in, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
     MB_CUDA(cudaMemcpyAsync(ws.targets, tgt, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
-    enqueue_forward(ws, true);
+    enqueue_forward(ws, true, true);
     launch_loss(ws);
     return read_loss(ws);
   }
@@ -461,7 +465,7 @@ class GptModel {
     MB_CUDA(cudaSetDevice(device_));
     Workspace& ws = workspace(rows, seq);
     MB_CUDA(cudaMemcpyAsync(ws.tokens, in, rows * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
-    enqueue_forward(ws, false);
+    enqueue_forward(ws, false, false);
     const size_t n = rows * (hidden ? cfg_.width : cfg_.vocab_size);
     MB_CUDA(cudaMemcpyAsync(out, hidden ? ws.x[cfg_.layers] : ws.logits, n * sizeof(float), cudaMemcpyDeviceToHost,
                             stream_));
@@ -489,8 +493,8 @@ class GptModel {
     Workspace& ws = workspace(rows, seq);
     MB_CUDA(cudaMemcpyAsync(ws.tokens, d_in, rows * sizeof(uint32_t), cudaMemcpyDeviceToDevice, stream_));
     MB_CUDA(cudaMemcpyAsync(ws.targets, d_tgt, rows * sizeof(uint32_t), cudaMemcpyDeviceToDevice, stream_));
-    run_gradient_graph(ws);
-    allreduce_and_update(opt);
+    gradient_pass(ws);
+    update(ws, opt);
     if (d_loss != nullptr)
       MB_CUDA(cudaMemcpyAsync(d_loss, ws.loss, sizeof(double), cudaMemcpyDeviceToDevice, stream_));
     last_ = &ws;
@@ -569,7 +573,8 @@ class GptModel {
     // group reduce + embedding bwd + optimizer advance + AdamW
     // (a table embedding has no embedding mesh forward or backward)
     const size_t L = cfg_.layers, mesh = table() ? 0 : 1;
-    return 1 + mesh + L * (2 + attention_->forward_launches()) + 5 + 1 + L * (2 + attention_->backward_launches()) +
+    // data parallelism adds finish_supervised to the count (NCCL calls are not counted)
+    return 1 + (data_parallel() ? 1 : 0) + mesh + L * (2 + attention_->forward_launches()) + 5 + 1 + L * (2 + attention_->backward_launches()) +
            gemm_launches(2 * rows, embedding_k_chunk(rows)) + 1 + mesh + mesh + 2;
   }
 
@@ -582,16 +587,34 @@ class GptModel {
     static_assert(sizeof(uid) == MB_NCCL_ID_BYTES, "NCCL unique id size");
     std::memcpy(&uid, id, sizeof(uid));
     nccl_check(nccl().comm_init_rank(&comm_, world, uid, rank), "ncclCommInitRank");
+    owns_comm_ = true;
+    world_ = world;
+  }
+  // A communicator the caller created (and keeps ownership of) for this
+  // model's device; world is its size, checked against NCCL's own count.
+  void attach_nccl_comm(ncclComm_t comm, int world) {
+    require(comm != nullptr && world >= 1, "communicator must not be null and world size must be positive");
+    detach_nccl();
+    MB_CUDA(cudaSetDevice(device_));
+    if (nccl().comm_count != nullptr) {
+      int n = 0;
+      nccl_check(nccl().comm_count(comm, &n), "ncclCommCount");
+      require(n == world, "world size does not match the communicator");
+    }
+    comm_ = comm;
+    owns_comm_ = false;
     world_ = world;
   }
   void detach_nccl() {
     if (comm_ != nullptr) {
       cudaStreamSynchronize(stream_);
-      nccl().comm_destroy(comm_);
+      if (owns_comm_) nccl().comm_destroy(comm_);
       comm_ = nullptr;
     }
+    owns_comm_ = false;
     world_ = 1;
   }
+  bool data_parallel() const { return comm_ != nullptr && world_ > 1; }
 
  private:
   Workspace& workspace(size_t rows, size_t seq) {
@@ -664,10 +687,12 @@ class GptModel {
     if (!table()) ws->emb_mesh_partial = a.alloc<float>((size_t)V * layout_.groups[layout_.embedding].size);
     ws->tokens = a.alloc<uint32_t>(rows);
     ws->targets = a.alloc<uint32_t>(rows);
-    ws->supervised = a.alloc<float>(1);
+    ws->stats = a.alloc<float>(4);
+    ws->step_flags = a.alloc<int>(1);
     ws->flags = a.alloc<int>(1);
     ws->loss = a.alloc<double>(1);
     MB_CUDA(cudaMemset(ws->flags, 0, sizeof(int)));
+    MB_CUDA(cudaMemset(ws->step_flags, 0, sizeof(int)));
     // RoPE table [seq][hd/2] of (cos, sin), angle = pos / 10000^(i / (hd/2)),
     // evaluated in f64 (src/gpt/gpu.rs:175-208 evaluates it in f32).
     const int half = W / H / 2;
@@ -731,13 +756,18 @@ class GptModel {
     return emb_acts_ + (size_t)cfg_.vocab_size * cfg_.width * cfg_.attention_mesh_depth;
   }
 
-  void enqueue_forward(Workspace& ws, bool with_targets) {
+  // with_targets: the head also computes the cross-entropy and its adjoint;
+  // count: the batch's supervised count is taken here (single-rank graphs and
+  // the rank-local evaluation), else count_and_exchange has taken it.
+  void enqueue_forward(Workspace& ws, bool with_targets, bool count) {
     const Dims d = dims(ws);
     attention_->scratch = ws.att_scratch;
     const int L = cfg_.layers, W = cfg_.width, V = cfg_.vocab_size, H = cfg_.heads;
-    mark("count_supervised");
-    if (with_targets)
-      count_supervised<<<1, 1024, 0, stream_>>>(ws.rows, V, ws.tokens, ws.targets, ws.supervised, ws.flags);
+    if (with_targets && count) {
+      mark("count_supervised");
+      count_supervised<<<1, 1024, 0, stream_>>>(ws.rows, V, ws.tokens, ws.targets, ws.stats, ws.step_flags,
+                                                ws.flags, 0);
+    }
     mark("embedding_forward");
     if (!table()) launch_embedding_forward();
     for (int b = 0; b < L; ++b) {
@@ -761,7 +791,7 @@ class GptModel {
     head_norm<<<hgrid, kHeadWarps * 32, 0, stream_>>>(ws.rows, W, ws.x[L], ws.nf, ws.head_inv);
     launch_gemm({ws.nf, W, false}, {E, W, false}, ws.logits, V, ws.rows, V, W, 0, nullptr, tc_err_, stream_);
     if (with_targets) {
-      head_loss<<<hgrid, kHeadWarps * 32, 0, stream_>>>(ws.rows, V, ws.logits, ws.targets, ws.supervised,
+      head_loss<<<hgrid, kHeadWarps * 32, 0, stream_>>>(ws.rows, V, ws.logits, ws.targets, ws.stats,
                                                           ws.tokens, ws.loss_rows, ws.dlog, ws.indicator);
       launch_gemm({ws.dlog, V, false}, {E, W, true}, ws.head_dn, W, ws.rows, W, V, 0, nullptr, tc_err_, stream_);
       head_norm_backward<<<hgrid, kHeadWarps * 32, 0, stream_>>>(ws.rows, W, ws.nf, ws.head_inv, ws.head_dn, ws.g);
@@ -771,7 +801,7 @@ class GptModel {
 
   void launch_loss(Workspace& ws) {
     mark("loss_reduce");
-    loss_reduce<<<1, 1024, 0, stream_>>>(ws.rows, ws.loss_rows, ws.supervised, ws.loss);
+    loss_reduce<<<1, 1024, 0, stream_>>>(ws.rows, ws.loss_rows, ws.stats, ws.loss);
   }
 
   void enqueue_backward(Workspace& ws) {
@@ -815,8 +845,38 @@ class GptModel {
     MB_CUDA(cudaGetLastError());
   }
 
-  void run_gradient_graph(Workspace& ws) {
+  // One gradient evaluation.  Single rank: the captured graph (count,
+  // forward, loss, backward).  Data parallel (the reference's loss is the mean
+  // over the supervised rows of the whole batch, src/gpt/gpu.rs:2296-2313):
+  // every rank's supervised count and flags are summed first, so each rank
+  // divides its cross-entropy adjoint by the global count; the graph then
+  // yields this rank's share of the gradient and of the loss, and one sum
+  // over ranks of each gives the global mean loss and its exact gradient for
+  // any split of the supervised targets.
+  void gradient_pass(Workspace& ws) {
+    const bool dp = data_parallel();
+    if (dp) {
+      count_supervised<<<1, 1024, 0, stream_>>>(ws.rows, cfg_.vocab_size, ws.tokens, ws.targets, ws.stats,
+                                                ws.step_flags, ws.flags, 1);
+      MB_CUDA(cudaGetLastError());
+      nccl_check(nccl().all_reduce(ws.stats, ws.stats, 4, ncclFloat32, ncclSum, comm_, stream_), "ncclAllReduce");
+      finish_supervised<<<1, 1, 0, stream_>>>(ws.stats, ws.step_flags, ws.flags);
+      MB_CUDA(cudaGetLastError());
+    }
+    run_gradient_graph(ws, dp);
+    if (dp) {
+      nccl_check(nccl().all_reduce(grad_, grad_, count(), ncclFloat32, ncclSum, comm_, stream_), "ncclAllReduce");
+      nccl_check(nccl().all_reduce(ws.loss, ws.loss, 1, ncclFloat64, ncclSum, comm_, stream_), "ncclAllReduce");
+    }
+  }
+
+  void run_gradient_graph(Workspace& ws, bool dp) {
+    if (ws.graph != nullptr && ws.graph_dp != dp) {
+      cudaGraphExecDestroy(ws.graph);
+      ws.graph = nullptr;
+    }
     if (ws.graph == nullptr) {
+      ws.graph_dp = dp;
       cudaGraph_t g = nullptr;
       for (cudaEvent_t e : ws.marks) cudaEventDestroy(e);
       ws.marks.clear();
@@ -824,7 +884,7 @@ class GptModel {
       MB_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
       capturing_ = &ws;
       try {
-        enqueue_forward(ws, true);
+        enqueue_forward(ws, true, !dp);
         launch_loss(ws);
         enqueue_backward(ws);
       } catch (...) {
@@ -843,7 +903,7 @@ class GptModel {
     last_ = &ws;
   }
 
-  void allreduce_and_update(const mb_adamw* opt) {
+  void update(Workspace& ws, const mb_adamw* opt) {
     const size_t P = count();
     auto omark = [&](size_t i, const char* name) {
       if (!timing_) return;
@@ -855,24 +915,31 @@ class GptModel {
       }
       MB_CUDA(cudaEventRecord(opt_marks_[i], stream_));
     };
-    omark(0, "nccl_allreduce");
-    if (comm_ != nullptr && world_ > 1)
-      nccl_check(nccl().all_reduce(grad_, grad_, P, ncclFloat32, ncclAvg, comm_, stream_), "ncclAllReduce");
     OptimizerState st{opt->learning_rate, opt->weight_decay, opt->beta1, opt->beta2, opt->epsilon, 0.f, 0.f, 0};
-    omark(1, "optimizer_set");
-    optimizer_set<<<1, 1, 0, stream_>>>(opt_, st);
+    omark(0, "optimizer_set");
+    optimizer_set<<<1, 1, 0, stream_>>>(opt_, st, ws.step_flags);
     const int threads = 256;
     const int blocks = std::min((int)((P + threads - 1) / threads), sms_ * 8);
-    omark(2, "adamw");
-    adamw<<<blocks, threads, 0, stream_>>>((int)P, opt_, grad_, w_, m_, v_);
-    omark(3, "end");
+    omark(1, "adamw");
+    adamw<<<blocks, threads, 0, stream_>>>((int)P, opt_, grad_, w_, m_, v_, ws.step_flags);
+    omark(2, "end");
     MB_CUDA(cudaGetLastError());
   }
 
+  // The step's loss; with data parallelism also the step's flags, since
+  // only the device sees whether the ranks' batches together hold a
+  // supervised target (a step that holds none updated nothing).
   double read_loss(Workspace& ws) {
     double loss = 0.0;
+    int flags = 0;
     MB_CUDA(cudaMemcpyAsync(&loss, ws.loss, sizeof(double), cudaMemcpyDeviceToHost, stream_));
+    if (ws.graph_dp) MB_CUDA(cudaMemcpyAsync(&flags, ws.step_flags, sizeof(int), cudaMemcpyDeviceToHost, stream_));
     MB_CUDA(cudaStreamSynchronize(stream_));
+    if (flags != 0) {
+      MB_CUDA(cudaMemset(ws.flags, 0, sizeof(int)));
+      require(!(flags & 4), "batch must contain at least one supervised target over all ranks");
+      require(false, "a rank's batch holds a token or target outside the vocabulary");
+    }
     require(std::isfinite(loss), "cross-entropy must contain only finite values", MB_ERR_NONFINITE);
     return loss;
   }
@@ -890,6 +957,7 @@ class GptModel {
   std::deque<std::unique_ptr<Workspace>> workspaces_;
   Workspace* last_ = nullptr;
   ncclComm_t comm_ = nullptr;
+  bool owns_comm_ = false;
   int world_ = 1;
   bool timing_ = false;
   Workspace* capturing_ = nullptr;
@@ -1159,6 +1227,10 @@ int mb_gpt_attach_nccl(mb_gpt* m, const uint8_t id[MB_NCCL_ID_BYTES], int rank, 
     need(id, "id");
     model_of(m).attach_nccl(id, rank, world_size);
   });
+}
+
+int mb_gpt_attach_nccl_comm(mb_gpt* m, void* comm, int world_size) {
+  return guarded([&] { model_of(m).attach_nccl_comm(static_cast<ncclComm_t>(comm), world_size); });
 }
 
 int mb_gpt_detach_nccl(mb_gpt* m) {

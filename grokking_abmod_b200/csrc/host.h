@@ -96,8 +96,10 @@ Layout make_layout(const mb_gpt_config& c);
 std::vector<float> initial_parameters(const mb_gpt_config& c, uint64_t seed);
 std::vector<float> token_codes(const mb_gpt_config& c);
 int mesh_stride(const mb_gpt_config& c, int layer);
+// allow_unsupervised: a data-parallel rank's share may hold no supervised
+// target; the device checks the count over all ranks instead.
 size_t validate_batch(const mb_gpt_config& c, const uint32_t* inputs, const uint32_t* targets, size_t rows,
-                      size_t sequence);
+                      size_t sequence, bool allow_unsupervised = false);
 void validate_optimizer(const mb_adamw& o);
 
 // ---- data

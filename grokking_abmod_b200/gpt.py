@@ -245,6 +245,11 @@ class MeshGpt:
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id)
         check(self._lib.mb_gpt_attach_nccl(self._h, buf, rank, world_size))
 
+    def attach_nccl_comm(self, comm: int, world_size: int) -> None:
+        """Uses a caller-owned NCCL communicator (an ``ncclComm_t`` as an
+        integer address) created on this model's device."""
+        check(self._lib.mb_gpt_attach_nccl_comm(self._h, ctypes.c_void_p(comm), world_size))
+
     def detach_nccl(self) -> None:
         check(self._lib.mb_gpt_detach_nccl(self._h))
 

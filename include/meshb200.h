@@ -137,11 +137,24 @@ int mb_gpt_set_timing(mb_gpt* model, int enable);
 int mb_gpt_kernel_times(mb_gpt* model, char* names, size_t names_len, float* ms, size_t* count);
 
 /* ---- data parallelism (no reference counterpart: the reference is single
- * GPU).  Every rank holds the full model; train_step all-reduces (average)
- * the flat FP32 gradient over NCCL before AdamW, so ranks stay identical. ---- */
+ * GPU).  Every rank holds the full model and passes its own share of the
+ * batch.  The loss is the reference's mean over the supervised rows of the
+ * whole batch (src/gpt/gpu.rs:2296-2313): each training step and each
+ * loss_and_gradient first sums the ranks' supervised counts over NCCL,
+ * divides the cross-entropy adjoint by that global count, then sums the flat
+ * FP32 gradient and the loss over the ranks.  Loss and gradient are
+ * therefore exact for any split of the supervised targets (a rank's share
+ * may hold none), every rank returns the global loss, and AdamW keeps the
+ * ranks identical.  logits, hidden_states and cross_entropy stay local to
+ * the rank.  Every rank must make the same sequence of these calls. ---- */
 #define MB_NCCL_ID_BYTES 128
 int mb_nccl_unique_id(uint8_t id[MB_NCCL_ID_BYTES]);
+/* Creates the model's own communicator from NCCL's 128-byte unique id. */
 int mb_gpt_attach_nccl(mb_gpt* model, const uint8_t id[MB_NCCL_ID_BYTES], int rank, int world_size);
+/* Uses a communicator the caller created on this model's device (an
+ * ncclComm_t passed as void*); the caller keeps ownership and destroys it
+ * after mb_gpt_detach_nccl or mb_gpt_destroy. */
+int mb_gpt_attach_nccl_comm(mb_gpt* model, void* comm, int world_size);
 int mb_gpt_detach_nccl(mb_gpt* model);
 
 /* ---- per-op entry points: device pointers, the caller's cudaStream_t (NULL =

@@ -224,3 +224,47 @@ def test_benchmark_shape_step_is_finite_and_learns():
     losses = [gpu.train_batch_with_optimizer(x, y, 256, opt) for _ in range(6)]
     assert all(np.isfinite(losses)) and losses[-1] < losses[0]
     assert np.isfinite(gpu.parameters()).all()
+
+
+def _adamw_first_step_close(name, params, ref_grad, got, opt, grad_tol):
+    """Parameters after one AdamW step from `params` against the f32 host
+    optimizer applied to the oracle's gradient.  The first step moves each
+    weight by lr * g / (|g| + eps) (+ decay), so a gradient error d changes
+    it by at most lr * min(2, 2 d / |g|): the bound is tight where gradients
+    are well determined and a full step where they sit at the error level."""
+    want, m, v = params.copy(), np.zeros_like(params), np.zeros_like(params)
+    adamw_step(want, m, v, ref_grad, 1, opt.learning_rate, opt.weight_decay, opt.beta1, opt.beta2, opt.epsilon,
+               (np.float32(opt.beta1), np.float32(opt.beta2)))
+    g = np.abs(ref_grad)
+    bound = opt.learning_rate * np.minimum(2.0, 2.0 * grad_tol / np.maximum(g, 1e-30)) + 1e-6 * (1 + np.abs(want))
+    err = np.abs(got.astype(np.float64) - want)
+    assert np.all(err <= bound), f"{name}: worst excess {(err - bound).max():.3e}"
+    # and most weights move by the oracle's step to FP32 accuracy
+    assert np.mean(err <= 1e-6 * (1 + np.abs(want))) > 0.99
+
+
+@pytest.mark.parametrize("name,kw,seqs", [
+    # BASELINE configs[4]'s model and context (one 1024-token sequence; the
+    # timed step runs 32 of them, which are independent until the loss mean)
+    ("cfg4", dict(vocab_size=64, context=1024, width=512, heads=8, layers=8), 1),
+    # BASELINE configs[3]'s model and context, 4 of its 64 sequences
+    ("cfg3", dict(vocab_size=64, context=256, width=256, heads=4, layers=4), 4),
+])
+def test_timed_shapes_match_oracle(name, kw, seqs):
+    """Loss, every gradient and one AdamW step at the shapes the bench times,
+    on its seeded Zipf(1.1) tokens: the attention's long-row paths (1024-key
+    online softmax, the 16-tile causal work order) run here."""
+    from grokking_abmod_b200.data import zipf_batch
+    ref, gpu = _pair(kw)
+    T = kw["context"]
+    x, y = zipf_batch(7, 0, 0, seqs, T)
+    rl, rg = ref.loss_and_gradient(x, y, T)
+    gl, gg = gpu.loss_and_gradient(x, y, T)
+    assert abs(rl - gl) <= 1e-5 * abs(rl), (rl, gl)
+    assert np.abs(rg - gg).max() <= 1e-4 * np.abs(rg).max(), np.abs(rg - gg).max() / np.abs(rg).max()
+    _close("gradients", rg, gg)
+    opt = AdamWOptions(learning_rate=3e-4, weight_decay=0.1)
+    params = gpu.parameters()
+    assert gpu.train_batch_with_optimizer(x, y, T, opt) == gl
+    _adamw_first_step_close(name, params, rg, gpu.parameters(), opt, 1e-4 * np.abs(rg).max())
+    gpu.close()

@@ -267,3 +267,48 @@ def test_archived_mesh_records(case):
     assert abs(got[0] - want[0]) <= 1e-3 * want[0] and abs(got[1] - want[1]) <= 1e-3 * want[1], (got, want)
     assert abs(got[2] - want[2]) <= 2e-3 and abs(got[3] - want[3]) <= 2e-3, (got, want)
     assert abs(got[4] - want[4]) <= 1e-4 * want[4], (got, want)
+
+
+@pytest.mark.parametrize("name", ["cfg0", "cfg1", "cfg2"])
+def test_timed_full_batch_matches_oracle(name):
+    """The bench's grok workload itself: the seed-11 p=97 division split, all
+    4656 training rows in the sampler's order, the reference's seed-11
+    initial weights; loss, every gradient and one AdamW step."""
+    from oracle.data import EquationSampler
+    kw = FULL[["cfg0", "cfg1", "cfg2"].index(name)]
+    config = SimpleConfig(**kw)
+    dataset = EquationDataset(97, "div", 0.5, 11)
+    features, targets = config.encode(dataset.split(False))
+    idx = np.asarray(EquationSampler(len(targets), 11).sample(len(targets)), np.uint32)
+    assert len(idx) == 4656
+    model = GpuSimpleModel(0, config, seed=11)
+    table = model.upload_table(features, targets)
+    loss, grad = model.loss_and_gradient(table, idx)
+    ref = osr.ReferenceSimpleModel(osr.SimpleConfig(**kw), seed=11)
+    assert model.parameters().tobytes() == ref.parameters.tobytes()
+    ref_loss, ref_grad = ref.loss_and_gradient(features[idx], targets[idx])
+    assert abs(loss - ref_loss) <= 1e-5 * abs(ref_loss), (loss, ref_loss)
+    assert _max_rel(grad, ref_grad) <= 1e-4, _max_rel(grad, ref_grad)
+    wd = GROK[name]["optimizer"]["weight_decay"]
+    opt = AdamWOptions(learning_rate=1e-3, weight_decay=wd, beta1=0.9, beta2=0.98)
+    params = model.parameters()
+    batches = model.upload_batches(table, idx)
+    model.train_batch(table, batches, 0, len(idx), opt)
+    model.check()
+    got = model.parameters()
+    oc = osr.SimpleConfig(**kw)
+    scales = np.repeat(np.array(oc.group_learning_rate_scale(), np.float32), oc.groups())
+    want, m, v = params.copy(), np.zeros_like(params), np.zeros_like(params)
+    for scale in np.unique(scales):
+        sel = scales == scale
+        ws, ms, vs = want[sel], m[sel], v[sel]
+        adamw_step(ws, ms, vs, ref_grad[sel], 1, np.float32(opt.learning_rate * scale), opt.weight_decay,
+                   opt.beta1, opt.beta2, opt.epsilon, (np.float32(opt.beta1), np.float32(opt.beta2)))
+        want[sel] = ws
+    # The first AdamW step moves a weight by lr * g / (|g| + eps): a gradient
+    # error d changes it by at most lr * min(2, 2 d / |g|).
+    d = 1e-4 * np.abs(ref_grad).max()
+    bound = opt.learning_rate * scales * np.minimum(2.0, 2.0 * d / np.maximum(np.abs(ref_grad), 1e-30)) \
+        + 1e-6 * (1 + np.abs(want))
+    err = np.abs(got.astype(np.float64) - want)
+    assert np.all(err <= bound), (err - bound).max()
