@@ -93,14 +93,21 @@ def _oracle_sequence(args):
     return time.perf_counter() - t0
 
 
+def _nproc():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def _pool_workers():
     # Each worker holds ~1.3 GB of f64 activations at cfg4; cap the pool.
-    return max(1, min(os.cpu_count() or 1, 16))
+    return max(1, min(_nproc(), 16))
 
 
 def run_oracle_tasks(cfg, tasks, workers):
     """Runs `tasks` oracle sequences over a spawn pool of single-threaded
-    workers; returns (wall seconds, tokens)."""
+    workers; returns (wall seconds, tokens, per-sequence seconds)."""
     import multiprocessing as mp
     env = {"OMP_NUM_THREADS": "1", "OPENBLAS_NUM_THREADS": "1", "MKL_NUM_THREADS": "1"}
     old = {k: os.environ.get(k) for k in env}
@@ -109,7 +116,7 @@ def run_oracle_tasks(cfg, tasks, workers):
         ctx = mp.get_context("spawn")
         with ctx.Pool(workers) as pool:
             t0 = time.perf_counter()
-            pool.map(_oracle_sequence, [(model_kwargs(cfg), 0, i) for i in range(tasks)], chunksize=1)
+            each = pool.map(_oracle_sequence, [(model_kwargs(cfg), 0, i) for i in range(tasks)], chunksize=1)
             wall = time.perf_counter() - t0
     finally:
         for k, v in old.items():
@@ -117,15 +124,17 @@ def run_oracle_tasks(cfg, tasks, workers):
                 os.environ.pop(k, None)
             else:
                 os.environ[k] = v
-    return wall, tasks * cfg["context"]
+    return wall, tasks * cfg["context"], each
 
 
 def cpu_baseline(cfg):
     workers = _pool_workers()
-    wall, tokens = run_oracle_tasks(cfg, workers, workers)
-    return {"value": tokens / wall, "unit": "tokens/s", "cores": workers, "kind": "port",
+    wall, tokens, each = run_oracle_tasks(cfg, workers, workers)
+    return {"value": tokens / wall, "unit": "tokens/s", "cores": workers, "nproc": _nproc(), "kind": "port",
+            "single_thread_value": cfg["context"] * len(each) / sum(each),
             "sample": f"{workers} sequences x {cfg['context']} tokens, one f64 oracle fwd+bwd+AdamW each, "
-                      f"one single-threaded spawn worker per sequence ({wall:.1f} s wall)"}
+                      f"one single-threaded spawn worker per sequence ({wall:.1f} s wall); "
+                      f"single_thread_value = tokens / summed per-sequence seconds of one worker"}
 
 
 def reference_arm(args, cfg):
@@ -137,16 +146,20 @@ def reference_arm(args, cfg):
     warm = min(args.warmup, workers)
     if warm:
         run_oracle_tasks(cfg, warm, workers)
-    wall, tokens = run_oracle_tasks(cfg, args.steps, workers)
+    # whole waves: every worker busy until the end
+    tasks = -(-args.steps // workers) * workers
+    wall, tokens, each = run_oracle_tasks(cfg, tasks, workers)
     value = tokens / wall
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * wall / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * wall / tasks,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": config_block(args, cfg),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "kind": "port",
-                         "sample": f"each step = one {cfg['context']}-token sequence fwd+bwd+AdamW of the f64 "
-                                   f"oracle (the Rust reference cannot be built here), {workers} spawn workers"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": workers, "nproc": _nproc(), "kind": "port",
+                         "single_thread_value": cfg["context"] * len(each) / sum(each),
+                         "sample": f"{tasks} one-{cfg['context']}-token-sequence fwd+bwd+AdamW steps of the f64 "
+                                   f"oracle ({args.steps} requested, rounded up to whole waves of {workers} "
+                                   f"single-threaded spawn workers; the Rust reference cannot be built here)"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -185,7 +198,7 @@ def kernel_work(name, cfg, rows):
     return work.get(name)
 
 
-def roofline(times, cfg, rows, peaks):
+def roofline(times, cfg, rows, peaks, config_name):
     """Dominant kernel of the step (largest summed time) and its roofline."""
     totals, counts = {}, {}
     for name, ms in times:
@@ -218,7 +231,7 @@ def roofline(times, cfg, rows, peaks):
                        "dense bf16 tensor peak, the 3xTF32 ceiling is peak / 6")
         out["frac_of_3xtf32_ceiling"] = achieved / (peak / 6.0) if peak else None
     out.update(bound=kind, achieved=achieved, peak=peak, unit=unit,
-               frac=(achieved / peak if peak else None), traffic=traffic_from_profiles(name))
+               frac=(achieved / peak if peak else None), traffic=traffic_from_profiles(name, config_name))
     out["peak_source"] = "measured (MEASURED_PEAKS.json)" if peaks.get("_measured") else "fallback"
     return out
 
@@ -242,9 +255,10 @@ def step_roofline(cfg, rows, ms_per_step, peaks):
             "peak_source": "measured (MEASURED_PEAKS.json)" if peaks.get("_measured") else "fallback"}
 
 
-def traffic_from_profiles(kernel):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any
-    (a line 'traffic_bytes_per_launch <kernel> <bytes>')."""
+def traffic_from_profiles(kernel, config):
+    """DRAM bytes per launch of `kernel` at bench config `config` from the
+    committed ncu summaries, if any (a line
+    'traffic_bytes_per_launch <config> <kernel> <bytes>')."""
     d = os.path.join(ROOT, "profiles")
     if not os.path.isdir(d):
         return None
@@ -253,9 +267,9 @@ def traffic_from_profiles(kernel):
             continue
         for line in open(os.path.join(d, fn)):
             parts = line.strip().strip("`").split()
-            if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == kernel:
+            if len(parts) == 4 and parts[0] == "traffic_bytes_per_launch" and parts[1:3] == [config, kernel]:
                 try:
-                    return float(parts[2])
+                    return float(parts[3])
                 except ValueError:
                     pass
     return None
@@ -455,7 +469,7 @@ def main():
             "e2e": {"value": e2e, "unit": "tokens/s", "ms_per_step": e_ms / args.steps,
                     "h2d_bytes_per_step": 2 * rows * 4, "d2h_bytes_per_step": 8,
                     "api": "MeshGpt.train_batch_with_optimizer (mb_gpt_train_step), pinned host batches"},
-            "roofline": roofline(times, cfg, rows, peaks),
+            "roofline": roofline(times, cfg, rows, peaks, args.config),
             "step_roofline": step_roofline(cfg, rows, ms / args.steps, peaks),
             "cpu_baseline": base,
             "gpu_launches": model.step_launches(rows, T) * args.steps,
@@ -608,26 +622,38 @@ def grok_main(args):
     torch.cuda.synchronize()
     clock_info = clocks.stop()
     model.check()
-    ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in events))
+    ms_rank = sum(a.elapsed_time(b) for a, b in events)
+    ms = max_over_ranks(ms_rank)
     value = world * args.steps / (ms / 1000.0)
+    per_replica = [args.steps / (ms_rank / 1000.0)]
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, per_replica[0])
+        per_replica = gathered
 
-    # end to end through the public API, as grok-simple's loop does: the
-    # step's row indices uploaded from the host every step and both splits
-    # evaluated (logits and predictions read back) every 10 steps.
-    e2e_steps = max(10, args.steps)
+    # end to end through the public API, as grok-simple's loop does
+    # (src/bin/mesh-gpt/simple.rs:571-612): one epoch of row indices uploaded
+    # from the host per full-batch step, and every 10 steps a record: both
+    # splits evaluated into page-locked logits plus the page-locked
+    # parameters, whose buffers the next record reuses.
+    e2e_steps = max(20, args.steps)
+    P = config.parameter_count()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    evals = 0
+    evals, held = 0, []
     for s in range(e2e_steps):
         b = model.upload_batches(table, idx)
         model.train_batch(table, b, 0, GROK_ROWS, opt)
         if (s + 1) % 10 == 0:
-            model.evaluate(table, valid)
+            for buf in held:
+                model.reuse(buf)
+            held = [logits for logits, _ in model.evaluate(table, valid)] + [model.pinned_parameters()]
             evals += 1
     model.check()
-    e_wall = max_over_ranks(time.perf_counter() - t0)
+    e_wall_rank = time.perf_counter() - t0
+    e_wall = max_over_ranks(e_wall_rank)
     e2e = world * e2e_steps / e_wall
-    d2h = evals * 2 * GROK_ROWS * (97 * 4 + 4) / e2e_steps
+    d2h = evals * (2 * GROK_ROWS * (97 * 4 + 4) + 4 * P) / e2e_steps
 
     if rank == 0:
         peaks = load_peaks()
@@ -649,8 +675,8 @@ def grok_main(args):
             "config": _grok_config_block(args),
             "e2e": {"value": e2e, "unit": "steps/s", "ms_per_step": 1000 * e_wall / e2e_steps,
                     "h2d_bytes_per_step": GROK_ROWS * 4, "d2h_bytes_per_step": d2h,
-                    "api": "GpuSimpleModel.upload_batches + train_batch every step, evaluate(train, valid) every "
-                           "10 steps (wall clock)"},
+                    "api": "GpuSimpleModel.upload_batches + train_batch every step; every 10 steps a record: "
+                           "evaluate(train, valid) into page-locked logits and pinned_parameters() (wall clock)"},
             "roofline": {"kernel": "whole step", "bound": "hbm", "achieved": achieved, "peak": peaks.get("hbm_gbs"),
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
                          "algorithmic_bytes_per_step": step_bytes,
@@ -660,6 +686,8 @@ def grok_main(args):
             "cpu_baseline": base,
             "gpu_launches": model.step_launches() * args.steps,
             "clocks": clock_info,
+            "per_replica_steps_per_s": per_replica,
+            "seeds": [11 + r for r in range(world)],
         }
         print(json.dumps(line), flush=True)
     del batches, table, valid

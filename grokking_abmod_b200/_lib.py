@@ -140,6 +140,8 @@ SIGNATURES = {
     "mb_simple_evaluate": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_float_p, c_u32_p]),
     "mb_simple_loss_and_gradient": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, c_u32_p, ctypes.c_size_t,
                                                    c_double_p, c_float_p, ctypes.c_size_t]),
+    "mb_host_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "mb_host_free": (ctypes.c_int, [ctypes.c_void_p]),
     "mb_simple_stream": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
     "mb_simple_check": (ctypes.c_int, [ctypes.c_void_p]),
     "mb_simple_step_launches": (ctypes.c_int, [ctypes.c_void_p, c_u32_p]),

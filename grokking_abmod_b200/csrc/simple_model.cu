@@ -41,7 +41,9 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1427,11 +1429,66 @@ struct mb_simple_table {
   uint32_t *a, *b, *t, *identity;
 };
 
+namespace mb {
+namespace simple {
+// Device index buffers kept by a model for its uploaded batches.  A batch
+// set takes a buffer from the pool and gives it back when destroyed, so the
+// per-epoch upload of the reference's training loop (one per step at full
+// batch) allocates nothing once the pool holds a buffer of that size.  The
+// pool outlives the model while batch sets still hold buffers.  Buffers are
+// only written by copies on the model's stream, in order after every step
+// that read them before.
+class IndexPool {
+ public:
+  explicit IndexPool(int device) : device_(device) {}
+  ~IndexPool() {
+    cudaSetDevice(device_);
+    for (auto& kv : free_) cudaFree(kv.second);
+  }
+  uint32_t* take(size_t count, size_t* capacity) {
+    {
+      std::lock_guard<std::mutex> lock(mu_);
+      auto it = free_.lower_bound(count);
+      if (it != free_.end() && it->first <= 2 * count + 4096) {
+        uint32_t* p = it->second;
+        *capacity = it->first;
+        free_.erase(it);
+        return p;
+      }
+    }
+    void* p = nullptr;
+    SIMPLE_CUDA(cudaMalloc(&p, count * sizeof(uint32_t)));
+    *capacity = count;
+    return static_cast<uint32_t*>(p);
+  }
+  void give(uint32_t* p, size_t capacity) {
+    std::lock_guard<std::mutex> lock(mu_);
+    free_.emplace(capacity, p);
+    while (free_.size() > 8) {  // keep a few: the largest go first
+      auto last = std::prev(free_.end());
+      cudaSetDevice(device_);
+      cudaFree(last->second);
+      free_.erase(last);
+    }
+  }
+
+ private:
+  int device_;
+  std::mutex mu_;
+  std::multimap<size_t, uint32_t*> free_;
+};
+}  // namespace simple
+}  // namespace mb
+
 struct mb_simple_batches {
   const void* owner;
   size_t count, table_rows;
-  mb::simple::DeviceBuffers mem;
-  uint32_t* idx;
+  std::shared_ptr<mb::simple::IndexPool> pool;
+  size_t capacity = 0;
+  uint32_t* idx = nullptr;
+  ~mb_simple_batches() {
+    if (idx != nullptr) pool->give(idx, capacity);
+  }
 };
 
 namespace mb {
@@ -1446,6 +1503,7 @@ class SimpleModel {
     require(device >= 0 && device < count, "CUDA device index out of range");
     SIMPLE_CUDA(cudaSetDevice(device));
     SIMPLE_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    index_pool_ = std::make_shared<IndexPool>(device);
     gemm_prepare();
     groups_ = groups(c);
     size_t off = 0;
@@ -1556,8 +1614,11 @@ class SimpleModel {
     bt->owner = this;
     bt->count = count;
     bt->table_rows = table->rows;
-    bt->idx = bt->mem.alloc<uint32_t>(count);
-    SIMPLE_CUDA(cudaMemcpy(bt->idx, idx, count * 4, cudaMemcpyHostToDevice));
+    bt->pool = index_pool_;
+    bt->idx = index_pool_->take(count, &bt->capacity);
+    // Ordered on the model's stream after every step that read a recycled
+    // buffer; the host indices may be reused as soon as this returns.
+    SIMPLE_CUDA(cudaMemcpyAsync(bt->idx, idx, count * 4, cudaMemcpyHostToDevice, stream_));
     return bt.release();
   }
 
@@ -2314,6 +2375,7 @@ class SimpleModel {
   StepScalars* scalars_;
   float beta1_power_ = 1.0f, beta2_power_ = 1.0f;
   std::vector<std::unique_ptr<Workspace>> workspaces_;
+  std::shared_ptr<IndexPool> index_pool_;
   uint32_t launches_ = 0, last_launches_ = 0;
 };
 
@@ -2445,6 +2507,23 @@ int mb_simple_upload_batches(mb_simple* model, const mb_simple_table* table, con
     need(indices, "indices");
     need(out, "out");
     *out = model->model->upload_batches(table, indices, count);
+  });
+}
+
+int mb_host_alloc(size_t bytes, void** out) {
+  return guarded([&] {
+    need(out, "out");
+    *out = nullptr;
+    mb::require(bytes >= 1, "a host buffer needs at least one byte");
+    cudaError_t e = cudaHostAlloc(out, bytes, cudaHostAllocDefault);
+    if (e != cudaSuccess) throw mb::Error(MB_ERR_CUDA, std::string("cudaHostAlloc failed: ") + cudaGetErrorString(e));
+  });
+}
+
+int mb_host_free(void* p) {
+  return guarded([&] {
+    cudaError_t e = p != nullptr ? cudaFreeHost(p) : cudaSuccess;
+    if (e != cudaSuccess) throw mb::Error(MB_ERR_CUDA, std::string("cudaFreeHost failed: ") + cudaGetErrorString(e));
   });
 }
 

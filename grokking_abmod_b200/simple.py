@@ -13,6 +13,7 @@ fallback.
 
 import ctypes
 import math
+import weakref
 from dataclasses import dataclass, replace
 
 import numpy as np
@@ -110,6 +111,18 @@ class SimpleConfig:
         return features, targets
 
 
+def pinned_empty(count: int, dtype=np.float32) -> np.ndarray:
+    """A numpy array of ``count`` elements in page-locked host memory
+    (``PinnedHostBuffer``), freed when the last view of it is gone."""
+    lib = _lib.load()
+    nbytes = max(1, int(count) * np.dtype(dtype).itemsize)
+    p = ctypes.c_void_p()
+    check(lib.mb_host_alloc(nbytes, ctypes.byref(p)))
+    raw = (ctypes.c_byte * nbytes).from_address(p.value)
+    weakref.finalize(raw, lib.mb_host_free, ctypes.c_void_p(p.value))
+    return np.frombuffer(raw, dtype=dtype, count=int(count))
+
+
 class DeviceTable:
     """Encoded rows resident on the device (``DeviceTable``)."""
 
@@ -148,6 +161,7 @@ class GpuSimpleModel:
         check(self._lib.mb_simple_create(device, ctypes.byref(c), seed, ctypes.byref(h)))
         self._h = h
         self._count = config.parameter_count()
+        self._host_buffers = []  # page-locked float32 buffers returned by reuse()
 
     def close(self):
         if getattr(self, "_h", None):
@@ -161,6 +175,25 @@ class GpuSimpleModel:
         out = np.empty(self._count, dtype=np.float32)
         check(self._lib.mb_simple_get_parameters(self._h, ptr(out, ctypes.c_float), out.size))
         return out
+
+    def _take_pinned(self, count: int) -> np.ndarray:
+        for i, b in enumerate(self._host_buffers):
+            if b.size >= count:
+                return self._host_buffers.pop(i)[:count]
+        return pinned_empty(count)
+
+    def pinned_parameters(self) -> np.ndarray:
+        """``parameters`` in page-locked memory that ``reuse`` takes back
+        (src/simple/gpu.rs:1827-1836)."""
+        out = self._take_pinned(self._count)
+        check(self._lib.mb_simple_get_parameters(self._h, ptr(out, ctypes.c_float), out.size))
+        return out
+
+    def reuse(self, buffer: np.ndarray) -> None:
+        """Takes back the page-locked logits or parameters of earlier results
+        so that later copies skip allocating them (src/simple/gpu.rs:1838-1842)."""
+        if buffer.dtype == np.float32 and buffer.flags.c_contiguous:
+            self._host_buffers.append(buffer.reshape(-1))
 
     def set_parameters(self, values):
         """Sets the weights and resets AdamW's moments and step count."""
@@ -188,7 +221,7 @@ class GpuSimpleModel:
         """(logits [rows][modulus], first-maximum predictions [rows]) per table."""
         out = []
         for table in tables:
-            logits = np.empty((table.rows, self.config.modulus), dtype=np.float32)
+            logits = self._take_pinned(table.rows * self.config.modulus).reshape(table.rows, self.config.modulus)
             preds = np.empty(table.rows, dtype=np.uint32)
             check(self._lib.mb_simple_evaluate(self._h, table._handle, ptr(logits, ctypes.c_float),
                                                ptr(preds, ctypes.c_uint32)))

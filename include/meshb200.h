@@ -313,7 +313,10 @@ int mb_simple_set_parameters(mb_simple* model, const float* values, size_t count
 int mb_simple_upload_table(mb_simple* model, const float* features, const uint32_t* targets, size_t rows,
                            mb_simple_table** out);
 int mb_simple_table_destroy(mb_simple_table* table);
-/* upload_batches (:1909-1920): host indices into the table. */
+/* upload_batches (:1909-1920): host indices into the table.  The device
+ * buffer comes from a pool the model keeps (destroying the batches returns
+ * it), and the copy is asynchronous on the model's stream, so a training
+ * loop that uploads every epoch allocates nothing after its first upload. */
 int mb_simple_upload_batches(mb_simple* model, const mb_simple_table* table, const uint32_t* indices,
                              size_t count, mb_simple_batches** out);
 int mb_simple_batches_destroy(mb_simple_batches* batches);
@@ -329,6 +332,12 @@ int mb_simple_evaluate(mb_simple* model, const mb_simple_table* table, float* lo
  * f32 logits) and every parameter gradient on the selected table rows. */
 int mb_simple_loss_and_gradient(mb_simple* model, const mb_simple_table* table, const uint32_t* indices,
                                 size_t count, double* loss, float* gradient, size_t n_gradient);
+/* Page-locked host memory (PinnedHostBuffer, src/simple/gpu.rs:1827-1842):
+ * logits, predictions and parameters copied into it cross the bus at full
+ * speed.  The host mirrors keep such buffers in a pool, as the reference's
+ * pinned_parameters / reuse do. */
+int mb_host_alloc(size_t bytes, void** ptr);
+int mb_host_free(void* ptr);
 /* Device stream, pending device errors, and kernels per train step. */
 int mb_simple_stream(mb_simple* model, void** stream);
 int mb_simple_check(mb_simple* model);

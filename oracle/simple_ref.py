@@ -415,12 +415,25 @@ def _split(config, parameters):
 class ReferenceSimpleModel:
     """f64 forward / loss / gradient of ``src/simple/reference.rs:143-448``."""
 
-    def __init__(self, config: SimpleConfig, parameters=None, seed: int = 11):
+    def __init__(self, config: SimpleConfig, parameters=None, seed: int = 11, fp32_kink: bool = False):
+        """``fp32_kink``: decide ReLU's kink (slope 1 above 0, else 0, as
+        ``simple_slope`` at src/simple/gpu.rs:62-72 and the tape's relu at
+        src/gpt/reference.rs:318-324) on the pre-activation rounded to f32,
+        as any FP32 implementation of the model does.  It matters only where
+        the f64 pre-activation is below f32's range: the shared-Neighbor
+        model's near-identity chain makes values such as 1e-50 (products of
+        its small mixing weights) that FP32 holds as exactly 0."""
+        self.fp32_kink = fp32_kink
         self.config = config.validate()
         self.parameters = (initial_parameters(config, seed) if parameters is None
                            else np.asarray(parameters, dtype=np.float32).copy())
         if self.parameters.size != config.parameter_count():
             raise ValueError("parameter count does not match the model")
+
+    def _slope(self, x):
+        if self.fp32_kink and self.config.activation == "relu":
+            return (np.asarray(x).astype(np.float32) > 0.0).astype(np.float64)
+        return _act_grad(self.config, x)
 
     # forward returns logits [rows][modulus] and a cache for the backward
     def _forward(self, features):
@@ -590,7 +603,7 @@ class ReferenceSimpleModel:
             dh = _rmsnorm_backward(s["hf"], s["invf"], dlog @ g[1].reshape(w, m).T)
         for block in reversed(range(c.depth)):
             n, inv, zs = s["blocks"][block]
-            dz = dh * _act_grad(c, zs[-1]) if c.mesh_output_activation else dh
+            dz = dh * self._slope(zs[-1]) if c.mesh_output_activation else dh
             for layer in reversed(range(md)):
                 mesh = block * md + layer
                 xin = n if layer == 0 else _act(c, zs[layer - 1])
@@ -603,7 +616,7 @@ class ReferenceSimpleModel:
                     gw[:, 1] = (dz * np.roll(xin, -st, axis=1)).sum(axis=0)
                     dx = dx + np.roll(dz * mw[:, 1], st, axis=1)
                 grads[nd + mesh] = gw.reshape(-1)
-                dz = dx * _act_grad(c, zs[layer - 1]) if layer > 0 else dx
+                dz = dx * self._slope(zs[layer - 1]) if layer > 0 else dx
             dh = dh + _rmsnorm_backward(n, inv, dz)
         if c.architecture == "tied-rotary-residual-mesh-mlp":
             perm, sign = _rotation(w)
@@ -646,7 +659,7 @@ class ReferenceSimpleModel:
             for layer in range(c.depth, 0, -1):
                 out = c.layers()[layer][1]
                 grads[layer] = (s["acts"][layer - 1].T @ dz).reshape(-1)
-                dz = (dz @ g[layer].reshape(-1, out).T) * _act_grad(c, s["zs"][layer - 1])
+                dz = (dz @ g[layer].reshape(-1, out).T) * self._slope(s["zs"][layer - 1])
             grads[0] = (s["x"].T @ dz).reshape(-1)
             return loss, np.concatenate(grads)
         if c.architecture == "residual-mlp":
@@ -659,7 +672,7 @@ class ReferenceSimpleModel:
                 down = g[2 + 2 * block].reshape(hidden, w)
                 up = g[1 + 2 * block].reshape(w, hidden)
                 grads[2 + 2 * block] = (act.T @ dh).reshape(-1)
-                de = (dh @ down.T) * _act_grad(c, e)
+                de = (dh @ down.T) * self._slope(e)
                 grads[1 + 2 * block] = (n.T @ de).reshape(-1)
                 dh = dh + _rmsnorm_backward(n, inv, de @ up.T)
             grads[0] = (s["x"].T @ dh).reshape(-1)
@@ -674,7 +687,7 @@ class ReferenceSimpleModel:
         if c.architecture == "mesh-mlp":
             readout = g[1].reshape(w, m)
             grads[1] = (s["act"].T @ dlog).reshape(-1)
-            dh = (dlog @ readout.T) * _act_grad(c, s["h"][-1])
+            dh = (dlog @ readout.T) * self._slope(s["h"][-1])
             for layer in reversed(range(c.mesh_layers())):
                 mw = g[2 + c.stored_mesh_layer(layer)].reshape(w, c.parents())
                 hin = s["h"][layer]
@@ -687,13 +700,13 @@ class ReferenceSimpleModel:
                     gw[:, 1] = (dh * np.roll(act, -st, axis=1)).sum(axis=0)
                     dact = dact + np.roll(dh * mw[:, 1], st, axis=1)
                 grads[2 + c.stored_mesh_layer(layer)] = grads[2 + c.stored_mesh_layer(layer)] + gw.reshape(-1)
-                dh = dact * _act_grad(c, hin)
+                dh = dact * self._slope(hin)
             grads[0] = (s["x"].T @ dh).reshape(-1)
             return loss, np.concatenate(grads)
         if c.architecture == "tied-concat-mesh-mlp":
             emb = s["emb"]
             demb = dlog.T @ s["act"]
-            dh = (dlog @ emb) * _act_grad(c, s["h"][-1])
+            dh = (dlog @ emb) * self._slope(s["h"][-1])
             for layer in reversed(range(c.mesh_layers())):
                 mw = g[2 + c.stored_mesh_layer(layer)].reshape(w, c.parents())
                 hin = s["h"][layer]
@@ -706,7 +719,7 @@ class ReferenceSimpleModel:
                     gw[:, 1] = (dh * np.roll(act, -st, axis=1)).sum(axis=0)
                     dact = dact + np.roll(dh * mw[:, 1], st, axis=1)
                 grads[2 + c.stored_mesh_layer(layer)] = grads[2 + c.stored_mesh_layer(layer)] + gw.reshape(-1)
-                dh = dact * _act_grad(c, hin)
+                dh = dact * self._slope(hin)
             grads[1] = (s["j"].T @ dh).reshape(-1)
             dj = dh @ g[1].reshape(2 * w, w).T
             x = s["x"]
@@ -728,7 +741,7 @@ class ReferenceSimpleModel:
                     dx = np.zeros_like(xin)
                     np.add.at(dx.T, a, (dz * p[:, 0]).T)
                     np.add.at(dx.T, b, (dz * p[:, 1]).T)
-                    dz = dx * _act_grad(c, s["zs"][index - 1])
+                    dz = dx * self._slope(s["zs"][index - 1])
             return loss, np.concatenate(grads)
         perm, sign = _rotation(w)
         x = s["x"]
@@ -738,7 +751,7 @@ class ReferenceSimpleModel:
             dh = _rmsnorm_backward(s["hf"], s["invf"], dlog @ emb)
             for block in reversed(range(c.depth)):
                 hin, n, inv, z = s["blocks"][block]
-                dz = dh * _act_grad(c, z)
+                dz = dh * self._slope(z)
                 d = g[1 + block].reshape(w, w)
                 grads[1 + block] = (n.T @ dz).reshape(-1)
                 dh = dh + _rmsnorm_backward(n, inv, dz @ d.T)
@@ -764,7 +777,7 @@ class ReferenceSimpleModel:
             hin, n, inv, z = s["blocks"][layer]
             p = core[layer]
             st = c.stride(layer)
-            dz = dh * _act_grad(c, z)
+            dz = dh * self._slope(z)
             gp = np.stack([(dz * n).sum(axis=0), (dz * np.roll(n, -st, axis=1)).sum(axis=0),
                            dz.sum(axis=0)], axis=1)
             grads[ed + layer] = gp.reshape(-1)

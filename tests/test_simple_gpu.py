@@ -273,7 +273,12 @@ def test_archived_mesh_records(case):
 def test_timed_full_batch_matches_oracle(name):
     """The bench's grok workload itself: the seed-11 p=97 division split, all
     4656 training rows in the sampler's order, the reference's seed-11
-    initial weights; loss, every gradient and one AdamW step."""
+    initial weights; loss, every gradient and one AdamW step.  The oracle
+    decides ReLU's kink on the f32-rounded pre-activation: at this init the
+    shared-Neighbor core (cfg2) sees ~11M pre-activations that are nonzero
+    in f64 but below f32's range (products of the chain's small mixing
+    weights), which FP32 holds as 0; deciding their slope in f64 moves the
+    gradient by 1e-2 of its largest entry, in the oracle alone."""
     from oracle.data import EquationSampler
     kw = FULL[["cfg0", "cfg1", "cfg2"].index(name)]
     config = SimpleConfig(**kw)
@@ -284,7 +289,7 @@ def test_timed_full_batch_matches_oracle(name):
     model = GpuSimpleModel(0, config, seed=11)
     table = model.upload_table(features, targets)
     loss, grad = model.loss_and_gradient(table, idx)
-    ref = osr.ReferenceSimpleModel(osr.SimpleConfig(**kw), seed=11)
+    ref = osr.ReferenceSimpleModel(osr.SimpleConfig(**kw), seed=11, fp32_kink=True)
     assert model.parameters().tobytes() == ref.parameters.tobytes()
     ref_loss, ref_grad = ref.loss_and_gradient(features[idx], targets[idx])
     assert abs(loss - ref_loss) <= 1e-5 * abs(ref_loss), (loss, ref_loss)

@@ -360,3 +360,30 @@ def test_full_mesh_initialization_is_seeded_and_identity_applies_only_to_hidden_
     identity = initial_parameters(config.with_(full_mesh_initialization="identity-hidden").validate(), 11)
     assert (identity[24:72].reshape(-1, 3) == [1.0, 0.0, 0.0]).all()
     assert (identity[:24].reshape(-1, 3)[:, 1] != 0).any() and (identity[72:].reshape(-1, 3)[:, 1] != 0).any()
+
+
+def test_fp32_kink_only_changes_slopes_below_f32_range():
+    """Deciding ReLU's kink on the f32-rounded pre-activation changes nothing
+    where pre-activations are ordinary numbers, and changes the gradient of
+    the shared-Neighbor model at its near-identity seed-11 init, whose core
+    sees pre-activations far below f32's range."""
+    import numpy as np
+    from oracle import simple_ref as osr
+    from oracle.data import EquationDataset
+    kw = dict(architecture="mesh-mlp", modulus=7, width=32, depth=3, connectivity="butterfly")
+    oc = osr.SimpleConfig(**kw)
+    f, t = osr.encode(oc, EquationDataset(7, "div", 0.5, 3).split(False))
+    a = osr.ReferenceSimpleModel(oc, seed=5).loss_and_gradient(f, t)
+    b = osr.ReferenceSimpleModel(oc, seed=5, fp32_kink=True).loss_and_gradient(f, t)
+    assert a[0] == b[0] and np.array_equal(a[1], b[1])
+    oc = osr.SimpleConfig(architecture="shared-neighbor-mesh-mlp", modulus=13, width=16, depth=6,
+                          embedding_mesh_depth=8, full_mesh_initialization="identity-hidden")
+    f, t = osr.encode(oc, EquationDataset(13, "div", 0.5, 3).split(False))
+    model = osr.ReferenceSimpleModel(oc, seed=11)
+    _, cache = model._forward(f)
+    z = np.array([blk[3] for blk in cache["blocks"]])
+    tiny = (z != 0) & (np.abs(z) < 1e-45)
+    a = model.loss_and_gradient(f, t)
+    b = osr.ReferenceSimpleModel(oc, seed=11, fp32_kink=True).loss_and_gradient(f, t)
+    assert a[0] == b[0]
+    assert np.array_equal(a[1], b[1]) == (not tiny.any())
