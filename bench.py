@@ -638,17 +638,26 @@ def grok_main(args):
     # parameters, whose buffers the next record reuses.
     e2e_steps = max(20, args.steps)
     P = config.parameter_count()
+    held = []
+
+    def e2e_loop(steps):
+        nonlocal held
+        records = 0
+        for s in range(steps):
+            b = model.upload_batches(table, idx)
+            model.train_batch(table, b, 0, GROK_ROWS, opt)
+            if (s + 1) % 10 == 0:
+                for buf in held:
+                    model.reuse(buf)
+                held = [logits for logits, _ in model.evaluate(table, valid)] + [model.pinned_parameters()]
+                records += 1
+        return records
+
+    e2e_loop(10)  # warm-up: the batch-buffer pool and the page-locked record buffers
+    model.check()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    evals, held = 0, []
-    for s in range(e2e_steps):
-        b = model.upload_batches(table, idx)
-        model.train_batch(table, b, 0, GROK_ROWS, opt)
-        if (s + 1) % 10 == 0:
-            for buf in held:
-                model.reuse(buf)
-            held = [logits for logits, _ in model.evaluate(table, valid)] + [model.pinned_parameters()]
-            evals += 1
+    evals = e2e_loop(e2e_steps)
     model.check()
     e_wall_rank = time.perf_counter() - t0
     e_wall = max_over_ranks(e_wall_rank)

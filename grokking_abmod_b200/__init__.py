@@ -5,9 +5,9 @@
 reference's seeded equation datasets and the benchmark token streams.
 """
 
-from .gpt import AdamWOptions, GptConfig, IGNORE_TARGET, MeshGpt, initial_parameters, nccl_unique_id, \
+from .gpt import AdamWOptions, Context, GptConfig, IGNORE_TARGET, MeshGpt, initial_parameters, nccl_unique_id, \
     parameter_count, token_codes
 from ._lib import MeshError, UnsupportedShape
 
-__all__ = ["AdamWOptions", "GptConfig", "IGNORE_TARGET", "MeshGpt", "MeshError", "UnsupportedShape",
+__all__ = ["AdamWOptions", "Context", "GptConfig", "IGNORE_TARGET", "MeshGpt", "MeshError", "UnsupportedShape",
            "initial_parameters", "nccl_unique_id", "parameter_count", "token_codes"]

@@ -106,6 +106,30 @@ SIGNATURES = {
                                                    ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32,
                                                    ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
                                                    ctypes.c_void_p]),
+    "mb_ctx_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
+    "mb_ctx_destroy": (ctypes.c_int, [ctypes.c_void_p]),
+    "mb_ctx_stream": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "mb_gpt_create_in": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(GptConfigC), ctypes.c_uint64,
+                                        ctypes.POINTER(ctypes.c_void_p)]),
+    "mb_op_rmsnorm_forward": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_size_t, ctypes.c_uint32,
+                                                                     ctypes.c_uint32, ctypes.c_void_p]),
+    "mb_op_rmsnorm_backward": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_size_t, ctypes.c_uint32,
+                                                                      ctypes.c_uint32, ctypes.c_void_p]),
+    "mb_op_rope": (ctypes.c_int, [ctypes.c_void_p] * 2 + [ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32,
+                                                         ctypes.c_uint32, ctypes.c_int, ctypes.c_void_p]),
+    "mb_op_attn_forward": (ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32,
+                                                                 ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p]),
+    "mb_op_attn_backward": (ctypes.c_int, [ctypes.c_void_p] * 9 + [ctypes.c_size_t, ctypes.c_uint32,
+                                                                  ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p,
+                                                                  ctypes.c_void_p]),
+    "mb_op_xsa_forward": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32,
+                                                                 ctypes.c_void_p]),
+    "mb_op_xsa_backward": (ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_size_t, ctypes.c_uint32,
+                                                                  ctypes.c_uint32, ctypes.c_void_p]),
+    "mb_op_head_ce": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32] +
+                      [ctypes.c_void_p] * 6),
+    "mb_op_adamw": (ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_size_t, ctypes.POINTER(AdamWC),
+                                                           ctypes.c_uint32, ctypes.c_void_p]),
     "mb_gpt_checkpoint_write": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(GptConfigC), c_u32_p, ctypes.c_size_t,
                                                c_float_p, ctypes.c_size_t]),
     "mb_gpt_checkpoint_read": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(GptConfigC), c_u32_p, c_size_p,

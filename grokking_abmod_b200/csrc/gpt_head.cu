@@ -218,6 +218,21 @@ __global__ void optimizer_set(OptimizerState* st, OptimizerState h, const int* _
   st->step += 1;
 }
 
+// One parameter's AdamW update with bias corrections c1 = 1 - beta1^t and
+// c2 = 1 - beta2^t: unfused f32 arithmetic, term by term as
+// src/bin/mesh-gpt.rs:459-466.
+__device__ __forceinline__ void adamw_element(float g, float& w, float& m, float& v, float lr, float wd, float b1,
+                                              float b2, float eps, float c1, float c2) {
+  const float mi = __fadd_rn(__fmul_rn(b1, m), __fmul_rn(__fsub_rn(1.0f, b1), g));
+  const float vi = __fadd_rn(__fmul_rn(b2, v), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, b2), g), g));
+  m = mi;
+  v = vi;
+  const float mh = __fdiv_rn(mi, c1);
+  const float vh = __fdiv_rn(vi, c2);
+  const float step = __fadd_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), __fmul_rn(wd, w));
+  w = __fsub_rn(w, __fmul_rn(lr, step));
+}
+
 __global__ void adamw(int n, const OptimizerState* __restrict__ st, const float* __restrict__ grad,
                       float* __restrict__ w, float* __restrict__ m, float* __restrict__ v,
                       const int* __restrict__ step_flags) {
@@ -225,16 +240,11 @@ __global__ void adamw(int n, const OptimizerState* __restrict__ st, const float*
   const float lr = st->learning_rate, wd = st->weight_decay, b1 = st->beta1, b2 = st->beta2, eps = st->epsilon;
   const float c1 = __fsub_rn(1.0f, st->beta1_power), c2 = __fsub_rn(1.0f, st->beta2_power);
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const float g = grad[i];
-    // Unfused f32 arithmetic, term by term as src/bin/mesh-gpt.rs:459-466.
-    const float mi = __fadd_rn(__fmul_rn(b1, m[i]), __fmul_rn(__fsub_rn(1.0f, b1), g));
-    const float vi = __fadd_rn(__fmul_rn(b2, v[i]), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, b2), g), g));
+    float wi = w[i], mi = m[i], vi = v[i];
+    adamw_element(grad[i], wi, mi, vi, lr, wd, b1, b2, eps, c1, c2);
+    w[i] = wi;
     m[i] = mi;
     v[i] = vi;
-    const float mh = __fdiv_rn(mi, c1);
-    const float vh = __fdiv_rn(vi, c2);
-    const float step = __fadd_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), __fmul_rn(wd, w[i]));
-    w[i] = __fsub_rn(w[i], __fmul_rn(lr, step));
   }
 }
 

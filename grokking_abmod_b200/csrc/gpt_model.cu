@@ -177,6 +177,9 @@ struct AttentionOps {
   virtual int backward_launches() const { return 2; }
   float* scratch = nullptr;
   int layer = 0;
+  // Lays out the key operand tiles that forward and dQ read (tensor-core
+  // kernels only); forward does it itself.
+  virtual void prepare_keys(cudaStream_t s, int rows, int W, int H, const float* k, const float* v) {}
   virtual void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                        const float* v, float* o, float* lse) = 0;
   virtual void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q,
@@ -244,10 +247,13 @@ struct AttentionOpsTc final : AttentionOps {
   int backward_launches() const override { return 3; }  // query format + dK/dV, dQ
   float* qfmt() const { return scratch; }
   float* kfmt(int rows, int H) const { return scratch + query_floats(rows, H) + (size_t)layer * key_floats(rows, H); }
-  void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
-               const float* v, float* o, float* lse) override {
+  void prepare_keys(cudaStream_t s, int rows, int W, int H, const float* k, const float* v) override {
     attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), kFmtThreads, 0, s>>>(
         rows, W, k, v, kfmt(rows, H), (1u << F::K_HI) | (1u << F::VT_HI) | (1u << F::V_HI) | (1u << F::KT_HI));
+  }
+  void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
+               const float* v, float* o, float* lse) override {
+    prepare_keys(s, rows, W, H, k, v);
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
     attention_forward_tc<HD><<<grid, kTcThreads2, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
                                                                         kfmt(rows, H), o, lse, err);
@@ -354,7 +360,10 @@ struct Workspace {
 // --------------------------------------------------------------------- model
 class GptModel {
  public:
-  GptModel(int device, const mb_gpt_config& cfg, uint64_t seed) : cfg_(cfg), device_(device) {
+  // shared: a stream the caller owns (a context's), used instead of the
+  // model's own.
+  GptModel(int device, const mb_gpt_config& cfg, uint64_t seed, cudaStream_t shared = nullptr)
+      : cfg_(cfg), device_(device) {
     validate_kernel_shapes(cfg);
     layout_ = make_layout(cfg);
     int count = 0;
@@ -365,7 +374,12 @@ class GptModel {
     MB_CUDA(cudaGetDeviceProperties(&prop, device));
     require(prop.major >= 10, "this library is built for sm_100a (B200)", MB_ERR_UNSUPPORTED);
     sms_ = prop.multiProcessorCount;
-    MB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    if (shared != nullptr) {
+      stream_ = shared;
+    } else {
+      MB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+      owns_stream_ = true;
+    }
     blocks_ = make_block_ops(cfg.width, cfg.attention_mesh_depth, cfg.ffn_mesh_depth, (int)cfg.connectivity);
     tc_err_ = mem_.alloc<int>(1);
     MB_CUDA(cudaMemset(tc_err_, 0, sizeof(int)));
@@ -389,7 +403,7 @@ class GptModel {
     workspaces_.clear();
     for (cudaEvent_t e : opt_marks_) cudaEventDestroy(e);
     detach_nccl();
-    if (stream_) cudaStreamDestroy(stream_);
+    if (stream_ && owns_stream_) cudaStreamDestroy(stream_);
   }
 
   const mb_gpt_config& config() const { return cfg_; }
@@ -948,6 +962,7 @@ class GptModel {
   int device_ = 0, sms_ = 1;
   Layout layout_;
   cudaStream_t stream_ = nullptr;
+  bool owns_stream_ = false;
   DeviceArena mem_;
   std::unique_ptr<BlockOps> blocks_;
   std::unique_ptr<AttentionOps> attention_;
@@ -984,6 +999,13 @@ using mb::Error;
 
 struct mb_gpt {
   std::unique_ptr<mb::GptModel> model;
+};
+
+// A device and one stream that models created in it share
+// (mb_ctx_create; src/gpt/gpu.rs:1718-1736 takes an Arc<CudaContext>).
+struct mb_ctx {
+  int device;
+  cudaStream_t stream;
 };
 
 namespace {
@@ -1074,6 +1096,51 @@ int mb_gpt_create(int device, const mb_gpt_config* c, uint64_t seed, mb_gpt** ou
     *out = nullptr;
     auto h = std::make_unique<mb_gpt>();
     h->model = std::make_unique<mb::GptModel>(device, *c, seed);
+    *out = h.release();
+  });
+}
+
+int mb_ctx_create(int device, mb_ctx** out) {
+  return guarded([&] {
+    need(out, "context");
+    *out = nullptr;
+    int count = 0;
+    MB_CUDA(cudaGetDeviceCount(&count));
+    mb::require(device >= 0 && device < count, "CUDA device index out of range");
+    MB_CUDA(cudaSetDevice(device));
+    auto c = std::make_unique<mb_ctx>();
+    c->device = device;
+    MB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    *out = c.release();
+  });
+}
+
+int mb_ctx_destroy(mb_ctx* ctx) {
+  return guarded([&] {
+    if (ctx == nullptr) return;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+  });
+}
+
+int mb_ctx_stream(mb_ctx* ctx, void** stream) {
+  return guarded([&] {
+    need(ctx, "context");
+    need(stream, "stream");
+    *stream = (void*)ctx->stream;
+  });
+}
+
+int mb_gpt_create_in(mb_ctx* ctx, const mb_gpt_config* c, uint64_t seed, mb_gpt** out) {
+  return guarded([&] {
+    need(ctx, "context");
+    need(c, "config");
+    need(out, "model");
+    *out = nullptr;
+    auto h = std::make_unique<mb_gpt>();
+    h->model = std::make_unique<mb::GptModel>(ctx->device, *c, seed, ctx->stream);
     *out = h.release();
   });
 }
@@ -1303,3 +1370,5 @@ int mb_zipf_batch(uint64_t base_seed, uint32_t rank, uint64_t step, size_t seque
 }
 
 }  // extern "C"
+
+#include "gpt_ops.cu"

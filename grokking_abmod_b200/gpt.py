@@ -98,6 +98,35 @@ def _u32(a) -> np.ndarray:
     return arr.astype(np.uint32)
 
 
+class Context:
+    """A CUDA device and one stream that the models built in it share (the
+    reference's ``Arc<CudaContext>``).  Close the models before the context."""
+
+    def __init__(self, device: int):
+        self._lib = _lib.load()
+        h = ctypes.c_void_p()
+        check(self._lib.mb_ctx_create(device, ctypes.byref(h)))
+        self._h = h
+        self.device = device
+
+    @property
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        check(self._lib.mb_ctx_stream(self._h, ctypes.byref(s)))
+        return s.value or 0
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self._lib.mb_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class MeshGpt:
     """``SpecializedMeshGpt``: a Mesh GPT on one CUDA device.
 
@@ -105,12 +134,18 @@ class MeshGpt:
     and AdamW on the GPU.  Repeated ``train_batch`` calls continue the same
     AdamW state; ``set_parameters`` resets it."""
 
-    def __init__(self, device: int, config: GptConfig, seed: int):
+    def __init__(self, device, config: GptConfig, seed: int):
+        """``device``: a CUDA device index, or a ``Context`` whose device and
+        stream the model then uses."""
         self._lib = _lib.load()
         self.config = config
         self._c = config.to_c()
         handle = ctypes.c_void_p()
-        check(self._lib.mb_gpt_create(device, ctypes.byref(self._c), seed, ctypes.byref(handle)))
+        if isinstance(device, Context):
+            self._context = device  # kept alive while the model uses its stream
+            check(self._lib.mb_gpt_create_in(device._h, ctypes.byref(self._c), seed, ctypes.byref(handle)))
+        else:
+            check(self._lib.mb_gpt_create(device, ctypes.byref(self._c), seed, ctypes.byref(handle)))
         self._h = handle
         self._count = parameter_count(config)
 

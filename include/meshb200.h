@@ -68,6 +68,7 @@ typedef struct mb_adamw {
 } mb_adamw;
 
 typedef struct mb_gpt mb_gpt; /* opaque model handle */
+typedef struct mb_ctx mb_ctx; /* a device and the stream its models share */
 
 /* Copies the calling thread's last error message (NUL-terminated, truncated
  * to len) and returns its status code. */
@@ -88,8 +89,19 @@ int mb_gpt_initial_parameters(const mb_gpt_config* config, uint64_t seed, float*
 /* token_codes (src/gpt/config.rs:552-591); out: host, vocab*width floats. */
 int mb_gpt_token_codes(const mb_gpt_config* config, float* out, size_t count);
 
+/* ---- context: the Arc<CudaContext> + default stream a SpecializedMeshGpt
+ * is built on (src/gpt/gpu.rs:1718-1736).  mb_ctx_create selects the device
+ * and creates one non-blocking stream; models made with mb_gpt_create_in
+ * enqueue all their work on it.  Destroy those models before the context. */
+int mb_ctx_create(int device, mb_ctx** ctx);
+int mb_ctx_destroy(mb_ctx* ctx);
+int mb_ctx_stream(mb_ctx* ctx, void** stream);
+
 /* ---- model (SpecializedMeshGpt, src/gpt/gpu.rs:1701-2092) ---- */
+/* SpecializedMeshGpt::new (:1718-1806) on its own device and stream. */
 int mb_gpt_create(int device, const mb_gpt_config* config, uint64_t seed, mb_gpt** model);
+/* The same on a context's device and stream. */
+int mb_gpt_create_in(mb_ctx* ctx, const mb_gpt_config* config, uint64_t seed, mb_gpt** model);
 int mb_gpt_destroy(mb_gpt* model);
 int mb_gpt_get_config(const mb_gpt* model, mb_gpt_config* config);
 /* parameters() (:1846-1853); out: host. */
@@ -176,15 +188,83 @@ int mb_op_mesh_backward(const float* x, const float* dy, float* dx, float* dweig
                         uint32_t width, uint32_t depth, uint32_t connectivity, const float* weights,
                         void* stream);
 
-/* C[m][n] = A[m][k] . op(B) in FP32 on the tcgen05 tensor cores with the
+/* C[m][n] = op(A) . op(B) in FP32 on the tcgen05 tensor cores with the
  * 3xTF32 split (hi.hi + hi.lo + lo.hi), the dense contraction of the
  * reference's FP32 blocked_product GEMMs (src/simple/dense_tiled.rs:161-232).
- * layout 0: B is [n][k] (C = A B^T); 1: B is [k][n] (C = A B, transposed
- * while staged); 2: the same as 0 (A is always staged through tensor
- * memory, the A-from-TMEM MMA form).  All row-major FP32 device arrays.  d_status (device
- * int) is set to 1 if a tensor-core completion wait gave up. */
+ * layout is a set of bit flags: 1 = B stored [k][n] (C = A B; otherwise B is
+ * [n][k] and C = A B^T); 4 = A stored [k][m] (otherwise [m][k]); 2 is
+ * accepted and changes nothing (A always goes through tensor memory, the
+ * A-from-TMEM MMA form) but may not be combined with 4.  Valid layouts:
+ * 0-5.  All row-major FP32 device arrays.  d_status (device int) is set to
+ * 1 if a tensor-core completion wait gave up. */
 int mb_op_gemm_tf32x3(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k, uint32_t layout,
                       int* d_status, void* stream);
+
+/* ---- per-op entry points of the Mesh GPT operators (device pointers, the
+ * caller's stream, validation on the host before any launch).  The training
+ * step runs the same arithmetic fused into its own kernels; these serve
+ * callers that compose the model themselves and per-op tests.  rows x width
+ * row-major FP32 arrays; heads divides width (head width hd = width/heads);
+ * head h owns channels [h*hd, (h+1)*hd) of each row. */
+/* Parameter-free RMSNorm per (row, head), eps 1e-5: y = x / rms(x); inv
+ * [rows][heads] receives 1/rms (may be NULL); heads = 1 is the full-row norm
+ * (gpt_rmsnorm_statistics + gpt_rmsnorm_apply, src/gpt/gpu.rs:65-94,
+ * :1035-1077).  y may equal x. */
+int mb_op_rmsnorm_forward(const float* x, float* y, float* inv, size_t rows, uint32_t width, uint32_t heads,
+                          void* stream);
+/* Its backward from the input x: dx = inv (dy - n mean(dy n)), n = x inv
+ * (statistics recomputed from x, as the reference's backward does). */
+int mb_op_rmsnorm_backward(const float* x, const float* dy, float* dx, size_t rows, uint32_t width,
+                           uint32_t heads, void* stream);
+/* Slice RoPE (gpt_rope, src/gpt/gpu.rs:175-208): per head, channels i and
+ * i + hd/2 rotate by pos / 10000^(i/(hd/2)), pos = row mod sequence; inverse
+ * != 0 rotates back (the backward).  hd even; y may equal x. */
+int mb_op_rope(const float* x, float* y, size_t rows, uint32_t sequence, uint32_t width, uint32_t heads,
+               int inverse, void* stream);
+/* Causal softmax(Q K^T / sqrt(hd)) V per head over sequences of `sequence`
+ * rows (diagonal included), the FA2 forward of src/gpt/gpu.rs:381-498,
+ * :752-779.  lse: device [heads][rows], each row's base-2 log-sum-exp of
+ * its scaled scores times log2(e).  Head widths 32 and 64 run on the tcgen05
+ * tensor cores (3xTF32), 2..16 on FP32 SIMT; others MB_ERR_UNSUPPORTED.
+ * Q, K, V, O 16-byte aligned, width a multiple of 4.  Scratch for the
+ * formatted key tiles comes from cudaMallocAsync on `stream`.  d_status
+ * (device int) is set to 1 if a tensor-core wait gave up. */
+int mb_op_attn_forward(const float* q, const float* k, const float* v, float* o, float* lse, size_t rows,
+                       uint32_t sequence, uint32_t width, uint32_t heads, int* d_status, void* stream);
+/* Its backward from dO, O and the forward's lse: dQ, dK, dV
+ * (gpt_flash_delta, gpt_flash_query_gradient, gpt_flash_key_value_gradient,
+ * src/gpt/gpu.rs:500-750).  Same shapes, limits and status as the forward. */
+int mb_op_attn_backward(const float* q, const float* k, const float* v, const float* o, const float* dout,
+                        const float* lse, float* dq, float* dk, float* dv, size_t rows, uint32_t sequence,
+                        uint32_t width, uint32_t heads, int* d_status, void* stream);
+/* Exclusive self-attention (exclusive_terms, gpt_exclusive,
+ * src/gpt/gpu.rs:781-853): z = y - (y.u)u per head, u = v / max(|v|, 1e-12). */
+int mb_op_xsa_forward(const float* y, const float* v, float* z, size_t rows, uint32_t width, uint32_t heads,
+                      void* stream);
+/* Its backward (gpt_exclusive_backward, :861-897): dy and dv from dz; the
+ * norm's gradient is taken only above the 1e-12 floor. */
+int mb_op_xsa_backward(const float* y, const float* v, const float* dz, float* dy, float* dv, size_t rows,
+                       uint32_t width, uint32_t heads, void* stream);
+/* The tied head and cross-entropy (gpt_head, gpt_cross_entropy,
+ * gpt_head_backward, src/gpt/gpu.rs:927-1021): logits = RMSNorm(h) E^T
+ * ([rows][vocab], E = embeddings [vocab][width]); *loss (device double) =
+ * mean cross-entropy over the rows whose target is not MB_IGNORE_TARGET;
+ * dh (may be NULL) = its gradient with respect to h; dembeddings (may be
+ * NULL) = the head's contribution to dE, [vocab][width].  targets: device
+ * [rows].  d_status (device int) becomes nonzero on failure: 1 a tensor-core
+ * wait gave up, 2 a target outside the vocabulary, 4 no supervised row.
+ * h and dh 16-byte aligned, width a multiple of 4.  Scratch from
+ * cudaMallocAsync on `stream`. */
+int mb_op_head_ce(const float* h, const float* embeddings, const uint32_t* targets, size_t rows, uint32_t width,
+                  uint32_t vocab, float* logits, double* loss, float* dh, float* dembeddings, int* d_status,
+                  void* stream);
+/* AdamW with decoupled decay over a flat buffer (gpt_adam,
+ * src/gpt/gpu.rs:1369-1391): the update number `step` (>= 1) gives the bias
+ * corrections 1 - beta^step with beta^step accumulated in f32 one factor per
+ * update, as the reference's host does (:1980-1981).  Updates weights, m and
+ * v in place. */
+int mb_op_adamw(float* weights, float* m, float* v, const float* gradient, size_t count, const mb_adamw* options,
+                uint32_t step, void* stream);
 
 /* The same mesh stack backward without any allocation (no reference
  * counterpart: the reference always allocates its workspace).  For callers

@@ -273,12 +273,16 @@ def test_archived_mesh_records(case):
 def test_timed_full_batch_matches_oracle(name):
     """The bench's grok workload itself: the seed-11 p=97 division split, all
     4656 training rows in the sampler's order, the reference's seed-11
-    initial weights; loss, every gradient and one AdamW step.  The oracle
-    decides ReLU's kink on the f32-rounded pre-activation: at this init the
-    shared-Neighbor core (cfg2) sees ~11M pre-activations that are nonzero
-    in f64 but below f32's range (products of the chain's small mixing
-    weights), which FP32 holds as 0; deciding their slope in f64 moves the
-    gradient by 1e-2 of its largest entry, in the oracle alone."""
+    initial weights; loss, every gradient and one AdamW step.
+
+    At this init the shared-Neighbor core (cfg2) sees ~11M pre-activations
+    that are nonzero in f64 but at or below f32's smallest magnitudes
+    (products of the chain's small mixing weights), so ReLU's kink there is
+    decided by how an implementation rounds, not by the model: deciding it in
+    f64 or on the f32-rounded value moves some gradients by up to 1e-2 of the
+    largest.  The oracle decides it in f32, and each parameter may also
+    differ by the spread between the two conventions (zero for every
+    parameter of cfg0 and cfg1, above the tolerance for 3.6% of cfg2's)."""
     from oracle.data import EquationSampler
     kw = FULL[["cfg0", "cfg1", "cfg2"].index(name)]
     config = SimpleConfig(**kw)
@@ -292,8 +296,14 @@ def test_timed_full_batch_matches_oracle(name):
     ref = osr.ReferenceSimpleModel(osr.SimpleConfig(**kw), seed=11, fp32_kink=True)
     assert model.parameters().tobytes() == ref.parameters.tobytes()
     ref_loss, ref_grad = ref.loss_and_gradient(features[idx], targets[idx])
+    _, f64_grad = osr.ReferenceSimpleModel(osr.SimpleConfig(**kw), seed=11).loss_and_gradient(features[idx],
+                                                                                             targets[idx])
+    spread = np.abs(ref_grad - f64_grad)
+    # the kink-decided gradients: 3.6% of cfg2's parameters beyond the tolerance, none elsewhere
+    assert np.mean(spread > 1e-4 * np.abs(ref_grad).max()) < (0.05 if name == "cfg2" else 1e-12)
     assert abs(loss - ref_loss) <= 1e-5 * abs(ref_loss), (loss, ref_loss)
-    assert _max_rel(grad, ref_grad) <= 1e-4, _max_rel(grad, ref_grad)
+    tol = 1e-4 * np.abs(ref_grad).max() + spread
+    assert np.all(np.abs(grad - ref_grad) <= tol), np.abs(grad - ref_grad).max() / np.abs(ref_grad).max()
     wd = GROK[name]["optimizer"]["weight_decay"]
     opt = AdamWOptions(learning_rate=1e-3, weight_decay=wd, beta1=0.9, beta2=0.98)
     params = model.parameters()
@@ -312,7 +322,7 @@ def test_timed_full_batch_matches_oracle(name):
         want[sel] = ws
     # The first AdamW step moves a weight by lr * g / (|g| + eps): a gradient
     # error d changes it by at most lr * min(2, 2 d / |g|).
-    d = 1e-4 * np.abs(ref_grad).max()
+    d = tol
     bound = opt.learning_rate * scales * np.minimum(2.0, 2.0 * d / np.maximum(np.abs(ref_grad), 1e-30)) \
         + 1e-6 * (1 + np.abs(want))
     err = np.abs(got.astype(np.float64) - want)
