@@ -1,0 +1,668 @@
+// Causal flash attention on the sm_100a tensor cores with three-term FP16
+// products (tcgen05 kind::f16, "3xF16"; tc05.cuh): the same semantics and
+// statistics as gpt_attention_tc.cu's 3xTF32 kernels (the reference's FA2
+// kernels, src/gpt/gpu.rs:381-750) at twice the MMA rate and half the
+// operand bytes.
+//
+// Scaling.  FP16 holds magnitudes in [2^-24, 65504], so every operand is
+// scaled by a power of two before it is split, and the scale is divided out
+// of the FP32 result exactly:
+//  * Q: per query row (the thread that owns the row splits it into TMEM);
+//  * K and V: per 64-key tile, chosen by the format pass and stored in the
+//    tile's header; a score is S_tmem / (s_q(row) s_k(tile));
+//  * P (the unnormalised probabilities, at most 2^8 under the lazy rescale)
+//    is stored as P c_j with c_j = C / s_v(j), C = 2^7 min_j s_v(j) over the
+//    CTA's key tiles, so every step's P.V product carries the same factor C
+//    and O = O_tmem / (C L).  c_j <= 2^7 keeps P c_j <= 2^15; a tile whose
+//    values are smaller than the largest by more than 2^7 has c_j < 1, which
+//    costs precision only in products far below the accumulated magnitude.
+
+namespace mb {
+
+// Inside a role loop: a wait that gives up marks the CTA failed and leaves.
+#define F16_WAIT_OR_FAIL(bar, parity)    \
+  if (!tc::bar_wait((bar), (parity))) {  \
+    sh.failed = 1;                       \
+    break;                               \
+  }
+
+template <int HD>
+struct F16Fmt {
+  static constexpr int PART_BYTES = kTcK * HD * 2;  // one 64 x HD FP16 part
+  static constexpr int HEADER_BYTES = 128;          // scales (and room to keep tiles 128-byte aligned)
+  static constexpr int KTILE_BYTES = 8 * PART_BYTES + HEADER_BYTES;
+  // parts: K, K', Vt, Vt', V, V', Kt, Kt' (TcFmt's order); header floats:
+  // s_k, s_v, the largest row norm of V, the largest |V|
+  static constexpr int K_HI = 0, VT_HI = 2, V_HI = 4, KT_HI = 6;
+};
+
+constexpr int kMaxKeyTiles = 72;  // key tiles one query CTA visits: (4096 + 128) / 64 + 2
+
+// Writes the FP16 hi/lo parts p, p + 1 of one operand tile in the blocked
+// K-major layout from a shared-memory copy x ([R][HD], row stride HD + 2),
+// scaled by `scale`; `transposed` writes x^T ([HD rows][R columns]).  Each
+// thread writes whole 16-byte core-matrix rows, contiguous across a warp.
+template <int R, int HD>
+__device__ __forceinline__ void store_parts16(uint8_t* __restrict__ tile, int p, bool transposed, const float* x,
+                                              float scale) {
+  constexpr int XS = HD + 2, PB = F16Fmt<HD>::PART_BYTES;
+  const int cols = transposed ? R : HD;
+  uint4* hi = reinterpret_cast<uint4*>(tile + (size_t)p * PB);
+  uint4* lo = reinterpret_cast<uint4*>(tile + (size_t)(p + 1) * PB);
+  for (int q = threadIdx.x; q < R * HD / 8; q += kFmtThreads) {
+    const int rl = q & 7, c8 = (q >> 3) % (cols / 8), rg = (q >> 3) / (cols / 8);
+    const int r = rg * 8 + rl, c = c8 * 8;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = (transposed ? x[(c + e) * XS + r] : x[r * XS + c + e]) * scale;
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) tc::split_f16x2(v[2 * e], v[2 * e + 1], h[e], l[e]);
+    hi[q] = make_uint4(h[0], h[1], h[2], h[3]);
+    lo[q] = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// Key tiles of K and V in FP16 parts with their scales: grid
+// (ceil(rows/64), H), kFmtThreads threads.  `parts` is a bit mask over the
+// hi parts (K_HI, VT_HI, V_HI, KT_HI): only the parts later kernels read are
+// written; the header always is.
+template <int HD>
+__global__ void __launch_bounds__(kFmtThreads) attention_format_keys_f16(int rows, int W, const float* __restrict__ k,
+                                                                   const float* __restrict__ v,
+                                                                   uint8_t* __restrict__ fmt, unsigned parts) {
+  using F = F16Fmt<HD>;
+  constexpr int XS = HD + 2, NW = kFmtThreads / 32;
+  __shared__ float xk[kTcK * XS], xv[kTcK * XS];
+  __shared__ float red[3][NW];
+  const int t = blockIdx.x, h = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint8_t* tile = fmt + ((size_t)h * gridDim.x + t) * F::KTILE_BYTES;
+  load_rows2<kTcK, HD>(xk, k, xv, v, t * kTcK, rows, W, h);
+  __syncthreads();
+  float mk = 0.f, mv = 0.f, nv = 0.f;
+  for (int i = threadIdx.x; i < kTcK * HD; i += kFmtThreads) {
+    const int r = i / HD, c = i % HD;
+    mk = fmaxf(mk, fabsf(xk[r * XS + c]));
+    mv = fmaxf(mv, fabsf(xv[r * XS + c]));
+  }
+  if (threadIdx.x < kTcK) {
+    float s = 0.f;
+    for (int c = 0; c < HD; ++c) s += xv[threadIdx.x * XS + c] * xv[threadIdx.x * XS + c];
+    nv = sqrtf(s);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+    mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, o));
+    nv = fmaxf(nv, __shfl_xor_sync(0xffffffffu, nv, o));
+  }
+  if (lane == 0) {
+    red[0][warp] = mk;
+    red[1][warp] = mv;
+    red[2][warp] = nv;
+  }
+  __syncthreads();
+  mk = mv = nv = 0.f;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    mk = fmaxf(mk, red[0][w]);
+    mv = fmaxf(mv, red[1][w]);
+    nv = fmaxf(nv, red[2][w]);
+  }
+  const float sk = tc::f16_scale(mk), sv = tc::f16_scale(mv);
+  if (parts & (1u << F::K_HI)) store_parts16<kTcK, HD>(tile, F::K_HI, false, xk, sk);
+  if (parts & (1u << F::VT_HI)) store_parts16<kTcK, HD>(tile, F::VT_HI, true, xv, sv);
+  if (parts & (1u << F::V_HI)) store_parts16<kTcK, HD>(tile, F::V_HI, false, xv, sv);
+  if (parts & (1u << F::KT_HI)) store_parts16<kTcK, HD>(tile, F::KT_HI, true, xk, sk);
+  if (threadIdx.x == 0)
+    *reinterpret_cast<float4*>(tile + 8 * F::PART_BYTES) = make_float4(sk, sv, nv, mv);
+}
+
+// This thread's row (HD floats) of head h split into FP16 hi/lo TMEM columns
+// (HD / 2 packed columns each) with a per-row scale, which it returns.
+template <int HD>
+__device__ __forceinline__ float row_to_tmem16(const float* __restrict__ g, int row, int rows, int W, int h,
+                                               uint32_t thi, uint32_t tlo) {
+  float x[HD];
+#pragma unroll
+  for (int c = 0; c < HD; c += 4) {
+    const float4 v = row < rows ? __ldg(reinterpret_cast<const float4*>(g + (size_t)row * W + h * HD + c))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+    x[c] = v.x, x[c + 1] = v.y, x[c + 2] = v.z, x[c + 3] = v.w;
+  }
+  float m = 0.f;
+#pragma unroll
+  for (int c = 0; c < HD; ++c) m = fmaxf(m, fabsf(x[c]));
+  const float s = tc::f16_scale(m);
+#pragma unroll
+  for (int c = 0; c < HD; c += 32) {
+    uint32_t hi[16], lo[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) tc::split_f16x2(x[c + 2 * e] * s, x[c + 2 * e + 1] * s, hi[e], lo[e]);
+    tc::tmem_st16u(thi + c / 2, hi);
+    tc::tmem_st16u(tlo + c / 2, lo);
+  }
+  return s;
+}
+
+// D (+)= A . B^T with A = FP16 hi/lo TMEM columns and B a K-major FP16 hi/lo
+// shared tile with KC columns, over K steps [s0, s0 + NSTEP) of 16 elements:
+// three MMAs per step.
+template <int KC, int NSTEP>
+__device__ __forceinline__ void mma16_tmem_a(uint32_t d, uint32_t ah, uint32_t al, const void* bh, const void* bl,
+                                             uint32_t idesc, bool accumulate, int s0) {
+#pragma unroll
+  for (int i = 0; i < NSTEP; ++i) {
+    const int s = s0 + i;
+    const uint64_t b_h = tc::desc_kmajor16(bh, KC, s), b_l = tc::desc_kmajor16(bl, KC, s);
+    tc::mma_ts_f16(d, ah + 8 * s, b_h, idesc, (accumulate || i > 0) ? 1u : 0u);
+    tc::mma_ts_f16(d, ah + 8 * s, b_l, idesc, 1u);
+    tc::mma_ts_f16(d, al + 8 * s, b_h, idesc, 1u);
+  }
+}
+
+// NC values scaled by `scale`, split into FP16 hi/lo pairs and stored to
+// NC / 2 packed TMEM columns each.
+template <int NC>
+__device__ __forceinline__ void tc_st_split16(uint32_t thi, uint32_t tlo, const float* v, float scale) {
+#pragma unroll
+  for (int c = 0; c < NC; c += 32) {
+    uint32_t hi[16], lo[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) tc::split_f16x2(v[c + 2 * e] * scale, v[c + 2 * e + 1] * scale, hi[e], lo[e]);
+    tc::tmem_st16u(thi + c / 2, hi);
+    tc::tmem_st16u(tlo + c / 2, lo);
+  }
+}
+
+template <int HD>
+struct F16Att {
+  using F = F16Fmt<HD>;
+  static constexpr int FWD_STAGES = 4;
+  static constexpr int FWD_STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', Vt, Vt'
+  static constexpr size_t smem_forward = (size_t)FWD_STAGES * FWD_STAGE_BYTES;
+};
+
+// ------------------------------------------------------------------ forward
+// Roles as attention_forward_tc: threads 0-255 compute (row = tid % 128 =
+// TMEM lane, half = tid / 128 takes keys [32 half, 32 half + 32) of each
+// 64-key step with its own online-softmax stream and O accumulator), thread
+// 256 streams key tiles, thread 288 issues S = Q K^T and thread 320 P.V.
+// S and P are double-buffered (buffer j & 1 for step j): the softmax of step
+// j + 1 runs while P.V of step j executes, and writing P waits only for P.V
+// of step j - 1 to have read that buffer (o_done[b], one commit per step).
+// A lazy O rescale at step j waits for P.V of step j - 1, so O is stable.
+// TMEM columns: Q hi | Q lo (32 each) | S0 | S1 (64 each) | P0 hi | P0 lo |
+// P1 hi | P1 lo (32 each) | O0 | O1 (64 each) = 448.
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads2, 1)
+    attention_forward_f16(int rows, int W, int T, float scale, const float* __restrict__ q,
+                          const uint8_t* __restrict__ kfmt, float* __restrict__ o, float* __restrict__ lse2,
+                          int* __restrict__ err) {
+  using A = F16Att<HD>;
+  using F = F16Fmt<HD>;
+  constexpr int NS = A::FWD_STAGES;
+  extern __shared__ __align__(128) uint8_t sm8[];
+  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full[2], s_empty[2], p_full[2], o_done[2];
+  __shared__ TcShared sh;
+  __shared__ float xm[2][kTcRows], xl[2][kTcRows], qscale[kTcRows];
+  __shared__ float2 tscale[kMaxKeyTiles];  // (s_k, s_v) of each visited key tile
+  __shared__ float vmin;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int nt = (rows + kTcRows - 1) / kTcRows;
+  const int q0 = tile_by_work(blockIdx.x, nt, rows, T, true) * kTcRows;
+  const int h = blockIdx.y;
+  const int nkt = (rows + kTcK - 1) / kTcK;
+  const int kbeg = ((q0 - q0 % T) / kTcK) * kTcK;  // 64-aligned start of the first sequence
+  const int kend = min(rows, q0 + kTcRows);
+  const int n = (kend - kbeg + kTcK - 1) / kTcK;
+  const int kt0 = kbeg / kTcK;
+  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
+  if (tid == 0) {
+    for (int b = 0; b < NS; ++b) {
+      tc::bar_init(&kv_full[b], 1);
+      tc::bar_init(&kv_empty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::bar_init(&s_full[b], 1);
+      tc::bar_init(&s_empty[b], kTcCompute);
+      tc::bar_init(&p_full[b], kTcCompute);
+      tc::bar_init(&o_done[b], 1);
+    }
+    tc::bar_init_fence();
+    sh.failed = 0;
+  }
+  if (warp == 8) {
+    // the scales of the CTA's key tiles, and the smallest V scale
+    float mn = INFINITY;
+    for (int j = threadIdx.x & 31; j < n; j += 32) {
+      const float4 hd4 = __ldg(reinterpret_cast<const float4*>(kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES +
+                                                               8 * F::PART_BYTES));
+      tscale[j] = make_float2(hd4.x, hd4.y);
+      mn = fminf(mn, hd4.y);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+    if ((threadIdx.x & 31) == 0) vmin = mn;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t t0 = sh.tmem_base;
+  // P buffer b: hi at tP + 64 b, lo at tP + 64 b + 32
+  const uint32_t tQh = t0, tQl = t0 + 32, tS = t0 + 64, tP = t0 + 192, tO = t0 + 320;
+  if (warp < 4) {
+    const uint32_t lane = (uint32_t)(warp * 32) << 16;
+    qscale[tid] = row_to_tmem16<HD>(q, q0 + tid, rows, W, h, tQh + lane, tQl + lane);
+    tc::tmem_st_wait();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const float pv_c = 128.0f * vmin;  // C: every step's P.V carries this factor
+
+  if (tid < kTcCompute) {
+    // ---------------------------------------------------------- softmax
+    const int row = tid & (kTcRows - 1), half = tid >> 7;
+    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t myO = tO + 64 * half + lane;
+    const float scale2 = scale * 1.4426950408889634f / qscale[row];
+    const int qr = q0 + row, qs = qr - qr % T;
+    const int seq0 = q0 - q0 % T;
+    const bool one_seq = (q0 + kTcRows - 1) / T == q0 / T && q0 + kTcRows <= rows;
+    float m = -INFINITY, l = 0.f;
+    bool done = false;
+    for (int j = 0; j < n; ++j) {
+      const int b = j & 1;
+      const float2 ts = tscale[j];
+      const float coef = scale2 / ts.x;  // scaled score -> log2 units
+      F16_WAIT_OR_FAIL(&s_full[b], (j >> 1) & 1);
+      tc::fence_after_sync();
+      float s[32];
+      tc::tmem_ld32(tS + 64 * b + 32 * half + lane, s);
+      tc::fence_before_sync();
+      tc::bar_arrive(&s_empty[b]);
+      const int kt = kbeg + j * kTcK;
+      const bool full = one_seq && kt >= seq0 && kt + kTcK - 1 <= q0;
+      const int kh = kt + 32 * half;
+      if (!full) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int kr = kh + c;
+          s[c] = (kr <= qr && kr >= qs && kr < rows) ? s[c] : -INFINITY;
+        }
+      }
+      float m4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+      for (int c = 4; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
+      float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      mx *= coef;
+      const bool need = mx > m + 8.0f;  // false while every key so far is masked
+      float alpha = 1.0f;
+      if (need) {
+        alpha = ex2(m - mx);  // 0 when m = -inf
+        m = mx;
+      }
+      const float nm = m == -INFINITY ? 0.f : -m;
+      float2 rs2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < 32; c += 2) {
+        const float2 t = fma2(make_float2(s[c], s[c + 1]), splat2(coef), splat2(nm));
+        s[c] = ex2(t.x);  // ex2(-inf) = 0 for masked keys
+        s[c + 1] = ex2(t.y);
+        rs2 = add2(rs2, make_float2(s[c], s[c + 1]));
+      }
+      l = l * alpha + (rs2.x + rs2.y);
+      if (j >= 2) {
+        // P.V of step j-2 has read this P buffer.
+        F16_WAIT_OR_FAIL(&o_done[b], ((j - 2) >> 1) & 1);
+        tc::fence_after_sync();
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // P.V of step j-1 complete: O is stable for the rescale.
+        F16_WAIT_OR_FAIL(&o_done[b ^ 1], ((j - 1) >> 1) & 1);
+        tc::fence_after_sync();
+        {
+#pragma unroll
+          for (int c = 0; c < HD; c += 16) {
+            float ov[16];
+            tc::tmem_ld16(myO + c, ov);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ov[e] *= alpha;
+            tc::tmem_st16(myO + c, ov);
+          }
+        }
+      }
+      const uint32_t tPb = tP + 64 * b;
+      tc_st_split16<32>(tPb + 16 * half + lane, tPb + 32 + 16 * half + lane, s, pv_c / ts.y);
+      tc::tmem_st_wait();
+      tc::fence_before_sync();
+      tc::bar_arrive(&p_full[b]);
+      if (j + 1 == n) done = true;
+    }
+    if (done && !tc::bar_wait(&o_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
+    tc::fence_after_sync();
+    xm[half][row] = m;
+    xl[half][row] = l;
+    compute_sync();
+    if (done && !sh.failed) {
+      // Merge the two streams: O = (O0 2^(m0-M) + O1 2^(m1-M)) / (C L).
+      const float m0 = xm[0][row], m1 = xm[1][row];
+      const float mt = fmaxf(m0, m1);
+      const float f0 = m0 == -INFINITY ? 0.f : ex2(m0 - mt), f1 = m1 == -INFINITY ? 0.f : ex2(m1 - mt);
+      const float L = xl[0][row] * f0 + xl[1][row] * f1;
+      const float inv = L > 0.f ? 1.0f / (L * pv_c) : 0.f;
+      const uint32_t o0 = tO + lane, o1 = tO + 64 + lane;
+#pragma unroll
+      for (int c = 0; c < HD / 2; c += 16) {
+        const int col = (HD / 2) * half + c;
+        float a[16], bb[16];
+        tc::tmem_ld16_pair(o0 + col, a, o1 + col, bb);
+        if (qr < rows) {
+          float4* dst = reinterpret_cast<float4*>(o + (size_t)qr * W + h * HD + col);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            dst[e] = make_float4((a[4 * e] * f0 + bb[4 * e] * f1) * inv, (a[4 * e + 1] * f0 + bb[4 * e + 1] * f1) * inv,
+                                 (a[4 * e + 2] * f0 + bb[4 * e + 2] * f1) * inv,
+                                 (a[4 * e + 3] * f0 + bb[4 * e + 3] * f1) * inv);
+        }
+      }
+      if (qr < rows && half == 0) lse2[(size_t)h * rows + qr] = mt + log2f(L);
+    }
+  } else if (tid == kTcProducer) {
+    // ---------------------------------------------------------- producer
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      if (j >= NS) {
+        F16_WAIT_OR_FAIL(&kv_empty[st], ((j - NS) / NS) & 1);
+      }
+      tc::bar_expect_tx(&kv_full[st], A::FWD_STAGE_BYTES);
+      tc::bulk_g2s(sm8 + st * A::FWD_STAGE_BYTES, kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES,
+                   A::FWD_STAGE_BYTES, &kv_full[st]);
+    }
+  } else if (tid == kTcIssuer) {
+    // ---------------------------------------------------------- S issuer
+    constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS, b = j & 1;
+      const uint8_t* stage = sm8 + st * A::FWD_STAGE_BYTES;
+      F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
+      if (j >= 2) {
+        F16_WAIT_OR_FAIL(&s_empty[b], ((j - 2) >> 1) & 1);
+      }
+      tc::fence_after_sync();
+      // S_j = Q K_j^T over HD / 16 steps
+      mma16_tmem_a<HD, HD / 16>(tS + 64 * b, tQh, tQl, stage, stage + F::PART_BYTES, idS, false, 0);
+      tc::commit(&s_full[b]);
+    }
+  } else if (tid == kTcIssuer2) {
+    // ---------------------------------------------------------- P.V issuer
+    constexpr uint32_t idO = tc::idesc_f16(kTcRows, HD);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS, b = j & 1;
+      const uint8_t* stage = sm8 + st * A::FWD_STAGE_BYTES;
+      F16_WAIT_OR_FAIL(&p_full[b], (j >> 1) & 1);
+      F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
+      tc::fence_after_sync();
+      // O_half += P[:, half keys] V[half keys]  (B = V^T tile [HD][64 keys],
+      // K steps of 16 keys: half 0 steps 0-1, half 1 steps 2-3)
+      const uint8_t* vh = stage + 2 * F::PART_BYTES;
+      const uint8_t* vl = stage + 3 * F::PART_BYTES;
+      const uint32_t tPb = tP + 64 * b;
+      mma16_tmem_a<kTcK, 2>(tO, tPb, tPb + 32, vh, vl, idO, j > 0, 0);
+      mma16_tmem_a<kTcK, 2>(tO + 64, tPb, tPb + 32, vh, vl, idO, j > 0, 2);
+      tc::commit(&o_done[b]);
+      tc::commit(&kv_empty[st]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (sh.failed && tid == 0) atomicExch(err, 1);
+  if (warp == 0) tc::tmem_dealloc(t0, 512);
+}
+
+// ---------------------------------------------------------------------- dQ
+// A CTA owns 128 query rows of one head and walks their key tiles (K, V, K^T
+// FP16 parts and scales from the key format).  Per 64-key step: S = Q K^T and
+// dP = dO V^T (thread 288), then the compute threads form
+// dS = P (dP - delta) scale in two 32-key halves, each handed to thread 320
+// for dQ += dS K as soon as it is stored.  dS is double-buffered, so the next
+// step's S and dP are issued as soon as this step's S and dP have been read,
+// and a dS buffer is rewritten only after dQ of two steps back has read it.
+// Scales: Q rows s_q(i), dO rows t(i) (per row, like the forward's Q); key
+// tiles s_k(j), s_v(j); dS_ij is stored as dS_ij r(i) d(j) with
+// r(i) = f16_scale(2 |dO_i| max|V_row| scale), a bound on |dS_i.| (|dP| and
+// |delta| are at most |dO_i| max|V_row|), and d(j) = min_j s_k / s_k(j), so
+// dQ_i = dQ_tmem / (r(i) min_j s_k).
+// TMEM: Q hi | Q lo | dO hi | dO lo (32 each) | S | dP (64 each) |
+// dS0 hi | dS0 lo | dS1 hi | dS1 lo (32 each) | dQ (64) = 448.
+template <int HD>
+struct F16Dq {
+  using F = F16Fmt<HD>;
+  static constexpr int STAGES = 3;
+  static constexpr int STAGE_BYTES = 6 * F::PART_BYTES;  // K, K', V, V', Kt, Kt'
+  static constexpr size_t smem = (size_t)STAGES * STAGE_BYTES;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads2, 1)
+    attention_backward_dq_f16(int rows, int W, int T, float scale, const float* __restrict__ q,
+                              const float* __restrict__ dout, const uint8_t* __restrict__ kfmt,
+                              const float* __restrict__ lse2, const float* __restrict__ delta,
+                              float* __restrict__ dq, int* __restrict__ err) {
+  using A = F16Dq<HD>;
+  using F = F16Fmt<HD>;
+  constexpr int NS = A::STAGES;
+  extern __shared__ __align__(128) uint8_t sm8[];
+  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full, d_full[2][2], q_done[2];
+  __shared__ TcShared sh;
+  __shared__ float qscale[kTcRows], oscale[kTcRows], gscale[kTcRows];
+  __shared__ float2 tscale[kMaxKeyTiles];  // (s_k, s_v) of each visited key tile
+  __shared__ float kmin_s, vnorm_s;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int nt = (rows + kTcRows - 1) / kTcRows;
+  const int q0 = tile_by_work(blockIdx.x, nt, rows, T, true) * kTcRows;
+  const int h = blockIdx.y;
+  const int nkt = (rows + kTcK - 1) / kTcK;
+  const int kbeg = ((q0 - q0 % T) / kTcK) * kTcK;
+  const int kend = min(rows, q0 + kTcRows);
+  const int n = (kend - kbeg + kTcK - 1) / kTcK;
+  const int kt0 = kbeg / kTcK;
+  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
+  if (tid == 0) {
+    for (int b = 0; b < NS; ++b) {
+      tc::bar_init(&kv_full[b], 1);
+      tc::bar_init(&kv_empty[b], 1);
+    }
+    tc::bar_init(&s_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::bar_init(&d_full[b][0], kTcCompute);
+      tc::bar_init(&d_full[b][1], kTcCompute);
+      tc::bar_init(&q_done[b], 1);
+    }
+    tc::bar_init_fence();
+    sh.failed = 0;
+  }
+  if (warp == 8) {
+    float kmin = INFINITY, vnorm = 0.f;
+    for (int j = threadIdx.x & 31; j < n; j += 32) {
+      const float4 hd4 = __ldg(reinterpret_cast<const float4*>(kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES +
+                                                               8 * F::PART_BYTES));
+      tscale[j] = make_float2(hd4.x, hd4.y);
+      kmin = fminf(kmin, hd4.x);
+      vnorm = fmaxf(vnorm, hd4.z);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      kmin = fminf(kmin, __shfl_xor_sync(0xffffffffu, kmin, off));
+      vnorm = fmaxf(vnorm, __shfl_xor_sync(0xffffffffu, vnorm, off));
+    }
+    if ((threadIdx.x & 31) == 0) {
+      kmin_s = kmin;
+      vnorm_s = vnorm;
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t t0 = sh.tmem_base;
+  const uint32_t tQh = t0, tQl = t0 + 32, tDh = t0 + 64, tDl = t0 + 96, tS = t0 + 128, tdP = t0 + 192,
+                 tG = t0 + 384;
+  // dS buffer b: hi at tdS + 64 b, lo at tdS + 64 b + 32
+  const uint32_t tdS = t0 + 256;
+  if (warp < 4) {
+    const uint32_t lane = (uint32_t)(warp * 32) << 16;
+    qscale[tid] = row_to_tmem16<HD>(q, q0 + tid, rows, W, h, tQh + lane, tQl + lane);
+    oscale[tid] = row_to_tmem16<HD>(dout, q0 + tid, rows, W, h, tDh + lane, tDl + lane);
+    // |dO_row| for the dS bound
+    float ss = 0.f;
+    const int r = q0 + tid;
+    if (r < rows) {
+#pragma unroll
+      for (int c = 0; c < HD; c += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(dout + (size_t)r * W + h * HD + c));
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+    }
+    gscale[tid] = tc::f16_scale(2.0f * sqrtf(ss) * vnorm_s * scale);
+    tc::tmem_st_wait();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+
+  if (tid < kTcCompute) {
+    // Thread (row, half) handles key columns [16 half, +16) of each 32-key half.
+    const int row = tid & (kTcRows - 1), half = tid >> 7;
+    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    const float sq_inv = 1.0f / qscale[row], so_inv = 1.0f / oscale[row], rg = gscale[row];
+    const float scale2 = scale * 1.4426950408889634f * sq_inv;
+    const int qr = q0 + row, qs = qr - qr % T;
+    const int seq0 = q0 - q0 % T;
+    const bool one_seq = (q0 + kTcRows - 1) / T == q0 / T && q0 + kTcRows <= rows;
+    const bool in = qr < rows;
+    const float L = in ? lse2[(size_t)h * rows + qr] : 0.f;
+    const float dl = in ? delta[(size_t)h * rows + qr] : 0.f;
+    const float kmin = kmin_s;
+    bool done = false;
+    for (int j = 0; j < n; ++j) {
+      const int b = j & 1;
+      const float2 ts = tscale[j];
+      const float coef = scale2 / ts.x;                // S_tmem -> log2 units
+      const float dcoef = so_inv / ts.y;               // dP_tmem -> dP
+      const float gcoef = scale * rg * (kmin / ts.x);  // dS -> stored dS
+      F16_WAIT_OR_FAIL(&s_full, j & 1);
+      tc::fence_after_sync();
+      if (j >= 2) {
+        F16_WAIT_OR_FAIL(&q_done[b], ((j - 2) >> 1) & 1);  // dQ of step j-2 has read this dS buffer
+        tc::fence_after_sync();
+      }
+      const int kt = kbeg + j * kTcK;
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int col = 32 * k2 + 16 * half;
+        float s[16], dp[16];
+        tc::tmem_ld16_pair(tS + col + lane, s, tdP + col + lane, dp);
+        const bool full = one_seq && kt + 32 * k2 >= seq0 && kt + 32 * k2 + 31 <= q0;
+        const int kh = kt + col;
+#pragma unroll
+        for (int c = 0; c < 16; c += 2) {
+          const float2 t = fma2(make_float2(s[c], s[c + 1]), splat2(coef), splat2(-L));
+          const bool ok0 = full || (kh + c <= qr && kh + c >= qs && kh + c < rows);
+          const bool ok1 = full || (kh + c + 1 <= qr && kh + c + 1 >= qs && kh + c + 1 < rows);
+          const float2 p = make_float2(ok0 ? ex2(t.x) : 0.f, ok1 ? ex2(t.y) : 0.f);
+          const float2 g = mul2(p, fma2(make_float2(dp[c], dp[c + 1]), splat2(dcoef), splat2(-dl)));
+          s[c] = g.x;
+          s[c + 1] = g.y;
+        }
+        const uint32_t tB = tdS + 64 * b + 8 * (2 * k2 + half);
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tc::split_f16x2(s[2 * e] * gcoef, s[2 * e + 1] * gcoef, hi[e], lo[e]);
+        tc::tmem_st8u(tB + lane, hi);
+        tc::tmem_st8u(tB + 32 + lane, lo);
+        tc::tmem_st_wait();
+        tc::fence_before_sync();
+        tc::bar_arrive(&d_full[b][k2]);
+      }
+      if (j + 1 == n) done = true;
+    }
+    if (done && !tc::bar_wait(&q_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
+    tc::fence_after_sync();
+    if (done && !sh.failed) {
+      const float out = 1.0f / (rg * kmin);
+#pragma unroll
+      for (int c = 0; c < HD / 2; c += 16) {
+        const int col = (HD / 2) * half + c;
+        float gv[16];
+        tc::tmem_ld16(tG + lane + col, gv);
+        if (in) {
+          float4* dst = reinterpret_cast<float4*>(dq + (size_t)qr * W + h * HD + col);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            dst[e] = make_float4(gv[4 * e] * out, gv[4 * e + 1] * out, gv[4 * e + 2] * out, gv[4 * e + 3] * out);
+        }
+      }
+    }
+  } else if (tid == kTcProducer) {
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      if (j >= NS) {
+        F16_WAIT_OR_FAIL(&kv_empty[st], ((j - NS) / NS) & 1);
+      }
+      const uint8_t* tile = kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES;
+      uint8_t* stage = sm8 + st * A::STAGE_BYTES;
+      tc::bar_expect_tx(&kv_full[st], A::STAGE_BYTES);
+      tc::bulk_g2s(stage, tile, 2 * F::PART_BYTES, &kv_full[st]);                                          // K, K'
+      tc::bulk_g2s(stage + 2 * F::PART_BYTES, tile + 4 * F::PART_BYTES, 4 * F::PART_BYTES, &kv_full[st]);  // V, V', Kt, Kt'
+    }
+  } else if (tid == kTcIssuer) {
+    // ---------------------------------------------------------- S / dP issuer
+    constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS;
+      const uint8_t* stage = sm8 + st * A::STAGE_BYTES;  // K, K', V, V', Kt, Kt'
+      F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
+      if (j > 0) {
+        F16_WAIT_OR_FAIL(&d_full[(j - 1) & 1][1], ((j - 1) >> 1) & 1);  // S_{j-1}, dP_{j-1} read
+      }
+      tc::fence_after_sync();
+      mma16_tmem_a<HD, HD / 16>(tS, tQh, tQl, stage, stage + F::PART_BYTES, idS, false, 0);  // S_j = Q K_j^T
+      mma16_tmem_a<HD, HD / 16>(tdP, tDh, tDl, stage + 2 * F::PART_BYTES, stage + 3 * F::PART_BYTES, idS, false,
+                                0);  // dP_j = dO V_j^T
+      tc::commit(&s_full);
+    }
+  } else if (tid == kTcIssuer2) {
+    // ---------------------------------------------------------- dQ issuer
+    constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD);
+    for (int j = 0; j < n; ++j) {
+      const int st = j % NS, b = j & 1;
+      const uint8_t* stage = sm8 + st * A::STAGE_BYTES;
+      F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
+      const uint32_t tB = tdS + 64 * b;
+      bool ok = true;
+      for (int k2 = 0; k2 < 2 && ok; ++k2) {
+        ok = tc::bar_wait(&d_full[b][k2], (j >> 1) & 1);
+        tc::fence_after_sync();
+        // dQ += dS K over keys [32 k2, 32 k2 + 32): K steps 2 k2, 2 k2 + 1 of
+        // the K^T tile [HD][64 keys]
+        if (ok)
+          mma16_tmem_a<kTcK, 2>(tG, tB, tB + 32, stage + 4 * F::PART_BYTES, stage + 5 * F::PART_BYTES, idG,
+                                j > 0 || k2 > 0, 2 * k2);
+      }
+      if (!ok) {
+        sh.failed = 1;
+        break;
+      }
+      tc::commit(&q_done[b]);
+      tc::commit(&kv_empty[st]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (sh.failed && tid == 0) atomicExch(err, 1);
+  if (warp == 0) tc::tmem_dealloc(t0, 512);
+}
+
+#undef F16_WAIT_OR_FAIL
+
+}  // namespace mb

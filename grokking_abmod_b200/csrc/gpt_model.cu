@@ -34,6 +34,7 @@
 #include "gpt_attention.cu"
 #include "gpt_blocks.cu"
 #include "gpt_attention_tc.cu"
+#include "gpt_attention_f16.cu"
 #include "gpt_head.cu"
 
 namespace mb {
@@ -229,14 +230,17 @@ struct AttentionOpsTc final : AttentionOps {
   using F = TcFmt<HD>;
   int* err;
   explicit AttentionOpsTc(int* e) : err(e) {
-    MB_CUDA(cudaFuncSetAttribute(&attention_forward_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)K::smem_forward));
-    MB_CUDA(cudaFuncSetAttribute(&attention_backward_dq_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)K::smem_dq));
+    MB_CUDA(cudaFuncSetAttribute(&attention_forward_f16<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)F16Att<HD>::smem_forward));
+    MB_CUDA(cudaFuncSetAttribute(&attention_backward_dq_f16<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)F16Dq<HD>::smem));
     MB_CUDA(cudaFuncSetAttribute(&attention_backward_dkdv_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)TcKv<HD>::smem));
   }
-  static size_t key_floats(int rows, int H) { return (size_t)H * ((rows + kTcK - 1) / kTcK) * F::KTILE; }
+  // per block: the FP16 key tiles the forward and dQ read
+  static size_t key_floats(int rows, int H) {
+    return (size_t)H * ((rows + kTcK - 1) / kTcK) * F16Fmt<HD>::KTILE_BYTES / sizeof(float);
+  }
   static size_t query_floats(int rows, int H) { return (size_t)H * ((rows + kTcQ - 1) / kTcQ) * F::QTILE; }
   // One query-tile set (rebuilt per backward block) and one key-tile set per
   // block: the forward formats every key part once and dQ reuses them.
@@ -246,17 +250,20 @@ struct AttentionOpsTc final : AttentionOps {
   int forward_launches() const override { return 2; }   // key format + forward
   int backward_launches() const override { return 3; }  // query format + dK/dV, dQ
   float* qfmt() const { return scratch; }
-  float* kfmt(int rows, int H) const { return scratch + query_floats(rows, H) + (size_t)layer * key_floats(rows, H); }
+  uint8_t* kfmt16(int rows, int H) const {
+    return reinterpret_cast<uint8_t*>(scratch + query_floats(rows, H) + (size_t)layer * key_floats(rows, H));
+  }
   void prepare_keys(cudaStream_t s, int rows, int W, int H, const float* k, const float* v) override {
-    attention_format_keys<HD><<<dim3((rows + kTcK - 1) / kTcK, H), kFmtThreads, 0, s>>>(
-        rows, W, k, v, kfmt(rows, H), (1u << F::K_HI) | (1u << F::VT_HI) | (1u << F::V_HI) | (1u << F::KT_HI));
+    using G = F16Fmt<HD>;
+    attention_format_keys_f16<HD><<<dim3((rows + kTcK - 1) / kTcK, H), kFmtThreads, 0, s>>>(
+        rows, W, k, v, kfmt16(rows, H), (1u << G::K_HI) | (1u << G::VT_HI) | (1u << G::V_HI) | (1u << G::KT_HI));
   }
   void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                const float* v, float* o, float* lse) override {
     prepare_keys(s, rows, W, H, k, v);
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_forward_tc<HD><<<grid, kTcThreads2, K::smem_forward, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
-                                                                        kfmt(rows, H), o, lse, err);
+    attention_forward_f16<HD><<<grid, kTcThreads2, F16Att<HD>::smem_forward, s>>>(
+        rows, W, T, 1.0f / sqrtf((float)hd), q, kfmt16(rows, H), o, lse, err);
   }
   void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                      const float* v, const float* dout, const float* lse, const float* delta, const float* dv_add,
@@ -270,8 +277,9 @@ struct AttentionOpsTc final : AttentionOps {
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dq_tc<HD><<<grid, kTcThreads2, K::smem_dq, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q, dout,
-                                                                       kfmt(rows, H), lse, delta, dq, err);
+    attention_backward_dq_f16<HD><<<grid, kTcThreads2, F16Dq<HD>::smem, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
+                                                                             dout, kfmt16(rows, H), lse, delta, dq,
+                                                                             err);
   }
 };
 

@@ -18,6 +18,7 @@
 // operand needed with its rows along N is stored transposed instead.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -189,10 +190,6 @@ __device__ __forceinline__ void tmem_ld16_pair(uint32_t ta, float (&a)[16], uint
   }
 }
 
-// Kept for call sites written against separate load / wait steps; the loads
-// above already waited.
-__device__ __forceinline__ void tmem_ld_wait() {}
-
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -215,6 +212,96 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 // loops already load with ex2.
 __device__ __forceinline__ float tf32_hi(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
+// ---------------------------------------------------------------- f16 forms
+// Three-term FP16 products ("3xF16"): a finite FP32 value x, first scaled by
+// a power of two s that puts the operand's largest magnitude near 2^13, is
+// split into hi = FP16(x s) and lo = FP16(x s - hi); a product
+// is accumulated as hi.hi + hi.lo + lo.hi in FP32 (TMEM) on kind::f16 MMAs,
+// which run at twice the kind::tf32 rate.  The relative error per product is
+// near 2^-21 as with 3xTF32; the scaling keeps hi within FP16's range, and
+// magnitudes below 2^-16 of the operand's largest lose low bits of lo only,
+// an absolute error near 2^-38 of that largest magnitude.
+//
+// FP16 operand tiles use the same unswizzled blocked layout with 8 x 8 core
+// matrices of 128 contiguous bytes: half-element (r, c) of an R x C tile is
+// at half offset ((r / 8) * (C / 8) + c / 8) * 64 + (r % 8) * 8 + c % 8; a K
+// step of 16 elements is again two core matrices 128 B apart.  In tensor
+// memory an FP16 A operand packs two consecutive K elements per 32-bit
+// column (the lower index in the low half), so K step s reads columns
+// [8s, 8s + 8).
+__device__ __forceinline__ int blk16(int r, int c, int C) {
+  return ((r >> 3) * (C >> 3) + (c >> 3)) * 64 + (r & 7) * 8 + (c & 7);
+}
+
+// K-major FP16 operand with C columns (half elements); step s covers K
+// columns [16s, 16s + 16).
+__device__ __forceinline__ uint64_t desc_kmajor16(const void* tile, int C, int s) {
+  return sdesc(smem_addr(tile) + (uint32_t)s * 256u, 128u, (uint32_t)(C / 8) * 128u);
+}
+
+// Instruction descriptor: FP32 accumulator, FP16 A and B, M x N, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D (TMEM) (+)= A (TMEM, FP16 pairs, lane = row) * B (smem, FP16)
+__device__ __forceinline__ void mma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// D (TMEM) (+)= A (smem, FP16) * B (smem, FP16)
+__device__ __forceinline__ void mma_ss_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// The power of two 2^(13 - e), 2^(e-1) <= max_abs < 2^e: scales an operand
+// whose largest magnitude is max_abs into [2^12, 2^13).  1 for an all-zero
+// operand; clamped so that the scale and its inverse stay normal FP32.
+__device__ __forceinline__ float f16_scale(float max_abs) {
+  if (!(max_abs > 0.f)) return 1.0f;
+  int e;
+  frexpf(max_abs, &e);  // max_abs = m 2^e, 0.5 <= m < 1
+  int k = 13 - e;
+  k = k > 120 ? 120 : (k < -120 ? -120 : k);
+  return __int_as_float((k + 127) << 23);
+}
+
+// hi/lo FP16 parts of x (already scaled) packed with those of y: the pair
+// (x, y) in one 32-bit word each, x in the low half.  lo is taken from the
+// FP16 hi itself (x - hi is exact in FP32), so subnormal hi parts stay exact.
+__device__ __forceinline__ void split_f16x2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
 }
 
 }  // namespace tc

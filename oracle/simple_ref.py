@@ -424,6 +424,7 @@ class ReferenceSimpleModel:
         model's near-identity chain makes values such as 1e-50 (products of
         its small mixing weights) that FP32 holds as exactly 0."""
         self.fp32_kink = fp32_kink
+        self.kink_band = None  # (band, slope): ReLU slope for nonzero |pre-activation| <= band
         self.config = config.validate()
         self.parameters = (initial_parameters(config, seed) if parameters is None
                            else np.asarray(parameters, dtype=np.float32).copy())
@@ -431,6 +432,10 @@ class ReferenceSimpleModel:
             raise ValueError("parameter count does not match the model")
 
     def _slope(self, x):
+        if self.kink_band is not None and self.config.activation == "relu":
+            band, value = self.kink_band
+            x = np.asarray(x)
+            return np.where((np.abs(x) <= band) & (x != 0.0), value, (x > 0.0).astype(np.float64))
         if self.fp32_kink and self.config.activation == "relu":
             return (np.asarray(x).astype(np.float32) > 0.0).astype(np.float64)
         return _act_grad(self.config, x)
