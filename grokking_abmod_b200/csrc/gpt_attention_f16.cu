@@ -423,19 +423,23 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
 
 // ---------------------------------------------------------------------- dQ
 // A CTA owns 128 query rows of one head and walks their key tiles (K, V, K^T
-// FP16 parts and scales from the key format).  Per 64-key step: S = Q K^T and
-// dP = dO V^T (thread 288), then the compute threads form
-// dS = P (dP - delta) scale in two 32-key halves, each handed to thread 320
-// for dQ += dS K as soon as it is stored.  dS is double-buffered, so the next
-// step's S and dP are issued as soon as this step's S and dP have been read,
-// and a dS buffer is rewritten only after dQ of two steps back has read it.
+// FP16 parts and scales from the key format).  Per 64-key step j (TMEM
+// buffer b = j & 1): S = Q K^T and dP = dO V^T (thread 288); the compute
+// threads form dS = P (dP - delta) scale in two 32-key halves, each handed to
+// thread 320 for dQ += dS K as soon as it is stored.  S and dP are
+// double-buffered, so step j + 1's MMAs run while step j's softmax computes.
+// dS is written over the S columns its thread has just read: the thread
+// owning keys [16m, 16m + 16) stores their FP16 hi parts in S columns
+// [16m, 16m + 8) and lo parts in [16m + 8, 16m + 16), so no thread overwrites
+// columns another has yet to read; S_{j+2} is issued into the buffer once
+// dQ of step j has read that dS.
 // Scales: Q rows s_q(i), dO rows t(i) (per row, like the forward's Q); key
 // tiles s_k(j), s_v(j); dS_ij is stored as dS_ij r(i) d(j) with
 // r(i) = f16_scale(2 |dO_i| max|V_row| scale), a bound on |dS_i.| (|dP| and
 // |delta| are at most |dO_i| max|V_row|), and d(j) = min_j s_k / s_k(j), so
 // dQ_i = dQ_tmem / (r(i) min_j s_k).
-// TMEM: Q hi | Q lo | dO hi | dO lo (32 each) | S | dP (64 each) |
-// dS0 hi | dS0 lo | dS1 hi | dS1 lo (32 each) | dQ (64) = 448.
+// TMEM: Q hi | Q lo | dO hi | dO lo (32 each) | S0 | dP0 | S1 | dP1 (64 each) |
+// dQ (64) = 448.
 template <int HD>
 struct F16Dq {
   using F = F16Fmt<HD>;
@@ -443,6 +447,22 @@ struct F16Dq {
   static constexpr int STAGE_BYTES = 6 * F::PART_BYTES;  // K, K', V, V', Kt, Kt'
   static constexpr size_t smem = (size_t)STAGES * STAGE_BYTES;
 };
+
+// D (+)= A . B^T over K steps [s0, s0 + NSTEP) of 16 elements with A's FP16
+// hi and lo parts interleaved in TMEM: step s reads hi columns [16s, 16s + 8)
+// and lo columns [16s + 8, 16s + 16) of `a`.
+template <int KC, int NSTEP>
+__device__ __forceinline__ void mma16_tmem_a_il(uint32_t d, uint32_t a, const void* bh, const void* bl,
+                                                uint32_t idesc, bool accumulate, int s0) {
+#pragma unroll
+  for (int i = 0; i < NSTEP; ++i) {
+    const int s = s0 + i;
+    const uint64_t b_h = tc::desc_kmajor16(bh, KC, s), b_l = tc::desc_kmajor16(bl, KC, s);
+    tc::mma_ts_f16(d, a + 16 * s, b_h, idesc, (accumulate || i > 0) ? 1u : 0u);
+    tc::mma_ts_f16(d, a + 16 * s, b_l, idesc, 1u);
+    tc::mma_ts_f16(d, a + 16 * s + 8, b_h, idesc, 1u);
+  }
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kTcThreads2, 1)
@@ -454,7 +474,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   using F = F16Fmt<HD>;
   constexpr int NS = A::STAGES;
   extern __shared__ __align__(128) uint8_t sm8[];
-  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full, d_full[2][2], q_done[2];
+  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full[2], d_full[2][2], q_done[2];
   __shared__ TcShared sh;
   __shared__ float qscale[kTcRows], oscale[kTcRows], gscale[kTcRows];
   __shared__ float2 tscale[kMaxKeyTiles];  // (s_k, s_v) of each visited key tile
@@ -474,8 +494,8 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       tc::bar_init(&kv_full[b], 1);
       tc::bar_init(&kv_empty[b], 1);
     }
-    tc::bar_init(&s_full, 1);
     for (int b = 0; b < 2; ++b) {
+      tc::bar_init(&s_full[b], 1);
       tc::bar_init(&d_full[b][0], kTcCompute);
       tc::bar_init(&d_full[b][1], kTcCompute);
       tc::bar_init(&q_done[b], 1);
@@ -506,10 +526,8 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t t0 = sh.tmem_base;
-  const uint32_t tQh = t0, tQl = t0 + 32, tDh = t0 + 64, tDl = t0 + 96, tS = t0 + 128, tdP = t0 + 192,
-                 tG = t0 + 384;
-  // dS buffer b: hi at tdS + 64 b, lo at tdS + 64 b + 32
-  const uint32_t tdS = t0 + 256;
+  // buffer b: S at tS + 128 b (later dS, interleaved), dP at tS + 128 b + 64
+  const uint32_t tQh = t0, tQl = t0 + 32, tDh = t0 + 64, tDl = t0 + 96, tS = t0 + 128, tG = t0 + 384;
   if (warp < 4) {
     const uint32_t lane = (uint32_t)(warp * 32) << 16;
     qscale[tid] = row_to_tmem16<HD>(q, q0 + tid, rows, W, h, tQh + lane, tQl + lane);
@@ -551,17 +569,14 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       const float coef = scale2 / ts.x;                // S_tmem -> log2 units
       const float dcoef = so_inv / ts.y;               // dP_tmem -> dP
       const float gcoef = scale * rg * (kmin / ts.x);  // dS -> stored dS
-      F16_WAIT_OR_FAIL(&s_full, j & 1);
+      const uint32_t tSb = tS + 128 * b;
+      F16_WAIT_OR_FAIL(&s_full[b], (j >> 1) & 1);
       tc::fence_after_sync();
-      if (j >= 2) {
-        F16_WAIT_OR_FAIL(&q_done[b], ((j - 2) >> 1) & 1);  // dQ of step j-2 has read this dS buffer
-        tc::fence_after_sync();
-      }
       const int kt = kbeg + j * kTcK;
       for (int k2 = 0; k2 < 2; ++k2) {
         const int col = 32 * k2 + 16 * half;
         float s[16], dp[16];
-        tc::tmem_ld16_pair(tS + col + lane, s, tdP + col + lane, dp);
+        tc::tmem_ld16_pair(tSb + col + lane, s, tSb + 64 + col + lane, dp);
         const bool full = one_seq && kt + 32 * k2 >= seq0 && kt + 32 * k2 + 31 <= q0;
         const int kh = kt + col;
 #pragma unroll
@@ -574,12 +589,11 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
           s[c] = g.x;
           s[c + 1] = g.y;
         }
-        const uint32_t tB = tdS + 64 * b + 8 * (2 * k2 + half);
         uint32_t hi[8], lo[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) tc::split_f16x2(s[2 * e] * gcoef, s[2 * e + 1] * gcoef, hi[e], lo[e]);
-        tc::tmem_st8u(tB + lane, hi);
-        tc::tmem_st8u(tB + 32 + lane, lo);
+        tc::tmem_st8u(tSb + col + lane, hi);      // over the S columns just read
+        tc::tmem_st8u(tSb + col + 8 + lane, lo);
         tc::tmem_st_wait();
         tc::fence_before_sync();
         tc::bar_arrive(&d_full[b][k2]);
@@ -619,17 +633,19 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
     // ---------------------------------------------------------- S / dP issuer
     constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
     for (int j = 0; j < n; ++j) {
-      const int st = j % NS;
+      const int st = j % NS, b = j & 1;
       const uint8_t* stage = sm8 + st * A::STAGE_BYTES;  // K, K', V, V', Kt, Kt'
       F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
-      if (j > 0) {
-        F16_WAIT_OR_FAIL(&d_full[(j - 1) & 1][1], ((j - 1) >> 1) & 1);  // S_{j-1}, dP_{j-1} read
+      if (j >= 2) {
+        // dQ of step j-2 has read this buffer's dS, so its S and dP are free
+        F16_WAIT_OR_FAIL(&q_done[b], ((j - 2) >> 1) & 1);
       }
       tc::fence_after_sync();
-      mma16_tmem_a<HD, HD / 16>(tS, tQh, tQl, stage, stage + F::PART_BYTES, idS, false, 0);  // S_j = Q K_j^T
-      mma16_tmem_a<HD, HD / 16>(tdP, tDh, tDl, stage + 2 * F::PART_BYTES, stage + 3 * F::PART_BYTES, idS, false,
-                                0);  // dP_j = dO V_j^T
-      tc::commit(&s_full);
+      const uint32_t tSb = tS + 128 * b;
+      mma16_tmem_a<HD, HD / 16>(tSb, tQh, tQl, stage, stage + F::PART_BYTES, idS, false, 0);  // S_j = Q K_j^T
+      mma16_tmem_a<HD, HD / 16>(tSb + 64, tDh, tDl, stage + 2 * F::PART_BYTES, stage + 3 * F::PART_BYTES, idS,
+                                false, 0);  // dP_j = dO V_j^T
+      tc::commit(&s_full[b]);
     }
   } else if (tid == kTcIssuer2) {
     // ---------------------------------------------------------- dQ issuer
@@ -638,7 +654,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       const int st = j % NS, b = j & 1;
       const uint8_t* stage = sm8 + st * A::STAGE_BYTES;
       F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
-      const uint32_t tB = tdS + 64 * b;
+      const uint32_t tSb = tS + 128 * b;
       bool ok = true;
       for (int k2 = 0; k2 < 2 && ok; ++k2) {
         ok = tc::bar_wait(&d_full[b][k2], (j >> 1) & 1);
@@ -646,8 +662,8 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
         // dQ += dS K over keys [32 k2, 32 k2 + 32): K steps 2 k2, 2 k2 + 1 of
         // the K^T tile [HD][64 keys]
         if (ok)
-          mma16_tmem_a<kTcK, 2>(tG, tB, tB + 32, stage + 4 * F::PART_BYTES, stage + 5 * F::PART_BYTES, idG,
-                                j > 0 || k2 > 0, 2 * k2);
+          mma16_tmem_a_il<kTcK, 2>(tG, tSb, stage + 4 * F::PART_BYTES, stage + 5 * F::PART_BYTES, idG,
+                                   j > 0 || k2 > 0, 2 * k2);
       }
       if (!ok) {
         sh.failed = 1;
