@@ -679,6 +679,382 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   if (warp == 0) tc::tmem_dealloc(t0, 512);
 }
 
+// ------------------------------------------------------------------- dK/dV
+// Query tiles in FP16 parts: Q, Q', dO, dO', Q^T, Q^T', dO^T, dO^T' (64 x HD
+// each) and a header with the 64 rows' LSE and delta, the tile's scales
+// s_q and s_do, its largest dO row norm and its largest |delta|.
+template <int HD>
+struct F16Q {
+  static constexpr int PART_BYTES = kTcQ * HD * 2;
+  static constexpr int HEADER_BYTES = 1024;
+  static constexpr int QTILE_BYTES = 8 * PART_BYTES + HEADER_BYTES;
+  static constexpr int Q_HI = 0, D_HI = 2, QT_HI = 4, DT_HI = 6;
+  static constexpr int LSE = 0, DELTA = kTcQ, SCALES = 2 * kTcQ;  // header floats
+};
+
+// Query tiles of Q and dO with LSE and delta: grid (ceil(rows/64), H).
+template <int HD>
+__global__ void __launch_bounds__(kFmtThreads) attention_format_queries_f16(int rows, int W, const float* __restrict__ q,
+                                                                      const float* __restrict__ dout,
+                                                                      const float* __restrict__ lse2,
+                                                                      const float* __restrict__ delta,
+                                                                      uint8_t* __restrict__ fmt) {
+  using G = F16Q<HD>;
+  constexpr int XS = HD + 2, NW = kFmtThreads / 32;
+  __shared__ float xq[kTcQ * XS], xd[kTcQ * XS];
+  __shared__ float red[4][NW];
+  const int t = blockIdx.x, h = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint8_t* tile = fmt + ((size_t)h * gridDim.x + t) * G::QTILE_BYTES;
+  float* hdr = reinterpret_cast<float*>(tile + 8 * G::PART_BYTES);
+  load_rows2<kTcQ, HD>(xq, q, xd, dout, t * kTcQ, rows, W, h);
+  __syncthreads();
+  float mq = 0.f, md = 0.f, nd = 0.f, mdl = 0.f;
+  for (int i = threadIdx.x; i < kTcQ * HD; i += kFmtThreads) {
+    const int r = i / HD, c = i % HD;
+    mq = fmaxf(mq, fabsf(xq[r * XS + c]));
+    md = fmaxf(md, fabsf(xd[r * XS + c]));
+  }
+  if (threadIdx.x < kTcQ) {
+    const int row = t * kTcQ + threadIdx.x;
+    float ss = 0.f;
+    for (int c = 0; c < HD; ++c) ss += xd[threadIdx.x * XS + c] * xd[threadIdx.x * XS + c];
+    nd = sqrtf(ss);
+    const float L = row < rows ? lse2[(size_t)h * rows + row] : 0.f;
+    const float dl = row < rows ? delta[(size_t)h * rows + row] : 0.f;
+    hdr[G::LSE + threadIdx.x] = L;
+    hdr[G::DELTA + threadIdx.x] = dl;
+    mdl = fabsf(dl);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    mq = fmaxf(mq, __shfl_xor_sync(0xffffffffu, mq, o));
+    md = fmaxf(md, __shfl_xor_sync(0xffffffffu, md, o));
+    nd = fmaxf(nd, __shfl_xor_sync(0xffffffffu, nd, o));
+    mdl = fmaxf(mdl, __shfl_xor_sync(0xffffffffu, mdl, o));
+  }
+  if (lane == 0) {
+    red[0][warp] = mq;
+    red[1][warp] = md;
+    red[2][warp] = nd;
+    red[3][warp] = mdl;
+  }
+  __syncthreads();
+  mq = md = nd = mdl = 0.f;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    mq = fmaxf(mq, red[0][w]);
+    md = fmaxf(md, red[1][w]);
+    nd = fmaxf(nd, red[2][w]);
+    mdl = fmaxf(mdl, red[3][w]);
+  }
+  const float sq = tc::f16_scale(mq), sd = tc::f16_scale(md);
+  store_parts16<kTcQ, HD>(tile, G::Q_HI, false, xq, sq);
+  store_parts16<kTcQ, HD>(tile, G::D_HI, false, xd, sd);
+  store_parts16<kTcQ, HD>(tile, G::QT_HI, true, xq, sq);
+  store_parts16<kTcQ, HD>(tile, G::DT_HI, true, xd, sd);
+  if (threadIdx.x == 0) *reinterpret_cast<float4*>(hdr + G::SCALES) = make_float4(sq, sd, nd, mdl);
+}
+
+// A CTA owns 128 keys of one head (K and V split into TMEM with per-row
+// scales) and walks their queries 64 at a time through a 3-stage ring of
+// query tiles.  Per step i (TMEM buffer b = i & 1): thread 288 issues
+// S^T = K Q^T and dP^T = V dO^T (keys on lanes, N = 64 queries); the compute
+// threads form P^T = exp2(S^T scale - lse) and store it over the S^T columns
+// they have read (FP16 hi/lo interleaved, as in dQ), then dS^T =
+// P^T (dP^T - delta) scale over the dP^T columns; thread 320 issues
+// dV += P^T dO and dK += dS^T Q.  S^T and dP^T are double-buffered, so step
+// i + 1's MMAs run while step i's softmax computes.
+// Scales: K rows s_K(k), V rows s_V(k); query tiles s_q(i), s_do(i).  P^T is
+// stored as P c_i, c_i = 2^13 min_i s_do / s_do(i) (P <= 1), so
+// dV = dV_tmem / (2^13 min_i s_do); dS^T as dS r(k) min_i s_q / s_q(i) with
+// r(k) = f16_scale((max|dO_q| |V_k| + max|delta|) scale), a bound on
+// |dS_k.|, so dK = dK_tmem / (r(k) min_i s_q).
+// TMEM: K hi | K lo | V hi | V lo (32 each) | dV | dK (64 each) |
+// S^T0 | dP^T0 | S^T1 | dP^T1 (64 each) = 512.
+template <int HD>
+struct F16Kv {
+  using G = F16Q<HD>;
+  static constexpr int STAGES = 3;
+  static constexpr size_t smem = (size_t)STAGES * G::QTILE_BYTES;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads2, 1)
+    attention_backward_dkdv_f16(int rows, int W, int T, float scale, const float* __restrict__ k,
+                                const float* __restrict__ v, const uint8_t* __restrict__ qfmt,
+                                const float* __restrict__ dv_add, float* __restrict__ dk, float* __restrict__ dv,
+                                int* __restrict__ err) {
+  using G = F16Q<HD>;
+  constexpr int NS = F16Kv<HD>::STAGES;
+  extern __shared__ __align__(128) uint8_t sm8[];
+  __shared__ uint64_t q_full[NS], q_empty[NS], s_full[2], dp_full[2], p_full[2], ds_full[2][2], g_done[2];
+  __shared__ TcShared sh;
+  __shared__ float kscale[kTcRows], vscale[kTcRows], vnorm[kTcRows];
+  __shared__ float2 tscale[kMaxKeyTiles];  // (s_q, s_do) of each visited query tile
+  __shared__ float sqmin_s, sdomin_s, ndmax_s, dlmax_s;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int k0 = tile_by_work(blockIdx.x, gridDim.x, rows, T, false) * kTcRows;
+  const int h = blockIdx.y;
+  const int nqt = (rows + kTcQ - 1) / kTcQ;
+  const int last = min(rows, k0 + kTcRows) - 1;
+  const int qend = min(rows, (last / T + 1) * T);
+  const int n = (qend - k0 + kTcQ - 1) / kTcQ;
+  const int qt0 = k0 / kTcQ;
+  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
+  if (tid == 0) {
+    for (int b = 0; b < NS; ++b) {
+      tc::bar_init(&q_full[b], 1);
+      tc::bar_init(&q_empty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::bar_init(&s_full[b], 1);
+      tc::bar_init(&dp_full[b], 1);
+      tc::bar_init(&p_full[b], kTcCompute);
+      tc::bar_init(&ds_full[b][0], kTcCompute);
+      tc::bar_init(&ds_full[b][1], kTcCompute);
+      tc::bar_init(&g_done[b], 1);
+    }
+    tc::bar_init_fence();
+    sh.failed = 0;
+  }
+  if (warp == 8) {
+    float sqm = INFINITY, sdm = INFINITY, ndm = 0.f, dlm = 0.f;
+    for (int i = threadIdx.x & 31; i < n; i += 32) {
+      const float4 sc = __ldg(reinterpret_cast<const float4*>(qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES +
+                                                              8 * G::PART_BYTES + G::SCALES * 4));
+      tscale[i] = make_float2(sc.x, sc.y);
+      sqm = fminf(sqm, sc.x);
+      sdm = fminf(sdm, sc.y);
+      ndm = fmaxf(ndm, sc.z);
+      dlm = fmaxf(dlm, sc.w);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      sqm = fminf(sqm, __shfl_xor_sync(0xffffffffu, sqm, off));
+      sdm = fminf(sdm, __shfl_xor_sync(0xffffffffu, sdm, off));
+      ndm = fmaxf(ndm, __shfl_xor_sync(0xffffffffu, ndm, off));
+      dlm = fmaxf(dlm, __shfl_xor_sync(0xffffffffu, dlm, off));
+    }
+    if ((threadIdx.x & 31) == 0) {
+      sqmin_s = sqm;
+      sdomin_s = sdm;
+      ndmax_s = ndm;
+      dlmax_s = dlm;
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t t0 = sh.tmem_base;
+  const uint32_t tKh = t0, tKl = t0 + 32, tVh = t0 + 64, tVl = t0 + 96, tdV = t0 + 128, tdK = t0 + 192,
+                 tS = t0 + 256;  // buffer b: S^T at tS + 128 b, dP^T at tS + 128 b + 64
+  if (warp < 8) {
+    const int row = tid & (kTcRows - 1);
+    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    if (warp < 4) {
+      kscale[row] = row_to_tmem16<HD>(k, k0 + row, rows, W, h, tKh + lane, tKl + lane);
+    } else {
+      vscale[row] = row_to_tmem16<HD>(v, k0 + row, rows, W, h, tVh + lane, tVl + lane);
+      float ss = 0.f;
+      if (k0 + row < rows) {
+#pragma unroll
+        for (int c = 0; c < HD; c += 4) {
+          const float4 x = __ldg(reinterpret_cast<const float4*>(v + (size_t)(k0 + row) * W + h * HD + c));
+          ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+        }
+      }
+      vnorm[row] = sqrtf(ss);
+    }
+    tc::tmem_st_wait();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+
+  if (tid < kTcCompute) {
+    // ---------------------------------------------------------- softmax
+    const int row = tid & (kTcRows - 1), half = tid >> 7;
+    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    const float scale2 = scale * 1.4426950408889634f / kscale[row];
+    const float vinv = 1.0f / vscale[row];
+    const float sqmin = sqmin_s, pv_e = 8192.0f * sdomin_s;
+    const float rk = tc::f16_scale((ndmax_s * vnorm[row] + dlmax_s) * scale);
+    const int kr = k0 + row;
+    const int ke = (kr / T + 1) * T;  // end of the key's sequence
+    const int kseq_end = (k0 / T + 1) * T;
+    const bool one_seq = (k0 + kTcRows - 1) / T == k0 / T && k0 + kTcRows <= rows;
+    bool done = false;
+    for (int i = 0; i < n; ++i) {
+      const int b = i & 1, st = i % NS;
+      const float2 ts = tscale[i];
+      const float coef = scale2 / ts.x;          // S^T_tmem -> log2 units
+      const float dcoef = vinv / ts.y;           // dP^T_tmem -> dP
+      const float pc = pv_e / ts.y;              // P -> stored P
+      const float gc = scale * rk * (sqmin / ts.x);  // (dP - delta) P -> stored dS
+      const float* hdr = reinterpret_cast<const float*>(sm8 + st * G::QTILE_BYTES + 8 * G::PART_BYTES);
+      const uint32_t tSb = tS + 128 * b;
+      F16_WAIT_OR_FAIL(&q_full[st], (i / NS) & 1);
+      F16_WAIT_OR_FAIL(&s_full[b], (i >> 1) & 1);
+      tc::fence_after_sync();
+      float pv[32];
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const int col = 32 * q2 + 16 * half;  // query columns [col, col + 16) of the step
+        float s[16];
+        tc::tmem_ld16(tSb + col + lane, s);
+        const int qh = k0 + i * kTcQ + col;
+        const bool full = one_seq && k0 + i * kTcQ + 32 * q2 >= k0 + kTcRows - 1 &&
+                          k0 + i * kTcQ + 32 * q2 + 32 <= min(kseq_end, rows);
+#pragma unroll
+        for (int c = 0; c < 16; c += 4) {
+          const float4 l4 = *reinterpret_cast<const float4*>(hdr + G::LSE + col + c);
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {
+            const float2 lv = u == 0 ? make_float2(l4.x, l4.y) : make_float2(l4.z, l4.w);
+            const int q0j = qh + c + u;
+            const float2 t = fma2(make_float2(s[c + u], s[c + u + 1]), splat2(coef), make_float2(-lv.x, -lv.y));
+            const bool ok0 = full || (q0j >= kr && q0j < ke && q0j < rows && kr < rows);
+            const bool ok1 = full || (q0j + 1 >= kr && q0j + 1 < ke && q0j + 1 < rows && kr < rows);
+            s[c + u] = ok0 ? ex2(t.x) : 0.f;
+            s[c + u + 1] = ok1 ? ex2(t.y) : 0.f;
+          }
+        }
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pv[16 * q2 + 2 * e] = s[2 * e];
+          pv[16 * q2 + 2 * e + 1] = s[2 * e + 1];
+          tc::split_f16x2(s[2 * e] * pc, s[2 * e + 1] * pc, hi[e], lo[e]);
+        }
+        tc::tmem_st8u(tSb + col + lane, hi);  // P^T over the S^T columns just read
+        tc::tmem_st8u(tSb + col + 8 + lane, lo);
+      }
+      tc::tmem_st_wait();
+      tc::fence_before_sync();
+      tc::bar_arrive(&p_full[b]);
+      F16_WAIT_OR_FAIL(&dp_full[b], (i >> 1) & 1);
+      tc::fence_after_sync();
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const int col = 32 * q2 + 16 * half;
+        float dp[16];
+        tc::tmem_ld16(tSb + 64 + col + lane, dp);
+#pragma unroll
+        for (int c = 0; c < 16; c += 4) {
+          const float4 e4 = *reinterpret_cast<const float4*>(hdr + G::DELTA + col + c);
+#pragma unroll
+          for (int u = 0; u < 4; u += 2) {
+            const float2 ev = u == 0 ? make_float2(e4.x, e4.y) : make_float2(e4.z, e4.w);
+            const float2 pp = make_float2(pv[16 * q2 + c + u], pv[16 * q2 + c + u + 1]);
+            const float2 g = mul2(pp, fma2(make_float2(dp[c + u], dp[c + u + 1]), splat2(dcoef),
+                                           make_float2(-ev.x, -ev.y)));
+            dp[c + u] = g.x;
+            dp[c + u + 1] = g.y;
+          }
+        }
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tc::split_f16x2(dp[2 * e] * gc, dp[2 * e + 1] * gc, hi[e], lo[e]);
+        tc::tmem_st8u(tSb + 64 + col + lane, hi);  // dS^T over the dP^T columns just read
+        tc::tmem_st8u(tSb + 64 + col + 8 + lane, lo);
+        tc::tmem_st_wait();
+        tc::fence_before_sync();
+        tc::bar_arrive(&ds_full[b][q2]);
+      }
+      if (i + 1 == n) done = true;
+    }
+    // dV and dK of the last step complete before the accumulators are read.
+    if (done && !tc::bar_wait(&g_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
+    tc::fence_after_sync();
+    if (done && !sh.failed) {
+      const bool in = kr < rows;
+      const float ov = 1.0f / pv_e, ok = 1.0f / (rk * sqmin);
+#pragma unroll
+      for (int c = 0; c < HD / 2; c += 16) {
+        const int col = (HD / 2) * half + c;
+        float gk[16], gv[16];
+        tc::tmem_ld16_pair(tdK + lane + col, gk, tdV + lane + col, gv);
+        if (in) {
+          const size_t base = (size_t)kr * W + h * HD + col;  // 16-float aligned
+          float4* dk4 = reinterpret_cast<float4*>(dk + base);
+          float4* dv4 = reinterpret_cast<float4*>(dv + base);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float4 a = make_float4(gv[4 * e] * ov, gv[4 * e + 1] * ov, gv[4 * e + 2] * ov, gv[4 * e + 3] * ov);
+            if (dv_add != nullptr) {
+              const float4 x = __ldg(reinterpret_cast<const float4*>(dv_add + base) + e);
+              a = make_float4(a.x + x.x, a.y + x.y, a.z + x.z, a.w + x.w);
+            }
+            dk4[e] = make_float4(gk[4 * e] * ok, gk[4 * e + 1] * ok, gk[4 * e + 2] * ok, gk[4 * e + 3] * ok);
+            dv4[e] = a;
+          }
+        }
+      }
+    }
+  } else if (tid == kTcProducer) {
+    // ---------------------------------------------------------- query tiles
+    for (int i = 0; i < n; ++i) {
+      const int st = i % NS;
+      if (i >= NS) {
+        F16_WAIT_OR_FAIL(&q_empty[st], ((i - NS) / NS) & 1);
+      }
+      tc::bar_expect_tx(&q_full[st], G::QTILE_BYTES);
+      tc::bulk_g2s(sm8 + st * G::QTILE_BYTES, qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES, G::QTILE_BYTES,
+                   &q_full[st]);
+    }
+  } else if (tid == kTcIssuer) {
+    // ---------------------------------------------------------- S^T / dP^T issuer
+    constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcQ);
+    for (int i = 0; i < n; ++i) {
+      const int st = i % NS, b = i & 1;
+      const uint8_t* stage = sm8 + st * G::QTILE_BYTES;
+      F16_WAIT_OR_FAIL(&q_full[st], (i / NS) & 1);
+      if (i >= 2) {
+        F16_WAIT_OR_FAIL(&g_done[b], ((i - 2) >> 1) & 1);  // dV and dK of step i-2 have read this buffer
+      }
+      tc::fence_after_sync();
+      const uint32_t tSb = tS + 128 * b;
+      mma16_tmem_a<HD, HD / 16>(tSb, tKh, tKl, stage + G::Q_HI * G::PART_BYTES,
+                                stage + (G::Q_HI + 1) * G::PART_BYTES, idS, false, 0);  // S^T = K Q^T
+      tc::commit(&s_full[b]);
+      mma16_tmem_a<HD, HD / 16>(tSb + 64, tVh, tVl, stage + G::D_HI * G::PART_BYTES,
+                                stage + (G::D_HI + 1) * G::PART_BYTES, idS, false, 0);  // dP^T = V dO^T
+      tc::commit(&dp_full[b]);
+    }
+  } else if (tid == kTcIssuer2) {
+    // ---------------------------------------------------------- dV / dK issuer
+    constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD);
+    for (int i = 0; i < n; ++i) {
+      const int st = i % NS, b = i & 1;
+      const uint8_t* stage = sm8 + st * G::QTILE_BYTES;
+      const uint32_t tSb = tS + 128 * b;
+      F16_WAIT_OR_FAIL(&q_full[st], (i / NS) & 1);
+      F16_WAIT_OR_FAIL(&p_full[b], (i >> 1) & 1);
+      tc::fence_after_sync();
+      // dV += P^T dO over the step's 64 queries (B = dO^T [HD][64 queries])
+      mma16_tmem_a_il<kTcQ, 4>(tdV, tSb, stage + G::DT_HI * G::PART_BYTES, stage + (G::DT_HI + 1) * G::PART_BYTES,
+                               idG, i > 0, 0);
+      bool okw = true;
+      for (int q2 = 0; q2 < 2 && okw; ++q2) {
+        okw = tc::bar_wait(&ds_full[b][q2], (i >> 1) & 1);
+        tc::fence_after_sync();
+        // dK += dS^T Q over queries [32 q2, 32 q2 + 32) (B = Q^T [HD][64 queries])
+        if (okw)
+          mma16_tmem_a_il<kTcQ, 2>(tdK, tSb + 64, stage + G::QT_HI * G::PART_BYTES,
+                                   stage + (G::QT_HI + 1) * G::PART_BYTES, idG, i > 0 || q2 > 0, 2 * q2);
+      }
+      if (!okw) {
+        sh.failed = 1;
+        break;
+      }
+      tc::commit(&g_done[b]);
+      tc::commit(&q_empty[st]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (sh.failed && tid == 0) atomicExch(err, 1);
+  if (warp == 0) tc::tmem_dealloc(t0, 512);
+}
+
 #undef F16_WAIT_OR_FAIL
 
 }  // namespace mb

@@ -234,14 +234,16 @@ struct AttentionOpsTc final : AttentionOps {
                                  (int)F16Att<HD>::smem_forward));
     MB_CUDA(cudaFuncSetAttribute(&attention_backward_dq_f16<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)F16Dq<HD>::smem));
-    MB_CUDA(cudaFuncSetAttribute(&attention_backward_dkdv_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)TcKv<HD>::smem));
+    MB_CUDA(cudaFuncSetAttribute(&attention_backward_dkdv_f16<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)F16Kv<HD>::smem));
   }
   // per block: the FP16 key tiles the forward and dQ read
   static size_t key_floats(int rows, int H) {
     return (size_t)H * ((rows + kTcK - 1) / kTcK) * F16Fmt<HD>::KTILE_BYTES / sizeof(float);
   }
-  static size_t query_floats(int rows, int H) { return (size_t)H * ((rows + kTcQ - 1) / kTcQ) * F::QTILE; }
+  static size_t query_floats(int rows, int H) {
+    return (size_t)H * ((rows + kTcQ - 1) / kTcQ) * F16Q<HD>::QTILE_BYTES / sizeof(float);
+  }
   // One query-tile set (rebuilt per backward block) and one key-tile set per
   // block: the forward formats every key part once and dQ reuses them.
   size_t scratch_floats(int rows, int H, int layers) const override {
@@ -249,7 +251,7 @@ struct AttentionOpsTc final : AttentionOps {
   }
   int forward_launches() const override { return 2; }   // key format + forward
   int backward_launches() const override { return 3; }  // query format + dK/dV, dQ
-  float* qfmt() const { return scratch; }
+  uint8_t* qfmt16() const { return reinterpret_cast<uint8_t*>(scratch); }
   uint8_t* kfmt16(int rows, int H) const {
     return reinterpret_cast<uint8_t*>(scratch + query_floats(rows, H) + (size_t)layer * key_floats(rows, H));
   }
@@ -268,11 +270,11 @@ struct AttentionOpsTc final : AttentionOps {
   void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                      const float* v, const float* dout, const float* lse, const float* delta, const float* dv_add,
                      float* dk, float* dv) override {
-    attention_format_queries<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), kFmtThreads, 0, s>>>(rows, W, q, dout, lse, delta,
-                                                                                   qfmt());
+    attention_format_queries_f16<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), kFmtThreads, 0, s>>>(rows, W, q, dout, lse,
+                                                                                           delta, qfmt16());
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dkdv_tc<HD><<<grid, kTcKvThreads, TcKv<HD>::smem, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), k, v,
-                                                                           qfmt(), dv_add, dk, dv, err);
+    attention_backward_dkdv_f16<HD><<<grid, kTcThreads2, F16Kv<HD>::smem, s>>>(
+        rows, W, T, 1.0f / sqrtf((float)hd), k, v, qfmt16(), dv_add, dk, dv, err);
   }
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
