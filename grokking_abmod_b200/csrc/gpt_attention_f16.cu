@@ -1,8 +1,10 @@
 // Causal flash attention on the sm_100a tensor cores with three-term FP16
-// products (tcgen05 kind::f16, "3xF16"; tc05.cuh): the same semantics and
-// statistics as gpt_attention_tc.cu's 3xTF32 kernels (the reference's FA2
-// kernels, src/gpt/gpu.rs:381-750) at twice the MMA rate and half the
-// operand bytes.
+// products (tcgen05 kind::f16, "3xF16"; tc05.cuh): softmax(Q K^T / sqrt(hd)) V
+// with a causal, same-sequence mask over the flattened token rows, base-2
+// LSE, and dQ and dK/dV as separate kernels (no atomics, bitwise
+// reproducible) - the semantics and statistics of the reference's FA2
+// kernels (src/gpt/gpu.rs:381-750) and of gpt_attention.cu's FP32 SIMT
+// kernels, at FP32-level accuracy with twice the MMA rate of 3xTF32.
 //
 // Scaling.  FP16 holds magnitudes in [2^-24, 65504], so every operand is
 // scaled by a power of two before it is split, and the scale is divided out
@@ -16,8 +18,87 @@
 //    and O = O_tmem / (C L).  c_j <= 2^7 keeps P c_j <= 2^15; a tile whose
 //    values are smaller than the largest by more than 2^7 has c_j < 1, which
 //    costs precision only in products far below the accumulated magnitude.
+//
+// Roles (every CTA): 8 compute warps (thread i < 128 owns TMEM lane / row i
+// with the first column half, thread 128 + i the second), a producer thread
+// that streams operand tiles into shared-memory rings with cp.async.bulk
+// (plain, no multicast; completion counted on mbarriers), and two MMA issuer
+// threads in separate warps, each committing its own MMAs to mbarriers, so
+// one issuer's waits overlap the other's MMAs.  All waits are bounded and
+// report through `err` instead of hanging.  Operand tiles are written once
+// per use by format passes in the unswizzled FP16 K-major layout of
+// tc05.cuh; operands needed with rows along N are stored transposed.  CTAs
+// are ordered by causal work, longest first.
+
+#include "common.cuh"
+#include "tc05.cuh"
 
 namespace mb {
+
+constexpr int kTcRows = 128;     // CTA tile rows = TMEM lanes
+constexpr int kTcK = 64;         // key-tile rows (forward, dQ)
+constexpr int kTcQ = 64;         // query-tile rows (dK/dV)
+constexpr int kTcCompute = 256;  // compute threads: row = tid % 128, column half = tid / 128
+// Forward and dQ: 8 compute warps, a producer warp (thread 256), and two MMA
+// issuers in separate warps (threads 288 and 320).
+constexpr int kTcProducer = 256, kTcIssuer = 288;
+constexpr int kTcThreads2 = 352, kTcIssuer2 = 320;
+
+constexpr int kFmtThreads = 256;  // threads of the format kernels
+
+// Rows [row0, row0 + R) of head h of two row-major [rows][W] tensors into
+// shared memory ([R][HD], stride HD + 2), zero past the last row.  Every
+// load of the thread is issued before the first store, so a CTA keeps all
+// of its 2 R HD floats in flight.
+template <int R, int HD>
+__device__ __forceinline__ void load_rows2(float* xa, const float* __restrict__ ga, float* xb,
+                                           const float* __restrict__ gb, int row0, int rows, int W, int h) {
+  constexpr int XS = HD + 2, PER = R * HD / 4 / kFmtThreads;
+  static_assert(PER * kFmtThreads * 4 == R * HD, "tile must split evenly over the threads");
+  float4 va[PER], vb[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = threadIdx.x + kFmtThreads * j, r = i / (HD / 4), c = (i % (HD / 4)) * 4, row = row0 + r;
+    const size_t off = (size_t)row * W + h * HD + c;
+    va[j] = row < rows ? __ldg(reinterpret_cast<const float4*>(ga + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    vb[j] = row < rows ? __ldg(reinterpret_cast<const float4*>(gb + off)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int i = threadIdx.x + kFmtThreads * j, r = i / (HD / 4), c = (i % (HD / 4)) * 4;
+    float* a = xa + r * XS + c;
+    float* b = xb + r * XS + c;
+    a[0] = va[j].x, a[1] = va[j].y, a[2] = va[j].z, a[3] = va[j].w;
+    b[0] = vb[j].x, b[1] = vb[j].y, b[2] = vb[j].z, b[3] = vb[j].w;
+  }
+}
+
+// The 128-row tile CTA b works on, ordered by causal work (most first) so the
+// last wave of the grid holds the shortest CTAs.  With sequences made of
+// whole tiles, all sequences' tiles at one position come together; a query
+// tile's work grows with its position (more keys before it), a key tile's
+// shrinks (fewer queries after it).  Other shapes keep a plain order.
+__device__ __forceinline__ int tile_by_work(int b, int nt, int rows, int T, bool queries) {
+  if (T % kTcRows != 0 || rows % T != 0) return queries ? nt - 1 - b : b;
+  const int per_seq = T / kTcRows, nseq = nt / per_seq;
+  const int i = b / nseq, seq = b % nseq;
+  return seq * per_seq + (queries ? per_seq - 1 - i : i);
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Named barrier over the 256 compute threads.
+__device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+struct TcShared {
+  uint32_t tmem_base;
+  int failed;
+};
+
 
 // Inside a role loop: a wait that gives up marks the CTA failed and leaves.
 #define F16_WAIT_OR_FAIL(bar, parity)    \
@@ -31,7 +112,7 @@ struct F16Fmt {
   static constexpr int PART_BYTES = kTcK * HD * 2;  // one 64 x HD FP16 part
   static constexpr int HEADER_BYTES = 128;          // scales (and room to keep tiles 128-byte aligned)
   static constexpr int KTILE_BYTES = 8 * PART_BYTES + HEADER_BYTES;
-  // parts: K, K', Vt, Vt', V, V', Kt, Kt' (TcFmt's order); header floats:
+  // parts: K, K', Vt, Vt', V, V', Kt, Kt'; header floats:
   // s_k, s_v, the largest row norm of V, the largest |V|
   static constexpr int K_HI = 0, VT_HI = 2, V_HI = 4, KT_HI = 6;
 };

@@ -33,7 +33,6 @@
 
 #include "gpt_attention.cu"
 #include "gpt_blocks.cu"
-#include "gpt_attention_tc.cu"
 #include "gpt_attention_f16.cu"
 #include "gpt_head.cu"
 
@@ -223,11 +222,9 @@ struct AttentionOpsD final : AttentionOps {
   }
 };
 
-// Tensor-core (tcgen05, 3xTF32) attention for head widths 32 and 64.
+// Tensor-core (tcgen05, 3xF16) attention for head widths 32 and 64.
 template <int HD>
 struct AttentionOpsTc final : AttentionOps {
-  using K = TcAtt<HD>;
-  using F = TcFmt<HD>;
   int* err;
   explicit AttentionOpsTc(int* e) : err(e) {
     MB_CUDA(cudaFuncSetAttribute(&attention_forward_f16<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
