@@ -21,6 +21,11 @@ struct Error : std::runtime_error {
 inline void require(bool ok, const std::string& message, int code = MB_ERR_INVALID) {
   if (!ok) throw Error(code, message);
 }
+// The same for a literal message: nothing is built unless the check fails,
+// so per-element validation loops cost a compare and a branch.
+inline void require(bool ok, const char* message, int code = MB_ERR_INVALID) {
+  if (!ok) throw Error(code, message);
+}
 
 inline void need(const void* p, const char* what) { require(p != nullptr, std::string(what) + " must not be null"); }
 

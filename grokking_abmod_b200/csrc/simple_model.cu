@@ -1434,48 +1434,72 @@ namespace simple {
 // Device index buffers kept by a model for its uploaded batches.  A batch
 // set takes a buffer from the pool and gives it back when destroyed, so the
 // per-epoch upload of the reference's training loop (one per step at full
-// batch) allocates nothing once the pool holds a buffer of that size.  The
-// pool outlives the model while batch sets still hold buffers.  Buffers are
-// only written by copies on the model's stream, in order after every step
-// that read them before.
+// batch) allocates nothing once the pool holds a buffer of that size.  Each
+// buffer has a page-locked staging copy: the caller's indices are copied
+// there on the host and then to the device asynchronously (a copy from
+// pageable memory may wait for the stream, which would serialise the host
+// with every queued step); an event recorded after that copy guards the
+// staging buffer's next reuse.  The pool outlives the model while batch sets
+// still hold buffers.  Device buffers are only written by copies on the
+// model's stream, in order after every step that read them before.
+struct IndexBuffer {
+  uint32_t* dev = nullptr;
+  uint32_t* host = nullptr;
+  size_t capacity = 0;
+  cudaEvent_t copied = nullptr;
+};
+
 class IndexPool {
  public:
   explicit IndexPool(int device) : device_(device) {}
   ~IndexPool() {
     cudaSetDevice(device_);
-    for (auto& kv : free_) cudaFree(kv.second);
+    for (auto& kv : free_) release(kv.second);
   }
-  uint32_t* take(size_t count, size_t* capacity) {
+  IndexBuffer take(size_t count) {
     {
       std::lock_guard<std::mutex> lock(mu_);
       auto it = free_.lower_bound(count);
       if (it != free_.end() && it->first <= 2 * count + 4096) {
-        uint32_t* p = it->second;
-        *capacity = it->first;
+        IndexBuffer b = it->second;
         free_.erase(it);
-        return p;
+        return b;
       }
     }
-    void* p = nullptr;
-    SIMPLE_CUDA(cudaMalloc(&p, count * sizeof(uint32_t)));
-    *capacity = count;
-    return static_cast<uint32_t*>(p);
+    IndexBuffer b;
+    b.capacity = count;
+    SIMPLE_CUDA(cudaMalloc(&b.dev, count * sizeof(uint32_t)));
+    cudaError_t e = cudaHostAlloc(&b.host, count * sizeof(uint32_t), cudaHostAllocDefault);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&b.copied, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      release(b);
+      throw Error(MB_ERR_CUDA, std::string("index staging buffer: ") + cudaGetErrorString(e));
+    }
+    return b;
   }
-  void give(uint32_t* p, size_t capacity) {
+  void give(const IndexBuffer& b) {
     std::lock_guard<std::mutex> lock(mu_);
-    free_.emplace(capacity, p);
+    free_.emplace(b.capacity, b);
     while (free_.size() > 8) {  // keep a few: the largest go first
       auto last = std::prev(free_.end());
       cudaSetDevice(device_);
-      cudaFree(last->second);
+      release(last->second);
       free_.erase(last);
     }
   }
 
  private:
+  static void release(const IndexBuffer& b) {
+    if (b.copied) {
+      cudaEventSynchronize(b.copied);
+      cudaEventDestroy(b.copied);
+    }
+    if (b.host) cudaFreeHost(b.host);
+    if (b.dev) cudaFree(b.dev);
+  }
   int device_;
   std::mutex mu_;
-  std::multimap<size_t, uint32_t*> free_;
+  std::multimap<size_t, IndexBuffer> free_;
 };
 }  // namespace simple
 }  // namespace mb
@@ -1484,10 +1508,10 @@ struct mb_simple_batches {
   const void* owner;
   size_t count, table_rows;
   std::shared_ptr<mb::simple::IndexPool> pool;
-  size_t capacity = 0;
+  mb::simple::IndexBuffer buf;
   uint32_t* idx = nullptr;
   ~mb_simple_batches() {
-    if (idx != nullptr) pool->give(idx, capacity);
+    if (idx != nullptr) pool->give(buf);
   }
 };
 
@@ -1520,6 +1544,9 @@ class SimpleModel {
     grad_ = mem_.alloc<float>(P_);
     flags_ = mem_.alloc<int>(kFlags);
     scalars_ = mem_.alloc<StepScalars>(1);
+    SIMPLE_CUDA(cudaHostAlloc((void**)&host_scalars_, kScalarSlots * sizeof(StepScalars), cudaHostAllocDefault));
+    for (int i = 0; i < kScalarSlots; ++i)
+      SIMPLE_CUDA(cudaEventCreateWithFlags(&scalar_copied_[i], cudaEventDisableTiming));
     SIMPLE_CUDA(cudaMemsetAsync(flags_, 0, kFlags * sizeof(int), stream_));
     SIMPLE_CUDA(cudaMemsetAsync(grad_, 0, P_ * sizeof(float), stream_));
     // Strides per mesh layer (mesh stacks) or per core layer (shared-Neighbor).
@@ -1557,6 +1584,10 @@ class SimpleModel {
   }
   ~SimpleModel() {
     workspaces_.clear();
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (cudaEvent_t e : scalar_copied_)
+      if (e) cudaEventDestroy(e);
+    if (host_scalars_) cudaFreeHost(host_scalars_);
     if (stream_) cudaStreamDestroy(stream_);
   }
 
@@ -1615,10 +1646,15 @@ class SimpleModel {
     bt->count = count;
     bt->table_rows = table->rows;
     bt->pool = index_pool_;
-    bt->idx = index_pool_->take(count, &bt->capacity);
-    // Ordered on the model's stream after every step that read a recycled
-    // buffer; the host indices may be reused as soon as this returns.
-    SIMPLE_CUDA(cudaMemcpyAsync(bt->idx, idx, count * 4, cudaMemcpyHostToDevice, stream_));
+    bt->buf = index_pool_->take(count);
+    bt->idx = bt->buf.dev;
+    // The staging copy's previous transfer has completed; the device copy is
+    // ordered on the model's stream after every step that read a recycled
+    // buffer, and the caller's indices may be reused as soon as this returns.
+    SIMPLE_CUDA(cudaEventSynchronize(bt->buf.copied));
+    std::memcpy(bt->buf.host, idx, count * 4);
+    SIMPLE_CUDA(cudaMemcpyAsync(bt->idx, bt->buf.host, count * 4, cudaMemcpyHostToDevice, stream_));
+    SIMPLE_CUDA(cudaEventRecord(bt->buf.copied, stream_));
     return bt.release();
   }
 
@@ -1646,8 +1682,13 @@ class SimpleModel {
     s.epsilon = o.epsilon;
     s.correction1 = 1.0f - beta1_power_;
     s.correction2 = 1.0f - beta2_power_;
-    // Pageable source: the copy has consumed `s` when the call returns.
-    SIMPLE_CUDA(cudaMemcpyAsync(scalars_, &s, sizeof(s), cudaMemcpyHostToDevice, stream_));
+    // Through a ring of page-locked slots, so the copy does not wait for the
+    // stream; a slot is rewritten once its copy of kScalarSlots steps ago is done.
+    const int slot = (int)(scalar_step_++ % kScalarSlots);
+    SIMPLE_CUDA(cudaEventSynchronize(scalar_copied_[slot]));
+    host_scalars_[slot] = s;
+    SIMPLE_CUDA(cudaMemcpyAsync(scalars_, host_scalars_ + slot, sizeof(s), cudaMemcpyHostToDevice, stream_));
+    SIMPLE_CUDA(cudaEventRecord(scalar_copied_[slot], stream_));
     if (ws.step_graph == nullptr) {
       cudaGraph_t g = nullptr;
       SIMPLE_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
@@ -2373,6 +2414,10 @@ class SimpleModel {
   FmLayer* fm_layers_ = nullptr;  // full mesh layer descriptors
   int fm_z_ = 0;                  // full mesh pre-activation floats per row (all but the readout)
   StepScalars* scalars_;
+  static constexpr int kScalarSlots = 16;
+  StepScalars* host_scalars_ = nullptr;  // page-locked [kScalarSlots]
+  cudaEvent_t scalar_copied_[kScalarSlots] = {};
+  uint64_t scalar_step_ = 0;
   float beta1_power_ = 1.0f, beta2_power_ = 1.0f;
   std::vector<std::unique_ptr<Workspace>> workspaces_;
   std::shared_ptr<IndexPool> index_pool_;

@@ -131,7 +131,10 @@ class DeviceTable:
 
     def __del__(self):
         if getattr(self, "_handle", None):
-            _lib.load().mb_simple_table_destroy(self._handle)
+            try:
+                _lib.load().mb_simple_table_destroy(self._handle)
+            except TypeError:  # interpreter shutdown: the library is already gone
+                pass
             self._handle = None
 
 
@@ -146,7 +149,10 @@ class DeviceBatches:
 
     def __del__(self):
         if getattr(self, "_handle", None):
-            _lib.load().mb_simple_batches_destroy(self._handle)
+            try:
+                _lib.load().mb_simple_batches_destroy(self._handle)
+            except TypeError:  # interpreter shutdown: the library is already gone
+                pass
             self._handle = None
 
 
