@@ -279,7 +279,9 @@ int mb_op_adamw(float* weights, float* m, float* v, const float* gradient, size_
  * with that device current; make that first call before any stream capture.
  * All calls share the array: every partial a call reads is written by the
  * same call first, so nothing needs clearing, but calls that overlap on the
- * GPU (other streams, other threads) race on it and must be serialised. */
+ * GPU (other streams, other threads) race on it and must be serialised.
+ * The looked-up address is kept for the life of the process: after a
+ * cudaDeviceReset of a device, do not call this entry point on it again. */
 int mb_op_mesh_backward_noalloc(const float* x, const float* dy, float* dx, float* dweights, size_t rows,
                                 uint32_t width, uint32_t depth, uint32_t connectivity, const float* weights,
                                 void* stream);
