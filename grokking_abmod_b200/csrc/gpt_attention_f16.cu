@@ -43,6 +43,9 @@ constexpr int kTcCompute = 256;  // compute threads: row = tid % 128, column hal
 // issuers in separate warps (threads 288 and 320).
 constexpr int kTcProducer = 256, kTcIssuer = 288;
 constexpr int kTcThreads2 = 352, kTcIssuer2 = 320;
+// dK/dV: 16 compute warps (row = tid % 128, 16-query column block =
+// tid / 128), a producer warp (thread 512) and two issuers (544, 576).
+constexpr int kKvCompute = 512, kKvProducer = 512, kKvIssuer = 544, kKvIssuer2 = 576, kKvThreads = 608;
 
 constexpr int kFmtThreads = 256;  // threads of the format kernels
 
@@ -199,21 +202,71 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_keys_f16(int row
     *reinterpret_cast<float4*>(tile + 8 * F::PART_BYTES) = make_float4(sk, sv, nv, mv);
 }
 
-// This thread's row (HD floats) of head h split into FP16 hi/lo TMEM columns
-// (HD / 2 packed columns each) with a per-row scale, which it returns.
+// A CTA's 128 rows of one head in shared memory as float4 chunks, chunk c of
+// row r at r C4 + (c ^ (r % C4)): a thread walking its own row and a warp
+// walking consecutive chunks both hit distinct banks.  The row blocks move
+// between global memory and shared memory with coalesced float4 accesses
+// (consecutive threads, consecutive chunks of a row) and between shared
+// memory and TMEM one row per thread.
 template <int HD>
-__device__ __forceinline__ float row_to_tmem16(const float* __restrict__ g, int row, int rows, int W, int h,
-                                               uint32_t thi, uint32_t tlo) {
+struct RowBlock {
+  static constexpr int C4 = HD / 4;
+  static constexpr int CHUNKS = kTcRows * C4;
+  static constexpr size_t BYTES = (size_t)CHUNKS * sizeof(float4);
+  __device__ static int at(int r, int c) { return r * C4 + (c ^ (r & (C4 - 1))); }
+};
+
+template <int ID, int NT>
+__device__ __forceinline__ void named_sync() {
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(NT) : "memory");
+}
+
+// Rows [r0, r0 + 128) of head h of one or two row-major [rows][W] tensors
+// into row blocks by NT threads (this one is t); rows past `rows` read as 0.
+// Every load of the thread is issued before its first store.
+template <int HD, int NT, bool TWO>
+__device__ __forceinline__ void stage_rows(float4* da, const float* __restrict__ ga, float4* db,
+                                           const float* __restrict__ gb, int r0, int rows, int W, int h, int t) {
+  using B = RowBlock<HD>;
+  constexpr int PER = B::CHUNKS / NT;
+  static_assert(PER * NT == B::CHUNKS, "row block must split evenly over the threads");
+  float4 va[PER], vb[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int f = t + j * NT, r = f / B::C4, c = f % B::C4, row = r0 + r;
+    const size_t off = (size_t)row * W + h * HD + 4 * c;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    va[j] = row < rows ? __ldg(reinterpret_cast<const float4*>(ga + off)) : z;
+    if (TWO) vb[j] = row < rows ? __ldg(reinterpret_cast<const float4*>(gb + off)) : z;
+  }
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int f = t + j * NT, r = f / B::C4, c = f % B::C4;
+    da[B::at(r, c)] = va[j];
+    if (TWO) db[B::at(r, c)] = vb[j];
+  }
+}
+
+// Row r of a row block split into FP16 hi/lo TMEM columns (HD / 2 packed
+// columns each) with a per-row scale, which it returns; `norm` receives the
+// row's Euclidean norm.
+template <int HD>
+__device__ __forceinline__ float block_row_to_tmem16(const float4* blk, int r, uint32_t thi, uint32_t tlo,
+                                                     float& norm) {
+  using B = RowBlock<HD>;
   float x[HD];
 #pragma unroll
-  for (int c = 0; c < HD; c += 4) {
-    const float4 v = row < rows ? __ldg(reinterpret_cast<const float4*>(g + (size_t)row * W + h * HD + c))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-    x[c] = v.x, x[c + 1] = v.y, x[c + 2] = v.z, x[c + 3] = v.w;
+  for (int c = 0; c < B::C4; ++c) {
+    const float4 v = blk[B::at(r, c)];
+    x[4 * c] = v.x, x[4 * c + 1] = v.y, x[4 * c + 2] = v.z, x[4 * c + 3] = v.w;
   }
-  float m = 0.f;
+  float m = 0.f, ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < HD; ++c) m = fmaxf(m, fabsf(x[c]));
+  for (int c = 0; c < HD; ++c) {
+    m = fmaxf(m, fabsf(x[c]));
+    ss += x[c] * x[c];
+  }
+  norm = sqrtf(ss);
   const float s = tc::f16_scale(m);
 #pragma unroll
   for (int c = 0; c < HD; c += 32) {
@@ -224,6 +277,38 @@ __device__ __forceinline__ float row_to_tmem16(const float* __restrict__ g, int 
     tc::tmem_st16u(tlo + c / 2, lo);
   }
   return s;
+}
+
+// 16 values of row r, columns [c0, c0 + 16), times `mul` into a row block.
+template <int HD>
+__device__ __forceinline__ void block_put16(float4* blk, int r, int c0, const float (&v)[16], float mul) {
+  using B = RowBlock<HD>;
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    blk[B::at(r, c0 / 4 + e)] = make_float4(v[4 * e] * mul, v[4 * e + 1] * mul, v[4 * e + 2] * mul, v[4 * e + 3] * mul);
+}
+
+// A row block out to rows [r0, r0 + 128) of head h of a row-major [rows][W]
+// tensor (plus `add`, same layout, when given) by NT threads.
+template <int HD, int NT>
+__device__ __forceinline__ void write_rows(float* __restrict__ g, const float4* blk, const float* __restrict__ add,
+                                           int r0, int rows, int W, int h, int t) {
+  using B = RowBlock<HD>;
+  constexpr int PER = B::CHUNKS / NT;
+  static_assert(PER * NT == B::CHUNKS, "row block must split evenly over the threads");
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int f = t + j * NT, r = f / B::C4, c = f % B::C4, row = r0 + r;
+    if (row < rows) {
+      const size_t off = (size_t)row * W + h * HD + 4 * c;
+      float4 v = blk[B::at(r, c)];
+      if (add != nullptr) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(add + off));
+        v = make_float4(v.x + a.x, v.y + a.y, v.z + a.z, v.w + a.w);
+      }
+      *reinterpret_cast<float4*>(g + off) = v;
+    }
+  }
 }
 
 // D (+)= A . B^T with A = FP16 hi/lo TMEM columns and B a K-major FP16 hi/lo
@@ -261,7 +346,8 @@ struct F16Att {
   using F = F16Fmt<HD>;
   static constexpr int FWD_STAGES = 4;
   static constexpr int FWD_STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', Vt, Vt'
-  static constexpr size_t smem_forward = (size_t)FWD_STAGES * FWD_STAGE_BYTES;
+  static constexpr size_t ROWS_OFF = (size_t)FWD_STAGES * FWD_STAGE_BYTES;  // Q row block, later O
+  static constexpr size_t smem_forward = ROWS_OFF + RowBlock<HD>::BYTES;
 };
 
 // ------------------------------------------------------------------ forward
@@ -332,10 +418,17 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   const uint32_t t0 = sh.tmem_base;
   // P buffer b: hi at tP + 64 b, lo at tP + 64 b + 32
   const uint32_t tQh = t0, tQl = t0 + 32, tS = t0 + 64, tP = t0 + 192, tO = t0 + 320;
-  if (warp < 4) {
-    const uint32_t lane = (uint32_t)(warp * 32) << 16;
-    qscale[tid] = row_to_tmem16<HD>(q, q0 + tid, rows, W, h, tQh + lane, tQl + lane);
-    tc::tmem_st_wait();
+  if (tid < kTcCompute) {
+    // Q rows through shared memory into TMEM with per-row scales.
+    float4* bq = reinterpret_cast<float4*>(sm8 + A::ROWS_OFF);
+    stage_rows<HD, kTcCompute, false>(bq, q, nullptr, nullptr, q0, rows, W, h, tid);
+    named_sync<2, kTcCompute>();
+    if (warp < 4) {
+      const uint32_t lane = (uint32_t)(warp * 32) << 16;
+      float nrm;
+      qscale[tid] = block_row_to_tmem16<HD>(bq, tid, tQh + lane, tQl + lane, nrm);
+      tc::tmem_st_wait();
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -434,22 +527,21 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       const float L = xl[0][row] * f0 + xl[1][row] * f1;
       const float inv = L > 0.f ? 1.0f / (L * pv_c) : 0.f;
       const uint32_t o0 = tO + lane, o1 = tO + 64 + lane;
+      float4* bo = reinterpret_cast<float4*>(sm8 + A::ROWS_OFF);  // O through the Q row block
 #pragma unroll
       for (int c = 0; c < HD / 2; c += 16) {
         const int col = (HD / 2) * half + c;
         float a[16], bb[16];
         tc::tmem_ld16_pair(o0 + col, a, o1 + col, bb);
-        if (qr < rows) {
-          float4* dst = reinterpret_cast<float4*>(o + (size_t)qr * W + h * HD + col);
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            dst[e] = make_float4((a[4 * e] * f0 + bb[4 * e] * f1) * inv, (a[4 * e + 1] * f0 + bb[4 * e + 1] * f1) * inv,
-                                 (a[4 * e + 2] * f0 + bb[4 * e + 2] * f1) * inv,
-                                 (a[4 * e + 3] * f0 + bb[4 * e + 3] * f1) * inv);
-        }
+        for (int e = 0; e < 16; ++e) a[e] = a[e] * f0 + bb[e] * f1;
+        block_put16<HD>(bo, row, col, a, inv);
       }
       if (qr < rows && half == 0) lse2[(size_t)h * rows + qr] = mt + log2f(L);
     }
+    named_sync<2, kTcCompute>();
+    if (done && !sh.failed)
+      write_rows<HD, kTcCompute>(o, reinterpret_cast<const float4*>(sm8 + A::ROWS_OFF), nullptr, q0, rows, W, h, tid);
   } else if (tid == kTcProducer) {
     // ---------------------------------------------------------- producer
     for (int j = 0; j < n; ++j) {
@@ -526,7 +618,8 @@ struct F16Dq {
   using F = F16Fmt<HD>;
   static constexpr int STAGES = 3;
   static constexpr int STAGE_BYTES = 6 * F::PART_BYTES;  // K, K', V, V', Kt, Kt'
-  static constexpr size_t smem = (size_t)STAGES * STAGE_BYTES;
+  static constexpr size_t ROWS_OFF = (size_t)STAGES * STAGE_BYTES;  // Q and dO row blocks, later dQ
+  static constexpr size_t smem = ROWS_OFF + 2 * RowBlock<HD>::BYTES;
 };
 
 // D (+)= A . B^T over K steps [s0, s0 + NSTEP) of 16 elements with A's FP16
@@ -546,7 +639,7 @@ __device__ __forceinline__ void mma16_tmem_a_il(uint32_t d, uint32_t a, const vo
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kTcThreads2, 1)
+__global__ void __launch_bounds__(kKvThreads, 1)
     attention_backward_dq_f16(int rows, int W, int T, float scale, const float* __restrict__ q,
                               const float* __restrict__ dout, const uint8_t* __restrict__ kfmt,
                               const float* __restrict__ lse2, const float* __restrict__ delta,
@@ -577,14 +670,14 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
     }
     for (int b = 0; b < 2; ++b) {
       tc::bar_init(&s_full[b], 1);
-      tc::bar_init(&d_full[b][0], kTcCompute);
-      tc::bar_init(&d_full[b][1], kTcCompute);
+      tc::bar_init(&d_full[b][0], kKvCompute / 2);
+      tc::bar_init(&d_full[b][1], kKvCompute / 2);
       tc::bar_init(&q_done[b], 1);
     }
     tc::bar_init_fence();
     sh.failed = 0;
   }
-  if (warp == 8) {
+  if (warp == kKvProducer / 32) {
     float kmin = INFINITY, vnorm = 0.f;
     for (int j = threadIdx.x & 31; j < n; j += 32) {
       const float4 hd4 = __ldg(reinterpret_cast<const float4*>(kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES +
@@ -609,30 +702,34 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   const uint32_t t0 = sh.tmem_base;
   // buffer b: S at tS + 128 b (later dS, interleaved), dP at tS + 128 b + 64
   const uint32_t tQh = t0, tQl = t0 + 32, tDh = t0 + 64, tDl = t0 + 96, tS = t0 + 128, tG = t0 + 384;
-  if (warp < 4) {
-    const uint32_t lane = (uint32_t)(warp * 32) << 16;
-    qscale[tid] = row_to_tmem16<HD>(q, q0 + tid, rows, W, h, tQh + lane, tQl + lane);
-    oscale[tid] = row_to_tmem16<HD>(dout, q0 + tid, rows, W, h, tDh + lane, tDl + lane);
-    // |dO_row| for the dS bound
-    float ss = 0.f;
-    const int r = q0 + tid;
-    if (r < rows) {
-#pragma unroll
-      for (int c = 0; c < HD; c += 4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(dout + (size_t)r * W + h * HD + c));
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  if (tid < kKvCompute) {
+    // Q and dO rows through shared memory into TMEM with per-row scales.
+    using B = RowBlock<HD>;
+    float4* bq = reinterpret_cast<float4*>(sm8 + A::ROWS_OFF);
+    float4* bo = bq + B::CHUNKS;
+    stage_rows<HD, kKvCompute, true>(bq, q, bo, dout, q0, rows, W, h, tid);
+    named_sync<2, kKvCompute>();
+    if (warp < 8) {
+      const int row = tid & (kTcRows - 1);
+      const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+      float nrm;
+      if (warp < 4) {
+        qscale[row] = block_row_to_tmem16<HD>(bq, row, tQh + lane, tQl + lane, nrm);
+      } else {
+        oscale[row] = block_row_to_tmem16<HD>(bo, row, tDh + lane, tDl + lane, nrm);
+        gscale[row] = tc::f16_scale(2.0f * nrm * vnorm_s * scale);  // |dO_row| bounds dS
       }
+      tc::tmem_st_wait();
     }
-    gscale[tid] = tc::f16_scale(2.0f * sqrtf(ss) * vnorm_s * scale);
-    tc::tmem_st_wait();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
 
-  if (tid < kTcCompute) {
-    // Thread (row, half) handles key columns [16 half, +16) of each 32-key half.
-    const int row = tid & (kTcRows - 1), half = tid >> 7;
+  if (tid < kKvCompute) {
+    // Thread (row, quarter) handles key columns [16 quarter, +16) of each step.
+    const int row = tid & (kTcRows - 1), quarter = tid >> 7;
+    const int col = 16 * quarter;
     const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
     const float sq_inv = 1.0f / qscale[row], so_inv = 1.0f / oscale[row], rg = gscale[row];
     const float scale2 = scale * 1.4426950408889634f * sq_inv;
@@ -654,12 +751,11 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       F16_WAIT_OR_FAIL(&s_full[b], (j >> 1) & 1);
       tc::fence_after_sync();
       const int kt = kbeg + j * kTcK;
-      for (int k2 = 0; k2 < 2; ++k2) {
-        const int col = 32 * k2 + 16 * half;
+      {
         float s[16], dp[16];
         tc::tmem_ld16_pair(tSb + col + lane, s, tSb + 64 + col + lane, dp);
-        const bool full = one_seq && kt + 32 * k2 >= seq0 && kt + 32 * k2 + 31 <= q0;
         const int kh = kt + col;
+        const bool full = one_seq && kh >= seq0 && kh + 15 <= q0;
 #pragma unroll
         for (int c = 0; c < 16; c += 2) {
           const float2 t = fma2(make_float2(s[c], s[c + 1]), splat2(coef), splat2(-L));
@@ -677,28 +773,26 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
         tc::tmem_st8u(tSb + col + 8 + lane, lo);
         tc::tmem_st_wait();
         tc::fence_before_sync();
-        tc::bar_arrive(&d_full[b][k2]);
+        tc::bar_arrive(&d_full[b][quarter >> 1]);  // key columns [0, 32) or [32, 64)
       }
       if (j + 1 == n) done = true;
     }
     if (done && !tc::bar_wait(&q_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
     tc::fence_after_sync();
-    if (done && !sh.failed) {
+    // dQ through the Q row block into coalesced row stores.
+    float4* bq = reinterpret_cast<float4*>(sm8 + A::ROWS_OFF);
+    const bool ok_out = done && !sh.failed;
+    if (ok_out) {
       const float out = 1.0f / (rg * kmin);
-#pragma unroll
-      for (int c = 0; c < HD / 2; c += 16) {
-        const int col = (HD / 2) * half + c;
+      for (int oc = col; oc < HD; oc += 64) {  // 16-column chunks of dQ
         float gv[16];
-        tc::tmem_ld16(tG + lane + col, gv);
-        if (in) {
-          float4* dst = reinterpret_cast<float4*>(dq + (size_t)qr * W + h * HD + col);
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            dst[e] = make_float4(gv[4 * e] * out, gv[4 * e + 1] * out, gv[4 * e + 2] * out, gv[4 * e + 3] * out);
-        }
+        tc::tmem_ld16(tG + lane + oc, gv);
+        block_put16<HD>(bq, row, oc, gv, out);
       }
     }
-  } else if (tid == kTcProducer) {
+    named_sync<2, kKvCompute>();
+    if (ok_out) write_rows<HD, kKvCompute>(dq, bq, nullptr, q0, rows, W, h, tid);
+  } else if (tid == kKvProducer) {
     for (int j = 0; j < n; ++j) {
       const int st = j % NS;
       if (j >= NS) {
@@ -710,7 +804,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       tc::bulk_g2s(stage, tile, 2 * F::PART_BYTES, &kv_full[st]);                                          // K, K'
       tc::bulk_g2s(stage + 2 * F::PART_BYTES, tile + 4 * F::PART_BYTES, 4 * F::PART_BYTES, &kv_full[st]);  // V, V', Kt, Kt'
     }
-  } else if (tid == kTcIssuer) {
+  } else if (tid == kKvIssuer) {
     // ---------------------------------------------------------- S / dP issuer
     constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
     for (int j = 0; j < n; ++j) {
@@ -728,7 +822,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
                                 false, 0);  // dP_j = dO V_j^T
       tc::commit(&s_full[b]);
     }
-  } else if (tid == kTcIssuer2) {
+  } else if (tid == kKvIssuer2) {
     // ---------------------------------------------------------- dQ issuer
     constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD);
     for (int j = 0; j < n; ++j) {
@@ -860,7 +954,7 @@ struct F16Kv {
 };
 
 template <int HD>
-__global__ void __launch_bounds__(kTcThreads2, 1)
+__global__ void __launch_bounds__(kKvThreads, 1)
     attention_backward_dkdv_f16(int rows, int W, int T, float scale, const float* __restrict__ k,
                                 const float* __restrict__ v, const uint8_t* __restrict__ qfmt,
                                 const float* __restrict__ dv_add, float* __restrict__ dk, float* __restrict__ dv,
@@ -890,15 +984,15 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
     for (int b = 0; b < 2; ++b) {
       tc::bar_init(&s_full[b], 1);
       tc::bar_init(&dp_full[b], 1);
-      tc::bar_init(&p_full[b], kTcCompute);
-      tc::bar_init(&ds_full[b][0], kTcCompute);
-      tc::bar_init(&ds_full[b][1], kTcCompute);
+      tc::bar_init(&p_full[b], kKvCompute);
+      tc::bar_init(&ds_full[b][0], kKvCompute / 2);
+      tc::bar_init(&ds_full[b][1], kKvCompute / 2);
       tc::bar_init(&g_done[b], 1);
     }
     tc::bar_init_fence();
     sh.failed = 0;
   }
-  if (warp == 8) {
+  if (warp == kKvProducer / 32) {
     float sqm = INFINITY, sdm = INFINITY, ndm = 0.f, dlm = 0.f;
     for (int i = threadIdx.x & 31; i < n; i += 32) {
       const float4 sc = __ldg(reinterpret_cast<const float4*>(qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES +
@@ -929,32 +1023,42 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   const uint32_t t0 = sh.tmem_base;
   const uint32_t tKh = t0, tKl = t0 + 32, tVh = t0 + 64, tVl = t0 + 96, tdV = t0 + 128, tdK = t0 + 192,
                  tS = t0 + 256;  // buffer b: S^T at tS + 128 b, dP^T at tS + 128 b + 64
-  if (warp < 8) {
-    const int row = tid & (kTcRows - 1);
-    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
-    if (warp < 4) {
-      kscale[row] = row_to_tmem16<HD>(k, k0 + row, rows, W, h, tKh + lane, tKl + lane);
-    } else {
-      vscale[row] = row_to_tmem16<HD>(v, k0 + row, rows, W, h, tVh + lane, tVl + lane);
-      float ss = 0.f;
-      if (k0 + row < rows) {
-#pragma unroll
-        for (int c = 0; c < HD; c += 4) {
-          const float4 x = __ldg(reinterpret_cast<const float4*>(v + (size_t)(k0 + row) * W + h * HD + c));
-          ss += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
-        }
+  if (tid < kKvCompute) {
+    // K and V rows through the last ring stage (its query tile is issued
+    // after this) into TMEM, split with per-row scales.
+    using B = RowBlock<HD>;
+    float4* bk = reinterpret_cast<float4*>(sm8 + (NS - 1) * G::QTILE_BYTES);
+    float4* bv = bk + B::CHUNKS;
+    stage_rows<HD, kKvCompute, true>(bk, k, bv, v, k0, rows, W, h, tid);
+    named_sync<2, kKvCompute>();
+    if (warp < 8) {
+      const int row = tid & (kTcRows - 1);
+      const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+      float nrm;
+      if (warp < 4) {
+        kscale[row] = block_row_to_tmem16<HD>(bk, row, tKh + lane, tKl + lane, nrm);
+      } else {
+        vscale[row] = block_row_to_tmem16<HD>(bv, row, tVh + lane, tVl + lane, nrm);
+        vnorm[row] = nrm;
       }
-      vnorm[row] = sqrtf(ss);
+      tc::tmem_st_wait();
     }
-    tc::tmem_st_wait();
+    tc::fence_async_smem();  // the staged rows are read before a bulk copy reuses the stage
+  } else if (tid == kKvProducer) {
+    for (int i = 0; i < n && i < NS - 1; ++i) {
+      tc::bar_expect_tx(&q_full[i], G::QTILE_BYTES);
+      tc::bulk_g2s(sm8 + i * G::QTILE_BYTES, qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES, G::QTILE_BYTES,
+                   &q_full[i]);
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
 
-  if (tid < kTcCompute) {
+  if (tid < kKvCompute) {
     // ---------------------------------------------------------- softmax
-    const int row = tid & (kTcRows - 1), half = tid >> 7;
+    const int row = tid & (kTcRows - 1), quarter = tid >> 7;
+    const int col = 16 * quarter;  // query columns [col, col + 16) of each step
     const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
     const float scale2 = scale * 1.4426950408889634f / kscale[row];
     const float vinv = 1.0f / vscale[row];
@@ -977,14 +1081,11 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       F16_WAIT_OR_FAIL(&q_full[st], (i / NS) & 1);
       F16_WAIT_OR_FAIL(&s_full[b], (i >> 1) & 1);
       tc::fence_after_sync();
-      float pv[32];
-      for (int q2 = 0; q2 < 2; ++q2) {
-        const int col = 32 * q2 + 16 * half;  // query columns [col, col + 16) of the step
-        float s[16];
-        tc::tmem_ld16(tSb + col + lane, s);
+      float pv[16];
+      {
+        tc::tmem_ld16(tSb + col + lane, pv);
         const int qh = k0 + i * kTcQ + col;
-        const bool full = one_seq && k0 + i * kTcQ + 32 * q2 >= k0 + kTcRows - 1 &&
-                          k0 + i * kTcQ + 32 * q2 + 32 <= min(kseq_end, rows);
+        const bool full = one_seq && qh >= k0 + kTcRows - 1 && qh + 16 <= min(kseq_end, rows);
 #pragma unroll
         for (int c = 0; c < 16; c += 4) {
           const float4 l4 = *reinterpret_cast<const float4*>(hdr + G::LSE + col + c);
@@ -992,20 +1093,16 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
           for (int u = 0; u < 4; u += 2) {
             const float2 lv = u == 0 ? make_float2(l4.x, l4.y) : make_float2(l4.z, l4.w);
             const int q0j = qh + c + u;
-            const float2 t = fma2(make_float2(s[c + u], s[c + u + 1]), splat2(coef), make_float2(-lv.x, -lv.y));
+            const float2 t = fma2(make_float2(pv[c + u], pv[c + u + 1]), splat2(coef), make_float2(-lv.x, -lv.y));
             const bool ok0 = full || (q0j >= kr && q0j < ke && q0j < rows && kr < rows);
             const bool ok1 = full || (q0j + 1 >= kr && q0j + 1 < ke && q0j + 1 < rows && kr < rows);
-            s[c + u] = ok0 ? ex2(t.x) : 0.f;
-            s[c + u + 1] = ok1 ? ex2(t.y) : 0.f;
+            pv[c + u] = ok0 ? ex2(t.x) : 0.f;
+            pv[c + u + 1] = ok1 ? ex2(t.y) : 0.f;
           }
         }
         uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[16 * q2 + 2 * e] = s[2 * e];
-          pv[16 * q2 + 2 * e + 1] = s[2 * e + 1];
-          tc::split_f16x2(s[2 * e] * pc, s[2 * e + 1] * pc, hi[e], lo[e]);
-        }
+        for (int e = 0; e < 8; ++e) tc::split_f16x2(pv[2 * e] * pc, pv[2 * e + 1] * pc, hi[e], lo[e]);
         tc::tmem_st8u(tSb + col + lane, hi);  // P^T over the S^T columns just read
         tc::tmem_st8u(tSb + col + 8 + lane, lo);
       }
@@ -1014,8 +1111,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       tc::bar_arrive(&p_full[b]);
       F16_WAIT_OR_FAIL(&dp_full[b], (i >> 1) & 1);
       tc::fence_after_sync();
-      for (int q2 = 0; q2 < 2; ++q2) {
-        const int col = 32 * q2 + 16 * half;
+      {
         float dp[16];
         tc::tmem_ld16(tSb + 64 + col + lane, dp);
 #pragma unroll
@@ -1024,7 +1120,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
 #pragma unroll
           for (int u = 0; u < 4; u += 2) {
             const float2 ev = u == 0 ? make_float2(e4.x, e4.y) : make_float2(e4.z, e4.w);
-            const float2 pp = make_float2(pv[16 * q2 + c + u], pv[16 * q2 + c + u + 1]);
+            const float2 pp = make_float2(pv[c + u], pv[c + u + 1]);
             const float2 g = mul2(pp, fma2(make_float2(dp[c + u], dp[c + u + 1]), splat2(dcoef),
                                            make_float2(-ev.x, -ev.y)));
             dp[c + u] = g.x;
@@ -1038,41 +1134,35 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
         tc::tmem_st8u(tSb + 64 + col + 8 + lane, lo);
         tc::tmem_st_wait();
         tc::fence_before_sync();
-        tc::bar_arrive(&ds_full[b][q2]);
+        tc::bar_arrive(&ds_full[b][quarter >> 1]);  // columns [0, 32) or [32, 64)
       }
       if (i + 1 == n) done = true;
     }
     // dV and dK of the last step complete before the accumulators are read.
     if (done && !tc::bar_wait(&g_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
     tc::fence_after_sync();
-    if (done && !sh.failed) {
-      const bool in = kr < rows;
-      const float ov = 1.0f / pv_e, ok = 1.0f / (rk * sqmin);
-#pragma unroll
-      for (int c = 0; c < HD / 2; c += 16) {
-        const int col = (HD / 2) * half + c;
+    // dK and dV through the idle ring into coalesced row stores.
+    using B = RowBlock<HD>;
+    float4* bk = reinterpret_cast<float4*>(sm8);
+    float4* bv = bk + B::CHUNKS;
+    const bool ok_out = done && !sh.failed;
+    if (ok_out) {
+      const float ov = 1.0f / pv_e, okk = 1.0f / (rk * sqmin);
+      for (int oc = col; oc < HD; oc += 64) {  // 16-column chunks of dK and dV
         float gk[16], gv[16];
-        tc::tmem_ld16_pair(tdK + lane + col, gk, tdV + lane + col, gv);
-        if (in) {
-          const size_t base = (size_t)kr * W + h * HD + col;  // 16-float aligned
-          float4* dk4 = reinterpret_cast<float4*>(dk + base);
-          float4* dv4 = reinterpret_cast<float4*>(dv + base);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float4 a = make_float4(gv[4 * e] * ov, gv[4 * e + 1] * ov, gv[4 * e + 2] * ov, gv[4 * e + 3] * ov);
-            if (dv_add != nullptr) {
-              const float4 x = __ldg(reinterpret_cast<const float4*>(dv_add + base) + e);
-              a = make_float4(a.x + x.x, a.y + x.y, a.z + x.z, a.w + x.w);
-            }
-            dk4[e] = make_float4(gk[4 * e] * ok, gk[4 * e + 1] * ok, gk[4 * e + 2] * ok, gk[4 * e + 3] * ok);
-            dv4[e] = a;
-          }
-        }
+        tc::tmem_ld16_pair(tdK + lane + oc, gk, tdV + lane + oc, gv);
+        block_put16<HD>(bk, row, oc, gk, okk);
+        block_put16<HD>(bv, row, oc, gv, ov);
       }
     }
-  } else if (tid == kTcProducer) {
+    named_sync<2, kKvCompute>();
+    if (ok_out) {
+      write_rows<HD, kKvCompute>(dk, bk, nullptr, k0, rows, W, h, tid);
+      write_rows<HD, kKvCompute>(dv, bv, dv_add, k0, rows, W, h, tid);
+    }
+  } else if (tid == kKvProducer) {
     // ---------------------------------------------------------- query tiles
-    for (int i = 0; i < n; ++i) {
+    for (int i = NS - 1; i < n; ++i) {  // the first NS - 1 went out before the K/V staging ended
       const int st = i % NS;
       if (i >= NS) {
         F16_WAIT_OR_FAIL(&q_empty[st], ((i - NS) / NS) & 1);
@@ -1081,7 +1171,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       tc::bulk_g2s(sm8 + st * G::QTILE_BYTES, qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES, G::QTILE_BYTES,
                    &q_full[st]);
     }
-  } else if (tid == kTcIssuer) {
+  } else if (tid == kKvIssuer) {
     // ---------------------------------------------------------- S^T / dP^T issuer
     constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcQ);
     for (int i = 0; i < n; ++i) {
@@ -1100,7 +1190,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
                                 stage + (G::D_HI + 1) * G::PART_BYTES, idS, false, 0);  // dP^T = V dO^T
       tc::commit(&dp_full[b]);
     }
-  } else if (tid == kTcIssuer2) {
+  } else if (tid == kKvIssuer2) {
     // ---------------------------------------------------------- dV / dK issuer
     constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD);
     for (int i = 0; i < n; ++i) {

@@ -270,13 +270,13 @@ struct AttentionOpsTc final : AttentionOps {
     attention_format_queries_f16<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), kFmtThreads, 0, s>>>(rows, W, q, dout, lse,
                                                                                            delta, qfmt16());
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dkdv_f16<HD><<<grid, kTcThreads2, F16Kv<HD>::smem, s>>>(
+    attention_backward_dkdv_f16<HD><<<grid, kKvThreads, F16Kv<HD>::smem, s>>>(
         rows, W, T, 1.0f / sqrtf((float)hd), k, v, qfmt16(), dv_add, dk, dv, err);
   }
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
     dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dq_f16<HD><<<grid, kTcThreads2, F16Dq<HD>::smem, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
+    attention_backward_dq_f16<HD><<<grid, kKvThreads, F16Dq<HD>::smem, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
                                                                              dout, kfmt16(rows, H), lse, delta, dq,
                                                                              err);
   }
