@@ -19,16 +19,19 @@
 //    values are smaller than the largest by more than 2^7 has c_j < 1, which
 //    costs precision only in products far below the accumulated magnitude.
 //
-// Roles (every CTA): 8 compute warps (thread i < 128 owns TMEM lane / row i
-// with the first column half, thread 128 + i the second), a producer thread
-// that streams operand tiles into shared-memory rings with cp.async.bulk
-// (plain, no multicast; completion counted on mbarriers), and two MMA issuer
-// threads in separate warps, each committing its own MMAs to mbarriers, so
-// one issuer's waits overlap the other's MMAs.  All waits are bounded and
-// report through `err` instead of hanging.  Operand tiles are written once
-// per use by format passes in the unswizzled FP16 K-major layout of
-// tc05.cuh; operands needed with rows along N are stored transposed.  CTAs
-// are ordered by causal work, longest first.
+// Roles (every CTA): compute warps (8 in the forward, 16 in dQ and dK/dV;
+// thread i owns TMEM lane / row i % 128 and one column slice of each step), a
+// producer thread that streams operand tiles into shared-memory rings with
+// cp.async.bulk (plain, no multicast; completion counted on mbarriers), and
+// two MMA issuer threads in separate warps, each committing its own MMAs to
+// mbarriers, so one issuer's waits overlap the other's MMAs.  All waits are
+// bounded and report through `err` instead of hanging.  Operand tiles are
+// written once per use by format passes in the unswizzled FP16 blocked
+// layout of tc05.cuh, [64 rows][HD]: the same tile is the K-major B operand
+// of one product (Q K^T) and the MN-major B operand of another (P V).  The
+// CTA's own 128 rows move between global memory and TMEM through shared
+// memory with coalesced accesses.  CTAs are ordered by causal work, longest
+// first.
 
 #include "common.cuh"
 #include "tc05.cuh"
@@ -114,31 +117,30 @@ template <int HD>
 struct F16Fmt {
   static constexpr int PART_BYTES = kTcK * HD * 2;  // one 64 x HD FP16 part
   static constexpr int HEADER_BYTES = 128;          // scales (and room to keep tiles 128-byte aligned)
-  static constexpr int KTILE_BYTES = 8 * PART_BYTES + HEADER_BYTES;
-  // parts: K, K', Vt, Vt', V, V', Kt, Kt'; header floats:
-  // s_k, s_v, the largest row norm of V, the largest |V|
-  static constexpr int K_HI = 0, VT_HI = 2, V_HI = 4, KT_HI = 6;
+  static constexpr int KTILE_BYTES = 4 * PART_BYTES + HEADER_BYTES;
+  // parts: K, K', V, V' ([64 keys][HD] each; K-major B operands of Q K^T and
+  // dO V^T, MN-major B operands of P V and dS K); header floats: s_k, s_v,
+  // the largest row norm of V, the largest |V|
+  static constexpr int K_HI = 0, V_HI = 2, HEADER_OFF = 4 * PART_BYTES;
 };
 
 constexpr int kMaxKeyTiles = 72;  // key tiles one query CTA visits: (4096 + 128) / 64 + 2
 
 // Writes the FP16 hi/lo parts p, p + 1 of one operand tile in the blocked
-// K-major layout from a shared-memory copy x ([R][HD], row stride HD + 2),
-// scaled by `scale`; `transposed` writes x^T ([HD rows][R columns]).  Each
-// thread writes whole 16-byte core-matrix rows, contiguous across a warp.
+// layout ([R rows][HD columns]) from a shared-memory copy x ([R][HD], row
+// stride HD + 2), scaled by `scale`.  Each thread writes whole 16-byte
+// core-matrix rows, contiguous across a warp.
 template <int R, int HD>
-__device__ __forceinline__ void store_parts16(uint8_t* __restrict__ tile, int p, bool transposed, const float* x,
-                                              float scale) {
+__device__ __forceinline__ void store_parts16(uint8_t* __restrict__ tile, int p, const float* x, float scale) {
   constexpr int XS = HD + 2, PB = F16Fmt<HD>::PART_BYTES;
-  const int cols = transposed ? R : HD;
   uint4* hi = reinterpret_cast<uint4*>(tile + (size_t)p * PB);
   uint4* lo = reinterpret_cast<uint4*>(tile + (size_t)(p + 1) * PB);
   for (int q = threadIdx.x; q < R * HD / 8; q += kFmtThreads) {
-    const int rl = q & 7, c8 = (q >> 3) % (cols / 8), rg = (q >> 3) / (cols / 8);
+    const int rl = q & 7, c8 = (q >> 3) % (HD / 8), rg = (q >> 3) / (HD / 8);
     const int r = rg * 8 + rl, c = c8 * 8;
     float v[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = (transposed ? x[(c + e) * XS + r] : x[r * XS + c + e]) * scale;
+    for (int e = 0; e < 8; ++e) v[e] = x[r * XS + c + e] * scale;
     uint32_t h[4], l[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) tc::split_f16x2(v[2 * e], v[2 * e + 1], h[e], l[e]);
@@ -148,13 +150,11 @@ __device__ __forceinline__ void store_parts16(uint8_t* __restrict__ tile, int p,
 }
 
 // Key tiles of K and V in FP16 parts with their scales: grid
-// (ceil(rows/64), H), kFmtThreads threads.  `parts` is a bit mask over the
-// hi parts (K_HI, VT_HI, V_HI, KT_HI): only the parts later kernels read are
-// written; the header always is.
+// (ceil(rows/64), H), kFmtThreads threads.
 template <int HD>
 __global__ void __launch_bounds__(kFmtThreads) attention_format_keys_f16(int rows, int W, const float* __restrict__ k,
                                                                    const float* __restrict__ v,
-                                                                   uint8_t* __restrict__ fmt, unsigned parts) {
+                                                                   uint8_t* __restrict__ fmt) {
   using F = F16Fmt<HD>;
   constexpr int XS = HD + 2, NW = kFmtThreads / 32;
   __shared__ float xk[kTcK * XS], xv[kTcK * XS];
@@ -194,12 +194,9 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_keys_f16(int row
     nv = fmaxf(nv, red[2][w]);
   }
   const float sk = tc::f16_scale(mk), sv = tc::f16_scale(mv);
-  if (parts & (1u << F::K_HI)) store_parts16<kTcK, HD>(tile, F::K_HI, false, xk, sk);
-  if (parts & (1u << F::VT_HI)) store_parts16<kTcK, HD>(tile, F::VT_HI, true, xv, sv);
-  if (parts & (1u << F::V_HI)) store_parts16<kTcK, HD>(tile, F::V_HI, false, xv, sv);
-  if (parts & (1u << F::KT_HI)) store_parts16<kTcK, HD>(tile, F::KT_HI, true, xk, sk);
-  if (threadIdx.x == 0)
-    *reinterpret_cast<float4*>(tile + 8 * F::PART_BYTES) = make_float4(sk, sv, nv, mv);
+  store_parts16<kTcK, HD>(tile, F::K_HI, xk, sk);
+  store_parts16<kTcK, HD>(tile, F::V_HI, xv, sv);
+  if (threadIdx.x == 0) *reinterpret_cast<float4*>(tile + F::HEADER_OFF) = make_float4(sk, sv, nv, mv);
 }
 
 // A CTA's 128 rows of one head in shared memory as float4 chunks, chunk c of
@@ -314,13 +311,16 @@ __device__ __forceinline__ void write_rows(float* __restrict__ g, const float4* 
 // D (+)= A . B^T with A = FP16 hi/lo TMEM columns and B a K-major FP16 hi/lo
 // shared tile with KC columns, over K steps [s0, s0 + NSTEP) of 16 elements:
 // three MMAs per step.
-template <int KC, int NSTEP>
+// MN: B is MN-major and C is the tile's column count (N) instead of its K
+// column count.
+template <int C, int NSTEP, bool MN = false>
 __device__ __forceinline__ void mma16_tmem_a(uint32_t d, uint32_t ah, uint32_t al, const void* bh, const void* bl,
                                              uint32_t idesc, bool accumulate, int s0) {
 #pragma unroll
   for (int i = 0; i < NSTEP; ++i) {
     const int s = s0 + i;
-    const uint64_t b_h = tc::desc_kmajor16(bh, KC, s), b_l = tc::desc_kmajor16(bl, KC, s);
+    const uint64_t b_h = MN ? tc::desc_mn16(bh, C, s) : tc::desc_kmajor16(bh, C, s);
+    const uint64_t b_l = MN ? tc::desc_mn16(bl, C, s) : tc::desc_kmajor16(bl, C, s);
     tc::mma_ts_f16(d, ah + 8 * s, b_h, idesc, (accumulate || i > 0) ? 1u : 0u);
     tc::mma_ts_f16(d, ah + 8 * s, b_l, idesc, 1u);
     tc::mma_ts_f16(d, al + 8 * s, b_h, idesc, 1u);
@@ -345,7 +345,7 @@ template <int HD>
 struct F16Att {
   using F = F16Fmt<HD>;
   static constexpr int FWD_STAGES = 4;
-  static constexpr int FWD_STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', Vt, Vt'
+  static constexpr int FWD_STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', V, V'
   static constexpr size_t ROWS_OFF = (size_t)FWD_STAGES * FWD_STAGE_BYTES;  // Q row block, later O
   static constexpr size_t smem_forward = ROWS_OFF + RowBlock<HD>::BYTES;
 };
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
     float mn = INFINITY;
     for (int j = threadIdx.x & 31; j < n; j += 32) {
       const float4 hd4 = __ldg(reinterpret_cast<const float4*>(kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES +
-                                                               8 * F::PART_BYTES));
+                                                               F::HEADER_OFF));
       tscale[j] = make_float2(hd4.x, hd4.y);
       mn = fminf(mn, hd4.y);
     }
@@ -570,20 +570,20 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
     }
   } else if (tid == kTcIssuer2) {
     // ---------------------------------------------------------- P.V issuer
-    constexpr uint32_t idO = tc::idesc_f16(kTcRows, HD);
+    constexpr uint32_t idO = tc::idesc_f16(kTcRows, HD, true);
     for (int j = 0; j < n; ++j) {
       const int st = j % NS, b = j & 1;
       const uint8_t* stage = sm8 + st * A::FWD_STAGE_BYTES;
       F16_WAIT_OR_FAIL(&p_full[b], (j >> 1) & 1);
       F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
       tc::fence_after_sync();
-      // O_half += P[:, half keys] V[half keys]  (B = V^T tile [HD][64 keys],
-      // K steps of 16 keys: half 0 steps 0-1, half 1 steps 2-3)
-      const uint8_t* vh = stage + 2 * F::PART_BYTES;
-      const uint8_t* vl = stage + 3 * F::PART_BYTES;
+      // O_half += P[:, half keys] V[half keys]  (B = the V tile [64 keys][HD],
+      // MN-major; K steps of 16 keys: half 0 steps 0-1, half 1 steps 2-3)
+      const uint8_t* vh = stage + F::V_HI * F::PART_BYTES;
+      const uint8_t* vl = stage + (F::V_HI + 1) * F::PART_BYTES;
       const uint32_t tPb = tP + 64 * b;
-      mma16_tmem_a<kTcK, 2>(tO, tPb, tPb + 32, vh, vl, idO, j > 0, 0);
-      mma16_tmem_a<kTcK, 2>(tO + 64, tPb, tPb + 32, vh, vl, idO, j > 0, 2);
+      mma16_tmem_a<HD, 2, true>(tO, tPb, tPb + 32, vh, vl, idO, j > 0, 0);
+      mma16_tmem_a<HD, 2, true>(tO + 64, tPb, tPb + 32, vh, vl, idO, j > 0, 2);
       tc::commit(&o_done[b]);
       tc::commit(&kv_empty[st]);
     }
@@ -595,7 +595,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
 }
 
 // ---------------------------------------------------------------------- dQ
-// A CTA owns 128 query rows of one head and walks their key tiles (K, V, K^T
+// A CTA owns 128 query rows of one head and walks their key tiles (K and V
 // FP16 parts and scales from the key format).  Per 64-key step j (TMEM
 // buffer b = j & 1): S = Q K^T and dP = dO V^T (thread 288); the compute
 // threads form dS = P (dP - delta) scale in two 32-key halves, each handed to
@@ -616,22 +616,23 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
 template <int HD>
 struct F16Dq {
   using F = F16Fmt<HD>;
-  static constexpr int STAGES = 3;
-  static constexpr int STAGE_BYTES = 6 * F::PART_BYTES;  // K, K', V, V', Kt, Kt'
+  static constexpr int STAGES = 4;
+  static constexpr int STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', V, V'
   static constexpr size_t ROWS_OFF = (size_t)STAGES * STAGE_BYTES;  // Q and dO row blocks, later dQ
   static constexpr size_t smem = ROWS_OFF + 2 * RowBlock<HD>::BYTES;
 };
 
 // D (+)= A . B^T over K steps [s0, s0 + NSTEP) of 16 elements with A's FP16
 // hi and lo parts interleaved in TMEM: step s reads hi columns [16s, 16s + 8)
-// and lo columns [16s + 8, 16s + 16) of `a`.
-template <int KC, int NSTEP>
+// and lo columns [16s + 8, 16s + 16) of `a`.  B is MN-major (tc05.cuh
+// desc_mn16) from a tile with NC columns along N.
+template <int NC, int NSTEP>
 __device__ __forceinline__ void mma16_tmem_a_il(uint32_t d, uint32_t a, const void* bh, const void* bl,
                                                 uint32_t idesc, bool accumulate, int s0) {
 #pragma unroll
   for (int i = 0; i < NSTEP; ++i) {
     const int s = s0 + i;
-    const uint64_t b_h = tc::desc_kmajor16(bh, KC, s), b_l = tc::desc_kmajor16(bl, KC, s);
+    const uint64_t b_h = tc::desc_mn16(bh, NC, s), b_l = tc::desc_mn16(bl, NC, s);
     tc::mma_ts_f16(d, a + 16 * s, b_h, idesc, (accumulate || i > 0) ? 1u : 0u);
     tc::mma_ts_f16(d, a + 16 * s, b_l, idesc, 1u);
     tc::mma_ts_f16(d, a + 16 * s + 8, b_h, idesc, 1u);
@@ -681,7 +682,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     float kmin = INFINITY, vnorm = 0.f;
     for (int j = threadIdx.x & 31; j < n; j += 32) {
       const float4 hd4 = __ldg(reinterpret_cast<const float4*>(kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES +
-                                                               8 * F::PART_BYTES));
+                                                               F::HEADER_OFF));
       tscale[j] = make_float2(hd4.x, hd4.y);
       kmin = fminf(kmin, hd4.x);
       vnorm = fmaxf(vnorm, hd4.z);
@@ -727,9 +728,10 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   tc::fence_after_sync();
 
   if (tid < kKvCompute) {
-    // Thread (row, quarter) handles key columns [16 quarter, +16) of each step.
-    const int row = tid & (kTcRows - 1), quarter = tid >> 7;
-    const int col = 16 * quarter;
+    // Two groups of 8 warps take alternate steps (group g: steps j = g mod 2,
+    // TMEM buffer g); in a group, thread (row, half) handles key columns
+    // [32 k2 + 16 half, +16) for k2 = 0, 1.
+    const int row = tid & (kTcRows - 1), half = (tid >> 7) & 1, grp = tid >> 8;
     const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
     const float sq_inv = 1.0f / qscale[row], so_inv = 1.0f / oscale[row], rg = gscale[row];
     const float scale2 = scale * 1.4426950408889634f * sq_inv;
@@ -740,18 +742,18 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     const float L = in ? lse2[(size_t)h * rows + qr] : 0.f;
     const float dl = in ? delta[(size_t)h * rows + qr] : 0.f;
     const float kmin = kmin_s;
-    bool done = false;
-    for (int j = 0; j < n; ++j) {
-      const int b = j & 1;
+    const uint32_t tSb = tS + 128 * grp;
+    for (int j = grp; j < n; j += 2) {
       const float2 ts = tscale[j];
       const float coef = scale2 / ts.x;                // S_tmem -> log2 units
       const float dcoef = so_inv / ts.y;               // dP_tmem -> dP
       const float gcoef = scale * rg * (kmin / ts.x);  // dS -> stored dS
-      const uint32_t tSb = tS + 128 * b;
-      F16_WAIT_OR_FAIL(&s_full[b], (j >> 1) & 1);
+      F16_WAIT_OR_FAIL(&s_full[grp], (j >> 1) & 1);
       tc::fence_after_sync();
       const int kt = kbeg + j * kTcK;
-      {
+#pragma unroll
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int col = 32 * k2 + 16 * half;
         float s[16], dp[16];
         tc::tmem_ld16_pair(tSb + col + lane, s, tSb + 64 + col + lane, dp);
         const int kh = kt + col;
@@ -773,18 +775,22 @@ __global__ void __launch_bounds__(kKvThreads, 1)
         tc::tmem_st8u(tSb + col + 8 + lane, lo);
         tc::tmem_st_wait();
         tc::fence_before_sync();
-        tc::bar_arrive(&d_full[b][quarter >> 1]);  // key columns [0, 32) or [32, 64)
+        tc::bar_arrive(&d_full[grp][k2]);  // key columns [0, 32) or [32, 64)
       }
-      if (j + 1 == n) done = true;
     }
-    if (done && !tc::bar_wait(&q_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
+    // dQ of the last two steps complete before the accumulator is read.  A
+    // group has seen the other buffer's barrier only up to the step before
+    // its own last one, so it waits for step n - 2 first: a parity wait is
+    // only exact within one phase of the barrier.
+    for (int j = max(n - 2, 0); j < n && !sh.failed; ++j)
+      if (!tc::bar_wait(&q_done[j & 1], (j >> 1) & 1)) sh.failed = 1;
     tc::fence_after_sync();
     // dQ through the Q row block into coalesced row stores.
     float4* bq = reinterpret_cast<float4*>(sm8 + A::ROWS_OFF);
-    const bool ok_out = done && !sh.failed;
+    const bool ok_out = !sh.failed;
     if (ok_out) {
       const float out = 1.0f / (rg * kmin);
-      for (int oc = col; oc < HD; oc += 64) {  // 16-column chunks of dQ
+      for (int oc = 16 * (tid >> 7); oc < HD; oc += 64) {  // 16-column chunks of dQ
         float gv[16];
         tc::tmem_ld16(tG + lane + oc, gv);
         block_put16<HD>(bq, row, oc, gv, out);
@@ -801,15 +807,14 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       const uint8_t* tile = kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES;
       uint8_t* stage = sm8 + st * A::STAGE_BYTES;
       tc::bar_expect_tx(&kv_full[st], A::STAGE_BYTES);
-      tc::bulk_g2s(stage, tile, 2 * F::PART_BYTES, &kv_full[st]);                                          // K, K'
-      tc::bulk_g2s(stage + 2 * F::PART_BYTES, tile + 4 * F::PART_BYTES, 4 * F::PART_BYTES, &kv_full[st]);  // V, V', Kt, Kt'
+      tc::bulk_g2s(stage, tile, A::STAGE_BYTES, &kv_full[st]);  // K, K', V, V'
     }
   } else if (tid == kKvIssuer) {
     // ---------------------------------------------------------- S / dP issuer
     constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
     for (int j = 0; j < n; ++j) {
       const int st = j % NS, b = j & 1;
-      const uint8_t* stage = sm8 + st * A::STAGE_BYTES;  // K, K', V, V', Kt, Kt'
+      const uint8_t* stage = sm8 + st * A::STAGE_BYTES;  // K, K', V, V'
       F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
       if (j >= 2) {
         // dQ of step j-2 has read this buffer's dS, so its S and dP are free
@@ -824,7 +829,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     }
   } else if (tid == kKvIssuer2) {
     // ---------------------------------------------------------- dQ issuer
-    constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD);
+    constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD, true);
     for (int j = 0; j < n; ++j) {
       const int st = j % NS, b = j & 1;
       const uint8_t* stage = sm8 + st * A::STAGE_BYTES;
@@ -835,10 +840,10 @@ __global__ void __launch_bounds__(kKvThreads, 1)
         ok = tc::bar_wait(&d_full[b][k2], (j >> 1) & 1);
         tc::fence_after_sync();
         // dQ += dS K over keys [32 k2, 32 k2 + 32): K steps 2 k2, 2 k2 + 1 of
-        // the K^T tile [HD][64 keys]
+        // the K tile [64 keys][HD], MN-major
         if (ok)
-          mma16_tmem_a_il<kTcK, 2>(tG, tSb, stage + 4 * F::PART_BYTES, stage + 5 * F::PART_BYTES, idG,
-                                   j > 0 || k2 > 0, 2 * k2);
+          mma16_tmem_a_il<HD, 2>(tG, tSb, stage + F::K_HI * F::PART_BYTES, stage + (F::K_HI + 1) * F::PART_BYTES,
+                                 idG, j > 0 || k2 > 0, 2 * k2);
       }
       if (!ok) {
         sh.failed = 1;
@@ -855,15 +860,14 @@ __global__ void __launch_bounds__(kKvThreads, 1)
 }
 
 // ------------------------------------------------------------------- dK/dV
-// Query tiles in FP16 parts: Q, Q', dO, dO', Q^T, Q^T', dO^T, dO^T' (64 x HD
-// each) and a header with the 64 rows' LSE and delta, the tile's scales
+// Query tiles in FP16 parts: Q, Q', dO, dO' ([64 queries][HD] each) and a header with the 64 rows' LSE and delta, the tile's scales
 // s_q and s_do, its largest dO row norm and its largest |delta|.
 template <int HD>
 struct F16Q {
   static constexpr int PART_BYTES = kTcQ * HD * 2;
   static constexpr int HEADER_BYTES = 1024;
-  static constexpr int QTILE_BYTES = 8 * PART_BYTES + HEADER_BYTES;
-  static constexpr int Q_HI = 0, D_HI = 2, QT_HI = 4, DT_HI = 6;
+  static constexpr int QTILE_BYTES = 4 * PART_BYTES + HEADER_BYTES;
+  static constexpr int Q_HI = 0, D_HI = 2, HEADER_OFF = 4 * PART_BYTES;
   static constexpr int LSE = 0, DELTA = kTcQ, SCALES = 2 * kTcQ;  // header floats
 };
 
@@ -880,7 +884,7 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_queries_f16(int 
   __shared__ float red[4][NW];
   const int t = blockIdx.x, h = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint8_t* tile = fmt + ((size_t)h * gridDim.x + t) * G::QTILE_BYTES;
-  float* hdr = reinterpret_cast<float*>(tile + 8 * G::PART_BYTES);
+  float* hdr = reinterpret_cast<float*>(tile + G::HEADER_OFF);
   load_rows2<kTcQ, HD>(xq, q, xd, dout, t * kTcQ, rows, W, h);
   __syncthreads();
   float mq = 0.f, md = 0.f, nd = 0.f, mdl = 0.f;
@@ -923,15 +927,13 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_queries_f16(int 
     mdl = fmaxf(mdl, red[3][w]);
   }
   const float sq = tc::f16_scale(mq), sd = tc::f16_scale(md);
-  store_parts16<kTcQ, HD>(tile, G::Q_HI, false, xq, sq);
-  store_parts16<kTcQ, HD>(tile, G::D_HI, false, xd, sd);
-  store_parts16<kTcQ, HD>(tile, G::QT_HI, true, xq, sq);
-  store_parts16<kTcQ, HD>(tile, G::DT_HI, true, xd, sd);
+  store_parts16<kTcQ, HD>(tile, G::Q_HI, xq, sq);
+  store_parts16<kTcQ, HD>(tile, G::D_HI, xd, sd);
   if (threadIdx.x == 0) *reinterpret_cast<float4*>(hdr + G::SCALES) = make_float4(sq, sd, nd, mdl);
 }
 
 // A CTA owns 128 keys of one head (K and V split into TMEM with per-row
-// scales) and walks their queries 64 at a time through a 3-stage ring of
+// scales) and walks their queries 64 at a time through a 4-stage ring of
 // query tiles.  Per step i (TMEM buffer b = i & 1): thread 288 issues
 // S^T = K Q^T and dP^T = V dO^T (keys on lanes, N = 64 queries); the compute
 // threads form P^T = exp2(S^T scale - lse) and store it over the S^T columns
@@ -949,8 +951,9 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_queries_f16(int 
 template <int HD>
 struct F16Kv {
   using G = F16Q<HD>;
-  static constexpr int STAGES = 3;
-  static constexpr size_t smem = (size_t)STAGES * G::QTILE_BYTES;
+  static constexpr int STAGES = 4;
+  static constexpr size_t ROWS_OFF = (size_t)STAGES * G::QTILE_BYTES;  // K and V row blocks, later dK and dV
+  static constexpr size_t smem = ROWS_OFF + 2 * RowBlock<HD>::BYTES;
 };
 
 template <int HD>
@@ -984,7 +987,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     for (int b = 0; b < 2; ++b) {
       tc::bar_init(&s_full[b], 1);
       tc::bar_init(&dp_full[b], 1);
-      tc::bar_init(&p_full[b], kKvCompute);
+      tc::bar_init(&p_full[b], kKvCompute / 2);  // one compute group per buffer
       tc::bar_init(&ds_full[b][0], kKvCompute / 2);
       tc::bar_init(&ds_full[b][1], kKvCompute / 2);
       tc::bar_init(&g_done[b], 1);
@@ -996,7 +999,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     float sqm = INFINITY, sdm = INFINITY, ndm = 0.f, dlm = 0.f;
     for (int i = threadIdx.x & 31; i < n; i += 32) {
       const float4 sc = __ldg(reinterpret_cast<const float4*>(qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES +
-                                                              8 * G::PART_BYTES + G::SCALES * 4));
+                                                              G::HEADER_OFF + G::SCALES * 4));
       tscale[i] = make_float2(sc.x, sc.y);
       sqm = fminf(sqm, sc.x);
       sdm = fminf(sdm, sc.y);
@@ -1024,10 +1027,9 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   const uint32_t tKh = t0, tKl = t0 + 32, tVh = t0 + 64, tVl = t0 + 96, tdV = t0 + 128, tdK = t0 + 192,
                  tS = t0 + 256;  // buffer b: S^T at tS + 128 b, dP^T at tS + 128 b + 64
   if (tid < kKvCompute) {
-    // K and V rows through the last ring stage (its query tile is issued
-    // after this) into TMEM, split with per-row scales.
+    // K and V rows through shared memory into TMEM, split with per-row scales.
     using B = RowBlock<HD>;
-    float4* bk = reinterpret_cast<float4*>(sm8 + (NS - 1) * G::QTILE_BYTES);
+    float4* bk = reinterpret_cast<float4*>(sm8 + F16Kv<HD>::ROWS_OFF);
     float4* bv = bk + B::CHUNKS;
     stage_rows<HD, kKvCompute, true>(bk, k, bv, v, k0, rows, W, h, tid);
     named_sync<2, kKvCompute>();
@@ -1043,13 +1045,6 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       }
       tc::tmem_st_wait();
     }
-    tc::fence_async_smem();  // the staged rows are read before a bulk copy reuses the stage
-  } else if (tid == kKvProducer) {
-    for (int i = 0; i < n && i < NS - 1; ++i) {
-      tc::bar_expect_tx(&q_full[i], G::QTILE_BYTES);
-      tc::bulk_g2s(sm8 + i * G::QTILE_BYTES, qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES, G::QTILE_BYTES,
-                   &q_full[i]);
-    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1057,8 +1052,11 @@ __global__ void __launch_bounds__(kKvThreads, 1)
 
   if (tid < kKvCompute) {
     // ---------------------------------------------------------- softmax
-    const int row = tid & (kTcRows - 1), quarter = tid >> 7;
-    const int col = 16 * quarter;  // query columns [col, col + 16) of each step
+    // Two groups of 8 warps take alternate steps (group g: steps i = g mod 2,
+    // TMEM buffer g), so one group's softmax overlaps the other's and the
+    // MMAs of both.  In a group, thread (row, half) handles query columns
+    // [32 q2 + 16 half, +16) for q2 = 0, 1.
+    const int row = tid & (kTcRows - 1), half = (tid >> 7) & 1, grp = tid >> 8;
     const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
     const float scale2 = scale * 1.4426950408889634f / kscale[row];
     const float vinv = 1.0f / vscale[row];
@@ -1068,22 +1066,25 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     const int ke = (kr / T + 1) * T;  // end of the key's sequence
     const int kseq_end = (k0 / T + 1) * T;
     const bool one_seq = (k0 + kTcRows - 1) / T == k0 / T && k0 + kTcRows <= rows;
-    bool done = false;
-    for (int i = 0; i < n; ++i) {
-      const int b = i & 1, st = i % NS;
+    const uint32_t tSb = tS + 128 * grp;
+    for (int i = grp; i < n; i += 2) {
+      const int st = i % NS;
       const float2 ts = tscale[i];
-      const float coef = scale2 / ts.x;          // S^T_tmem -> log2 units
-      const float dcoef = vinv / ts.y;           // dP^T_tmem -> dP
-      const float pc = pv_e / ts.y;              // P -> stored P
+      const float coef = scale2 / ts.x;              // S^T_tmem -> log2 units
+      const float dcoef = vinv / ts.y;               // dP^T_tmem -> dP
+      const float pc = pv_e / ts.y;                  // P -> stored P
       const float gc = scale * rk * (sqmin / ts.x);  // (dP - delta) P -> stored dS
-      const float* hdr = reinterpret_cast<const float*>(sm8 + st * G::QTILE_BYTES + 8 * G::PART_BYTES);
-      const uint32_t tSb = tS + 128 * b;
+      const float* hdr = reinterpret_cast<const float*>(sm8 + st * G::QTILE_BYTES + G::HEADER_OFF);
       F16_WAIT_OR_FAIL(&q_full[st], (i / NS) & 1);
-      F16_WAIT_OR_FAIL(&s_full[b], (i >> 1) & 1);
+      F16_WAIT_OR_FAIL(&s_full[grp], (i >> 1) & 1);
       tc::fence_after_sync();
-      float pv[16];
-      {
-        tc::tmem_ld16(tSb + col + lane, pv);
+      float pv[32];
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const int col = 32 * q2 + 16 * half;  // query columns [col, col + 16) of the step
+        float* p = pv + 16 * q2;
+        float sv[16];
+        tc::tmem_ld16(tSb + col + lane, sv);
         const int qh = k0 + i * kTcQ + col;
         const bool full = one_seq && qh >= k0 + kTcRows - 1 && qh + 16 <= min(kseq_end, rows);
 #pragma unroll
@@ -1093,25 +1094,28 @@ __global__ void __launch_bounds__(kKvThreads, 1)
           for (int u = 0; u < 4; u += 2) {
             const float2 lv = u == 0 ? make_float2(l4.x, l4.y) : make_float2(l4.z, l4.w);
             const int q0j = qh + c + u;
-            const float2 t = fma2(make_float2(pv[c + u], pv[c + u + 1]), splat2(coef), make_float2(-lv.x, -lv.y));
+            const float2 t = fma2(make_float2(sv[c + u], sv[c + u + 1]), splat2(coef), make_float2(-lv.x, -lv.y));
             const bool ok0 = full || (q0j >= kr && q0j < ke && q0j < rows && kr < rows);
             const bool ok1 = full || (q0j + 1 >= kr && q0j + 1 < ke && q0j + 1 < rows && kr < rows);
-            pv[c + u] = ok0 ? ex2(t.x) : 0.f;
-            pv[c + u + 1] = ok1 ? ex2(t.y) : 0.f;
+            p[c + u] = ok0 ? ex2(t.x) : 0.f;
+            p[c + u + 1] = ok1 ? ex2(t.y) : 0.f;
           }
         }
         uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) tc::split_f16x2(pv[2 * e] * pc, pv[2 * e + 1] * pc, hi[e], lo[e]);
+        for (int e = 0; e < 8; ++e) tc::split_f16x2(p[2 * e] * pc, p[2 * e + 1] * pc, hi[e], lo[e]);
         tc::tmem_st8u(tSb + col + lane, hi);  // P^T over the S^T columns just read
         tc::tmem_st8u(tSb + col + 8 + lane, lo);
       }
       tc::tmem_st_wait();
       tc::fence_before_sync();
-      tc::bar_arrive(&p_full[b]);
-      F16_WAIT_OR_FAIL(&dp_full[b], (i >> 1) & 1);
+      tc::bar_arrive(&p_full[grp]);
+      F16_WAIT_OR_FAIL(&dp_full[grp], (i >> 1) & 1);
       tc::fence_after_sync();
-      {
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const int col = 32 * q2 + 16 * half;
+        const float* p = pv + 16 * q2;
         float dp[16];
         tc::tmem_ld16(tSb + 64 + col + lane, dp);
 #pragma unroll
@@ -1120,7 +1124,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
 #pragma unroll
           for (int u = 0; u < 4; u += 2) {
             const float2 ev = u == 0 ? make_float2(e4.x, e4.y) : make_float2(e4.z, e4.w);
-            const float2 pp = make_float2(pv[c + u], pv[c + u + 1]);
+            const float2 pp = make_float2(p[c + u], p[c + u + 1]);
             const float2 g = mul2(pp, fma2(make_float2(dp[c + u], dp[c + u + 1]), splat2(dcoef),
                                            make_float2(-ev.x, -ev.y)));
             dp[c + u] = g.x;
@@ -1134,21 +1138,24 @@ __global__ void __launch_bounds__(kKvThreads, 1)
         tc::tmem_st8u(tSb + 64 + col + 8 + lane, lo);
         tc::tmem_st_wait();
         tc::fence_before_sync();
-        tc::bar_arrive(&ds_full[b][quarter >> 1]);  // columns [0, 32) or [32, 64)
+        tc::bar_arrive(&ds_full[grp][q2]);
       }
-      if (i + 1 == n) done = true;
     }
-    // dV and dK of the last step complete before the accumulators are read.
-    if (done && !tc::bar_wait(&g_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
+    // dV and dK of the last two steps complete before the accumulators are
+    // read, step n - 2 first (a group has seen the other buffer's barrier
+    // only up to the step before its own last one, and a parity wait is only
+    // exact within one phase of the barrier).
+    for (int i = max(n - 2, 0); i < n && !sh.failed; ++i)
+      if (!tc::bar_wait(&g_done[i & 1], (i >> 1) & 1)) sh.failed = 1;
     tc::fence_after_sync();
-    // dK and dV through the idle ring into coalesced row stores.
+    // dK and dV through the K and V row blocks into coalesced row stores.
     using B = RowBlock<HD>;
-    float4* bk = reinterpret_cast<float4*>(sm8);
+    float4* bk = reinterpret_cast<float4*>(sm8 + F16Kv<HD>::ROWS_OFF);
     float4* bv = bk + B::CHUNKS;
-    const bool ok_out = done && !sh.failed;
+    const bool ok_out = !sh.failed;
     if (ok_out) {
       const float ov = 1.0f / pv_e, okk = 1.0f / (rk * sqmin);
-      for (int oc = col; oc < HD; oc += 64) {  // 16-column chunks of dK and dV
+      for (int oc = 16 * (tid >> 7); oc < HD; oc += 64) {  // 16-column chunks of dK and dV
         float gk[16], gv[16];
         tc::tmem_ld16_pair(tdK + lane + oc, gk, tdV + lane + oc, gv);
         block_put16<HD>(bk, row, oc, gk, okk);
@@ -1162,7 +1169,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     }
   } else if (tid == kKvProducer) {
     // ---------------------------------------------------------- query tiles
-    for (int i = NS - 1; i < n; ++i) {  // the first NS - 1 went out before the K/V staging ended
+    for (int i = 0; i < n; ++i) {
       const int st = i % NS;
       if (i >= NS) {
         F16_WAIT_OR_FAIL(&q_empty[st], ((i - NS) / NS) & 1);
@@ -1192,7 +1199,7 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     }
   } else if (tid == kKvIssuer2) {
     // ---------------------------------------------------------- dV / dK issuer
-    constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD);
+    constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD, true);
     for (int i = 0; i < n; ++i) {
       const int st = i % NS, b = i & 1;
       const uint8_t* stage = sm8 + st * G::QTILE_BYTES;
@@ -1200,17 +1207,17 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       F16_WAIT_OR_FAIL(&q_full[st], (i / NS) & 1);
       F16_WAIT_OR_FAIL(&p_full[b], (i >> 1) & 1);
       tc::fence_after_sync();
-      // dV += P^T dO over the step's 64 queries (B = dO^T [HD][64 queries])
-      mma16_tmem_a_il<kTcQ, 4>(tdV, tSb, stage + G::DT_HI * G::PART_BYTES, stage + (G::DT_HI + 1) * G::PART_BYTES,
-                               idG, i > 0, 0);
+      // dV += P^T dO over the step's 64 queries (B = the dO tile [64 queries][HD], MN-major)
+      mma16_tmem_a_il<HD, 4>(tdV, tSb, stage + G::D_HI * G::PART_BYTES, stage + (G::D_HI + 1) * G::PART_BYTES, idG,
+                             i > 0, 0);
       bool okw = true;
       for (int q2 = 0; q2 < 2 && okw; ++q2) {
         okw = tc::bar_wait(&ds_full[b][q2], (i >> 1) & 1);
         tc::fence_after_sync();
-        // dK += dS^T Q over queries [32 q2, 32 q2 + 32) (B = Q^T [HD][64 queries])
+        // dK += dS^T Q over queries [32 q2, 32 q2 + 32) (B = the Q tile [64 queries][HD], MN-major)
         if (okw)
-          mma16_tmem_a_il<kTcQ, 2>(tdK, tSb + 64, stage + G::QT_HI * G::PART_BYTES,
-                                   stage + (G::QT_HI + 1) * G::PART_BYTES, idG, i > 0 || q2 > 0, 2 * q2);
+          mma16_tmem_a_il<HD, 2>(tdK, tSb + 64, stage + G::Q_HI * G::PART_BYTES,
+                                 stage + (G::Q_HI + 1) * G::PART_BYTES, idG, i > 0 || q2 > 0, 2 * q2);
       }
       if (!okw) {
         sh.failed = 1;

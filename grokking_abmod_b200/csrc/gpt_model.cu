@@ -253,9 +253,8 @@ struct AttentionOpsTc final : AttentionOps {
     return reinterpret_cast<uint8_t*>(scratch + query_floats(rows, H) + (size_t)layer * key_floats(rows, H));
   }
   void prepare_keys(cudaStream_t s, int rows, int W, int H, const float* k, const float* v) override {
-    using G = F16Fmt<HD>;
     attention_format_keys_f16<HD><<<dim3((rows + kTcK - 1) / kTcK, H), kFmtThreads, 0, s>>>(
-        rows, W, k, v, kfmt16(rows, H), (1u << G::K_HI) | (1u << G::VT_HI) | (1u << G::V_HI) | (1u << G::KT_HI));
+        rows, W, k, v, kfmt16(rows, H));
   }
   void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                const float* v, float* o, float* lse) override {

@@ -13,9 +13,11 @@
 // at float offset ((r / 8) * (C / 4) + c / 4) * 32 + (r % 8) * 4 + c % 4.
 // Tiles are K-major operands (rows = M or N, columns = K); fields per the PTX
 // ISA tcgen05 shared memory descriptor (CUTLASS cute/arch/mma_sm100_desc.hpp
-// documents them).  Operands are never given MN-major: measured on this
-// sm_100a pool, a TF32 MMA with the transpose bit set for B reads zeros, so an
-// operand needed with its rows along N is stored transposed instead.
+// documents them).  TF32 operands are never given MN-major: measured on this
+// sm_100a pool, a TF32 MMA with the transpose bit set for B reads zeros, so a
+// TF32 operand needed with its rows along N is stored transposed instead.
+// FP16 B operands may be MN-major (desc_mn16), which lets one FP16 tile
+// serve both as the K-major B of one product and the MN-major B of another.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -241,9 +243,20 @@ __device__ __forceinline__ uint64_t desc_kmajor16(const void* tile, int C, int s
   return sdesc(smem_addr(tile) + (uint32_t)s * 256u, 128u, (uint32_t)(C / 8) * 128u);
 }
 
-// Instruction descriptor: FP32 accumulator, FP16 A and B, M x N, both K-major.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
-  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// MN-major FP16 B operand read from a blocked tile whose rows run along K
+// and whose C columns run along N (the bytes of the K-major tile of the
+// transposed product): K step s covers tile rows [16s, 16s + 16).  LBO is
+// the stride between 8-row groups along K, SBO the stride between 8-column
+// groups along N (checked against a CPU product on sm_100a, kind::f16).
+__device__ __forceinline__ uint64_t desc_mn16(const void* tile, int C, int s) {
+  const uint32_t kgroup = (uint32_t)(C / 8) * 128u;
+  return sdesc(smem_addr(tile) + (uint32_t)s * 2u * kgroup, kgroup, 128u);
+}
+
+// Instruction descriptor: FP32 accumulator, FP16 A and B, M x N, A K-major,
+// B K-major or (b_mn) MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool b_mn = false) {
+  return (1u << 4) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // D (TMEM) (+)= A (TMEM, FP16 pairs, lane = row) * B (smem, FP16)
