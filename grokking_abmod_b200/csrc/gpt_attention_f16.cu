@@ -519,7 +519,8 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
     xm[half][row] = m;
     xl[half][row] = l;
     compute_sync();
-    if (done && !sh.failed) {
+    const bool okf = __all_sync(0xffffffffu, done && !sh.failed);  // warp-uniform: .aligned TMEM loads
+    if (okf) {
       // Merge the two streams: O = (O0 2^(m0-M) + O1 2^(m1-M)) / (C L).
       const float m0 = xm[0][row], m1 = xm[1][row];
       const float mt = fmaxf(m0, m1);
@@ -540,7 +541,7 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
       if (qr < rows && half == 0) lse2[(size_t)h * rows + qr] = mt + log2f(L);
     }
     named_sync<2, kTcCompute>();
-    if (done && !sh.failed)
+    if (okf)
       write_rows<HD, kTcCompute>(o, reinterpret_cast<const float4*>(sm8 + A::ROWS_OFF), nullptr, q0, rows, W, h, tid);
   } else if (tid == kTcProducer) {
     // ---------------------------------------------------------- producer
@@ -594,33 +595,67 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   if (warp == 0) tc::tmem_dealloc(t0, 512);
 }
 
-// ---------------------------------------------------------------------- dQ
-// A CTA owns 128 query rows of one head and walks their key tiles (K and V
-// FP16 parts and scales from the key format).  Per 64-key step j (TMEM
-// buffer b = j & 1): S = Q K^T and dP = dO V^T (thread 288); the compute
-// threads form dS = P (dP - delta) scale in two 32-key halves, each handed to
-// thread 320 for dQ += dS K as soon as it is stored.  S and dP are
-// double-buffered, so step j + 1's MMAs run while step j's softmax computes.
-// dS is written over the S columns its thread has just read: the thread
-// owning keys [16m, 16m + 16) stores their FP16 hi parts in S columns
-// [16m, 16m + 8) and lo parts in [16m + 8, 16m + 16), so no thread overwrites
-// columns another has yet to read; S_{j+2} is issued into the buffer once
-// dQ of step j has read that dS.
-// Scales: Q rows s_q(i), dO rows t(i) (per row, like the forward's Q); key
-// tiles s_k(j), s_v(j); dS_ij is stored as dS_ij r(i) d(j) with
-// r(i) = f16_scale(2 |dO_i| max|V_row| scale), a bound on |dS_i.| (|dP| and
-// |delta| are at most |dO_i| max|V_row|), and d(j) = min_j s_k / s_k(j), so
-// dQ_i = dQ_tmem / (r(i) min_j s_k).
-// TMEM: Q hi | Q lo | dO hi | dO lo (32 each) | S0 | dP0 | S1 | dP1 (64 each) |
-// dQ (64) = 448.
-template <int HD>
-struct F16Dq {
-  using F = F16Fmt<HD>;
-  static constexpr int STAGES = 4;
-  static constexpr int STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', V, V'
-  static constexpr size_t ROWS_OFF = (size_t)STAGES * STAGE_BYTES;  // Q and dO row blocks, later dQ
-  static constexpr size_t smem = ROWS_OFF + 2 * RowBlock<HD>::BYTES;
-};
+// One 128-row block of rows into FP16 hi/lo parts in shared memory (the
+// blocked layout of tc05.cuh, [128 rows][HD]), in place of the FP32 row block
+// it was staged in: every thread (warps 0-7; rows of A for warps 0-3, of B
+// for warps 4-7) first reads its row, then all of them write.  Returns the
+// row's scale; `norm` receives its Euclidean norm.  Other threads of the CTA
+// call only the two named barriers.
+template <int HD, int NT>
+__device__ __forceinline__ float rows_to_parts16(uint8_t* region, int warp, int r, float& norm) {
+  using B = RowBlock<HD>;
+  constexpr int PB = kTcRows * HD * 2;  // one [128][HD] FP16 part
+  float x[HD];
+  float s = 1.0f;
+  norm = 0.f;
+  if (warp < 8) {
+    const float4* blk = reinterpret_cast<const float4*>(region) + (warp < 4 ? 0 : B::CHUNKS);
+#pragma unroll
+    for (int c = 0; c < B::C4; ++c) {
+      const float4 v = blk[B::at(r, c)];
+      x[4 * c] = v.x, x[4 * c + 1] = v.y, x[4 * c + 2] = v.z, x[4 * c + 3] = v.w;
+    }
+    float m = 0.f, ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < HD; ++c) {
+      m = fmaxf(m, fabsf(x[c]));
+      ss += x[c] * x[c];
+    }
+    norm = sqrtf(ss);
+    s = tc::f16_scale(m);
+  }
+  named_sync<2, NT>();  // every row is read before any part is written over the block
+  if (warp < 8) {
+    uint4* hi = reinterpret_cast<uint4*>(region + (warp < 4 ? 0 : 2 * PB));
+    uint4* lo = reinterpret_cast<uint4*>(region + (warp < 4 ? PB : 3 * PB));
+#pragma unroll
+    for (int c = 0; c < HD; c += 8) {
+      uint32_t h[4], l[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tc::split_f16x2(x[c + 2 * e] * s, x[c + 2 * e + 1] * s, h[e], l[e]);
+      const int q = tc::blk16(r, c, HD) / 8;  // 16-byte core-matrix row
+      hi[q] = make_uint4(h[0], h[1], h[2], h[3]);
+      lo[q] = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+  }
+  return s;
+}
+
+// D (+)= A . B^T with A and B K-major FP16 hi/lo shared tiles of KC columns
+// (A: 128 rows, B: N rows), K steps [s0, s0 + NSTEP): three MMAs per step.
+template <int KC, int NSTEP>
+__device__ __forceinline__ void mma16_ss(uint32_t d, const void* ah, const void* al, const void* bh, const void* bl,
+                                         uint32_t idesc, bool accumulate, int s0) {
+#pragma unroll
+  for (int i = 0; i < NSTEP; ++i) {
+    const int s = s0 + i;
+    const uint64_t a_h = tc::desc_kmajor16(ah, KC, s), a_l = tc::desc_kmajor16(al, KC, s);
+    const uint64_t b_h = tc::desc_kmajor16(bh, KC, s), b_l = tc::desc_kmajor16(bl, KC, s);
+    tc::mma_ss_f16(d, a_h, b_h, idesc, (accumulate || i > 0) ? 1u : 0u);
+    tc::mma_ss_f16(d, a_h, b_l, idesc, 1u);
+    tc::mma_ss_f16(d, a_l, b_h, idesc, 1u);
+  }
+}
 
 // D (+)= A . B^T over K steps [s0, s0 + NSTEP) of 16 elements with A's FP16
 // hi and lo parts interleaved in TMEM: step s reads hi columns [16s, 16s + 8)
@@ -639,6 +674,39 @@ __device__ __forceinline__ void mma16_tmem_a_il(uint32_t d, uint32_t a, const vo
   }
 }
 
+// ---------------------------------------------------------------------- dQ
+// A CTA owns 128 query rows of one head and walks their key tiles (K and V
+// FP16 parts and scales from the key format).  Q and dO sit in shared memory
+// as FP16 hi/lo parts with per-row scales (A operands of S = Q K^T and
+// dP = dO V^T), so TMEM holds dQ and three S/dP buffers: step j uses buffer
+// j mod 3, and step j + 3's products wait only for dQ of step j.  Per 64-key
+// step: thread 544 issues S and dP; all 16 compute warps (thread (row,
+// quarter) owns key columns [16 quarter, +16)) form dS = P (dP - delta)
+// scale, each 32-key half handed to thread 576 for dQ += dS K as soon as it
+// is stored.  dS is written over the S columns its thread has just read (FP16
+// hi parts in S columns [16m, 16m + 8), lo parts in [16m + 8, 16m + 16) for
+// keys [16m, 16m + 16)), so no thread overwrites columns another has yet to
+// read.
+// Scales: Q rows s_q(i), dO rows t(i); key tiles s_k(j), s_v(j); dS_ij is
+// stored as dS_ij r(i) d(j) with r(i) = f16_scale(2 |dO_i| max|V_row| scale),
+// a bound on |dS_i.| (|dP| and |delta| are at most |dO_i| max|V_row|), and
+// d(j) = min_j s_k / s_k(j), so dQ_i = dQ_tmem / (r(i) min_j s_k).
+// TMEM: dQ | (S | dP) x 3, 64 columns each = 448 (512 allocated).
+// Shared memory: the key ring, then one 64 KB region that holds the FP32 Q
+// and dO rows, then their FP16 parts (Q, Q', dO, dO'), then dQ on the way
+// out.
+template <int HD>
+struct F16Dq {
+  using F = F16Fmt<HD>;
+  static constexpr int STAGES = 4;
+  static constexpr int BUFS = 3;
+  static constexpr int STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', V, V'
+  static constexpr int QPART = kTcRows * HD * 2;         // one [128 rows][HD] FP16 part
+  static constexpr size_t ROWS_OFF = (size_t)STAGES * STAGE_BYTES;
+  static constexpr size_t smem = ROWS_OFF + 4 * (size_t)QPART;
+  static_assert(4 * (size_t)QPART == 2 * RowBlock<HD>::BYTES, "parts and row blocks share the region");
+};
+
 template <int HD>
 __global__ void __launch_bounds__(kKvThreads, 1)
     attention_backward_dq_f16(int rows, int W, int T, float scale, const float* __restrict__ q,
@@ -647,11 +715,11 @@ __global__ void __launch_bounds__(kKvThreads, 1)
                               float* __restrict__ dq, int* __restrict__ err) {
   using A = F16Dq<HD>;
   using F = F16Fmt<HD>;
-  constexpr int NS = A::STAGES;
+  constexpr int NS = A::STAGES, NB = A::BUFS;
   extern __shared__ __align__(128) uint8_t sm8[];
-  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full[2], d_full[2][2], q_done[2];
+  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full[NB], d_full[NB][2], q_done[NB];
   __shared__ TcShared sh;
-  __shared__ float qscale[kTcRows], oscale[kTcRows], gscale[kTcRows];
+  __shared__ float qscale[kTcRows], oscale[kTcRows], onorm[kTcRows];
   __shared__ float2 tscale[kMaxKeyTiles];  // (s_k, s_v) of each visited key tile
   __shared__ float kmin_s, vnorm_s;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -663,13 +731,14 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   const int kend = min(rows, q0 + kTcRows);
   const int n = (kend - kbeg + kTcK - 1) / kTcK;
   const int kt0 = kbeg / kTcK;
+  uint8_t* region = sm8 + A::ROWS_OFF;
   if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
   if (tid == 0) {
     for (int b = 0; b < NS; ++b) {
       tc::bar_init(&kv_full[b], 1);
       tc::bar_init(&kv_empty[b], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       tc::bar_init(&s_full[b], 1);
       tc::bar_init(&d_full[b][0], kKvCompute / 2);
       tc::bar_init(&d_full[b][1], kKvCompute / 2);
@@ -697,43 +766,37 @@ __global__ void __launch_bounds__(kKvThreads, 1)
       vnorm_s = vnorm;
     }
   }
+  if (tid < kKvCompute) {
+    // Q and dO rows, coalesced into the region, then split in place into
+    // FP16 parts with per-row scales.
+    using B = RowBlock<HD>;
+    float4* bq = reinterpret_cast<float4*>(region);
+    stage_rows<HD, kKvCompute, true>(bq, q, bq + B::CHUNKS, dout, q0, rows, W, h, tid);
+    named_sync<2, kKvCompute>();
+    const int row = tid & (kTcRows - 1);
+    float nrm;
+    const float sc = rows_to_parts16<HD, kKvCompute>(region, warp, row, nrm);
+    if (warp < 4) {
+      qscale[row] = sc;
+    } else if (warp < 8) {
+      oscale[row] = sc;
+      onorm[row] = nrm;
+    }
+    tc::fence_async_smem();  // the parts are read by the tensor cores
+  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t t0 = sh.tmem_base;
   // buffer b: S at tS + 128 b (later dS, interleaved), dP at tS + 128 b + 64
-  const uint32_t tQh = t0, tQl = t0 + 32, tDh = t0 + 64, tDl = t0 + 96, tS = t0 + 128, tG = t0 + 384;
-  if (tid < kKvCompute) {
-    // Q and dO rows through shared memory into TMEM with per-row scales.
-    using B = RowBlock<HD>;
-    float4* bq = reinterpret_cast<float4*>(sm8 + A::ROWS_OFF);
-    float4* bo = bq + B::CHUNKS;
-    stage_rows<HD, kKvCompute, true>(bq, q, bo, dout, q0, rows, W, h, tid);
-    named_sync<2, kKvCompute>();
-    if (warp < 8) {
-      const int row = tid & (kTcRows - 1);
-      const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
-      float nrm;
-      if (warp < 4) {
-        qscale[row] = block_row_to_tmem16<HD>(bq, row, tQh + lane, tQl + lane, nrm);
-      } else {
-        oscale[row] = block_row_to_tmem16<HD>(bo, row, tDh + lane, tDl + lane, nrm);
-        gscale[row] = tc::f16_scale(2.0f * nrm * vnorm_s * scale);  // |dO_row| bounds dS
-      }
-      tc::tmem_st_wait();
-    }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
+  const uint32_t tG = t0, tS = t0 + 64;
 
   if (tid < kKvCompute) {
-    // Two groups of 8 warps take alternate steps (group g: steps j = g mod 2,
-    // TMEM buffer g); in a group, thread (row, half) handles key columns
-    // [32 k2 + 16 half, +16) for k2 = 0, 1.
-    const int row = tid & (kTcRows - 1), half = (tid >> 7) & 1, grp = tid >> 8;
+    const int row = tid & (kTcRows - 1), quarter = tid >> 7;
+    const int col = 16 * quarter;  // key columns [col, col + 16) of each step
     const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
-    const float sq_inv = 1.0f / qscale[row], so_inv = 1.0f / oscale[row], rg = gscale[row];
+    const float sq_inv = 1.0f / qscale[row], so_inv = 1.0f / oscale[row];
+    const float rg = tc::f16_scale(2.0f * onorm[row] * vnorm_s * scale);  // |dO_row| bounds dS
     const float scale2 = scale * 1.4426950408889634f * sq_inv;
     const int qr = q0 + row, qs = qr - qr % T;
     const int seq0 = q0 - q0 % T;
@@ -742,55 +805,50 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     const float L = in ? lse2[(size_t)h * rows + qr] : 0.f;
     const float dl = in ? delta[(size_t)h * rows + qr] : 0.f;
     const float kmin = kmin_s;
-    const uint32_t tSb = tS + 128 * grp;
-    for (int j = grp; j < n; j += 2) {
+    for (int j = 0; j < n; ++j) {
+      const int b = j % NB;
       const float2 ts = tscale[j];
       const float coef = scale2 / ts.x;                // S_tmem -> log2 units
       const float dcoef = so_inv / ts.y;               // dP_tmem -> dP
       const float gcoef = scale * rg * (kmin / ts.x);  // dS -> stored dS
-      F16_WAIT_OR_FAIL(&s_full[grp], (j >> 1) & 1);
+      const uint32_t tSb = tS + 128 * b;
+      F16_WAIT_OR_FAIL(&s_full[b], (j / NB) & 1);
       tc::fence_after_sync();
-      const int kt = kbeg + j * kTcK;
+      const int kh = kbeg + j * kTcK + col;
+      float s[16], dp[16];
+      tc::tmem_ld16_pair(tSb + col + lane, s, tSb + 64 + col + lane, dp);
+      const bool full = one_seq && kh >= seq0 && kh + 15 <= q0;
 #pragma unroll
-      for (int k2 = 0; k2 < 2; ++k2) {
-        const int col = 32 * k2 + 16 * half;
-        float s[16], dp[16];
-        tc::tmem_ld16_pair(tSb + col + lane, s, tSb + 64 + col + lane, dp);
-        const int kh = kt + col;
-        const bool full = one_seq && kh >= seq0 && kh + 15 <= q0;
-#pragma unroll
-        for (int c = 0; c < 16; c += 2) {
-          const float2 t = fma2(make_float2(s[c], s[c + 1]), splat2(coef), splat2(-L));
-          const bool ok0 = full || (kh + c <= qr && kh + c >= qs && kh + c < rows);
-          const bool ok1 = full || (kh + c + 1 <= qr && kh + c + 1 >= qs && kh + c + 1 < rows);
-          const float2 p = make_float2(ok0 ? ex2(t.x) : 0.f, ok1 ? ex2(t.y) : 0.f);
-          const float2 g = mul2(p, fma2(make_float2(dp[c], dp[c + 1]), splat2(dcoef), splat2(-dl)));
-          s[c] = g.x;
-          s[c + 1] = g.y;
-        }
-        uint32_t hi[8], lo[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) tc::split_f16x2(s[2 * e] * gcoef, s[2 * e + 1] * gcoef, hi[e], lo[e]);
-        tc::tmem_st8u(tSb + col + lane, hi);      // over the S columns just read
-        tc::tmem_st8u(tSb + col + 8 + lane, lo);
-        tc::tmem_st_wait();
-        tc::fence_before_sync();
-        tc::bar_arrive(&d_full[grp][k2]);  // key columns [0, 32) or [32, 64)
+      for (int c = 0; c < 16; c += 2) {
+        const float2 t = fma2(make_float2(s[c], s[c + 1]), splat2(coef), splat2(-L));
+        const bool ok0 = full || (kh + c <= qr && kh + c >= qs && kh + c < rows);
+        const bool ok1 = full || (kh + c + 1 <= qr && kh + c + 1 >= qs && kh + c + 1 < rows);
+        const float2 p = make_float2(ok0 ? ex2(t.x) : 0.f, ok1 ? ex2(t.y) : 0.f);
+        const float2 g = mul2(p, fma2(make_float2(dp[c], dp[c + 1]), splat2(dcoef), splat2(-dl)));
+        s[c] = g.x;
+        s[c + 1] = g.y;
       }
+      uint32_t hi[8], lo[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tc::split_f16x2(s[2 * e] * gcoef, s[2 * e + 1] * gcoef, hi[e], lo[e]);
+      tc::tmem_st8u(tSb + col + lane, hi);  // over the S columns just read
+      tc::tmem_st8u(tSb + col + 8 + lane, lo);
+      tc::tmem_st_wait();
+      tc::fence_before_sync();
+      tc::bar_arrive(&d_full[b][quarter >> 1]);  // key columns [0, 32) or [32, 64)
     }
-    // dQ of the last two steps complete before the accumulator is read.  A
-    // group has seen the other buffer's barrier only up to the step before
-    // its own last one, so it waits for step n - 2 first: a parity wait is
-    // only exact within one phase of the barrier.
-    for (int j = max(n - 2, 0); j < n && !sh.failed; ++j)
-      if (!tc::bar_wait(&q_done[j & 1], (j >> 1) & 1)) sh.failed = 1;
+    // dQ of the last step (and so every MMA, the S and dP products that read
+    // the Q and dO parts included) complete before the accumulator is read
+    // and the region is reused.  Every compute thread passed s_full of step
+    // n - 1, issued after q_done of step n - 4, so the parity wait is exact.
+    if (!sh.failed && !tc::bar_wait(&q_done[(n - 1) % NB], ((n - 1) / NB) & 1)) sh.failed = 1;
     tc::fence_after_sync();
-    // dQ through the Q row block into coalesced row stores.
-    float4* bq = reinterpret_cast<float4*>(sm8 + A::ROWS_OFF);
-    const bool ok_out = !sh.failed;
+    // dQ through the region into coalesced row stores.
+    float4* bq = reinterpret_cast<float4*>(region);
+    const bool ok_out = __all_sync(0xffffffffu, !sh.failed);  // warp-uniform: .aligned TMEM loads
     if (ok_out) {
       const float out = 1.0f / (rg * kmin);
-      for (int oc = 16 * (tid >> 7); oc < HD; oc += 64) {  // 16-column chunks of dQ
+      for (int oc = col; oc < HD; oc += 64) {  // 16-column chunks of dQ
         float gv[16];
         tc::tmem_ld16(tG + lane + oc, gv);
         block_put16<HD>(bq, row, oc, gv, out);
@@ -812,32 +870,35 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   } else if (tid == kKvIssuer) {
     // ---------------------------------------------------------- S / dP issuer
     constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
+    const uint8_t* qh = region;
+    const uint8_t* oh = region + 2 * A::QPART;
     for (int j = 0; j < n; ++j) {
-      const int st = j % NS, b = j & 1;
+      const int st = j % NS, b = j % NB;
       const uint8_t* stage = sm8 + st * A::STAGE_BYTES;  // K, K', V, V'
       F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
-      if (j >= 2) {
-        // dQ of step j-2 has read this buffer's dS, so its S and dP are free
-        F16_WAIT_OR_FAIL(&q_done[b], ((j - 2) >> 1) & 1);
+      if (j >= NB) {
+        // dQ of step j - 3 has read this buffer's dS, so its S and dP are free
+        F16_WAIT_OR_FAIL(&q_done[b], ((j - NB) / NB) & 1);
       }
       tc::fence_after_sync();
       const uint32_t tSb = tS + 128 * b;
-      mma16_tmem_a<HD, HD / 16>(tSb, tQh, tQl, stage, stage + F::PART_BYTES, idS, false, 0);  // S_j = Q K_j^T
-      mma16_tmem_a<HD, HD / 16>(tSb + 64, tDh, tDl, stage + 2 * F::PART_BYTES, stage + 3 * F::PART_BYTES, idS,
-                                false, 0);  // dP_j = dO V_j^T
+      mma16_ss<HD, HD / 16>(tSb, qh, qh + A::QPART, stage + F::K_HI * F::PART_BYTES,
+                            stage + (F::K_HI + 1) * F::PART_BYTES, idS, false, 0);  // S_j = Q K_j^T
+      mma16_ss<HD, HD / 16>(tSb + 64, oh, oh + A::QPART, stage + F::V_HI * F::PART_BYTES,
+                            stage + (F::V_HI + 1) * F::PART_BYTES, idS, false, 0);  // dP_j = dO V_j^T
       tc::commit(&s_full[b]);
     }
   } else if (tid == kKvIssuer2) {
     // ---------------------------------------------------------- dQ issuer
     constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD, true);
     for (int j = 0; j < n; ++j) {
-      const int st = j % NS, b = j & 1;
+      const int st = j % NS, b = j % NB;
       const uint8_t* stage = sm8 + st * A::STAGE_BYTES;
       F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
       const uint32_t tSb = tS + 128 * b;
       bool ok = true;
       for (int k2 = 0; k2 < 2 && ok; ++k2) {
-        ok = tc::bar_wait(&d_full[b][k2], (j >> 1) & 1);
+        ok = tc::bar_wait(&d_full[b][k2], (j / NB) & 1);
         tc::fence_after_sync();
         // dQ += dS K over keys [32 k2, 32 k2 + 32): K steps 2 k2, 2 k2 + 1 of
         // the K tile [64 keys][HD], MN-major
@@ -932,52 +993,87 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_queries_f16(int 
   if (threadIdx.x == 0) *reinterpret_cast<float4*>(hdr + G::SCALES) = make_float4(sq, sd, nd, mdl);
 }
 
-// A CTA owns 128 keys of one head (K and V split into TMEM with per-row
-// scales) and walks their queries 64 at a time through a 4-stage ring of
-// query tiles.  Per step i (TMEM buffer b = i & 1): thread 288 issues
-// S^T = K Q^T and dP^T = V dO^T (keys on lanes, N = 64 queries); the compute
-// threads form P^T = exp2(S^T scale - lse) and store it over the S^T columns
-// they have read (FP16 hi/lo interleaved, as in dQ), then dS^T =
-// P^T (dP^T - delta) scale over the dP^T columns; thread 320 issues
-// dV += P^T dO and dK += dS^T Q.  S^T and dP^T are double-buffered, so step
-// i + 1's MMAs run while step i's softmax computes.
+// Persistent dK/dV: each CTA (one per SM) walks a fixed list of key tiles
+// (128 keys of one head; the grid-wide order puts the longest causal work
+// first and deals it to the CTAs in snake order) and, for each, their
+// queries 64 at a time through a ring of query tiles that runs on across key
+// tiles.  K and V sit in TMEM split into FP16 hi/lo columns with per-row
+// scales; dV and dK accumulate in TMEM; S^T/dP^T are double-buffered.
+// Per step i (buffer b = i & 1, i counted over the CTA's whole list):
+// thread 544 issues S^T = K Q^T and dP^T = V dO^T (keys on lanes, N = 64
+// queries); all 16 compute warps (thread (row, quarter) owns query columns
+// [16 quarter, +16)) form P^T = exp2(S^T scale - lse) and store it over the
+// S^T columns they have read (FP16 hi/lo interleaved), then
+// dS^T = P^T (dP^T - delta) scale over the dP^T columns; thread 576 issues
+// dV += P^T dO and dK += dS^T Q.
+// A loader warp (608) brings the next key tile's FP32 K and V rows into a
+// shared staging area with bulk copies, and the scales of its query tiles,
+// while the current tile runs.  Between two key tiles the compute warps
+// split the staged rows into TMEM (once the last S^T/dP^T of the previous
+// tile have been read), release the issuer, drain the previous tile's dK and
+// dV through the staging area into coalesced row stores and release the
+// staging area to the loader.
 // Scales: K rows s_K(k), V rows s_V(k); query tiles s_q(i), s_do(i).  P^T is
 // stored as P c_i, c_i = 2^13 min_i s_do / s_do(i) (P <= 1), so
 // dV = dV_tmem / (2^13 min_i s_do); dS^T as dS r(k) min_i s_q / s_q(i) with
 // r(k) = f16_scale((max|dO_q| |V_k| + max|delta|) scale), a bound on
-// |dS_k.|, so dK = dK_tmem / (r(k) min_i s_q).
+// |dS_k.|, so dK = dK_tmem / (r(k) min_i s_q); minima and maxima run over
+// the key tile's query tiles.
 // TMEM: K hi | K lo | V hi | V lo (32 each) | dV | dK (64 each) |
 // S^T0 | dP^T0 | S^T1 | dP^T1 (64 each) = 512.
 template <int HD>
 struct F16Kv {
   using G = F16Q<HD>;
   static constexpr int STAGES = 4;
-  static constexpr size_t ROWS_OFF = (size_t)STAGES * G::QTILE_BYTES;  // K and V row blocks, later dK and dV
-  static constexpr size_t smem = ROWS_OFF + 2 * RowBlock<HD>::BYTES;
+  static constexpr int ROW_BYTES = HD * 4 + 16;  // a staged row, padded: thread-per-row access is conflict-free
+  static constexpr size_t STAGING_OFF = (size_t)STAGES * G::QTILE_BYTES;
+  static constexpr size_t smem = STAGING_OFF + 2 * (size_t)kTcRows * ROW_BYTES;  // K rows, V rows
 };
 
+// Threads of the persistent dK/dV kernel: 16 compute warps, then one warp
+// each for the query-tile producer, the two issuers and the key-row loader.
+constexpr int kKvLoader = 608, kKvThreadsP = 640;
+
+// Key tile `item` of the grid-wide work list: its first key and head.
+__device__ __forceinline__ void kv_item(int item, int rows, int T, int H, int& k0, int& h) {
+  const int nt = (rows + kTcRows - 1) / kTcRows;
+  h = item % H;
+  k0 = tile_by_work(item / H, nt, rows, T, false) * kTcRows;
+}
+
+// The CTA's k-th work item in snake order over a grid of G CTAs (-1: none).
+__device__ __forceinline__ int snake_item(int k, int G, int items) {
+  const int g = k * G + ((k & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  return g < items ? g : -1;
+}
+
+// Queries steps of the key tile starting at k0: its keys' sequences to the end.
+__device__ __forceinline__ int kv_steps(int k0, int rows, int T) {
+  const int last = min(rows, k0 + kTcRows) - 1;
+  const int qend = min(rows, (last / T + 1) * T);
+  return (qend - k0 + kTcQ - 1) / kTcQ;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(kKvThreads, 1)
-    attention_backward_dkdv_f16(int rows, int W, int T, float scale, const float* __restrict__ k,
+__global__ void __launch_bounds__(kKvThreadsP, 1)
+    attention_backward_dkdv_f16(int rows, int W, int T, int H, float scale, const float* __restrict__ k,
                                 const float* __restrict__ v, const uint8_t* __restrict__ qfmt,
                                 const float* __restrict__ dv_add, float* __restrict__ dk, float* __restrict__ dv,
                                 int* __restrict__ err) {
   using G = F16Q<HD>;
-  constexpr int NS = F16Kv<HD>::STAGES;
+  using KV = F16Kv<HD>;
+  constexpr int NS = KV::STAGES, RB = KV::ROW_BYTES;
   extern __shared__ __align__(128) uint8_t sm8[];
   __shared__ uint64_t q_full[NS], q_empty[NS], s_full[2], dp_full[2], p_full[2], ds_full[2][2], g_done[2];
+  __shared__ uint64_t staged, kv_ready, staging_free;
   __shared__ TcShared sh;
   __shared__ float kscale[kTcRows], vscale[kTcRows], vnorm[kTcRows];
-  __shared__ float2 tscale[kMaxKeyTiles];  // (s_q, s_do) of each visited query tile
-  __shared__ float sqmin_s, sdomin_s, ndmax_s, dlmax_s;
+  __shared__ float2 tscale[2][kMaxKeyTiles];  // (s_q, s_do) of each query tile of a key tile, by item parity
+  __shared__ float4 tmin[2];                  // (min s_q, min s_do, max dO row norm, max |delta|), by item parity
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int k0 = tile_by_work(blockIdx.x, gridDim.x, rows, T, false) * kTcRows;
-  const int h = blockIdx.y;
+  const int items = ((rows + kTcRows - 1) / kTcRows) * H;
   const int nqt = (rows + kTcQ - 1) / kTcQ;
-  const int last = min(rows, k0 + kTcRows) - 1;
-  const int qend = min(rows, (last / T + 1) * T);
-  const int n = (qend - k0 + kTcQ - 1) / kTcQ;
-  const int qt0 = k0 / kTcQ;
+  uint8_t* staging = sm8 + KV::STAGING_OFF;
   if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
   if (tid == 0) {
     for (int b = 0; b < NS; ++b) {
@@ -987,38 +1083,16 @@ __global__ void __launch_bounds__(kKvThreads, 1)
     for (int b = 0; b < 2; ++b) {
       tc::bar_init(&s_full[b], 1);
       tc::bar_init(&dp_full[b], 1);
-      tc::bar_init(&p_full[b], kKvCompute / 2);  // one compute group per buffer
+      tc::bar_init(&p_full[b], kKvCompute);
       tc::bar_init(&ds_full[b][0], kKvCompute / 2);
       tc::bar_init(&ds_full[b][1], kKvCompute / 2);
       tc::bar_init(&g_done[b], 1);
     }
+    tc::bar_init(&staged, 33);  // loader lane 0 once (the scales), every loader lane's copies once
+    tc::bar_init(&kv_ready, kKvCompute);
+    tc::bar_init(&staging_free, kKvCompute);
     tc::bar_init_fence();
     sh.failed = 0;
-  }
-  if (warp == kKvProducer / 32) {
-    float sqm = INFINITY, sdm = INFINITY, ndm = 0.f, dlm = 0.f;
-    for (int i = threadIdx.x & 31; i < n; i += 32) {
-      const float4 sc = __ldg(reinterpret_cast<const float4*>(qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES +
-                                                              G::HEADER_OFF + G::SCALES * 4));
-      tscale[i] = make_float2(sc.x, sc.y);
-      sqm = fminf(sqm, sc.x);
-      sdm = fminf(sdm, sc.y);
-      ndm = fmaxf(ndm, sc.z);
-      dlm = fmaxf(dlm, sc.w);
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      sqm = fminf(sqm, __shfl_xor_sync(0xffffffffu, sqm, off));
-      sdm = fminf(sdm, __shfl_xor_sync(0xffffffffu, sdm, off));
-      ndm = fmaxf(ndm, __shfl_xor_sync(0xffffffffu, ndm, off));
-      dlm = fmaxf(dlm, __shfl_xor_sync(0xffffffffu, dlm, off));
-    }
-    if ((threadIdx.x & 31) == 0) {
-      sqmin_s = sqm;
-      sdomin_s = sdm;
-      ndmax_s = ndm;
-      dlmax_s = dlm;
-    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -1026,205 +1100,329 @@ __global__ void __launch_bounds__(kKvThreads, 1)
   const uint32_t t0 = sh.tmem_base;
   const uint32_t tKh = t0, tKl = t0 + 32, tVh = t0 + 64, tVl = t0 + 96, tdV = t0 + 128, tdK = t0 + 192,
                  tS = t0 + 256;  // buffer b: S^T at tS + 128 b, dP^T at tS + 128 b + 64
-  if (tid < kKvCompute) {
-    // K and V rows through shared memory into TMEM, split with per-row scales.
-    using B = RowBlock<HD>;
-    float4* bk = reinterpret_cast<float4*>(sm8 + F16Kv<HD>::ROWS_OFF);
-    float4* bv = bk + B::CHUNKS;
-    stage_rows<HD, kKvCompute, true>(bk, k, bv, v, k0, rows, W, h, tid);
-    named_sync<2, kKvCompute>();
-    if (warp < 8) {
-      const int row = tid & (kTcRows - 1);
-      const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
-      float nrm;
-      if (warp < 4) {
-        kscale[row] = block_row_to_tmem16<HD>(bk, row, tKh + lane, tKl + lane, nrm);
-      } else {
-        vscale[row] = block_row_to_tmem16<HD>(bv, row, tVh + lane, tVl + lane, nrm);
-        vnorm[row] = nrm;
-      }
-      tc::tmem_st_wait();
-    }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
+  // A wait that gives up marks the CTA failed; once failed, waits return
+  // at once, so every role runs its loops to the end (the compute warps'
+  // named barriers stay matched) and the kernel leaves quickly.
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    if (sh.failed) return false;
+    if (tc::bar_wait(bar, parity)) return true;
+    sh.failed = 1;
+    return false;
+  };
 
   if (tid < kKvCompute) {
-    // ---------------------------------------------------------- softmax
-    // Two groups of 8 warps take alternate steps (group g: steps i = g mod 2,
-    // TMEM buffer g), so one group's softmax overlaps the other's and the
-    // MMAs of both.  In a group, thread (row, half) handles query columns
-    // [32 q2 + 16 half, +16) for q2 = 0, 1.
-    const int row = tid & (kTcRows - 1), half = (tid >> 7) & 1, grp = tid >> 8;
+    // ---------------------------------------------------------- compute warps
+    const int row = tid & (kTcRows - 1), quarter = tid >> 7;
+    const int col = 16 * quarter;  // query columns [col, col + 16) of each step
     const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
-    const float scale2 = scale * 1.4426950408889634f / kscale[row];
-    const float vinv = 1.0f / vscale[row];
-    const float sqmin = sqmin_s, pv_e = 8192.0f * sdomin_s;
-    const float rk = tc::f16_scale((ndmax_s * vnorm[row] + dlmax_s) * scale);
-    const int kr = k0 + row;
-    const int ke = (kr / T + 1) * T;  // end of the key's sequence
-    const int kseq_end = (k0 / T + 1) * T;
-    const bool one_seq = (k0 + kTcRows - 1) / T == k0 / T && k0 + kTcRows <= rows;
-    const uint32_t tSb = tS + 128 * grp;
-    for (int i = grp; i < n; i += 2) {
-      const int st = i % NS;
-      const float2 ts = tscale[i];
-      const float coef = scale2 / ts.x;              // S^T_tmem -> log2 units
-      const float dcoef = vinv / ts.y;               // dP^T_tmem -> dP
-      const float pc = pv_e / ts.y;                  // P -> stored P
-      const float gc = scale * rk * (sqmin / ts.x);  // (dP - delta) P -> stored dS
-      const float* hdr = reinterpret_cast<const float*>(sm8 + st * G::QTILE_BYTES + G::HEADER_OFF);
-      F16_WAIT_OR_FAIL(&q_full[st], (i / NS) & 1);
-      F16_WAIT_OR_FAIL(&s_full[grp], (i >> 1) & 1);
+    int it = 0;                    // steps so far over the CTA's list
+    int pk0 = 0, ph = 0;           // the previous key tile, still to be drained
+    float p_ov = 0.f, p_ok = 0.f;  // its output scales
+    // Drains the previous key tile's dK and dV: TMEM -> staging -> rows.
+    auto drain = [&]() {
+      // its last step's dV and dK; warp-uniform, as the TMEM loads are .aligned
+      const bool ok = __all_sync(0xffffffffu, wait(&g_done[(it - 1) & 1], ((it - 1) >> 1) & 1));
       tc::fence_after_sync();
-      float pv[32];
+      if (ok) {
+        for (int oc = col; oc < HD; oc += 64) {  // 16-column chunks
+          float gk[16], gv[16];
+          tc::tmem_ld16_pair(tdK + lane + oc, gk, tdV + lane + oc, gv);
+          float* rk_ = reinterpret_cast<float*>(staging + row * RB) + oc;
+          float* rv_ = reinterpret_cast<float*>(staging + (kTcRows + row) * RB) + oc;
 #pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) {
-        const int col = 32 * q2 + 16 * half;  // query columns [col, col + 16) of the step
-        float* p = pv + 16 * q2;
-        float sv[16];
-        tc::tmem_ld16(tSb + col + lane, sv);
-        const int qh = k0 + i * kTcQ + col;
-        const bool full = one_seq && qh >= k0 + kTcRows - 1 && qh + 16 <= min(kseq_end, rows);
-#pragma unroll
-        for (int c = 0; c < 16; c += 4) {
-          const float4 l4 = *reinterpret_cast<const float4*>(hdr + G::LSE + col + c);
-#pragma unroll
-          for (int u = 0; u < 4; u += 2) {
-            const float2 lv = u == 0 ? make_float2(l4.x, l4.y) : make_float2(l4.z, l4.w);
-            const int q0j = qh + c + u;
-            const float2 t = fma2(make_float2(sv[c + u], sv[c + u + 1]), splat2(coef), make_float2(-lv.x, -lv.y));
-            const bool ok0 = full || (q0j >= kr && q0j < ke && q0j < rows && kr < rows);
-            const bool ok1 = full || (q0j + 1 >= kr && q0j + 1 < ke && q0j + 1 < rows && kr < rows);
-            p[c + u] = ok0 ? ex2(t.x) : 0.f;
-            p[c + u + 1] = ok1 ? ex2(t.y) : 0.f;
+          for (int e = 0; e < 16; e += 4) {
+            *reinterpret_cast<float4*>(rk_ + e) = make_float4(gk[e] * p_ok, gk[e + 1] * p_ok, gk[e + 2] * p_ok,
+                                                              gk[e + 3] * p_ok);
+            *reinterpret_cast<float4*>(rv_ + e) = make_float4(gv[e] * p_ov, gv[e + 1] * p_ov, gv[e + 2] * p_ov,
+                                                              gv[e + 3] * p_ov);
           }
         }
-        uint32_t hi[8], lo[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) tc::split_f16x2(p[2 * e] * pc, p[2 * e + 1] * pc, hi[e], lo[e]);
-        tc::tmem_st8u(tSb + col + lane, hi);  // P^T over the S^T columns just read
-        tc::tmem_st8u(tSb + col + 8 + lane, lo);
       }
-      tc::tmem_st_wait();
       tc::fence_before_sync();
-      tc::bar_arrive(&p_full[grp]);
-      F16_WAIT_OR_FAIL(&dp_full[grp], (i >> 1) & 1);
-      tc::fence_after_sync();
-#pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) {
-        const int col = 32 * q2 + 16 * half;
-        const float* p = pv + 16 * q2;
-        float dp[16];
-        tc::tmem_ld16(tSb + 64 + col + lane, dp);
-#pragma unroll
-        for (int c = 0; c < 16; c += 4) {
-          const float4 e4 = *reinterpret_cast<const float4*>(hdr + G::DELTA + col + c);
-#pragma unroll
-          for (int u = 0; u < 4; u += 2) {
-            const float2 ev = u == 0 ? make_float2(e4.x, e4.y) : make_float2(e4.z, e4.w);
-            const float2 pp = make_float2(p[c + u], p[c + u + 1]);
-            const float2 g = mul2(pp, fma2(make_float2(dp[c + u], dp[c + u + 1]), splat2(dcoef),
-                                           make_float2(-ev.x, -ev.y)));
-            dp[c + u] = g.x;
-            dp[c + u + 1] = g.y;
+      named_sync<2, kKvCompute>();
+      if (!sh.failed) {
+        constexpr int C4 = HD / 4;
+        for (int f = tid; f < 2 * kTcRows * C4; f += kKvCompute) {
+          const int r = f / C4, c = f % C4;  // staged row r (K rows, then V rows), chunk c
+          const int kr = pk0 + (r & (kTcRows - 1));
+          if (kr < rows) {
+            const size_t off = (size_t)kr * W + ph * HD + 4 * c;
+            float4 x = *reinterpret_cast<const float4*>(staging + r * RB + 16 * c);
+            if (r < kTcRows) {
+              *reinterpret_cast<float4*>(dk + off) = x;
+            } else {
+              if (dv_add != nullptr) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(dv_add + off));
+                x = make_float4(x.x + a.x, x.y + a.y, x.z + a.z, x.w + a.w);
+              }
+              *reinterpret_cast<float4*>(dv + off) = x;
+            }
           }
         }
-        uint32_t hi[8], lo[8];
+      }
+    };
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int k0, h;
+      kv_item(item, rows, T, H, k0, h);
+      const int n = kv_steps(k0, rows, T);
+      // The key tile's K and V rows: staged -> TMEM (K, V columns are free:
+      // every S^T / dP^T of the previous tile has been read).
+      const bool staged_ok = __all_sync(0xffffffffu, wait(&staged, kk & 1));  // warp-uniform: .aligned TMEM stores
+      if (warp < 8 && staged_ok) {
+        const bool kv = warp >= 4;
+        const float* src = reinterpret_cast<const float*>(staging + ((kv ? kTcRows : 0) + row) * RB);
+        float x[HD];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) tc::split_f16x2(dp[2 * e] * gc, dp[2 * e + 1] * gc, hi[e], lo[e]);
-        tc::tmem_st8u(tSb + 64 + col + lane, hi);  // dS^T over the dP^T columns just read
-        tc::tmem_st8u(tSb + 64 + col + 8 + lane, lo);
+        for (int c = 0; c < HD; c += 4) {
+          const float4 t4 = k0 + row < rows ? *reinterpret_cast<const float4*>(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+          x[c] = t4.x, x[c + 1] = t4.y, x[c + 2] = t4.z, x[c + 3] = t4.w;
+        }
+        float m = 0.f, ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < HD; ++c) {
+          m = fmaxf(m, fabsf(x[c]));
+          ss += x[c] * x[c];
+        }
+        const float sc = tc::f16_scale(m);
+        const uint32_t thi = (kv ? tVh : tKh) + lane, tlo = (kv ? tVl : tKl) + lane;
+#pragma unroll
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) tc::split_f16x2(x[c + 2 * e] * sc, x[c + 2 * e + 1] * sc, hi[e], lo[e]);
+          tc::tmem_st16u(thi + c / 2, hi);
+          tc::tmem_st16u(tlo + c / 2, lo);
+        }
+        if (kv) {
+          vscale[row] = sc;
+          vnorm[row] = sqrtf(ss);
+        } else {
+          kscale[row] = sc;
+        }
+        tc::tmem_st_wait();
+      }
+      tc::fence_before_sync();
+      named_sync<2, kKvCompute>();  // staged rows read; scales visible
+      tc::bar_arrive(&kv_ready);    // the issuer may start this key tile
+      // This tile's per-row constants.
+      const float4 mn = tmin[kk & 1];
+      const float scale2 = scale * 1.4426950408889634f / kscale[row];
+      const float vinv = 1.0f / vscale[row];
+      const float sqmin = mn.x, pv_e = 8192.0f * mn.y;
+      const float rk = tc::f16_scale((mn.z * vnorm[row] + mn.w) * scale);
+      if (kk > 0) drain();
+      tc::bar_arrive(&staging_free);  // the loader may stage the next key tile
+      pk0 = k0;
+      ph = h;
+      p_ov = 1.0f / pv_e;
+      p_ok = 1.0f / (rk * sqmin);
+      const int kr = k0 + row;
+      const int ke = (kr / T + 1) * T;  // end of the key's sequence
+      const int kseq_end = (k0 / T + 1) * T;
+      const bool one_seq = (k0 + kTcRows - 1) / T == k0 / T && k0 + kTcRows <= rows;
+      const float2* tsc = tscale[kk & 1];
+      for (int i = 0; i < n; ++i, ++it) {
+        const int st = it % NS, b = it & 1, pb = (it >> 1) & 1;
+        const float2 ts = tsc[i];
+        const float coef = scale2 / ts.x;              // S^T_tmem -> log2 units
+        const float dcoef = vinv / ts.y;               // dP^T_tmem -> dP
+        const float pc = pv_e / ts.y;                  // P -> stored P
+        const float gc = scale * rk * (sqmin / ts.x);  // (dP - delta) P -> stored dS
+        const float* hdr = reinterpret_cast<const float*>(sm8 + st * G::QTILE_BYTES + G::HEADER_OFF);
+        const uint32_t tSb = tS + 128 * b;
+        wait(&q_full[st], (it / NS) & 1);
+        wait(&s_full[b], pb);
+        tc::fence_after_sync();
+        float pv[16];
+        {
+          float sv[16];
+          tc::tmem_ld16(tSb + col + lane, sv);
+          const int qh = k0 + i * kTcQ + col;
+          const bool full = one_seq && qh >= k0 + kTcRows - 1 && qh + 16 <= min(kseq_end, rows);
+#pragma unroll
+          for (int c = 0; c < 16; c += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(hdr + G::LSE + col + c);
+#pragma unroll
+            for (int u = 0; u < 4; u += 2) {
+              const float2 lv = u == 0 ? make_float2(l4.x, l4.y) : make_float2(l4.z, l4.w);
+              const int q0j = qh + c + u;
+              const float2 t = fma2(make_float2(sv[c + u], sv[c + u + 1]), splat2(coef), make_float2(-lv.x, -lv.y));
+              const bool ok0 = full || (q0j >= kr && q0j < ke && q0j < rows && kr < rows);
+              const bool ok1 = full || (q0j + 1 >= kr && q0j + 1 < ke && q0j + 1 < rows && kr < rows);
+              pv[c + u] = ok0 ? ex2(t.x) : 0.f;
+              pv[c + u + 1] = ok1 ? ex2(t.y) : 0.f;
+            }
+          }
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) tc::split_f16x2(pv[2 * e] * pc, pv[2 * e + 1] * pc, hi[e], lo[e]);
+          tc::tmem_st8u(tSb + col + lane, hi);  // P^T over the S^T columns just read
+          tc::tmem_st8u(tSb + col + 8 + lane, lo);
+        }
         tc::tmem_st_wait();
         tc::fence_before_sync();
-        tc::bar_arrive(&ds_full[grp][q2]);
+        tc::bar_arrive(&p_full[b]);
+        wait(&dp_full[b], pb);
+        tc::fence_after_sync();
+        {
+          float dp[16];
+          tc::tmem_ld16(tSb + 64 + col + lane, dp);
+#pragma unroll
+          for (int c = 0; c < 16; c += 4) {
+            const float4 e4 = *reinterpret_cast<const float4*>(hdr + G::DELTA + col + c);
+#pragma unroll
+            for (int u = 0; u < 4; u += 2) {
+              const float2 ev = u == 0 ? make_float2(e4.x, e4.y) : make_float2(e4.z, e4.w);
+              const float2 pp = make_float2(pv[c + u], pv[c + u + 1]);
+              const float2 g = mul2(pp, fma2(make_float2(dp[c + u], dp[c + u + 1]), splat2(dcoef),
+                                             make_float2(-ev.x, -ev.y)));
+              dp[c + u] = g.x;
+              dp[c + u + 1] = g.y;
+            }
+          }
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) tc::split_f16x2(dp[2 * e] * gc, dp[2 * e + 1] * gc, hi[e], lo[e]);
+          tc::tmem_st8u(tSb + 64 + col + lane, hi);  // dS^T over the dP^T columns just read
+          tc::tmem_st8u(tSb + 64 + col + 8 + lane, lo);
+          tc::tmem_st_wait();
+          tc::fence_before_sync();
+          tc::bar_arrive(&ds_full[b][quarter >> 1]);  // query columns [0, 32) or [32, 64)
+        }
       }
     }
-    // dV and dK of the last two steps complete before the accumulators are
-    // read, step n - 2 first (a group has seen the other buffer's barrier
-    // only up to the step before its own last one, and a parity wait is only
-    // exact within one phase of the barrier).
-    for (int i = max(n - 2, 0); i < n && !sh.failed; ++i)
-      if (!tc::bar_wait(&g_done[i & 1], (i >> 1) & 1)) sh.failed = 1;
-    tc::fence_after_sync();
-    // dK and dV through the K and V row blocks into coalesced row stores.
-    using B = RowBlock<HD>;
-    float4* bk = reinterpret_cast<float4*>(sm8 + F16Kv<HD>::ROWS_OFF);
-    float4* bv = bk + B::CHUNKS;
-    const bool ok_out = !sh.failed;
-    if (ok_out) {
-      const float ov = 1.0f / pv_e, okk = 1.0f / (rk * sqmin);
-      for (int oc = 16 * (tid >> 7); oc < HD; oc += 64) {  // 16-column chunks of dK and dV
-        float gk[16], gv[16];
-        tc::tmem_ld16_pair(tdK + lane + oc, gk, tdV + lane + oc, gv);
-        block_put16<HD>(bk, row, oc, gk, okk);
-        block_put16<HD>(bv, row, oc, gv, ov);
-      }
-    }
-    named_sync<2, kKvCompute>();
-    if (ok_out) {
-      write_rows<HD, kKvCompute>(dk, bk, nullptr, k0, rows, W, h, tid);
-      write_rows<HD, kKvCompute>(dv, bv, dv_add, k0, rows, W, h, tid);
-    }
+    if (it > 0) drain();  // the last key tile
   } else if (tid == kKvProducer) {
     // ---------------------------------------------------------- query tiles
-    for (int i = 0; i < n; ++i) {
-      const int st = i % NS;
-      if (i >= NS) {
-        F16_WAIT_OR_FAIL(&q_empty[st], ((i - NS) / NS) & 1);
+    int it = 0;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int k0, h;
+      kv_item(item, rows, T, H, k0, h);
+      const int n = kv_steps(k0, rows, T), qt0 = k0 / kTcQ;
+      for (int i = 0; i < n; ++i, ++it) {
+        const int st = it % NS;
+        if (it >= NS && !wait(&q_empty[st], ((it - NS) / NS) & 1)) continue;
+        if (sh.failed) continue;
+        tc::bar_expect_tx(&q_full[st], G::QTILE_BYTES);
+        tc::bulk_g2s(sm8 + st * G::QTILE_BYTES, qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES,
+                     G::QTILE_BYTES, &q_full[st]);
       }
-      tc::bar_expect_tx(&q_full[st], G::QTILE_BYTES);
-      tc::bulk_g2s(sm8 + st * G::QTILE_BYTES, qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES, G::QTILE_BYTES,
-                   &q_full[st]);
     }
   } else if (tid == kKvIssuer) {
     // ---------------------------------------------------------- S^T / dP^T issuer
     constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcQ);
-    for (int i = 0; i < n; ++i) {
-      const int st = i % NS, b = i & 1;
-      const uint8_t* stage = sm8 + st * G::QTILE_BYTES;
-      F16_WAIT_OR_FAIL(&q_full[st], (i / NS) & 1);
-      if (i >= 2) {
-        F16_WAIT_OR_FAIL(&g_done[b], ((i - 2) >> 1) & 1);  // dV and dK of step i-2 have read this buffer
+    int it = 0;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int k0, h;
+      kv_item(item, rows, T, H, k0, h);
+      const int n = kv_steps(k0, rows, T);
+      wait(&kv_ready, kk & 1);  // this key tile's K and V are in TMEM
+      for (int i = 0; i < n; ++i, ++it) {
+        const int st = it % NS, b = it & 1;
+        const uint8_t* stage = sm8 + st * G::QTILE_BYTES;
+        wait(&q_full[st], (it / NS) & 1);
+        if (it >= 2) wait(&g_done[b], ((it - 2) >> 1) & 1);  // dV and dK of step it - 2 have read this buffer
+        tc::fence_after_sync();
+        if (sh.failed) continue;
+        const uint32_t tSb = tS + 128 * b;
+        mma16_tmem_a<HD, HD / 16>(tSb, tKh, tKl, stage + G::Q_HI * G::PART_BYTES,
+                                  stage + (G::Q_HI + 1) * G::PART_BYTES, idS, false, 0);  // S^T = K Q^T
+        tc::commit(&s_full[b]);
+        mma16_tmem_a<HD, HD / 16>(tSb + 64, tVh, tVl, stage + G::D_HI * G::PART_BYTES,
+                                  stage + (G::D_HI + 1) * G::PART_BYTES, idS, false, 0);  // dP^T = V dO^T
+        tc::commit(&dp_full[b]);
       }
-      tc::fence_after_sync();
-      const uint32_t tSb = tS + 128 * b;
-      mma16_tmem_a<HD, HD / 16>(tSb, tKh, tKl, stage + G::Q_HI * G::PART_BYTES,
-                                stage + (G::Q_HI + 1) * G::PART_BYTES, idS, false, 0);  // S^T = K Q^T
-      tc::commit(&s_full[b]);
-      mma16_tmem_a<HD, HD / 16>(tSb + 64, tVh, tVl, stage + G::D_HI * G::PART_BYTES,
-                                stage + (G::D_HI + 1) * G::PART_BYTES, idS, false, 0);  // dP^T = V dO^T
-      tc::commit(&dp_full[b]);
     }
   } else if (tid == kKvIssuer2) {
     // ---------------------------------------------------------- dV / dK issuer
     constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD, true);
-    for (int i = 0; i < n; ++i) {
-      const int st = i % NS, b = i & 1;
-      const uint8_t* stage = sm8 + st * G::QTILE_BYTES;
-      const uint32_t tSb = tS + 128 * b;
-      F16_WAIT_OR_FAIL(&q_full[st], (i / NS) & 1);
-      F16_WAIT_OR_FAIL(&p_full[b], (i >> 1) & 1);
-      tc::fence_after_sync();
-      // dV += P^T dO over the step's 64 queries (B = the dO tile [64 queries][HD], MN-major)
-      mma16_tmem_a_il<HD, 4>(tdV, tSb, stage + G::D_HI * G::PART_BYTES, stage + (G::D_HI + 1) * G::PART_BYTES, idG,
-                             i > 0, 0);
-      bool okw = true;
-      for (int q2 = 0; q2 < 2 && okw; ++q2) {
-        okw = tc::bar_wait(&ds_full[b][q2], (i >> 1) & 1);
+    int it = 0;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int k0, h;
+      kv_item(item, rows, T, H, k0, h);
+      const int n = kv_steps(k0, rows, T);
+      for (int i = 0; i < n; ++i, ++it) {
+        const int st = it % NS, b = it & 1, pb = (it >> 1) & 1;
+        const uint8_t* stage = sm8 + st * G::QTILE_BYTES;
+        const uint32_t tSb = tS + 128 * b;
+        wait(&q_full[st], (it / NS) & 1);
+        wait(&p_full[b], pb);
         tc::fence_after_sync();
-        // dK += dS^T Q over queries [32 q2, 32 q2 + 32) (B = the Q tile [64 queries][HD], MN-major)
-        if (okw)
-          mma16_tmem_a_il<HD, 2>(tdK, tSb + 64, stage + G::Q_HI * G::PART_BYTES,
-                                 stage + (G::Q_HI + 1) * G::PART_BYTES, idG, i > 0 || q2 > 0, 2 * q2);
+        // dV += P^T dO over the step's 64 queries (B = the dO tile [64 queries][HD], MN-major)
+        if (!sh.failed)
+          mma16_tmem_a_il<HD, 4>(tdV, tSb, stage + G::D_HI * G::PART_BYTES, stage + (G::D_HI + 1) * G::PART_BYTES,
+                                 idG, i > 0, 0);
+        for (int q2 = 0; q2 < 2; ++q2) {
+          wait(&ds_full[b][q2], pb);
+          tc::fence_after_sync();
+          // dK += dS^T Q over queries [32 q2, 32 q2 + 32) (B = the Q tile [64 queries][HD], MN-major)
+          if (!sh.failed)
+            mma16_tmem_a_il<HD, 2>(tdK, tSb + 64, stage + G::Q_HI * G::PART_BYTES,
+                                   stage + (G::Q_HI + 1) * G::PART_BYTES, idG, i > 0 || q2 > 0, 2 * q2);
+        }
+        if (sh.failed) continue;
+        tc::commit(&g_done[b]);
+        tc::commit(&q_empty[st]);
       }
-      if (!okw) {
-        sh.failed = 1;
-        break;
+    }
+  } else if (warp == kKvLoader / 32) {
+    // ---------------------------------------------------------- key-row loader
+    const int ln = tid & 31;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int k0, h;
+      kv_item(item, rows, T, H, k0, h);
+      const int n = kv_steps(k0, rows, T), qt0 = k0 / kTcQ;
+      if (kk > 0) wait(&staging_free, (kk - 1) & 1);  // the previous tile's rows are in TMEM, its outputs out
+      __syncwarp();
+      // Scales of the key tile's query tiles (the buffer of item kk - 2,
+      // whose steps are over).
+      float sqm = INFINITY, sdm = INFINITY, ndm = 0.f, dlm = 0.f;
+      for (int i = ln; i < n; i += 32) {
+        const float4 sc = __ldg(reinterpret_cast<const float4*>(qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES +
+                                                                G::HEADER_OFF + G::SCALES * 4));
+        tscale[kk & 1][i] = make_float2(sc.x, sc.y);
+        sqm = fminf(sqm, sc.x);
+        sdm = fminf(sdm, sc.y);
+        ndm = fmaxf(ndm, sc.z);
+        dlm = fmaxf(dlm, sc.w);
       }
-      tc::commit(&g_done[b]);
-      tc::commit(&q_empty[st]);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        sqm = fminf(sqm, __shfl_xor_sync(0xffffffffu, sqm, off));
+        sdm = fminf(sdm, __shfl_xor_sync(0xffffffffu, sdm, off));
+        ndm = fmaxf(ndm, __shfl_xor_sync(0xffffffffu, ndm, off));
+        dlm = fmaxf(dlm, __shfl_xor_sync(0xffffffffu, dlm, off));
+      }
+      if (ln == 0) tmin[kk & 1] = make_float4(sqm, sdm, ndm, dlm);
+      __syncwarp();
+      if (ln == 0) tc::bar_arrive(&staged);  // releases the scales written above
+      // The key tile's K rows, then its V rows, in 16-byte cp.async copies
+      // (consecutive lanes, consecutive chunks of a row); each lane's copies
+      // arrive on `staged` when they land.  Rows past `rows` are not copied:
+      // the compute warps read them as zero.
+      const int valid = min(kTcRows, rows - k0);
+      constexpr int C4 = HD / 4;
+      if (!sh.failed) {
+        for (int f = ln; f < 2 * valid * C4; f += 32) {
+          const int r = f / C4, c = f % C4;
+          const bool isv = r >= valid;
+          const int kr = isv ? r - valid : r;
+          const float* src = (isv ? v : k) + (size_t)(k0 + kr) * W + h * HD + 4 * c;
+          uint8_t* dst = staging + ((isv ? kTcRows : 0) + kr) * RB + 16 * c;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_addr(dst)), "l"(src) : "memory");
+        }
+      }
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_addr(&staged)) : "memory");
     }
   }
   tc::fence_before_sync();

@@ -226,7 +226,11 @@ struct AttentionOpsD final : AttentionOps {
 template <int HD>
 struct AttentionOpsTc final : AttentionOps {
   int* err;
+  int sms = 148;  // CTAs of the persistent dK/dV kernel: one per SM
   explicit AttentionOpsTc(int* e) : err(e) {
+    int dev = 0;
+    MB_CUDA(cudaGetDevice(&dev));
+    MB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     MB_CUDA(cudaFuncSetAttribute(&attention_forward_f16<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)F16Att<HD>::smem_forward));
     MB_CUDA(cudaFuncSetAttribute(&attention_backward_dq_f16<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -268,9 +272,9 @@ struct AttentionOpsTc final : AttentionOps {
                      float* dk, float* dv) override {
     attention_format_queries_f16<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), kFmtThreads, 0, s>>>(rows, W, q, dout, lse,
                                                                                            delta, qfmt16());
-    dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dkdv_f16<HD><<<grid, kKvThreads, F16Kv<HD>::smem, s>>>(
-        rows, W, T, 1.0f / sqrtf((float)hd), k, v, qfmt16(), dv_add, dk, dv, err);
+    const int items = ((rows + kTcRows - 1) / kTcRows) * H;
+    attention_backward_dkdv_f16<HD><<<std::min(items, sms), kKvThreadsP, F16Kv<HD>::smem, s>>>(
+        rows, W, T, H, 1.0f / sqrtf((float)hd), k, v, qfmt16(), dv_add, dk, dv, err);
   }
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
