@@ -449,6 +449,19 @@ bool encode_operand(CUtensorMap* map, const GemmOperand& op, int rows, int K, in
 
 }  // namespace
 
+bool encode_rows_map(CUtensorMap* map, const float* p, int rows, int width, int box_rows) {
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) != 0 || width % 4 != 0) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+  const cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  const cuuint64_t stride[1] = {(cuuint64_t)width * sizeof(float)};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, stride, box, elem,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 void gemm_prepare() {
   cudaError_t e =
       cudaFuncSetAttribute(&gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem());

@@ -1,6 +1,7 @@
 // Host interface of the tcgen05 3xTF32 GEMM (gemm_tc.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -29,5 +30,11 @@ int gemm_chunks(int K, int k_chunk);
 size_t gemm_partial_floats(int M, int N, int K, int k_chunk);
 // Kernel launches of one launch_gemm call.
 int gemm_launches(int K, int k_chunk);
+
+// TMA map of a row-major [rows][width] FP32 tensor whose boxes are box_rows
+// rows x 32 columns (128 bytes) with the 128-byte swizzle: 16-byte piece c of
+// box row r lands at piece c ^ (r % 8).  False when the base or the row
+// stride is not 16-byte aligned or the driver refuses the map.
+bool encode_rows_map(CUtensorMap* map, const float* p, int rows, int width, int box_rows);
 
 }  // namespace mb

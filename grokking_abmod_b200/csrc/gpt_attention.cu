@@ -101,9 +101,9 @@ __device__ __forceinline__ void tile_pv(float (&out)[4][Att<HD>::OC], const floa
 }
 
 template <int HD>
-__device__ __forceinline__ void store_rows(float* __restrict__ g, const float (&o)[4][Att<HD>::OC], int r0,
+__device__ __forceinline__ void store_rows(float* g, const float (&o)[4][Att<HD>::OC], int r0,
                                            int rows, int W, int h, int hd, int ty, int tx, float scale_row[4],
-                                           const float* __restrict__ add) {
+                                           const float* add) {  // may alias g (element-wise in place)
   constexpr int OC = Att<HD>::OC;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -267,8 +267,8 @@ __global__ void __launch_bounds__(256)
     attention_backward_dkdv(int rows, int W, int T, int hd, float scale, const float* __restrict__ q,
                             const float* __restrict__ k, const float* __restrict__ v,
                             const float* __restrict__ dout, const float* __restrict__ lse2,
-                            const float* __restrict__ delta, const float* __restrict__ dv_add,
-                            float* __restrict__ dk, float* __restrict__ dv) {
+                            const float* __restrict__ delta, const float* dv_add, float* __restrict__ dk,
+                            float* dv) {
   using A = Att<HD>;
   constexpr int OC = A::OC;
   extern __shared__ float4 smem4[];

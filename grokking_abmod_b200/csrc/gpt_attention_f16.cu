@@ -33,6 +33,8 @@
 // memory with coalesced accesses.  CTAs are ordered by causal work, longest
 // first.
 
+#include <cuda.h>
+
 #include "common.cuh"
 #include "tc05.cuh"
 
@@ -1006,13 +1008,14 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_queries_f16(int 
 // S^T columns they have read (FP16 hi/lo interleaved), then
 // dS^T = P^T (dP^T - delta) scale over the dP^T columns; thread 576 issues
 // dV += P^T dO and dK += dS^T Q.
-// A loader warp (608) brings the next key tile's FP32 K and V rows into a
-// shared staging area with bulk copies, and the scales of its query tiles,
-// while the current tile runs.  Between two key tiles the compute warps
-// split the staged rows into TMEM (once the last S^T/dP^T of the previous
-// tile have been read), release the issuer, drain the previous tile's dK and
-// dV through the staging area into coalesced row stores and release the
-// staging area to the loader.
+// A loader warp (608) works one key tile ahead in a shared staging area: it
+// reads the scales of the next tile's query tiles and brings its FP32 K and
+// V rows in with TMA box copies; after a key tile it writes the tile's dK
+// and dV out of the staging area with TMA box stores (dV as a TMA reduce-add
+// onto the XSA term when that is given).  Between two key tiles compute
+// warps 0-7 split the staged K and V rows into TMEM (once the last S^T/dP^T
+// of the previous tile have been read) and release the issuer, while warps
+// 8-15 move the previous tile's dK and dV from TMEM into the staging area.
 // Scales: K rows s_K(k), V rows s_V(k); query tiles s_q(i), s_do(i).  P^T is
 // stored as P c_i, c_i = 2^13 min_i s_do / s_do(i) (P <= 1), so
 // dV = dV_tmem / (2^13 min_i s_do); dS^T as dS r(k) min_i s_q / s_q(i) with
@@ -1025,10 +1028,47 @@ template <int HD>
 struct F16Kv {
   using G = F16Q<HD>;
   static constexpr int STAGES = 4;
-  static constexpr int ROW_BYTES = HD * 4 + 16;  // a staged row, padded: thread-per-row access is conflict-free
+  // Staging: the K (t = 0) and V (t = 1) rows of a key tile on the way in,
+  // its dK and dV rows on the way out, as TMA boxes of 128 rows x 32 FP32
+  // columns with the 128-byte swizzle (1024-byte aligned; one slack KB).
+  static constexpr int BOX_BYTES = kTcRows * 32 * 4;
   static constexpr size_t STAGING_OFF = (size_t)STAGES * G::QTILE_BYTES;
-  static constexpr size_t smem = STAGING_OFF + 2 * (size_t)kTcRows * ROW_BYTES;  // K rows, V rows
+  static constexpr size_t smem = STAGING_OFF + 2 * (HD / 32) * (size_t)BOX_BYTES + 1024;
 };
+
+// Float4 chunk c of staged row r of tensor t (0: K/dK, 1: V/dV): box
+// (t, c / 8), 16-byte piece (c % 8) ^ (r % 8) of the box's 128-byte row r.
+template <int HD>
+__device__ __forceinline__ float4* staged_chunk(uint8_t* staging, int t, int r, int c) {
+  return reinterpret_cast<float4*>(staging + (t * (HD / 32) + (c >> 3)) * F16Kv<HD>::BOX_BYTES + r * 128 +
+                                   (((c & 7) ^ (r & 7)) << 4));
+}
+
+// TMA tensor copies of one 2D box (x: first column, a multiple of 32 FP32
+// columns, so every copy starts 16-byte aligned; y: first row >= 0).
+__device__ __forceinline__ void tma_load_box(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(tc::smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc::smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_box(const CUtensorMap* map, int x, int y, const void* src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(tc::smem_addr(src))
+               : "memory");
+}
+// global += box, element-wise (one addition per element: exact order-free).
+__device__ __forceinline__ void tma_add_box(const CUtensorMap* map, int x, int y, const void* src) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(tc::smem_addr(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Threads of the persistent dK/dV kernel: 16 compute warps, then one warp
 // each for the query-tile producer, the two issuers and the key-row loader.
@@ -1047,7 +1087,7 @@ __device__ __forceinline__ int snake_item(int k, int G, int items) {
   return g < items ? g : -1;
 }
 
-// Queries steps of the key tile starting at k0: its keys' sequences to the end.
+// Query steps of the key tile starting at k0: its keys' sequences to the end.
 __device__ __forceinline__ int kv_steps(int k0, int rows, int T) {
   const int last = min(rows, k0 + kTcRows) - 1;
   const int qend = min(rows, (last / T + 1) * T);
@@ -1056,24 +1096,25 @@ __device__ __forceinline__ int kv_steps(int k0, int rows, int T) {
 
 template <int HD>
 __global__ void __launch_bounds__(kKvThreadsP, 1)
-    attention_backward_dkdv_f16(int rows, int W, int T, int H, float scale, const float* __restrict__ k,
-                                const float* __restrict__ v, const uint8_t* __restrict__ qfmt,
-                                const float* __restrict__ dv_add, float* __restrict__ dk, float* __restrict__ dv,
-                                int* __restrict__ err) {
+    attention_backward_dkdv_f16(int rows, int T, int H, float scale, const __grid_constant__ CUtensorMap map_k,
+                                const __grid_constant__ CUtensorMap map_v, const uint8_t* __restrict__ qfmt,
+                                const __grid_constant__ CUtensorMap map_dk, const __grid_constant__ CUtensorMap map_dv,
+                                int dv_add, int* __restrict__ err) {
   using G = F16Q<HD>;
   using KV = F16Kv<HD>;
-  constexpr int NS = KV::STAGES, RB = KV::ROW_BYTES;
+  constexpr int NS = KV::STAGES;
   extern __shared__ __align__(128) uint8_t sm8[];
   __shared__ uint64_t q_full[NS], q_empty[NS], s_full[2], dp_full[2], p_full[2], ds_full[2][2], g_done[2];
-  __shared__ uint64_t staged, kv_ready, staging_free;
+  __shared__ uint64_t staged, kv_ready, drained;
   __shared__ TcShared sh;
-  __shared__ float kscale[kTcRows], vscale[kTcRows], vnorm[kTcRows];
+  __shared__ float kscale[2][kTcRows], vscale[2][kTcRows], vnorm[2][kTcRows];  // by item parity
   __shared__ float2 tscale[2][kMaxKeyTiles];  // (s_q, s_do) of each query tile of a key tile, by item parity
   __shared__ float4 tmin[2];                  // (min s_q, min s_do, max dO row norm, max |delta|), by item parity
   const int tid = threadIdx.x, warp = tid >> 5;
   const int items = ((rows + kTcRows - 1) / kTcRows) * H;
   const int nqt = (rows + kTcQ - 1) / kTcQ;
   uint8_t* staging = sm8 + KV::STAGING_OFF;
+  staging += (1024u - (tc::smem_addr(staging) & 1023u)) & 1023u;  // the swizzle's period
   if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
   if (tid == 0) {
     for (int b = 0; b < NS; ++b) {
@@ -1088,9 +1129,9 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
       tc::bar_init(&ds_full[b][1], kKvCompute / 2);
       tc::bar_init(&g_done[b], 1);
     }
-    tc::bar_init(&staged, 33);  // loader lane 0 once (the scales), every loader lane's copies once
+    tc::bar_init(&staged, 1);
     tc::bar_init(&kv_ready, kKvCompute);
-    tc::bar_init(&staging_free, kKvCompute);
+    tc::bar_init(&drained, kKvCompute);
     tc::bar_init_fence();
     sh.failed = 0;
   }
@@ -1116,113 +1157,116 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
     const int col = 16 * quarter;  // query columns [col, col + 16) of each step
     const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
     int it = 0;                    // steps so far over the CTA's list
-    int pk0 = 0, ph = 0;           // the previous key tile, still to be drained
-    float p_ov = 0.f, p_ok = 0.f;  // its output scales
-    // Drains the previous key tile's dK and dV: TMEM -> staging -> rows.
-    auto drain = [&]() {
-      // its last step's dV and dK; warp-uniform, as the TMEM loads are .aligned
+    float p_ov = 0.f, p_ok = 0.f;  // output scales of the previous key tile
+    // Warps 8-15 carry the previous key tile's dK (warps 8-11) or dV
+    // (warps 12-15) rows from TMEM into staging, where the loader writes them
+    // out: the first half of each row waits in registers while warps 0-7
+    // still read the staged K and V rows.  Warp-uniform waits: the TMEM loads
+    // are .aligned.
+    const int half8 = (warp >> 2) & 1;  // for warps 8-15: 0 = dK, 1 = dV
+    const uint32_t dsrc = (half8 ? tdV : tdK) + lane;
+    float g[HD / 2];  // the first half of the row until staging is free
+    auto drain_load = [&]() {
       const bool ok = __all_sync(0xffffffffu, wait(&g_done[(it - 1) & 1], ((it - 1) >> 1) & 1));
       tc::fence_after_sync();
       if (ok) {
-        for (int oc = col; oc < HD; oc += 64) {  // 16-column chunks
-          float gk[16], gv[16];
-          tc::tmem_ld16_pair(tdK + lane + oc, gk, tdV + lane + oc, gv);
-          float* rk_ = reinterpret_cast<float*>(staging + row * RB) + oc;
-          float* rv_ = reinterpret_cast<float*>(staging + (kTcRows + row) * RB) + oc;
 #pragma unroll
-          for (int e = 0; e < 16; e += 4) {
-            *reinterpret_cast<float4*>(rk_ + e) = make_float4(gk[e] * p_ok, gk[e + 1] * p_ok, gk[e + 2] * p_ok,
-                                                              gk[e + 3] * p_ok);
-            *reinterpret_cast<float4*>(rv_ + e) = make_float4(gv[e] * p_ov, gv[e + 1] * p_ov, gv[e + 2] * p_ov,
-                                                              gv[e + 3] * p_ov);
-          }
+        for (int c = 0; c < HD / 2; c += 16) {
+          float a16[16];
+          tc::tmem_ld16(dsrc + c, a16);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) g[c + e] = a16[e];
         }
       }
-      tc::fence_before_sync();
-      named_sync<2, kKvCompute>();
-      if (!sh.failed) {
-        constexpr int C4 = HD / 4;
-        for (int f = tid; f < 2 * kTcRows * C4; f += kKvCompute) {
-          const int r = f / C4, c = f % C4;  // staged row r (K rows, then V rows), chunk c
-          const int kr = pk0 + (r & (kTcRows - 1));
-          if (kr < rows) {
-            const size_t off = (size_t)kr * W + ph * HD + 4 * c;
-            float4 x = *reinterpret_cast<const float4*>(staging + r * RB + 16 * c);
-            if (r < kTcRows) {
-              *reinterpret_cast<float4*>(dk + off) = x;
-            } else {
-              if (dv_add != nullptr) {
-                const float4 a = __ldg(reinterpret_cast<const float4*>(dv_add + off));
-                x = make_float4(x.x + a.x, x.y + a.y, x.z + a.z, x.w + a.w);
-              }
-              *reinterpret_cast<float4*>(dv + off) = x;
-            }
-          }
-        }
-      }
+      return ok;
     };
-    for (int kk = 0;; ++kk) {
+    auto drain_store = [&](bool ok) {
+      if (!ok) return;
+      const float mul = half8 ? p_ov : p_ok;
+#pragma unroll
+      for (int c = 0; c < HD / 2; c += 4)
+        *staged_chunk<HD>(staging, half8, row, c / 4) = make_float4(g[c] * mul, g[c + 1] * mul, g[c + 2] * mul,
+                                                                    g[c + 3] * mul);
+#pragma unroll
+      for (int c = HD / 2; c < HD; c += 16) {
+        float a16[16];
+        tc::tmem_ld16(dsrc + c, a16);
+#pragma unroll
+        for (int e = 0; e < 16; e += 4)
+          *staged_chunk<HD>(staging, half8, row, (c + e) / 4) =
+              make_float4(a16[e] * mul, a16[e + 1] * mul, a16[e + 2] * mul, a16[e + 3] * mul);
+      }
+      tc::fence_async_smem();  // the loader's TMA stores read these rows
+    };
+    int kk = 0;
+    for (;; ++kk) {
       const int item = snake_item(kk, gridDim.x, items);
       if (item < 0) break;
       int k0, h;
       kv_item(item, rows, T, H, k0, h);
       const int n = kv_steps(k0, rows, T);
-      // The key tile's K and V rows: staged -> TMEM (K, V columns are free:
-      // every S^T / dP^T of the previous tile has been read).
-      const bool staged_ok = __all_sync(0xffffffffu, wait(&staged, kk & 1));  // warp-uniform: .aligned TMEM stores
-      if (warp < 8 && staged_ok) {
-        const bool kv = warp >= 4;
-        const float* src = reinterpret_cast<const float*>(staging + ((kv ? kTcRows : 0) + row) * RB);
-        float x[HD];
+      const int pb_ = kk & 1;
+      // Warps 0-7: the key tile's staged FP32 K (warps 0-3) and V (4-7) rows
+      // -> FP16 hi/lo TMEM columns with per-row scales (the K, V columns are
+      // free: every S^T / dP^T of the previous tile has been read).
+      // Warps 8-15 meanwhile take the previous tile's dK / dV out of TMEM.
+      bool dok = false;
+      if (warp < 8) {
+        const bool staged_ok = __all_sync(0xffffffffu, wait(&staged, kk & 1));
+        if (staged_ok) {
+          const bool isv = warp >= 4;
+          // Two passes over the staged row (its largest magnitude and norm,
+          // then the split), so the row is never held in registers whole.
+          float m = 0.f, ss = 0.f;  // rows past `rows` arrive as zeros (TMA fill)
 #pragma unroll
-        for (int c = 0; c < HD; c += 4) {
-          const float4 t4 = k0 + row < rows ? *reinterpret_cast<const float4*>(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-          x[c] = t4.x, x[c + 1] = t4.y, x[c + 2] = t4.z, x[c + 3] = t4.w;
-        }
-        float m = 0.f, ss = 0.f;
+          for (int c = 0; c < HD / 4; ++c) {
+            const float4 t4 = *staged_chunk<HD>(staging, isv, row, c);
+            m = fmaxf(fmaxf(m, fmaxf(fabsf(t4.x), fabsf(t4.y))), fmaxf(fabsf(t4.z), fabsf(t4.w)));
+            ss += t4.x * t4.x + t4.y * t4.y + t4.z * t4.z + t4.w * t4.w;
+          }
+          const float sc = tc::f16_scale(m);
+          const uint32_t thi = (isv ? tVh : tKh) + lane, tlo = (isv ? tVl : tKl) + lane;
 #pragma unroll
-        for (int c = 0; c < HD; ++c) {
-          m = fmaxf(m, fabsf(x[c]));
-          ss += x[c] * x[c];
-        }
-        const float sc = tc::f16_scale(m);
-        const uint32_t thi = (kv ? tVh : tKh) + lane, tlo = (kv ? tVl : tKl) + lane;
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int c = 0; c < HD; c += 32) {
-          uint32_t hi[16], lo[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) tc::split_f16x2(x[c + 2 * e] * sc, x[c + 2 * e + 1] * sc, hi[e], lo[e]);
-          tc::tmem_st16u(thi + c / 2, hi);
-          tc::tmem_st16u(tlo + c / 2, lo);
+            for (int e = 0; e < 16; e += 2) {
+              const float4 t4 = *staged_chunk<HD>(staging, isv, row, (c + 2 * e) / 4);
+              tc::split_f16x2(t4.x * sc, t4.y * sc, hi[e], lo[e]);
+              tc::split_f16x2(t4.z * sc, t4.w * sc, hi[e + 1], lo[e + 1]);
+            }
+            tc::tmem_st16u(thi + c / 2, hi);
+            tc::tmem_st16u(tlo + c / 2, lo);
+          }
+          if (isv) {
+            vscale[pb_][row] = sc;
+            vnorm[pb_][row] = sqrtf(ss);
+          } else {
+            kscale[pb_][row] = sc;
+          }
+          tc::tmem_st_wait();
         }
-        if (kv) {
-          vscale[row] = sc;
-          vnorm[row] = sqrtf(ss);
-        } else {
-          kscale[row] = sc;
-        }
-        tc::tmem_st_wait();
+      } else if (kk > 0) {
+        dok = drain_load();
       }
       tc::fence_before_sync();
       named_sync<2, kKvCompute>();  // staged rows read; scales visible
       tc::bar_arrive(&kv_ready);    // the issuer may start this key tile
+      if (warp >= 8 && kk > 0) drain_store(dok);
+      tc::bar_arrive(&drained);  // staging holds the previous tile's dK and dV (or nothing)
       // This tile's per-row constants.
-      const float4 mn = tmin[kk & 1];
-      const float scale2 = scale * 1.4426950408889634f / kscale[row];
-      const float vinv = 1.0f / vscale[row];
+      const float4 mn = tmin[pb_];
+      const float scale2 = scale * 1.4426950408889634f / kscale[pb_][row];
+      const float vinv = 1.0f / vscale[pb_][row];
       const float sqmin = mn.x, pv_e = 8192.0f * mn.y;
-      const float rk = tc::f16_scale((mn.z * vnorm[row] + mn.w) * scale);
-      if (kk > 0) drain();
-      tc::bar_arrive(&staging_free);  // the loader may stage the next key tile
-      pk0 = k0;
-      ph = h;
+      const float rk = tc::f16_scale((mn.z * vnorm[pb_][row] + mn.w) * scale);
       p_ov = 1.0f / pv_e;
       p_ok = 1.0f / (rk * sqmin);
       const int kr = k0 + row;
       const int ke = (kr / T + 1) * T;  // end of the key's sequence
       const int kseq_end = (k0 / T + 1) * T;
       const bool one_seq = (k0 + kTcRows - 1) / T == k0 / T && k0 + kTcRows <= rows;
-      const float2* tsc = tscale[kk & 1];
+      const float2* tsc = tscale[pb_];
       for (int i = 0; i < n; ++i, ++it) {
         const int st = it % NS, b = it & 1, pb = (it >> 1) & 1;
         const float2 ts = tsc[i];
@@ -1293,7 +1337,16 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
         }
       }
     }
-    if (it > 0) drain();  // the last key tile
+    if (kk > 0) {
+      // The last key tile, once the loader has written out the one before.
+      bool dok = false;
+      if (warp >= 8) {
+        wait(&staged, kk & 1);
+        dok = drain_load();
+        drain_store(dok);
+      }
+      tc::bar_arrive(&drained);
+    }
   } else if (tid == kKvProducer) {
     // ---------------------------------------------------------- query tiles
     int it = 0;
@@ -1376,21 +1429,38 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
   } else if (warp == kKvLoader / 32) {
     // ---------------------------------------------------------- key-row loader
     const int ln = tid & 31;
-    for (int kk = 0;; ++kk) {
-      const int item = snake_item(kk, gridDim.x, items);
-      if (item < 0) break;
+    // dK and dV of work item j (TMEM -> staging by the compute warps) out to
+    // its rows with TMA box stores; dV is added onto the XSA term instead
+    // when one is given.  Rows past `rows` are clipped by the TMA.  Lane 0.
+    auto write_out = [&](int j) {
       int k0, h;
-      kv_item(item, rows, T, H, k0, h);
-      const int n = kv_steps(k0, rows, T), qt0 = k0 / kTcQ;
-      if (kk > 0) wait(&staging_free, (kk - 1) & 1);  // the previous tile's rows are in TMEM, its outputs out
-      __syncwarp();
-      // Scales of the key tile's query tiles (the buffer of item kk - 2,
-      // whose steps are over).
+      kv_item(snake_item(j, gridDim.x, items), rows, T, H, k0, h);
+      if (!sh.failed) {
+#pragma unroll
+        for (int half = 0; half < HD / 32; ++half) {
+          const int x = h * HD + 32 * half;
+          tma_store_box(&map_dk, x, k0, staging + half * KV::BOX_BYTES);
+          const uint8_t* vb = staging + (HD / 32 + half) * KV::BOX_BYTES;
+          if (dv_add) {
+            tma_add_box(&map_dv, x, k0, vb);
+          } else {
+            tma_store_box(&map_dv, x, k0, vb);
+          }
+        }
+      }
+      bulk_commit();
+    };
+    // Work item kk: the scales of its query tiles (all lanes), then its K and
+    // V rows as TMA boxes (lane 0; rows past `rows` fill with zeros).
+    auto load = [&](int kk) {
+      int k0, h;
+      kv_item(snake_item(kk, gridDim.x, items), rows, T, H, k0, h);
+      const int n = kv_steps(k0, rows, T), qt0 = k0 / kTcQ, pb = kk & 1;
       float sqm = INFINITY, sdm = INFINITY, ndm = 0.f, dlm = 0.f;
       for (int i = ln; i < n; i += 32) {
         const float4 sc = __ldg(reinterpret_cast<const float4*>(qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES +
                                                                 G::HEADER_OFF + G::SCALES * 4));
-        tscale[kk & 1][i] = make_float2(sc.x, sc.y);
+        tscale[pb][i] = make_float2(sc.x, sc.y);
         sqm = fminf(sqm, sc.x);
         sdm = fminf(sdm, sc.y);
         ndm = fmaxf(ndm, sc.z);
@@ -1403,26 +1473,47 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
         ndm = fmaxf(ndm, __shfl_xor_sync(0xffffffffu, ndm, off));
         dlm = fmaxf(dlm, __shfl_xor_sync(0xffffffffu, dlm, off));
       }
-      if (ln == 0) tmin[kk & 1] = make_float4(sqm, sdm, ndm, dlm);
+      if (ln == 0) tmin[pb] = make_float4(sqm, sdm, ndm, dlm);
       __syncwarp();
-      if (ln == 0) tc::bar_arrive(&staged);  // releases the scales written above
-      // The key tile's K rows, then its V rows, in 16-byte cp.async copies
-      // (consecutive lanes, consecutive chunks of a row); each lane's copies
-      // arrive on `staged` when they land.  Rows past `rows` are not copied:
-      // the compute warps read them as zero.
-      const int valid = min(kTcRows, rows - k0);
-      constexpr int C4 = HD / 4;
-      if (!sh.failed) {
-        for (int f = ln; f < 2 * valid * C4; f += 32) {
-          const int r = f / C4, c = f % C4;
-          const bool isv = r >= valid;
-          const int kr = isv ? r - valid : r;
-          const float* src = (isv ? v : k) + (size_t)(k0 + kr) * W + h * HD + 4 * c;
-          uint8_t* dst = staging + ((isv ? kTcRows : 0) + kr) * RB + 16 * c;
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_addr(dst)), "l"(src) : "memory");
+      if (ln == 0) {
+        // arrive (releasing the scales) and expect the boxes' bytes
+        tc::bar_expect_tx(&staged, sh.failed ? 0u : (uint32_t)(2 * (HD / 32) * KV::BOX_BYTES));
+        if (!sh.failed) {
+#pragma unroll
+          for (int half = 0; half < HD / 32; ++half) {
+            tma_load_box(staging + half * KV::BOX_BYTES, &map_k, h * HD + 32 * half, k0, &staged);
+            tma_load_box(staging + (HD / 32 + half) * KV::BOX_BYTES, &map_v, h * HD + 32 * half, k0, &staged);
+          }
         }
       }
-      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_addr(&staged)) : "memory");
+    };
+    int ni = 0;
+    while (snake_item(ni, gridDim.x, items) >= 0) ++ni;
+    for (int kk = 0; kk < ni; ++kk) {
+      if (kk >= 1) wait(&drained, (kk - 1) & 1);  // rows kk - 1 are in TMEM; staging holds dK/dV of kk - 2
+      __syncwarp();
+      if (kk >= 2 && ln == 0) {
+        write_out(kk - 2);
+        bulk_wait_read();  // the stores have read staging before it is refilled
+      }
+      __syncwarp();
+      load(kk);
+    }
+    if (ni > 0) {
+      wait(&drained, (ni - 1) & 1);
+      if (ln == 0) {
+        if (ni >= 2) {
+          write_out(ni - 2);
+          bulk_wait_read();
+        }
+        tc::bar_arrive(&staged);  // staging is free for the last tile's dK and dV
+      }
+      wait(&drained, ni & 1);
+      if (ln == 0) {
+        write_out(ni - 1);
+        bulk_wait_all();  // every store done before the CTA leaves
+      }
+      __syncwarp();
     }
   }
   tc::fence_before_sync();

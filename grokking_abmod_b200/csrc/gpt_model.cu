@@ -184,7 +184,7 @@ struct AttentionOps {
                        const float* v, float* o, float* lse) = 0;
   virtual void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q,
                              const float* k, const float* v, const float* dout, const float* lse,
-                             const float* delta, const float* dv_add, float* dk, float* dv) = 0;
+                             const float* delta, const float* dv_add, float* dk, float* dv) = 0;  // dv_add may be dv
   virtual void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                            const float* v, const float* dout, const float* lse, const float* delta,
                            float* dq) = 0;
@@ -272,9 +272,17 @@ struct AttentionOpsTc final : AttentionOps {
                      float* dk, float* dv) override {
     attention_format_queries_f16<HD><<<dim3((rows + kTcQ - 1) / kTcQ, H), kFmtThreads, 0, s>>>(rows, W, q, dout, lse,
                                                                                            delta, qfmt16());
+    // TMA maps over the [rows][W] K, V, dK and dV tensors, 128 x 32 boxes.
+    CUtensorMap mk, mv, mdk, mdv;
+    require(encode_rows_map(&mk, k, rows, W, kTcRows) && encode_rows_map(&mv, v, rows, W, kTcRows) &&
+                encode_rows_map(&mdk, dk, rows, W, kTcRows) && encode_rows_map(&mdv, dv, rows, W, kTcRows),
+            "attention backward: TMA maps need 16-byte aligned tensors", MB_ERR_UNSUPPORTED);
+    // dV is added onto the XSA term: in place when dv_add is dv, else onto a copy.
+    if (dv_add != nullptr && dv_add != dv)
+      MB_CUDA(cudaMemcpyAsync(dv, dv_add, (size_t)rows * W * sizeof(float), cudaMemcpyDeviceToDevice, s));
     const int items = ((rows + kTcRows - 1) / kTcRows) * H;
     attention_backward_dkdv_f16<HD><<<std::min(items, sms), kKvThreadsP, F16Kv<HD>::smem, s>>>(
-        rows, W, T, H, 1.0f / sqrtf((float)hd), k, v, qfmt16(), dv_add, dk, dv, err);
+        rows, T, H, 1.0f / sqrtf((float)hd), mk, mv, qfmt16(), mdk, mdv, dv_add != nullptr ? 1 : 0, err);
   }
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
@@ -341,7 +349,7 @@ struct Workspace {
   std::vector<float*> q, k, v, o, xm, lse;
   // nf and g are one allocation ([2][rows][W]), as are dlog and indicator
   // ([2][rows][V]): the embedding gradient contracts both halves in one GEMM.
-  float *nf, *dlog, *indicator, *logits, *loss_rows, *g, *dO, *dvx, *dxm, *delta, *dq, *dk, *dv, *emb_partial, *dE;
+  float *nf, *dlog, *indicator, *logits, *loss_rows, *g, *dO, *dvx, *dxm, *delta, *dq, *dk, *emb_partial, *dE;
   float *head_inv, *head_dn;  // final RMSNorm's 1/rms per row and the head's dn = dlogits E
   float* emb_mesh_partial;
   float* att_scratch;
@@ -703,7 +711,6 @@ class GptModel {
     ws->delta = a.alloc<float>((size_t)H * rows);
     ws->dq = a.alloc<float>(NW);
     ws->dk = a.alloc<float>(NW);
-    ws->dv = a.alloc<float>(NW);
     ws->emb_k_chunk = embedding_k_chunk(rows);
     ws->emb_partial = a.alloc<float>(std::max<size_t>(1, gemm_partial_floats(V, W, 2 * rows, ws->emb_k_chunk)));
     ws->dE = a.alloc<float>((size_t)V * W);
@@ -841,12 +848,12 @@ class GptModel {
       mark("attention_backward_dkdv");
       attention_->layer = b;
       attention_->backward_dkdv(stream_, ws.rows, W, ws.seq, H, W / H, ws.q[b], ws.k[b], ws.v[b], ws.dO, ws.lse[b],
-                                ws.delta, ws.dvx, ws.dk, ws.dv);
+                                ws.delta, ws.dvx, ws.dk, ws.dvx);  // dV added into the XSA term in place
       mark("attention_backward_dq");
       attention_->backward_dq(stream_, ws.rows, W, ws.seq, H, W / H, ws.q[b], ws.k[b], ws.v[b], ws.dO, ws.lse[b],
                               ws.delta, ws.dq);
       mark("qkv_backward");
-      blocks_->qkv_backward(stream_, ws.grid_qb, d, ws.dq, ws.dk, ws.dv, ws.x[b], ws.dxm, group(bg.query),
+      blocks_->qkv_backward(stream_, ws.grid_qb, d, ws.dq, ws.dk, ws.dvx, ws.x[b], ws.dxm, group(bg.query),
                             group(bg.key), group(bg.value), ws.rope, ws.g, ws.part[bg.query], ws.part[bg.key],
                             ws.part[bg.value]);
     }
