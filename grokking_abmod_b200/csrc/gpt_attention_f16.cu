@@ -597,68 +597,6 @@ __global__ void __launch_bounds__(kTcThreads2, 1)
   if (warp == 0) tc::tmem_dealloc(t0, 512);
 }
 
-// One 128-row block of rows into FP16 hi/lo parts in shared memory (the
-// blocked layout of tc05.cuh, [128 rows][HD]), in place of the FP32 row block
-// it was staged in: every thread (warps 0-7; rows of A for warps 0-3, of B
-// for warps 4-7) first reads its row, then all of them write.  Returns the
-// row's scale; `norm` receives its Euclidean norm.  Other threads of the CTA
-// call only the two named barriers.
-template <int HD, int NT>
-__device__ __forceinline__ float rows_to_parts16(uint8_t* region, int warp, int r, float& norm) {
-  using B = RowBlock<HD>;
-  constexpr int PB = kTcRows * HD * 2;  // one [128][HD] FP16 part
-  float x[HD];
-  float s = 1.0f;
-  norm = 0.f;
-  if (warp < 8) {
-    const float4* blk = reinterpret_cast<const float4*>(region) + (warp < 4 ? 0 : B::CHUNKS);
-#pragma unroll
-    for (int c = 0; c < B::C4; ++c) {
-      const float4 v = blk[B::at(r, c)];
-      x[4 * c] = v.x, x[4 * c + 1] = v.y, x[4 * c + 2] = v.z, x[4 * c + 3] = v.w;
-    }
-    float m = 0.f, ss = 0.f;
-#pragma unroll
-    for (int c = 0; c < HD; ++c) {
-      m = fmaxf(m, fabsf(x[c]));
-      ss += x[c] * x[c];
-    }
-    norm = sqrtf(ss);
-    s = tc::f16_scale(m);
-  }
-  named_sync<2, NT>();  // every row is read before any part is written over the block
-  if (warp < 8) {
-    uint4* hi = reinterpret_cast<uint4*>(region + (warp < 4 ? 0 : 2 * PB));
-    uint4* lo = reinterpret_cast<uint4*>(region + (warp < 4 ? PB : 3 * PB));
-#pragma unroll
-    for (int c = 0; c < HD; c += 8) {
-      uint32_t h[4], l[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) tc::split_f16x2(x[c + 2 * e] * s, x[c + 2 * e + 1] * s, h[e], l[e]);
-      const int q = tc::blk16(r, c, HD) / 8;  // 16-byte core-matrix row
-      hi[q] = make_uint4(h[0], h[1], h[2], h[3]);
-      lo[q] = make_uint4(l[0], l[1], l[2], l[3]);
-    }
-  }
-  return s;
-}
-
-// D (+)= A . B^T with A and B K-major FP16 hi/lo shared tiles of KC columns
-// (A: 128 rows, B: N rows), K steps [s0, s0 + NSTEP): three MMAs per step.
-template <int KC, int NSTEP>
-__device__ __forceinline__ void mma16_ss(uint32_t d, const void* ah, const void* al, const void* bh, const void* bl,
-                                         uint32_t idesc, bool accumulate, int s0) {
-#pragma unroll
-  for (int i = 0; i < NSTEP; ++i) {
-    const int s = s0 + i;
-    const uint64_t a_h = tc::desc_kmajor16(ah, KC, s), a_l = tc::desc_kmajor16(al, KC, s);
-    const uint64_t b_h = tc::desc_kmajor16(bh, KC, s), b_l = tc::desc_kmajor16(bl, KC, s);
-    tc::mma_ss_f16(d, a_h, b_h, idesc, (accumulate || i > 0) ? 1u : 0u);
-    tc::mma_ss_f16(d, a_h, b_l, idesc, 1u);
-    tc::mma_ss_f16(d, a_l, b_h, idesc, 1u);
-  }
-}
-
 // D (+)= A . B^T over K steps [s0, s0 + NSTEP) of 16 elements with A's FP16
 // hi and lo parts interleaved in TMEM: step s reads hi columns [16s, 16s + 8)
 // and lo columns [16s + 8, 16s + 16) of `a`.  B is MN-major (tc05.cuh
@@ -674,252 +612,6 @@ __device__ __forceinline__ void mma16_tmem_a_il(uint32_t d, uint32_t a, const vo
     tc::mma_ts_f16(d, a + 16 * s, b_l, idesc, 1u);
     tc::mma_ts_f16(d, a + 16 * s + 8, b_h, idesc, 1u);
   }
-}
-
-// ---------------------------------------------------------------------- dQ
-// A CTA owns 128 query rows of one head and walks their key tiles (K and V
-// FP16 parts and scales from the key format).  Q and dO sit in shared memory
-// as FP16 hi/lo parts with per-row scales (A operands of S = Q K^T and
-// dP = dO V^T), so TMEM holds dQ and three S/dP buffers: step j uses buffer
-// j mod 3, and step j + 3's products wait only for dQ of step j.  Per 64-key
-// step: thread 544 issues S and dP; all 16 compute warps (thread (row,
-// quarter) owns key columns [16 quarter, +16)) form dS = P (dP - delta)
-// scale, each 32-key half handed to thread 576 for dQ += dS K as soon as it
-// is stored.  dS is written over the S columns its thread has just read (FP16
-// hi parts in S columns [16m, 16m + 8), lo parts in [16m + 8, 16m + 16) for
-// keys [16m, 16m + 16)), so no thread overwrites columns another has yet to
-// read.
-// Scales: Q rows s_q(i), dO rows t(i); key tiles s_k(j), s_v(j); dS_ij is
-// stored as dS_ij r(i) d(j) with r(i) = f16_scale(2 |dO_i| max|V_row| scale),
-// a bound on |dS_i.| (|dP| and |delta| are at most |dO_i| max|V_row|), and
-// d(j) = min_j s_k / s_k(j), so dQ_i = dQ_tmem / (r(i) min_j s_k).
-// TMEM: dQ | (S | dP) x 3, 64 columns each = 448 (512 allocated).
-// Shared memory: the key ring, then one 64 KB region that holds the FP32 Q
-// and dO rows, then their FP16 parts (Q, Q', dO, dO'), then dQ on the way
-// out.
-template <int HD>
-struct F16Dq {
-  using F = F16Fmt<HD>;
-  static constexpr int STAGES = 4;
-  static constexpr int BUFS = 3;
-  static constexpr int STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', V, V'
-  static constexpr int QPART = kTcRows * HD * 2;         // one [128 rows][HD] FP16 part
-  static constexpr size_t ROWS_OFF = (size_t)STAGES * STAGE_BYTES;
-  static constexpr size_t smem = ROWS_OFF + 4 * (size_t)QPART;
-  static_assert(4 * (size_t)QPART == 2 * RowBlock<HD>::BYTES, "parts and row blocks share the region");
-};
-
-template <int HD>
-__global__ void __launch_bounds__(kKvThreads, 1)
-    attention_backward_dq_f16(int rows, int W, int T, float scale, const float* __restrict__ q,
-                              const float* __restrict__ dout, const uint8_t* __restrict__ kfmt,
-                              const float* __restrict__ lse2, const float* __restrict__ delta,
-                              float* __restrict__ dq, int* __restrict__ err) {
-  using A = F16Dq<HD>;
-  using F = F16Fmt<HD>;
-  constexpr int NS = A::STAGES, NB = A::BUFS;
-  extern __shared__ __align__(128) uint8_t sm8[];
-  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full[NB], d_full[NB][2], q_done[NB];
-  __shared__ TcShared sh;
-  __shared__ float qscale[kTcRows], oscale[kTcRows], onorm[kTcRows];
-  __shared__ float2 tscale[kMaxKeyTiles];  // (s_k, s_v) of each visited key tile
-  __shared__ float kmin_s, vnorm_s;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int nt = (rows + kTcRows - 1) / kTcRows;
-  const int q0 = tile_by_work(blockIdx.x, nt, rows, T, true) * kTcRows;
-  const int h = blockIdx.y;
-  const int nkt = (rows + kTcK - 1) / kTcK;
-  const int kbeg = ((q0 - q0 % T) / kTcK) * kTcK;
-  const int kend = min(rows, q0 + kTcRows);
-  const int n = (kend - kbeg + kTcK - 1) / kTcK;
-  const int kt0 = kbeg / kTcK;
-  uint8_t* region = sm8 + A::ROWS_OFF;
-  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
-  if (tid == 0) {
-    for (int b = 0; b < NS; ++b) {
-      tc::bar_init(&kv_full[b], 1);
-      tc::bar_init(&kv_empty[b], 1);
-    }
-    for (int b = 0; b < NB; ++b) {
-      tc::bar_init(&s_full[b], 1);
-      tc::bar_init(&d_full[b][0], kKvCompute / 2);
-      tc::bar_init(&d_full[b][1], kKvCompute / 2);
-      tc::bar_init(&q_done[b], 1);
-    }
-    tc::bar_init_fence();
-    sh.failed = 0;
-  }
-  if (warp == kKvProducer / 32) {
-    float kmin = INFINITY, vnorm = 0.f;
-    for (int j = threadIdx.x & 31; j < n; j += 32) {
-      const float4 hd4 = __ldg(reinterpret_cast<const float4*>(kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES +
-                                                               F::HEADER_OFF));
-      tscale[j] = make_float2(hd4.x, hd4.y);
-      kmin = fminf(kmin, hd4.x);
-      vnorm = fmaxf(vnorm, hd4.z);
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      kmin = fminf(kmin, __shfl_xor_sync(0xffffffffu, kmin, off));
-      vnorm = fmaxf(vnorm, __shfl_xor_sync(0xffffffffu, vnorm, off));
-    }
-    if ((threadIdx.x & 31) == 0) {
-      kmin_s = kmin;
-      vnorm_s = vnorm;
-    }
-  }
-  if (tid < kKvCompute) {
-    // Q and dO rows, coalesced into the region, then split in place into
-    // FP16 parts with per-row scales.
-    using B = RowBlock<HD>;
-    float4* bq = reinterpret_cast<float4*>(region);
-    stage_rows<HD, kKvCompute, true>(bq, q, bq + B::CHUNKS, dout, q0, rows, W, h, tid);
-    named_sync<2, kKvCompute>();
-    const int row = tid & (kTcRows - 1);
-    float nrm;
-    const float sc = rows_to_parts16<HD, kKvCompute>(region, warp, row, nrm);
-    if (warp < 4) {
-      qscale[row] = sc;
-    } else if (warp < 8) {
-      oscale[row] = sc;
-      onorm[row] = nrm;
-    }
-    tc::fence_async_smem();  // the parts are read by the tensor cores
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t t0 = sh.tmem_base;
-  // buffer b: S at tS + 128 b (later dS, interleaved), dP at tS + 128 b + 64
-  const uint32_t tG = t0, tS = t0 + 64;
-
-  if (tid < kKvCompute) {
-    const int row = tid & (kTcRows - 1), quarter = tid >> 7;
-    const int col = 16 * quarter;  // key columns [col, col + 16) of each step
-    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
-    const float sq_inv = 1.0f / qscale[row], so_inv = 1.0f / oscale[row];
-    const float rg = tc::f16_scale(2.0f * onorm[row] * vnorm_s * scale);  // |dO_row| bounds dS
-    const float scale2 = scale * 1.4426950408889634f * sq_inv;
-    const int qr = q0 + row, qs = qr - qr % T;
-    const int seq0 = q0 - q0 % T;
-    const bool one_seq = (q0 + kTcRows - 1) / T == q0 / T && q0 + kTcRows <= rows;
-    const bool in = qr < rows;
-    const float L = in ? lse2[(size_t)h * rows + qr] : 0.f;
-    const float dl = in ? delta[(size_t)h * rows + qr] : 0.f;
-    const float kmin = kmin_s;
-    for (int j = 0; j < n; ++j) {
-      const int b = j % NB;
-      const float2 ts = tscale[j];
-      const float coef = scale2 / ts.x;                // S_tmem -> log2 units
-      const float dcoef = so_inv / ts.y;               // dP_tmem -> dP
-      const float gcoef = scale * rg * (kmin / ts.x);  // dS -> stored dS
-      const uint32_t tSb = tS + 128 * b;
-      F16_WAIT_OR_FAIL(&s_full[b], (j / NB) & 1);
-      tc::fence_after_sync();
-      const int kh = kbeg + j * kTcK + col;
-      float s[16], dp[16];
-      tc::tmem_ld16_pair(tSb + col + lane, s, tSb + 64 + col + lane, dp);
-      const bool full = one_seq && kh >= seq0 && kh + 15 <= q0;
-#pragma unroll
-      for (int c = 0; c < 16; c += 2) {
-        const float2 t = fma2(make_float2(s[c], s[c + 1]), splat2(coef), splat2(-L));
-        const bool ok0 = full || (kh + c <= qr && kh + c >= qs && kh + c < rows);
-        const bool ok1 = full || (kh + c + 1 <= qr && kh + c + 1 >= qs && kh + c + 1 < rows);
-        const float2 p = make_float2(ok0 ? ex2(t.x) : 0.f, ok1 ? ex2(t.y) : 0.f);
-        const float2 g = mul2(p, fma2(make_float2(dp[c], dp[c + 1]), splat2(dcoef), splat2(-dl)));
-        s[c] = g.x;
-        s[c + 1] = g.y;
-      }
-      uint32_t hi[8], lo[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) tc::split_f16x2(s[2 * e] * gcoef, s[2 * e + 1] * gcoef, hi[e], lo[e]);
-      tc::tmem_st8u(tSb + col + lane, hi);  // over the S columns just read
-      tc::tmem_st8u(tSb + col + 8 + lane, lo);
-      tc::tmem_st_wait();
-      tc::fence_before_sync();
-      tc::bar_arrive(&d_full[b][quarter >> 1]);  // key columns [0, 32) or [32, 64)
-    }
-    // dQ of the last step (and so every MMA, the S and dP products that read
-    // the Q and dO parts included) complete before the accumulator is read
-    // and the region is reused.  Every compute thread passed s_full of step
-    // n - 1, issued after q_done of step n - 4, so the parity wait is exact.
-    if (!sh.failed && !tc::bar_wait(&q_done[(n - 1) % NB], ((n - 1) / NB) & 1)) sh.failed = 1;
-    tc::fence_after_sync();
-    // dQ through the region into coalesced row stores.
-    float4* bq = reinterpret_cast<float4*>(region);
-    const bool ok_out = __all_sync(0xffffffffu, !sh.failed);  // warp-uniform: .aligned TMEM loads
-    if (ok_out) {
-      const float out = 1.0f / (rg * kmin);
-      for (int oc = col; oc < HD; oc += 64) {  // 16-column chunks of dQ
-        float gv[16];
-        tc::tmem_ld16(tG + lane + oc, gv);
-        block_put16<HD>(bq, row, oc, gv, out);
-      }
-    }
-    named_sync<2, kKvCompute>();
-    if (ok_out) write_rows<HD, kKvCompute>(dq, bq, nullptr, q0, rows, W, h, tid);
-  } else if (tid == kKvProducer) {
-    for (int j = 0; j < n; ++j) {
-      const int st = j % NS;
-      if (j >= NS) {
-        F16_WAIT_OR_FAIL(&kv_empty[st], ((j - NS) / NS) & 1);
-      }
-      const uint8_t* tile = kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES;
-      uint8_t* stage = sm8 + st * A::STAGE_BYTES;
-      tc::bar_expect_tx(&kv_full[st], A::STAGE_BYTES);
-      tc::bulk_g2s(stage, tile, A::STAGE_BYTES, &kv_full[st]);  // K, K', V, V'
-    }
-  } else if (tid == kKvIssuer) {
-    // ---------------------------------------------------------- S / dP issuer
-    constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
-    const uint8_t* qh = region;
-    const uint8_t* oh = region + 2 * A::QPART;
-    for (int j = 0; j < n; ++j) {
-      const int st = j % NS, b = j % NB;
-      const uint8_t* stage = sm8 + st * A::STAGE_BYTES;  // K, K', V, V'
-      F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
-      if (j >= NB) {
-        // dQ of step j - 3 has read this buffer's dS, so its S and dP are free
-        F16_WAIT_OR_FAIL(&q_done[b], ((j - NB) / NB) & 1);
-      }
-      tc::fence_after_sync();
-      const uint32_t tSb = tS + 128 * b;
-      mma16_ss<HD, HD / 16>(tSb, qh, qh + A::QPART, stage + F::K_HI * F::PART_BYTES,
-                            stage + (F::K_HI + 1) * F::PART_BYTES, idS, false, 0);  // S_j = Q K_j^T
-      mma16_ss<HD, HD / 16>(tSb + 64, oh, oh + A::QPART, stage + F::V_HI * F::PART_BYTES,
-                            stage + (F::V_HI + 1) * F::PART_BYTES, idS, false, 0);  // dP_j = dO V_j^T
-      tc::commit(&s_full[b]);
-    }
-  } else if (tid == kKvIssuer2) {
-    // ---------------------------------------------------------- dQ issuer
-    constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD, true);
-    for (int j = 0; j < n; ++j) {
-      const int st = j % NS, b = j % NB;
-      const uint8_t* stage = sm8 + st * A::STAGE_BYTES;
-      F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
-      const uint32_t tSb = tS + 128 * b;
-      bool ok = true;
-      for (int k2 = 0; k2 < 2 && ok; ++k2) {
-        ok = tc::bar_wait(&d_full[b][k2], (j / NB) & 1);
-        tc::fence_after_sync();
-        // dQ += dS K over keys [32 k2, 32 k2 + 32): K steps 2 k2, 2 k2 + 1 of
-        // the K tile [64 keys][HD], MN-major
-        if (ok)
-          mma16_tmem_a_il<HD, 2>(tG, tSb, stage + F::K_HI * F::PART_BYTES, stage + (F::K_HI + 1) * F::PART_BYTES,
-                                 idG, j > 0 || k2 > 0, 2 * k2);
-      }
-      if (!ok) {
-        sh.failed = 1;
-        break;
-      }
-      tc::commit(&q_done[b]);
-      tc::commit(&kv_empty[st]);
-    }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  if (sh.failed && tid == 0) atomicExch(err, 1);
-  if (warp == 0) tc::tmem_dealloc(t0, 512);
 }
 
 // ------------------------------------------------------------------- dK/dV
@@ -1024,6 +716,8 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_queries_f16(int 
 // the key tile's query tiles.
 // TMEM: K hi | K lo | V hi | V lo (32 each) | dV | dK (64 each) |
 // S^T0 | dP^T0 | S^T1 | dP^T1 (64 each) = 512.
+constexpr int kBoxBytes = kTcRows * 32 * 4;  // a TMA box: 128 rows x 32 FP32 columns
+
 template <int HD>
 struct F16Kv {
   using G = F16Q<HD>;
@@ -1031,7 +725,7 @@ struct F16Kv {
   // Staging: the K (t = 0) and V (t = 1) rows of a key tile on the way in,
   // its dK and dV rows on the way out, as TMA boxes of 128 rows x 32 FP32
   // columns with the 128-byte swizzle (1024-byte aligned; one slack KB).
-  static constexpr int BOX_BYTES = kTcRows * 32 * 4;
+  static constexpr int BOX_BYTES = kBoxBytes;
   static constexpr size_t STAGING_OFF = (size_t)STAGES * G::QTILE_BYTES;
   static constexpr size_t smem = STAGING_OFF + 2 * (HD / 32) * (size_t)BOX_BYTES + 1024;
 };
@@ -1040,7 +734,7 @@ struct F16Kv {
 // (t, c / 8), 16-byte piece (c % 8) ^ (r % 8) of the box's 128-byte row r.
 template <int HD>
 __device__ __forceinline__ float4* staged_chunk(uint8_t* staging, int t, int r, int c) {
-  return reinterpret_cast<float4*>(staging + (t * (HD / 32) + (c >> 3)) * F16Kv<HD>::BOX_BYTES + r * 128 +
+  return reinterpret_cast<float4*>(staging + (t * (HD / 32) + (c >> 3)) * kBoxBytes + r * 128 +
                                    (((c & 7) ^ (r & 7)) << 4));
 }
 
@@ -1511,6 +1205,406 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
       wait(&drained, ni & 1);
       if (ln == 0) {
         write_out(ni - 1);
+        bulk_wait_all();  // every store done before the CTA leaves
+      }
+      __syncwarp();
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (sh.failed && tid == 0) atomicExch(err, 1);
+  if (warp == 0) tc::tmem_dealloc(t0, 512);
+}
+
+// ---------------------------------------------------------------------- dQ
+// Persistent dQ, built like the persistent dK/dV: each CTA (one per SM)
+// walks a fixed list of query tiles (128 rows of one head, the longest
+// causal work first, dealt in snake order) and, for each, its key tiles 64 at
+// a time through a ring that runs on across query tiles.  Q and dO sit in
+// TMEM split into FP16 hi/lo columns with per-row scales; dQ accumulates in
+// TMEM; S/dP are double-buffered.  Per step j (buffer b = j & 1, j counted
+// over the CTA's list): thread 544 issues S = Q K^T and dP = dO V^T; all 16
+// compute warps (thread (row, quarter) owns key columns [16 quarter, +16))
+// form dS = P (dP - delta) scale over the S columns they have read (FP16
+// hi/lo interleaved: hi in S columns [16m, 16m + 8), lo in [16m + 8,
+// 16m + 16) for keys [16m, 16m + 16)), each 32-key half handed to thread 576
+// for dQ += dS K (B = the K tile, MN-major) as soon as it is stored.
+// The loader warp (608) works one query tile ahead: the scales of its key
+// tiles, its rows' LSE and delta, and its FP32 Q and dO rows as TMA boxes;
+// after a query tile it stores the tile's dQ rows with TMA.  Between two
+// query tiles compute warps 0-7 split the staged Q and dO rows into TMEM
+// (once the last S/dP of the previous tile have been read) while warps 8-15
+// move the previous tile's dQ from TMEM into the staging area.
+// Scales: Q rows s_q(i), dO rows t(i); key tiles s_k(j), s_v(j); dS_ij is
+// stored as dS_ij r(i) d(j) with r(i) = f16_scale(2 |dO_i| max|V_row| scale),
+// a bound on |dS_i.| (|dP| and |delta| are at most |dO_i| max|V_row|), and
+// d(j) = min_j s_k / s_k(j), so dQ_i = dQ_tmem / (r(i) min_j s_k); the
+// minima and maxima run over the query tile's key tiles.
+// TMEM: Q hi | Q lo | dO hi | dO lo (32 each) | S0 | dP0 | S1 | dP1 (64 each) |
+// dQ (64) = 448 (512 allocated).
+template <int HD>
+struct F16Dq {
+  using F = F16Fmt<HD>;
+  static constexpr int STAGES = 4;
+  static constexpr int STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', V, V'
+  // Staging: Q (t = 0) and dO (t = 1) rows in, dQ rows (t = 0) out, as
+  // 128 x 32 swizzled TMA boxes (staged_chunk), 1024-byte aligned.
+  static constexpr size_t STAGING_OFF = (size_t)STAGES * STAGE_BYTES;
+  static constexpr size_t smem = STAGING_OFF + 2 * (HD / 32) * (size_t)kBoxBytes + 1024;
+};
+
+// Query tile `item` of the grid-wide work list: its first row and head.
+__device__ __forceinline__ void dq_item(int item, int rows, int T, int H, int& q0, int& h) {
+  const int nt = (rows + kTcRows - 1) / kTcRows;
+  h = item % H;
+  q0 = tile_by_work(item / H, nt, rows, T, true) * kTcRows;
+}
+// Its key tiles: from the 64-aligned start of its first row's sequence.
+__device__ __forceinline__ void dq_keys(int q0, int rows, int T, int& kbeg, int& n) {
+  kbeg = ((q0 - q0 % T) / kTcK) * kTcK;
+  const int kend = min(rows, q0 + kTcRows);
+  n = (kend - kbeg + kTcK - 1) / kTcK;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kKvThreadsP, 1)
+    attention_backward_dq_f16(int rows, int T, int H, float scale, const __grid_constant__ CUtensorMap map_q,
+                              const __grid_constant__ CUtensorMap map_do, const uint8_t* __restrict__ kfmt,
+                              const float* __restrict__ lse2, const float* __restrict__ delta,
+                              const __grid_constant__ CUtensorMap map_dq, int* __restrict__ err) {
+  using A = F16Dq<HD>;
+  using F = F16Fmt<HD>;
+  constexpr int NS = A::STAGES;
+  extern __shared__ __align__(128) uint8_t sm8[];
+  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full[2], d_full[2][2], q_done[2];
+  __shared__ uint64_t staged, qo_ready, drained;
+  __shared__ TcShared sh;
+  __shared__ float qscale[2][kTcRows], oscale[2][kTcRows], onorm[2][kTcRows];  // by item parity
+  __shared__ float lrow[2][kTcRows], drow[2][kTcRows];                        // LSE and delta, by item parity
+  __shared__ float2 tscale[2][kMaxKeyTiles];  // (s_k, s_v) of each key tile of a query tile, by item parity
+  __shared__ float2 tmin[2];                  // (min s_k, max V row norm), by item parity
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int items = ((rows + kTcRows - 1) / kTcRows) * H;
+  const int nkt = (rows + kTcK - 1) / kTcK;
+  uint8_t* staging = sm8 + A::STAGING_OFF;
+  staging += (1024u - (tc::smem_addr(staging) & 1023u)) & 1023u;  // the swizzle's period
+  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
+  if (tid == 0) {
+    for (int b = 0; b < NS; ++b) {
+      tc::bar_init(&kv_full[b], 1);
+      tc::bar_init(&kv_empty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::bar_init(&s_full[b], 1);
+      tc::bar_init(&d_full[b][0], kKvCompute / 2);
+      tc::bar_init(&d_full[b][1], kKvCompute / 2);
+      tc::bar_init(&q_done[b], 1);
+    }
+    tc::bar_init(&staged, 1);
+    tc::bar_init(&qo_ready, kKvCompute);
+    tc::bar_init(&drained, kKvCompute);
+    tc::bar_init_fence();
+    sh.failed = 0;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t t0 = sh.tmem_base;
+  const uint32_t tQh = t0, tQl = t0 + 32, tDh = t0 + 64, tDl = t0 + 96, tS = t0 + 128, tG = t0 + 384;
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    if (sh.failed) return false;
+    if (tc::bar_wait(bar, parity)) return true;
+    sh.failed = 1;
+    return false;
+  };
+
+  if (tid < kKvCompute) {
+    // ---------------------------------------------------------- compute warps
+    const int row = tid & (kTcRows - 1), quarter = tid >> 7;
+    const int col = 16 * quarter;  // key columns [col, col + 16) of each step
+    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    int it = 0;
+    float p_out = 0.f;  // output scale of the previous query tile
+    // Warps 8-15: the previous tile's dQ rows (lane quarter warp % 4,
+    // column half (warp / 4) % 2) from TMEM into staging box area t = 0.
+    const int half8 = (warp >> 2) & 1;
+    float g[HD / 2];
+    auto drain_load = [&]() {
+      const bool ok = __all_sync(0xffffffffu, wait(&q_done[(it - 1) & 1], ((it - 1) >> 1) & 1));
+      tc::fence_after_sync();
+      if (ok) {
+#pragma unroll
+        for (int c = 0; c < HD / 2; c += 16) {
+          float a16[16];
+          tc::tmem_ld16(tG + lane + half8 * (HD / 2) + c, a16);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) g[c + e] = a16[e];
+        }
+      }
+      return ok;
+    };
+    auto drain_store = [&](bool ok) {
+      if (ok) {
+#pragma unroll
+        for (int c = 0; c < HD / 2; c += 4)
+          *staged_chunk<HD>(staging, 0, row, (half8 * (HD / 2) + c) / 4) =
+              make_float4(g[c] * p_out, g[c + 1] * p_out, g[c + 2] * p_out, g[c + 3] * p_out);
+      }
+      tc::fence_async_smem();  // the loader's TMA stores read these rows
+    };
+    int kk = 0;
+    for (;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int q0, h, kbeg, n;
+      dq_item(item, rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      const int pb_ = kk & 1;
+      bool dok = false;
+      if (warp < 8) {
+        // Staged FP32 Q (warps 0-3) and dO (4-7) rows -> FP16 hi/lo TMEM
+        // columns with per-row scales, two passes over the row.
+        const bool staged_ok = __all_sync(0xffffffffu, wait(&staged, kk & 1));
+        if (staged_ok) {
+          const int t = warp >= 4 ? 1 : 0;
+          float m = 0.f, ss = 0.f;  // rows past `rows` arrive as zeros (TMA fill)
+#pragma unroll
+          for (int c = 0; c < HD / 4; ++c) {
+            const float4 t4 = *staged_chunk<HD>(staging, t, row, c);
+            m = fmaxf(fmaxf(m, fmaxf(fabsf(t4.x), fabsf(t4.y))), fmaxf(fabsf(t4.z), fabsf(t4.w)));
+            ss += t4.x * t4.x + t4.y * t4.y + t4.z * t4.z + t4.w * t4.w;
+          }
+          const float sc = tc::f16_scale(m);
+          const uint32_t thi = (t ? tDh : tQh) + lane, tlo = (t ? tDl : tQl) + lane;
+#pragma unroll
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const float4 t4 = *staged_chunk<HD>(staging, t, row, (c + 2 * e) / 4);
+              tc::split_f16x2(t4.x * sc, t4.y * sc, hi[e], lo[e]);
+              tc::split_f16x2(t4.z * sc, t4.w * sc, hi[e + 1], lo[e + 1]);
+            }
+            tc::tmem_st16u(thi + c / 2, hi);
+            tc::tmem_st16u(tlo + c / 2, lo);
+          }
+          if (t) {
+            oscale[pb_][row] = sc;
+            onorm[pb_][row] = sqrtf(ss);
+          } else {
+            qscale[pb_][row] = sc;
+          }
+          tc::tmem_st_wait();
+        }
+      } else if (kk > 0) {
+        dok = drain_load();
+      }
+      tc::fence_before_sync();
+      named_sync<2, kKvCompute>();  // staged rows read; scales visible
+      tc::bar_arrive(&qo_ready);    // the issuer may start this query tile
+      if (warp >= 8 && kk > 0) drain_store(dok);
+      tc::bar_arrive(&drained);  // staging holds the previous tile's dQ (or nothing)
+      // This tile's per-row constants.
+      const float2 mn = tmin[pb_];
+      const float sq_inv = 1.0f / qscale[pb_][row], so_inv = 1.0f / oscale[pb_][row];
+      const float rg = tc::f16_scale(2.0f * onorm[pb_][row] * mn.y * scale);  // |dO_row| bounds dS
+      const float scale2 = scale * 1.4426950408889634f * sq_inv;
+      const float kmin = mn.x;
+      const float L = lrow[pb_][row], dl = drow[pb_][row];
+      p_out = 1.0f / (rg * kmin);
+      const int qr = q0 + row, qs = qr - qr % T;
+      const int seq0 = q0 - q0 % T;
+      const bool one_seq = (q0 + kTcRows - 1) / T == q0 / T && q0 + kTcRows <= rows;
+      const float2* tsc = tscale[pb_];
+      for (int j = 0; j < n; ++j, ++it) {
+        const int b = it & 1;
+        const float2 ts = tsc[j];
+        const float coef = scale2 / ts.x;                // S_tmem -> log2 units
+        const float dcoef = so_inv / ts.y;               // dP_tmem -> dP
+        const float gcoef = scale * rg * (kmin / ts.x);  // dS -> stored dS
+        const uint32_t tSb = tS + 128 * b;
+        wait(&s_full[b], (it >> 1) & 1);
+        tc::fence_after_sync();
+        const int kh = kbeg + j * kTcK + col;
+        float sv[16], dp[16];
+        tc::tmem_ld16_pair(tSb + col + lane, sv, tSb + 64 + col + lane, dp);
+        const bool full = one_seq && kh >= seq0 && kh + 15 <= q0;
+#pragma unroll
+        for (int c = 0; c < 16; c += 2) {
+          const float2 t = fma2(make_float2(sv[c], sv[c + 1]), splat2(coef), splat2(-L));
+          const bool ok0 = full || (kh + c <= qr && kh + c >= qs && kh + c < rows);
+          const bool ok1 = full || (kh + c + 1 <= qr && kh + c + 1 >= qs && kh + c + 1 < rows);
+          const float2 p = make_float2(ok0 ? ex2(t.x) : 0.f, ok1 ? ex2(t.y) : 0.f);
+          const float2 gg = mul2(p, fma2(make_float2(dp[c], dp[c + 1]), splat2(dcoef), splat2(-dl)));
+          sv[c] = gg.x;
+          sv[c + 1] = gg.y;
+        }
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tc::split_f16x2(sv[2 * e] * gcoef, sv[2 * e + 1] * gcoef, hi[e], lo[e]);
+        tc::tmem_st8u(tSb + col + lane, hi);  // over the S columns just read
+        tc::tmem_st8u(tSb + col + 8 + lane, lo);
+        tc::tmem_st_wait();
+        tc::fence_before_sync();
+        tc::bar_arrive(&d_full[b][quarter >> 1]);  // key columns [0, 32) or [32, 64)
+      }
+    }
+    if (kk > 0) {
+      // The last query tile, once the loader has stored the one before.
+      bool dok = false;
+      if (warp >= 8) {
+        wait(&staged, kk & 1);
+        dok = drain_load();
+        drain_store(dok);
+      }
+      tc::bar_arrive(&drained);
+    }
+  } else if (tid == kKvProducer) {
+    // ---------------------------------------------------------- key tiles
+    int it = 0;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int q0, h, kbeg, n;
+      dq_item(item, rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      const int kt0 = kbeg / kTcK;
+      for (int j = 0; j < n; ++j, ++it) {
+        const int st = it % NS;
+        if (it >= NS && !wait(&kv_empty[st], ((it - NS) / NS) & 1)) continue;
+        if (sh.failed) continue;
+        tc::bar_expect_tx(&kv_full[st], A::STAGE_BYTES);
+        tc::bulk_g2s(sm8 + st * A::STAGE_BYTES, kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES, A::STAGE_BYTES,
+                     &kv_full[st]);  // K, K', V, V'
+      }
+    }
+  } else if (tid == kKvIssuer) {
+    // ---------------------------------------------------------- S / dP issuer
+    constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
+    int it = 0;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int q0, h, kbeg, n;
+      dq_item(item, rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      wait(&qo_ready, kk & 1);  // this query tile's Q and dO are in TMEM
+      for (int j = 0; j < n; ++j, ++it) {
+        const int st = it % NS, b = it & 1;
+        const uint8_t* stage = sm8 + st * A::STAGE_BYTES;
+        wait(&kv_full[st], (it / NS) & 1);
+        if (it >= 2) wait(&q_done[b], ((it - 2) >> 1) & 1);  // dQ of step it - 2 has read this buffer's dS
+        tc::fence_after_sync();
+        if (sh.failed) continue;
+        const uint32_t tSb = tS + 128 * b;
+        mma16_tmem_a<HD, HD / 16>(tSb, tQh, tQl, stage + F::K_HI * F::PART_BYTES,
+                                  stage + (F::K_HI + 1) * F::PART_BYTES, idS, false, 0);  // S = Q K^T
+        mma16_tmem_a<HD, HD / 16>(tSb + 64, tDh, tDl, stage + F::V_HI * F::PART_BYTES,
+                                  stage + (F::V_HI + 1) * F::PART_BYTES, idS, false, 0);  // dP = dO V^T
+        tc::commit(&s_full[b]);
+      }
+    }
+  } else if (tid == kKvIssuer2) {
+    // ---------------------------------------------------------- dQ issuer
+    constexpr uint32_t idG = tc::idesc_f16(kTcRows, HD, true);
+    int it = 0;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int q0, h, kbeg, n;
+      dq_item(item, rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      for (int j = 0; j < n; ++j, ++it) {
+        const int st = it % NS, b = it & 1;
+        const uint8_t* stage = sm8 + st * A::STAGE_BYTES;
+        const uint32_t tSb = tS + 128 * b;
+        wait(&kv_full[st], (it / NS) & 1);
+        for (int k2 = 0; k2 < 2; ++k2) {
+          wait(&d_full[b][k2], (it >> 1) & 1);
+          tc::fence_after_sync();
+          // dQ += dS K over keys [32 k2, 32 k2 + 32): K steps 2 k2, 2 k2 + 1
+          // of the K tile [64 keys][HD], MN-major
+          if (!sh.failed)
+            mma16_tmem_a_il<HD, 2>(tG, tSb, stage + F::K_HI * F::PART_BYTES, stage + (F::K_HI + 1) * F::PART_BYTES,
+                                   idG, j > 0 || k2 > 0, 2 * k2);
+        }
+        if (sh.failed) continue;
+        tc::commit(&q_done[b]);
+        tc::commit(&kv_empty[st]);
+      }
+    }
+  } else if (warp == kKvLoader / 32) {
+    // ---------------------------------------------------------- query-row loader
+    const int ln = tid & 31;
+    auto write_out = [&](int j, const CUtensorMap* map) {  // lane 0
+      int q0, h;
+      dq_item(snake_item(j, gridDim.x, items), rows, T, H, q0, h);
+      if (!sh.failed)
+#pragma unroll
+        for (int half = 0; half < HD / 32; ++half) tma_store_box(map, h * HD + 32 * half, q0, staging + half * kBoxBytes);
+      bulk_commit();
+    };
+    auto load = [&](int kk) {
+      int q0, h, kbeg, n;
+      dq_item(snake_item(kk, gridDim.x, items), rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      const int kt0 = kbeg / kTcK, pb = kk & 1;
+      float kmn = INFINITY, vn = 0.f;
+      for (int j = ln; j < n; j += 32) {
+        const float4 hd4 = __ldg(reinterpret_cast<const float4*>(kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES +
+                                                                 F::HEADER_OFF));
+        tscale[pb][j] = make_float2(hd4.x, hd4.y);
+        kmn = fminf(kmn, hd4.x);
+        vn = fmaxf(vn, hd4.z);
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        kmn = fminf(kmn, __shfl_xor_sync(0xffffffffu, kmn, off));
+        vn = fmaxf(vn, __shfl_xor_sync(0xffffffffu, vn, off));
+      }
+      if (ln == 0) tmin[pb] = make_float2(kmn, vn);
+      for (int r = ln; r < kTcRows; r += 32) {
+        const int qr = q0 + r;
+        lrow[pb][r] = qr < rows ? __ldg(lse2 + (size_t)h * rows + qr) : 0.f;
+        drow[pb][r] = qr < rows ? __ldg(delta + (size_t)h * rows + qr) : 0.f;
+      }
+      __syncwarp();
+      if (ln == 0) {
+        // arrive (releasing the values above) and expect the boxes' bytes
+        tc::bar_expect_tx(&staged, sh.failed ? 0u : (uint32_t)(2 * (HD / 32) * kBoxBytes));
+        if (!sh.failed) {
+#pragma unroll
+          for (int half = 0; half < HD / 32; ++half) {
+            tma_load_box(staging + half * kBoxBytes, &map_q, h * HD + 32 * half, q0, &staged);
+            tma_load_box(staging + (HD / 32 + half) * kBoxBytes, &map_do, h * HD + 32 * half, q0, &staged);
+          }
+        }
+      }
+    };
+    int ni = 0;
+    while (snake_item(ni, gridDim.x, items) >= 0) ++ni;
+    for (int kk = 0; kk < ni; ++kk) {
+      if (kk >= 1) wait(&drained, (kk - 1) & 1);  // rows kk - 1 are in TMEM; staging holds dQ of kk - 2
+      __syncwarp();
+      if (kk >= 2 && ln == 0) {
+        write_out(kk - 2, &map_dq);
+        bulk_wait_read();  // the stores have read staging before it is refilled
+      }
+      __syncwarp();
+      load(kk);
+    }
+    if (ni > 0) {
+      wait(&drained, (ni - 1) & 1);
+      if (ln == 0) {
+        if (ni >= 2) {
+          write_out(ni - 2, &map_dq);
+          bulk_wait_read();
+        }
+        tc::bar_arrive(&staged);  // staging is free for the last tile's dQ
+      }
+      wait(&drained, ni & 1);
+      if (ln == 0) {
+        write_out(ni - 1, &map_dq);
         bulk_wait_all();  // every store done before the CTA leaves
       }
       __syncwarp();

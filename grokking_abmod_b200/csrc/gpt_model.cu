@@ -286,10 +286,15 @@ struct AttentionOpsTc final : AttentionOps {
   }
   void backward_dq(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                    const float* v, const float* dout, const float* lse, const float* delta, float* dq) override {
-    dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_backward_dq_f16<HD><<<grid, kKvThreads, F16Dq<HD>::smem, s>>>(rows, W, T, 1.0f / sqrtf((float)hd), q,
-                                                                             dout, kfmt16(rows, H), lse, delta, dq,
-                                                                             err);
+    (void)k;
+    (void)v;  // read through the key tiles of the forward's format pass
+    CUtensorMap mq, mo, mdq;
+    require(encode_rows_map(&mq, q, rows, W, kTcRows) && encode_rows_map(&mo, dout, rows, W, kTcRows) &&
+                encode_rows_map(&mdq, dq, rows, W, kTcRows),
+            "attention backward: TMA maps need 16-byte aligned tensors", MB_ERR_UNSUPPORTED);
+    const int items = ((rows + kTcRows - 1) / kTcRows) * H;
+    attention_backward_dq_f16<HD><<<std::min(items, sms), kKvThreadsP, F16Dq<HD>::smem, s>>>(
+        rows, T, H, 1.0f / sqrtf((float)hd), mq, mo, kfmt16(rows, H), lse, delta, mdq, err);
   }
 };
 
