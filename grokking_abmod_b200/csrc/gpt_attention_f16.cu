@@ -43,14 +43,14 @@ namespace mb {
 constexpr int kTcRows = 128;     // CTA tile rows = TMEM lanes
 constexpr int kTcK = 64;         // key-tile rows (forward, dQ)
 constexpr int kTcQ = 64;         // query-tile rows (dK/dV)
-constexpr int kTcCompute = 256;  // compute threads: row = tid % 128, column half = tid / 128
-// Forward and dQ: 8 compute warps, a producer warp (thread 256), and two MMA
-// issuers in separate warps (threads 288 and 320).
-constexpr int kTcProducer = 256, kTcIssuer = 288;
-constexpr int kTcThreads2 = 352, kTcIssuer2 = 320;
-// dK/dV: 16 compute warps (row = tid % 128, 16-query column block =
-// tid / 128), a producer warp (thread 512) and two issuers (544, 576).
-constexpr int kKvCompute = 512, kKvProducer = 512, kKvIssuer = 544, kKvIssuer2 = 576, kKvThreads = 608;
+// Forward: 8 compute warps (row = tid % 128, column half = tid / 128), a
+// producer warp (thread 256), two MMA issuers in separate warps (threads 288
+// and 320) and a loader warp (352).
+constexpr int kTcCompute = 256, kTcProducer = 256, kTcIssuer = 288, kTcIssuer2 = 320;
+// dQ and dK/dV: 16 compute warps (row = tid % 128, 16-column block of a step
+// = tid / 128), a producer warp (thread 512), two issuers (544, 576) and a
+// loader warp (608).
+constexpr int kKvCompute = 512, kKvProducer = 512, kKvIssuer = 544, kKvIssuer2 = 576;
 
 constexpr int kFmtThreads = 256;  // threads of the format kernels
 
@@ -99,8 +99,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Named barrier over the 256 compute threads.
-__device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 struct TcShared {
   uint32_t tmem_base;
@@ -201,113 +199,10 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_keys_f16(int row
   if (threadIdx.x == 0) *reinterpret_cast<float4*>(tile + F::HEADER_OFF) = make_float4(sk, sv, nv, mv);
 }
 
-// A CTA's 128 rows of one head in shared memory as float4 chunks, chunk c of
-// row r at r C4 + (c ^ (r % C4)): a thread walking its own row and a warp
-// walking consecutive chunks both hit distinct banks.  The row blocks move
-// between global memory and shared memory with coalesced float4 accesses
-// (consecutive threads, consecutive chunks of a row) and between shared
-// memory and TMEM one row per thread.
-template <int HD>
-struct RowBlock {
-  static constexpr int C4 = HD / 4;
-  static constexpr int CHUNKS = kTcRows * C4;
-  static constexpr size_t BYTES = (size_t)CHUNKS * sizeof(float4);
-  __device__ static int at(int r, int c) { return r * C4 + (c ^ (r & (C4 - 1))); }
-};
-
+// Named barrier ID over NT threads.
 template <int ID, int NT>
 __device__ __forceinline__ void named_sync() {
   asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(NT) : "memory");
-}
-
-// Rows [r0, r0 + 128) of head h of one or two row-major [rows][W] tensors
-// into row blocks by NT threads (this one is t); rows past `rows` read as 0.
-// Every load of the thread is issued before its first store.
-template <int HD, int NT, bool TWO>
-__device__ __forceinline__ void stage_rows(float4* da, const float* __restrict__ ga, float4* db,
-                                           const float* __restrict__ gb, int r0, int rows, int W, int h, int t) {
-  using B = RowBlock<HD>;
-  constexpr int PER = B::CHUNKS / NT;
-  static_assert(PER * NT == B::CHUNKS, "row block must split evenly over the threads");
-  float4 va[PER], vb[PER];
-#pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    const int f = t + j * NT, r = f / B::C4, c = f % B::C4, row = r0 + r;
-    const size_t off = (size_t)row * W + h * HD + 4 * c;
-    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-    va[j] = row < rows ? __ldg(reinterpret_cast<const float4*>(ga + off)) : z;
-    if (TWO) vb[j] = row < rows ? __ldg(reinterpret_cast<const float4*>(gb + off)) : z;
-  }
-#pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    const int f = t + j * NT, r = f / B::C4, c = f % B::C4;
-    da[B::at(r, c)] = va[j];
-    if (TWO) db[B::at(r, c)] = vb[j];
-  }
-}
-
-// Row r of a row block split into FP16 hi/lo TMEM columns (HD / 2 packed
-// columns each) with a per-row scale, which it returns; `norm` receives the
-// row's Euclidean norm.
-template <int HD>
-__device__ __forceinline__ float block_row_to_tmem16(const float4* blk, int r, uint32_t thi, uint32_t tlo,
-                                                     float& norm) {
-  using B = RowBlock<HD>;
-  float x[HD];
-#pragma unroll
-  for (int c = 0; c < B::C4; ++c) {
-    const float4 v = blk[B::at(r, c)];
-    x[4 * c] = v.x, x[4 * c + 1] = v.y, x[4 * c + 2] = v.z, x[4 * c + 3] = v.w;
-  }
-  float m = 0.f, ss = 0.f;
-#pragma unroll
-  for (int c = 0; c < HD; ++c) {
-    m = fmaxf(m, fabsf(x[c]));
-    ss += x[c] * x[c];
-  }
-  norm = sqrtf(ss);
-  const float s = tc::f16_scale(m);
-#pragma unroll
-  for (int c = 0; c < HD; c += 32) {
-    uint32_t hi[16], lo[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) tc::split_f16x2(x[c + 2 * e] * s, x[c + 2 * e + 1] * s, hi[e], lo[e]);
-    tc::tmem_st16u(thi + c / 2, hi);
-    tc::tmem_st16u(tlo + c / 2, lo);
-  }
-  return s;
-}
-
-// 16 values of row r, columns [c0, c0 + 16), times `mul` into a row block.
-template <int HD>
-__device__ __forceinline__ void block_put16(float4* blk, int r, int c0, const float (&v)[16], float mul) {
-  using B = RowBlock<HD>;
-#pragma unroll
-  for (int e = 0; e < 4; ++e)
-    blk[B::at(r, c0 / 4 + e)] = make_float4(v[4 * e] * mul, v[4 * e + 1] * mul, v[4 * e + 2] * mul, v[4 * e + 3] * mul);
-}
-
-// A row block out to rows [r0, r0 + 128) of head h of a row-major [rows][W]
-// tensor (plus `add`, same layout, when given) by NT threads.
-template <int HD, int NT>
-__device__ __forceinline__ void write_rows(float* __restrict__ g, const float4* blk, const float* __restrict__ add,
-                                           int r0, int rows, int W, int h, int t) {
-  using B = RowBlock<HD>;
-  constexpr int PER = B::CHUNKS / NT;
-  static_assert(PER * NT == B::CHUNKS, "row block must split evenly over the threads");
-#pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    const int f = t + j * NT, r = f / B::C4, c = f % B::C4, row = r0 + r;
-    if (row < rows) {
-      const size_t off = (size_t)row * W + h * HD + 4 * c;
-      float4 v = blk[B::at(r, c)];
-      if (add != nullptr) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(add + off));
-        v = make_float4(v.x + a.x, v.y + a.y, v.z + a.z, v.w + a.w);
-      }
-      *reinterpret_cast<float4*>(g + off) = v;
-    }
-  }
 }
 
 // D (+)= A . B^T with A = FP16 hi/lo TMEM columns and B a K-major FP16 hi/lo
@@ -341,260 +236,6 @@ __device__ __forceinline__ void tc_st_split16(uint32_t thi, uint32_t tlo, const 
     tc::tmem_st16u(thi + c / 2, hi);
     tc::tmem_st16u(tlo + c / 2, lo);
   }
-}
-
-template <int HD>
-struct F16Att {
-  using F = F16Fmt<HD>;
-  static constexpr int FWD_STAGES = 4;
-  static constexpr int FWD_STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', V, V'
-  static constexpr size_t ROWS_OFF = (size_t)FWD_STAGES * FWD_STAGE_BYTES;  // Q row block, later O
-  static constexpr size_t smem_forward = ROWS_OFF + RowBlock<HD>::BYTES;
-};
-
-// ------------------------------------------------------------------ forward
-// Roles as attention_forward_tc: threads 0-255 compute (row = tid % 128 =
-// TMEM lane, half = tid / 128 takes keys [32 half, 32 half + 32) of each
-// 64-key step with its own online-softmax stream and O accumulator), thread
-// 256 streams key tiles, thread 288 issues S = Q K^T and thread 320 P.V.
-// S and P are double-buffered (buffer j & 1 for step j): the softmax of step
-// j + 1 runs while P.V of step j executes, and writing P waits only for P.V
-// of step j - 1 to have read that buffer (o_done[b], one commit per step).
-// A lazy O rescale at step j waits for P.V of step j - 1, so O is stable.
-// TMEM columns: Q hi | Q lo (32 each) | S0 | S1 (64 each) | P0 hi | P0 lo |
-// P1 hi | P1 lo (32 each) | O0 | O1 (64 each) = 448.
-template <int HD>
-__global__ void __launch_bounds__(kTcThreads2, 1)
-    attention_forward_f16(int rows, int W, int T, float scale, const float* __restrict__ q,
-                          const uint8_t* __restrict__ kfmt, float* __restrict__ o, float* __restrict__ lse2,
-                          int* __restrict__ err) {
-  using A = F16Att<HD>;
-  using F = F16Fmt<HD>;
-  constexpr int NS = A::FWD_STAGES;
-  extern __shared__ __align__(128) uint8_t sm8[];
-  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full[2], s_empty[2], p_full[2], o_done[2];
-  __shared__ TcShared sh;
-  __shared__ float xm[2][kTcRows], xl[2][kTcRows], qscale[kTcRows];
-  __shared__ float2 tscale[kMaxKeyTiles];  // (s_k, s_v) of each visited key tile
-  __shared__ float vmin;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int nt = (rows + kTcRows - 1) / kTcRows;
-  const int q0 = tile_by_work(blockIdx.x, nt, rows, T, true) * kTcRows;
-  const int h = blockIdx.y;
-  const int nkt = (rows + kTcK - 1) / kTcK;
-  const int kbeg = ((q0 - q0 % T) / kTcK) * kTcK;  // 64-aligned start of the first sequence
-  const int kend = min(rows, q0 + kTcRows);
-  const int n = (kend - kbeg + kTcK - 1) / kTcK;
-  const int kt0 = kbeg / kTcK;
-  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
-  if (tid == 0) {
-    for (int b = 0; b < NS; ++b) {
-      tc::bar_init(&kv_full[b], 1);
-      tc::bar_init(&kv_empty[b], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      tc::bar_init(&s_full[b], 1);
-      tc::bar_init(&s_empty[b], kTcCompute);
-      tc::bar_init(&p_full[b], kTcCompute);
-      tc::bar_init(&o_done[b], 1);
-    }
-    tc::bar_init_fence();
-    sh.failed = 0;
-  }
-  if (warp == 8) {
-    // the scales of the CTA's key tiles, and the smallest V scale
-    float mn = INFINITY;
-    for (int j = threadIdx.x & 31; j < n; j += 32) {
-      const float4 hd4 = __ldg(reinterpret_cast<const float4*>(kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES +
-                                                               F::HEADER_OFF));
-      tscale[j] = make_float2(hd4.x, hd4.y);
-      mn = fminf(mn, hd4.y);
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
-    if ((threadIdx.x & 31) == 0) vmin = mn;
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t t0 = sh.tmem_base;
-  // P buffer b: hi at tP + 64 b, lo at tP + 64 b + 32
-  const uint32_t tQh = t0, tQl = t0 + 32, tS = t0 + 64, tP = t0 + 192, tO = t0 + 320;
-  if (tid < kTcCompute) {
-    // Q rows through shared memory into TMEM with per-row scales.
-    float4* bq = reinterpret_cast<float4*>(sm8 + A::ROWS_OFF);
-    stage_rows<HD, kTcCompute, false>(bq, q, nullptr, nullptr, q0, rows, W, h, tid);
-    named_sync<2, kTcCompute>();
-    if (warp < 4) {
-      const uint32_t lane = (uint32_t)(warp * 32) << 16;
-      float nrm;
-      qscale[tid] = block_row_to_tmem16<HD>(bq, tid, tQh + lane, tQl + lane, nrm);
-      tc::tmem_st_wait();
-    }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const float pv_c = 128.0f * vmin;  // C: every step's P.V carries this factor
-
-  if (tid < kTcCompute) {
-    // ---------------------------------------------------------- softmax
-    const int row = tid & (kTcRows - 1), half = tid >> 7;
-    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t myO = tO + 64 * half + lane;
-    const float scale2 = scale * 1.4426950408889634f / qscale[row];
-    const int qr = q0 + row, qs = qr - qr % T;
-    const int seq0 = q0 - q0 % T;
-    const bool one_seq = (q0 + kTcRows - 1) / T == q0 / T && q0 + kTcRows <= rows;
-    float m = -INFINITY, l = 0.f;
-    bool done = false;
-    for (int j = 0; j < n; ++j) {
-      const int b = j & 1;
-      const float2 ts = tscale[j];
-      const float coef = scale2 / ts.x;  // scaled score -> log2 units
-      F16_WAIT_OR_FAIL(&s_full[b], (j >> 1) & 1);
-      tc::fence_after_sync();
-      float s[32];
-      tc::tmem_ld32(tS + 64 * b + 32 * half + lane, s);
-      tc::fence_before_sync();
-      tc::bar_arrive(&s_empty[b]);
-      const int kt = kbeg + j * kTcK;
-      const bool full = one_seq && kt >= seq0 && kt + kTcK - 1 <= q0;
-      const int kh = kt + 32 * half;
-      if (!full) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int kr = kh + c;
-          s[c] = (kr <= qr && kr >= qs && kr < rows) ? s[c] : -INFINITY;
-        }
-      }
-      float m4[4] = {s[0], s[1], s[2], s[3]};
-#pragma unroll
-      for (int c = 4; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
-      float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      mx *= coef;
-      const bool need = mx > m + 8.0f;  // false while every key so far is masked
-      float alpha = 1.0f;
-      if (need) {
-        alpha = ex2(m - mx);  // 0 when m = -inf
-        m = mx;
-      }
-      const float nm = m == -INFINITY ? 0.f : -m;
-      float2 rs2 = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int c = 0; c < 32; c += 2) {
-        const float2 t = fma2(make_float2(s[c], s[c + 1]), splat2(coef), splat2(nm));
-        s[c] = ex2(t.x);  // ex2(-inf) = 0 for masked keys
-        s[c + 1] = ex2(t.y);
-        rs2 = add2(rs2, make_float2(s[c], s[c + 1]));
-      }
-      l = l * alpha + (rs2.x + rs2.y);
-      if (j >= 2) {
-        // P.V of step j-2 has read this P buffer.
-        F16_WAIT_OR_FAIL(&o_done[b], ((j - 2) >> 1) & 1);
-        tc::fence_after_sync();
-      }
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // P.V of step j-1 complete: O is stable for the rescale.
-        F16_WAIT_OR_FAIL(&o_done[b ^ 1], ((j - 1) >> 1) & 1);
-        tc::fence_after_sync();
-        {
-#pragma unroll
-          for (int c = 0; c < HD; c += 16) {
-            float ov[16];
-            tc::tmem_ld16(myO + c, ov);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) ov[e] *= alpha;
-            tc::tmem_st16(myO + c, ov);
-          }
-        }
-      }
-      const uint32_t tPb = tP + 64 * b;
-      tc_st_split16<32>(tPb + 16 * half + lane, tPb + 32 + 16 * half + lane, s, pv_c / ts.y);
-      tc::tmem_st_wait();
-      tc::fence_before_sync();
-      tc::bar_arrive(&p_full[b]);
-      if (j + 1 == n) done = true;
-    }
-    if (done && !tc::bar_wait(&o_done[(n - 1) & 1], ((n - 1) >> 1) & 1)) sh.failed = 1;
-    tc::fence_after_sync();
-    xm[half][row] = m;
-    xl[half][row] = l;
-    compute_sync();
-    const bool okf = __all_sync(0xffffffffu, done && !sh.failed);  // warp-uniform: .aligned TMEM loads
-    if (okf) {
-      // Merge the two streams: O = (O0 2^(m0-M) + O1 2^(m1-M)) / (C L).
-      const float m0 = xm[0][row], m1 = xm[1][row];
-      const float mt = fmaxf(m0, m1);
-      const float f0 = m0 == -INFINITY ? 0.f : ex2(m0 - mt), f1 = m1 == -INFINITY ? 0.f : ex2(m1 - mt);
-      const float L = xl[0][row] * f0 + xl[1][row] * f1;
-      const float inv = L > 0.f ? 1.0f / (L * pv_c) : 0.f;
-      const uint32_t o0 = tO + lane, o1 = tO + 64 + lane;
-      float4* bo = reinterpret_cast<float4*>(sm8 + A::ROWS_OFF);  // O through the Q row block
-#pragma unroll
-      for (int c = 0; c < HD / 2; c += 16) {
-        const int col = (HD / 2) * half + c;
-        float a[16], bb[16];
-        tc::tmem_ld16_pair(o0 + col, a, o1 + col, bb);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) a[e] = a[e] * f0 + bb[e] * f1;
-        block_put16<HD>(bo, row, col, a, inv);
-      }
-      if (qr < rows && half == 0) lse2[(size_t)h * rows + qr] = mt + log2f(L);
-    }
-    named_sync<2, kTcCompute>();
-    if (okf)
-      write_rows<HD, kTcCompute>(o, reinterpret_cast<const float4*>(sm8 + A::ROWS_OFF), nullptr, q0, rows, W, h, tid);
-  } else if (tid == kTcProducer) {
-    // ---------------------------------------------------------- producer
-    for (int j = 0; j < n; ++j) {
-      const int st = j % NS;
-      if (j >= NS) {
-        F16_WAIT_OR_FAIL(&kv_empty[st], ((j - NS) / NS) & 1);
-      }
-      tc::bar_expect_tx(&kv_full[st], A::FWD_STAGE_BYTES);
-      tc::bulk_g2s(sm8 + st * A::FWD_STAGE_BYTES, kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES,
-                   A::FWD_STAGE_BYTES, &kv_full[st]);
-    }
-  } else if (tid == kTcIssuer) {
-    // ---------------------------------------------------------- S issuer
-    constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
-    for (int j = 0; j < n; ++j) {
-      const int st = j % NS, b = j & 1;
-      const uint8_t* stage = sm8 + st * A::FWD_STAGE_BYTES;
-      F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
-      if (j >= 2) {
-        F16_WAIT_OR_FAIL(&s_empty[b], ((j - 2) >> 1) & 1);
-      }
-      tc::fence_after_sync();
-      // S_j = Q K_j^T over HD / 16 steps
-      mma16_tmem_a<HD, HD / 16>(tS + 64 * b, tQh, tQl, stage, stage + F::PART_BYTES, idS, false, 0);
-      tc::commit(&s_full[b]);
-    }
-  } else if (tid == kTcIssuer2) {
-    // ---------------------------------------------------------- P.V issuer
-    constexpr uint32_t idO = tc::idesc_f16(kTcRows, HD, true);
-    for (int j = 0; j < n; ++j) {
-      const int st = j % NS, b = j & 1;
-      const uint8_t* stage = sm8 + st * A::FWD_STAGE_BYTES;
-      F16_WAIT_OR_FAIL(&p_full[b], (j >> 1) & 1);
-      F16_WAIT_OR_FAIL(&kv_full[st], (j / NS) & 1);
-      tc::fence_after_sync();
-      // O_half += P[:, half keys] V[half keys]  (B = the V tile [64 keys][HD],
-      // MN-major; K steps of 16 keys: half 0 steps 0-1, half 1 steps 2-3)
-      const uint8_t* vh = stage + F::V_HI * F::PART_BYTES;
-      const uint8_t* vl = stage + (F::V_HI + 1) * F::PART_BYTES;
-      const uint32_t tPb = tP + 64 * b;
-      mma16_tmem_a<HD, 2, true>(tO, tPb, tPb + 32, vh, vl, idO, j > 0, 0);
-      mma16_tmem_a<HD, 2, true>(tO + 64, tPb, tPb + 32, vh, vl, idO, j > 0, 2);
-      tc::commit(&o_done[b]);
-      tc::commit(&kv_empty[st]);
-    }
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  if (sh.failed && tid == 0) atomicExch(err, 1);
-  if (warp == 0) tc::tmem_dealloc(t0, 512);
 }
 
 // D (+)= A . B^T over K steps [s0, s0 + NSTEP) of 16 elements with A's FP16
@@ -1605,6 +1246,406 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
       wait(&drained, ni & 1);
       if (ln == 0) {
         write_out(ni - 1, &map_dq);
+        bulk_wait_all();  // every store done before the CTA leaves
+      }
+      __syncwarp();
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (sh.failed && tid == 0) atomicExch(err, 1);
+  if (warp == 0) tc::tmem_dealloc(t0, 512);
+}
+
+// ------------------------------------------------------------------ forward
+// Persistent forward, built like the persistent backward kernels: each CTA
+// (one per SM) walks a fixed list of query tiles (128 rows of one head, the
+// longest causal work first, dealt in snake order) and, for each, its key
+// tiles 64 at a time through a ring that runs on across query tiles.
+// Compute threads 0-255: row = tid % 128 = TMEM lane, half = tid / 128 takes
+// keys [32 half, 32 half + 32) of each 64-key step with its own
+// online-softmax stream and O accumulator; thread 256 streams key tiles,
+// thread 288 issues S = Q K^T and thread 320 P.V; the loader warp (352)
+// works one query tile ahead (the scales of its key tiles, its FP32 Q rows as
+// TMA boxes) and stores each finished tile's O rows with TMA.  S and P are
+// double-buffered (buffer j & 1 for step j, counted over the CTA's list):
+// the softmax of step j + 1 runs while P.V of step j executes, and writing P
+// waits only for P.V of step j - 2 to have read that buffer.  A lazy O
+// rescale at step j waits for P.V of step j - 1, so O is stable.  Between two
+// query tiles warps 0-3 split the staged Q rows into TMEM (once the last S of
+// the previous tile has been read), then all compute warps merge the
+// previous tile's two streams into staging.
+// TMEM columns: Q hi | Q lo (32 each) | S0 | S1 (64 each) | P0 hi | P0 lo |
+// P1 hi | P1 lo (32 each) | O0 | O1 (64 each) = 448.
+template <int HD>
+struct F16Att {
+  using F = F16Fmt<HD>;
+  static constexpr int FWD_STAGES = 4;
+  static constexpr int FWD_STAGE_BYTES = 4 * F::PART_BYTES;  // K, K', V, V'
+  // Staging: Q rows in, O rows out (staged_chunk box area t = 0), 1024-byte aligned.
+  static constexpr size_t STAGING_OFF = (size_t)FWD_STAGES * FWD_STAGE_BYTES;
+  static constexpr size_t smem_forward = STAGING_OFF + (HD / 32) * (size_t)kBoxBytes + 1024;
+};
+constexpr int kFwdLoader = 352, kFwdThreads = 384;
+
+template <int HD>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    attention_forward_f16(int rows, int T, int H, float scale, const __grid_constant__ CUtensorMap map_q,
+                          const uint8_t* __restrict__ kfmt, const __grid_constant__ CUtensorMap map_o,
+                          float* __restrict__ lse2, int* __restrict__ err) {
+  using A = F16Att<HD>;
+  using F = F16Fmt<HD>;
+  constexpr int NS = A::FWD_STAGES;
+  extern __shared__ __align__(128) uint8_t sm8[];
+  __shared__ uint64_t kv_full[NS], kv_empty[NS], s_full[2], s_empty[2], p_full[2], o_done[2];
+  __shared__ uint64_t staged, q_ready, drained;
+  __shared__ TcShared sh;
+  __shared__ float xm[2][kTcRows], xl[2][kTcRows], qscale[2][kTcRows];
+  __shared__ float2 tscale[2][kMaxKeyTiles];  // (s_k, s_v) of each key tile of a query tile, by item parity
+  __shared__ float vmin[2];                   // the smallest V scale over them, by item parity
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int items = ((rows + kTcRows - 1) / kTcRows) * H;
+  const int nkt = (rows + kTcK - 1) / kTcK;
+  uint8_t* staging = sm8 + A::STAGING_OFF;
+  staging += (1024u - (tc::smem_addr(staging) & 1023u)) & 1023u;  // the swizzle's period
+  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, 512);
+  if (tid == 0) {
+    for (int b = 0; b < NS; ++b) {
+      tc::bar_init(&kv_full[b], 1);
+      tc::bar_init(&kv_empty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::bar_init(&s_full[b], 1);
+      tc::bar_init(&s_empty[b], kTcCompute);
+      tc::bar_init(&p_full[b], kTcCompute);
+      tc::bar_init(&o_done[b], 1);
+    }
+    tc::bar_init(&staged, 1);
+    tc::bar_init(&q_ready, kTcCompute);
+    tc::bar_init(&drained, kTcCompute);
+    tc::bar_init_fence();
+    sh.failed = 0;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t t0 = sh.tmem_base;
+  // P buffer b: hi at tP + 64 b, lo at tP + 64 b + 32
+  const uint32_t tQh = t0, tQl = t0 + 32, tS = t0 + 64, tP = t0 + 192, tO = t0 + 320;
+  auto wait = [&](uint64_t* bar, uint32_t parity) {
+    if (sh.failed) return false;
+    if (tc::bar_wait(bar, parity)) return true;
+    sh.failed = 1;
+    return false;
+  };
+
+  if (tid < kTcCompute) {
+    // ---------------------------------------------------------- softmax
+    const int row = tid & (kTcRows - 1), half = tid >> 7;
+    const uint32_t lane = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t myO = tO + 64 * half + lane;
+    int it = 0;
+    float m = -INFINITY, l = 0.f;     // this thread's stream of the current tile
+    float p_pvc = 0.f;                // C of the previous tile
+    int p_q0 = 0, p_h = 0;            // the previous tile
+    // The previous tile's two streams merged into staging (rows of box area
+    // t = 0): O = (O0 2^(m0-M) + O1 2^(m1-M)) / (C L), and its LSE.  Needs
+    // xm / xl of both halves (a named barrier before).  Warp-uniform: the
+    // TMEM loads are .aligned.
+    auto merge = [&](bool ok) {
+      if (__all_sync(0xffffffffu, ok)) {
+        const float m0 = xm[0][row], m1 = xm[1][row];
+        const float mt = fmaxf(m0, m1);
+        const float f0 = m0 == -INFINITY ? 0.f : ex2(m0 - mt), f1 = m1 == -INFINITY ? 0.f : ex2(m1 - mt);
+        const float L = xl[0][row] * f0 + xl[1][row] * f1;
+        const float inv = L > 0.f ? 1.0f / (L * p_pvc) : 0.f;
+#pragma unroll
+        for (int c = 0; c < HD / 2; c += 16) {
+          const int col = (HD / 2) * half + c;
+          float a[16], bb[16];
+          tc::tmem_ld16_pair(tO + lane + col, a, tO + 64 + lane + col, bb);
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *staged_chunk<HD>(staging, 0, row, (col + e) / 4) =
+                make_float4((a[e] * f0 + bb[e] * f1) * inv, (a[e + 1] * f0 + bb[e + 1] * f1) * inv,
+                            (a[e + 2] * f0 + bb[e + 2] * f1) * inv, (a[e + 3] * f0 + bb[e + 3] * f1) * inv);
+        }
+        const int qr = p_q0 + row;
+        if (qr < rows && half == 0) lse2[(size_t)p_h * rows + qr] = mt + log2f(L);
+      }
+      tc::fence_async_smem();  // the loader's TMA stores read these rows
+    };
+    // The previous tile's last P.V done, its streams' (m, l) published.
+    // Every thread passed its wait for P.V of step it - 3, so the parity
+    // wait is exact.
+    auto finish = [&]() {
+      const bool ok = wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1);
+      tc::fence_after_sync();
+      xm[half][row] = m;
+      xl[half][row] = l;
+      return ok;
+    };
+    int kk = 0;
+    for (;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int q0, h, kbeg, n;
+      dq_item(item, rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      const int pb_ = kk & 1;
+      const bool fin = kk > 0 ? finish() : true;
+      if (warp < 4) {
+        // Staged FP32 Q rows -> FP16 hi/lo TMEM columns with per-row scales
+        // (the Q columns are free: the previous tile's last S has been read).
+        const bool staged_ok = __all_sync(0xffffffffu, wait(&staged, kk & 1));
+        if (staged_ok) {
+          float mq = 0.f;  // rows past `rows` arrive as zeros (TMA fill)
+#pragma unroll
+          for (int c = 0; c < HD / 4; ++c) {
+            const float4 t4 = *staged_chunk<HD>(staging, 0, row, c);
+            mq = fmaxf(fmaxf(mq, fmaxf(fabsf(t4.x), fabsf(t4.y))), fmaxf(fabsf(t4.z), fabsf(t4.w)));
+          }
+          const float sc = tc::f16_scale(mq);
+#pragma unroll
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const float4 t4 = *staged_chunk<HD>(staging, 0, row, (c + 2 * e) / 4);
+              tc::split_f16x2(t4.x * sc, t4.y * sc, hi[e], lo[e]);
+              tc::split_f16x2(t4.z * sc, t4.w * sc, hi[e + 1], lo[e + 1]);
+            }
+            tc::tmem_st16u(tQh + lane + c / 2, hi);
+            tc::tmem_st16u(tQl + lane + c / 2, lo);
+          }
+          qscale[pb_][row] = sc;
+          tc::tmem_st_wait();
+        }
+      }
+      tc::fence_before_sync();
+      named_sync<2, kTcCompute>();  // staged rows read; scales and (m, l) visible
+      tc::bar_arrive(&q_ready);     // the issuer may start this query tile
+      if (kk > 0) merge(fin);
+      tc::bar_arrive(&drained);  // staging holds the previous tile's O (or nothing)
+      // This tile's constants.
+      const float pv_c = 128.0f * vmin[pb_];  // C: every step's P.V carries this factor
+      p_pvc = pv_c;
+      p_q0 = q0;
+      p_h = h;
+      const float scale2 = scale * 1.4426950408889634f / qscale[pb_][row];
+      const int qr = q0 + row, qs = qr - qr % T;
+      const int seq0 = q0 - q0 % T;
+      const bool one_seq = (q0 + kTcRows - 1) / T == q0 / T && q0 + kTcRows <= rows;
+      const float2* tsc = tscale[pb_];
+      m = -INFINITY;
+      l = 0.f;
+      for (int j = 0; j < n; ++j, ++it) {
+        const int b = it & 1;
+        const float2 ts = tsc[j];
+        const float coef = scale2 / ts.x;  // scaled score -> log2 units
+        wait(&s_full[b], (it >> 1) & 1);
+        tc::fence_after_sync();
+        float sv[32];
+        tc::tmem_ld32(tS + 64 * b + 32 * half + lane, sv);
+        tc::fence_before_sync();
+        tc::bar_arrive(&s_empty[b]);
+        const int kt = kbeg + j * kTcK;
+        const bool full = one_seq && kt >= seq0 && kt + kTcK - 1 <= q0;
+        const int kh = kt + 32 * half;
+        if (!full) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int kr = kh + c;
+            sv[c] = (kr <= qr && kr >= qs && kr < rows) ? sv[c] : -INFINITY;
+          }
+        }
+        float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+        for (int c = 4; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], sv[c]);
+        float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        mx *= coef;
+        const bool need = mx > m + 8.0f;  // false while every key so far is masked
+        float alpha = 1.0f;
+        if (need) {
+          alpha = ex2(m - mx);  // 0 when m = -inf
+          m = mx;
+        }
+        const float nm = m == -INFINITY ? 0.f : -m;
+        float2 rs2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const float2 t = fma2(make_float2(sv[c], sv[c + 1]), splat2(coef), splat2(nm));
+          sv[c] = ex2(t.x);  // ex2(-inf) = 0 for masked keys
+          sv[c + 1] = ex2(t.y);
+          rs2 = add2(rs2, make_float2(sv[c], sv[c + 1]));
+        }
+        l = l * alpha + (rs2.x + rs2.y);
+        if (it >= 2) {
+          // P.V of step it - 2 has read this P buffer.
+          wait(&o_done[b], ((it - 2) >> 1) & 1);
+          tc::fence_after_sync();
+        }
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // P.V of step it - 1 complete: O is stable for the rescale.
+          const bool ok = __all_sync(0xffffffffu, wait(&o_done[b ^ 1], ((it - 1) >> 1) & 1));
+          tc::fence_after_sync();
+          if (ok) {
+#pragma unroll
+            for (int c = 0; c < HD; c += 16) {
+              float ov[16];
+              tc::tmem_ld16(myO + c, ov);
+#pragma unroll
+              for (int e = 0; e < 16; ++e) ov[e] *= alpha;
+              tc::tmem_st16(myO + c, ov);
+            }
+          }
+        }
+        const uint32_t tPb = tP + 64 * b;
+        tc_st_split16<32>(tPb + 16 * half + lane, tPb + 32 + 16 * half + lane, sv, pv_c / ts.y);
+        tc::tmem_st_wait();
+        tc::fence_before_sync();
+        tc::bar_arrive(&p_full[b]);
+      }
+    }
+    if (kk > 0) {
+      // The last query tile, once the loader has stored the one before.
+      const bool fin = finish();
+      wait(&staged, kk & 1);
+      named_sync<2, kTcCompute>();  // (m, l) of both halves visible
+      merge(fin);
+      tc::bar_arrive(&drained);
+    }
+  } else if (tid == kTcProducer) {
+    // ---------------------------------------------------------- producer
+    int it = 0;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int q0, h, kbeg, n;
+      dq_item(item, rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      const int kt0 = kbeg / kTcK;
+      for (int j = 0; j < n; ++j, ++it) {
+        const int st = it % NS;
+        if (it >= NS && !wait(&kv_empty[st], ((it - NS) / NS) & 1)) continue;
+        if (sh.failed) continue;
+        tc::bar_expect_tx(&kv_full[st], A::FWD_STAGE_BYTES);
+        tc::bulk_g2s(sm8 + st * A::FWD_STAGE_BYTES, kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES,
+                     A::FWD_STAGE_BYTES, &kv_full[st]);
+      }
+    }
+  } else if (tid == kTcIssuer) {
+    // ---------------------------------------------------------- S issuer
+    constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcK);
+    int it = 0;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int q0, h, kbeg, n;
+      dq_item(item, rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      wait(&q_ready, kk & 1);  // this query tile's Q is in TMEM
+      for (int j = 0; j < n; ++j, ++it) {
+        const int st = it % NS, b = it & 1;
+        const uint8_t* stage = sm8 + st * A::FWD_STAGE_BYTES;
+        wait(&kv_full[st], (it / NS) & 1);
+        if (it >= 2) wait(&s_empty[b], ((it - 2) >> 1) & 1);
+        tc::fence_after_sync();
+        if (sh.failed) continue;
+        // S_j = Q K_j^T over HD / 16 steps
+        mma16_tmem_a<HD, HD / 16>(tS + 64 * b, tQh, tQl, stage, stage + F::PART_BYTES, idS, false, 0);
+        tc::commit(&s_full[b]);
+      }
+    }
+  } else if (tid == kTcIssuer2) {
+    // ---------------------------------------------------------- P.V issuer
+    constexpr uint32_t idO = tc::idesc_f16(kTcRows, HD, true);
+    int it = 0;
+    for (int kk = 0;; ++kk) {
+      const int item = snake_item(kk, gridDim.x, items);
+      if (item < 0) break;
+      int q0, h, kbeg, n;
+      dq_item(item, rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      for (int j = 0; j < n; ++j, ++it) {
+        const int st = it % NS, b = it & 1;
+        const uint8_t* stage = sm8 + st * A::FWD_STAGE_BYTES;
+        wait(&p_full[b], (it >> 1) & 1);
+        wait(&kv_full[st], (it / NS) & 1);
+        tc::fence_after_sync();
+        if (sh.failed) continue;
+        // O_half += P[:, half keys] V[half keys]  (B = the V tile [64 keys][HD],
+        // MN-major; K steps of 16 keys: half 0 steps 0-1, half 1 steps 2-3)
+        const uint8_t* vh = stage + F::V_HI * F::PART_BYTES;
+        const uint8_t* vl = stage + (F::V_HI + 1) * F::PART_BYTES;
+        const uint32_t tPb = tP + 64 * b;
+        mma16_tmem_a<HD, 2, true>(tO, tPb, tPb + 32, vh, vl, idO, j > 0, 0);
+        mma16_tmem_a<HD, 2, true>(tO + 64, tPb, tPb + 32, vh, vl, idO, j > 0, 2);
+        tc::commit(&o_done[b]);
+        tc::commit(&kv_empty[st]);
+      }
+    }
+  } else if (warp == kFwdLoader / 32) {
+    // ---------------------------------------------------------- query-row loader
+    const int ln = tid & 31;
+    auto write_out = [&](int j) {  // lane 0
+      int q0, h;
+      dq_item(snake_item(j, gridDim.x, items), rows, T, H, q0, h);
+      if (!sh.failed)
+#pragma unroll
+        for (int half = 0; half < HD / 32; ++half)
+          tma_store_box(&map_o, h * HD + 32 * half, q0, staging + half * kBoxBytes);
+      bulk_commit();
+    };
+    auto load = [&](int kk) {
+      int q0, h, kbeg, n;
+      dq_item(snake_item(kk, gridDim.x, items), rows, T, H, q0, h);
+      dq_keys(q0, rows, T, kbeg, n);
+      const int kt0 = kbeg / kTcK, pb = kk & 1;
+      float mn = INFINITY;
+      for (int j = ln; j < n; j += 32) {
+        const float4 hd4 = __ldg(reinterpret_cast<const float4*>(kfmt + ((size_t)h * nkt + kt0 + j) * F::KTILE_BYTES +
+                                                                 F::HEADER_OFF));
+        tscale[pb][j] = make_float2(hd4.x, hd4.y);
+        mn = fminf(mn, hd4.y);
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+      if (ln == 0) vmin[pb] = mn;
+      __syncwarp();
+      if (ln == 0) {
+        // arrive (releasing the scales) and expect the boxes' bytes
+        tc::bar_expect_tx(&staged, sh.failed ? 0u : (uint32_t)((HD / 32) * kBoxBytes));
+        if (!sh.failed)
+#pragma unroll
+          for (int half = 0; half < HD / 32; ++half)
+            tma_load_box(staging + half * kBoxBytes, &map_q, h * HD + 32 * half, q0, &staged);
+      }
+    };
+    int ni = 0;
+    while (snake_item(ni, gridDim.x, items) >= 0) ++ni;
+    for (int kk = 0; kk < ni; ++kk) {
+      if (kk >= 1) wait(&drained, (kk - 1) & 1);  // rows kk - 1 are in TMEM; staging holds O of kk - 2
+      __syncwarp();
+      if (kk >= 2 && ln == 0) {
+        write_out(kk - 2);
+        bulk_wait_read();  // the stores have read staging before it is refilled
+      }
+      __syncwarp();
+      load(kk);
+    }
+    if (ni > 0) {
+      wait(&drained, (ni - 1) & 1);
+      if (ln == 0) {
+        if (ni >= 2) {
+          write_out(ni - 2);
+          bulk_wait_read();
+        }
+        tc::bar_arrive(&staged);  // staging is free for the last tile's O
+      }
+      wait(&drained, ni & 1);
+      if (ln == 0) {
+        write_out(ni - 1);
         bulk_wait_all();  // every store done before the CTA leaves
       }
       __syncwarp();

@@ -263,9 +263,12 @@ struct AttentionOpsTc final : AttentionOps {
   void forward(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                const float* v, float* o, float* lse) override {
     prepare_keys(s, rows, W, H, k, v);
-    dim3 grid((rows + kTcRows - 1) / kTcRows, H);
-    attention_forward_f16<HD><<<grid, kTcThreads2, F16Att<HD>::smem_forward, s>>>(
-        rows, W, T, 1.0f / sqrtf((float)hd), q, kfmt16(rows, H), o, lse, err);
+    CUtensorMap mq, mo;
+    require(encode_rows_map(&mq, q, rows, W, kTcRows) && encode_rows_map(&mo, o, rows, W, kTcRows),
+            "attention forward: TMA maps need 16-byte aligned tensors", MB_ERR_UNSUPPORTED);
+    const int items = ((rows + kTcRows - 1) / kTcRows) * H;
+    attention_forward_f16<HD><<<std::min(items, sms), kFwdThreads, F16Att<HD>::smem_forward, s>>>(
+        rows, T, H, 1.0f / sqrtf((float)hd), mq, kfmt16(rows, H), mo, lse, err);
   }
   void backward_dkdv(cudaStream_t s, int rows, int W, int T, int H, int hd, const float* q, const float* k,
                      const float* v, const float* dout, const float* lse, const float* delta, const float* dv_add,
