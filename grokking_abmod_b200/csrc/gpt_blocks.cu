@@ -299,20 +299,25 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
   const RopeLane rope(c.cp, hp);
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    float2 n1[RPT], dn[RPT];
+    float2 n1[RPT], dn[RPT], gin[3][RPT], gx[RPT];
     float inv1[RPT];
     int pos[RPT];
     tile_positions<T>(c, tile, d.sequence, pos);
+    // Every row load of the tile is issued here, so their latencies overlap.
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
-      n1[k] = ld2<T>(x, tile * T::TR + c.row(k), d.rows, W, c.cp);
+      const int r = tile * T::TR + c.row(k);
+      n1[k] = ld2<T>(x, r, d.rows, W, c.cp);
+      gin[0][k] = ld2<T>(dq, r, d.rows, W, c.cp);
+      gin[1][k] = ld2<T>(dk, r, d.rows, W, c.cp);
+      gin[2][k] = ld2<T>(dv, r, d.rows, W, c.cp);
+      gx[k] = ld2<T>(dxm, r, d.rows, W, c.cp);
       dn[k] = make_float2(0.f, 0.f);
     }
     rmsnorm_rows<T>(c, n1, inv1, red, phase, W);
 #pragma unroll 1
     for (int m = 0; m < 3; ++m) {
       const float4* wg = reinterpret_cast<const float4*>(m == 0 ? wq : (m == 1 ? wk : wv));
-      const float* grad = m == 0 ? dq : (m == 1 ? dk : dv);
       float2 a[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) a[k] = n1[k];
@@ -322,8 +327,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       float2 gm[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) {
-        const int r = tile * T::TR + c.row(k);
-        float2 gg = ld2<T>(grad, r, d.rows, W, c.cp);
+        float2 gg = m == 0 ? gin[0][k] : (m == 1 ? gin[1][k] : gin[2][k]);
         if (m < 2) {
           // QK-Norm then RoPE in forward; backward: inverse RoPE, then the
           // per-head RMSNorm adjoint.
@@ -343,7 +347,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
       const int r = tile * T::TR + c.row(k);
-      st2(dx_out, r, d.rows, W, c.cp, ld2<T>(dxm, r, d.rows, W, c.cp) + dn[k]);
+      st2(dx_out, r, d.rows, W, c.cp, gx[k] + dn[k]);
     }
   }
   __syncthreads();
