@@ -89,6 +89,8 @@ SIGNATURES = {
     "mb_gpt_allocated_device_bytes": (ctypes.c_int, [ctypes.c_void_p, c_size_p]),
     "mb_gpt_step_launches": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, c_size_p]),
     "mb_gpt_set_timing": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "mb_gpt_set_workspace_capacity": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t]),
+    "mb_gpt_workspace_capacity": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
     "mb_gpt_kernel_times": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t, c_float_p, c_size_p]),
     "mb_nccl_unique_id": (ctypes.c_int, [c_u8_p]),
     "mb_gpt_attach_nccl": (ctypes.c_int, [ctypes.c_void_p, c_u8_p, ctypes.c_int, ctypes.c_int]),

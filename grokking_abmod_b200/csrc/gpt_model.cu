@@ -561,6 +561,19 @@ class GptModel {
     }
   }
 
+  // src/gpt/gpu.rs:1779-1791: how many batch-shape workspaces stay cached
+  // (1..3); lowering it frees the oldest ones at once.
+  void set_workspace_capacity(size_t capacity) {
+    require(capacity >= 1 && capacity <= 3, "workspace capacity must be in 1..3");
+    capacity_ = capacity;
+    if (workspaces_.size() > capacity_) MB_CUDA(cudaStreamSynchronize(stream_));
+    while (workspaces_.size() > capacity_) {
+      if (last_ == workspaces_.front().get()) last_ = nullptr;
+      workspaces_.pop_front();
+    }
+  }
+  size_t workspace_capacity() const { return capacity_; }
+
   void set_timing(bool on) {
     if (on == timing_) return;
     timing_ = on;
@@ -666,7 +679,7 @@ class GptModel {
         return *workspaces_.back();
       }
     }
-    if (workspaces_.size() == 3) {
+    if (workspaces_.size() >= capacity_) {
       MB_CUDA(cudaStreamSynchronize(stream_));
       if (last_ == workspaces_.front().get()) last_ = nullptr;
       workspaces_.pop_front();
@@ -995,6 +1008,7 @@ class GptModel {
   OptimizerState* opt_ = nullptr;
   int* tc_err_ = nullptr;
   std::deque<std::unique_ptr<Workspace>> workspaces_;
+  size_t capacity_ = 1;  // the reference's default (src/gpt/gpu.rs:1767)
   Workspace* last_ = nullptr;
   ncclComm_t comm_ = nullptr;
   bool owns_comm_ = false;
@@ -1280,6 +1294,17 @@ int mb_gpt_step_launches(mb_gpt* m, size_t rows, size_t sequence, size_t* launch
     (void)sequence;
     mb::require(rows >= 1 && rows <= (size_t)INT32_MAX / 2, "rows out of range");
     *launches = model_of(m).step_launches((int)rows);
+  });
+}
+
+int mb_gpt_set_workspace_capacity(mb_gpt* m, size_t capacity) {
+  return guarded([&] { model_of(m).set_workspace_capacity(capacity); });
+}
+
+int mb_gpt_workspace_capacity(mb_gpt* m, size_t* capacity) {
+  return guarded([&] {
+    need(capacity, "capacity");
+    *capacity = model_of(m).workspace_capacity();
   });
 }
 

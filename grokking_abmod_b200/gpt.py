@@ -12,7 +12,7 @@ from dataclasses import dataclass, replace
 import numpy as np
 
 from . import _lib
-from ._lib import AdamWC, GptConfigC, IGNORE_TARGET, check, ptr
+from ._lib import MB_ERR_INVALID, AdamWC, GptConfigC, IGNORE_TARGET, MeshError, check, ptr
 
 __all__ = ["GptConfig", "AdamWOptions", "MeshGpt", "IGNORE_TARGET", "parameter_count",
            "initial_parameters", "token_codes"]
@@ -260,6 +260,18 @@ class MeshGpt:
     def step_launches(self, rows: int, sequence: int) -> int:
         n = ctypes.c_size_t()
         check(self._lib.mb_gpt_step_launches(self._h, rows, sequence, ctypes.byref(n)))
+        return n.value
+
+    def set_workspace_capacity(self, capacity: int) -> None:
+        """How many batch-shape workspaces stay cached, 1..3 (src/gpt/gpu.rs:1779-1787)."""
+        if capacity < 0:
+            raise MeshError(MB_ERR_INVALID, "workspace capacity must be in 1..3")
+        check(self._lib.mb_gpt_set_workspace_capacity(self._h, capacity))
+
+    def workspace_capacity(self) -> int:
+        """src/gpt/gpu.rs:1789-1791."""
+        n = ctypes.c_size_t()
+        check(self._lib.mb_gpt_workspace_capacity(self._h, ctypes.byref(n)))
         return n.value
 
     # ------------------------------------------------------------- timing

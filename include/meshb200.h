@@ -137,6 +137,15 @@ int mb_gpt_check(mb_gpt* model);
 int mb_gpt_stream(mb_gpt* model, void** stream);
 /* Device bytes owned by the model (allocated_device_bytes(), :1808-1844). */
 int mb_gpt_allocated_device_bytes(mb_gpt* model, size_t* bytes);
+/* Batch-shape workspaces kept cached (src/gpt/gpu.rs:1779-1791
+ * set_workspace_capacity / workspace_capacity): each distinct
+ * (rows, sequence) gets a workspace with its own captured step graph; at
+ * most `capacity` (1..3, MB_ERR_INVALID otherwise; default 1 as in the
+ * reference) are kept, the least recently used dropped first.  Lowering the
+ * capacity frees the excess at once (after the model's stream drains). */
+int mb_gpt_set_workspace_capacity(mb_gpt* model, size_t capacity);
+int mb_gpt_workspace_capacity(mb_gpt* model, size_t* capacity);
+
 /* Number of kernel launches one training step enqueues (diagnostics). */
 int mb_gpt_step_launches(mb_gpt* model, size_t rows, size_t sequence, size_t* launches);
 

@@ -99,6 +99,29 @@ def test_gradients_are_bitwise_repeatable():
     assert l1 == l2 and g1.tobytes() == g2.tobytes()
 
 
+def test_workspace_capacity():
+    """set_workspace_capacity / workspace_capacity (src/gpt/gpu.rs:1779-1791;
+    the reference's CLI checks 0 and 4 are refused, src/bin/mesh-gpt.rs:600-606):
+    results do not depend on which batch shapes stay cached."""
+    kw = dict(vocab_size=64, context=64, width=256, heads=4, layers=2)
+    _, gpu = _pair(kw)
+    assert gpu.workspace_capacity() == 1
+    for bad in (0, 4):
+        with pytest.raises(MeshError):
+            gpu.set_workspace_capacity(bad)
+    assert gpu.workspace_capacity() == 1
+    xa, ya = _batch(GptConfig(**kw), 4, 64, seed=3)
+    xb, yb = _batch(GptConfig(**kw), 2, 32, seed=4)
+    want_a, want_b = gpu.loss_and_gradient(xa, ya, 64), gpu.loss_and_gradient(xb, yb, 32)
+    for cap in (3, 2, 1):
+        gpu.set_workspace_capacity(cap)
+        assert gpu.workspace_capacity() == cap
+        for _ in range(2):
+            for (x, y, s), want in (((xa, ya, 64), want_a), ((xb, yb, 32), want_b)):
+                loss, grad = gpu.loss_and_gradient(x, y, s)
+                assert loss == want[0] and grad.tobytes() == want[1].tobytes()
+
+
 @pytest.mark.parametrize("opt", [AdamWOptions(learning_rate=0.002, weight_decay=0.01),
                                  AdamWOptions(learning_rate=0.001, weight_decay=1.0, beta2=0.98)])
 def test_adamw_matches_f32_host_optimizer_and_resets(opt):
