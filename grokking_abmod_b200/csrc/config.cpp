@@ -38,7 +38,7 @@ void validate_kernel_shapes(const mb_gpt_config& c) {
   const uint32_t hd = c.width / c.heads;
   const bool width_ok = c.width == 64 || c.width == 128 || c.width == 256 || c.width == 384 || c.width == 512;
   require(width_ok, "this build's fused kernels support widths 64, 128, 256, 384 and 512", MB_ERR_UNSUPPORTED);
-  require(hd <= 64 && (hd & (hd - 1)) == 0, "this build's kernels support power-of-two head widths up to 64",
+  require(hd <= 128 && (hd & (hd - 1)) == 0, "this build's kernels support power-of-two head widths up to 128",
           MB_ERR_UNSUPPORTED);
   require((size_t)c.vocab_size * c.width <= 65536 && c.vocab_size <= 1024,
           "this build's fused head supports vocab * width <= 65536", MB_ERR_UNSUPPORTED);

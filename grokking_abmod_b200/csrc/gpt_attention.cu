@@ -81,9 +81,12 @@ __device__ __forceinline__ void tile_pv(float (&out)[4][Att<HD>::OC], const floa
     for (int jj = 0; jj < 4; ++jj) {
       float vv[OC];
       const float* vr = v + (j + jj) * A::LD + tx * OC;
-      if constexpr (OC == 4) {
-        float4 t = *reinterpret_cast<const float4*>(vr);
-        vv[0] = t.x; vv[1] = t.y; vv[2] = t.z; vv[3] = t.w;
+      if constexpr (OC % 4 == 0) {
+#pragma unroll
+        for (int c = 0; c < OC; c += 4) {
+          const float4 t = *reinterpret_cast<const float4*>(vr + c);
+          vv[c] = t.x; vv[c + 1] = t.y; vv[c + 2] = t.z; vv[c + 3] = t.w;
+        }
       } else if constexpr (OC == 2) {
         float2 t = *reinterpret_cast<const float2*>(vr);
         vv[0] = t.x; vv[1] = t.y;

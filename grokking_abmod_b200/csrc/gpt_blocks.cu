@@ -32,10 +32,13 @@ __device__ __forceinline__ void st2(float* p, int row, int rows, int W, int cp, 
   if (row < rows) reinterpret_cast<float2*>(p + (size_t)row * W)[cp] = v;
 }
 
-// Per-head RMS (QK-Norm): returns 1/rms of the owned pair's head, and the
-// normalized pair in v.  inv_hw = 1 / head width.
-__device__ __forceinline__ float head_rmsnorm(float2& v, int hp, float inv_hw) {
-  float s = head_sum(v.x * v.x + v.y * v.y, hp);
+// Per-head RMS (QK-Norm) of row k's pair: returns 1/rms of the pair's head,
+// and the normalized pair in v.  inv_hw = 1 / head width.  Every thread of
+// the CTA calls it at the same point (wide heads reduce through `red`).
+template <bool WIDE, class T>
+__device__ __forceinline__ float head_rmsnorm(const Ctx<T>& c, float2& v, int hp, float inv_hw, int k, float* red,
+                                              int& phase) {
+  float s = head_sum_any<WIDE, T>(c, v.x * v.x + v.y * v.y, hp, k, red, phase);
   float inv = rms_scale(s, inv_hw);
   v = v * inv;
   return inv;
@@ -99,8 +102,8 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
         const int r = tile * T::TR + c.row(k);
         float2 v = a[k];
         if (m < 2) {
-          head_rmsnorm(v, hp, inv_hw);
-          v = rope.apply(v, pos[k], rope_cs, false);
+          head_rmsnorm<S::WIDE, T>(c, v, hp, inv_hw, k, red, phase);
+          v = rope_any<S::WIDE, T>(c, rope, v, k, pos[k], rope_cs, false, bufs);
         }
         st2(out, r, d.rows, W, c.cp, v);
       }
@@ -132,10 +135,10 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
       float2 vv = ld2<T>(v, r, d.rows, W, c.cp);
       res[k] = ld2<T>(x, r, d.rows, W, c.cp);
       // XSA: z = y - (y.u)u, u = v / max(|v|, eps)   (src/gpt/gpu.rs:829-853)
-      float sq = head_sum(vv.x * vv.x + vv.y * vv.y, hp);
+      float sq = head_sum_any<S::WIDE, T>(c, vv.x * vv.x + vv.y * vv.y, hp, k, red, phase);
       float iv = xsa_scale(sq);
       float2 u = vv * iv;
-      float proj = head_sum(y.x * u.x + y.y * u.y, hp);
+      float proj = head_sum_any<S::WIDE, T>(c, y.x * u.x + y.y * u.y, hp, k, red, phase);
       a[k] = make_float2(y.x - proj * u.x, y.y - proj * u.y);
     }
     mesh_forward<W, T, S::A, S::CONN>(c, d, a, reinterpret_cast<const float4*>(wo), S::attn(d), bufs, false);
@@ -229,10 +232,10 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
     float proj[RPT], iv[RPT], sq[RPT];
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
-      sq[k] = head_sum(vv[k].x * vv[k].x + vv[k].y * vv[k].y, hp);
+      sq[k] = head_sum_any<S::WIDE, T>(c, vv[k].x * vv[k].x + vv[k].y * vv[k].y, hp, k, red, phase);
       iv[k] = xsa_scale(sq[k]);
       u[k] = vv[k] * iv[k];
-      proj[k] = head_sum(y[k].x * u[k].x + y[k].y * u[k].y, hp);
+      proj[k] = head_sum_any<S::WIDE, T>(c, y[k].x * u[k].x + y[k].y * u[k].y, hp, k, red, phase);
     }
     __syncthreads();  // the FFN backward may still read bufs
     KeptInputs<T, S::A, S::CONN> kept_o;
@@ -250,7 +253,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
       const int r = tile * T::TR + c.row(k);
-      float gp = head_sum(dy[k].x * u[k].x + dy[k].y * u[k].y, hp);
+      float gp = head_sum_any<S::WIDE, T>(c, dy[k].x * u[k].x + dy[k].y * u[k].y, hp, k, red, phase);
       float2 dO = make_float2(dy[k].x - gp * u[k].x, dy[k].y - gp * u[k].y);
       float2 dv;
       const bool above = sq[k] >= kXsaEpsilon * kXsaEpsilon;
@@ -261,7 +264,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
         dv.y += 2.0f * proj[k] * gp * u[k].y;
       }
       dv = dv * iv[k];
-      float delta = head_sum(dO.x * y[k].x + dO.y * y[k].y, hp);
+      float delta = head_sum_any<S::WIDE, T>(c, dO.x * y[k].x + dO.y * y[k].y, hp, k, red, phase);
       st2(do_out, r, d.rows, W, c.cp, dO);
       st2(dvx_out, r, d.rows, W, c.cp, dv);
       st2(dxm_out, r, d.rows, W, c.cp, g[k]);
@@ -332,9 +335,9 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
           // QK-Norm then RoPE in forward; backward: inverse RoPE, then the
           // per-head RMSNorm adjoint.
           float2 qn = a[k];
-          float ih = head_rmsnorm(qn, hp, inv_hw);
-          gg = rope.apply(gg, pos[k], rope_cs, true);
-          float dot = head_sum(gg.x * qn.x + gg.y * qn.y, hp) * inv_hw;
+          float ih = head_rmsnorm<S::WIDE, T>(c, qn, hp, inv_hw, k, red, phase);
+          gg = rope_any<S::WIDE, T>(c, rope, gg, k, pos[k], rope_cs, true, xch);
+          float dot = head_sum_any<S::WIDE, T>(c, gg.x * qn.x + gg.y * qn.y, hp, k, red, phase) * inv_hw;
           gg = make_float2(ih * (gg.x - qn.x * dot), ih * (gg.y - qn.y * dot));
         }
         gm[k] = gg;

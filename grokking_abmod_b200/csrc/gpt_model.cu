@@ -146,21 +146,25 @@ struct BlockOpsW final : BlockOps {
 
 // The reference's default mesh depths (attention 4, FFN 6; src/gpt/config.rs:46-47)
 // get kernels with the shape compiled in; other depths run the same kernels
-// with the shape read at run time.
+// with the shape read at run time, and heads of 128 channels or more (hd,
+// from width 128 up) the variant whose head sums and RoPE partners cross warps.
 template <int W>
-std::unique_ptr<BlockOps> make_block_ops_w(int A, int F, int conn) {
+std::unique_ptr<BlockOps> make_block_ops_w(int A, int F, int conn, int hd) {
+  if constexpr (W >= 128) {
+    if (hd > 64) return std::make_unique<BlockOpsW<W, RuntimeShapeWide>>(A, F);
+  }
   if (A == 4 && F == 6 && conn == 0) return std::make_unique<BlockOpsW<W, MeshShape<4, 6, 0>>>(A, F);
   if (A == 4 && F == 6 && conn == 1) return std::make_unique<BlockOpsW<W, MeshShape<4, 6, 1>>>(A, F);
   return std::make_unique<BlockOpsW<W, RuntimeShape>>(A, F);
 }
 
-std::unique_ptr<BlockOps> make_block_ops(int W, int A, int F, int conn) {
+std::unique_ptr<BlockOps> make_block_ops(int W, int A, int F, int conn, int hd) {
   switch (W) {
-    case 64: return make_block_ops_w<64>(A, F, conn);
-    case 128: return make_block_ops_w<128>(A, F, conn);
-    case 256: return make_block_ops_w<256>(A, F, conn);
-    case 384: return make_block_ops_w<384>(A, F, conn);
-    case 512: return make_block_ops_w<512>(A, F, conn);
+    case 64: return make_block_ops_w<64>(A, F, conn, hd);
+    case 128: return make_block_ops_w<128>(A, F, conn, hd);
+    case 256: return make_block_ops_w<256>(A, F, conn, hd);
+    case 384: return make_block_ops_w<384>(A, F, conn, hd);
+    case 512: return make_block_ops_w<512>(A, F, conn, hd);
   }
   throw Error(MB_ERR_UNSUPPORTED, "unsupported width");
 }
@@ -307,6 +311,7 @@ std::unique_ptr<AttentionOps> make_attention_ops(int hd, int* err) {
   if (hd <= 16) return std::make_unique<AttentionOpsD<16>>();
   if (hd <= 32) return std::make_unique<AttentionOpsD<32>>();
   if (hd <= 64) return std::make_unique<AttentionOpsD<64>>();
+  if (hd <= 128) return std::make_unique<AttentionOpsD<128>>();
   throw Error(MB_ERR_UNSUPPORTED, "unsupported head width");
 }
 
@@ -406,7 +411,8 @@ class GptModel {
       MB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
       owns_stream_ = true;
     }
-    blocks_ = make_block_ops(cfg.width, cfg.attention_mesh_depth, cfg.ffn_mesh_depth, (int)cfg.connectivity);
+    blocks_ = make_block_ops(cfg.width, cfg.attention_mesh_depth, cfg.ffn_mesh_depth, (int)cfg.connectivity,
+                             (int)(cfg.width / cfg.heads));
     tc_err_ = mem_.alloc<int>(1);
     MB_CUDA(cudaMemset(tc_err_, 0, sizeof(int)));
     attention_ = make_attention_ops(cfg.width / cfg.heads, tc_err_);

@@ -268,8 +268,8 @@ inline AttentionShape attention_shape(size_t rows, uint32_t sequence, uint32_t w
   require(sequence >= 1 && sequence <= 4096 && rows % sequence == 0,
           "rows must hold whole sequences of 1..4096 tokens");
   require(width % 4 == 0, "width must be a multiple of 4");
-  require(rh.hd == 32 || rh.hd == 64 || rh.hd <= 16, "attention supports head widths 2..16, 32 and 64",
-          MB_ERR_UNSUPPORTED);
+  require(rh.hd == 32 || rh.hd == 64 || rh.hd == 128 || rh.hd <= 16,
+          "attention supports head widths 2..16, 32, 64 and 128", MB_ERR_UNSUPPORTED);
   return AttentionShape{rows, (int)sequence, rh.W, rh.H, rh.hd};
 }
 

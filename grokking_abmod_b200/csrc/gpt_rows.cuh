@@ -51,13 +51,18 @@ __device__ __forceinline__ int mesh_stride(const Dims& d, int layer) {
 // from Dims at run time) and connectivity (-1 = read from Dims).  With a
 // fixed shape the layer loops unroll, so every stride, shared-memory offset
 // and weight address is a constant instead of per-layer integer work.
-template <int A_, int F_, int CONN_>
+// WIDE_: heads of 128 channels or more (hp > 32 pairs), whose per-head
+// sums and RoPE partners cross warps (head_sum_any, rope_any); the common
+// shapes compile without that path.
+template <int A_, int F_, int CONN_, bool WIDE_ = false>
 struct MeshShape {
   static constexpr int A = A_, F = F_, CONN = CONN_;
+  static constexpr bool WIDE = WIDE_;
   __device__ static __forceinline__ int attn(const Dims& d) { return A > 0 ? A : d.attn_depth; }
   __device__ static __forceinline__ int ffn(const Dims& d) { return F > 0 ? F : d.ffn_depth; }
 };
 using RuntimeShape = MeshShape<0, 0, -1>;
+using RuntimeShapeWide = MeshShape<0, 0, -1, true>;
 
 // floor(log2 W), the butterfly period (Dims::log2w).
 template <int W>
@@ -168,6 +173,30 @@ __device__ __forceinline__ float head_sum(float v, int hp) {
     case 4: return group_sum<4>(v);
     case 2: return group_sum<2>(v);
     default: return v;
+  }
+}
+
+// Per-head sums for any head width: up to 64 channels a head lies within a
+// warp (shuffles); wider heads (hp > 32 pairs) span hp / 32 warps, whose
+// warp sums meet in `red` (2 x TR x WPR floats, halves alternating with
+// `phase` as in row_sums) behind one barrier.  Row k of the thread's rows;
+// every thread of the CTA calls it at the same point.
+template <bool WIDE, class T>
+__device__ __forceinline__ float head_sum_any(const Ctx<T>& c, float v, int hp, int k, float* red, int& phase) {
+  if constexpr (!WIDE) {
+    return head_sum(v, hp);
+  } else {
+    if (hp <= 32) return head_sum(v, hp);
+    v = group_sum<32>(v);
+    float* r = red + phase * T::TR * T::WPR;
+    phase ^= 1;
+    const int wir = c.cp >> 5, row = c.row(k);
+    if (c.lane == 0) r[row * T::WPR + wir] = v;
+    __syncthreads();
+    const int g = hp >> 5, first = (wir / g) * g;
+    float s = 0.f;
+    for (int j = 0; j < g; ++j) s += r[row * T::WPR + first + j];
+    return s;
   }
 }
 
@@ -399,13 +428,33 @@ struct RopeLane {
       const float sn = inverse ? -t.y : t.y;
       return make_float2(v.x * t.x - v.y * sn, v.y * t.x + v.x * sn);
     }
-    const float2 p = shfl_xor2(v, half);
+    return combine(v, shfl_xor2(v, half), pos, cs, inverse);
+  }
+  // The rotation given the partner pair p (hp >= 2).
+  __device__ __forceinline__ float2 combine(float2 v, float2 p, int pos, const float2* cs, bool inverse) const {
     // (cos, sin) of the pair's two frequencies, one 16-byte load (i0 and hp are even).
     const float4 t = __ldg(reinterpret_cast<const float4*>(cs + pos * hp + i0));
     const float sg = inverse ? -sign : sign;
     return fma2(v, make_float2(t.x, t.z), mul2(p * sg, make_float2(t.y, t.w)));
   }
 };
+
+// RoPE of row k's pair for any head width: in heads of 128 channels or more
+// the split-half partner sits in another warp, exchanged through `xs`
+// (TR x W floats that nothing else uses across the three barriers).  Every
+// thread of the CTA calls it at the same point.
+template <bool WIDE, class T>
+__device__ __forceinline__ float2 rope_any(const Ctx<T>& c, const RopeLane& rope, float2 v, int k, int pos,
+                                           const float2* cs, bool inverse, float* xs) {
+  if (!WIDE || rope.hp == 1 || rope.half < 32) return rope.apply(v, pos, cs, inverse);
+  float2* x2 = reinterpret_cast<float2*>(xs);
+  __syncthreads();
+  x2[c.row(k) * T::PAIRS + c.cp] = v;
+  __syncthreads();
+  const float2 p = x2[c.row(k) * T::PAIRS + (c.cp ^ rope.half)];
+  __syncthreads();
+  return rope.combine(v, p, pos, cs, inverse);
+}
 
 // Position within its sequence of each owned row of a tile.
 template <class T>

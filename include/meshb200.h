@@ -234,7 +234,8 @@ int mb_op_rope(const float* x, float* y, size_t rows, uint32_t sequence, uint32_
  * rows (diagonal included), the FA2 forward of src/gpt/gpu.rs:381-498,
  * :752-779.  lse: device [heads][rows], each row's base-2 log-sum-exp of
  * its scaled scores times log2(e).  Head widths 32 and 64 run on the tcgen05
- * tensor cores (3xTF32), 2..16 on FP32 SIMT; others MB_ERR_UNSUPPORTED.
+ * tensor cores (3xF16: scaled FP16 hi/lo parts, three MMAs per product),
+ * 2..16 and 128 on FP32 SIMT; others MB_ERR_UNSUPPORTED.
  * Q, K, V, O 16-byte aligned, width a multiple of 4.  Scratch for the
  * formatted key tiles comes from cudaMallocAsync on `stream`.  d_status
  * (device int) is set to 1 if a tensor-core wait gave up. */

@@ -121,6 +121,7 @@ def _max_growth(q, k, seq, heads):
     (768, 256, 256, 4, False),    # the cfg3 shape
     (390, 130, 128, 4, True),     # hd 32, ragged tiles
     (96, 32, 64, 8, False),       # hd 8 on the FP32 SIMT kernels
+    (256, 128, 256, 2, False),    # hd 128 on the FP32 SIMT kernels
 ])
 def test_attention_forward_and_backward(rows, seq, width, heads, large):
     q, k, v, do = _attention_case(rows, seq, width, heads, large)
@@ -204,8 +205,8 @@ def test_invalid_op_arguments_are_rejected():
     with pytest.raises(MeshError):
         ops.rope(x, 5, 2)  # rows must hold whole sequences
     with pytest.raises(UnsupportedShape):
-        big = _t(np.zeros((4, 256)))
-        ops.attention_forward(big, big, big, 4, 2)  # head width 128
+        big = _t(np.zeros((4, 512)))
+        ops.attention_forward(big, big, big, 4, 2)  # head width 256
 
 
 def test_models_share_a_context_stream():

@@ -75,6 +75,10 @@ def test_config_validation_and_unsupported_shapes():
     assert lib.mb_gpt_validate(ctypes.byref(c)) == _lib.MB_ERR_UNSUPPORTED
     c = GptConfig(vocab_size=64, width=512, heads=8, context=1024, layers=8).to_c()
     assert lib.mb_gpt_validate(ctypes.byref(c)) == 0
+    c = GptConfig(vocab_size=64, width=512, heads=4).to_c()  # head width 128
+    assert lib.mb_gpt_validate(ctypes.byref(c)) == 0
+    c = GptConfig(vocab_size=64, width=512, heads=2).to_c()  # head width 256
+    assert lib.mb_gpt_validate(ctypes.byref(c)) == _lib.MB_ERR_UNSUPPORTED
 
 
 def test_random_units_match_splitmix():
