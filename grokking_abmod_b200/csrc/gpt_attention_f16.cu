@@ -335,12 +335,15 @@ __global__ void __launch_bounds__(kFmtThreads) attention_format_queries_f16(int 
 // tiles.  K and V sit in TMEM split into FP16 hi/lo columns with per-row
 // scales; dV and dK accumulate in TMEM; S^T/dP^T are double-buffered.
 // Per step i (buffer b = i & 1, i counted over the CTA's whole list):
-// thread 544 issues S^T = K Q^T and dP^T = V dO^T (keys on lanes, N = 64
-// queries); all 16 compute warps (thread (row, quarter) owns query columns
-// [16 quarter, +16)) form P^T = exp2(S^T scale - lse) and store it over the
-// S^T columns they have read (FP16 hi/lo interleaved), then
+// threads 544 and 512 issue S^T = K Q^T and dP^T = V dO^T (keys on lanes,
+// N = 64 queries); all 16 compute warps (thread (row, quarter) owns query
+// columns [16 quarter, +16)) form P^T = exp2(S^T scale - lse) and store it
+// over the S^T columns they have read (FP16 hi/lo interleaved), then
 // dS^T = P^T (dP^T - delta) scale over the dP^T columns; thread 576 issues
-// dV += P^T dO and dK += dS^T Q.
+// dV += P^T dO and dK += dS^T Q.  Thread 512 also streams the query tiles.
+// The MMAs come from three warps because a warp issues at most one MMA per
+// ~48 cycles (~100 beside busy compute warps), while the tensor pipe
+// finishes an N = 64 MMA in 32: a single issuing warp would set the pace.
 // A loader warp (608) works one key tile ahead in a shared staging area: it
 // reads the scales of the next tile's query tiles and brings its FP32 K and
 // V rows in with TMA box copies; after a key tile it writes the tile's dK
@@ -439,7 +442,8 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
   using KV = F16Kv<HD>;
   constexpr int NS = KV::STAGES;
   extern __shared__ __align__(128) uint8_t sm8[];
-  __shared__ uint64_t q_full[NS], q_empty[NS], s_full[2], dp_full[2], p_full[2], ds_full[2][2], g_done[2];
+  __shared__ uint64_t q_full[NS], q_empty[NS], s_full[2], dp_full[2], p_full[2], ds_full[2][2], dv_done[2],
+      dk_done[2];
   __shared__ uint64_t staged, kv_ready, drained;
   __shared__ TcShared sh;
   __shared__ float kscale[2][kTcRows], vscale[2][kTcRows], vnorm[2][kTcRows];  // by item parity
@@ -462,7 +466,8 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
       tc::bar_init(&p_full[b], kKvCompute);
       tc::bar_init(&ds_full[b][0], kKvCompute / 2);
       tc::bar_init(&ds_full[b][1], kKvCompute / 2);
-      tc::bar_init(&g_done[b], 1);
+      tc::bar_init(&dv_done[b], 1);
+      tc::bar_init(&dk_done[b], 1);
     }
     tc::bar_init(&staged, 1);
     tc::bar_init(&kv_ready, kKvCompute);
@@ -502,7 +507,8 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
     const uint32_t dsrc = (half8 ? tdV : tdK) + lane;
     float g[HD / 2];  // the first half of the row until staging is free
     auto drain_load = [&]() {
-      const bool ok = __all_sync(0xffffffffu, wait(&g_done[(it - 1) & 1], ((it - 1) >> 1) & 1));
+      uint64_t* done = half8 ? &dv_done[(it - 1) & 1] : &dk_done[(it - 1) & 1];
+      const bool ok = __all_sync(0xffffffffu, wait(done, ((it - 1) >> 1) & 1));
       tc::fence_after_sync();
       if (ok) {
 #pragma unroll
@@ -634,11 +640,10 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
               pv[c + u + 1] = ok1 ? ex2(t.y) : 0.f;
             }
           }
-          uint32_t hi[8], lo[8];
+          uint32_t hl[16];  // hi parts, then lo parts
 #pragma unroll
-          for (int e = 0; e < 8; ++e) tc::split_f16x2(pv[2 * e] * pc, pv[2 * e + 1] * pc, hi[e], lo[e]);
-          tc::tmem_st8u(tSb + col + lane, hi);  // P^T over the S^T columns just read
-          tc::tmem_st8u(tSb + col + 8 + lane, lo);
+          for (int e = 0; e < 8; ++e) tc::split_f16x2(pv[2 * e] * pc, pv[2 * e + 1] * pc, hl[e], hl[8 + e]);
+          tc::tmem_st16u(tSb + col + lane, hl);  // P^T over the S^T columns just read
         }
         tc::tmem_st_wait();
         tc::fence_before_sync();
@@ -661,11 +666,10 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
               dp[c + u + 1] = g.y;
             }
           }
-          uint32_t hi[8], lo[8];
+          uint32_t hl[16];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) tc::split_f16x2(dp[2 * e] * gc, dp[2 * e + 1] * gc, hi[e], lo[e]);
-          tc::tmem_st8u(tSb + 64 + col + lane, hi);  // dS^T over the dP^T columns just read
-          tc::tmem_st8u(tSb + 64 + col + 8 + lane, lo);
+          for (int e = 0; e < 8; ++e) tc::split_f16x2(dp[2 * e] * gc, dp[2 * e + 1] * gc, hl[e], hl[8 + e]);
+          tc::tmem_st16u(tSb + 64 + col + lane, hl);  // dS^T over the dP^T columns just read
           tc::tmem_st_wait();
           tc::fence_before_sync();
           tc::bar_arrive(&ds_full[b][quarter >> 1]);  // query columns [0, 32) or [32, 64)
@@ -682,27 +686,47 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
       }
       tc::bar_arrive(&drained);
     }
-  } else if (tid == kKvProducer) {
-    // ---------------------------------------------------------- query tiles
-    int it = 0;
-    for (int kk = 0;; ++kk) {
-      const int item = snake_item(kk, gridDim.x, items);
-      if (item < 0) break;
-      int k0, h;
-      kv_item(item, rows, T, H, k0, h);
-      const int n = kv_steps(k0, rows, T), qt0 = k0 / kTcQ;
-      for (int i = 0; i < n; ++i, ++it) {
-        const int st = it % NS;
-        if (it >= NS && !wait(&q_empty[st], ((it - NS) / NS) & 1)) continue;
-        if (sh.failed) continue;
+  } else if (tid == kKvIssuer || tid == kKvProducer) {
+    // ---------------------------------------------------------- S^T / dP^T issuers
+    // Thread 544: S^T = K Q^T into buffer b's first 64 columns (free once dV
+    // of step it - 2 has read P^T there); thread 512: dP^T = V dO^T into its
+    // last 64 (free once dK of step it - 2 has read dS^T).  Separate warps,
+    // so the two products issue concurrently.
+    const bool dp = tid == kKvProducer;
+    constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcQ);
+    uint64_t* full = dp ? dp_full : s_full;
+    uint64_t* freed = dp ? dk_done : dv_done;
+    const uint32_t ah = dp ? tVh : tKh, al = dp ? tVl : tKl, col = dp ? 64u : 0u;
+    const int part = dp ? G::D_HI : G::Q_HI;
+    // Thread 512 also streams the query tiles, NS - 1 steps ahead: the tile
+    // of step j goes into stage j % NS once dV and dK of step j - NS have
+    // read that stage.  It issues the load for step it + NS - 1 after its
+    // dP^T of step it, so the wait for step it - 1's release holds up only
+    // dP^T of step it + 1, which waits for dK of step it - 1 anyway.
+    int lk = 0, li = 0, lsteps = 0, lh = 0, lq0 = 0, lj = 0;  // the load cursor
+    auto load_next = [&]() {
+      while (li == lsteps) {  // the cursor's work item is done: take the next
+        const int item = snake_item(lk, gridDim.x, items);
+        if (item < 0) return;
+        int k0;
+        kv_item(item, rows, T, H, k0, lh);
+        lsteps = kv_steps(k0, rows, T);
+        lq0 = k0 / kTcQ;
+        li = 0;
+        ++lk;
+      }
+      const int st = lj % NS;
+      const bool ok = lj < NS || wait(&q_empty[st], ((lj - NS) / NS) & 1);
+      if (ok && !sh.failed) {
         tc::bar_expect_tx(&q_full[st], G::QTILE_BYTES);
-        tc::bulk_g2s(sm8 + st * G::QTILE_BYTES, qfmt + ((size_t)h * nqt + qt0 + i) * G::QTILE_BYTES,
+        tc::bulk_g2s(sm8 + st * G::QTILE_BYTES, qfmt + ((size_t)lh * nqt + lq0 + li) * G::QTILE_BYTES,
                      G::QTILE_BYTES, &q_full[st]);
       }
-    }
-  } else if (tid == kKvIssuer) {
-    // ---------------------------------------------------------- S^T / dP^T issuer
-    constexpr uint32_t idS = tc::idesc_f16(kTcRows, kTcQ);
+      ++li;
+      ++lj;
+    };
+    if (dp)
+      for (int j = 0; j < NS - 1; ++j) load_next();
     int it = 0;
     for (int kk = 0;; ++kk) {
       const int item = snake_item(kk, gridDim.x, items);
@@ -715,16 +739,14 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
         const int st = it % NS, b = it & 1;
         const uint8_t* stage = sm8 + st * G::QTILE_BYTES;
         wait(&q_full[st], (it / NS) & 1);
-        if (it >= 2) wait(&g_done[b], ((it - 2) >> 1) & 1);  // dV and dK of step it - 2 have read this buffer
+        if (it >= 2) wait(&freed[b], ((it - 2) >> 1) & 1);
         tc::fence_after_sync();
-        if (sh.failed) continue;
-        const uint32_t tSb = tS + 128 * b;
-        mma16_tmem_a<HD, HD / 16>(tSb, tKh, tKl, stage + G::Q_HI * G::PART_BYTES,
-                                  stage + (G::Q_HI + 1) * G::PART_BYTES, idS, false, 0);  // S^T = K Q^T
-        tc::commit(&s_full[b]);
-        mma16_tmem_a<HD, HD / 16>(tSb + 64, tVh, tVl, stage + G::D_HI * G::PART_BYTES,
-                                  stage + (G::D_HI + 1) * G::PART_BYTES, idS, false, 0);  // dP^T = V dO^T
-        tc::commit(&dp_full[b]);
+        if (!sh.failed) {
+          mma16_tmem_a<HD, HD / 16>(tS + 128 * b + col, ah, al, stage + part * G::PART_BYTES,
+                                    stage + (part + 1) * G::PART_BYTES, idS, false, 0);
+          tc::commit(&full[b]);
+        }
+        if (dp) load_next();
       }
     }
   } else if (tid == kKvIssuer2) {
@@ -745,9 +767,11 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
         wait(&p_full[b], pb);
         tc::fence_after_sync();
         // dV += P^T dO over the step's 64 queries (B = the dO tile [64 queries][HD], MN-major)
-        if (!sh.failed)
+        if (!sh.failed) {
           mma16_tmem_a_il<HD, 4>(tdV, tSb, stage + G::D_HI * G::PART_BYTES, stage + (G::D_HI + 1) * G::PART_BYTES,
                                  idG, i > 0, 0);
+          tc::commit(&dv_done[b]);
+        }
         for (int q2 = 0; q2 < 2; ++q2) {
           wait(&ds_full[b][q2], pb);
           tc::fence_after_sync();
@@ -757,8 +781,8 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
                                    stage + (G::Q_HI + 1) * G::PART_BYTES, idG, i > 0 || q2 > 0, 2 * q2);
         }
         if (sh.failed) continue;
-        tc::commit(&g_done[b]);
-        tc::commit(&q_empty[st]);
+        tc::commit(&dk_done[b]);
+        tc::commit(&q_empty[st]);  // both products of the step have read the stage
       }
     }
   } else if (warp == kKvLoader / 32) {
@@ -1080,11 +1104,10 @@ __global__ void __launch_bounds__(kKvThreadsP, 1)
           sv[c] = gg.x;
           sv[c + 1] = gg.y;
         }
-        uint32_t hi[8], lo[8];
+        uint32_t hl[16];  // hi parts, then lo parts
 #pragma unroll
-        for (int e = 0; e < 8; ++e) tc::split_f16x2(sv[2 * e] * gcoef, sv[2 * e + 1] * gcoef, hi[e], lo[e]);
-        tc::tmem_st8u(tSb + col + lane, hi);  // over the S columns just read
-        tc::tmem_st8u(tSb + col + 8 + lane, lo);
+        for (int e = 0; e < 8; ++e) tc::split_f16x2(sv[2 * e] * gcoef, sv[2 * e + 1] * gcoef, hl[e], hl[8 + e]);
+        tc::tmem_st16u(tSb + col + lane, hl);  // over the S columns just read
         tc::tmem_st_wait();
         tc::fence_before_sync();
         tc::bar_arrive(&d_full[b][quarter >> 1]);  // key columns [0, 32) or [32, 64)
