@@ -1192,19 +1192,54 @@ __global__ void bilinear_gradient(int n, int W, const uint32_t* __restrict__ a, 
 //  mode 4 (tied concatenation, dh0 rows of 2W): rows with a == k add
 //         dh0[r][c], rows with b == k add dh0[r][W + c].
 // `extra` ([rows][W], may be null) is added (the readout's share of dE).
-constexpr int kClassThreads = 256;
+// The block of class k first gathers every matching row (in row order) into
+// a shared list, scanning 512 rows per round, and only then sums the rows'
+// gradients, 16 loads in flight per thread: the additions per column keep
+// row order, so the result does not depend on the launch shape.  A list
+// that could overflow is summed and emptied on the way.
+constexpr int kClassThreads = 512;
+constexpr int kClassList = 4096;  // matching rows held before they are summed
 __global__ void __launch_bounds__(kClassThreads)
     class_gradient(int n, int W, int m, int mode, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
                    const float* __restrict__ dh0, const float* __restrict__ extra, float* __restrict__ out) {
-  __shared__ int list[kClassThreads];
-  __shared__ int kinds[kClassThreads];
+  __shared__ int list[kClassList];
+  __shared__ uint8_t kinds[kClassList];
   __shared__ int warp_count[kClassThreads / 32];
   __shared__ int total;
   const int k = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr int kPer = kMaxKernelWidth / kClassThreads;
+  constexpr int kPer = (kMaxKernelWidth + kClassThreads - 1) / kClassThreads;
   float acc[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+  if (tid == 0) total = 0;
+  __syncthreads();
+  const int stride = mode == 4 ? 2 * W : W;
+  // Sums list[0, cnt) into acc in list order, kBatch rows' loads at a time.
+  auto sum_list = [&](int cnt) {
+    constexpr int kBatch = 16;
+    for (int e0 = 0; e0 < cnt; e0 += kBatch) {
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int c = tid + kClassThreads * j;
+        if (c >= W) continue;
+        const int c2 = mode == 4 ? W + c : (c ^ 1);
+        float v1[kBatch], v2[kBatch];
+        int kd[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          kd[i] = e0 + i < cnt ? kinds[e0 + i] : 0;
+          const float* g = dh0 + (size_t)(e0 + i < cnt ? list[e0 + i] : 0) * stride;
+          v1[i] = (kd[i] & 1) ? g[c] : 0.f;
+          v2[i] = (kd[i] & 2) ? g[c2] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          if (kd[i] & 1) acc[j] += v1[i];
+          if (kd[i] & 2) acc[j] += (mode == 4 || !(c & 1)) ? v2[i] : -v2[i];
+        }
+      }
+    }
+  };
   for (int r0 = 0; r0 < n; r0 += kClassThreads) {
     const int r = r0 + tid;
     int kind = 0;
@@ -1221,7 +1256,7 @@ __global__ void __launch_bounds__(kClassThreads)
     if (lane == 0) warp_count[warp] = __popc(ballot);
     __syncthreads();
     if (tid == 0) {
-      int s = 0;
+      int s = total;
       for (int q = 0; q < kClassThreads / 32; ++q) {
         const int c = warp_count[q];
         warp_count[q] = s;
@@ -1233,37 +1268,17 @@ __global__ void __launch_bounds__(kClassThreads)
     if (kind != 0) {
       const int pos = warp_count[warp] + __popc(ballot & ((1u << lane) - 1u));
       list[pos] = r;
-      kinds[pos] = kind;
+      kinds[pos] = (uint8_t)kind;
     }
     __syncthreads();
-    // Rows in list order; each group of kBatch rows issues all of its loads
-    // before the adds, which keep the same order (one dependent add chain).
-    constexpr int kBatch = 8;
-    const int stride = mode == 4 ? 2 * W : W;
-    for (int e0 = 0; e0 < total; e0 += kBatch) {
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int c = tid + kClassThreads * j;
-        if (c >= W) continue;
-        const int c2 = mode == 4 ? W + c : (c ^ 1);
-        float v1[kBatch], v2[kBatch];
-        int kd[kBatch];
-#pragma unroll
-        for (int i = 0; i < kBatch; ++i) {
-          kd[i] = e0 + i < total ? kinds[e0 + i] : 0;
-          const float* g = dh0 + (size_t)(e0 + i < total ? list[e0 + i] : 0) * stride;
-          v1[i] = (kd[i] & 1) ? g[c] : 0.f;
-          v2[i] = (kd[i] & 2) ? g[c2] : 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < kBatch; ++i) {
-          if (kd[i] & 1) acc[j] += v1[i];
-          if (kd[i] & 2) acc[j] += (mode == 4 || !(c & 1)) ? v2[i] : -v2[i];
-        }
-      }
+    if (total > kClassList - kClassThreads) {  // room for one more round only
+      sum_list(total);
+      __syncthreads();
+      if (tid == 0) total = 0;
+      __syncthreads();
     }
-    __syncthreads();
   }
+  sum_list(total);
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int c = tid + kClassThreads * j;
