@@ -70,6 +70,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
     float2 n[RPT];
     float inv[RPT];
     int pos[RPT];
+    prefetch_next_tile<W, T::TR>(c.tid, tile, d.rows, tokens != nullptr ? nullptr : x, nullptr);
     tile_positions<T>(c, tile, d.sequence, pos);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     float2 a[RPT], res[RPT];
+    prefetch_next_tile<W, T::TR>(c.tid, tile, d.rows, o, v, x);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
       const int r = tile * T::TR + c.row(k);
@@ -198,6 +200,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     float2 g[RPT], n2[RPT], dy[RPT];
     float inv2[RPT];
+    prefetch_next_tile<W, T::TR>(c.tid, tile, d.rows, dxn, xmid, o, v);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
       const int r = tile * T::TR + c.row(k);
@@ -305,6 +308,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
     float2 n1[RPT], dn[RPT], gin[3][RPT], gx[RPT];
     float inv1[RPT];
     int pos[RPT];
+    prefetch_next_tile<W, T::TR>(c.tid, tile, d.rows, x, dq, dk, dv, dxm);
     tile_positions<T>(c, tile, d.sequence, pos);
     // Every row load of the tile is issued here, so their latencies overlap.
 #pragma unroll

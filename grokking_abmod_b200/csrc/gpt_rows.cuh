@@ -456,6 +456,30 @@ __device__ __forceinline__ float2 rope_any(const Ctx<T>& c, const RopeLane& rope
   return rope.combine(v, p, pos, cs, inverse);
 }
 
+// Asks L2 to fetch rows [r0, r0 + n) of a [rows][W] FP32 tensor (one bulk
+// prefetch, no registers or shared memory), so that a tile's row loads a few
+// microseconds later hit L2 instead of waiting on HBM.  Skipped past the last
+// row and for a base that is not 16-byte aligned (the instruction's rule).
+template <int W>
+__device__ __forceinline__ void prefetch_rows(const float* p, int r0, int n, int rows) {
+  if (p == nullptr || r0 >= rows) return;
+  n = n < rows - r0 ? n : rows - r0;
+  const float* a = p + (size_t)r0 * W;
+  if ((reinterpret_cast<uintptr_t>(a) & 15) != 0) return;
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((uint32_t)(n * W * 4)) : "memory");
+}
+
+// Lanes 0.. of warp 0 each prefetch one of up to five row tensors for the
+// CTA's next tile (tile + gridDim.x).
+template <int W, int TR>
+__device__ __forceinline__ void prefetch_next_tile(int tid, int tile, int rows, const float* p0, const float* p1,
+                                                   const float* p2 = nullptr, const float* p3 = nullptr,
+                                                   const float* p4 = nullptr) {
+  if (tid >= 5) return;
+  const float* p = tid == 0 ? p0 : (tid == 1 ? p1 : (tid == 2 ? p2 : (tid == 3 ? p3 : p4)));
+  prefetch_rows<W>(p, (tile + (int)gridDim.x) * TR, TR, rows);
+}
+
 // Position within its sequence of each owned row of a tile.
 template <class T>
 __device__ __forceinline__ void tile_positions(const Ctx<T>& c, int tile, int sequence, int (&pos)[T::RPT]) {
