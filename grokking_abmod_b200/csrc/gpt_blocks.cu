@@ -305,36 +305,36 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
   const RopeLane rope(c.cp, hp);
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    float2 n1[RPT], dn[RPT], gin[3][RPT], gx[RPT];
+    float2 n1[RPT], dn[RPT];
     float inv1[RPT];
     int pos[RPT];
     prefetch_next_tile<W, T::TR>(c.tid, tile, d.rows, x, dq, dk, dv, dxm);
     tile_positions<T>(c, tile, d.sequence, pos);
-    // Every row load of the tile is issued here, so their latencies overlap.
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
-      const int r = tile * T::TR + c.row(k);
-      n1[k] = ld2<T>(x, r, d.rows, W, c.cp);
-      gin[0][k] = ld2<T>(dq, r, d.rows, W, c.cp);
-      gin[1][k] = ld2<T>(dk, r, d.rows, W, c.cp);
-      gin[2][k] = ld2<T>(dv, r, d.rows, W, c.cp);
-      gx[k] = ld2<T>(dxm, r, d.rows, W, c.cp);
+      n1[k] = ld2<T>(x, tile * T::TR + c.row(k), d.rows, W, c.cp);
       dn[k] = make_float2(0.f, 0.f);
     }
     rmsnorm_rows<T>(c, n1, inv1, red, phase, W);
 #pragma unroll 1
     for (int m = 0; m < 3; ++m) {
       const float4* wg = reinterpret_cast<const float4*>(m == 0 ? wq : (m == 1 ? wk : wv));
-      float2 a[RPT];
+      // The stack's output gradient (an L2 hit after the prefetch) is
+      // requested before the forward recompute, which hides its latency;
+      // loading one stack's rows at a time keeps the register budget.
+      const float* gsrc = m == 0 ? dq : (m == 1 ? dk : dv);
+      float2 a[RPT], gm[RPT];
 #pragma unroll
-      for (int k = 0; k < RPT; ++k) a[k] = n1[k];
+      for (int k = 0; k < RPT; ++k) {
+        a[k] = n1[k];
+        gm[k] = ld2<T>(gsrc, tile * T::TR + c.row(k), d.rows, W, c.cp);
+      }
       __syncthreads();  // the previous mesh backward may still read bufs
       KeptInputs<T, S::A, S::CONN> kept;
       mesh_forward_kept<W, T, S::A, S::CONN>(c, d, a, wg, A, bufs, kept);
-      float2 gm[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) {
-        float2 gg = m == 0 ? gin[0][k] : (m == 1 ? gin[1][k] : gin[2][k]);
+        float2 gg = gm[k];
         if (m < 2) {
           // QK-Norm then RoPE in forward; backward: inverse RoPE, then the
           // per-head RMSNorm adjoint.
@@ -350,6 +350,9 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
 #pragma unroll
       for (int k = 0; k < RPT; ++k) dn[k] = dn[k] + gm[k];
     }
+    float2 gx[RPT];
+#pragma unroll
+    for (int k = 0; k < RPT; ++k) gx[k] = ld2<T>(dxm, tile * T::TR + c.row(k), d.rows, W, c.cp);
     rmsnorm_rows_backward<T>(c, n1, inv1, dn, red, phase, W);
 #pragma unroll
     for (int k = 0; k < RPT; ++k) {
