@@ -323,11 +323,16 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       // requested before the forward recompute, which hides its latency;
       // loading one stack's rows at a time keeps the register budget.
       const float* gsrc = m == 0 ? dq : (m == 1 ? dk : dv);
+      // The inverse RoPE's angles (Q and K, heads within a warp) are
+      // requested with the rows.
+      const bool early_rope = !S::WIDE && rope.hp > 1 && m < 2;
       float2 a[RPT], gm[RPT];
+      float4 ang[RPT];
 #pragma unroll
       for (int k = 0; k < RPT; ++k) {
         a[k] = n1[k];
         gm[k] = ld2<T>(gsrc, tile * T::TR + c.row(k), d.rows, W, c.cp);
+        ang[k] = early_rope ? rope.angles(pos[k], rope_cs) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       __syncthreads();  // the previous mesh backward may still read bufs
       KeptInputs<T, S::A, S::CONN> kept;
@@ -340,7 +345,8 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
           // per-head RMSNorm adjoint.
           float2 qn = a[k];
           float ih = head_rmsnorm<S::WIDE, T>(c, qn, hp, inv_hw, k, red, phase);
-          gg = rope_any<S::WIDE, T>(c, rope, gg, k, pos[k], rope_cs, true, xch);
+          gg = early_rope ? rope.rotate(gg, shfl_xor2(gg, rope.half), ang[k], true)
+                          : rope_any<S::WIDE, T>(c, rope, gg, k, pos[k], rope_cs, true, xch);
           float dot = head_sum_any<S::WIDE, T>(c, gg.x * qn.x + gg.y * qn.y, hp, k, red, phase) * inv_hw;
           gg = make_float2(ih * (gg.x - qn.x * dot), ih * (gg.y - qn.y * dot));
         }

@@ -430,12 +430,18 @@ struct RopeLane {
     }
     return combine(v, shfl_xor2(v, half), pos, cs, inverse);
   }
-  // The rotation given the partner pair p (hp >= 2).
-  __device__ __forceinline__ float2 combine(float2 v, float2 p, int pos, const float2* cs, bool inverse) const {
-    // (cos, sin) of the pair's two frequencies, one 16-byte load (i0 and hp are even).
-    const float4 t = __ldg(reinterpret_cast<const float4*>(cs + pos * hp + i0));
+  // (cos, sin) of the pair's two frequencies at position pos, one 16-byte
+  // load (i0 and hp are even; hp >= 2), so a caller can request it early.
+  __device__ __forceinline__ float4 angles(int pos, const float2* cs) const {
+    return __ldg(reinterpret_cast<const float4*>(cs + pos * hp + i0));
+  }
+  // The rotation given the partner pair p and the pair's angles t (hp >= 2).
+  __device__ __forceinline__ float2 rotate(float2 v, float2 p, float4 t, bool inverse) const {
     const float sg = inverse ? -sign : sign;
     return fma2(v, make_float2(t.x, t.z), mul2(p * sg, make_float2(t.y, t.w)));
+  }
+  __device__ __forceinline__ float2 combine(float2 v, float2 p, int pos, const float2* cs, bool inverse) const {
+    return rotate(v, p, angles(pos, cs), inverse);
   }
 };
 
