@@ -208,6 +208,7 @@ __global__ void __launch_bounds__(kGemmThreads + 32, 1)
     gemm_tf32x3_kernel(GemmOperand A, GemmOperand B, const __grid_constant__ CUtensorMap tma_a,
                        const __grid_constant__ CUtensorMap tma_b, int tma, float* __restrict__ C, int ldc,
                        size_t chunk_stride, int M, int N, int K, int k_chunk, int* __restrict__ err) {
+  wait_prior_grids();
   extern __shared__ __align__(1024) float sm[];
   __shared__ uint64_t ready[kGemmStages], done[kGemmStages];
   __shared__ uint64_t full[kGemmRaw];  // TMA completion per raw stage
@@ -393,6 +394,7 @@ __global__ void __launch_bounds__(kGemmThreads + 32, 1)
 // C[m][n] = sum over chunks (in order) of partial[chunk][m][n].
 __global__ void gemm_reduce_chunks(const float* __restrict__ partial, int chunks, int M, int N,
                                    float* __restrict__ C, int ldc) {
+  wait_prior_grids();
   const size_t mn = (size_t)M * N;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < mn; i += (size_t)gridDim.x * blockDim.x) {
     float s = partial[i];

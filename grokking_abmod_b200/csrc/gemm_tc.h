@@ -8,6 +8,12 @@
 
 namespace mb {
 
+// First statement of every grok-simple and GEMM kernel: waits until the
+// grids this one depends on through a programmatic graph edge have completed
+// and their writes are visible (PTX griddepcontrol.wait).  A kernel launched
+// without such an edge returns from it at once.
+__device__ __forceinline__ void wait_prior_grids() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // One GEMM operand of `rows` (M or N) x K: element (r, k) is p[r * ld + k]
 // (K-major) or, with k_outer, p[k * ld + r].
 struct GemmOperand {

@@ -73,6 +73,40 @@ constexpr int kMaxJ = kMaxKernelWidth / 32;  // row values per lane at the wides
 constexpr int kSplitK = 256;          // batch rows per weight-gradient GEMM chunk
 constexpr unsigned kFull = 0xffffffffu;
 
+// Turns every kernel-to-kernel edge of a captured step graph into a
+// programmatic edge from the upstream kernel's launch-completion port: the
+// downstream grid is scheduled once every block of the upstream grid has
+// started, instead of after the upstream grid has completed and the launch
+// has gone through, and its threads begin with wait_prior_grids, which
+// returns once the upstream grid has completed and its writes are visible.
+// Every kernel that a step graph holds (this file's and the GEMM's) starts
+// with that wait, so each kernel still sees all of its predecessors' writes
+// (the waits chain) and no kernel writes what a predecessor still reads.
+// A step of a few hundred microseconds spends much of its time in the
+// launch gaps between its 15 to 40 kernels; this overlaps them.
+static cudaError_t programmatic_edges(cudaGraph_t g) {
+  size_t n = 0;
+  cudaError_t e = cudaGraphGetEdges_v2(g, nullptr, nullptr, nullptr, &n);
+  if (e != cudaSuccess || n == 0) return e;
+  std::vector<cudaGraphNode_t> from(n), to(n);
+  std::vector<cudaGraphEdgeData> data(n);
+  e = cudaGraphGetEdges_v2(g, from.data(), to.data(), data.data(), &n);
+  for (size_t i = 0; e == cudaSuccess && i < n; ++i) {
+    cudaGraphNodeType a, b;
+    if ((e = cudaGraphNodeGetType(from[i], &a)) != cudaSuccess || (e = cudaGraphNodeGetType(to[i], &b)) != cudaSuccess)
+      break;
+    if (a != cudaGraphNodeTypeKernel || b != cudaGraphNodeTypeKernel || data[i].type != cudaGraphDependencyTypeDefault)
+      continue;
+    cudaGraphEdgeData pe;
+    std::memset(&pe, 0, sizeof(pe));
+    pe.from_port = cudaGraphKernelNodePortProgrammatic;
+    pe.type = cudaGraphDependencyTypeProgrammatic;
+    e = cudaGraphRemoveDependencies_v2(g, &from[i], &to[i], &data[i], 1);
+    if (e == cudaSuccess) e = cudaGraphAddDependencies_v2(g, &from[i], &to[i], &pe, 1);
+  }
+  return e;
+}
+
 // Values that change from step to step, read by the captured kernels: the
 // minibatch (table columns and index list), learning rates and corrections.
 // The step graph therefore serves every table and batch list of its size.
@@ -112,6 +146,7 @@ __global__ void gather_batch(int n, const StepScalars* __restrict__ sc, const ui
                              const uint32_t* __restrict__ ta, const uint32_t* __restrict__ tb,
                              const uint32_t* __restrict__ tt, uint32_t* __restrict__ a, uint32_t* __restrict__ b,
                              uint32_t* __restrict__ y) {
+  wait_prior_grids();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= n) return;
   if (sc != nullptr) {
@@ -137,6 +172,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
                 const uint32_t* __restrict__ a,
                 const uint32_t* __restrict__ b, const float* __restrict__ w0, const float* __restrict__ h0_in,
                 const float* __restrict__ mesh, float* __restrict__ h, float* __restrict__ act) {
+  wait_prior_grids();
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
@@ -183,6 +219,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
     mlp_backward(int n, int W, int L, int p, int lstride, const int* __restrict__ strides, const float* __restrict__ mesh,
                  const float* __restrict__ h, const float* __restrict__ dact, float* __restrict__ dh0,
                  float* __restrict__ partials) {
+  wait_prior_grids();
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pw = p * W;
@@ -274,6 +311,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
 // gradient to the last one's, src/simple/gpu.rs:2771-2792).
 __global__ void reduce_layer_partials(const float* __restrict__ partials, int ctas, int L, int count,
                                       float* __restrict__ out) {
+  wait_prior_grids();
   for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < count; t += gridDim.x * blockDim.x) {
     float total = 0.f;
     for (int l = L - 1; l >= 0; --l) {
@@ -288,6 +326,7 @@ __global__ void reduce_layer_partials(const float* __restrict__ partials, int ct
 // out[t] = sum over CTAs (in order) of partials[cta][t].
 __global__ void reduce_cta_partials(const float* __restrict__ partials, int ctas, size_t count,
                                     float* __restrict__ out) {
+  wait_prior_grids();
   for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < count; t += (size_t)gridDim.x * blockDim.x) {
     float s = 0.f;
     for (int q = 0; q < ctas; ++q) s += partials[(size_t)q * count + t];
@@ -314,6 +353,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     rotary_embed(int n, int W, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
                  const float* __restrict__ E, float* __restrict__ h0, float* __restrict__ n0,
                  float* __restrict__ inv0) {
+  wait_prior_grids();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
   if (r >= n) return;
@@ -342,6 +382,7 @@ template <int ACT, int J>
 __global__ void __launch_bounds__(kFwdWarps * 32)
     residual_norm(int n, int W, const float* __restrict__ h, const float* __restrict__ z, float* __restrict__ hn,
                   float* __restrict__ nn, float* __restrict__ inv_out) {
+  wait_prior_grids();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
   if (r >= n) return;
@@ -370,6 +411,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     concat_embed(int n, int W, int m, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
                  const float* __restrict__ w0, float* __restrict__ h0, float* __restrict__ n0,
                  float* __restrict__ inv0) {
+  wait_prior_grids();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
   if (r >= n) return;
@@ -398,6 +440,7 @@ template <int J>
 __global__ void __launch_bounds__(kFwdWarps * 32)
     rms_backward(int n, int W, const float* __restrict__ y, const float* __restrict__ inv,
                  const float* __restrict__ dy, const float* add, float* dx) {
+  wait_prior_grids();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
   if (r >= n) return;
@@ -425,6 +468,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
 template <int ACT>
 __global__ void activation_gradient(size_t count, const float* __restrict__ dh, const float* __restrict__ z,
                                     float* __restrict__ dz) {
+  wait_prior_grids();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
     dz[i] = dh[i] * act_g<ACT>(z[i]);
 }
@@ -440,6 +484,7 @@ __global__ void activation_gradient(size_t count, const float* __restrict__ dh, 
 constexpr int kChainThreads = 1024;
 __global__ void __launch_bounds__(kChainThreads)
     chain_forward(int m, int W, int ed, const float* __restrict__ chain, float* __restrict__ states) {
+  wait_prior_grids();
   __shared__ float buf[2][kChainThreads];
   const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
   const int k = blockIdx.x * RG + rg;
@@ -473,6 +518,7 @@ __global__ void __launch_bounds__(kChainThreads)
 __global__ void __launch_bounds__(kChainThreads)
     chain_backward(int m, int W, int ed, const float* __restrict__ chain, const float* __restrict__ states,
                    const float* __restrict__ dE, float* __restrict__ partials) {
+  wait_prior_grids();
   __shared__ float buf[2][kChainThreads];
   __shared__ float part[2][kChainThreads];
   const int c = threadIdx.x % W, rg = threadIdx.x / W, RG = kChainThreads / W;
@@ -528,6 +574,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     shared_forward(int n, int W, int depth, const int* __restrict__ strides, const uint32_t* __restrict__ a,
                    const uint32_t* __restrict__ b, const float* __restrict__ E, const float* __restrict__ core,
                    float* __restrict__ hs, float* __restrict__ hf, float* __restrict__ invf) {
+  wait_prior_grids();
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
@@ -583,6 +630,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
     shared_backward(int n, int W, int depth, const int* __restrict__ strides, const float* __restrict__ core,
                     const float* __restrict__ hs, const float* __restrict__ hf, const float* __restrict__ invf,
                     const float* __restrict__ dhf, float* __restrict__ dh0, float* __restrict__ partials) {
+  wait_prior_grids();
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pw = 3 * W;
@@ -724,6 +772,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
                     const float* __restrict__ mesh, const float* __restrict__ h0, float* __restrict__ ns,
                     float* __restrict__ invs, float* __restrict__ zs, float* __restrict__ hf,
                     float* __restrict__ invf) {
+  wait_prior_grids();
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
@@ -797,6 +846,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
                      const float* __restrict__ mesh, const float* __restrict__ ns, const float* __restrict__ invs,
                      const float* __restrict__ zs, const float* __restrict__ hf, const float* __restrict__ invf,
                      const float* __restrict__ dhf, float* __restrict__ dh0, float* __restrict__ partials) {
+  wait_prior_grids();
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pw = P * W;
@@ -938,6 +988,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
 // [E a | E b] of each batch row, [n][2W].
 __global__ void concat_rows(int n, int W, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
                             const float* __restrict__ E, float* __restrict__ cat) {
+  wait_prior_grids();
   const size_t total = (size_t)n * 2 * W;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / (2 * W);
@@ -953,6 +1004,7 @@ __global__ void concat_rows(int n, int W, const uint32_t* __restrict__ a, const 
 // own rows for one-hot operands: x W0 = T[a] W0a + T[b] W0b.
 __global__ void encoded_embedding(int m, int F, int W, const float* __restrict__ table, const float* __restrict__ wa,
                                   const float* __restrict__ wb, float* __restrict__ out) {
+  wait_prior_grids();
   const int total = 2 * m * W;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int k = i / W, c = i % W;
@@ -969,6 +1021,7 @@ __global__ void encoded_embedding(int m, int F, int W, const float* __restrict__
 __global__ void encoded_embedding_gradient(int m, int F, int W, const float* __restrict__ table,
                                            const float* __restrict__ dE, float* __restrict__ ga,
                                            float* __restrict__ gb) {
+  wait_prior_grids();
   const int total = 2 * F * W;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const int half = i / (F * W), rem = i % (F * W), f = rem / W, c = rem % W;
@@ -999,6 +1052,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
     fullmesh_forward(int n, int F, int nl, const FmLayer* __restrict__ layers, const float* __restrict__ table,
                      const uint32_t* __restrict__ a, const uint32_t* __restrict__ b, const float* __restrict__ w,
                      float* __restrict__ zs, float* __restrict__ logits) {
+  wait_prior_grids();
   __shared__ float bufs[kFwdWarps][2][kFmMax];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
@@ -1038,6 +1092,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
                       const uint32_t* __restrict__ a, const uint32_t* __restrict__ b, const float* __restrict__ w,
                       const float* __restrict__ zs, const float* __restrict__ dlog, int P,
                       float* __restrict__ partials) {
+  wait_prior_grids();
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* xrow = sm + warp * (kBwdRows + 1) * kFmMax;  // the layer input of the current row
@@ -1141,6 +1196,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32)
 template <int ACT>
 __global__ void mlp_input(int n, int W, int m, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
                           const float* __restrict__ w0, float* __restrict__ z, float* __restrict__ act) {
+  wait_prior_grids();
   const size_t count = (size_t)n * W;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / W, c = i % W;
@@ -1152,6 +1208,7 @@ __global__ void mlp_input(int n, int W, int m, const uint32_t* __restrict__ a, c
 
 template <int ACT>
 __global__ void activate(size_t count, const float* __restrict__ z, float* __restrict__ act) {
+  wait_prior_grids();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
     act[i] = act_f<ACT>(z[i]);
 }
@@ -1160,6 +1217,7 @@ __global__ void activate(size_t count, const float* __restrict__ z, float* __res
 // (one-hot rows), p = left * right elementwise.
 __global__ void bilinear_input(int n, int W, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
                                const float* __restrict__ ea, const float* __restrict__ eb, float* __restrict__ p) {
+  wait_prior_grids();
   const size_t count = (size_t)n * W;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / W, c = i % W;
@@ -1172,6 +1230,7 @@ __global__ void bilinear_gradient(int n, int W, const uint32_t* __restrict__ a, 
                                   const float* __restrict__ ea, const float* __restrict__ eb,
                                   const float* __restrict__ dp, float* __restrict__ dleft,
                                   float* __restrict__ dright) {
+  wait_prior_grids();
   const size_t count = (size_t)n * W;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / W, c = i % W;
@@ -1202,6 +1261,7 @@ constexpr int kClassList = 4096;  // matching rows held before they are summed
 __global__ void __launch_bounds__(kClassThreads)
     class_gradient(int n, int W, int m, int mode, const uint32_t* __restrict__ a, const uint32_t* __restrict__ b,
                    const float* __restrict__ dh0, const float* __restrict__ extra, float* __restrict__ out) {
+  wait_prior_grids();
   __shared__ int list[kClassList];
   __shared__ uint8_t kinds[kClassList];
   __shared__ int warp_count[kClassThreads / 32];
@@ -1292,6 +1352,7 @@ __global__ void __launch_bounds__(kClassThreads)
 __global__ void __launch_bounds__(kFwdWarps * 32)
     cross_entropy_gradient(int n, int m, const float* __restrict__ logits, const uint32_t* __restrict__ y,
                            float* __restrict__ dlog, int* __restrict__ flags) {
+  wait_prior_grids();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
   if (r >= n) return;
@@ -1320,6 +1381,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
 // (src/simple/gpu.rs:748-772).
 __global__ void __launch_bounds__(kFwdWarps * 32)
     predictions(int n, int m, const float* __restrict__ logits, uint32_t* __restrict__ out) {
+  wait_prior_grids();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kFwdWarps + warp;
   if (r >= n) return;
@@ -1358,6 +1420,7 @@ __global__ void __launch_bounds__(kFwdWarps * 32)
 __global__ void adamw(size_t count, size_t mesh_start, const StepScalars* __restrict__ sc,
                       const float* __restrict__ grad, float* __restrict__ w, float* __restrict__ m1,
                       float* __restrict__ m2, const float* __restrict__ channel, int W, int m, size_t n_in) {
+  wait_prior_grids();
   const float b1 = sc->beta1, b2 = sc->beta2, eps = sc->epsilon;
   const float c1 = sc->correction1, c2 = sc->correction2;
   const float ob1 = __fsub_rn(1.0f, b1), ob2 = __fsub_rn(1.0f, b2);
@@ -1381,6 +1444,7 @@ __global__ void adamw(size_t count, size_t mesh_start, const StepScalars* __rest
 // the step (E input-major [inputs][W], R [W][m]).
 __global__ void channel_decay(int inputs, int W, int m, float exponent, const StepScalars* __restrict__ sc,
                               const float* __restrict__ E, const float* __restrict__ R, float* __restrict__ out) {
+  wait_prior_grids();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= W) return;
   float squares = 0.f;
@@ -1720,7 +1784,8 @@ class SimpleModel {
         throw;
       }
       SIMPLE_CUDA(cudaStreamEndCapture(stream_, &g));
-      cudaError_t e = cudaGraphInstantiate(&ws.step_graph, g, 0);
+      cudaError_t e = programmatic_edges(g);
+      if (e == cudaSuccess) e = cudaGraphInstantiate(&ws.step_graph, g, 0);
       cudaGraphDestroy(g);
       SIMPLE_CUDA(e);
       ws.step_launches = launches_;
