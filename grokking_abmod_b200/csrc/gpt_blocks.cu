@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
   float* red = smem + 2 * T::BUF;   // 2 * TR * WPR
   Ctx<T> c;
   int phase = 0;
-  const int hp = d.head_width / 2;
+  const int hp = S::head_pairs(d);
   const float inv_hw = 1.0f / (float)d.head_width;
   const RopeLane rope(c.cp, hp);
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT)
   float* red = smem + 2 * T::BUF;
   Ctx<T> c;
   int phase = 0;
-  const int hp = d.head_width / 2;
+  const int hp = S::head_pairs(d);
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     float2 a[RPT], res[RPT];
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
   zero_slots<T>(c, acc_f, F);
   zero_slots<T>(c, acc_o, A);
   int phase = 0;
-  const int hp = d.head_width / 2;
+  const int hp = S::head_pairs(d);
   const int ntiles = (d.rows + T::TR - 1) / T::TR;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     float2 g[RPT], n2[RPT], dy[RPT];
@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
   Ctx<T> c;
   zero_slots<T>(c, accs, 3 * A);
   int phase = 0;
-  const int hp = d.head_width / 2;
+  const int hp = S::head_pairs(d);
   const float inv_hw = 1.0f / (float)d.head_width;
   const RopeLane rope(c.cp, hp);
   const int ntiles = (d.rows + T::TR - 1) / T::TR;

@@ -145,13 +145,18 @@ struct BlockOpsW final : BlockOps {
 };
 
 // The reference's default mesh depths (attention 4, FFN 6; src/gpt/config.rs:46-47)
-// get kernels with the shape compiled in; other depths run the same kernels
+// get kernels with the shape compiled in (and, for 64-channel heads, the
+// head width too); other depths run the same kernels
 // with the shape read at run time, and heads of 128 channels or more (hd,
 // from width 128 up) the variant whose head sums and RoPE partners cross warps.
 template <int W>
 std::unique_ptr<BlockOps> make_block_ops_w(int A, int F, int conn, int hd) {
   if constexpr (W >= 128) {
     if (hd > 64) return std::make_unique<BlockOpsW<W, RuntimeShapeWide>>(A, F);
+  }
+  if (A == 4 && F == 6 && hd == 64) {
+    if (conn == 0) return std::make_unique<BlockOpsW<W, MeshShape<4, 6, 0, false, 32>>>(A, F);
+    if (conn == 1) return std::make_unique<BlockOpsW<W, MeshShape<4, 6, 1, false, 32>>>(A, F);
   }
   if (A == 4 && F == 6 && conn == 0) return std::make_unique<BlockOpsW<W, MeshShape<4, 6, 0>>>(A, F);
   if (A == 4 && F == 6 && conn == 1) return std::make_unique<BlockOpsW<W, MeshShape<4, 6, 1>>>(A, F);

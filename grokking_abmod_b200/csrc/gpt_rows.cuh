@@ -53,13 +53,16 @@ __device__ __forceinline__ int mesh_stride(const Dims& d, int layer) {
 // and weight address is a constant instead of per-layer integer work.
 // WIDE_: heads of 128 channels or more (hp > 32 pairs), whose per-head
 // sums and RoPE partners cross warps (head_sum_any, rope_any); the common
-// shapes compile without that path.
-template <int A_, int F_, int CONN_, bool WIDE_ = false>
+// shapes compile without that path.  HP_: channel pairs per head fixed at
+// compile time (0 = head_width / 2 read at run time), so the per-head
+// shuffle sums and head indexing need no run-time dispatch.
+template <int A_, int F_, int CONN_, bool WIDE_ = false, int HP_ = 0>
 struct MeshShape {
-  static constexpr int A = A_, F = F_, CONN = CONN_;
+  static constexpr int A = A_, F = F_, CONN = CONN_, HP = HP_;
   static constexpr bool WIDE = WIDE_;
   __device__ static __forceinline__ int attn(const Dims& d) { return A > 0 ? A : d.attn_depth; }
   __device__ static __forceinline__ int ffn(const Dims& d) { return F > 0 ? F : d.ffn_depth; }
+  __device__ static __forceinline__ int head_pairs(const Dims& d) { return HP > 0 ? HP : d.head_width / 2; }
 };
 using RuntimeShape = MeshShape<0, 0, -1>;
 using RuntimeShapeWide = MeshShape<0, 0, -1, true>;
