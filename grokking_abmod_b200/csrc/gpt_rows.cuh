@@ -272,7 +272,10 @@ __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, fl
     const float* xin = bufs + l * T::BUF;
     const float* yout = bufs + (l + 1) * T::BUF;  // valid when l + 1 < depth
     float* ex = xch + (l & 1) * T::BUF;
-    float2 gs = make_float2(0.f, 0.f), gn = make_float2(0.f, 0.f);
+    // The rows' edge-gradient terms accumulate straight onto the thread's slot.
+    float4& slot = acc[l * T::NT + c.tid];
+    const float4 sv = slot;
+    float2 gs = make_float2(sv.x, sv.y), gn = make_float2(sv.z, sv.w);
 #pragma unroll
     for (int k = 0; k < T::RPT; ++k) {
       const int r = c.row(k);
@@ -292,10 +295,7 @@ __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, fl
         Planes<W>::put(ex + r * W, c.cp, back);
       }
     }
-    float4& slot = acc[l * T::NT + c.tid];
-    const float2 ss = add2(make_float2(slot.x, slot.y), gs);
-    const float2 sn = add2(make_float2(slot.z, slot.w), gn);
-    slot = make_float4(ss.x, ss.y, sn.x, sn.y);
+    slot = make_float4(gs.x, gs.y, gn.x, gn.y);
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < T::RPT; ++k) {
@@ -350,7 +350,10 @@ __device__ __forceinline__ void mesh_backward_kept(const Ctx<T>& c, const Dims& 
       const float2 w0 = make_float2(w.x, w.z), w1 = make_float2(w.y, w.w);
       const float* xin = bufs + l * T::BUF;  // even plane of layer l's input
       float* ex = xch + (l & 1) * T::BUF;
-      float2 gs = make_float2(0.f, 0.f), gn = make_float2(0.f, 0.f);
+      // The rows' edge-gradient terms accumulate straight onto the thread's slot.
+      float4& slot = acc[l * T::NT + c.tid];
+      const float4 sv = slot;
+      float2 gs = make_float2(sv.x, sv.y), gn = make_float2(sv.z, sv.w);
 #pragma unroll
       for (int k = 0; k < T::RPT; ++k) {
         const int r = c.row(k);
@@ -364,10 +367,7 @@ __device__ __forceinline__ void mesh_backward_kept(const Ctx<T>& c, const Dims& 
         // Channel c's neighbour term dz*w1 flows back to channel c + 1.
         ex[r * W + Planes<W>::P + c.cp] = dz.y * w1.y;
       }
-      float4& slot = acc[l * T::NT + c.tid];
-      const float2 ss = add2(make_float2(slot.x, slot.y), gs);
-      const float2 sn = add2(make_float2(slot.z, slot.w), gn);
-      slot = make_float4(ss.x, ss.y, sn.x, sn.y);
+      slot = make_float4(gs.x, gs.y, gn.x, gn.y);
       __syncthreads();
 #pragma unroll
       for (int k = 0; k < T::RPT; ++k) {
