@@ -174,10 +174,12 @@ __device__ __forceinline__ void split_a_row(const float* raw, bool k_outer, int 
   tc::tmem_st_wait();
 }
 
-// Bounded wait on an mbarrier phase that also gives up as soon as another
-// warp of the CTA has flagged a failure.
-__device__ __forceinline__ bool wait_or_failed(uint64_t* bar, uint32_t parity, volatile int* failed) {
-  for (uint32_t i = 0; i < (1u << 22); ++i) {
+// Bounded wait on an mbarrier phase (`rounds` rounds of four polls) that
+// also gives up as soon as another warp of the CTA has flagged a failure.
+constexpr uint32_t kWaitRounds = 1u << 22;
+__device__ __forceinline__ bool wait_or_failed(uint64_t* bar, uint32_t parity, volatile int* failed,
+                                               uint32_t rounds) {
+  for (uint32_t i = 0; i < rounds; ++i) {
     if (tc::bar_wait(bar, parity, 4)) return true;
     if (*failed) return false;
   }
@@ -207,7 +209,8 @@ __device__ __forceinline__ bool workers_any(bool v) {
 __global__ void __launch_bounds__(kGemmThreads + 32, 1)
     gemm_tf32x3_kernel(GemmOperand A, GemmOperand B, const __grid_constant__ CUtensorMap tma_a,
                        const __grid_constant__ CUtensorMap tma_b, int tma, float* __restrict__ C, int ldc,
-                       size_t chunk_stride, int M, int N, int K, int k_chunk, int* __restrict__ err) {
+                       size_t chunk_stride, int M, int N, int K, int k_chunk, int* __restrict__ err,
+                       int lost_block, uint32_t wait_rounds) {
   wait_prior_grids();
   extern __shared__ __align__(1024) float sm[];
   __shared__ uint64_t ready[kGemmStages], done[kGemmStages];
@@ -275,13 +278,18 @@ __global__ void __launch_bounds__(kGemmThreads + 32, 1)
       cp_async_wait<kGemmRaw - 1>();  // this thread's pieces of block i have landed
       bool bad = false;
       if (tma) {
-        bad |= !wait_or_failed(&full[s], (full_phase >> s) & 1u, vfailed);
-        full_phase ^= 1u << s;
-        landed = i + 1;
+        // A wait cut short (own limit, or another warp's failure) leaves
+        // block i's copy in flight: it stays with the drain below.
+        if (wait_or_failed(&full[s], (full_phase >> s) & 1u, vfailed, wait_rounds)) {
+          full_phase ^= 1u << s;
+          landed = i + 1;
+        } else {
+          bad = true;
+        }
       }
       // hi/lo stage st was last read by the MMAs of block i - 2.
       if (i >= 2) {
-        bad |= !wait_or_failed(&done[st], (done_phase >> st) & 1u, vfailed);
+        bad |= !wait_or_failed(&done[st], (done_phase >> st) & 1u, vfailed, wait_rounds);
         done_phase ^= 1u << st;
         tc::fence_after_sync();
       }
@@ -303,7 +311,9 @@ __global__ void __launch_bounds__(kGemmThreads + 32, 1)
       tc::fence_async_smem();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::bar_arrive(&ready[st]);
+      // lost_block (a test hook, -1 in every product launch) withholds warp
+      // 0's arrival for that K block, so the MMA warp's wait must give up.
+      if (lane == 0 && !(warp == 0 && i == lost_block)) tc::bar_arrive(&ready[st]);
       // Every worker has read raw stage s: refill it with block i + kGemmRaw.
       workers_sync();
       stage(i + kGemmRaw);
@@ -328,7 +338,7 @@ __global__ void __launch_bounds__(kGemmThreads + 32, 1)
     int committed = 0;
     for (int i = 0; lane == 0 && i < nb; ++i) {
       const int st = i & 1;
-      if (!wait_or_failed(&ready[st], (ready_phase >> st) & 1u, vfailed)) {
+      if (!wait_or_failed(&ready[st], (ready_phase >> st) & 1u, vfailed, wait_rounds)) {
         failed = 1;
         break;
       }
@@ -480,7 +490,7 @@ size_t gemm_partial_floats(int M, int N, int K, int k_chunk) {
 int gemm_launches(int K, int k_chunk) { return gemm_chunks(K, k_chunk) > 1 ? 2 : 1; }
 
 void launch_gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, int M, int N, int K, int k_chunk,
-                 float* partial, int* err, cudaStream_t st, bool a_tmem) {
+                 float* partial, int* err, cudaStream_t st, bool a_tmem, int lost_block, uint32_t wait_rounds) {
   (void)a_tmem;  // A is always staged through tensor memory
   const int chunks = gemm_chunks(K, k_chunk);
   const int kc = chunks > 1 ? k_chunk : K;
@@ -492,10 +502,11 @@ void launch_gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, 
   if (encode_operand(&ta, A, M, K, kGemmBM)) tma |= kTmaA;
   if (encode_operand(&tb, B, N, K, kGemmBN)) tma |= kTmaB;
   if (chunks == 1) {
-    gemm_tf32x3_kernel<<<grid, kGemmThreads + 32, gemm_smem(), st>>>(A, B, ta, tb, tma, C, ldc, 0, M, N, K, kc, err);
+    gemm_tf32x3_kernel<<<grid, kGemmThreads + 32, gemm_smem(), st>>>(A, B, ta, tb, tma, C, ldc, 0, M, N, K, kc, err,
+                                                                lost_block, wait_rounds);
   } else {
     gemm_tf32x3_kernel<<<grid, kGemmThreads + 32, gemm_smem(), st>>>(A, B, ta, tb, tma, partial, N, (size_t)M * N, M, N,
-                                                                K, kc, err);
+                                                                K, kc, err, lost_block, wait_rounds);
     const size_t mn = (size_t)M * N;
     const int blocks = (int)std::min<size_t>((mn + 255) / 256, 148 * 8);
     gemm_reduce_chunks<<<blocks, 256, 0, st>>>(partial, chunks, M, N, C, ldc);
@@ -522,5 +533,27 @@ extern "C" int mb_op_gemm_tf32x3(const float* a, const float* b, float* c, uint3
     const mb::GemmOperand A{a, a_outer ? (int)m : (int)k, a_outer};
     const mb::GemmOperand B{b, b_outer ? (int)n : (int)k, b_outer};
     mb::launch_gemm(A, B, c, (int)n, (int)m, (int)n, (int)k, 0, nullptr, d_status, (cudaStream_t)stream, a_tmem);
+  });
+}
+
+// Test hook for the bounded waits: one K-major GEMM whose K block
+// `lost_block` is never published to the MMA warp, with waits of
+// `wait_rounds` rounds, so every CTA gives up, drains its copies, skips its
+// epilogue and sets *d_status.  Not a product path.
+extern "C" int mb_test_gemm_lost_arrival(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k,
+                                         uint32_t lost_block, uint32_t wait_rounds, int* d_status, void* stream) {
+  return mb::guarded([&] {
+    mb::need(a, "a");
+    mb::need(b, "b");
+    mb::need(c, "c");
+    mb::need(d_status, "status");
+    mb::require(m >= 1 && n >= 1 && k >= 1, "GEMM dimensions must be positive");
+    mb::require(lost_block < (k + 31) / 32, "lost_block must name one of the K blocks");
+    mb::require(wait_rounds >= 1 && wait_rounds <= mb::kWaitRounds, "wait_rounds must be in 1..2^22");
+    mb::gemm_prepare();
+    const mb::GemmOperand A{a, (int)k, false};
+    const mb::GemmOperand B{b, (int)k, false};
+    mb::launch_gemm(A, B, c, (int)n, (int)m, (int)n, (int)k, 0, nullptr, d_status, (cudaStream_t)stream, false,
+                    (int)lost_block, wait_rounds);
   });
 }

@@ -30,8 +30,11 @@ void gemm_prepare();
 // `partial` (gemm_partial_floats floats) summed in chunk order.  `err` is a
 // device flag set if an mbarrier wait gave up.  A is always staged through
 // tensor memory; `a_tmem` is accepted for callers that ask for it.
+// lost_block and wait_rounds are the bounded-wait test hook of
+// mb_test_gemm_lost_arrival; every product call keeps the defaults.
 void launch_gemm(const GemmOperand& A, const GemmOperand& B, float* C, int ldc, int M, int N, int K, int k_chunk,
-                 float* partial, int* err, cudaStream_t st, bool a_tmem = false);
+                 float* partial, int* err, cudaStream_t st, bool a_tmem = false, int lost_block = -1,
+                 uint32_t wait_rounds = 1u << 22);
 int gemm_chunks(int K, int k_chunk);
 size_t gemm_partial_floats(int M, int N, int K, int k_chunk);
 // Kernel launches of one launch_gemm call.

@@ -209,6 +209,15 @@ int mb_op_mesh_backward(const float* x, const float* dy, float* dx, float* dweig
 int mb_op_gemm_tf32x3(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k, uint32_t layout,
                       int* d_status, void* stream);
 
+/* Test hook of the tensor-core waits (no counterpart in the reference): the
+ * GEMM of mb_op_gemm_tf32x3 (layout 0) with K block `lost_block` never handed
+ * to the MMA warp and every wait bounded by `wait_rounds` rounds of four
+ * polls (1..2^22; product launches use 2^22).  Each CTA gives up, waits for
+ * its copies in flight, skips its epilogue, frees its tensor memory and sets
+ * *d_status to 1; the context stays usable.  Returns MB_OK once launched. */
+int mb_test_gemm_lost_arrival(const float* a, const float* b, float* c, uint32_t m, uint32_t n, uint32_t k,
+                              uint32_t lost_block, uint32_t wait_rounds, int* d_status, void* stream);
+
 /* ---- per-op entry points of the Mesh GPT operators (device pointers, the
  * caller's stream, validation on the host before any launch).  The training
  * step runs the same arithmetic fused into its own kernels; these serve
