@@ -102,12 +102,17 @@ __device__ __forceinline__ void layer_loop(int n, F&& body) {
 template <class T>
 struct Ctx {
   int tid, rl, cp, lane, warp;
+  // Plane indices of the stride-1 neighbours, fixed per thread: the even
+  // channel of pair cp + 1 and the odd channel of pair cp - 1 (both mod P).
+  int nxt, prv;
   __device__ Ctx() {
     tid = threadIdx.x;
     rl = tid / T::PAIRS;
     cp = tid % T::PAIRS;
     lane = tid & 31;
     warp = tid >> 5;
+    nxt = cp + 1 == T::PAIRS ? 0 : cp + 1;
+    prv = T::PAIRS + (cp == 0 ? T::PAIRS - 1 : cp - 1);
   }
   __device__ __forceinline__ int row(int k) const { return k * T::RL + rl; }
 };
@@ -122,10 +127,6 @@ struct Planes {
     row[P + cp] = v.y;
   }
   __device__ static __forceinline__ float2 get(const float* row, int cp) { return make_float2(row[cp], row[P + cp]); }
-  // Even channel of pair cp + 1 (mod P): the stride-1 neighbour of 2cp + 1.
-  __device__ static __forceinline__ float next_even(const float* row, int cp) { return row[cp + 1 == P ? 0 : cp + 1]; }
-  // Odd channel of pair cp - 1 (mod P): the stride -1 neighbour of 2cp.
-  __device__ static __forceinline__ float prev_odd(const float* row, int cp) { return row[P + (cp == 0 ? P - 1 : cp - 1)]; }
   // Channels (2cp + s, 2cp + 1 + s) mod W for an even shift |s| <= W / 2.
   __device__ static __forceinline__ float2 shifted_even(const float* row, int cp, int s) {
     int h = cp + s / 2;
@@ -223,7 +224,7 @@ __device__ __forceinline__ void mesh_layer_forward(const Ctx<T>& c, float2 (&a)[
 #pragma unroll
   for (int k = 0; k < T::RPT; ++k) {
     const float* srow = buf + c.row(k) * W;
-    const float2 nb = stride == 1 ? make_float2(a[k].y, Planes<W>::next_even(srow, c.cp))
+    const float2 nb = stride == 1 ? make_float2(a[k].y, srow[c.nxt])
                                   : Planes<W>::shifted_even(srow, c.cp, stride);
     const float2 z = fma2(nb, make_float2(w.y, w.w), mul2(a[k], make_float2(w.x, w.z)));
     a[k] = activated ? elu2(z) : z;
@@ -282,7 +283,7 @@ __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, fl
       float2 dz = dy[k];
       if (l + 1 != depth) dz = mul2(dz, elu_slope2(Planes<W>::get(yout + r * W, c.cp)));
       const float2 x = Planes<W>::get(xin + r * W, c.cp);
-      const float2 nb = s == 1 ? make_float2(x.y, Planes<W>::next_even(xin + r * W, c.cp))
+      const float2 nb = s == 1 ? make_float2(x.y, xin[r * W + c.nxt])
                                : Planes<W>::shifted_even(xin + r * W, c.cp, s);
       gs = fma2(dz, x, gs);
       gn = fma2(dz, nb, gn);
@@ -300,7 +301,7 @@ __device__ __forceinline__ void mesh_backward(const Ctx<T>& c, const Dims& d, fl
 #pragma unroll
     for (int k = 0; k < T::RPT; ++k) {
       const float* erow = ex + c.row(k) * W;
-      const float2 t = s == 1 ? make_float2(Planes<W>::prev_odd(erow, c.cp), dy[k].x * w.y)
+      const float2 t = s == 1 ? make_float2(erow[c.prv], dy[k].x * w.y)
                               : Planes<W>::shifted_even(erow, c.cp, -s);
       dy[k] = fma2(dy[k], w0, t);
     }
@@ -360,7 +361,7 @@ __device__ __forceinline__ void mesh_backward_kept(const Ctx<T>& c, const Dims& 
         float2 dz = dy[k];
         if (l + 1 != DEPTH) dz = mul2(dz, elu_slope2(kept.x[l + 1 < DEPTH ? l + 1 : l][k]));
         const float2 x = kept.x[l][k];
-        const float2 nb = make_float2(x.y, Planes<W>::next_even(xin + r * W, c.cp));
+        const float2 nb = make_float2(x.y, xin[r * W + c.nxt]);
         gs = fma2(dz, x, gs);
         gn = fma2(dz, nb, gn);
         dy[k] = dz;
@@ -371,7 +372,7 @@ __device__ __forceinline__ void mesh_backward_kept(const Ctx<T>& c, const Dims& 
       __syncthreads();
 #pragma unroll
       for (int k = 0; k < T::RPT; ++k) {
-        const float2 t = make_float2(Planes<W>::prev_odd(ex + c.row(k) * W, c.cp), dy[k].x * w.y);
+        const float2 t = make_float2(ex[c.row(k) * W + c.prv], dy[k].x * w.y);
         dy[k] = fma2(dy[k], w0, t);
       }
     });
