@@ -316,7 +316,9 @@ __global__ void __launch_bounds__(RowTile<W, RPT>::NT, 3)
       dn[k] = make_float2(0.f, 0.f);
     }
     rmsnorm_rows<T>(c, n1, inv1, red, phase, W);
-#pragma unroll 1
+    // Unrolled over the three stacks: each copy has its pointers, QK-Norm
+    // and RoPE branches fixed at compile time (80 registers, no spills).
+#pragma unroll
     for (int m = 0; m < 3; ++m) {
       const float4* wg = reinterpret_cast<const float4*>(m == 0 ? wq : (m == 1 ? wk : wv));
       // The stack's output gradient (an L2 hit after the prefetch) is
